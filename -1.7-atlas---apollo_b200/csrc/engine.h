@@ -1,0 +1,122 @@
+// Host/device description of a decode "program" run by the persistent decode
+// kernel (decode.cu).
+//
+// A program is an ordered list of phases. Every CTA (one per SM) walks the
+// same list: for each phase it processes the work items i with
+// i % gridDim.x == blockIdx.x, then arrives on that phase's counter; before its
+// first item of a phase it waits until every CTA has arrived on the previous
+// phase's counter. A producer warp streams each item's weight (or KV-cache)
+// bytes into a shared-memory ring with 1-D bulk copies, running ahead across
+// phase boundaries because weights never depend on activations; consumer
+// warps wait only for the activations.
+#pragma once
+#include <cstdint>
+
+namespace atlas {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kStages = 6;
+constexpr uint32_t kStageBytes = 32768;
+constexpr int kMaxSlices = 4;        // per-lane x slices held in registers
+constexpr int kMaxItemRows = 64;     // rows of one segment in one item
+constexpr int kMaxSeg = 3;
+constexpr int kHeadDim = 128;
+constexpr int kAttnSplit = 128;      // positions per attention work item (one fp16 stage)
+constexpr int kMaxGroup = 16;        // query heads per KV head
+
+enum PhaseKind : uint32_t {
+    PH_EMBED = 0,   // x = dequant(token_embd row of the current token)
+    PH_GEMV = 1,    // segmented GEMV with a fused prologue / epilogue
+    PH_ATTN = 2,    // RoPE + KV append + split-K flash-decode + split combine
+    PH_ARGMAX = 3,  // reduce the head items' (max, index) partials -> next token
+};
+
+enum InputMode : uint32_t {
+    IN_RAW = 0,      // x as stored
+    IN_RMSNORM = 1,  // rms_norm(x, norm_w) computed per CTA (src/brain_runtime.c:1338)
+};
+
+enum Epilogue : uint32_t {
+    EPI_STORE = 0,       // out[r] = dot (+ bias[r])
+    EPI_RESID_ADD = 1,   // out[r] += dot      (residual stream)
+    EPI_SWIGLU = 2,      // out[r] = silu(dot0) * dot1   (segments 0 = gate, 1 = up)
+    EPI_LOGITS = 3,      // out[r] = dot and (max, argmax) per item
+};
+
+struct Seg {
+    const uint8_t *w;     // row 0 of the raw GGUF tensor
+    uint64_t row_bytes;
+    uint32_t type;        // 12 = Q4_K, 14 = Q6_K
+    uint32_t rows;
+    const float *bias;    // optional, EPI_STORE only
+    float *out;
+};
+
+struct Phase {
+    uint32_t kind;
+    uint32_t layer;
+    // ---- PH_GEMV ----
+    uint32_t n_items;
+    uint32_t item_rows;     // rows per item (row space: concatenated segments, or paired)
+    uint32_t paired;        // 1: each item covers rows [r0,r1) of EVERY segment (gate/up)
+    uint32_t n_seg;
+    uint32_t cols;          // input length (multiple of 256)
+    uint32_t warps_per_row; // W: consumer warps cooperating on one row
+    uint32_t n_slices;      // per-lane 32-element slices: ceil(cols/32 / (32*W))
+    uint32_t input_mode;
+    uint32_t epilogue;
+    uint32_t seg_start[kMaxSeg + 1];  // cumulative row offsets (concatenated row space)
+    Seg seg[kMaxSeg];
+    const float *in;        // input vector (cols floats)
+    const float *norm_w;    // IN_RMSNORM weight
+    float *partial_max;     // EPI_LOGITS: per-item max
+    uint32_t *partial_idx;  // EPI_LOGITS: per-item argmax
+    // ---- PH_ATTN ----
+    const float *q, *k, *v; // fresh projections (bias added, RoPE not yet applied)
+    void *k_cache, *v_cache;// this layer's cache, [kv_head][position][head_dim]
+    float *att;             // output, q_dim floats
+    float *part;            // split partials: [kv_head][split][group][head_dim + 2]
+    uint32_t *split_ctr;    // per KV head arrival counters (reset by the combiner)
+    // ---- PH_EMBED ----
+    const uint8_t *embd;    // token_embd raw rows
+    uint64_t embd_row_bytes;
+    uint32_t embd_type;
+    float *x;
+    // ---- PH_ARGMAX ----
+    uint32_t argmax_items;  // number of head items holding partials
+};
+
+// Mutable per-launch state in device memory. The first two fields are owned
+// by the device (they only ever grow); the host rewrites the rest before a
+// call (from `pos` on).
+struct StepState {
+    uint32_t epoch;        // launches completed (phase counters are epoch-relative)
+    uint32_t exit_ctr;     // CTAs that finished, epoch-relative
+    uint32_t pos;          // position of the token being processed
+    uint32_t token;        // token id being processed
+    uint32_t status;       // first error recorded (kStatus*), 0 = ok
+    uint32_t next_token;   // greedy pick of this step
+    float next_logit;
+    uint32_t step;         // index into out_ids for multi-step generation
+    uint32_t max_steps;
+    uint32_t pad_;
+    uint32_t *out_ids;     // optional device array of picks, or null
+};
+
+struct Program {
+    const Phase *phases;   // device array
+    uint32_t n_phases;
+    uint32_t *phase_ctr;   // device array [n_phases], epoch-relative arrival counts (stride 8)
+    StepState *state;
+    // model constants needed by PH_ATTN / PH_EMBED
+    uint32_t q_heads, kv_heads, head_dim, kv_fp16;
+    uint32_t hidden;
+    float rms_eps;
+    const float2 *rope;    // [max_context][head_dim/2] (cos, sin)
+    uint32_t max_context;
+    uint32_t advance;      // 1: after the step, token = next_token and pos += 1
+    uint64_t *trace;       // optional: [cta][phase][4] globaltimer stamps (diagnostics)
+};
+
+}  // namespace atlas

@@ -1,0 +1,703 @@
+// libatlas_cuda C ABI: model upload, decode-program construction, decode /
+// generate / prefill entry points and the stateless test kernels.
+//
+// Device memory layout of a model (one arena per tensor class, 256-byte
+// aligned tensors): raw GGUF weight bytes exactly as in the file; norm weights
+// and biases as fp32 vectors; the KV cache [layer][kv_head][position][128] in
+// fp16 (or fp32); activations x, q, k, v, att, ffn (fp32), logits (fp32);
+// attention split partials; a RoPE (cos, sin) table built on the host with the
+// reference's own powf / cosf / sinf (src/brain_runtime.c:1383-1387).
+#include <cmath>
+#include <cstddef>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+#include "../../include/atlas_cuda.h"
+#include "engine.h"
+#include "quant.cuh"
+
+extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream);
+
+
+using namespace atlas;
+
+namespace {
+
+thread_local char g_tls_error[512];
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t n = 0;
+};
+
+struct ProgramBuffers {
+    Program pg{};
+    Phase *d_phases = nullptr;
+    uint32_t *d_ctr = nullptr;
+    StepState *d_state = nullptr;
+    std::vector<Phase> phases;
+};
+
+}  // namespace
+
+struct AtlasCuda {
+    AtlasModelDesc desc{};
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    std::vector<void *> allocs;
+    // weights
+    struct W {
+        const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+        uint32_t tq = 0, tk = 0, tv = 0, to = 0, tg = 0, tu = 0, td = 0;
+        const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+        void *kc = nullptr, *vc = nullptr;
+    };
+    std::vector<W> layers;
+    const uint8_t *embd = nullptr, *head = nullptr;
+    uint32_t t_embd = 0, t_head = 0;
+    const float *out_norm = nullptr;
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *ffn = nullptr, *logits = nullptr;
+    float *part = nullptr;
+    uint32_t *split_ctr = nullptr;
+    float *pmax = nullptr;
+    uint32_t *pidx = nullptr;
+    float2 *rope = nullptr;
+    uint32_t *d_out_ids = nullptr;
+    uint32_t out_ids_cap = 0;
+    ProgramBuffers decode;
+    uint64_t launches = 0;
+    double last_ms = 0.0;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+namespace {
+
+int fail(AtlasCuda *h, int code, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (h) h->err = buf;
+    snprintf(g_tls_error, sizeof(g_tls_error), "%s", buf);
+    return code;
+}
+
+#define CU(h, call)                                                                          \
+    do {                                                                                     \
+        cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess)                                                               \
+            return fail((h), ATLAS_ECUDA, "%s failed: %s", #call, cudaGetErrorString(e_));   \
+    } while (0)
+
+int device_ok(int device, int *sms)
+{
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0 || device < 0 || device >= n) return ATLAS_ENODEV;
+    cudaDeviceProp p{};
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return ATLAS_ENODEV;
+    if (p.major != 10) return ATLAS_ENODEV;
+    if (sms) *sms = p.multiProcessorCount;
+    return ATLAS_OK;
+}
+
+template <typename T>
+int dalloc(AtlasCuda *h, T **out, size_t bytes)
+{
+    void *p = nullptr;
+    const size_t n = (bytes + 255) & ~size_t(255);
+    cudaError_t e = cudaMalloc(&p, n ? n : 256);
+    if (e != cudaSuccess) return fail(h, ATLAS_ENOMEM, "cudaMalloc(%zu) failed: %s", n, cudaGetErrorString(e));
+    h->allocs.push_back(p);
+    *out = reinterpret_cast<T *>(p);
+    return ATLAS_OK;
+}
+
+const AtlasTensorDesc *find(const AtlasTensorDesc *t, uint32_t n, const char *name)
+{
+    for (uint32_t i = 0; i < n; ++i)
+        if (t[i].name && !strcmp(t[i].name, name)) return &t[i];
+    return nullptr;
+}
+
+uint64_t elems(const AtlasTensorDesc *t)
+{
+    uint64_t e = 1;
+    for (uint32_t d = 0; d < t->n_dims; ++d) e *= t->dims[d];
+    return e;
+}
+
+// Matrix tensor [rows x cols] of a supported GEMV type, uploaded unchanged.
+int upload_matrix(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, uint64_t rows, const uint8_t **dev,
+                  uint32_t *type)
+{
+    if (!t) return fail(h, ATLAS_EINVAL, "missing matrix tensor");
+    if (t->type != ATLAS_TYPE_Q4_K && t->type != ATLAS_TYPE_Q6_K)
+        return fail(h, ATLAS_EINVAL, "%s: tensor type %u is not supported by the decode engine (Q4_K, Q6_K)",
+                    t->name, t->type);
+    if (t->n_dims != 2 || t->dims[0] != cols || t->dims[1] != rows || cols % 256)
+        return fail(h, ATLAS_EINVAL, "%s: dims %llu x %llu, expected %llu x %llu", t->name,
+                    (unsigned long long)t->dims[0], (unsigned long long)t->dims[1], (unsigned long long)cols,
+                    (unsigned long long)rows);
+    const uint64_t bytes = rows * (cols / 256) * block_bytes(t->type);
+    uint8_t *d = nullptr;
+    int rc = dalloc(h, &d, bytes);
+    if (rc) return rc;
+    CU(h, cudaMemcpy(d, t->data, bytes, cudaMemcpyHostToDevice));
+    *dev = d;
+    *type = t->type;
+    return ATLAS_OK;
+}
+
+// F32 or F16 vector of n elements -> fp32 on the device (load_f32_vector,
+// src/brain_runtime.c:1280-1309).
+int upload_vector(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t n, const float **dev)
+{
+    if (!t || elems(t) != n) return fail(h, ATLAS_EINVAL, "%s: vector of %llu elements expected", t ? t->name : "?",
+                                         (unsigned long long)n);
+    std::vector<float> tmp(n);
+    if (t->type == ATLAS_TYPE_F32) {
+        memcpy(tmp.data(), t->data, n * 4);
+    } else if (t->type == ATLAS_TYPE_F16) {
+        const uint16_t *s = static_cast<const uint16_t *>(t->data);
+        for (uint64_t i = 0; i < n; ++i) {
+            const uint32_t hb = s[i], sign = (hb & 0x8000u) << 16, e = (hb >> 10) & 31u;
+            uint32_t m = hb & 1023u, bits;
+            if (e == 31u) bits = sign | 0x7f800000u | (m << 13);
+            else if (e) bits = sign | ((e + 112u) << 23) | (m << 13);
+            else if (!m) bits = sign;
+            else {
+                uint32_t sh = 0;
+                while (!(m & 0x400u)) { m <<= 1; ++sh; }
+                bits = sign | ((113u - sh) << 23) | ((m & 1023u) << 13);
+            }
+            memcpy(&tmp[i], &bits, 4);
+        }
+    } else {
+        return fail(h, ATLAS_EINVAL, "%s: vector type %u unsupported", t->name, t->type);
+    }
+    float *d = nullptr;
+    int rc = dalloc(h, &d, n * 4);
+    if (rc) return rc;
+    CU(h, cudaMemcpy(d, tmp.data(), n * 4, cudaMemcpyHostToDevice));
+    *dev = d;
+    return ATLAS_OK;
+}
+
+// Rows per work item: as many as fit a stage (and kMaxItemRows), reduced where
+// that evens out the items over the grid.
+uint32_t pick_item_rows(uint32_t total_rows, uint64_t max_row_bytes, uint32_t grid)
+{
+    uint32_t fit = (uint32_t)((kStageBytes - 32) / max_row_bytes);
+    if (fit > (uint32_t)kMaxItemRows) fit = kMaxItemRows;
+    if (fit < 1) fit = 1;
+    uint32_t best = fit;
+    double best_eff = -1.0;
+    for (uint32_t r = fit; r >= 1; --r) {
+        const uint32_t items = (total_rows + r - 1) / r;
+        const uint32_t waves = (items + grid - 1) / grid;
+        const double eff = (double)items / ((double)waves * grid) * ((double)total_rows / ((double)items * r));
+        if (eff > best_eff + 1e-9) { best_eff = eff; best = r; }
+        if (r == 1) break;
+    }
+    return best;
+}
+
+void pick_row_split(uint32_t cols, uint32_t &W, uint32_t &ns)
+{
+    const uint32_t S = cols / 32u;
+    for (W = 1; W <= (uint32_t)kConsumerWarps; W *= 2) {
+        ns = (S + 32u * W - 1u) / (32u * W);
+        if (ns <= (uint32_t)kMaxSlices) return;
+    }
+    W = kConsumerWarps;
+    ns = (S + 32u * W - 1u) / (32u * W);
+}
+
+Phase gemv_phase(uint32_t cols, uint32_t grid, bool paired, std::initializer_list<Seg> segs, const float *in,
+                 uint32_t input_mode, const float *norm_w, uint32_t epi)
+{
+    Phase ph{};
+    ph.kind = PH_GEMV;
+    ph.cols = cols;
+    ph.paired = paired ? 1u : 0u;
+    ph.n_seg = 0;
+    uint64_t max_rb = 0;
+    for (const Seg &s : segs) {
+        ph.seg_start[ph.n_seg + 1] = ph.seg_start[ph.n_seg] + s.rows;
+        ph.seg[ph.n_seg++] = s;
+        if (s.row_bytes > max_rb) max_rb = s.row_bytes;
+    }
+    const uint32_t total = paired ? ph.seg[0].rows : ph.seg_start[ph.n_seg];
+    ph.item_rows = pick_item_rows(total, max_rb, grid);
+    ph.n_items = (total + ph.item_rows - 1) / ph.item_rows;
+    pick_row_split(cols, ph.warps_per_row, ph.n_slices);
+    ph.in = in;
+    ph.input_mode = input_mode;
+    ph.norm_w = norm_w;
+    ph.epilogue = epi;
+    return ph;
+}
+
+Seg seg_of(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, const float *bias, float *out)
+{
+    Seg s{};
+    s.w = w;
+    s.type = type;
+    s.rows = rows;
+    s.row_bytes = (uint64_t)(cols / 256) * block_bytes(type);
+    s.bias = bias;
+    s.out = out;
+    return s;
+}
+
+int finalize_program(AtlasCuda *h, ProgramBuffers &pb, const AtlasCuda *m)
+{
+    const size_t n = pb.phases.size();
+    int rc = dalloc(h, &pb.d_phases, n * sizeof(Phase));
+    if (rc) return rc;
+    CU(h, cudaMemcpy(pb.d_phases, pb.phases.data(), n * sizeof(Phase), cudaMemcpyHostToDevice));
+    if ((rc = dalloc(h, &pb.d_ctr, n * 8 * sizeof(uint32_t)))) return rc;
+    CU(h, cudaMemset(pb.d_ctr, 0, n * 8 * sizeof(uint32_t)));
+    if ((rc = dalloc(h, &pb.d_state, sizeof(StepState)))) return rc;
+    CU(h, cudaMemset(pb.d_state, 0, sizeof(StepState)));
+    pb.pg.phases = pb.d_phases;
+    pb.pg.n_phases = (uint32_t)n;
+    pb.pg.phase_ctr = pb.d_ctr;
+    pb.pg.state = pb.d_state;
+    if (m) {
+        pb.pg.q_heads = m->desc.q_heads;
+        pb.pg.kv_heads = m->desc.kv_heads;
+        pb.pg.head_dim = m->desc.head_dim;
+        pb.pg.kv_fp16 = m->desc.kv_fp16 ? 1u : 0u;
+        pb.pg.hidden = m->desc.hidden;
+        pb.pg.rms_eps = m->desc.rms_eps;
+        pb.pg.rope = m->rope;
+        pb.pg.max_context = m->desc.max_context;
+    }
+    return ATLAS_OK;
+}
+
+// Host-side copy of the step state fields the API reads back.
+struct StateHost {
+    StepState s;
+};
+
+int reset_program(AtlasCuda *h, ProgramBuffers &pb)
+{
+    CU(h, cudaMemsetAsync(pb.d_ctr, 0, pb.phases.size() * 8 * sizeof(uint32_t), h->stream));
+    CU(h, cudaMemsetAsync(pb.d_state, 0, sizeof(StepState), h->stream));
+    return ATLAS_OK;
+}
+
+int status_to_code(AtlasCuda *h, uint32_t st)
+{
+    if (st == kStatusOk) return ATLAS_OK;
+    if (st == kStatusBarrierTimeout) return fail(h, ATLAS_ETIMEOUT, "device phase barrier timed out (status %u)", st);
+    if (st == kStatusStageTimeout) return fail(h, ATLAS_ETIMEOUT, "device copy stage timed out (status %u)", st);
+    return fail(h, ATLAS_ECUDA, "device reported status %u", st);
+}
+
+// Run `steps` launches of the decode program starting from (token, pos).
+int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
+               float *last_logit)
+{
+    ProgramBuffers &pb = h->decode;
+    StepState init{};
+    init.pos = pos;
+    init.token = token;
+    init.out_ids = out_ids_dev;
+    init.max_steps = steps;
+    // epoch / exit_ctr continue from the device values: only the host-owned
+    // tail of the state (from pos on) is written.
+    const size_t off = offsetof(StepState, pos);
+    CU(h, cudaMemcpyAsync(reinterpret_cast<uint8_t *>(pb.d_state) + off, reinterpret_cast<const uint8_t *>(&init) + off,
+                          sizeof(StepState) - off, cudaMemcpyHostToDevice, h->stream));
+    CU(h, cudaEventRecord(h->ev0, h->stream));
+    for (uint32_t i = 0; i < steps; ++i) {
+        CU(h, atlas_launch_decode(&pb.pg, h->sm_count, h->stream));
+        ++h->launches;
+    }
+    CU(h, cudaEventRecord(h->ev1, h->stream));
+    StepState out{};
+    CU(h, cudaMemcpyAsync(&out, pb.d_state, sizeof(StepState), cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->last_ms = ms;
+    if (out.status != kStatusOk) {
+        const int rc = status_to_code(h, out.status);
+        reset_program(h, pb);
+        cudaStreamSynchronize(h->stream);
+        return rc;
+    }
+    if (last_token) *last_token = out.next_token;
+    if (last_logit) *last_logit = out.next_logit;
+    return ATLAS_OK;
+}
+
+int build_decode_program(AtlasCuda *h)
+{
+    const AtlasModelDesc &d = h->desc;
+    const uint32_t G = (uint32_t)h->sm_count;
+    std::vector<Phase> &P = h->decode.phases;
+    Phase e{};
+    e.kind = PH_EMBED;
+    e.embd = h->embd;
+    e.embd_type = h->t_embd;
+    e.embd_row_bytes = (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
+    e.x = h->x;
+    P.push_back(e);
+    for (uint32_t l = 0; l < d.layers; ++l) {
+        const AtlasCuda::W &w = h->layers[l];
+        Phase qkv = gemv_phase(d.hidden, G, false,
+                               {seg_of(w.q, w.tq, d.q_dim, d.hidden, w.bq, h->q),
+                                seg_of(w.k, w.tk, d.kv_dim, d.hidden, w.bk, h->k),
+                                seg_of(w.v, w.tv, d.kv_dim, d.hidden, w.bv, h->v)},
+                               h->x, IN_RMSNORM, w.attn_norm, EPI_STORE);
+        qkv.layer = l;
+        P.push_back(qkv);
+        Phase at{};
+        at.kind = PH_ATTN;
+        at.layer = l;
+        at.q = h->q; at.k = h->k; at.v = h->v;
+        at.k_cache = w.kc; at.v_cache = w.vc;
+        at.att = h->att;
+        at.part = h->part;
+        at.split_ctr = h->split_ctr;
+        P.push_back(at);
+        Phase o = gemv_phase(d.q_dim, G, false, {seg_of(w.o, w.to, d.hidden, d.q_dim, nullptr, h->x)}, h->att, IN_RAW,
+                             nullptr, EPI_RESID_ADD);
+        o.layer = l;
+        P.push_back(o);
+        Phase gu = gemv_phase(d.hidden, G, true,
+                              {seg_of(w.gate, w.tg, d.ffn, d.hidden, nullptr, h->ffn),
+                               seg_of(w.up, w.tu, d.ffn, d.hidden, nullptr, nullptr)},
+                              h->x, IN_RMSNORM, w.ffn_norm, EPI_SWIGLU);
+        gu.layer = l;
+        P.push_back(gu);
+        Phase dn = gemv_phase(d.ffn, G, false, {seg_of(w.down, w.td, d.hidden, d.ffn, nullptr, h->x)}, h->ffn, IN_RAW,
+                              nullptr, EPI_RESID_ADD);
+        dn.layer = l;
+        P.push_back(dn);
+    }
+    Phase hd = gemv_phase(d.hidden, G, false, {seg_of(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)}, h->x,
+                          IN_RMSNORM, h->out_norm, EPI_LOGITS);
+    int rc = dalloc(h, &h->pmax, hd.n_items * sizeof(float));
+    if (rc) return rc;
+    if ((rc = dalloc(h, &h->pidx, hd.n_items * sizeof(uint32_t)))) return rc;
+    hd.partial_max = h->pmax;
+    hd.partial_idx = h->pidx;
+    const uint32_t head_index = (uint32_t)P.size();
+    P.push_back(hd);
+    Phase am{};
+    am.kind = PH_ARGMAX;
+    am.layer = head_index;
+    am.argmax_items = hd.n_items;
+    P.push_back(am);
+    rc = finalize_program(h, h->decode, h);
+    if (rc) return rc;
+    h->decode.pg.advance = 1;
+    return ATLAS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int atlas_cuda_device_info(int device, int *sm_count, int *cc_major, int *cc_minor)
+{
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return ATLAS_ENODEV;
+    cudaDeviceProp p{};
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return ATLAS_ENODEV;
+    if (sm_count) *sm_count = p.multiProcessorCount;
+    if (cc_major) *cc_major = p.major;
+    if (cc_minor) *cc_minor = p.minor;
+    return ATLAS_OK;
+}
+
+const char *atlas_cuda_last_error(const AtlasCuda *h) { return h ? h->err.c_str() : g_tls_error; }
+
+void atlas_cuda_destroy(AtlasCuda *h)
+{
+    if (!h) return;
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    for (void *p : h->allocs) cudaFree(p);
+    if (h->ev0) cudaEventDestroy(h->ev0);
+    if (h->ev1) cudaEventDestroy(h->ev1);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors, uint32_t n_tensors, AtlasCuda **out)
+{
+    if (!desc || !tensors || !out) return fail(nullptr, ATLAS_EINVAL, "null argument");
+    *out = nullptr;
+    int sms = 0;
+    if (device_ok(desc->device, &sms) != ATLAS_OK)
+        return fail(nullptr, ATLAS_ENODEV, "device %d is not an sm_100 GPU (or no CUDA device)", desc->device);
+    const AtlasModelDesc &d = *desc;
+    if (d.head_dim != (uint32_t)kHeadDim || !d.q_heads || !d.kv_heads || d.q_heads % d.kv_heads ||
+        d.q_heads / d.kv_heads > (uint32_t)kMaxGroup || d.q_dim != d.q_heads * d.head_dim ||
+        d.kv_dim != d.kv_heads * d.head_dim || d.hidden % 256 || d.ffn % 256 || d.q_dim % 256 || !d.layers ||
+        !d.vocab || d.max_context < 2)
+        return fail(nullptr, ATLAS_EINVAL, "unsupported model shape (head_dim must be 128, dims multiples of 256)");
+    if (d.has_qk_norm) return fail(nullptr, ATLAS_EINVAL, "qwen3 q/k norm is not supported yet");
+    if (d.tp_size > 1) return fail(nullptr, ATLAS_EINVAL, "tensor parallel handles are created by atlas_cuda_create_tp");
+    AtlasCuda *h = new AtlasCuda();
+    h->desc = d;
+    if (h->desc.rms_eps <= 0.f) h->desc.rms_eps = 1e-6f;
+    if (h->desc.rope_base <= 0.f) h->desc.rope_base = 1000000.0f;
+    if (!h->desc.max_prefill) h->desc.max_prefill = 512;
+    h->sm_count = sms;
+    int rc = ATLAS_OK;
+#define TRY(x) do { rc = (x); if (rc) { snprintf(g_tls_error, sizeof(g_tls_error), "%s", h->err.c_str()); atlas_cuda_destroy(h); return rc; } } while (0)
+    if (cudaSetDevice(d.device) != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "cudaSetDevice failed"));
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+        TRY(fail(h, ATLAS_ECUDA, "stream creation failed"));
+    cudaEventCreate(&h->ev0);
+    cudaEventCreate(&h->ev1);
+    char name[96];
+    const AtlasTensorDesc *emb = find(tensors, n_tensors, "token_embd.weight");
+    if (!emb) TRY(fail(h, ATLAS_EINVAL, "missing token_embd.weight"));
+    TRY(upload_matrix(h, emb, d.hidden, d.vocab, &h->embd, &h->t_embd));
+    const AtlasTensorDesc *outw = find(tensors, n_tensors, "output.weight");
+    if (!outw || (outw->data == emb->data && outw->type == emb->type)) {
+        h->head = h->embd;  // tied embeddings: one device copy
+        h->t_head = h->t_embd;
+    } else {
+        TRY(upload_matrix(h, outw, d.hidden, d.vocab, &h->head, &h->t_head));
+    }
+    TRY(upload_vector(h, find(tensors, n_tensors, "output_norm.weight"), d.hidden, &h->out_norm));
+    h->layers.resize(d.layers);
+    const size_t esz = d.kv_fp16 ? 2 : 4;
+    const size_t kv_layer = (size_t)d.kv_heads * d.max_context * d.head_dim * esz;
+    for (uint32_t l = 0; l < d.layers; ++l) {
+        AtlasCuda::W &w = h->layers[l];
+#define TN(suffix) (snprintf(name, sizeof(name), "blk.%u." suffix, l), find(tensors, n_tensors, name))
+        TRY(upload_matrix(h, TN("attn_q.weight"), d.hidden, d.q_dim, &w.q, &w.tq));
+        TRY(upload_matrix(h, TN("attn_k.weight"), d.hidden, d.kv_dim, &w.k, &w.tk));
+        TRY(upload_matrix(h, TN("attn_v.weight"), d.hidden, d.kv_dim, &w.v, &w.tv));
+        TRY(upload_matrix(h, TN("attn_output.weight"), d.q_dim, d.hidden, &w.o, &w.to));
+        TRY(upload_matrix(h, TN("ffn_gate.weight"), d.hidden, d.ffn, &w.gate, &w.tg));
+        TRY(upload_matrix(h, TN("ffn_up.weight"), d.hidden, d.ffn, &w.up, &w.tu));
+        TRY(upload_matrix(h, TN("ffn_down.weight"), d.ffn, d.hidden, &w.down, &w.td));
+        TRY(upload_vector(h, TN("attn_norm.weight"), d.hidden, &w.attn_norm));
+        TRY(upload_vector(h, TN("ffn_norm.weight"), d.hidden, &w.ffn_norm));
+        // optional_bias: absent biases are skipped (src/brain_runtime.c:1540-1546)
+        if (TN("attn_q.bias")) TRY(upload_vector(h, TN("attn_q.bias"), d.q_dim, &w.bq));
+        if (TN("attn_k.bias")) TRY(upload_vector(h, TN("attn_k.bias"), d.kv_dim, &w.bk));
+        if (TN("attn_v.bias")) TRY(upload_vector(h, TN("attn_v.bias"), d.kv_dim, &w.bv));
+#undef TN
+        TRY(dalloc(h, &w.kc, kv_layer));
+        TRY(dalloc(h, &w.vc, kv_layer));
+    }
+    uint32_t big = d.ffn > d.q_dim ? d.ffn : d.q_dim;
+    if (d.hidden > big) big = d.hidden;
+    TRY(dalloc(h, &h->x, d.hidden * 4));
+    TRY(dalloc(h, &h->q, d.q_dim * 4));
+    TRY(dalloc(h, &h->k, d.kv_dim * 4));
+    TRY(dalloc(h, &h->v, d.kv_dim * 4));
+    TRY(dalloc(h, &h->att, d.q_dim * 4));
+    TRY(dalloc(h, &h->ffn, (size_t)d.ffn * 4));
+    TRY(dalloc(h, &h->logits, (size_t)d.vocab * 4));
+    const uint32_t split = kStageBytes / (d.head_dim * (uint32_t)esz);
+    const size_t nsplit_max = (d.max_context + split - 1) / split + 1;
+    TRY(dalloc(h, &h->part, (size_t)d.kv_heads * nsplit_max * (d.q_heads / d.kv_heads) * (d.head_dim + 2) * 4));
+    TRY(dalloc(h, &h->split_ctr, 64 * sizeof(uint32_t) * (d.kv_heads + 1)));
+    if (cudaMemset(h->split_ctr, 0, 64 * sizeof(uint32_t) * (d.kv_heads + 1)) != cudaSuccess)
+        TRY(fail(h, ATLAS_ECUDA, "memset failed"));
+    // RoPE table: the reference's angle formula, evaluated with the host libm.
+    {
+        const uint32_t half = d.head_dim / 2;
+        std::vector<float2> tab((size_t)d.max_context * half);
+        std::vector<float> freq(half);
+        for (uint32_t p = 0; p < half; ++p)
+            freq[p] = powf(h->desc.rope_base, -(2.0f * (float)p) / (float)d.head_dim);
+        for (uint32_t pos = 0; pos < d.max_context; ++pos)
+            for (uint32_t p = 0; p < half; ++p) {
+                const float th = (float)pos * freq[p];
+                tab[(size_t)pos * half + p] = make_float2(cosf(th), sinf(th));
+            }
+        TRY(dalloc(h, &h->rope, tab.size() * sizeof(float2)));
+        if (cudaMemcpy(h->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+            TRY(fail(h, ATLAS_ECUDA, "rope upload failed"));
+    }
+    TRY(build_decode_program(h));
+    if (cudaDeviceSynchronize() != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "device sync failed"));
+#undef TRY
+    *out = h;
+    return ATLAS_OK;
+}
+
+int atlas_cuda_decode(AtlasCuda *h, uint32_t id, uint32_t pos, float *logits, uint32_t *argmax)
+{
+    if (!h) return fail(nullptr, ATLAS_EINVAL, "null handle");
+    if (id >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab %u", id, h->desc.vocab);
+    if (pos >= h->desc.max_context) return fail(h, ATLAS_ERANGE, "position %u >= max_context %u", pos, h->desc.max_context);
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    uint32_t next = 0;
+    int rc = run_decode(h, id, pos, 1, nullptr, &next, nullptr);
+    if (rc) return rc;
+    if (logits) {
+        CU(h, cudaMemcpyAsync(logits, h->logits, (size_t)h->desc.vocab * 4, cudaMemcpyDeviceToHost, h->stream));
+        CU(h, cudaStreamSynchronize(h->stream));
+    }
+    if (argmax) *argmax = next;
+    return ATLAS_OK;
+}
+
+int atlas_cuda_generate(AtlasCuda *h, uint32_t first, uint32_t pos0, uint32_t steps, uint32_t *out_ids)
+{
+    if (!h || !out_ids) return fail(h, ATLAS_EINVAL, "null argument");
+    if (!steps) return ATLAS_OK;
+    if (first >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab", first);
+    if ((uint64_t)pos0 + steps > h->desc.max_context) return fail(h, ATLAS_ERANGE, "positions exceed max_context");
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    if (steps > h->out_ids_cap) {
+        uint32_t *p = nullptr;
+        int rc = dalloc(h, &p, (size_t)steps * 4);
+        if (rc) return rc;
+        h->d_out_ids = p;
+        h->out_ids_cap = steps;
+    }
+    int rc = run_decode(h, first, pos0, steps, h->d_out_ids, nullptr, nullptr);
+    if (rc) return rc;
+    CU(h, cudaMemcpyAsync(out_ids, h->d_out_ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    return ATLAS_OK;
+}
+
+// Prefill: consecutive decode steps over the prompt (the reference's
+// token-at-a-time prefill, src/brain_runtime.c:2025-2028).
+int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0, float *last_logits,
+                       uint32_t *argmax)
+{
+    if (!h || !ids || !n) return fail(h, ATLAS_EINVAL, "empty prefill");
+    if ((uint64_t)pos0 + n > h->desc.max_context) return fail(h, ATLAS_ERANGE, "positions exceed max_context");
+    for (uint32_t i = 0; i < n; ++i) {
+        const bool last = i + 1 == n;
+        int rc = atlas_cuda_decode(h, ids[i], pos0 + i, last ? last_logits : nullptr, last ? argmax : nullptr);
+        if (rc) return rc;
+    }
+    return ATLAS_OK;
+}
+
+int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out_ns, size_t cap, uint32_t *n_ctas,
+                          uint32_t *n_phases, uint32_t *phase_kinds)
+{
+    if (!h) return fail(h, ATLAS_EINVAL, "null handle");
+    const size_t np = h->decode.phases.size(), need = (size_t)h->sm_count * np * 4;
+    if (n_ctas) *n_ctas = (uint32_t)h->sm_count;
+    if (n_phases) *n_phases = (uint32_t)np;
+    if (!out_ns) return fail(h, ATLAS_EINVAL, "null trace buffer");
+    if (phase_kinds)
+        for (size_t i = 0; i < np; ++i) phase_kinds[i] = h->decode.phases[i].kind * 16u + h->decode.phases[i].epilogue;
+    if (cap < need) return fail(h, ATLAS_EINVAL, "trace buffer needs %zu slots", need);
+    if (id >= h->desc.vocab || pos >= h->desc.max_context) return fail(h, ATLAS_ERANGE, "token or position out of range");
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    uint64_t *d = nullptr;
+    CU(h, cudaMalloc(&d, need * sizeof(uint64_t)));
+    h->decode.pg.trace = d;
+    int rc = run_decode(h, id, pos, 1, nullptr, nullptr, nullptr);
+    h->decode.pg.trace = nullptr;
+    if (rc == ATLAS_OK) {
+        cudaError_t e = cudaMemcpy(out_ns, d, need * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = fail(h, ATLAS_ECUDA, "trace readback: %s", cudaGetErrorString(e));
+    }
+    cudaFree(d);
+    return rc;
+}
+
+int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last_ms)
+{
+    if (!h) return ATLAS_EINVAL;
+    if (kernel_launches) *kernel_launches = h->launches;
+    if (last_ms) *last_ms = h->last_ms;
+    return ATLAS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Stateless kernels for parity tests
+// ---------------------------------------------------------------------------
+
+namespace {
+
+__global__ void dequant_kernel(uint32_t type, const uint8_t *blocks, uint64_t nblocks, float *out)
+{
+    const uint32_t be = block_elems(type), bb = block_bytes(type);
+    const uint64_t total = nblocks * be;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = deq_elem(type, blocks + (i / be) * bb, (int)(i % be));
+}
+
+struct GemvCtx {
+    int device = -1;
+    int sms = 0;
+    ProgramBuffers pb;
+};
+
+GemvCtx g_gemv_ctx[16];
+
+}  // namespace
+
+extern "C" int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, float *d_out, void *stream)
+{
+    if (!block_bytes(type) || !d_blocks || !d_out) return fail(nullptr, ATLAS_EINVAL, "bad dequant arguments");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (device_ok(dev, nullptr) != ATLAS_OK) return fail(nullptr, ATLAS_ENODEV, "no sm_100 device");
+    if (!nblocks) return ATLAS_OK;
+    dequant_kernel<<<592, 256, 0, (cudaStream_t)stream>>>(type, (const uint8_t *)d_blocks, nblocks, d_out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "dequant launch: %s", cudaGetErrorString(e));
+    return ATLAS_OK;
+}
+
+extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols, const float *d_x,
+                               float *d_y, void *stream)
+{
+    if ((type != ATLAS_TYPE_Q4_K && type != ATLAS_TYPE_Q6_K) || !d_weights || !d_x || !d_y || !rows || !cols ||
+        cols % 256 || rows > 0xffffffffu || cols > (uint64_t)kMaxSlices * 32 * 32 * kConsumerWarps)
+        return fail(nullptr, ATLAS_EINVAL, "bad gemv arguments");
+    if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
+        return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
+    if ((uintptr_t)d_weights & 1u) return fail(nullptr, ATLAS_EINVAL, "weights must be 2-byte aligned");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    if (dev < 0 || dev >= 16 || device_ok(dev, &sms) != ATLAS_OK) return fail(nullptr, ATLAS_ENODEV, "no sm_100 device");
+    GemvCtx &c = g_gemv_ctx[dev];
+    AtlasCuda tmp;  // error sink for the helpers
+    if (c.device != dev) {
+        c.device = dev;
+        c.sms = sms;
+        c.pb.phases.assign(1, Phase{});
+        // the program buffers live for the rest of the process
+        int rc = finalize_program(&tmp, c.pb, nullptr);
+        if (rc) { c.device = -1; return rc; }
+    }
+    Phase ph = gemv_phase((uint32_t)cols, (uint32_t)c.sms, false,
+                          {seg_of((const uint8_t *)d_weights, type, (uint32_t)rows, (uint32_t)cols, nullptr, d_y)},
+                          d_x, IN_RAW, nullptr, EPI_STORE);
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = cudaMemcpyAsync(c.pb.d_phases, &ph, sizeof(Phase), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = atlas_launch_decode(&c.pb.pg, c.sms, s);
+    if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
+    return ATLAS_OK;
+}
+
+extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols, const float *d_x,
+                               uint64_t tokens, float *d_y, void *stream)
+{
+    (void)type; (void)d_weights; (void)rows; (void)cols; (void)d_x; (void)tokens; (void)d_y; (void)stream;
+    return fail(nullptr, ATLAS_EINVAL, "the tcgen05 prefill GEMM is not built in this version");
+}

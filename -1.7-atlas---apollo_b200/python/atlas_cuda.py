@@ -1,0 +1,256 @@
+"""ctypes binding of libatlas_cuda's C ABI (include/atlas_cuda.h, include/atlas_runtime.h,
+include/gpu_matvec.h, include/atlas_synth.h).
+
+The library is the in-tree ``libatlas_cuda.so`` next to this package's ``csrc/``.
+Loading fails loudly when it is missing: there is no Python or CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libatlas_cuda.so")
+
+ATLAS_OK = 0
+ERRORS = {
+    -1: "EINVAL", -2: "ENODEV", -3: "ENOMEM", -4: "ECUDA", -5: "ETIMEOUT", -6: "ENCCL", -7: "ERANGE",
+}
+TYPE_F32, TYPE_F16, TYPE_Q5_0, TYPE_Q5_1, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 0, 1, 6, 7, 8, 12, 13, 14
+BLOCK_BYTES = {TYPE_F16: 2, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_Q8_0: 34, TYPE_Q4_K: 144, TYPE_Q5_K: 176,
+               TYPE_Q6_K: 210}
+BLOCK_ELEMS = {TYPE_F16: 1, TYPE_Q5_0: 32, TYPE_Q5_1: 32, TYPE_Q8_0: 32, TYPE_Q4_K: 256, TYPE_Q5_K: 256,
+               TYPE_Q6_K: 256}
+
+# Every symbol the public headers declare (checked by the CPU test suite).
+EXPORTS = [
+    "atlas_cuda_create", "atlas_cuda_destroy", "atlas_cuda_last_error", "atlas_cuda_prefill",
+    "atlas_cuda_decode", "atlas_cuda_generate", "atlas_cuda_stats", "atlas_cuda_dequant",
+    "atlas_cuda_gemv", "atlas_cuda_gemm", "atlas_cuda_device_info", "atlas_cuda_trace_step",
+    "brain_gpu_init", "brain_gpu_matvec_batch", "brain_gpu_matvec", "brain_gpu_shutdown",
+    "atlas_rt_open", "atlas_rt_close", "atlas_rt_error", "atlas_rt_shape", "atlas_rt_data_base",
+    "atlas_rt_find_tensor", "atlas_rt_file_bytes", "atlas_rt_device", "atlas_rt_forward_token",
+    "atlas_rt_prefill", "atlas_rt_generate",
+    "atlas_synth_write_gguf", "atlas_synth_q4k_blocks", "atlas_synth_q6k_blocks", "atlas_synth_file_size",
+]
+
+
+class AtlasError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class SynthConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                ("hidden", "layers", "q_heads", "kv_heads", "head_dim", "ffn", "vocab", "context_length")] + [
+        ("rope_base", ctypes.c_float), ("tied", ctypes.c_int32), ("qkv_bias", ctypes.c_int32),
+        ("threads", ctypes.c_int32), ("seed", ctypes.c_uint64)]
+
+
+class Shape(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                ("hidden_size", "q_dim", "kv_dim", "q_heads", "kv_heads", "head_dim", "ffn_size", "layers",
+                 "max_context", "vocab_size")] + [
+        ("rope_base", ctypes.c_float), ("has_qk_norm", ctypes.c_int32), ("architecture", ctypes.c_char * 64)]
+
+
+class TensorInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 256), ("n_dims", ctypes.c_uint32), ("dims", ctypes.c_uint64 * 4),
+                ("type", ctypes.c_uint32), ("offset", ctypes.c_uint64)]
+
+
+class RtOptions(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("max_context", ctypes.c_uint32), ("max_prefill", ctypes.c_uint32),
+                ("kv_fp16", ctypes.c_int32), ("no_device", ctypes.c_int32)]
+
+
+class BrainGpuMatvec(ctypes.Structure):
+    _fields_ = [("offset", ctypes.c_uint64), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64),
+                ("type", ctypes.c_uint32), ("input", ctypes.c_void_p), ("output", ctypes.c_void_p)]
+
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the in-tree library (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} is missing: build it with __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+        P, U32, U64, I32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
+        L.atlas_cuda_last_error.restype = ctypes.c_char_p
+        L.atlas_cuda_last_error.argtypes = [P]
+        L.atlas_cuda_dequant.argtypes = [U32, P, U64, P, P]
+        L.atlas_cuda_gemv.argtypes = [U32, P, U64, U64, P, P, P]
+        L.atlas_cuda_gemm.argtypes = [U32, P, U64, U64, P, U64, P, P]
+        L.atlas_cuda_device_info.argtypes = [I32, P, P, P]
+        L.atlas_cuda_decode.argtypes = [P, U32, U32, P, P]
+        L.atlas_cuda_prefill.argtypes = [P, P, U32, U32, P, P]
+        L.atlas_cuda_generate.argtypes = [P, U32, U32, U32, P]
+        L.atlas_cuda_stats.argtypes = [P, P, P]
+        L.atlas_cuda_trace_step.argtypes = [P, U32, U32, P, ctypes.c_size_t, P, P, P]
+        L.atlas_rt_open.argtypes = [ctypes.c_char_p, P, P]
+        L.atlas_rt_close.argtypes = [P]
+        L.atlas_rt_error.restype = ctypes.c_char_p
+        L.atlas_rt_error.argtypes = [P]
+        L.atlas_rt_shape.argtypes = [P, P]
+        L.atlas_rt_data_base.restype = U64
+        L.atlas_rt_data_base.argtypes = [P]
+        L.atlas_rt_find_tensor.argtypes = [P, ctypes.c_char_p, P]
+        L.atlas_rt_file_bytes.restype = P
+        L.atlas_rt_file_bytes.argtypes = [P, P]
+        L.atlas_rt_device.restype = P
+        L.atlas_rt_device.argtypes = [P]
+        L.atlas_rt_forward_token.argtypes = [P, U32, U32, P, P]
+        L.atlas_rt_prefill.argtypes = [P, P, U32, U32, P, P]
+        L.atlas_rt_generate.argtypes = [P, U32, U32, U32, P]
+        L.atlas_synth_write_gguf.argtypes = [P, ctypes.c_char_p]
+        L.atlas_synth_q4k_blocks.argtypes = [U64, U64, P, U64]
+        L.atlas_synth_q6k_blocks.argtypes = [U64, U64, P, U64]
+        L.atlas_synth_file_size.restype = U64
+        L.atlas_synth_file_size.argtypes = [P]
+        L.brain_gpu_init.argtypes = [P, ctypes.c_size_t]
+        L.brain_gpu_matvec_batch.argtypes = [P, ctypes.c_size_t]
+        L.brain_gpu_matvec.argtypes = [U64, U32, U64, U64, P, P]
+        _LIB = L
+    return _LIB
+
+
+def check(rc: int, where: str = "", handle=None) -> None:
+    if rc != ATLAS_OK:
+        msg = lib().atlas_cuda_last_error(handle)
+        raise AtlasError(rc, f"{where}: {msg.decode() if msg else ''}")
+
+
+def _ptr(a) -> ctypes.c_void_p:
+    """Host numpy array or device torch tensor -> void*."""
+    if a is None:
+        return ctypes.c_void_p(0)
+    if hasattr(a, "data_ptr"):
+        return ctypes.c_void_p(a.data_ptr())
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def write_synthetic_gguf(path: str, *, hidden: int, layers: int, q_heads: int, kv_heads: int, ffn: int, vocab: int,
+                         head_dim: int = 128, context_length: int = 32768, rope_base: float = 1e6,
+                         tied: bool = True, qkv_bias: bool = True, seed: int = 0, threads: int = 0) -> int:
+    cfg = SynthConfig(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, context_length, rope_base,
+                      int(tied), int(qkv_bias), threads, seed)
+    rc = lib().atlas_synth_write_gguf(ctypes.byref(cfg), path.encode())
+    if rc != 0:
+        raise RuntimeError(f"synthetic GGUF write failed: {path}")
+    return lib().atlas_synth_file_size(ctypes.byref(cfg))
+
+
+def synth_blocks(type_id: int, n: int, seed: int = 0, stream: int = 0):
+    import numpy as np
+    out = np.zeros(n * BLOCK_BYTES[type_id], np.uint8)
+    fn = lib().atlas_synth_q4k_blocks if type_id == TYPE_Q4_K else lib().atlas_synth_q6k_blocks
+    fn(seed, stream, _ptr(out), n)
+    return out
+
+
+class Runtime:
+    """Reference-shaped model API: open a GGUF, forward tokens, prefill, generate."""
+
+    def __init__(self, path: str, *, device: int = 0, max_context: int = 0, max_prefill: int = 0,
+                 kv_fp16: bool = False, no_device: bool = False):
+        self._h = ctypes.c_void_p()
+        opt = RtOptions(device, max_context, max_prefill, int(kv_fp16), int(no_device))
+        rc = lib().atlas_rt_open(path.encode(), ctypes.byref(opt), ctypes.byref(self._h))
+        if rc != ATLAS_OK:
+            msg = lib().atlas_rt_error(self._h).decode()
+            lib().atlas_rt_close(self._h)
+            self._h = None
+            raise AtlasError(rc, f"atlas_rt_open({path}): {msg}")
+        s = Shape()
+        lib().atlas_rt_shape(self._h, ctypes.byref(s))
+        self.shape = s
+        self.vocab = s.vocab_size
+
+    def _check(self, rc: int, where: str) -> None:
+        if rc != ATLAS_OK:
+            raise AtlasError(rc, f"{where}: {lib().atlas_rt_error(self._h).decode()}")
+
+    def tensor(self, name: str) -> TensorInfo | None:
+        t = TensorInfo()
+        return t if lib().atlas_rt_find_tensor(self._h, name.encode(), ctypes.byref(t)) else None
+
+    @property
+    def data_base(self) -> int:
+        return lib().atlas_rt_data_base(self._h)
+
+    def forward(self, token: int, pos: int, want_logits: bool = True):
+        import numpy as np
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        am = ctypes.c_uint32()
+        self._check(lib().atlas_rt_forward_token(self._h, token, pos, _ptr(logits), ctypes.byref(am)), "forward")
+        return logits, am.value
+
+    def prefill(self, ids, pos0: int = 0, want_logits: bool = True):
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        am = ctypes.c_uint32()
+        self._check(lib().atlas_rt_prefill(self._h, _ptr(ids), len(ids), pos0, _ptr(logits), ctypes.byref(am)),
+                    "prefill")
+        return logits, am.value
+
+    def generate(self, first: int, pos0: int, steps: int):
+        import numpy as np
+        out = np.zeros(steps, np.uint32)
+        self._check(lib().atlas_rt_generate(self._h, first, pos0, steps, _ptr(out)), "generate")
+        return out
+
+    def trace_step(self, token: int, pos: int):
+        """One traced decode step: (stamps[cta, phase, 4] in ns, phase kind codes)."""
+        import numpy as np
+        dev = lib().atlas_rt_device(self._h)
+        nc, nph = ctypes.c_uint32(), ctypes.c_uint32()
+        lib().atlas_cuda_trace_step(dev, token, pos, None, 0, ctypes.byref(nc), ctypes.byref(nph), None)
+        buf = np.zeros(nc.value * nph.value * 4, np.uint64)
+        kinds = np.zeros(nph.value, np.uint32)
+        check(lib().atlas_cuda_trace_step(dev, token, pos, _ptr(buf), buf.size, ctypes.byref(nc), ctypes.byref(nph),
+                                          _ptr(kinds)), "trace_step", dev)
+        return buf.reshape(nc.value, nph.value, 4), kinds
+
+    def stats(self):
+        n = ctypes.c_uint64()
+        ms = ctypes.c_double()
+        lib().atlas_cuda_stats(lib().atlas_rt_device(self._h), ctypes.byref(n), ctypes.byref(ms))
+        return n.value, ms.value
+
+    def close(self) -> None:
+        if self._h:
+            lib().atlas_rt_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dequant(type_id: int, d_blocks, nblocks: int, d_out, stream: int = 0) -> None:
+    check(lib().atlas_cuda_dequant(type_id, _ptr(d_blocks), nblocks, _ptr(d_out), ctypes.c_void_p(stream)),
+          "atlas_cuda_dequant")
+
+
+def gemv(type_id: int, d_w, rows: int, cols: int, d_x, d_y, stream: int = 0) -> None:
+    check(lib().atlas_cuda_gemv(type_id, _ptr(d_w), rows, cols, _ptr(d_x), _ptr(d_y), ctypes.c_void_p(stream)),
+          "atlas_cuda_gemv")
+
+
+def gemm(type_id: int, d_w, rows: int, cols: int, d_x, tokens: int, d_y, stream: int = 0) -> None:
+    check(lib().atlas_cuda_gemm(type_id, _ptr(d_w), rows, cols, _ptr(d_x), tokens, _ptr(d_y),
+                                ctypes.c_void_p(stream)), "atlas_cuda_gemm")

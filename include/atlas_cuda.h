@@ -1,0 +1,145 @@
+/*
+ * libatlas_cuda: B200 (sm_100a) inference library for Qwen2-family models with
+ * raw GGUF Q4_K / Q6_K weights. Plain C ABI: pointers and sizes only.
+ *
+ * This is the wider device boundary under the reference's model/forward API
+ * (src/brain_runtime.c:1698 forward_token; src/brain_runtime_batch.c:1644
+ * forward_prefill_batch). The reference's own narrow device plugin
+ * (src/gpu_matvec.h:13-17) is provided unchanged in include/gpu_matvec.h.
+ *
+ * Conventions
+ *  - Every int-returning function returns ATLAS_OK (0) on success and a
+ *    negative ATLAS_E* code on failure; atlas_cuda_last_error() gives the text.
+ *    Nothing exits the process, nothing traps, and there is no CPU fallback:
+ *    without a usable sm_100 device every call fails with ATLAS_ENODEV.
+ *  - A handle is used by one host thread at a time. Host buffers passed in are
+ *    only read during the call; output buffers are written before return.
+ *  - Weight bytes are uploaded unchanged (144-byte Q4_K and 210-byte Q6_K
+ *    super-blocks, rows in file order).
+ */
+#ifndef ATLAS_CUDA_H
+#define ATLAS_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ATLAS_OK = 0,
+    ATLAS_EINVAL = -1,   /* bad argument or unsupported shape / tensor type */
+    ATLAS_ENODEV = -2,   /* no sm_100 CUDA device */
+    ATLAS_ENOMEM = -3,   /* device or host allocation failed */
+    ATLAS_ECUDA = -4,    /* a CUDA runtime call failed */
+    ATLAS_ETIMEOUT = -5, /* a bounded device-side wait ran out (status read back, context intact) */
+    ATLAS_ENCCL = -6,    /* a collective failed */
+    ATLAS_ERANGE = -7    /* position / token / size beyond what the handle was created for */
+};
+
+/* ggml tensor type ids as used by the reference (src/brain_runtime.c:79-86). */
+enum {
+    ATLAS_TYPE_F32 = 0,
+    ATLAS_TYPE_F16 = 1,
+    ATLAS_TYPE_Q5_0 = 6,
+    ATLAS_TYPE_Q5_1 = 7,
+    ATLAS_TYPE_Q8_0 = 8,
+    ATLAS_TYPE_Q4_K = 12,
+    ATLAS_TYPE_Q5_K = 13,
+    ATLAS_TYPE_Q6_K = 14
+};
+
+typedef struct AtlasCuda AtlasCuda;
+
+/* One GGUF tensor as the host loader found it (TensorInfo, src/brain_runtime.c:138-144).
+   dims[0] is the inner (column) extent, dims[1] the rows. `data` points at the
+   tensor's bytes in host memory (for example into an mmap of the file). */
+typedef struct {
+    const char *name;
+    uint32_t type;
+    uint32_t n_dims;
+    uint64_t dims[4];
+    const void *data;
+} AtlasTensorDesc;
+
+/* Model shape (ModelShape, src/brain_runtime.c:93-99) plus placement. */
+typedef struct {
+    uint32_t hidden, q_dim, kv_dim, q_heads, kv_heads, head_dim, ffn, layers, vocab;
+    uint32_t max_context;  /* KV-cache positions to allocate (no 8192 cap) */
+    uint32_t max_prefill;  /* largest prefill call, in tokens (0: 512) */
+    float rope_base;       /* rope.freq_base, default 1e6 */
+    float rms_eps;         /* 1e-6 in the reference (src/brain_runtime.c:115) */
+    int32_t has_qk_norm;   /* qwen3 per-head q/k RMSNorm (src/brain_runtime.c:1727-1737) */
+    int32_t kv_fp16;       /* 0: fp32 KV cache (default), 1: fp16 KV cache (see below) */
+    int32_t device;        /* CUDA device ordinal */
+    int32_t tp_rank;       /* tensor-parallel rank, 0..tp_size-1 */
+    int32_t tp_size;       /* 1, 2, 4 or 8; >1 needs nccl_comm */
+    void *nccl_comm;       /* ncclComm_t spanning the tp_size ranks, or NULL */
+} AtlasModelDesc;
+
+/* KV-cache precision: the reference keeps K and V in fp32 (src/brain_runtime.c:2019-2020).
+   fp16 halves the cache traffic, but on models whose attention logits are large
+   (the synthetic random-weight models reach |score| ~ 100s) its 2^-11 rounding of
+   K moves scores by ~0.1 and can change a peaked softmax, so fp32 is the default.
+
+   Uploads the tensors named by the reference's forward_token and builds the
+   decode program. Tied models may omit output.weight (token_embd is used). */
+int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors,
+                      uint32_t n_tensors, AtlasCuda **out);
+void atlas_cuda_destroy(AtlasCuda *h);
+const char *atlas_cuda_last_error(const AtlasCuda *h);
+
+/* Batched prefill of ids[0..n) at positions pos0..pos0+n-1 (as consecutive
+   forward_token calls would, src/brain_runtime.c:2025-2028). Optionally returns
+   the last token's logits (vocab floats, host) and its greedy pick. */
+int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0,
+                       float *last_logits, uint32_t *argmax);
+
+/* One decode step: forward_token(id, pos) then the greedy pick of
+   atlas_sample_token (src/brain_runtime.c:1783, greedy branch). logits may be NULL. */
+int atlas_cuda_decode(AtlasCuda *h, uint32_t id, uint32_t pos, float *logits, uint32_t *argmax);
+
+/* Greedy generation loop kept on the device: starting from token `first` at
+   position pos0, runs `steps` forward passes; out_ids[i] is the greedy pick after
+   step i (the reference's decode loop, src/brain_runtime.c:2036-2048, without
+   the stop-token test). */
+int atlas_cuda_generate(AtlasCuda *h, uint32_t first, uint32_t pos0, uint32_t steps,
+                        uint32_t *out_ids);
+
+/* Per-phase device time of the last decode/generate call and kernel launch
+   counts since creation (diagnostics for the benchmark). */
+int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last_ms);
+
+/* Diagnostics: runs one decode step of (id, pos) with device-side timestamps.
+   Fills out_ns (host) with n_ctas * n_phases * 4 globaltimer values per CTA and
+   phase: [wait start, wait end, phase end, producer done]; n_ctas / n_phases
+   receive the dimensions. cap is the number of uint64 slots in out_ns. */
+int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out_ns, size_t cap,
+                          uint32_t *n_ctas, uint32_t *n_phases, uint32_t *phase_kinds);
+
+/* ---- stateless kernels over caller-owned DEVICE memory (parity tests) ---- */
+
+/* Bit-exact dequantization of nblocks super-blocks (the reference's
+   dequant_q4_k / dequant_q6_k, src/brain_runtime.c:960 / :1049).
+   stream is a cudaStream_t or NULL for the default stream. */
+int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, float *d_out,
+                       void *stream);
+
+/* y[rows] = W[rows x cols] x[cols] for a Q4_K / Q6_K tensor in device memory
+   (the decode GEMV engine; matvec_rows, src/brain_runtime.c:1133). */
+int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
+                    const float *d_x, float *d_y, void *stream);
+
+/* Y[tokens x rows] = X[tokens x cols] W^T through the tcgen05 prefill GEMM
+   (batch_matvec_rows, src/brain_runtime_batch.c:1525): X fp32 in, fp16
+   operand tiles, fp32 accumulation. */
+int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
+                    const float *d_x, uint64_t tokens, float *d_y, void *stream);
+
+/* Number of SMs / compute capability of `device`, or a negative code. */
+int atlas_cuda_device_info(int device, int *sm_count, int *cc_major, int *cc_minor);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,111 @@
+"""GPU: end-to-end parity of the decode engine against the reference.
+
+Bar (the contract for this path): final logits within
+max|dlogit| <= 2e-2 * max|logit| of the reference CPU path, and identical greedy
+tokens for the first 32 steps. fp32 activations and fp32 KV cache (the default; the fp16 cache is an option
+whose parity these random-weight models do not support, see atlas_cuda.h)."""
+import os
+
+import numpy as np
+import pytest
+
+import atlas_cuda
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = 2e-2
+
+
+def _close(got, want, tol=TOL):
+    err = np.abs(got.astype(np.float64) - want).max()
+    bound = tol * np.abs(want).max()
+    assert err <= bound, f"max|dlogit| {err} > {bound}"
+    return err / np.abs(want).max()
+
+
+def test_tiny_matches_golden(torch_cuda, tiny_model):
+    g = np.load(os.path.join(GOLDEN, "tiny.npz"))
+    with atlas_cuda.Runtime(tiny_model, max_context=256) as rt:
+        prompt = g["prompt"]
+        for i, t in enumerate(prompt):
+            lg, am = rt.forward(int(t), i)
+            rel = _close(lg, g["logits"][i])
+            assert rel < 1e-3
+        picks = rt.generate(int(g["picks"][0]), len(prompt), 32)
+        # generate() returns the pick after each forward: picks[1:] of the reference
+        np.testing.assert_array_equal(picks[:31], g["picks"][1:32])
+        assert am == int(g["picks"][0])
+
+
+def test_tiny_untied_matches_oracle(torch_cuda, oracle, tiny_untied_model):
+    m = oracle.open(tiny_untied_model)
+    m.begin(128)
+    with atlas_cuda.Runtime(tiny_untied_model, max_context=128) as rt:
+        for pos, tok in enumerate([1, 900, 44, 1000, 2, 17, 17, 17]):
+            want = m.forward(tok, pos)
+            got, am = rt.forward(tok, pos)
+            _close(got, want, 1e-3)
+            assert am == m.argmax(want)
+
+
+def test_small_prefill_generate_matches_oracle(torch_cuda, oracle, small_model):
+    m = oracle.open(small_model)
+    m.begin(128)
+    prompt = np.random.default_rng(1).integers(0, 4096, 40).astype(np.uint32)
+    for i, t in enumerate(prompt):
+        want = m.forward(int(t), i, i + 1 == len(prompt))
+    want_picks = []
+    lg = want
+    for s in range(32):
+        nxt = m.argmax(lg)
+        want_picks.append(nxt)
+        lg = m.forward(nxt, len(prompt) + s)
+    with atlas_cuda.Runtime(small_model, max_context=128) as rt:
+        got, am = rt.prefill(prompt)
+        _close(got, want, 1e-3)
+        assert am == want_picks[0]
+        picks = rt.generate(am, len(prompt), 31)
+        np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
+
+
+def test_generate_equals_forward_loop(torch_cuda, small_model):
+    with atlas_cuda.Runtime(small_model, max_context=64) as rt:
+        _, am = rt.prefill(np.arange(10, 30, dtype=np.uint32))
+        a = rt.generate(am, 20, 12)
+        _, am2 = rt.prefill(np.arange(10, 30, dtype=np.uint32))
+        b = [am2]
+        for s in range(12):
+            _, nxt = rt.forward(b[-1], 20 + s)
+            b.append(nxt)
+        np.testing.assert_array_equal(a, np.array(b[1:], np.uint32))
+
+
+def test_range_errors(torch_cuda, tiny_model):
+    with atlas_cuda.Runtime(tiny_model, max_context=32) as rt:
+        with pytest.raises(atlas_cuda.AtlasError):
+            rt.forward(5, 32)                       # position beyond the KV cache
+        with pytest.raises(atlas_cuda.AtlasError):
+            rt.forward(1024, 0)                     # token >= vocab
+        with pytest.raises(atlas_cuda.AtlasError):
+            rt.prefill(np.zeros(0, np.uint32))      # empty prefill
+        rt.forward(5, 0)                            # the handle still works
+
+
+@pytest.mark.slow
+def test_cfg0_full_size_matches_reference(torch_cuda, model_dir):
+    """Qwen2-1.5B shape, 32-token prompt + 32 greedy steps vs the reference's own run."""
+    g = np.load(os.path.join(GOLDEN, "cfg0.npz"))
+    cfg = {k[4:]: int(g[k]) for k in g.files if k.startswith("cfg_")}
+    p = os.path.join(str(model_dir), "cfg0.gguf")
+    if not os.path.exists(p):
+        atlas_cuda.write_synthetic_gguf(p, tied=True, **cfg)
+    with atlas_cuda.Runtime(p, max_context=512) as rt:
+        prompt = g["prompt"]
+        lg, am = rt.prefill(prompt)
+        _close(lg, g["logits_prompt"].astype(np.float32))
+        assert am == int(g["picks"][0])
+        lg1, am1 = rt.forward(am, len(prompt))
+        _close(lg1, g["logits_step1"].astype(np.float32))
+        picks = rt.generate(am1, len(prompt) + 1, 30)
+        got = np.concatenate([[am, am1], picks]).astype(np.uint32)
+        np.testing.assert_array_equal(got, g["picks"])
