@@ -5,24 +5,28 @@
 // same list: for each phase it processes the work items i with
 // i % gridDim.x == blockIdx.x, then arrives on that phase's counter; before its
 // first item of a phase it waits until every CTA has arrived on the previous
-// phase's counter. A producer warp streams each item's weight (or KV-cache)
-// bytes into a shared-memory ring with 1-D bulk copies, running ahead across
-// phase boundaries because weights never depend on activations; consumer
-// warps wait only for the activations.
+// phase's counter. Each item's weight (or KV-cache) bytes are streamed into a
+// shared-memory ring with 1-D bulk copies issued ahead of use - across phase
+// boundaries too, because weights never depend on activations - so the warps
+// wait only for the activations.
 #pragma once
 #include <cstdint>
 
 namespace atlas {
 
+// 8 warps: two per SM sub-partition, which lets each thread hold up to 255
+// registers (the per-lane input slices live in registers). The bulk copies
+// are issued by thread 0 in between its own work (see the "pump" in decode.cu).
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kThreads = kConsumerWarps * 32;
 constexpr int kStages = 6;
 constexpr uint32_t kStageBytes = 32768;
 constexpr int kMaxSlices = 4;        // per-lane x slices held in registers
 constexpr int kMaxItemRows = 64;     // rows of one segment in one item
 constexpr int kMaxSeg = 3;
 constexpr int kHeadDim = 128;
-constexpr int kAttnSplit = 128;      // positions per attention work item (one fp16 stage)
+constexpr int kAttnChunk = 64;       // cached positions per staged K (or V) chunk
+constexpr int kMaxSplits = 128;      // attention splits per KV head
 constexpr int kMaxGroup = 16;        // query heads per KV head
 
 enum PhaseKind : uint32_t {
@@ -76,7 +80,7 @@ struct Phase {
     const float *q, *k, *v; // fresh projections (bias added, RoPE not yet applied)
     void *k_cache, *v_cache;// this layer's cache, [kv_head][position][head_dim]
     float *att;             // output, q_dim floats
-    float *part;            // split partials: [kv_head][split][group][head_dim + 2]
+    float *part;            // split partials: [kv_head][split][group][head_dim + 4]
     uint32_t *split_ctr;    // per KV head arrival counters (reset by the combiner)
     // ---- PH_EMBED ----
     const uint8_t *embd;    // token_embd raw rows

@@ -71,6 +71,7 @@ struct AtlasCuda {
     ProgramBuffers decode;
     uint64_t launches = 0;
     double last_ms = 0.0;
+    double total_ms = 0.0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 };
 
@@ -95,14 +96,25 @@ int fail(AtlasCuda *h, int code, const char *fmt, ...)
             return fail((h), ATLAS_ECUDA, "%s failed: %s", #call, cudaGetErrorString(e_));   \
     } while (0)
 
+// Device check with a per-device cache (cudaGetDeviceProperties costs
+// milliseconds; the attribute queries are cheap and asked once).
 int device_ok(int device, int *sms)
 {
-    int n = 0;
-    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0 || device < 0 || device >= n) return ATLAS_ENODEV;
-    cudaDeviceProp p{};
-    if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return ATLAS_ENODEV;
-    if (p.major != 10) return ATLAS_ENODEV;
-    if (sms) *sms = p.multiProcessorCount;
+    static int cached_sms[64];
+    static int cached_major[64];
+    if (device < 0 || device >= 64) return ATLAS_ENODEV;
+    if (!cached_major[device]) {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0 || device >= n) return ATLAS_ENODEV;
+        int major = 0, count = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+            cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+            return ATLAS_ENODEV;
+        cached_sms[device] = count;
+        cached_major[device] = major;
+    }
+    if (cached_major[device] != 10) return ATLAS_ENODEV;
+    if (sms) *sms = cached_sms[device];
     return ATLAS_OK;
 }
 
@@ -330,6 +342,7 @@ int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
     float ms = 0.f;
     cudaEventElapsedTime(&ms, h->ev0, h->ev1);
     h->last_ms = ms;
+    h->total_ms += ms;
     if (out.status != kStatusOk) {
         const int rc = status_to_code(h, out.status);
         reset_program(h, pb);
@@ -507,9 +520,9 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     TRY(dalloc(h, &h->att, d.q_dim * 4));
     TRY(dalloc(h, &h->ffn, (size_t)d.ffn * 4));
     TRY(dalloc(h, &h->logits, (size_t)d.vocab * 4));
-    const uint32_t split = kStageBytes / (d.head_dim * (uint32_t)esz);
-    const size_t nsplit_max = (d.max_context + split - 1) / split + 1;
-    TRY(dalloc(h, &h->part, (size_t)d.kv_heads * nsplit_max * (d.q_heads / d.kv_heads) * (d.head_dim + 2) * 4));
+    size_t nsplit_max = (d.max_context + kAttnChunk - 1) / kAttnChunk + 1;
+    if (nsplit_max > (size_t)kMaxSplits) nsplit_max = kMaxSplits;
+    TRY(dalloc(h, &h->part, (size_t)d.kv_heads * nsplit_max * (d.q_heads / d.kv_heads) * (d.head_dim + 4) * 4));
     TRY(dalloc(h, &h->split_ctr, 64 * sizeof(uint32_t) * (d.kv_heads + 1)));
     if (cudaMemset(h->split_ctr, 0, 64 * sizeof(uint32_t) * (d.kv_heads + 1)) != cudaSuccess)
         TRY(fail(h, ATLAS_ECUDA, "memset failed"));
@@ -623,6 +636,13 @@ int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last
     return ATLAS_OK;
 }
 
+int atlas_cuda_device_ms(const AtlasCuda *h, double *total_ms)
+{
+    if (!h || !total_ms) return ATLAS_EINVAL;
+    *total_ms = h->total_ms;
+    return ATLAS_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
@@ -671,6 +691,8 @@ extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t ro
     if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
         return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
     if ((uintptr_t)d_weights & 1u) return fail(nullptr, ATLAS_EINVAL, "weights must be 2-byte aligned");
+    if (((uintptr_t)d_x & 15u) || ((uintptr_t)d_y & 3u))
+        return fail(nullptr, ATLAS_EINVAL, "x must be 16-byte aligned and y 4-byte aligned");
     int dev = 0;
     cudaGetDevice(&dev);
     int sms = 0;

@@ -27,6 +27,7 @@ EXPORTS = [
     "atlas_cuda_create", "atlas_cuda_destroy", "atlas_cuda_last_error", "atlas_cuda_prefill",
     "atlas_cuda_decode", "atlas_cuda_generate", "atlas_cuda_stats", "atlas_cuda_dequant",
     "atlas_cuda_gemv", "atlas_cuda_gemm", "atlas_cuda_device_info", "atlas_cuda_trace_step",
+    "atlas_cuda_device_ms",
     "brain_gpu_init", "brain_gpu_matvec_batch", "brain_gpu_matvec", "brain_gpu_shutdown",
     "atlas_rt_open", "atlas_rt_close", "atlas_rt_error", "atlas_rt_shape", "atlas_rt_data_base",
     "atlas_rt_find_tensor", "atlas_rt_file_bytes", "atlas_rt_device", "atlas_rt_forward_token",
@@ -91,6 +92,7 @@ def lib() -> ctypes.CDLL:
         L.atlas_cuda_prefill.argtypes = [P, P, U32, U32, P, P]
         L.atlas_cuda_generate.argtypes = [P, U32, U32, U32, P]
         L.atlas_cuda_stats.argtypes = [P, P, P]
+        L.atlas_cuda_device_ms.argtypes = [P, P]
         L.atlas_cuda_trace_step.argtypes = [P, U32, U32, P, ctypes.c_size_t, P, P, P]
         L.atlas_rt_open.argtypes = [ctypes.c_char_p, P, P]
         L.atlas_rt_close.argtypes = [P]
@@ -218,10 +220,14 @@ class Runtime:
         return buf.reshape(nc.value, nph.value, 4), kinds
 
     def stats(self):
+        """(kernel launches since creation, device ms of the last call, device ms of all calls)."""
         n = ctypes.c_uint64()
         ms = ctypes.c_double()
-        lib().atlas_cuda_stats(lib().atlas_rt_device(self._h), ctypes.byref(n), ctypes.byref(ms))
-        return n.value, ms.value
+        tot = ctypes.c_double()
+        dev = lib().atlas_rt_device(self._h)
+        lib().atlas_cuda_stats(dev, ctypes.byref(n), ctypes.byref(ms))
+        lib().atlas_cuda_device_ms(dev, ctypes.byref(tot))
+        return n.value, ms.value, tot.value
 
     def close(self) -> None:
         if self._h:

@@ -110,6 +110,10 @@ int atlas_cuda_generate(AtlasCuda *h, uint32_t first, uint32_t pos0, uint32_t st
    counts since creation (diagnostics for the benchmark). */
 int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last_ms);
 
+/* Device time (CUDA events on the handle's stream) summed over every decode /
+   generate / prefill call since creation. */
+int atlas_cuda_device_ms(const AtlasCuda *h, double *total_ms);
+
 /* Diagnostics: runs one decode step of (id, pos) with device-side timestamps.
    Fills out_ns (host) with n_ctas * n_phases * 4 globaltimer values per CTA and
    phase: [wait start, wait end, phase end, producer done]; n_ctas / n_phases
@@ -126,7 +130,11 @@ int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, fl
                        void *stream);
 
 /* y[rows] = W[rows x cols] x[cols] for a Q4_K / Q6_K tensor in device memory
-   (the decode GEMV engine; matvec_rows, src/brain_runtime.c:1133). */
+   (the decode GEMV engine; matvec_rows, src/brain_runtime.c:1133).
+   d_weights: 16-byte aligned for Q4_K, 2-byte for Q6_K; the engine's bulk copies
+   read up to 15 bytes past the last row, which cudaMalloc'd buffers always allow.
+   d_x 16-byte aligned. Calls from several host threads or streams at once are
+   not supported (the kernel's descriptor lives in one per-device buffer). */
 int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                     const float *d_x, float *d_y, void *stream);
 
