@@ -2,17 +2,32 @@
 // reference's forward_token, src/brain_runtime.c:1698-1772, plus the greedy
 // pick of atlas_sample_token :1783) as a program of phases (engine.h).
 //
-// Per CTA (8 warps)
-//   * the pump (thread 0, called between its own work and inside every wait
-//     loop): walks the CTA's work items of every phase in order and issues 1-D
-//     bulk copies (cp.async.bulk, TMA) of their raw weight rows / KV-cache tiles
-//     into a kStages-deep shared-memory ring, limited only by free ring slots -
-//     never by activations - so weight streaming continues across phase
-//     boundaries;
-//   * all warps: wait for the previous phase's counter (acquire), load this
-//     phase's activation vector into registers, and consume the staged bytes:
-//     Q4_K/Q6_K decode + fp32 FMA + warp-shuffle row reductions, or
-//     flash-decode attention; then release the phase counter.
+// Warp roles per CTA
+//   warp 8 (producer): one lane walks the CTA's work items of every phase in
+//     order and issues 1-D bulk copies (cp.async.bulk) of their raw weight
+//     rows / KV-cache tiles into an n_stages-deep shared-memory ring, limited
+//     only by free ring slots - never by activations - so weight streaming
+//     continues across phase boundaries;
+//   warps 0-7 (consumers): wait for the previous phase's counter (acquire),
+//     stage the phase's input vector in shared memory, consume the staged
+//     bytes and release the phase counter.
+//
+// GEMV on tensor cores (mma.sync m16n8k16, fp32 accumulate), fp32-accurate:
+//   A = weights. A 4- or 6-bit quant q, zero-extended into a 16-bit lane, is
+//     the fp16 subnormal q * 2^-24 - exactly; one byte permute builds two A
+//     values straight from the raw super-block bytes.
+//   B = input x split as x = hi + lo, both fp16 (hi = fp16(x), lo =
+//     fp16(x - hi)), after scaling x by a power of two so max|x| sits near
+//     2^13: 22 significant bits. Even B columns hold hi, odd columns lo, so the
+//     fragment of every lane receives sum(q*hi) and sum(q*lo) for its rows.
+//   k order: inside each 16-wide k step, lane t's four k slots map to the four
+//     consecutive elements 4t..4t+3, so each A fragment register is built from
+//     one 32-bit word of the block and B is stored to match.
+//   Scales: per 32-element sub-block (Q4_K: d*sc, dmin*m) or 16-element group
+//     (Q6_K: d*sc, with the -32 offset folded via the group's sum of x); lane
+//     t applies the groups j with j % 4 == t, and the 4 lanes of a row group
+//     are summed at the end of an item.
+#include <algorithm>
 #include <cfloat>
 #include "common.cuh"
 #include "engine.h"
@@ -21,74 +36,135 @@
 namespace atlas {
 
 struct Chunk {
-    const uint8_t *src;   // 16-byte aligned source
-    uint32_t bytes;       // multiple of 16
-    uint32_t lead;        // offset of the first useful byte inside the stage
-    uint32_t seg, r0, r1; // GEMV: segment and its local rows; ATTN: 0=K / 1=V and positions
+    const uint8_t *src;     // contiguous chunk: 16-byte aligned source
+    uint32_t bytes;         // bytes delivered by the chunk's copies
+    uint32_t lead;          // contiguous chunk: offset of the first row in the stage
+    uint32_t seg, r0, r1;   // segment, segment-local rows [r0, r1) (ATTN: K/V and positions)
+    uint32_t b0, b1;        // block columns [b0, b1)
+    uint32_t rel0;          // item-relative row of r0
 };
 
-struct __align__(128) Smem {
-    uint8_t stage[kStages][kStageBytes];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
-    float rowres[kMaxSeg][kMaxItemRows];
-    float red[kConsumerWarps], red2[kConsumerWarps];
+struct __align__(16) SmemHdr {
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
+    Phase ph;
+    float wres[2][kConsumerWarps][2][kMaxItemRows];  // per-warp row partials, double-buffered by item
     double dred[kConsumerWarps];
-    Phase ph;                           // current GEMV phase descriptor
-    float inv_rms;
+    float fred[kConsumerWarps];
+    float inv_rms, xscale;
     float amax[kConsumerWarps];
     uint32_t aidx[kConsumerWarps];
     uint32_t flag;
-    // attention
+};
+
+// Attention buffers; they live in the x staging area, which only GEMV phases use.
+struct __align__(16) AttnSmem {
     float4 q[kMaxGroup][kHeadDim / 4];  // RoPE'd queries of the item's group
     float4 knew[kHeadDim / 4], vnew[kHeadDim / 4];
     float cw[kMaxSplits][kMaxGroup];    // combine weights exp(m_s - M)
     float cden[kMaxGroup];
-    // pump (thread 0): position of the next chunk to issue
-    uint32_t pump_p, pump_it, pump_c, pump_nc, pump_issued, pump_done;
-    Chunk pump_ch[kMaxSeg];
 };
 
+constexpr uint32_t kHdrBytes = (sizeof(SmemHdr) + 127u) & ~127u;
+
+// View of the dynamic shared memory: header, x staging area, stage ring.
+struct Smem {
+    SmemHdr *h;
+    AttnSmem *a;        // overlays xarea
+    uint8_t *xarea;     // GEMV input: groups of 4 elements as 4 hi + 4 lo halves, then one sum per 16 elements
+    uint8_t *ring;
+    uint32_t n_stages, stage_bytes;
+    __device__ __forceinline__ uint8_t *stage(uint32_t k) const { return ring + (size_t)(k % n_stages) * stage_bytes; }
+    __device__ __forceinline__ uint64_t *full(uint32_t k) const { return &h->full[k % n_stages]; }
+    __device__ __forceinline__ uint64_t *empty(uint32_t k) const { return &h->empty[k % n_stages]; }
+    __device__ __forceinline__ uint32_t par(uint32_t k) const { return (k / n_stages) & 1u; }
+};
 
 // ------------------------------------------------------ chunk enumeration --
 
-__device__ __forceinline__ Chunk make_chunk(const uint8_t *base, uint64_t start, uint64_t bytes)
+__device__ __forceinline__ void align_range(const uint8_t *p, uint64_t bytes, const uint8_t *&lo, uint32_t &n, uint32_t &lead)
 {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(base) + start;
-    const uintptr_t lo = a & ~uintptr_t(15), hi = (a + bytes + 15) & ~uintptr_t(15);
-    Chunk c;
-    c.src = reinterpret_cast<const uint8_t *>(lo);
-    c.bytes = (uint32_t)(hi - lo);
-    c.lead = (uint32_t)(a - lo);
-    return c;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t l = a & ~uintptr_t(15), e = (a + bytes + 15) & ~uintptr_t(15);
+    lo = reinterpret_cast<const uint8_t *>(l);
+    n = (uint32_t)(e - l);
+    lead = (uint32_t)(a - l);
 }
 
-// GEMV item -> up to kMaxSeg chunks (one per segment touched).
-__device__ __forceinline__ int gemv_chunks(const Phase &ph, uint32_t item, Chunk (&out)[kMaxSeg])
+// Segment portions of GEMV item `it`: (segment, local rows, item-relative row).
+__device__ __forceinline__ int gemv_portions(const Phase &ph, uint32_t it, uint32_t (&sg)[2], uint32_t (&la)[2],
+                                             uint32_t (&lb)[2], uint32_t (&rel)[2], uint32_t &np)
 {
-    int n = 0;
-    const uint32_t r0 = item * ph.item_rows;
+    const uint32_t r0 = it * ph.item_rows;
+    np = 0;
     if (ph.paired) {
         const uint32_t r1 = min(r0 + ph.item_rows, ph.seg[0].rows);
-        for (uint32_t s = 0; s < ph.n_seg; ++s) {
-            Chunk c = make_chunk(ph.seg[s].w, (uint64_t)r0 * ph.seg[s].row_bytes,
-                                 (uint64_t)(r1 - r0) * ph.seg[s].row_bytes);
-            c.seg = s; c.r0 = r0; c.r1 = r1;
-            out[n++] = c;
-        }
-        return n;
+        for (uint32_t s = 0; s < ph.n_seg && s < 2; ++s) { sg[np] = s; la[np] = r0; lb[np] = r1; rel[np] = 0; ++np; }
+        return (int)np;
     }
     const uint32_t r1 = min(r0 + ph.item_rows, ph.seg_start[ph.n_seg]);
-    for (uint32_t s = 0; s < ph.n_seg; ++s) {
+    for (uint32_t s = 0; s < ph.n_seg && np < 2; ++s) {
         const uint32_t a = max(r0, ph.seg_start[s]), b = min(r1, ph.seg_start[s + 1]);
         if (a >= b) continue;
-        const uint32_t la = a - ph.seg_start[s], lb = b - ph.seg_start[s];
-        Chunk c = make_chunk(ph.seg[s].w, (uint64_t)la * ph.seg[s].row_bytes,
-                             (uint64_t)(lb - la) * ph.seg[s].row_bytes);
-        c.seg = s; c.r0 = la; c.r1 = lb;
-        out[n++] = c;
+        sg[np] = s; la[np] = a - ph.seg_start[s]; lb[np] = b - ph.seg_start[s]; rel[np] = a - r0; ++np;
     }
-    return n;
+    return (int)np;
+}
+
+__device__ __forceinline__ uint32_t gemv_colchunks(const Phase &ph)
+{
+    const uint32_t nb = ph.cols / 256u;
+    return (nb + ph.chunk_blocks - 1u) / ph.chunk_blocks;
+}
+
+// Chunks of an item: for each segment portion, its rows in runs of
+// chunk_rows, each run in column chunks of chunk_blocks.
+__device__ __forceinline__ uint32_t gemv_item_chunks(const Phase &ph, uint32_t it)
+{
+    uint32_t sg[2], la[2], lb[2], rel[2], np;
+    gemv_portions(ph, it, sg, la, lb, rel, np);
+    uint32_t n = 0;
+    for (uint32_t p = 0; p < np; ++p) n += (lb[p] - la[p] + ph.chunk_rows - 1) / ph.chunk_rows;
+    return n * gemv_colchunks(ph);
+}
+
+__device__ __forceinline__ Chunk gemv_item_chunk(const Phase &ph, uint32_t it, uint32_t ci, bool need_bytes = true)
+{
+    uint32_t sg[2], la[2], lb[2], rel[2], np;
+    gemv_portions(ph, it, sg, la, lb, rel, np);
+    const uint32_t ncc = gemv_colchunks(ph), nb = ph.cols / 256u;
+    uint32_t run = ci / ncc;
+    const uint32_t cb = ci % ncc;
+    uint32_t p = 0;
+    for (; p + 1 < np; ++p) {
+        const uint32_t runs = (lb[p] - la[p] + ph.chunk_rows - 1) / ph.chunk_rows;
+        if (run < runs) break;
+        run -= runs;
+    }
+    Chunk c;
+    c.seg = sg[p];
+    c.r0 = la[p] + run * ph.chunk_rows;
+    c.r1 = min(c.r0 + ph.chunk_rows, lb[p]);
+    c.rel0 = rel[p] + run * ph.chunk_rows;
+    c.b0 = cb * ph.chunk_blocks;
+    c.b1 = min(c.b0 + ph.chunk_blocks, nb);
+    const Seg &s = ph.seg[c.seg];
+    if (ph.seg_stride == 0) {
+        align_range(s.w + (uint64_t)c.r0 * s.row_bytes, (uint64_t)(c.r1 - c.r0) * s.row_bytes, c.src, c.bytes, c.lead);
+    } else {
+        const uint32_t bb = block_bytes(s.type);
+        uint32_t total = 0;
+        for (uint32_t r = c.r0; need_bytes && r < c.r1; ++r) {
+            const uint8_t *lo;
+            uint32_t n, lead;
+            align_range(s.w + (uint64_t)r * s.row_bytes + (uint64_t)c.b0 * bb, (uint64_t)(c.b1 - c.b0) * bb, lo, n, lead);
+            total += n;
+        }
+        c.src = nullptr;
+        c.bytes = total;
+        c.lead = 0;
+    }
+    return c;
 }
 
 // Positions per attention item: a multiple of kAttnChunk, grown with the
@@ -98,7 +174,7 @@ __device__ __forceinline__ uint32_t attn_split_len(const Program &pg, uint32_t p
 {
     uint32_t target = gridDim.x / pg.kv_heads;
     if (target < 1u) target = 1u;
-    if (target > (uint32_t)kMaxSplits / 2u) target = kMaxSplits / 2u;
+    if (target > (uint32_t)kMaxSplits) target = kMaxSplits;
     const uint32_t n = pos + 1u;
     const uint32_t chunks = (n + (uint32_t)kAttnChunk * target - 1u) / ((uint32_t)kAttnChunk * target);
     return (uint32_t)kAttnChunk * (chunks ? chunks : 1u);
@@ -113,13 +189,6 @@ __device__ __forceinline__ uint32_t attn_items(const Program &pg, uint32_t pos)
 // ATTN item (kv head g, split s) covers positions [p0, min(p0 + L, pos + 1));
 // its cached part [p0, min(p0 + L, pos)) is staged as (K, V) chunk pairs of up
 // to kAttnChunk positions; position pos comes from the fresh projections.
-__device__ __forceinline__ int attn_chunks(const Program &pg, const Phase &ph, uint32_t item, uint32_t pos,
-                                           Chunk (&out)[kMaxSeg])
-{
-    (void)out;
-    return 0;  // attention items are enumerated chunk-pair by chunk-pair (attn_chunk_pair)
-}
-
 __device__ __forceinline__ uint32_t attn_item_pairs(const Program &pg, uint32_t item, uint32_t pos)
 {
     const uint32_t L = attn_split_len(pg, pos), nsplit = (pos + L) / L;
@@ -136,8 +205,9 @@ __device__ __forceinline__ Chunk attn_chunk(const Program &pg, const Phase &ph, 
     const uint32_t esz = pg.kv_fp16 ? 2u : 4u, row = pg.head_dim * esz;
     const uint64_t head_off = (uint64_t)g * pg.max_context * row;
     const uint8_t *base = reinterpret_cast<const uint8_t *>(kv ? ph.v_cache : ph.k_cache);
-    Chunk c = make_chunk(base, head_off + (uint64_t)t0 * row, (uint64_t)(t1 - t0) * row);
-    c.seg = kv; c.r0 = t0; c.r1 = t1;
+    Chunk c;
+    align_range(base + head_off + (uint64_t)t0 * row, (uint64_t)(t1 - t0) * row, c.src, c.bytes, c.lead);
+    c.seg = kv; c.r0 = t0; c.r1 = t1; c.b0 = c.b1 = 0; c.rel0 = 0;
     return c;
 }
 
@@ -152,120 +222,73 @@ __device__ __forceinline__ uint32_t phase_items(const Program &pg, const Phase &
     }
 }
 
-// Number of staged chunks of an item, and chunk i of it (GEMV chunks are
-// precomputed into `buf` by item_chunk_count).
-__device__ __forceinline__ uint32_t item_chunk_count(const Program &pg, const Phase &ph, uint32_t item, uint32_t pos,
-                                                     Chunk (&buf)[kMaxSeg])
-{
-    if (ph.kind == PH_GEMV) return (uint32_t)gemv_chunks(ph, item, buf);
-    if (ph.kind == PH_ATTN) return 2u * attn_item_pairs(pg, item, pos);
-    return 0u;
-}
+// --------------------------------------------------------------- producer --
 
-__device__ __forceinline__ Chunk item_chunk(const Program &pg, const Phase &ph, uint32_t item, uint32_t pos, uint32_t i,
-                                            const Chunk (&buf)[kMaxSeg])
+__device__ void producer(const Program &pg, const Smem &sm, uint32_t pos, volatile uint32_t *err)
 {
-    if (ph.kind == PH_ATTN) return attn_chunk(pg, ph, item, pos, i >> 1, i & 1u);
-    return buf[i];
-}
-
-// ------------------------------------------------------------------ pump --
-
-// Thread 0 only. Issues bulk copies for upcoming chunks while ring slots are
-// free (a slot is free once all 8 warps released the chunk kStages earlier);
-// never blocks.
-__device__ void pump(const Program &pg, Smem &sm, uint32_t pos)
-{
-    while (!sm.pump_done) {
-        const uint32_t k = sm.pump_issued, s = k % kStages, round = k / kStages;
-        if (round > 0 && !mbar_test(&sm.empty[s], (round - 1) & 1u)) return;
-        // find the next chunk
-        while (sm.pump_c >= sm.pump_nc) {
-            // advance to the next item of this CTA (or the next phase)
-            const Phase &ph = pg.phases[sm.pump_p];
-            uint32_t it = sm.pump_it + gridDim.x;
-            if (sm.pump_nc == 0xffffffffu) it = blockIdx.x;  // first item of phase pump_p
-            if (it < phase_items(pg, ph, pos)) {
-                sm.pump_it = it;
-                sm.pump_nc = item_chunk_count(pg, ph, it, pos, sm.pump_ch);
-                sm.pump_c = 0;
-            } else {
-                if (++sm.pump_p >= pg.n_phases) { sm.pump_done = 1; return; }
-                sm.pump_nc = 0xffffffffu;
-                sm.pump_c = 0xffffffffu;
+    const uint64_t policy = policy_evict_first();
+    uint32_t k = 0;
+    for (uint32_t p = 0; p < pg.n_phases; ++p) {
+        const Phase &ph = pg.phases[p];
+        const uint32_t n = phase_items(pg, ph, pos);
+        for (uint32_t it = blockIdx.x; it < n; it += gridDim.x) {
+            const uint32_t nc = ph.kind == PH_GEMV ? gemv_item_chunks(ph, it)
+                              : ph.kind == PH_ATTN ? 2u * attn_item_pairs(pg, it, pos) : 0u;
+            for (uint32_t ci = 0; ci < nc; ++ci, ++k) {
+                if (k >= sm.n_stages && !mbar_wait(sm.empty(k), sm.par(k) ^ 1u, err)) return;
+                uint8_t *dst = sm.stage(k);
+                if (ph.kind == PH_ATTN) {
+                    const Chunk c = attn_chunk(pg, ph, it, pos, ci >> 1, ci & 1u);
+                    mbar_arrive_expect_tx(sm.full(k), c.bytes);
+                    bulk_g2s(dst, c.src, c.bytes, sm.full(k));
+                    continue;
+                }
+                const Chunk c = gemv_item_chunk(ph, it, ci);
+                mbar_arrive_expect_tx(sm.full(k), c.bytes);
+                if (ph.seg_stride == 0) {
+                    bulk_g2s_hint(dst, c.src, c.bytes, sm.full(k), policy);
+                } else {
+                    const Seg &s = ph.seg[c.seg];
+                    const uint32_t bb = block_bytes(s.type);
+                    for (uint32_t r = c.r0; r < c.r1; ++r) {
+                        const uint8_t *lo;
+                        uint32_t nbytes, lead;
+                        align_range(s.w + (uint64_t)r * s.row_bytes + (uint64_t)c.b0 * bb, (uint64_t)(c.b1 - c.b0) * bb,
+                                    lo, nbytes, lead);
+                        bulk_g2s_hint(dst + (size_t)(r - c.r0) * ph.seg_stride, lo, nbytes, sm.full(k), policy);
+                    }
+                }
             }
         }
-        const Chunk c = item_chunk(pg, pg.phases[sm.pump_p], sm.pump_it, pos, sm.pump_c++, sm.pump_ch);
-        mbar_arrive_expect_tx(&sm.full[s], c.bytes);
-        if (pg.phases[sm.pump_p].kind == PH_GEMV) bulk_g2s_hint(sm.stage[s], c.src, c.bytes, &sm.full[s], policy_evict_first());
-        else bulk_g2s(sm.stage[s], c.src, c.bytes, &sm.full[s]);
-        sm.pump_issued = k + 1;
-        if (pg.trace && sm.pump_done == 0) pg.trace[((size_t)blockIdx.x * pg.n_phases + sm.pump_p) * 4 + 3] = global_ns();
+        if (pg.trace) pg.trace[((size_t)blockIdx.x * pg.n_phases + p) * 4 + 3] = global_ns();
     }
-}
-
-// Wait for chunk k's bytes (all threads); thread 0 keeps pumping meanwhile.
-__device__ __forceinline__ bool stage_wait(const Program &pg, Smem &sm, uint32_t k, uint32_t pos,
-                                           volatile uint32_t *err)
-{
-    const uint32_t s = k % kStages, par = (k / kStages) & 1u;
-    if (threadIdx.x != 0) return mbar_wait(&sm.full[s], par, err);
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; ++i) {
-        pump(pg, sm, pos);
-        if (mbar_test(&sm.full[s], par)) return true;
-        if ((i & 15u) == 15u) {
-            if (*err != kStatusOk) return false;
-            const uint64_t now = global_ns();
-            if (!t0) t0 = now;
-            else if (now - t0 > kWaitLimitNs) break;
-        }
-    }
-    atomicCAS(const_cast<uint32_t *>(err), kStatusOk, kStatusStageTimeout);
-    return false;
-}
-
-// Release chunk k's stage (one arrival per warp); thread 0 refills the ring.
-__device__ __forceinline__ void stage_release(const Program &pg, Smem &sm, uint32_t k, uint32_t pos)
-{
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.empty[k % kStages]);
-    if (threadIdx.x == 0) pump(pg, sm, pos);
+    // Drain: every issued copy has landed before the CTA may exit.
+    for (uint32_t j = (k > sm.n_stages ? k - sm.n_stages : 0); j < k; ++j)
+        if (!mbar_wait(sm.full(j), sm.par(j), err)) return;
 }
 
 // ------------------------------------------------------------- consumers --
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
 
-__device__ __forceinline__ void group_sync(int id, int nthreads)
+__device__ __forceinline__ bool stage_wait(const Smem &sm, uint32_t k, volatile uint32_t *err)
 {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+    return mbar_wait(sm.full(k), sm.par(k), err);
+}
+
+__device__ __forceinline__ void stage_release(const Smem &sm, uint32_t k)
+{
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(sm.empty(k));
 }
 
 // Wait (one thread) for every CTA to have finished phase p, then make the
 // results visible to all consumer threads.
-__device__ __forceinline__ bool wait_phase(const Program &pg, Smem &sm, uint32_t p, uint32_t epoch, uint32_t pos,
-                                           volatile uint32_t *err)
+__device__ __forceinline__ bool wait_phase(const Program &pg, uint32_t p, uint32_t epoch, volatile uint32_t *err)
 {
     __shared__ uint32_t ok_flag;
     if (threadIdx.x == 0) {
-        const uint32_t *ctr = pg.phase_ctr + 8u * p;
-        const uint32_t target = (epoch + 1u) * gridDim.x;
-        bool ok = false;
-        uint64_t t0 = 0;
-        for (uint32_t i = 0;; ++i) {
-            if ((int32_t)(ld_acquire(ctr) - target) >= 0) { ok = true; break; }
-            if (*err != kStatusOk) break;
-            pump(pg, sm, pos);
-            if ((i & 15u) == 15u) {
-                const uint64_t now = global_ns();
-                if (!t0) t0 = now;
-                else if (now - t0 > kWaitLimitNs) {
-                    atomicCAS(const_cast<uint32_t *>(err), kStatusOk, kStatusBarrierTimeout);
-                    break;
-                }
-            }
-        }
+        const bool ok = wait_counter(pg.phase_ctr + 8u * p, (epoch + 1u) * gridDim.x, err, kStatusBarrierTimeout);
         __threadfence();
         ok_flag = ok ? 1u : 0u;
     }
@@ -284,7 +307,7 @@ __device__ __forceinline__ void arrive_phase(const Program &pg, uint32_t p)
 
 // Per-CTA RMSNorm scale over the hidden vector (sum of squares in double as
 // src/brain_runtime.c:1345-1351; 1/sqrtf(float(mean)+eps) as :1353-1358).
-__device__ float cta_inv_rms(const float *x, uint32_t n, float eps, Smem &sm)
+__device__ float cta_inv_rms(const float *x, uint32_t n, float eps, const Smem &sm)
 {
     double ss = 0.0;
     for (uint32_t i = threadIdx.x * 4u; i < n; i += kConsumerWarps * 32 * 4) {
@@ -297,194 +320,382 @@ __device__ float cta_inv_rms(const float *x, uint32_t n, float eps, Smem &sm)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) sm.dred[warp] = ss;
+    if (lane == 0) sm.h->dred[warp] = ss;
     consumer_sync();
     if (threadIdx.x == 0) {
         double t = 0.0;
-        for (int w = 0; w < kConsumerWarps; ++w) t += sm.dred[w];
-        sm.inv_rms = 1.0f / sqrtf((float)(t / (double)n) + eps);
+        for (int w = 0; w < kConsumerWarps; ++w) t += sm.h->dred[w];
+        sm.h->inv_rms = 1.0f / sqrtf((float)(t / (double)n) + eps);
     }
     consumer_sync();
-    return sm.inv_rms;
+    return sm.h->inv_rms;
 }
 
-// Rows of one staged chunk, for the NS slices this lane owns. Two rows are in
-// flight per warp for instruction-level parallelism.
-template <int NS, bool Q6>
-__device__ __forceinline__ void chunk_rows(const uint8_t *base, uint64_t rb, uint32_t nrows, uint32_t NG, int gi,
-                                           const uint32_t (&boff)[NS], const int (&cc)[NS], const int (&hf)[NS],
-                                           const bool (&valid)[NS], const SliceX (&x)[NS], float *res, uint32_t W,
-                                           int wi, int warp, int lane, Smem &sm)
+// Stage the phase input in shared memory as fp16 (hi, lo) groups plus one sum
+// per 16 elements, all in units of x * xscale (a power of two).
+__device__ void stage_x(const Program &pg, const Phase &ph, const Smem &sm)
 {
-    for (uint32_t r = (uint32_t)gi; r < nrows; r += 2u * NG) {
-        const uint8_t *p0 = base + (uint64_t)r * rb;
-        const bool two = r + NG < nrows;
-        const uint8_t *p1 = two ? p0 + (uint64_t)NG * rb : p0;
-        float a0 = 0.f, a1 = 0.f;
+    const uint32_t n = ph.cols;
+    const bool norm = ph.input_mode == IN_RMSNORM;
+    const float inv = norm ? cta_inv_rms(ph.in, n, pg.rms_eps, sm) : 1.0f;
+    float4 *xf = reinterpret_cast<float4 *>(sm.xarea);
+    float mx = 0.f;
+    for (uint32_t i = threadIdx.x; i < n / 4u; i += kConsumerWarps * 32) {
+        float4 v = __ldcg(reinterpret_cast<const float4 *>(ph.in) + i);
+        if (norm) {
+            const float4 w = __ldg(reinterpret_cast<const float4 *>(ph.norm_w) + i);
+            v.x = v.x * inv * w.x; v.y = v.y * inv * w.y; v.z = v.z * inv * w.z; v.w = v.w * inv * w.w;
+        }
+        xf[i] = v;
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
-            if (valid[j]) {
-                if (Q6) {
-                    a0 += q6k_slice_dot(p0 + boff[j], cc[j], hf[j], x[j]);
-                    a1 += q6k_slice_dot(p1 + boff[j], cc[j], hf[j], x[j]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) sm.h->fred[warp] = mx;
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        float m = 0.f;
+        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, sm.h->fred[w]);
+        // scale so that max|x| lands in [2^13, 2^14): far from fp16 overflow,
+        // and the lo parts of small elements stay normal
+        sm.h->xscale = (m > 0.f && isfinite(m)) ? exp2f((float)(13 - ilogbf(m))) : 1.0f;
+    }
+    consumer_sync();
+    const float s = sm.h->xscale;
+    float *xs16 = reinterpret_cast<float *>(sm.xarea + (size_t)n * 4u);
+    for (uint32_t u = threadIdx.x; u < n / 16u; u += kConsumerWarps * 32) {
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = xf[4 * u + q];
+            const float e[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+            __half hi[4], lo[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                hi[i] = __float2half_rn(e[i]);
+                lo[i] = __float2half_rn(e[i] - __half2float(hi[i]));
+                sum += e[i];
+            }
+            uint4 pk;
+            pk.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
+            pk.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
+            pk.z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
+            pk.w = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+            reinterpret_cast<uint4 *>(sm.xarea)[4 * u + q] = pk;
+        }
+        xs16[u] = sum;
+    }
+    consumer_sync();
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b,
+                                         const float (&c)[4])
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+// bytes 0,1 (sel 0x4140) or 2,3 (sel 0x4342) of v as two zero-extended 16-bit
+// lanes: the fp16 subnormals q0 * 2^-24, q1 * 2^-24
+__device__ __forceinline__ uint32_t sub2(uint32_t v, uint32_t sel) { return __byte_perm(v, 0u, sel); }
+
+__device__ __forceinline__ uint32_t ld32u(const uint8_t *p)
+{
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    return __funnelshift_r(w[0], w[1], (uint32_t)(a & 3u) * 8u);
+}
+
+constexpr float kTwo24 = 16777216.0f;
+
+// NT independent 16-row x 256-element Q4_K tiles (NT = 1 or 2, interleaved
+// for instruction-level parallelism). Tile n: rows (g, g+8) of this lane at
+// r0[n] / r1[n] (nullptr: row absent), the block column's staged x groups
+// xb[n] and 16-element sums xs[n]. Adds this lane's sub-blocks (j = t, t + 4).
+template <int NT>
+__device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const uint8_t *const (&r1)[NT],
+                                          const uint8_t *const (&xb)[NT], const float *const (&xs)[NT], int g, int t,
+                                          float (&o0)[NT], float (&o1)[NT])
+{
+    float dsc[NT][2][2], dmn[NT][2][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        const uint8_t *rows[2] = {r0[n], r1[n]};
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            dsc[n][r][0] = dsc[n][r][1] = dmn[n][r][0] = dmn[n][r][1] = 0.f;
+            if (!rows[r]) continue;
+            const uint4 hd = *reinterpret_cast<const uint4 *>(rows[r]);
+            const float d = h2f((uint16_t)(hd.x & 0xffffu)), dm = h2f((uint16_t)(hd.x >> 16));
+            const uint32_t sh = 8u * (uint32_t)t;
+            const uint32_t y = (hd.y >> sh) & 255u, z = (hd.z >> sh) & 255u, w = (hd.w >> sh) & 255u;
+            dsc[n][r][0] = d * (float)(y & 63u);                        // j = t
+            dmn[n][r][0] = dm * (float)(z & 63u);
+            dsc[n][r][1] = d * (float)((w & 15u) | ((y >> 6) << 4));    // j = t + 4
+            dmn[n][r][1] = dm * (float)((w >> 4) | ((z >> 6) << 4));
+        }
+    }
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t podd = (uint32_t)(g & 1) * 8u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        float dlo[NT][4], dhi[NT][4];
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp) {
+            const uint32_t off = 16u + 32u * c + 16u * hp + 4u * t;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const uint32_t w0 = r0[n] ? *reinterpret_cast<const uint32_t *>(r0[n] + off) : 0u;
+                const uint32_t w1 = r1[n] ? *reinterpret_cast<const uint32_t *>(r1[n] + off) : 0u;
+                const uint32_t l0 = w0 & 0x0f0f0f0fu, h0 = (w0 >> 4) & 0x0f0f0f0fu;
+                const uint32_t l1 = w1 & 0x0f0f0f0fu, h1 = (w1 >> 4) & 0x0f0f0f0fu;
+                const uint2 blo = *reinterpret_cast<const uint2 *>(xb[n] + (16u * c + 4u * hp + (uint32_t)t) * 16u + podd);
+                const uint2 bhi = *reinterpret_cast<const uint2 *>(xb[n] + (16u * c + 8u + 4u * hp + (uint32_t)t) * 16u + podd);
+                if (hp == 0) {
+                    mma16816(dlo[n], sub2(l0, 0x4140), sub2(l1, 0x4140), sub2(l0, 0x4342), sub2(l1, 0x4342), blo, zero);
+                    mma16816(dhi[n], sub2(h0, 0x4140), sub2(h1, 0x4140), sub2(h0, 0x4342), sub2(h1, 0x4342), bhi, zero);
                 } else {
-                    a0 += q4k_slice_dot(p0 + boff[j], cc[j], hf[j], x[j]);
-                    a1 += q4k_slice_dot(p1 + boff[j], cc[j], hf[j], x[j]);
+                    const float clo[4] = {dlo[n][0], dlo[n][1], dlo[n][2], dlo[n][3]};
+                    const float chi[4] = {dhi[n][0], dhi[n][1], dhi[n][2], dhi[n][3]};
+                    mma16816(dlo[n], sub2(l0, 0x4140), sub2(l1, 0x4140), sub2(l0, 0x4342), sub2(l1, 0x4342), blo, clo);
+                    mma16816(dhi[n], sub2(h0, 0x4140), sub2(h1, 0x4140), sub2(h0, 0x4342), sub2(h1, 0x4342), bhi, chi);
                 }
             }
         }
-        a0 = warp_sum(a0);
-        a1 = warp_sum(a1);
-        if (W == 1u) {
-            if (lane == 0) {
-                res[r] = a0;
-                if (two) res[r + NG] = a1;
+        // this lane's sub-block in chunk c, if any: j = 2c + (t & 1) with (c & 1) == (t >> 1)
+        if ((c & 1) == (t >> 1)) {
+            const int slot = c >> 1, j = 2 * c + (t & 1);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const float *D = (t & 1) ? dhi[n] : dlo[n];
+                const float sx = xs[n][2 * j] + xs[n][2 * j + 1];
+                o0[n] += dsc[n][0][slot] * ((D[0] + D[1]) * kTwo24) - dmn[n][0][slot] * sx;
+                o1[n] += dsc[n][1][slot] * ((D[2] + D[3]) * kTwo24) - dmn[n][1][slot] * sx;
             }
-        } else {
-            if (lane == 0) { sm.red[warp] = a0; sm.red2[warp] = a1; }
-            group_sync(2 + gi, (int)W * 32);
-            if (wi == 0 && lane == 0) {
-                float t0 = 0.f, t1 = 0.f;
-                for (uint32_t q = 0; q < W; ++q) { t0 += sm.red[gi * W + q]; t1 += sm.red2[gi * W + q]; }
-                res[r] = t0;
-                if (two) res[r + NG] = t1;
-            }
-            group_sync(2 + gi, (int)W * 32);
         }
     }
 }
 
-template <int NS>
-__device__ bool run_gemv_phase(const Program &pg, const Phase &gph, Smem &sm, uint32_t &k, uint32_t pos,
-                               volatile uint32_t *err)
+// NT independent 16-row x 256-element Q6_K tiles (blocks at even, not
+// necessarily 4-aligned addresses). Lane t keeps the 16-element groups with
+// k == t: one scale per (h, hp) and row, selected outside the k loop.
+template <int NT>
+__device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const uint8_t *const (&r1)[NT],
+                                          const uint8_t *const (&xb)[NT], const float *const (&xs)[NT], int g, int t,
+                                          float (&o0)[NT], float (&o1)[NT])
 {
-    // The descriptor is read throughout the phase: keep a copy in shared memory.
-    for (uint32_t i = threadIdx.x; i < sizeof(Phase) / 4; i += kConsumerWarps * 32)
-        reinterpret_cast<uint32_t *>(&sm.ph)[i] = reinterpret_cast<const uint32_t *>(&gph)[i];
-    consumer_sync();
-    const Phase &ph = sm.ph;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t W = ph.warps_per_row, NG = kConsumerWarps / W;
-    const int gi = warp / (int)W, wi = warp % (int)W;
-    const uint32_t S = ph.cols / 32u;
-    const float *in = ph.in;
-    float inv = 1.f;
-    const bool norm = ph.input_mode == IN_RMSNORM;
-    if (norm) inv = cta_inv_rms(in, ph.cols, pg.rms_eps, sm);
-    // This lane's slices of the (normalized) input, and their positions.
-    SliceX x[NS];
-    uint32_t blk[NS];
-    int cc[NS], hf[NS];
-    bool valid[NS];
+    float d0[NT], d1[NT];
 #pragma unroll
-    for (int j = 0; j < NS; ++j) {
-        const uint32_t s = (uint32_t)(wi * 32 + lane) + (uint32_t)j * 32u * W;
-        valid[j] = s < S;
-        const uint32_t ss = valid[j] ? s : 0u;
-        blk[j] = ss >> 3;
-        cc[j] = (int)((ss & 7u) >> 1);
-        hf[j] = (int)(ss & 1u);
-        const uint32_t base = 256u * blk[j] + 64u * (uint32_t)cc[j] + 16u * (uint32_t)hf[j];
-        float lo[16], hi[16];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float4 a = __ldcg(reinterpret_cast<const float4 *>(in + base + 4 * q));
-            float4 b = __ldcg(reinterpret_cast<const float4 *>(in + base + 32 + 4 * q));
-            if (norm) {
-                const float4 wa = __ldg(reinterpret_cast<const float4 *>(ph.norm_w + base + 4 * q));
-                const float4 wb = __ldg(reinterpret_cast<const float4 *>(ph.norm_w + base + 32 + 4 * q));
-                a.x = a.x * inv * wa.x; a.y = a.y * inv * wa.y; a.z = a.z * inv * wa.z; a.w = a.w * inv * wa.w;
-                b.x = b.x * inv * wb.x; b.y = b.y * inv * wb.y; b.z = b.z * inv * wb.z; b.w = b.w * inv * wb.w;
-            }
-            lo[4 * q] = a.x; lo[4 * q + 1] = a.y; lo[4 * q + 2] = a.z; lo[4 * q + 3] = a.w;
-            hi[4 * q] = b.x; hi[4 * q + 1] = b.y; hi[4 * q + 2] = b.z; hi[4 * q + 3] = b.w;
-        }
-        float sl = 0.f, sh = 0.f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            if (!valid[j]) { lo[e] = 0.f; hi[e] = 0.f; }
-            sl += lo[e];
-            sh += hi[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            x[j].lo[e] = make_float2(lo[2 * e], lo[2 * e + 1]);
-            x[j].hi[e] = make_float2(hi[2 * e], hi[2 * e + 1]);
-        }
-        x[j].slo = sl;
-        x[j].shi = sh;
+    for (int n = 0; n < NT; ++n) {
+        d0[n] = r0[n] ? h2f((uint16_t)ld_u16(r0[n] + 208)) : 0.f;
+        d1[n] = r1[n] ? h2f((uint16_t)ld_u16(r1[n] + 208)) : 0.f;
     }
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t podd = (uint32_t)(g & 1) * 8u;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp) {
+            const uint32_t oa = 64u * h + 16u * hp + 4u * t, ob = oa + 32u, oq = 128u + 32u * h + 16u * hp + 4u * t;
+            const uint32_t si = 192u + 8u * h + hp + 2u * (uint32_t)t;   // scale of group k == t
+            uint32_t A0[NT], B0[NT], Q0[NT], A1[NT], B1[NT], Q1[NT];
+            float s0[NT], s1[NT], keep[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                A0[n] = r0[n] ? ld32u(r0[n] + oa) : 0u; B0[n] = r0[n] ? ld32u(r0[n] + ob) : 0u;
+                Q0[n] = r0[n] ? ld32u(r0[n] + oq) : 0u;
+                A1[n] = r1[n] ? ld32u(r1[n] + oa) : 0u; B1[n] = r1[n] ? ld32u(r1[n] + ob) : 0u;
+                Q1[n] = r1[n] ? ld32u(r1[n] + oq) : 0u;
+                s0[n] = r0[n] ? d0[n] * (float)(int8_t)r0[n][si] : 0.f;
+                s1[n] = r1[n] ? d1[n] * (float)(int8_t)r1[n][si] : 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t sa = (k & 2) ? 4u : 0u;
+                const uint32_t e0 = 128u * h + 32u * k + 16u * hp;  // first element of the 16-group
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    uint32_t v0, v1;
+                    if (k == 3) {
+                        v0 = ((B0[n] >> 4) & 0x0f0f0f0fu) | ((Q0[n] >> 2) & 0x30303030u);
+                        v1 = ((B1[n] >> 4) & 0x0f0f0f0fu) | ((Q1[n] >> 2) & 0x30303030u);
+                    } else {
+                        const uint32_t qs = (k == 0) ? 4u : (k == 1) ? 2u : 0u;
+                        const uint32_t x0 = (k & 1) ? B0[n] : A0[n], x1 = (k & 1) ? B1[n] : A1[n];
+                        v0 = ((x0 >> sa) & 0x0f0f0f0fu) | ((Q0[n] << qs) & 0x30303030u);
+                        v1 = ((x1 >> sa) & 0x0f0f0f0fu) | ((Q1[n] << qs) & 0x30303030u);
+                    }
+                    const uint2 b = *reinterpret_cast<const uint2 *>(xb[n] + (e0 / 4u + (uint32_t)t) * 16u + podd);
+                    float dd[4];
+                    mma16816(dd, sub2(v0, 0x4140), sub2(v1, 0x4140), sub2(v0, 0x4342), sub2(v1, 0x4342), b, zero);
+                    const bool mine = k == t;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) keep[n][e] = mine ? dd[e] : (k == 0 ? 0.f : keep[n][e]);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const float sx = 32.0f * xs[n][8u * h + 2u * (uint32_t)t + hp];
+                o0[n] += s0[n] * ((keep[n][0] + keep[n][1]) * kTwo24 - sx);
+                o1[n] += s1[n] * ((keep[n][2] + keep[n][3]) * kTwo24 - sx);
+            }
+        }
+    }
+}
+
+__device__ bool run_gemv_phase(const Program &pg, const Phase &gph, const Smem &sm, uint32_t &k, volatile uint32_t *err)
+{
+    for (uint32_t i = threadIdx.x; i < sizeof(Phase) / 4; i += kConsumerWarps * 32)
+        reinterpret_cast<uint32_t *>(&sm.h->ph)[i] = reinterpret_cast<const uint32_t *>(&gph)[i];
+    consumer_sync();
+    const Phase &ph = sm.h->ph;
+    stage_x(pg, ph, sm);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const float inv_scale = 1.0f / sm.h->xscale;
+    const float *xs16 = reinterpret_cast<const float *>(sm.xarea + (size_t)ph.cols * 4u);
     float best = -FLT_MAX;
     uint32_t best_i = 0xffffffffu;
-    for (uint32_t it = blockIdx.x; it < ph.n_items; it += gridDim.x) {
-        Chunk ch[kMaxSeg];
-        const int nc = gemv_chunks(ph, it, ch);
-        const uint32_t item_r0 = it * ph.item_rows;
-        for (int c = 0; c < nc; ++c, ++k) {
-            const uint32_t s = k % kStages;
-            if (!stage_wait(pg, sm, k, pos, err)) return false;
-            const uint32_t sg = ch[c].seg;
-            const uint64_t rb = ph.seg[sg].row_bytes;
-            const uint8_t *base = sm.stage[s] + ch[c].lead;
-            const uint32_t nrows = ch[c].r1 - ch[c].r0;
-            const uint32_t rel0 = ph.paired ? 0u : (ch[c].r0 + ph.seg_start[sg] - item_r0);
-            float *res = &sm.rowres[sg][rel0];
-            if (ph.seg[sg].type == 14u) {
-                uint32_t boff[NS];
+    uint32_t buf = 0;
+    for (uint32_t it = blockIdx.x; it < ph.n_items; it += gridDim.x, buf ^= 1u) {
+        float acc[2][kMaxItemRows / 16][2];
 #pragma unroll
-                for (int j = 0; j < NS; ++j) boff[j] = 210u * blk[j];
-                chunk_rows<NS, true>(base, rb, nrows, NG, gi, boff, cc, hf, valid, x, res, W, wi, warp, lane, sm);
-            } else {
-                uint32_t boff[NS];
+        for (int a = 0; a < 2; ++a)
 #pragma unroll
-                for (int j = 0; j < NS; ++j) boff[j] = 144u * blk[j];
-                chunk_rows<NS, false>(base, rb, nrows, NG, gi, boff, cc, hf, valid, x, res, W, wi, warp, lane, sm);
+            for (int b = 0; b < kMaxItemRows / 16; ++b) { acc[a][b][0] = 0.f; acc[a][b][1] = 0.f; }
+        const uint32_t nc = gemv_item_chunks(ph, it);
+        uint32_t task = 0;
+        for (uint32_t ci = 0; ci < nc; ++ci, ++k) {
+            const Chunk c = gemv_item_chunk(ph, it, ci, false);
+            if (!stage_wait(sm, k, err)) return false;
+            const Seg &sg = ph.seg[c.seg];
+            const uint32_t bb = block_bytes(sg.type);
+            const uint32_t nrows = c.r1 - c.r0, nrt = (nrows + 15u) / 16u, ncol = c.b1 - c.b0;
+            const uint32_t slot = ph.paired ? c.seg : 0u;
+            const uint8_t *st = sm.stage(k);
+            const uint32_t ntasks = nrt * ncol;
+            // tasks of this chunk handled by this warp: (task + i) % 8 == warp
+            const uint32_t first = (uint32_t)(warp - (int)(task % kConsumerWarps) + kConsumerWarps) % kConsumerWarps;
+            const uint64_t coff = (uint64_t)c.b0 * bb;
+            // row pointers of task ti for this lane's rows (nullptr: row absent)
+            auto rows_of = [&](uint32_t ti, const uint8_t *&p0, const uint8_t *&p1, uint32_t &bcol, uint32_t &irt) {
+                const uint32_t rt = ti / ncol, bl = ti % ncol;
+                const uint32_t i0 = rt * 16u + (uint32_t)g, i1 = i0 + 8u;
+                p0 = p1 = nullptr;
+                if (ph.seg_stride == 0) {
+                    const uint8_t *base = st + c.lead + (uint64_t)(c.b0 + bl) * bb;
+                    if (i0 < nrows) p0 = base + (uint64_t)i0 * sg.row_bytes;
+                    if (i1 < nrows) p1 = base + (uint64_t)i1 * sg.row_bytes;
+                } else {
+                    const uintptr_t w = reinterpret_cast<uintptr_t>(sg.w);
+                    if (i0 < nrows) p0 = st + (size_t)i0 * ph.seg_stride + ((w + (uint64_t)(c.r0 + i0) * sg.row_bytes + coff) & 15u) + (uint64_t)bl * bb;
+                    if (i1 < nrows) p1 = st + (size_t)i1 * ph.seg_stride + ((w + (uint64_t)(c.r0 + i1) * sg.row_bytes + coff) & 15u) + (uint64_t)bl * bb;
+                }
+                bcol = c.b0 + bl;
+                irt = (c.rel0 / 16u) + rt;   // item row tile
+            };
+            auto add = [&](uint32_t irt, float o0, float o1) {
+#pragma unroll
+                for (int q = 0; q < kMaxItemRows / 16; ++q) {
+                    if ((uint32_t)q != irt) continue;
+                    if (slot == 0u) { acc[0][q][0] += o0; acc[0][q][1] += o1; }
+                    else { acc[1][q][0] += o0; acc[1][q][1] += o1; }
+                }
+            };
+            uint32_t ti = first;
+            for (; ti + kConsumerWarps < ntasks; ti += 2u * kConsumerWarps) {
+                const uint8_t *p0[2], *p1[2], *xb[2];
+                const float *xs[2];
+                uint32_t bcol[2], irt[2];
+                rows_of(ti, p0[0], p1[0], bcol[0], irt[0]);
+                rows_of(ti + kConsumerWarps, p0[1], p1[1], bcol[1], irt[1]);
+#pragma unroll
+                for (int n = 0; n < 2; ++n) { xb[n] = sm.xarea + (size_t)bcol[n] * 1024u; xs[n] = xs16 + (size_t)bcol[n] * 16u; }
+                float o0[2] = {0.f, 0.f}, o1[2] = {0.f, 0.f};
+                if (sg.type == 12u) q4k_tiles<2>(p0, p1, xb, xs, g, t, o0, o1);
+                else q6k_tiles<2>(p0, p1, xb, xs, g, t, o0, o1);
+                add(irt[0], o0[0], o1[0]);
+                add(irt[1], o0[1], o1[1]);
             }
-            stage_release(pg, sm, k, pos);
+            if (ti < ntasks) {
+                const uint8_t *p0[1], *p1[1], *xb[1];
+                const float *xs[1];
+                uint32_t bcol, irt;
+                rows_of(ti, p0[0], p1[0], bcol, irt);
+                xb[0] = sm.xarea + (size_t)bcol * 1024u;
+                xs[0] = xs16 + (size_t)bcol * 16u;
+                float o0[1] = {0.f}, o1[1] = {0.f};
+                if (sg.type == 12u) q4k_tiles<1>(p0, p1, xb, xs, g, t, o0, o1);
+                else q6k_tiles<1>(p0, p1, xb, xs, g, t, o0, o1);
+                add(irt, o0[0], o1[0]);
+            }
+            task += ntasks;
+            stage_release(sm, k);
         }
-        consumer_sync();
-        // epilogue over the item's rows
+        // per-warp partials: sum the 4 lanes of each row group, stage them, one barrier
+        const uint32_t item_r0 = it * ph.item_rows;
         const uint32_t total = ph.paired ? ph.seg[0].rows : ph.seg_start[ph.n_seg];
         const uint32_t nr = min(ph.item_rows, total - item_r0);
+        const uint32_t nslots = ph.paired ? ph.n_seg : 1u;
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int q = 0; q < kMaxItemRows / 16; ++q)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float v = acc[a][q][e];
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    const uint32_t r = (uint32_t)q * 16u + (uint32_t)g + 8u * (uint32_t)e;
+                    if (t == 0 && (uint32_t)a < nslots && r < (uint32_t)kMaxItemRows) sm.h->wres[buf][warp][a][r] = v;
+                }
+        consumer_sync();
         for (uint32_t r = threadIdx.x; r < nr; r += kConsumerWarps * 32) {
+            float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                v0 += sm.h->wres[buf][w][0][r];
+                v1 += sm.h->wres[buf][w][1][r];
+            }
+            v0 *= inv_scale;
+            v1 *= inv_scale;
             const uint32_t row = item_r0 + r;
             if (ph.epilogue == EPI_SWIGLU) {
-                const float z = sm.rowres[0][r], up = sm.rowres[1][r];
-                ph.seg[0].out[row] = (z / (1.0f + expf(-z))) * up;   // src/brain_runtime.c:1755-1758
+                ph.seg[0].out[row] = (v0 / (1.0f + expf(-v0))) * v1;   // src/brain_runtime.c:1755-1758
             } else {
                 uint32_t sgi = 0;
                 while (sgi + 1 < ph.n_seg && row >= ph.seg_start[sgi + 1]) ++sgi;
                 const uint32_t lr = row - ph.seg_start[sgi];
-                const float v = sm.rowres[sgi][r];
                 float *out = ph.seg[sgi].out;
                 if (ph.epilogue == EPI_RESID_ADD) {
-                    out[lr] = __ldcg(out + lr) + v;
+                    out[lr] = __ldcg(out + lr) + v0;
                 } else {
                     const float *bias = ph.seg[sgi].bias;
-                    out[lr] = bias ? v + __ldg(bias + lr) : v;
-                    if (v > best || (v == best && lr < best_i)) { best = v; best_i = lr; }
+                    out[lr] = bias ? v0 + __ldg(bias + lr) : v0;
+                    if (v0 > best || (v0 == best && lr < best_i)) { best = v0; best_i = lr; }
                 }
             }
         }
-        consumer_sync();
     }
     if (ph.epilogue == EPI_LOGITS) {
-        // one (max, argmax) per CTA; the greedy pick reduces gridDim.x of them
+        // one (max, argmax) per CTA; the greedy pick reduces them
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ob = __shfl_xor_sync(0xffffffffu, best, o);
             const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
             if (ob > best || (ob == best && oi < best_i)) { best = ob; best_i = oi; }
         }
-        if (lane == 0) { sm.amax[warp] = best; sm.aidx[warp] = best_i; }
+        if (lane == 0) { sm.h->amax[warp] = best; sm.h->aidx[warp] = best_i; }
         consumer_sync();
         if (threadIdx.x == 0) {
             for (int w = 1; w < kConsumerWarps; ++w)
-                if (sm.amax[w] > best || (sm.amax[w] == best && sm.aidx[w] < best_i)) { best = sm.amax[w]; best_i = sm.aidx[w]; }
+                if (sm.h->amax[w] > best || (sm.h->amax[w] == best && sm.h->aidx[w] < best_i)) { best = sm.h->amax[w]; best_i = sm.h->aidx[w]; }
             ph.partial_max[blockIdx.x] = best;
             ph.partial_idx[blockIdx.x] = best_i;
         }
     }
+    consumer_sync();
     return true;
 }
 
@@ -520,7 +731,7 @@ __device__ __forceinline__ float warp_max(float v)
 // online softmax; P.V accumulates with lane = 4 output dims. The last split of
 // a head to finish combines all splits' (max, sum, acc) partials; a partial is
 // stored as acc[head_dim], max, sum, 2 pad floats (16-byte aligned records).
-__device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uint32_t &k, uint32_t pos,
+__device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &sm, uint32_t &k, uint32_t pos,
                                volatile uint32_t *err)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -535,7 +746,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
         const uint32_t p0 = s * L, p1 = min(p0 + L, pos + 1);
         const bool last_split = (p1 == pos + 1);
         // RoPE'd queries of the group; the fresh k (RoPE'd) and v in the last split
-        float *qf = reinterpret_cast<float *>(sm.q);
+        float *qf = reinterpret_cast<float *>(sm.a->q);
         for (uint32_t i = threadIdx.x; i < group * (hd / 2); i += kConsumerWarps * 32) {
             const uint32_t h = i / (hd / 2), p = i % (hd / 2);
             const float *qh = ph.q + (size_t)(g * group + h) * hd;
@@ -545,7 +756,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
             qf[h * hd + p + hd / 2] = b;
         }
         if (last_split) {
-            float *kn = reinterpret_cast<float *>(sm.knew), *vn = reinterpret_cast<float *>(sm.vnew);
+            float *kn = reinterpret_cast<float *>(sm.a->knew), *vn = reinterpret_cast<float *>(sm.a->vnew);
             for (uint32_t p = threadIdx.x; p < hd / 2; p += kConsumerWarps * 32) {
                 const float *kh = ph.k + (size_t)g * hd;
                 float a, b;
@@ -558,7 +769,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
         consumer_sync();
         if (last_split) {
             // KV append at pos (src/brain_runtime.c:1496-1500); read by the next steps.
-            const float *kn = reinterpret_cast<const float *>(sm.knew), *vn = reinterpret_cast<const float *>(sm.vnew);
+            const float *kn = reinterpret_cast<const float *>(sm.a->knew), *vn = reinterpret_cast<const float *>(sm.a->vnew);
             const size_t off = ((size_t)g * pg.max_context + pos) * hd;
             for (uint32_t i = threadIdx.x; i < hd; i += kConsumerWarps * 32) {
                 if (f16) {
@@ -570,32 +781,32 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
                 }
             }
         }
-        // per-warp state for up to two query heads (group <= 16 over 8 warps)
-        float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.f, 0.f};
-        float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+        // per-warp state for its query head (group <= 8 = one head per warp)
+        float m[1] = {-FLT_MAX}, l[1] = {0.f};
+        float4 acc[1] = {make_float4(0.f, 0.f, 0.f, 0.f)};
         const uint32_t cached_end = min(p1, pos);
         for (uint32_t t0 = p0; t0 < p1; t0 += kAttnChunk) {
             const bool staged = t0 < cached_end;
             const uint8_t *kst = nullptr, *vst = nullptr;
             if (staged) {
-                if (!stage_wait(pg, sm, k, pos, err)) return false;
-                if (!stage_wait(pg, sm, k + 1, pos, err)) return false;
+                if (!stage_wait(sm, k, err)) return false;
+                if (!stage_wait(sm, k + 1, err)) return false;
                 const uint32_t esz = f16 ? 2u : 4u;
                 const uintptr_t ka = reinterpret_cast<uintptr_t>(ph.k_cache) + ((size_t)g * pg.max_context + t0) * hd * esz;
                 const uintptr_t va = reinterpret_cast<uintptr_t>(ph.v_cache) + ((size_t)g * pg.max_context + t0) * hd * esz;
-                kst = sm.stage[k % kStages] + (ka & 15u);
-                vst = sm.stage[(k + 1) % kStages] + (va & 15u);
+                kst = sm.stage(k) + (ka & 15u);
+                vst = sm.stage(k + 1) + (va & 15u);
             }
             const uint32_t t_end = min(t0 + (uint32_t)kAttnChunk, p1);
             for (uint32_t sb = t0; sb < t_end; sb += 32) {
                 const uint32_t p = sb + (uint32_t)lane;
                 const bool valid = p < t_end;
                 const bool fresh = p == pos;
-                const uint8_t *krow = fresh ? reinterpret_cast<const uint8_t *>(sm.knew)
+                const uint8_t *krow = fresh ? reinterpret_cast<const uint8_t *>(sm.a->knew)
                                             : (staged ? kst + (size_t)(p - t0) * row_bytes : nullptr);
                 const bool krow_f16 = f16 && !fresh;
 #pragma unroll
-                for (int hi = 0; hi < 2; ++hi) {
+                for (int hi = 0; hi < 1; ++hi) {
                     const uint32_t h = (uint32_t)warp + (uint32_t)hi * kConsumerWarps;
                     if (h >= group) break;
                     float sc = -FLT_MAX;
@@ -604,7 +815,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
 #pragma unroll 8
                         for (uint32_t i = 0; i < 32; ++i) {
                             const uint32_t d4 = (i + (uint32_t)lane) & 31u;
-                            const float4 qv = sm.q[h][d4];
+                            const float4 qv = sm.a->q[h][d4];
                             const float4 kv = kv_row4(krow, d4, krow_f16);
                             dot = fmaf(qv.x, kv.x, dot);
                             dot = fmaf(qv.y, kv.y, dot);
@@ -623,7 +834,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
                     for (uint32_t j = 0; j < np; ++j) {
                         const float wj = __shfl_sync(0xffffffffu, w, (int)j);
                         const uint32_t pj = sb + j;
-                        const float4 vv = pj == pos ? sm.vnew[lane]
+                        const float4 vv = pj == pos ? sm.a->vnew[lane]
                                                     : kv_row4(vst + (size_t)(pj - t0) * row_bytes, (uint32_t)lane, f16);
                         a.x = fmaf(wj, vv.x, a.x);
                         a.y = fmaf(wj, vv.y, a.y);
@@ -635,12 +846,12 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
                 }
             }
             if (staged) {
-                stage_release(pg, sm, k, pos);
-                stage_release(pg, sm, k + 1, pos);
+                stage_release(sm, k);
+                stage_release(sm, k + 1);
                 k += 2;
             }
         }
-        for (int hi = 0; hi < 2; ++hi) {
+        for (int hi = 0; hi < 1; ++hi) {
             const uint32_t h = (uint32_t)warp + (uint32_t)hi * kConsumerWarps;
             if (h >= group) break;
             float *dst = ph.part + (((size_t)g * nsplit + s) * group + h) * (hd + 4);
@@ -652,11 +863,11 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
         if (threadIdx.x == 0) {
             __threadfence();
             const uint32_t old = atom_acq_rel_add(ph.split_ctr + g, 1u);
-            sm.flag = (old == nsplit - 1u) ? 1u : 0u;
-            if (sm.flag) { ph.split_ctr[g] = 0u; __threadfence(); }
+            sm.h->flag = (old == nsplit - 1u) ? 1u : 0u;
+            if (sm.h->flag) { ph.split_ctr[g] = 0u; __threadfence(); }
         }
         consumer_sync();
-        if (sm.flag) {
+        if (sm.h->flag) {
             for (uint32_t h = (uint32_t)warp; h < group; h += kConsumerWarps) {
                 float M = -FLT_MAX;
                 for (uint32_t q = (uint32_t)lane; q < nsplit; q += 32)
@@ -666,18 +877,18 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
                 for (uint32_t q = (uint32_t)lane; q < nsplit; q += 32) {
                     const float *src = ph.part + (((size_t)g * nsplit + q) * group + h) * (hd + 4);
                     const float w = expf(__ldcg(src + hd) - M);
-                    sm.cw[q][h] = w;
+                    sm.a->cw[q][h] = w;
                     den += w * __ldcg(src + hd + 1);
                 }
                 den = warp_sum(den);
-                if (lane == 0) sm.cden[h] = den;
+                if (lane == 0) sm.a->cden[h] = den;
             }
             consumer_sync();
             for (uint32_t i = threadIdx.x; i < group * (hd / 4); i += kConsumerWarps * 32) {
                 const uint32_t h = i / (hd / 4), d4 = i % (hd / 4);
                 float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (uint32_t q = 0; q < nsplit; ++q) {
-                    const float w = sm.cw[q][h];
+                    const float w = sm.a->cw[q][h];
                     const float4 v = __ldcg(reinterpret_cast<const float4 *>(
                         ph.part + (((size_t)g * nsplit + q) * group + h) * (hd + 4)) + d4);
                     num.x = fmaf(w, v.x, num.x);
@@ -685,7 +896,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, Smem &sm, uin
                     num.z = fmaf(w, v.z, num.z);
                     num.w = fmaf(w, v.w, num.w);
                 }
-                const float den = sm.cden[h];
+                const float den = sm.a->cden[h];
                 const float inv = den > 0.f ? 1.0f / den : 0.f;
                 float4 o = make_float4(num.x * inv, num.y * inv, num.z * inv, num.w * inv);
                 reinterpret_cast<float4 *>(ph.att + (size_t)(g * group + h) * hd)[d4] = o;
@@ -709,7 +920,7 @@ __device__ void run_embed_phase(const Program &pg, const Phase &ph, uint32_t tok
 }
 
 // Greedy pick over the head items' partials (lowest index among equal maxima).
-__device__ void run_argmax_phase(const Program &pg, const Phase &ph, Smem &sm)
+__device__ void run_argmax_phase(const Program &pg, const Phase &ph, const Smem &sm)
 {
     if (blockIdx.x != 0) return;
     const Phase &head = pg.phases[ph.layer];  // index of the logits phase
@@ -728,11 +939,11 @@ __device__ void run_argmax_phase(const Program &pg, const Phase &ph, Smem &sm)
         const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
     }
-    if (lane == 0) { sm.amax[warp] = best; sm.aidx[warp] = bi; }
+    if (lane == 0) { sm.h->amax[warp] = best; sm.h->aidx[warp] = bi; }
     consumer_sync();
     if (threadIdx.x == 0) {
         for (int w = 1; w < kConsumerWarps; ++w)
-            if (sm.amax[w] > best || (sm.amax[w] == best && sm.aidx[w] < bi)) { best = sm.amax[w]; bi = sm.aidx[w]; }
+            if (sm.h->amax[w] > best || (sm.h->amax[w] == best && sm.h->aidx[w] < bi)) { best = sm.h->amax[w]; bi = sm.h->aidx[w]; }
         StepState *st = pg.state;
         st->next_token = bi;
         st->next_logit = best;
@@ -740,10 +951,8 @@ __device__ void run_argmax_phase(const Program &pg, const Phase &ph, Smem &sm)
     }
 }
 
-template <int NS>
-__device__ bool dispatch_gemv(const Program &pg, const Phase &ph, Smem &sm, uint32_t &k, volatile uint32_t *err);
 
-__device__ bool consumer(const Program &pg, Smem &sm, uint32_t pos, uint32_t token, uint32_t epoch,
+__device__ bool consumer(const Program &pg, const Smem &sm, uint32_t pos, uint32_t token, uint32_t epoch,
                          volatile uint32_t *err)
 {
     uint32_t k = 0;
@@ -753,19 +962,12 @@ __device__ bool consumer(const Program &pg, Smem &sm, uint32_t pos, uint32_t tok
         const uint32_t n = phase_items(pg, ph, pos);
         const bool mine = blockIdx.x < n;
         if (tr && threadIdx.x == 0) tr[p * 4 + 0] = global_ns();
-        if (mine && p > 0 && !wait_phase(pg, sm, p - 1, epoch, pos, err)) return false;
+        if (mine && p > 0 && !wait_phase(pg, p - 1, epoch, err)) return false;
         if (tr && threadIdx.x == 0) tr[p * 4 + 1] = global_ns();
         if (mine) {
             bool ok = true;
             switch (ph.kind) {
-            case PH_GEMV:
-                switch (ph.n_slices) {
-                case 1: ok = run_gemv_phase<1>(pg, ph, sm, k, pos, err); break;
-                case 2: ok = run_gemv_phase<2>(pg, ph, sm, k, pos, err); break;
-                case 3: ok = run_gemv_phase<(kMaxSlices >= 3 ? 3 : 1)>(pg, ph, sm, k, pos, err); break;
-                default: ok = run_gemv_phase<kMaxSlices>(pg, ph, sm, k, pos, err); break;
-                }
-                break;
+            case PH_GEMV: ok = run_gemv_phase(pg, ph, sm, k, err); break;
             case PH_ATTN: ok = run_attn_phase(pg, ph, sm, k, pos, err); break;
             case PH_EMBED: run_embed_phase(pg, ph, token); break;
             case PH_ARGMAX: run_argmax_phase(pg, ph, sm); break;
@@ -782,36 +984,33 @@ __device__ bool consumer(const Program &pg, Smem &sm, uint32_t pos, uint32_t tok
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(Program pg)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    Smem sm;
+    sm.h = reinterpret_cast<SmemHdr *>(smem_raw);
+    sm.xarea = smem_raw + kHdrBytes;
+    sm.a = reinterpret_cast<AttnSmem *>(sm.xarea);
+    sm.ring = sm.xarea + max(x_area_bytes(pg.max_cols), (uint32_t)((sizeof(AttnSmem) + 127u) & ~127u));
+    sm.n_stages = pg.n_stages;
+    sm.stage_bytes = pg.stage_bytes;
     StepState *st = pg.state;
     volatile uint32_t *err = &st->status;
     const uint32_t pos = st->pos, token = st->token, epoch = st->epoch;
+    const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], kConsumerWarps);
+        for (uint32_t s = 0; s < sm.n_stages; ++s) {
+            mbar_init(&sm.h->full[s], 1);
+            mbar_init(&sm.h->empty[s], kConsumerWarps);
         }
         fence_mbar_init();
-        sm.pump_p = 0;
-        sm.pump_it = 0;
-        sm.pump_c = 0xffffffffu;
-        sm.pump_nc = 0xffffffffu;
-        sm.pump_issued = 0;
-        sm.pump_done = pg.n_phases == 0;
     }
     __syncthreads();
-    if (threadIdx.x == 0) pump(pg, sm, pos);
-    consumer(pg, sm, pos, token, epoch, err);
+    if (warp == kConsumerWarps) {
+        if ((threadIdx.x & 31) == 0) producer(pg, sm, pos, err);
+    } else {
+        consumer(pg, sm, pos, token, epoch, err);
+    }
     __syncthreads();
+    // The last CTA out advances the step state for the next launch.
     if (threadIdx.x == 0) {
-        // Every issued copy must have landed before the CTA exits (they all
-        // have on the normal path; after an error some may still be in flight).
-        for (uint32_t j = 0; j < sm.pump_issued; ++j) {
-            if (j + kStages < sm.pump_issued) continue;
-            uint64_t t0 = global_ns();
-            while (!mbar_test(&sm.full[j % kStages], (j / kStages) & 1u) && global_ns() - t0 < kWaitLimitNs) {}
-        }
-        // The last CTA out advances the step state for the next launch.
         __threadfence();
         const uint32_t old = atom_acq_rel_add(&st->exit_ctr, 1u);
         if (old == (epoch + 1u) * gridDim.x - 1u) {
@@ -828,23 +1027,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(Program pg)
 
 }  // namespace atlas
 
-// Host-side launcher (used by model.cu).
+extern "C" size_t atlas_decode_hdr_bytes() { return atlas::kHdrBytes; }
+extern "C" size_t atlas_decode_attn_bytes() { return (sizeof(atlas::AttnSmem) + 127u) & ~size_t(127); }
+
+// Host-side launcher (used by model.cu). smem = header + x area + ring.
 extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream)
 {
-    const size_t smem = sizeof(atlas::Smem);
-    static bool configured[64] = {};
+    const size_t xa = std::max<size_t>(atlas::x_area_bytes(pg->max_cols), (sizeof(atlas::AttnSmem) + 127u) & ~size_t(127));
+    const size_t smem = atlas::kHdrBytes + xa + (size_t)pg->n_stages * pg->stage_bytes;
+    static size_t configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
+    if (configured[dev] < smem) {
         e = cudaFuncSetAttribute(atlas::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured[dev] = smem;
     }
     void *args[] = {const_cast<atlas::Program *>(pg)};
     return cudaLaunchCooperativeKernel((const void *)atlas::decode_kernel, dim3(grid), dim3(atlas::kThreads), args, smem,
                                        stream);
 }
-
-extern "C" size_t atlas_decode_smem_bytes() { return sizeof(atlas::Smem); }

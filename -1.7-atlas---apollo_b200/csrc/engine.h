@@ -14,20 +14,16 @@
 
 namespace atlas {
 
-// 8 warps: two per SM sub-partition, which lets each thread hold up to 255
-// registers (the per-lane input slices live in registers). The bulk copies
-// are issued by thread 0 in between its own work (see the "pump" in decode.cu).
+// 8 consumer warps + 1 producer warp per CTA, one CTA per SM.
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = kConsumerWarps * 32;
-constexpr int kStages = 6;
-constexpr uint32_t kStageBytes = 32768;
-constexpr int kMaxSlices = 4;        // per-lane x slices held in registers
-constexpr int kMaxItemRows = 64;     // rows of one segment in one item
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxStages = 8;
+constexpr int kMaxItemRows = 64;     // rows of one segment in one GEMV item (multiple of 16)
 constexpr int kMaxSeg = 3;
 constexpr int kHeadDim = 128;
 constexpr int kAttnChunk = 64;       // cached positions per staged K (or V) chunk
-constexpr int kMaxSplits = 128;      // attention splits per KV head
-constexpr int kMaxGroup = 16;        // query heads per KV head
+constexpr int kMaxSplits = 64;       // attention splits per KV head
+constexpr int kMaxGroup = 8;         // query heads per KV head (one warp each)
 
 enum PhaseKind : uint32_t {
     PH_EMBED = 0,   // x = dequant(token_embd row of the current token)
@@ -61,21 +57,27 @@ struct Phase {
     uint32_t kind;
     uint32_t layer;
     // ---- PH_GEMV ----
+    // An item is item_rows rows of every segment it touches (paired: the same
+    // rows of each segment; otherwise a range of the concatenated row space).
+    // Its bytes are staged in chunks of item_rows rows x chunk_blocks block
+    // columns: contiguous rows when chunk_blocks covers the row (seg_stride 0),
+    // else one copy per row segment, row i at stage + i * seg_stride.
     uint32_t n_items;
-    uint32_t item_rows;     // rows per item (row space: concatenated segments, or paired)
-    uint32_t paired;        // 1: each item covers rows [r0,r1) of EVERY segment (gate/up)
+    uint32_t item_rows;
+    uint32_t paired;
     uint32_t n_seg;
     uint32_t cols;          // input length (multiple of 256)
-    uint32_t warps_per_row; // W: consumer warps cooperating on one row
-    uint32_t n_slices;      // per-lane 32-element slices: ceil(cols/32 / (32*W))
+    uint32_t chunk_rows;    // rows per chunk (16 or 32; divides item_rows)
+    uint32_t chunk_blocks;  // block columns per chunk
+    uint32_t seg_stride;    // bytes per row segment in a segmented chunk (0: contiguous)
     uint32_t input_mode;
     uint32_t epilogue;
     uint32_t seg_start[kMaxSeg + 1];  // cumulative row offsets (concatenated row space)
     Seg seg[kMaxSeg];
     const float *in;        // input vector (cols floats)
     const float *norm_w;    // IN_RMSNORM weight
-    float *partial_max;     // EPI_LOGITS: per-item max
-    uint32_t *partial_idx;  // EPI_LOGITS: per-item argmax
+    float *partial_max;     // EPI_LOGITS: per-CTA max
+    uint32_t *partial_idx;  // EPI_LOGITS: per-CTA argmax
     // ---- PH_ATTN ----
     const float *q, *k, *v; // fresh projections (bias added, RoPE not yet applied)
     void *k_cache, *v_cache;// this layer's cache, [kv_head][position][head_dim]
@@ -88,7 +90,7 @@ struct Phase {
     uint32_t embd_type;
     float *x;
     // ---- PH_ARGMAX ----
-    uint32_t argmax_items;  // number of head items holding partials
+    uint32_t argmax_items;  // number of CTAs holding head partials
 };
 
 // Mutable per-launch state in device memory. The first two fields are owned
@@ -121,6 +123,13 @@ struct Program {
     uint32_t max_context;
     uint32_t advance;      // 1: after the step, token = next_token and pos += 1
     uint64_t *trace;       // optional: [cta][phase][4] globaltimer stamps (diagnostics)
+    // shared-memory plan (host-chosen per model)
+    uint32_t n_stages;     // bulk-copy ring depth
+    uint32_t stage_bytes;  // bytes per stage (multiple of 128)
+    uint32_t max_cols;     // largest GEMV input length (x staging area)
 };
+
+// Dynamic shared memory: [SmemHdr][x staging: max_cols * 4.25 B][stages]
+constexpr uint32_t x_area_bytes(uint32_t max_cols) { return ((max_cols * 4u + max_cols / 4u) + 127u) & ~127u; }
 
 }  // namespace atlas

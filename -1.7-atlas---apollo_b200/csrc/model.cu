@@ -7,6 +7,7 @@
 // fp16 (or fp32); activations x, q, k, v, att, ffn (fp32), logits (fp32);
 // attention split partials; a RoPE (cos, sin) table built on the host with the
 // reference's own powf / cosf / sinf (src/brain_runtime.c:1383-1387).
+#include <algorithm>
 #include <cmath>
 #include <cstddef>
 #include <cstdarg>
@@ -20,6 +21,8 @@
 #include "quant.cuh"
 
 extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream);
+extern "C" size_t atlas_decode_hdr_bytes();
+extern "C" size_t atlas_decode_attn_bytes();
 
 
 using namespace atlas;
@@ -72,6 +75,7 @@ struct AtlasCuda {
     uint64_t launches = 0;
     double last_ms = 0.0;
     double total_ms = 0.0;
+    uint32_t n_stages = 0, stage_bytes = 0, max_cols = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 };
 
@@ -201,59 +205,79 @@ int upload_vector(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t n, const floa
     return ATLAS_OK;
 }
 
-// Rows per work item: as many as fit a stage (and kMaxItemRows), reduced where
-// that evens out the items over the grid.
-uint32_t pick_item_rows(uint32_t total_rows, uint64_t max_row_bytes, uint32_t grid)
+// GEMV geometry. Items are 16, 32 or 64 rows (MMA row tiles of 16; powers of
+// two so item boundaries line up with segment boundaries, which are multiples
+// of 128). Chunks are whole rows when 16 rows fit a stage, otherwise 16-row x
+// chunk_blocks-column tiles staged one row segment at a time.
+void plan_gemv(Phase &ph, uint32_t total_rows, uint32_t grid, uint32_t stage_bytes)
 {
-    uint32_t fit = (uint32_t)((kStageBytes - 32) / max_row_bytes);
-    if (fit > (uint32_t)kMaxItemRows) fit = kMaxItemRows;
-    if (fit < 1) fit = 1;
-    uint32_t best = fit;
-    double best_eff = -1.0;
-    for (uint32_t r = fit; r >= 1; --r) {
-        const uint32_t items = (total_rows + r - 1) / r;
-        const uint32_t waves = (items + grid - 1) / grid;
-        const double eff = (double)items / ((double)waves * grid) * ((double)total_rows / ((double)items * r));
-        if (eff > best_eff + 1e-9) { best_eff = eff; best = r; }
-        if (r == 1) break;
+    const uint32_t nb = ph.cols / 256u;
+    uint32_t bb_max = 0;
+    for (uint32_t s = 0; s < ph.n_seg; ++s) bb_max = std::max(bb_max, block_bytes(ph.seg[s].type));
+    const uint64_t row_max = (uint64_t)nb * bb_max;
+    if (16u * row_max + 32u <= stage_bytes) {
+        ph.chunk_blocks = nb;
+        ph.seg_stride = 0;
+        ph.chunk_rows = (32u * row_max + 32u <= stage_bytes) ? 32u : 16u;
+        // largest item (<= 64 rows) that still gives every CTA work
+        ph.item_rows = 16;
+        for (uint32_t r : {64u, 32u}) {
+            if ((total_rows + r - 1) / r >= grid) { ph.item_rows = r; break; }
+        }
+        if (ph.chunk_rows > ph.item_rows) ph.chunk_rows = ph.item_rows;
+    } else {
+        // 16 row segments of B blocks each, every segment padded by <= 45 bytes
+        uint32_t B = (stage_bytes - 16u * 48u) / (16u * bb_max);
+        if (B < 1) B = 1;
+        const uint32_t nch = (nb + B - 1) / B;
+        B = (nb + nch - 1) / nch;  // even out the column chunks
+        ph.chunk_blocks = B;
+        ph.seg_stride = (B * bb_max + 30u + 15u) & ~15u;
+        ph.chunk_rows = 16;
+        ph.item_rows = 16;
     }
-    return best;
+    ph.n_items = (total_rows + ph.item_rows - 1) / ph.item_rows;
 }
 
-void pick_row_split(uint32_t cols, uint32_t &W, uint32_t &ns)
-{
-    const uint32_t S = cols / 32u;
-    for (W = 1; W <= (uint32_t)kConsumerWarps; W *= 2) {
-        ns = (S + 32u * W - 1u) / (32u * W);
-        if (ns <= (uint32_t)kMaxSlices) return;
-    }
-    W = kConsumerWarps;
-    ns = (S + 32u * W - 1u) / (32u * W);
-}
-
-Phase gemv_phase(uint32_t cols, uint32_t grid, bool paired, std::initializer_list<Seg> segs, const float *in,
-                 uint32_t input_mode, const float *norm_w, uint32_t epi)
+Phase gemv_phase(uint32_t cols, uint32_t grid, uint32_t stage_bytes, bool paired, std::initializer_list<Seg> segs,
+                 const float *in, uint32_t input_mode, const float *norm_w, uint32_t epi)
 {
     Phase ph{};
     ph.kind = PH_GEMV;
     ph.cols = cols;
     ph.paired = paired ? 1u : 0u;
     ph.n_seg = 0;
-    uint64_t max_rb = 0;
     for (const Seg &s : segs) {
         ph.seg_start[ph.n_seg + 1] = ph.seg_start[ph.n_seg] + s.rows;
         ph.seg[ph.n_seg++] = s;
-        if (s.row_bytes > max_rb) max_rb = s.row_bytes;
     }
     const uint32_t total = paired ? ph.seg[0].rows : ph.seg_start[ph.n_seg];
-    ph.item_rows = pick_item_rows(total, max_rb, grid);
-    ph.n_items = (total + ph.item_rows - 1) / ph.item_rows;
-    pick_row_split(cols, ph.warps_per_row, ph.n_slices);
+    plan_gemv(ph, total, grid, stage_bytes);
     ph.in = in;
     ph.input_mode = input_mode;
     ph.norm_w = norm_w;
     ph.epilogue = epi;
     return ph;
+}
+
+// Shared-memory plan: header + x staging for the longest GEMV input + as many
+// 56 KB stages as fit (2..kMaxStages).
+constexpr uint32_t kStageBytesDefault = 57344;
+
+int plan_smem(int device, uint32_t max_cols, uint32_t &n_stages, uint32_t &stage_bytes)
+{
+    int optin = 0;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess) return ATLAS_ECUDA;
+    const size_t xa = std::max<size_t>(x_area_bytes(max_cols), atlas_decode_attn_bytes());
+    const size_t fixed = atlas_decode_hdr_bytes() + xa + 1024;  // + static shared margin
+    if ((size_t)optin <= fixed) return ATLAS_EINVAL;
+    const size_t avail = (size_t)optin - fixed;
+    // at least 3 stages; a stage must hold one 64-position fp32 K (or V) tile
+    size_t sb = std::min<size_t>(kStageBytesDefault, (avail / 3) & ~size_t(127));
+    if (sb < 33792) return ATLAS_EINVAL;
+    stage_bytes = (uint32_t)sb;
+    n_stages = (uint32_t)std::min<size_t>(kMaxStages, avail / sb);
+    return ATLAS_OK;
 }
 
 Seg seg_of(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, const float *bias, float *out)
@@ -279,6 +303,11 @@ int finalize_program(AtlasCuda *h, ProgramBuffers &pb, const AtlasCuda *m)
     if ((rc = dalloc(h, &pb.d_state, sizeof(StepState)))) return rc;
     CU(h, cudaMemset(pb.d_state, 0, sizeof(StepState)));
     pb.pg.phases = pb.d_phases;
+    if (m) {
+        pb.pg.n_stages = m->n_stages;
+        pb.pg.stage_bytes = m->stage_bytes;
+        pb.pg.max_cols = m->max_cols;
+    }
     pb.pg.n_phases = (uint32_t)n;
     pb.pg.phase_ctr = pb.d_ctr;
     pb.pg.state = pb.d_state;
@@ -358,6 +387,10 @@ int build_decode_program(AtlasCuda *h)
 {
     const AtlasModelDesc &d = h->desc;
     const uint32_t G = (uint32_t)h->sm_count;
+    h->max_cols = std::max(d.hidden, std::max(d.q_dim, d.ffn));
+    if (plan_smem(d.device, h->max_cols, h->n_stages, h->stage_bytes) != ATLAS_OK)
+        return fail(h, ATLAS_EINVAL, "model too large for the shared-memory plan (input length %u)", h->max_cols);
+    const uint32_t SB = h->stage_bytes;
     std::vector<Phase> &P = h->decode.phases;
     Phase e{};
     e.kind = PH_EMBED;
@@ -368,7 +401,7 @@ int build_decode_program(AtlasCuda *h)
     P.push_back(e);
     for (uint32_t l = 0; l < d.layers; ++l) {
         const AtlasCuda::W &w = h->layers[l];
-        Phase qkv = gemv_phase(d.hidden, G, false,
+        Phase qkv = gemv_phase(d.hidden, G, SB, false,
                                {seg_of(w.q, w.tq, d.q_dim, d.hidden, w.bq, h->q),
                                 seg_of(w.k, w.tk, d.kv_dim, d.hidden, w.bk, h->k),
                                 seg_of(w.v, w.tv, d.kv_dim, d.hidden, w.bv, h->v)},
@@ -384,26 +417,27 @@ int build_decode_program(AtlasCuda *h)
         at.part = h->part;
         at.split_ctr = h->split_ctr;
         P.push_back(at);
-        Phase o = gemv_phase(d.q_dim, G, false, {seg_of(w.o, w.to, d.hidden, d.q_dim, nullptr, h->x)}, h->att, IN_RAW,
+        Phase o = gemv_phase(d.q_dim, G, SB, false, {seg_of(w.o, w.to, d.hidden, d.q_dim, nullptr, h->x)}, h->att, IN_RAW,
                              nullptr, EPI_RESID_ADD);
         o.layer = l;
         P.push_back(o);
-        Phase gu = gemv_phase(d.hidden, G, true,
+        Phase gu = gemv_phase(d.hidden, G, SB, true,
                               {seg_of(w.gate, w.tg, d.ffn, d.hidden, nullptr, h->ffn),
                                seg_of(w.up, w.tu, d.ffn, d.hidden, nullptr, nullptr)},
                               h->x, IN_RMSNORM, w.ffn_norm, EPI_SWIGLU);
         gu.layer = l;
         P.push_back(gu);
-        Phase dn = gemv_phase(d.ffn, G, false, {seg_of(w.down, w.td, d.hidden, d.ffn, nullptr, h->x)}, h->ffn, IN_RAW,
+        Phase dn = gemv_phase(d.ffn, G, SB, false, {seg_of(w.down, w.td, d.hidden, d.ffn, nullptr, h->x)}, h->ffn, IN_RAW,
                               nullptr, EPI_RESID_ADD);
         dn.layer = l;
         P.push_back(dn);
     }
-    Phase hd = gemv_phase(d.hidden, G, false, {seg_of(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)}, h->x,
+    Phase hd = gemv_phase(d.hidden, G, SB, false, {seg_of(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)}, h->x,
                           IN_RMSNORM, h->out_norm, EPI_LOGITS);
-    int rc = dalloc(h, &h->pmax, hd.n_items * sizeof(float));
+    // one (max, argmax) partial per CTA that holds head items
+    int rc = dalloc(h, &h->pmax, (size_t)G * sizeof(float));
     if (rc) return rc;
-    if ((rc = dalloc(h, &h->pidx, hd.n_items * sizeof(uint32_t)))) return rc;
+    if ((rc = dalloc(h, &h->pidx, (size_t)G * sizeof(uint32_t)))) return rc;
     hd.partial_max = h->pmax;
     hd.partial_idx = h->pidx;
     const uint32_t head_index = (uint32_t)P.size();
@@ -411,7 +445,7 @@ int build_decode_program(AtlasCuda *h)
     Phase am{};
     am.kind = PH_ARGMAX;
     am.layer = head_index;
-    am.argmax_items = hd.n_items;
+    am.argmax_items = std::min(hd.n_items, G);
     P.push_back(am);
     rc = finalize_program(h, h->decode, h);
     if (rc) return rc;
@@ -686,7 +720,7 @@ extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t ro
                                float *d_y, void *stream)
 {
     if ((type != ATLAS_TYPE_Q4_K && type != ATLAS_TYPE_Q6_K) || !d_weights || !d_x || !d_y || !rows || !cols ||
-        cols % 256 || rows > 0xffffffffu || cols > (uint64_t)kMaxSlices * 32 * 32 * kConsumerWarps)
+        cols % 256 || rows > 0xffffffffu || cols > 65536)
         return fail(nullptr, ATLAS_EINVAL, "bad gemv arguments");
     if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
         return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
@@ -707,12 +741,19 @@ extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t ro
         int rc = finalize_program(&tmp, c.pb, nullptr);
         if (rc) { c.device = -1; return rc; }
     }
-    Phase ph = gemv_phase((uint32_t)cols, (uint32_t)c.sms, false,
+    uint32_t n_stages = 0, stage_bytes = 0;
+    if (plan_smem(dev, (uint32_t)cols, n_stages, stage_bytes) != ATLAS_OK)
+        return fail(nullptr, ATLAS_EINVAL, "input length %llu too large", (unsigned long long)cols);
+    Phase ph = gemv_phase((uint32_t)cols, (uint32_t)c.sms, stage_bytes, false,
                           {seg_of((const uint8_t *)d_weights, type, (uint32_t)rows, (uint32_t)cols, nullptr, d_y)},
                           d_x, IN_RAW, nullptr, EPI_STORE);
+    Program pg = c.pb.pg;
+    pg.n_stages = n_stages;
+    pg.stage_bytes = stage_bytes;
+    pg.max_cols = (uint32_t)cols;
     cudaStream_t s = (cudaStream_t)stream;
     cudaError_t e = cudaMemcpyAsync(c.pb.d_phases, &ph, sizeof(Phase), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = atlas_launch_decode(&c.pb.pg, c.sms, s);
+    if (e == cudaSuccess) e = atlas_launch_decode(&pg, c.sms, s);
     if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return ATLAS_OK;
 }
