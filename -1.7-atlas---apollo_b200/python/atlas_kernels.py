@@ -1,0 +1,93 @@
+"""Kernel-level timing of libatlas_cuda's C ABI entry points on seeded synthetic data.
+
+    python -m atlas_kernels gemv --type 14 --rows 151936 --cols 2048 [--reps 20]
+    python -m atlas_kernels trace --hidden 2048 --layers 36 --q-heads 16 --kv-heads 2 --ffn 11008 --pos 600
+
+`gemv` times atlas_cuda_gemv with CUDA events (with --reps 1 it runs one warm-up
+and one launch, the shape an ncu capture wants); `trace` runs one decode step
+with device-side timestamps (atlas_cuda_trace_step) and prints the time per
+phase kind. Device buffers come from torch; every kernel is this library's.
+"""
+import argparse
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import atlas_cuda  # noqa: E402
+
+KIND = {0: "embed", 16: "gemv_store", 17: "gemv_resid_add", 18: "gemv_swiglu", 19: "gemv_logits", 32: "attention",
+        48: "argmax"}
+
+
+def cmd_gemv(a):
+    import torch
+    nb = a.rows * a.cols // 256
+    w = atlas_cuda.synth_blocks(a.type, nb, seed=1)
+    d_w = torch.from_numpy(w).cuda()
+    d_x = torch.randn(a.cols, device="cuda")
+    d_y = torch.empty(a.rows, device="cuda")
+    atlas_cuda.gemv(a.type, d_w, a.rows, a.cols, d_x, d_y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        atlas_cuda.gemv(a.type, d_w, a.rows, a.cols, d_x, d_y)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.reps
+    print(f"gemv type {a.type} {a.rows}x{a.cols}: {w.nbytes / 1e6:.1f} MB, {ms * 1e3:.1f} us, "
+          f"{w.nbytes / ms / 1e6:.0f} GB/s")
+
+
+def cmd_trace(a):
+    path = os.path.join(tempfile.gettempdir(), f"atlas_trace_{a.hidden}_{a.layers}_{a.ffn}_{a.vocab}.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
+    with atlas_cuda.Runtime(path, max_context=a.pos + 16) as rt:
+        rt.prefill(np.arange(1, a.pos + 1, dtype=np.uint32) % a.vocab, 0, want_logits=False)
+        tr, kinds = rt.trace_step(7, a.pos)
+    tr = tr.astype(np.int64)
+    t0 = tr[tr > 0].min()
+    tr = np.where(tr > 0, tr - t0, -1)
+    end = tr[:, :, 2].max()
+    print(f"decode step at position {a.pos}: {end / 1e3:.1f} us over {len(kinds)} phases")
+    agg, prev = {}, 0
+    for p, k in enumerate(kinds):
+        done = tr[:, p, 2].max()
+        work = (tr[:, p, 2] - tr[:, p, 1]).mean()
+        s = agg.setdefault(KIND.get(int(k), str(k)), [0, 0.0, 0])
+        s[0] += done - prev
+        s[1] += work
+        s[2] += 1
+        prev = done
+    for name, (tot, work, n) in agg.items():
+        print(f"  {name:16s} x{n:3d}  {tot / 1e3:9.1f} us total  {tot / n / 1e3:7.2f} us each  (mean CTA work "
+              f"{work / n / 1e3:6.2f} us)")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemv")
+    g.add_argument("--type", type=int, default=14)
+    g.add_argument("--rows", type=int, default=151936)
+    g.add_argument("--cols", type=int, default=2048)
+    g.add_argument("--reps", type=int, default=20)
+    t = sub.add_parser("trace")
+    t.add_argument("--hidden", type=int, default=2048)
+    t.add_argument("--layers", type=int, default=36)
+    t.add_argument("--q-heads", type=int, default=16)
+    t.add_argument("--kv-heads", type=int, default=2)
+    t.add_argument("--ffn", type=int, default=11008)
+    t.add_argument("--vocab", type=int, default=151936)
+    t.add_argument("--pos", type=int, default=600)
+    a = ap.parse_args()
+    cmd_gemv(a) if a.cmd == "gemv" else cmd_trace(a)
+
+
+if __name__ == "__main__":
+    main()
