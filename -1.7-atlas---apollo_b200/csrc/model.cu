@@ -764,3 +764,88 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
     (void)type; (void)d_weights; (void)rows; (void)cols; (void)d_x; (void)tokens; (void)d_y; (void)stream;
     return fail(nullptr, ATLAS_EINVAL, "the tcgen05 prefill GEMM is not built in this version");
 }
+
+// ---------------------------------------------------------------------------
+// A GEMV entry point that allocates nothing
+// ---------------------------------------------------------------------------
+//
+// For callers that cannot allocate device memory: a host that reserves all of
+// HBM up front for weights and KV cache and hands plugins no allocator, or a
+// path with a latency budget that cannot absorb cudaMalloc's implicit device
+// synchronisation. atlas_cuda_gemv keeps its launch scratch in buffers it
+// cudaMallocs on first use; this variant keeps the same scratch - the decode
+// kernel's phase descriptor, its phase counters and its step state - in a
+// fixed 4 KB array of this module's static device memory instead, which every
+// GPU that loads the library holds until the process exits.
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4096;
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr size_t kNoAllocPhaseOff = 0;
+constexpr size_t kNoAllocCtrOff = (sizeof(Phase) + 255) & ~size_t(255);
+constexpr size_t kNoAllocStateOff = kNoAllocCtrOff + 256;
+constexpr size_t kNoAllocNeeded = kNoAllocStateOff + sizeof(StepState);
+static_assert(kNoAllocNeeded <= kNoAllocScratchBytes, "no-alloc scratch too small for the launch descriptor");
+
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[64];  // device address of g_noalloc_scratch, per device
+
+}  // namespace
+
+extern "C" int atlas_cuda_gemv_noalloc(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
+                                       const float *d_x, float *d_y, void *stream)
+{
+    if ((type != ATLAS_TYPE_Q4_K && type != ATLAS_TYPE_Q6_K) || !d_weights || !d_x || !d_y || !rows || !cols ||
+        cols % 256 || rows > 0xffffffffu)
+        return fail(nullptr, ATLAS_EINVAL, "bad gemv arguments");
+    if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
+        return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
+    if ((uintptr_t)d_weights & 1u) return fail(nullptr, ATLAS_EINVAL, "weights must be 2-byte aligned");
+    if (((uintptr_t)d_x & 15u) || ((uintptr_t)d_y & 3u))
+        return fail(nullptr, ATLAS_EINVAL, "x must be 16-byte aligned and y 4-byte aligned");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    if (dev < 0 || dev >= 64 || device_ok(dev, &sms) != ATLAS_OK) return fail(nullptr, ATLAS_ENODEV, "no sm_100 device");
+    uint32_t n_stages = 0, stage_bytes = 0;
+    if (plan_smem(dev, (uint32_t)cols, n_stages, stage_bytes) != ATLAS_OK)
+        return fail(nullptr, ATLAS_EINVAL,
+                     "input length %llu exceeds the largest this kernel stages in shared memory",
+                     (unsigned long long)cols);
+    uint8_t *scratch = nullptr;
+    {
+        // Set-up, once per device, with that device current: the scratch's
+        // device address (the symbol itself is only a host-side stand-in).
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess || !p)
+                return fail(nullptr, ATLAS_ECUDA, "cudaGetSymbolAddress(no-alloc scratch): %s", cudaGetErrorString(e));
+            g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    Phase ph = gemv_phase((uint32_t)cols, (uint32_t)sms, stage_bytes, false,
+                          {seg_of((const uint8_t *)d_weights, type, (uint32_t)rows, (uint32_t)cols, nullptr, d_y)},
+                          d_x, IN_RAW, nullptr, EPI_STORE);
+    Program pg{};
+    pg.phases = reinterpret_cast<const Phase *>(scratch + kNoAllocPhaseOff);
+    pg.n_phases = 1;
+    pg.phase_ctr = reinterpret_cast<uint32_t *>(scratch + kNoAllocCtrOff);
+    pg.state = reinterpret_cast<StepState *>(scratch + kNoAllocStateOff);
+    pg.n_stages = n_stages;
+    pg.stage_bytes = stage_bytes;
+    pg.max_cols = (uint32_t)cols;
+    cudaStream_t s = (cudaStream_t)stream;
+    // The array keeps the previous call's contents: the phase counters and the
+    // step state (epoch, exit count, status) must start at zero for each call.
+    cudaError_t e = cudaMemsetAsync(scratch + kNoAllocCtrOff, 0, kNoAllocNeeded - kNoAllocCtrOff, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(scratch + kNoAllocPhaseOff, &ph, sizeof(Phase), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = atlas_launch_decode(&pg, sms, s);
+    if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "gemv (no-alloc) launch: %s", cudaGetErrorString(e));
+    return ATLAS_OK;
+}

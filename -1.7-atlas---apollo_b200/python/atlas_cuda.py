@@ -27,7 +27,7 @@ EXPORTS = [
     "atlas_cuda_create", "atlas_cuda_destroy", "atlas_cuda_last_error", "atlas_cuda_prefill",
     "atlas_cuda_decode", "atlas_cuda_generate", "atlas_cuda_stats", "atlas_cuda_dequant",
     "atlas_cuda_gemv", "atlas_cuda_gemm", "atlas_cuda_device_info", "atlas_cuda_trace_step",
-    "atlas_cuda_device_ms",
+    "atlas_cuda_device_ms", "atlas_cuda_gemv_noalloc",
     "brain_gpu_init", "brain_gpu_matvec_batch", "brain_gpu_matvec", "brain_gpu_shutdown",
     "atlas_rt_open", "atlas_rt_close", "atlas_rt_error", "atlas_rt_shape", "atlas_rt_data_base",
     "atlas_rt_find_tensor", "atlas_rt_file_bytes", "atlas_rt_device", "atlas_rt_forward_token",
@@ -86,6 +86,7 @@ def lib() -> ctypes.CDLL:
         L.atlas_cuda_last_error.argtypes = [P]
         L.atlas_cuda_dequant.argtypes = [U32, P, U64, P, P]
         L.atlas_cuda_gemv.argtypes = [U32, P, U64, U64, P, P, P]
+        L.atlas_cuda_gemv_noalloc.argtypes = [U32, P, U64, U64, P, P, P]
         L.atlas_cuda_gemm.argtypes = [U32, P, U64, U64, P, U64, P, P]
         L.atlas_cuda_device_info.argtypes = [I32, P, P, P]
         L.atlas_cuda_decode.argtypes = [P, U32, U32, P, P]
@@ -255,6 +256,11 @@ def dequant(type_id: int, d_blocks, nblocks: int, d_out, stream: int = 0) -> Non
 def gemv(type_id: int, d_w, rows: int, cols: int, d_x, d_y, stream: int = 0) -> None:
     check(lib().atlas_cuda_gemv(type_id, _ptr(d_w), rows, cols, _ptr(d_x), _ptr(d_y), ctypes.c_void_p(stream)),
           "atlas_cuda_gemv")
+
+
+def gemv_noalloc(type_id: int, d_w, rows: int, cols: int, d_x, d_y, stream: int = 0) -> None:
+    check(lib().atlas_cuda_gemv_noalloc(type_id, _ptr(d_w), rows, cols, _ptr(d_x), _ptr(d_y),
+                                        ctypes.c_void_p(stream)), "atlas_cuda_gemv_noalloc")
 
 
 def gemm(type_id: int, d_w, rows: int, cols: int, d_x, tokens: int, d_y, stream: int = 0) -> None:

@@ -138,6 +138,20 @@ int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, fl
 int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                     const float *d_x, float *d_y, void *stream);
 
+/* atlas_cuda_gemv for callers that cannot allocate device memory (a host that
+   owns all of HBM, or a path that cannot absorb cudaMalloc's device
+   synchronisation). No counterpart in the reference. Same arguments, result
+   and limits as atlas_cuda_gemv, but it calls no cudaMalloc / cudaFree: its
+   launch scratch (kernel descriptor, phase counters, step state) is a 4 KB
+   static device array in this library, held by every GPU that loads it until
+   the process exits. The first call on a device looks up that array's device
+   address; make that first call before any stream capture. All calls share the
+   one array: calls that overlap on the GPU (other streams, other host threads)
+   race and give wrong results. Inputs longer than the shared-memory plan
+   supports are rejected with ATLAS_EINVAL. */
+int atlas_cuda_gemv_noalloc(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
+                            const float *d_x, float *d_y, void *stream);
+
 /* Y[tokens x rows] = X[tokens x cols] W^T through the tcgen05 prefill GEMM
    (batch_matvec_rows, src/brain_runtime_batch.c:1525): X fp32 in, fp16
    operand tiles, fp32 accumulation. */
