@@ -74,6 +74,7 @@ struct Smem {
     uint8_t *xarea;     // GEMV input: groups of 4 elements as 4 hi + 4 lo halves, then one sum per 16 elements
     uint8_t *ring;
     uint32_t n_stages, stage_bytes;
+    uint32_t phase_index;   // current phase (diagnostic stamps)
     __device__ __forceinline__ uint8_t *stage(uint32_t k) const { return ring + (size_t)(k % n_stages) * stage_bytes; }
     __device__ __forceinline__ uint64_t *full(uint32_t k) const { return &h->full[k % n_stages]; }
     __device__ __forceinline__ uint64_t *empty(uint32_t k) const { return &h->empty[k % n_stages]; }
@@ -288,8 +289,9 @@ __device__ __forceinline__ bool wait_phase(const Program &pg, uint32_t p, uint32
 {
     __shared__ uint32_t ok_flag;
     if (threadIdx.x == 0) {
+        // the acquire load orders this CTA's later reads (all from L2) after the
+        // producers' release arrivals; the barrier below extends it to the CTA
         const bool ok = wait_counter(pg.phase_ctr + 8u * p, (epoch + 1u) * gridDim.x, err, kStatusBarrierTimeout);
-        __threadfence();
         ok_flag = ok ? 1u : 0u;
     }
     consumer_sync();
@@ -305,64 +307,64 @@ __device__ __forceinline__ void arrive_phase(const Program &pg, uint32_t p)
     }
 }
 
-// Per-CTA RMSNorm scale over the hidden vector (sum of squares in double as
-// src/brain_runtime.c:1345-1351; 1/sqrtf(float(mean)+eps) as :1353-1358).
-__device__ float cta_inv_rms(const float *x, uint32_t n, float eps, const Smem &sm)
-{
-    double ss = 0.0;
-    for (uint32_t i = threadIdx.x * 4u; i < n; i += kConsumerWarps * 32 * 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4 *>(x + i));
-        ss += (double)v.x * (double)v.x;
-        ss += (double)v.y * (double)v.y;
-        ss += (double)v.z * (double)v.z;
-        ss += (double)v.w * (double)v.w;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) sm.h->dred[warp] = ss;
-    consumer_sync();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int w = 0; w < kConsumerWarps; ++w) t += sm.h->dred[w];
-        sm.h->inv_rms = 1.0f / sqrtf((float)(t / (double)n) + eps);
-    }
-    consumer_sync();
-    return sm.h->inv_rms;
-}
-
 // Stage the phase input in shared memory as fp16 (hi, lo) groups plus one sum
-// per 16 elements, all in units of x * xscale (a power of two).
-__device__ void stage_x(const Program &pg, const Phase &ph, const Smem &sm)
+// per 16 elements, in units of (x * norm_w) * xscale, xscale a power of two.
+// One pass over x from L2: the RMSNorm factor is a scalar, so it is applied
+// to the GEMV results instead (W (x w inv) = inv * W (x w)); the sum of
+// squares (in double, src/brain_runtime.c:1345-1351) and max|x w| come out of
+// the same pass and one block reduction. Returns the factor the epilogue
+// applies: inv_rms / xscale (1 / xscale for un-normalized inputs).
+__device__ float stage_x(const Program &pg, const Phase &ph, const Smem &sm)
 {
     const uint32_t n = ph.cols;
     const bool norm = ph.input_mode == IN_RMSNORM;
-    const float inv = norm ? cta_inv_rms(ph.in, n, pg.rms_eps, sm) : 1.0f;
     float4 *xf = reinterpret_cast<float4 *>(sm.xarea);
     float mx = 0.f;
-    for (uint32_t i = threadIdx.x; i < n / 4u; i += kConsumerWarps * 32) {
-        float4 v = __ldcg(reinterpret_cast<const float4 *>(ph.in) + i);
-        if (norm) {
-            const float4 w = __ldg(reinterpret_cast<const float4 *>(ph.norm_w) + i);
-            v.x = v.x * inv * w.x; v.y = v.y * inv * w.y; v.z = v.z * inv * w.z; v.w = v.w * inv * w.w;
+    double ss = 0.0;
+    // four independent loads in flight per thread (x comes from L2)
+    constexpr uint32_t kStride = kConsumerWarps * 32;
+    for (uint32_t i0 = threadIdx.x; i0 < n / 4u; i0 += 4u * kStride) {
+        float4 v[4], w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = i0 + (uint32_t)j * kStride;
+            if (i < n / 4u) {
+                v[j] = __ldcg(reinterpret_cast<const float4 *>(ph.in) + i);
+                if (norm) w[j] = __ldg(reinterpret_cast<const float4 *>(ph.norm_w) + i);
+            }
         }
-        xf[i] = v;
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = i0 + (uint32_t)j * kStride;
+            if (i >= n / 4u) continue;
+            float4 x = v[j];
+            if (norm) {
+                ss += (double)x.x * (double)x.x;
+                ss += (double)x.y * (double)x.y;
+                ss += (double)x.z * (double)x.z;
+                ss += (double)x.w * (double)x.w;
+                x.x *= w[j].x; x.y *= w[j].y; x.z *= w[j].z; x.w *= w[j].w;
+            }
+            xf[i] = x;
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+        }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) sm.h->fred[warp] = mx;
-    consumer_sync();
-    if (threadIdx.x == 0) {
-        float m = 0.f;
-        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, sm.h->fred[w]);
-        // scale so that max|x| lands in [2^13, 2^14): far from fp16 overflow,
-        // and the lo parts of small elements stay normal
-        sm.h->xscale = (m > 0.f && isfinite(m)) ? exp2f((float)(13 - ilogbf(m))) : 1.0f;
+    for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
     }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sm.h->fred[warp] = mx; sm.h->dred[warp] = ss; }
     consumer_sync();
-    const float s = sm.h->xscale;
+    float m = 0.f;
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) { m = fmaxf(m, sm.h->fred[w]); t += sm.h->dred[w]; }
+    // scale so that max|x| lands in [2^13, 2^14): far from fp16 overflow, and
+    // the lo parts of small elements stay normal
+    const float s = (m > 0.f && isfinite(m)) ? exp2f((float)(13 - ilogbf(m))) : 1.0f;
+    const float inv_rms = norm ? 1.0f / sqrtf((float)(t / (double)n) + pg.rms_eps) : 1.0f;
     float *xs16 = reinterpret_cast<float *>(sm.xarea + (size_t)n * 4u);
     for (uint32_t u = threadIdx.x; u < n / 16u; u += kConsumerWarps * 32) {
         float sum = 0.f;
@@ -387,6 +389,7 @@ __device__ void stage_x(const Program &pg, const Phase &ph, const Smem &sm)
         xs16[u] = sum;
     }
     consumer_sync();
+    return inv_rms / s;
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b,
@@ -414,7 +417,7 @@ constexpr float kTwo24 = 16777216.0f;
 // for instruction-level parallelism). Tile n: rows (g, g+8) of this lane at
 // r0[n] / r1[n] (nullptr: row absent), the block column's staged x groups
 // xb[n] and 16-element sums xs[n]. Adds this lane's sub-blocks (j = t, t + 4).
-template <int NT>
+template <int NT, bool FULL>
 __device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const uint8_t *const (&r1)[NT],
                                           const uint8_t *const (&xb)[NT], const float *const (&xs)[NT], int g, int t,
                                           float (&o0)[NT], float (&o1)[NT])
@@ -426,7 +429,7 @@ __device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const 
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             dsc[n][r][0] = dsc[n][r][1] = dmn[n][r][0] = dmn[n][r][1] = 0.f;
-            if (!rows[r]) continue;
+            if (!FULL && !rows[r]) continue;
             const uint4 hd = *reinterpret_cast<const uint4 *>(rows[r]);
             const float d = h2f((uint16_t)(hd.x & 0xffffu)), dm = h2f((uint16_t)(hd.x >> 16));
             const uint32_t sh = 8u * (uint32_t)t;
@@ -447,8 +450,8 @@ __device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const 
             const uint32_t off = 16u + 32u * c + 16u * hp + 4u * t;
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-                const uint32_t w0 = r0[n] ? *reinterpret_cast<const uint32_t *>(r0[n] + off) : 0u;
-                const uint32_t w1 = r1[n] ? *reinterpret_cast<const uint32_t *>(r1[n] + off) : 0u;
+                const uint32_t w0 = (FULL || r0[n]) ? *reinterpret_cast<const uint32_t *>(r0[n] + off) : 0u;
+                const uint32_t w1 = (FULL || r1[n]) ? *reinterpret_cast<const uint32_t *>(r1[n] + off) : 0u;
                 const uint32_t l0 = w0 & 0x0f0f0f0fu, h0 = (w0 >> 4) & 0x0f0f0f0fu;
                 const uint32_t l1 = w1 & 0x0f0f0f0fu, h1 = (w1 >> 4) & 0x0f0f0f0fu;
                 const uint2 blo = *reinterpret_cast<const uint2 *>(xb[n] + (16u * c + 4u * hp + (uint32_t)t) * 16u + podd);
@@ -481,7 +484,7 @@ __device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const 
 // NT independent 16-row x 256-element Q6_K tiles (blocks at even, not
 // necessarily 4-aligned addresses). Lane t keeps the 16-element groups with
 // k == t: one scale per (h, hp) and row, selected outside the k loop.
-template <int NT>
+template <int NT, bool FULL>
 __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const uint8_t *const (&r1)[NT],
                                           const uint8_t *const (&xb)[NT], const float *const (&xs)[NT], int g, int t,
                                           float (&o0)[NT], float (&o1)[NT])
@@ -489,8 +492,8 @@ __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const 
     float d0[NT], d1[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
-        d0[n] = r0[n] ? h2f((uint16_t)ld_u16(r0[n] + 208)) : 0.f;
-        d1[n] = r1[n] ? h2f((uint16_t)ld_u16(r1[n] + 208)) : 0.f;
+        d0[n] = (FULL || r0[n]) ? h2f((uint16_t)ld_u16(r0[n] + 208)) : 0.f;
+        d1[n] = (FULL || r1[n]) ? h2f((uint16_t)ld_u16(r1[n] + 208)) : 0.f;
     }
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t podd = (uint32_t)(g & 1) * 8u;
@@ -504,12 +507,13 @@ __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const 
             float s0[NT], s1[NT], keep[NT][4];
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-                A0[n] = r0[n] ? ld32u(r0[n] + oa) : 0u; B0[n] = r0[n] ? ld32u(r0[n] + ob) : 0u;
-                Q0[n] = r0[n] ? ld32u(r0[n] + oq) : 0u;
-                A1[n] = r1[n] ? ld32u(r1[n] + oa) : 0u; B1[n] = r1[n] ? ld32u(r1[n] + ob) : 0u;
-                Q1[n] = r1[n] ? ld32u(r1[n] + oq) : 0u;
-                s0[n] = r0[n] ? d0[n] * (float)(int8_t)r0[n][si] : 0.f;
-                s1[n] = r1[n] ? d1[n] * (float)(int8_t)r1[n][si] : 0.f;
+                const bool h0 = FULL || r0[n], h1 = FULL || r1[n];
+                A0[n] = h0 ? ld32u(r0[n] + oa) : 0u; B0[n] = h0 ? ld32u(r0[n] + ob) : 0u;
+                Q0[n] = h0 ? ld32u(r0[n] + oq) : 0u;
+                A1[n] = h1 ? ld32u(r1[n] + oa) : 0u; B1[n] = h1 ? ld32u(r1[n] + ob) : 0u;
+                Q1[n] = h1 ? ld32u(r1[n] + oq) : 0u;
+                s0[n] = h0 ? d0[n] * (float)(int8_t)r0[n][si] : 0.f;
+                s1[n] = h1 ? d1[n] * (float)(int8_t)r1[n][si] : 0.f;
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -551,9 +555,9 @@ __device__ bool run_gemv_phase(const Program &pg, const Phase &gph, const Smem &
         reinterpret_cast<uint32_t *>(&sm.h->ph)[i] = reinterpret_cast<const uint32_t *>(&gph)[i];
     consumer_sync();
     const Phase &ph = sm.h->ph;
-    stage_x(pg, ph, sm);
+    const float out_scale = stage_x(pg, ph, sm);
+    if (pg.trace_ext && threadIdx.x == 0) pg.trace_ext[((size_t)blockIdx.x * pg.n_phases + sm.phase_index) * 8 + 0] = global_ns();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const float inv_scale = 1.0f / sm.h->xscale;
     const float *xs16 = reinterpret_cast<const float *>(sm.xarea + (size_t)ph.cols * 4u);
     float best = -FLT_MAX;
     uint32_t best_i = 0xffffffffu;
@@ -603,6 +607,7 @@ __device__ bool run_gemv_phase(const Program &pg, const Phase &gph, const Smem &
                     else { acc[1][q][0] += o0; acc[1][q][1] += o1; }
                 }
             };
+            const bool full = (nrows % 16u) == 0u;   // every row tile of the chunk has its 16 rows
             uint32_t ti = first;
             for (; ti + kConsumerWarps < ntasks; ti += 2u * kConsumerWarps) {
                 const uint8_t *p0[2], *p1[2], *xb[2];
@@ -613,8 +618,13 @@ __device__ bool run_gemv_phase(const Program &pg, const Phase &gph, const Smem &
 #pragma unroll
                 for (int n = 0; n < 2; ++n) { xb[n] = sm.xarea + (size_t)bcol[n] * 1024u; xs[n] = xs16 + (size_t)bcol[n] * 16u; }
                 float o0[2] = {0.f, 0.f}, o1[2] = {0.f, 0.f};
-                if (sg.type == 12u) q4k_tiles<2>(p0, p1, xb, xs, g, t, o0, o1);
-                else q6k_tiles<2>(p0, p1, xb, xs, g, t, o0, o1);
+                if (full) {
+                    if (sg.type == 12u) q4k_tiles<2, true>(p0, p1, xb, xs, g, t, o0, o1);
+                    else q6k_tiles<2, true>(p0, p1, xb, xs, g, t, o0, o1);
+                } else {
+                    if (sg.type == 12u) q4k_tiles<2, false>(p0, p1, xb, xs, g, t, o0, o1);
+                    else q6k_tiles<2, false>(p0, p1, xb, xs, g, t, o0, o1);
+                }
                 add(irt[0], o0[0], o1[0]);
                 add(irt[1], o0[1], o1[1]);
             }
@@ -626,8 +636,8 @@ __device__ bool run_gemv_phase(const Program &pg, const Phase &gph, const Smem &
                 xb[0] = sm.xarea + (size_t)bcol * 1024u;
                 xs[0] = xs16 + (size_t)bcol * 16u;
                 float o0[1] = {0.f}, o1[1] = {0.f};
-                if (sg.type == 12u) q4k_tiles<1>(p0, p1, xb, xs, g, t, o0, o1);
-                else q6k_tiles<1>(p0, p1, xb, xs, g, t, o0, o1);
+                if (sg.type == 12u) q4k_tiles<1, false>(p0, p1, xb, xs, g, t, o0, o1);
+                else q6k_tiles<1, false>(p0, p1, xb, xs, g, t, o0, o1);
                 add(irt, o0[0], o1[0]);
             }
             task += ntasks;
@@ -658,8 +668,8 @@ __device__ bool run_gemv_phase(const Program &pg, const Phase &gph, const Smem &
                 v0 += sm.h->wres[buf][w][0][r];
                 v1 += sm.h->wres[buf][w][1][r];
             }
-            v0 *= inv_scale;
-            v1 *= inv_scale;
+            v0 *= out_scale;
+            v1 *= out_scale;
             const uint32_t row = item_r0 + r;
             if (ph.epilogue == EPI_SWIGLU) {
                 ph.seg[0].out[row] = (v0 / (1.0f + expf(-v0))) * v1;   // src/brain_runtime.c:1755-1758
@@ -747,13 +757,31 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
         const bool last_split = (p1 == pos + 1);
         // RoPE'd queries of the group; the fresh k (RoPE'd) and v in the last split
         float *qf = reinterpret_cast<float *>(sm.a->q);
-        for (uint32_t i = threadIdx.x; i < group * (hd / 2); i += kConsumerWarps * 32) {
-            const uint32_t h = i / (hd / 2), p = i % (hd / 2);
-            const float *qh = ph.q + (size_t)(g * group + h) * hd;
-            float a, b;
-            rope_pair(pg, pos, (int)p, __ldcg(qh + p), __ldcg(qh + p + hd / 2), a, b);
-            qf[h * hd + p] = a;
-            qf[h * hd + p + hd / 2] = b;
+        {
+            // group * 64 pairs over 256 threads: at most 2 per thread, loads first
+            constexpr uint32_t kStride = kConsumerWarps * 32;
+            float qa[2], qb[2];
+            float2 cs[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t i = threadIdx.x + (uint32_t)j * kStride;
+                if (i < group * (hd / 2)) {
+                    const uint32_t h = i / (hd / 2), p = i % (hd / 2);
+                    const float *qh = ph.q + (size_t)(g * group + h) * hd;
+                    qa[j] = __ldcg(qh + p);
+                    qb[j] = __ldcg(qh + p + hd / 2);
+                    cs[j] = __ldg(pg.rope + (size_t)pos * (hd / 2) + p);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t i = threadIdx.x + (uint32_t)j * kStride;
+                if (i < group * (hd / 2)) {
+                    const uint32_t h = i / (hd / 2), p = i % (hd / 2);
+                    qf[h * hd + p] = qa[j] * cs[j].x - qb[j] * cs[j].y;       // src/brain_runtime.c:1391-1393
+                    qf[h * hd + p + hd / 2] = qa[j] * cs[j].y + qb[j] * cs[j].x;
+                }
+            }
         }
         if (last_split) {
             float *kn = reinterpret_cast<float *>(sm.a->knew), *vn = reinterpret_cast<float *>(sm.a->vnew);
@@ -767,6 +795,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
             for (uint32_t i = threadIdx.x; i < hd; i += kConsumerWarps * 32) vn[i] = __ldcg(ph.v + (size_t)g * hd + i);
         }
         consumer_sync();
+        if (pg.trace_ext && threadIdx.x == 0 && it == blockIdx.x) pg.trace_ext[((size_t)blockIdx.x * pg.n_phases + sm.phase_index) * 8 + 0] = global_ns();
         if (last_split) {
             // KV append at pos (src/brain_runtime.c:1496-1500); read by the next steps.
             const float *kn = reinterpret_cast<const float *>(sm.a->knew), *vn = reinterpret_cast<const float *>(sm.a->vnew);
@@ -791,6 +820,8 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
             if (staged) {
                 if (!stage_wait(sm, k, err)) return false;
                 if (!stage_wait(sm, k + 1, err)) return false;
+                if (pg.trace_ext && threadIdx.x == 0 && it == blockIdx.x && t0 == p0)
+                    pg.trace_ext[((size_t)blockIdx.x * pg.n_phases + sm.phase_index) * 8 + 3] = global_ns();
                 const uint32_t esz = f16 ? 2u : 4u;
                 const uintptr_t ka = reinterpret_cast<uintptr_t>(ph.k_cache) + ((size_t)g * pg.max_context + t0) * hd * esz;
                 const uintptr_t va = reinterpret_cast<uintptr_t>(ph.v_cache) + ((size_t)g * pg.max_context + t0) * hd * esz;
@@ -845,6 +876,8 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
                     m[hi] = mn;
                 }
             }
+            if (pg.trace_ext && threadIdx.x == 0 && it == blockIdx.x && t0 == p0)
+                pg.trace_ext[((size_t)blockIdx.x * pg.n_phases + sm.phase_index) * 8 + 4] = global_ns();
             if (staged) {
                 stage_release(sm, k);
                 stage_release(sm, k + 1);
@@ -860,6 +893,7 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
         }
         // Last split of head g to arrive combines all splits.
         consumer_sync();
+        if (pg.trace_ext && threadIdx.x == 0 && it == blockIdx.x) pg.trace_ext[((size_t)blockIdx.x * pg.n_phases + sm.phase_index) * 8 + 1] = global_ns();
         if (threadIdx.x == 0) {
             __threadfence();
             const uint32_t old = atom_acq_rel_add(ph.split_ctr + g, 1u);
@@ -867,18 +901,31 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
             if (sm.h->flag) { ph.split_ctr[g] = 0u; __threadfence(); }
         }
         consumer_sync();
+        if (pg.trace_ext && threadIdx.x == 0 && it == blockIdx.x) pg.trace_ext[((size_t)blockIdx.x * pg.n_phases + sm.phase_index) * 8 + 2] = global_ns();
         if (sm.h->flag) {
             for (uint32_t h = (uint32_t)warp; h < group; h += kConsumerWarps) {
-                float M = -FLT_MAX;
-                for (uint32_t q = (uint32_t)lane; q < nsplit; q += 32)
-                    M = fmaxf(M, __ldcg(ph.part + (((size_t)g * nsplit + q) * group + h) * (hd + 4) + hd));
-                M = warp_max(M);
+                // one pass over the splits' (max, sum): lane q holds splits q, q + 32
+                float ms[2] = {-FLT_MAX, -FLT_MAX}, ls[2] = {0.f, 0.f};
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const uint32_t q = (uint32_t)lane + 32u * r;
+                    if (q < nsplit) {
+                        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(
+                            ph.part + (((size_t)g * nsplit + q) * group + h) * (hd + 4) + hd));
+                        ms[r] = ml.x;
+                        ls[r] = ml.y;
+                    }
+                }
+                const float M = warp_max(fmaxf(ms[0], ms[1]));
                 float den = 0.f;
-                for (uint32_t q = (uint32_t)lane; q < nsplit; q += 32) {
-                    const float *src = ph.part + (((size_t)g * nsplit + q) * group + h) * (hd + 4);
-                    const float w = expf(__ldcg(src + hd) - M);
-                    sm.a->cw[q][h] = w;
-                    den += w * __ldcg(src + hd + 1);
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const uint32_t q = (uint32_t)lane + 32u * r;
+                    if (q < nsplit) {
+                        const float w = expf(ms[r] - M);
+                        sm.a->cw[q][h] = w;
+                        den += w * ls[r];
+                    }
                 }
                 den = warp_sum(den);
                 if (lane == 0) sm.a->cden[h] = den;
@@ -887,14 +934,23 @@ __device__ bool run_attn_phase(const Program &pg, const Phase &ph, const Smem &s
             for (uint32_t i = threadIdx.x; i < group * (hd / 4); i += kConsumerWarps * 32) {
                 const uint32_t h = i / (hd / 4), d4 = i % (hd / 4);
                 float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (uint32_t q = 0; q < nsplit; ++q) {
-                    const float w = sm.a->cw[q][h];
-                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(
-                        ph.part + (((size_t)g * nsplit + q) * group + h) * (hd + 4)) + d4);
-                    num.x = fmaf(w, v.x, num.x);
-                    num.y = fmaf(w, v.y, num.y);
-                    num.z = fmaf(w, v.z, num.z);
-                    num.w = fmaf(w, v.w, num.w);
+                // eight partial loads in flight at a time (they come from L2)
+                for (uint32_t q0 = 0; q0 < nsplit; q0 += 8) {
+                    float4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (q0 + j < nsplit)
+                            v[j] = __ldcg(reinterpret_cast<const float4 *>(
+                                ph.part + (((size_t)g * nsplit + q0 + j) * group + h) * (hd + 4)) + d4);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (q0 + j < nsplit) {
+                            const float w = sm.a->cw[q0 + j][h];
+                            num.x = fmaf(w, v[j].x, num.x);
+                            num.y = fmaf(w, v[j].y, num.y);
+                            num.z = fmaf(w, v[j].z, num.z);
+                            num.w = fmaf(w, v[j].w, num.w);
+                        }
                 }
                 const float den = sm.a->cden[h];
                 const float inv = den > 0.f ? 1.0f / den : 0.f;
@@ -952,7 +1008,7 @@ __device__ void run_argmax_phase(const Program &pg, const Phase &ph, const Smem 
 }
 
 
-__device__ bool consumer(const Program &pg, const Smem &sm, uint32_t pos, uint32_t token, uint32_t epoch,
+__device__ bool consumer(const Program &pg, Smem sm, uint32_t pos, uint32_t token, uint32_t epoch,
                          volatile uint32_t *err)
 {
     uint32_t k = 0;
@@ -961,6 +1017,7 @@ __device__ bool consumer(const Program &pg, const Smem &sm, uint32_t pos, uint32
         const Phase &ph = pg.phases[p];
         const uint32_t n = phase_items(pg, ph, pos);
         const bool mine = blockIdx.x < n;
+        sm.phase_index = p;
         if (tr && threadIdx.x == 0) tr[p * 4 + 0] = global_ns();
         if (mine && p > 0 && !wait_phase(pg, p - 1, epoch, err)) return false;
         if (tr && threadIdx.x == 0) tr[p * 4 + 1] = global_ns();

@@ -123,6 +123,7 @@ struct Program {
     uint32_t max_context;
     uint32_t advance;      // 1: after the step, token = next_token and pos += 1
     uint64_t *trace;       // optional: [cta][phase][4] globaltimer stamps (diagnostics)
+    uint64_t *trace_ext;   // optional: [cta][phase][8] stamps inside a phase (diagnostics)
     // shared-memory plan (host-chosen per model)
     uint32_t n_stages;     // bulk-copy ring depth
     uint32_t stage_bytes;  // bytes per stage (multiple of 128)

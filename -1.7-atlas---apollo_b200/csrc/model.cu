@@ -219,10 +219,14 @@ void plan_gemv(Phase &ph, uint32_t total_rows, uint32_t grid, uint32_t stage_byt
         ph.chunk_blocks = nb;
         ph.seg_stride = 0;
         ph.chunk_rows = (32u * row_max + 32u <= stage_bytes) ? 32u : 16u;
-        // largest item (<= 64 rows) that still gives every CTA work
+        // item size minimising the busiest CTA's work: rows it streams plus a
+        // per-item cost of about 8 rows (partials, barrier, epilogue)
         ph.item_rows = 16;
-        for (uint32_t r : {64u, 32u}) {
-            if ((total_rows + r - 1) / r >= grid) { ph.item_rows = r; break; }
+        uint64_t best = ~0ull;
+        for (uint32_t r : {16u, 32u, 64u}) {
+            const uint64_t items = (total_rows + r - 1) / r, waves = (items + grid - 1) / grid;
+            const uint64_t cost = waves * (r + 8u);
+            if (cost <= best) { best = cost; ph.item_rows = r; }
         }
         if (ph.chunk_rows > ph.item_rows) ph.chunk_rows = ph.item_rows;
     } else {
@@ -640,20 +644,23 @@ int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out
                           uint32_t *n_phases, uint32_t *phase_kinds)
 {
     if (!h) return fail(h, ATLAS_EINVAL, "null handle");
-    const size_t np = h->decode.phases.size(), need = (size_t)h->sm_count * np * 4;
+    const size_t np = h->decode.phases.size(), per = (size_t)h->sm_count * np, need = per * 12;
     if (n_ctas) *n_ctas = (uint32_t)h->sm_count;
     if (n_phases) *n_phases = (uint32_t)np;
-    if (!out_ns) return fail(h, ATLAS_EINVAL, "null trace buffer");
     if (phase_kinds)
         for (size_t i = 0; i < np; ++i) phase_kinds[i] = h->decode.phases[i].kind * 16u + h->decode.phases[i].epilogue;
+    if (!out_ns) return fail(h, ATLAS_EINVAL, "null trace buffer");
     if (cap < need) return fail(h, ATLAS_EINVAL, "trace buffer needs %zu slots", need);
     if (id >= h->desc.vocab || pos >= h->desc.max_context) return fail(h, ATLAS_ERANGE, "token or position out of range");
     if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
     uint64_t *d = nullptr;
     CU(h, cudaMalloc(&d, need * sizeof(uint64_t)));
+    CU(h, cudaMemset(d, 0, need * sizeof(uint64_t)));
     h->decode.pg.trace = d;
+    h->decode.pg.trace_ext = d + per * 4;
     int rc = run_decode(h, id, pos, 1, nullptr, nullptr, nullptr);
     h->decode.pg.trace = nullptr;
+    h->decode.pg.trace_ext = nullptr;
     if (rc == ATLAS_OK) {
         cudaError_t e = cudaMemcpy(out_ns, d, need * sizeof(uint64_t), cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) rc = fail(h, ATLAS_ECUDA, "trace readback: %s", cudaGetErrorString(e));

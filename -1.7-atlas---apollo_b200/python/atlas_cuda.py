@@ -209,16 +209,17 @@ class Runtime:
         return out
 
     def trace_step(self, token: int, pos: int):
-        """One traced decode step: (stamps[cta, phase, 4] in ns, phase kind codes)."""
+        """One traced decode step: (stamps[cta, phase, 4], inner stamps[cta, phase, 8], phase kind codes)."""
         import numpy as np
         dev = lib().atlas_rt_device(self._h)
         nc, nph = ctypes.c_uint32(), ctypes.c_uint32()
         lib().atlas_cuda_trace_step(dev, token, pos, None, 0, ctypes.byref(nc), ctypes.byref(nph), None)
-        buf = np.zeros(nc.value * nph.value * 4, np.uint64)
+        per = nc.value * nph.value
+        buf = np.zeros(per * 12, np.uint64)
         kinds = np.zeros(nph.value, np.uint32)
         check(lib().atlas_cuda_trace_step(dev, token, pos, _ptr(buf), buf.size, ctypes.byref(nc), ctypes.byref(nph),
                                           _ptr(kinds)), "trace_step", dev)
-        return buf.reshape(nc.value, nph.value, 4), kinds
+        return buf[:per * 4].reshape(nc.value, nph.value, 4), buf[per * 4:].reshape(nc.value, nph.value, 8), kinds
 
     def stats(self):
         """(kernel launches since creation, device ms of the last call, device ms of all calls)."""

@@ -49,24 +49,33 @@ def cmd_trace(a):
                                         kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
     with atlas_cuda.Runtime(path, max_context=a.pos + 16) as rt:
         rt.prefill(np.arange(1, a.pos + 1, dtype=np.uint32) % a.vocab, 0, want_logits=False)
-        tr, kinds = rt.trace_step(7, a.pos)
-    tr = tr.astype(np.int64)
+        tr, ext, kinds = rt.trace_step(7, a.pos)
+    tr, ext = tr.astype(np.int64), ext.astype(np.int64)
     t0 = tr[tr > 0].min()
     tr = np.where(tr > 0, tr - t0, -1)
+    ext = np.where(ext > 0, ext - t0, -1)
     end = tr[:, :, 2].max()
     print(f"decode step at position {a.pos}: {end / 1e3:.1f} us over {len(kinds)} phases")
     agg, prev = {}, 0
     for p, k in enumerate(kinds):
         done = tr[:, p, 2].max()
-        work = (tr[:, p, 2] - tr[:, p, 1]).mean()
-        s = agg.setdefault(KIND.get(int(k), str(k)), [0, 0.0, 0])
+        busy = tr[:, p, 1] >= 0
+        start = tr[:, p, 1][busy].min() if busy.any() else prev
+        # inner stamps of the slowest CTA, relative to its wait end
+        slow = int(np.argmax(tr[:, p, 2]))
+        inner = [(ext[slow, p, i] - tr[slow, p, 1]) for i in range(8) if ext[slow, p, i] >= 0]
+        s = agg.setdefault(KIND.get(int(k), str(k)), [0, 0, 0, [0.0] * 8, 0])
         s[0] += done - prev
-        s[1] += work
+        s[1] += start - prev
         s[2] += 1
+        for i, v in enumerate(inner):
+            s[3][i] += v
+        s[4] = max(s[4], len(inner))
         prev = done
-    for name, (tot, work, n) in agg.items():
-        print(f"  {name:16s} x{n:3d}  {tot / 1e3:9.1f} us total  {tot / n / 1e3:7.2f} us each  (mean CTA work "
-              f"{work / n / 1e3:6.2f} us)")
+    for name, (tot, gap, n, inner, ni) in agg.items():
+        stamps = " ".join(f"{v / n / 1e3:.2f}" for v in inner[:ni])
+        print(f"  {name:16s} x{n:3d}  {tot / 1e3:9.1f} us total  {tot / n / 1e3:7.2f} us each  "
+              f"(barrier gap {gap / n / 1e3:5.2f} us; slowest CTA stamps {stamps} us)")
 
 
 def main():

@@ -114,10 +114,11 @@ int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last
    generate / prefill call since creation. */
 int atlas_cuda_device_ms(const AtlasCuda *h, double *total_ms);
 
-/* Diagnostics: runs one decode step of (id, pos) with device-side timestamps.
-   Fills out_ns (host) with n_ctas * n_phases * 4 globaltimer values per CTA and
-   phase: [wait start, wait end, phase end, producer done]; n_ctas / n_phases
-   receive the dimensions. cap is the number of uint64 slots in out_ns. */
+/* Diagnostics: runs one decode step of (id, pos) with device-side timestamps
+   (globaltimer, ns). out_ns (host, cap uint64 slots) receives n_ctas * n_phases
+   * 4 values [wait start, wait end, phase end, producer done] per CTA and phase,
+   followed by n_ctas * n_phases * 8 stamps taken inside the phases (0 = none).
+   n_ctas / n_phases / phase_kinds (kind * 16 + epilogue) describe the layout. */
 int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out_ns, size_t cap,
                           uint32_t *n_ctas, uint32_t *n_phases, uint32_t *phase_kinds);
 
