@@ -20,9 +20,21 @@
 #include "engine.h"
 #include "quant.cuh"
 
+#include "prefill.h"
+
 extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream);
 extern "C" size_t atlas_decode_hdr_bytes();
 extern "C" size_t atlas_decode_attn_bytes();
+extern "C" cudaError_t atlas_launch_prefill_gemm(const atlas::pf::GemmArgs *a, int grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_launch_prefill_split(const float *x, uint32_t ldx, uint32_t cols, uint32_t tokens,
+                                                  uint32_t tok_pad, const float *norm_w, float eps, uint8_t *xt,
+                                                  float *xscale, cudaStream_t stream);
+extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t tokens, const uint8_t *embd,
+                                                  uint32_t type, uint64_t row_bytes, uint32_t hidden, float *x,
+                                                  cudaStream_t stream);
+extern "C" cudaError_t atlas_launch_prefill_attn(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_launch_wbound(uint32_t type, const uint8_t *blocks, uint64_t nblocks, uint32_t *out_bits,
+                                           cudaStream_t stream);
 
 
 using namespace atlas;
@@ -58,7 +70,19 @@ struct AtlasCuda {
         uint32_t tq = 0, tk = 0, tv = 0, to = 0, tg = 0, tu = 0, td = 0;
         const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
         void *kc = nullptr, *vc = nullptr;
+        // prefill: power-of-two exponents that bring each tensor's weights into
+        // [2^14, 2^15) before the binary16 split
+        int eq = 0, ek = 0, ev = 0, eo = 0, eg = 0, eu = 0, ed = 0;
     };
+    // Batched prefill buffers, sized for desc.max_prefill tokens per chunk.
+    struct Prefill {
+        uint32_t cap = 0, tok_pad = 0, terms = 3, max_units = 0;
+        float *x = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *xscale = nullptr, *ws = nullptr;
+        float *apart = nullptr;
+        uint8_t *xt = nullptr;
+        uint32_t *ctr = nullptr, *actr = nullptr, *units = nullptr, *ids = nullptr, *status = nullptr;
+        ProgramBuffers tail;   // final rms_norm + head GEMV + argmax of the last token
+    } pf;
     std::vector<W> layers;
     const uint8_t *embd = nullptr, *head = nullptr;
     uint32_t t_embd = 0, t_head = 0;
@@ -348,11 +372,12 @@ int status_to_code(AtlasCuda *h, uint32_t st)
     return fail(h, ATLAS_ECUDA, "device reported status %u", st);
 }
 
-// Run `steps` launches of the decode program starting from (token, pos).
-int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
-               float *last_logit)
+// Run `steps` launches of a decode-kernel program starting from (token, pos).
+// `timed`: record the launches' device time as this call's (last_ms) - off
+// when the program is one part of a larger timed call.
+int run_program(AtlasCuda *h, ProgramBuffers &pb, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev,
+                uint32_t *last_token, float *last_logit, bool timed = true)
 {
-    ProgramBuffers &pb = h->decode;
     StepState init{};
     init.pos = pos;
     init.token = token;
@@ -363,19 +388,21 @@ int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
     const size_t off = offsetof(StepState, pos);
     CU(h, cudaMemcpyAsync(reinterpret_cast<uint8_t *>(pb.d_state) + off, reinterpret_cast<const uint8_t *>(&init) + off,
                           sizeof(StepState) - off, cudaMemcpyHostToDevice, h->stream));
-    CU(h, cudaEventRecord(h->ev0, h->stream));
+    if (timed) CU(h, cudaEventRecord(h->ev0, h->stream));
     for (uint32_t i = 0; i < steps; ++i) {
         CU(h, atlas_launch_decode(&pb.pg, h->sm_count, h->stream));
         ++h->launches;
     }
-    CU(h, cudaEventRecord(h->ev1, h->stream));
+    if (timed) CU(h, cudaEventRecord(h->ev1, h->stream));
     StepState out{};
     CU(h, cudaMemcpyAsync(&out, pb.d_state, sizeof(StepState), cudaMemcpyDeviceToHost, h->stream));
     CU(h, cudaStreamSynchronize(h->stream));
-    float ms = 0.f;
-    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
-    h->last_ms = ms;
-    h->total_ms += ms;
+    if (timed) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+        h->last_ms = ms;
+        h->total_ms += ms;
+    }
     if (out.status != kStatusOk) {
         const int rc = status_to_code(h, out.status);
         reset_program(h, pb);
@@ -385,6 +412,12 @@ int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
     if (last_token) *last_token = out.next_token;
     if (last_logit) *last_logit = out.next_logit;
     return ATLAS_OK;
+}
+
+int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
+               float *last_logit)
+{
+    return run_program(h, h->decode, token, pos, steps, out_ids_dev, last_token, last_logit);
 }
 
 int build_decode_program(AtlasCuda *h)
@@ -454,6 +487,281 @@ int build_decode_program(AtlasCuda *h)
     rc = finalize_program(h, h->decode, h);
     if (rc) return rc;
     h->decode.pg.advance = 1;
+    return ATLAS_OK;
+}
+
+// ------------------------------------------------------------------ prefill --
+
+// Exponent e with bound * 2^e in [2^14, 2^15): weights scaled by 2^e keep
+// their binary16 hi/lo split inside the normal range.
+int weight_exponent(float bound)
+{
+    if (!(bound > 0.f) || !(bound <= 3.0e38f)) return 0;
+    int e = 0;
+    frexpf(bound, &e);
+    return 15 - e;
+}
+
+int compute_weight_exponents(AtlasCuda *h)
+{
+    const AtlasModelDesc &d = h->desc;
+    const size_t n = (size_t)d.layers * 7;
+    uint32_t *bits = nullptr;
+    int rc = dalloc(h, &bits, n * 4);
+    if (rc) return rc;
+    CU(h, cudaMemsetAsync(bits, 0, n * 4, h->stream));
+    for (uint32_t l = 0; l < d.layers; ++l) {
+        const AtlasCuda::W &w = h->layers[l];
+        const struct { const uint8_t *p; uint32_t t; uint64_t elems; } m[7] = {
+            {w.q, w.tq, (uint64_t)d.q_dim * d.hidden},   {w.k, w.tk, (uint64_t)d.kv_dim * d.hidden},
+            {w.v, w.tv, (uint64_t)d.kv_dim * d.hidden},  {w.o, w.to, (uint64_t)d.hidden * d.q_dim},
+            {w.gate, w.tg, (uint64_t)d.ffn * d.hidden}, {w.up, w.tu, (uint64_t)d.ffn * d.hidden},
+            {w.down, w.td, (uint64_t)d.hidden * d.ffn}};
+        for (int i = 0; i < 7; ++i)
+            CU(h, atlas_launch_wbound(m[i].t, m[i].p, m[i].elems / 256, bits + l * 7 + i, h->stream));
+    }
+    std::vector<uint32_t> hb(n);
+    CU(h, cudaMemcpyAsync(hb.data(), bits, n * 4, cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    for (uint32_t l = 0; l < d.layers; ++l) {
+        AtlasCuda::W &w = h->layers[l];
+        int *e[7] = {&w.eq, &w.ek, &w.ev, &w.eo, &w.eg, &w.eu, &w.ed};
+        for (int i = 0; i < 7; ++i) {
+            float f;
+            memcpy(&f, &hb[l * 7 + i], 4);
+            *e[i] = weight_exponent(f);
+        }
+    }
+    return ATLAS_OK;
+}
+
+uint32_t prefill_max_units(const AtlasCuda *h)
+{
+    return 3u * (uint32_t)h->sm_count + ((h->pf.cap + 7) / 8) * h->desc.kv_heads + 16u;
+}
+
+int alloc_prefill(AtlasCuda *h)
+{
+    const AtlasModelDesc &d = h->desc;
+    AtlasCuda::Prefill &p = h->pf;
+    p.cap = d.max_prefill;
+    p.tok_pad = (p.cap + pf::kTokTile - 1) / pf::kTokTile * pf::kTokTile;
+    if (const char *t = getenv("ATLAS_PREFILL_TERMS")) {
+        const int v = atoi(t);
+        if (v >= 1 && v <= 3) p.terms = (uint32_t)v;
+    }
+    const uint32_t G = (uint32_t)h->sm_count, tok_tiles = p.tok_pad / pf::kTokTile;
+    const uint32_t max_cols = std::max(d.hidden, std::max(d.q_dim, d.ffn));
+    const uint32_t qkv_tiles = (d.q_dim + 255) / 256 + 2 * ((d.kv_dim + 255) / 256);
+    const uint32_t max_tiles = std::max(std::max(qkv_tiles, (d.hidden + 255) / 256), (d.ffn + 127) / 128);
+    int rc;
+    if ((rc = dalloc(h, &p.x, (size_t)p.cap * d.hidden * 4))) return rc;
+    if ((rc = dalloc(h, &p.q, (size_t)p.cap * d.q_dim * 4))) return rc;
+    if ((rc = dalloc(h, &p.att, (size_t)p.cap * d.q_dim * 4))) return rc;
+    if ((rc = dalloc(h, &p.ffn, (size_t)p.cap * d.ffn * 4))) return rc;
+    if ((rc = dalloc(h, &p.xt, (size_t)tok_tiles * (max_cols / pf::kKBlock) * pf::kXTileBytes))) return rc;
+    if ((rc = dalloc(h, &p.xscale, (size_t)p.tok_pad * 4))) return rc;
+    // split-K partials: a split contraction has at most G units of 128 x 256
+    if ((rc = dalloc(h, &p.ws, (size_t)G * pf::kTokTile * pf::kRowTile * 4))) return rc;
+    if ((rc = dalloc(h, &p.ctr, (size_t)max_tiles * tok_tiles * 4 * 4))) return rc;
+    CU(h, cudaMemset(p.ctr, 0, (size_t)max_tiles * tok_tiles * 4 * 4));
+    p.max_units = prefill_max_units(h);
+    if ((rc = dalloc(h, &p.apart, (size_t)p.max_units * 64 * 132 * 4))) return rc;
+    const size_t actr = (size_t)((p.cap + 7) / 8) * d.kv_heads * 4;
+    if ((rc = dalloc(h, &p.actr, actr))) return rc;
+    CU(h, cudaMemset(p.actr, 0, actr));
+    if ((rc = dalloc(h, &p.units, (size_t)p.max_units * 4))) return rc;
+    if ((rc = dalloc(h, &p.ids, (size_t)p.cap * 4))) return rc;
+    if ((rc = dalloc(h, &p.status, 256))) return rc;
+    CU(h, cudaMemset(p.status, 0, 256));
+    // tail program: rms_norm + head GEMV + argmax over x (the last token's row)
+    std::vector<Phase> &P = p.tail.phases;
+    Phase hd = gemv_phase(d.hidden, G, h->stage_bytes, false,
+                          {seg_of(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)}, h->x, IN_RMSNORM,
+                          h->out_norm, EPI_LOGITS);
+    hd.partial_max = h->pmax;
+    hd.partial_idx = h->pidx;
+    P.push_back(hd);
+    Phase am{};
+    am.kind = PH_ARGMAX;
+    am.layer = 0;
+    am.argmax_items = std::min(hd.n_items, G);
+    P.push_back(am);
+    rc = finalize_program(h, p.tail, h);
+    if (rc) return rc;
+    p.tail.pg.advance = 0;
+    return compute_weight_exponents(h);
+}
+
+pf::GemmSeg gseg(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, int wexp, const float *bias, float *out,
+                 uint64_t head_stride, uint64_t tok_stride, uint32_t tok_off, bool rope)
+{
+    pf::GemmSeg s{};
+    s.w = w;
+    s.type = type;
+    s.rows = rows;
+    s.row_bytes = (uint64_t)(cols / 256) * block_bytes(type);
+    s.wexp = wexp;
+    s.rope = rope ? 1u : 0u;
+    s.bias = bias;
+    s.out = out;
+    s.head_stride = head_stride;
+    s.tok_stride = tok_stride;
+    s.tok_off = tok_off;
+    return s;
+}
+
+// Split-K factor: enough K ranges to give every SM a unit when the tile count
+// alone does not, keeping at least four 64-wide K blocks per range.
+uint32_t plan_ksplit(uint32_t units, uint32_t kblocks, uint32_t grid)
+{
+    if (units >= grid) return 1;
+    uint32_t s = std::min(grid / units, kblocks / 4);
+    return s < 1 ? 1 : s;
+}
+
+// Fill the tiling fields of `a` and launch the contraction over the activation
+// tiles already written for `tokens` tokens of `cols` inputs.
+int launch_gemm(AtlasCuda *h, pf::GemmArgs &a, uint32_t cols, uint32_t tokens, uint32_t pos0)
+{
+    AtlasCuda::Prefill &p = h->pf;
+    const uint32_t G = (uint32_t)h->sm_count;
+    uint32_t tiles = 0;
+    if (a.epi == pf::GEPI_SWIGLU) {
+        tiles = (a.seg[0].rows + 127) / 128;
+    } else {
+        for (uint32_t s = 0; s < a.n_seg; ++s) {
+            a.seg[s].tile0 = tiles;
+            tiles += (a.seg[s].rows + pf::kRowTile - 1) / pf::kRowTile;
+        }
+    }
+    a.n_tiles = tiles;
+    a.tok_tiles = (tokens + pf::kTokTile - 1) / pf::kTokTile;
+    a.kblocks = cols / pf::kKBlock;
+    a.ksplit = plan_ksplit(a.n_tiles * a.tok_tiles, a.kblocks, G);
+    a.tokens = tokens;
+    a.pos0 = pos0;
+    a.terms = p.terms;
+    a.xt = p.xt;
+    a.xscale = p.xscale;
+    a.rope = reinterpret_cast<const float *>(h->rope);
+    a.ws = p.ws;
+    a.ctr = p.ctr;
+    a.status = p.status;
+    const uint32_t units = a.n_tiles * a.tok_tiles * a.ksplit;
+    CU(h, atlas_launch_prefill_gemm(&a, (int)std::min(units, G), h->stream));
+    ++h->launches;
+    return ATLAS_OK;
+}
+
+int launch_split(AtlasCuda *h, const float *x, uint32_t cols, uint32_t tokens, const float *norm_w)
+{
+    const uint32_t tok_pad = (tokens + pf::kTokTile - 1) / pf::kTokTile * pf::kTokTile;
+    CU(h, atlas_launch_prefill_split(x, cols, cols, tokens, tok_pad, norm_w, h->desc.rms_eps, h->pf.xt, h->pf.xscale,
+                                     h->stream));
+    ++h->launches;
+    return ATLAS_OK;
+}
+
+// Attention units for `n` prompt tokens at positions pos0..pos0+n-1: per KV
+// head and tile of 8 queries, the cached positions [0, pos0 + tile end) cut
+// into spans sized so that all units make about three waves over the SMs.
+int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
+{
+    const AtlasModelDesc &d = h->desc;
+    const uint32_t G = (uint32_t)h->sm_count, qt_n = (n + 7) / 8;
+    uint64_t chunks = 0;
+    for (uint32_t qt = 0; qt < qt_n; ++qt) chunks += (pos0 + std::min(8 * qt + 8, n) + 63) / 64;
+    chunks *= d.kv_heads;
+    uint32_t span_chunks = (uint32_t)std::max<uint64_t>(1, (chunks + 3 * G - 1) / (3 * G));
+    std::vector<uint32_t> tab;
+    for (;;) {
+        tab.clear();
+        const uint32_t span = 64 * span_chunks;
+        for (uint32_t g = 0; g < d.kv_heads; ++g)
+            for (uint32_t qt = 0; qt < qt_n; ++qt) {
+                const uint32_t kend = pos0 + std::min(8 * qt + 8, n), parts = (kend + span - 1) / span;
+                for (uint32_t s = 0; s < parts; ++s) tab.push_back(g | (qt << 8) | (s << 20));
+            }
+        if (tab.size() <= h->pf.max_units && (d.max_context + span - 1) / span < 4096) break;
+        ++span_chunks;
+    }
+    CU(h, cudaMemcpyAsync(h->pf.units, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, h->stream));
+    // the table must stay valid until the copy ran: synchronize before it goes out of scope
+    CU(h, cudaStreamSynchronize(h->stream));
+    a = pf::AttnArgs{};
+    a.q = h->pf.q;
+    a.out = h->pf.att;
+    a.part = h->pf.apart;
+    a.ctr = h->pf.actr;
+    a.status = h->pf.status;
+    a.tokens = n;
+    a.pos0 = pos0;
+    a.q_heads = d.q_heads;
+    a.kv_heads = d.kv_heads;
+    a.max_context = d.max_context;
+    a.q_tiles = qt_n;
+    a.span = 64 * span_chunks;
+    a.n_units = (uint32_t)tab.size();
+    a.unit_tab = h->pf.units;
+    return ATLAS_OK;
+}
+
+// One chunk of at most pf.cap prompt tokens through every layer
+// (forward_prefill_batch, src/brain_runtime_batch.c:1644-1718); leaves the
+// last token's final hidden state in x.
+int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
+{
+    const AtlasModelDesc &d = h->desc;
+    AtlasCuda::Prefill &p = h->pf;
+    CU(h, cudaMemcpyAsync(p.ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, h->stream));
+    CU(h, atlas_launch_prefill_embed(p.ids, n, h->embd, h->t_embd,
+                                     (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd), d.hidden,
+                                     p.x, h->stream));
+    ++h->launches;
+    pf::AttnArgs at;
+    int rc = plan_attention(h, n, pos0, at);
+    if (rc) return rc;
+    const uint64_t cache_head = (uint64_t)d.max_context * d.head_dim;
+    for (uint32_t l = 0; l < d.layers; ++l) {
+        const AtlasCuda::W &w = h->layers[l];
+        float *kc = static_cast<float *>(w.kc), *vc = static_cast<float *>(w.vc);
+        // attention block: rms_norm -> Q, K, V (+bias, RoPE, KV-cache store) -> attention -> O (+residual)
+        if ((rc = launch_split(h, p.x, d.hidden, n, w.attn_norm))) return rc;
+        pf::GemmArgs g{};
+        g.epi = pf::GEPI_STORE;
+        g.n_seg = 3;
+        g.seg[0] = gseg(w.q, w.tq, d.q_dim, d.hidden, w.eq, w.bq, p.q, 128, d.q_dim, 0, true);
+        g.seg[1] = gseg(w.k, w.tk, d.kv_dim, d.hidden, w.ek, w.bk, kc, cache_head, d.head_dim, pos0, true);
+        g.seg[2] = gseg(w.v, w.tv, d.kv_dim, d.hidden, w.ev, w.bv, vc, cache_head, d.head_dim, pos0, false);
+        if ((rc = launch_gemm(h, g, d.hidden, n, pos0))) return rc;
+        at.k_cache = kc;
+        at.v_cache = vc;
+        CU(h, atlas_launch_prefill_attn(&at, (int)std::min<uint32_t>(at.n_units, (uint32_t)h->sm_count), h->stream));
+        ++h->launches;
+        if ((rc = launch_split(h, p.att, d.q_dim, n, nullptr))) return rc;
+        g = pf::GemmArgs{};
+        g.epi = pf::GEPI_RESID;
+        g.n_seg = 1;
+        g.seg[0] = gseg(w.o, w.to, d.hidden, d.q_dim, w.eo, nullptr, p.x, 128, d.hidden, 0, false);
+        if ((rc = launch_gemm(h, g, d.q_dim, n, pos0))) return rc;
+        // feed-forward block: rms_norm -> gate, up -> SwiGLU -> down (+residual)
+        if ((rc = launch_split(h, p.x, d.hidden, n, w.ffn_norm))) return rc;
+        g = pf::GemmArgs{};
+        g.epi = pf::GEPI_SWIGLU;
+        g.n_seg = 2;
+        g.seg[0] = gseg(w.gate, w.tg, d.ffn, d.hidden, w.eg, nullptr, p.ffn, 128, d.ffn, 0, false);
+        g.seg[1] = gseg(w.up, w.tu, d.ffn, d.hidden, w.eu, nullptr, nullptr, 0, 0, 0, false);
+        if ((rc = launch_gemm(h, g, d.hidden, n, pos0))) return rc;
+        if ((rc = launch_split(h, p.ffn, d.ffn, n, nullptr))) return rc;
+        g = pf::GemmArgs{};
+        g.epi = pf::GEPI_RESID;
+        g.n_seg = 1;
+        g.seg[0] = gseg(w.down, w.td, d.hidden, d.ffn, w.ed, nullptr, p.x, 128, d.hidden, 0, false);
+        if ((rc = launch_gemm(h, g, d.ffn, n, pos0))) return rc;
+    }
+    CU(h, cudaMemcpyAsync(h->x, p.x + (size_t)(n - 1) * d.hidden, (size_t)d.hidden * 4, cudaMemcpyDeviceToDevice,
+                          h->stream));
     return ATLAS_OK;
 }
 
@@ -581,6 +889,7 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
             TRY(fail(h, ATLAS_ECUDA, "rope upload failed"));
     }
     TRY(build_decode_program(h));
+    TRY(alloc_prefill(h));
     if (cudaDeviceSynchronize() != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "device sync failed"));
 #undef TRY
     *out = h;
@@ -625,18 +934,63 @@ int atlas_cuda_generate(AtlasCuda *h, uint32_t first, uint32_t pos0, uint32_t st
     return ATLAS_OK;
 }
 
-// Prefill: consecutive decode steps over the prompt (the reference's
-// token-at-a-time prefill, src/brain_runtime.c:2025-2028).
+// Batched prefill (forward_prefill_batch, src/brain_runtime_batch.c:1644):
+// the prompt in chunks of up to max_prefill tokens through the tensor-core
+// contractions, then rms_norm + head + argmax for the last token only (the
+// reference's prompt loop asks for no logits before the last token,
+// src/brain_runtime.c:2025-2028).
 int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0, float *last_logits,
                        uint32_t *argmax)
 {
     if (!h || !ids || !n) return fail(h, ATLAS_EINVAL, "empty prefill");
     if ((uint64_t)pos0 + n > h->desc.max_context) return fail(h, ATLAS_ERANGE, "positions exceed max_context");
-    for (uint32_t i = 0; i < n; ++i) {
-        const bool last = i + 1 == n;
-        int rc = atlas_cuda_decode(h, ids[i], pos0 + i, last ? last_logits : nullptr, last ? argmax : nullptr);
+    for (uint32_t i = 0; i < n; ++i)
+        if (ids[i] >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab %u", ids[i], h->desc.vocab);
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    AtlasCuda::Prefill &p = h->pf;
+    CU(h, cudaEventRecord(h->ev0, h->stream));
+    for (uint32_t off = 0; off < n; off += p.cap) {
+        const int rc = prefill_chunk(h, ids + off, std::min(p.cap, n - off), pos0 + off);
         if (rc) return rc;
     }
+    // tail program on x: rms_norm + head GEMV + greedy pick
+    ProgramBuffers &pb = p.tail;
+    StepState init{};
+    init.max_steps = 1;
+    const size_t soff = offsetof(StepState, pos);
+    CU(h, cudaMemcpyAsync(reinterpret_cast<uint8_t *>(pb.d_state) + soff, reinterpret_cast<const uint8_t *>(&init) + soff,
+                          sizeof(StepState) - soff, cudaMemcpyHostToDevice, h->stream));
+    CU(h, atlas_launch_decode(&pb.pg, h->sm_count, h->stream));
+    ++h->launches;
+    CU(h, cudaEventRecord(h->ev1, h->stream));
+    StepState out{};
+    uint32_t st = 0;
+    CU(h, cudaMemcpyAsync(&out, pb.d_state, sizeof(StepState), cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaMemcpyAsync(&st, p.status, 4, cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->last_ms = ms;
+    h->total_ms += ms;
+    if (st != kStatusOk || out.status != kStatusOk) {
+        const int rc = status_to_code(h, st != kStatusOk ? st : out.status);
+        // clear what a failed launch may have left behind
+        cudaMemsetAsync(p.status, 0, 4, h->stream);
+        reset_program(h, pb);
+        const AtlasModelDesc &d = h->desc;
+        const uint32_t tok_tiles = p.tok_pad / pf::kTokTile;
+        const uint32_t max_tiles = std::max(std::max((d.q_dim + 255) / 256 + 2 * ((d.kv_dim + 255) / 256),
+                                                     (d.hidden + 255) / 256), (d.ffn + 127) / 128);
+        cudaMemsetAsync(p.ctr, 0, (size_t)max_tiles * tok_tiles * 16, h->stream);
+        cudaMemsetAsync(p.actr, 0, (size_t)((p.cap + 7) / 8) * d.kv_heads * 4, h->stream);
+        cudaStreamSynchronize(h->stream);
+        return rc;
+    }
+    if (last_logits) {
+        CU(h, cudaMemcpyAsync(last_logits, h->logits, (size_t)h->desc.vocab * 4, cudaMemcpyDeviceToHost, h->stream));
+        CU(h, cudaStreamSynchronize(h->stream));
+    }
+    if (argmax) *argmax = out.next_token;
     return ATLAS_OK;
 }
 
@@ -765,11 +1119,81 @@ extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t ro
     return ATLAS_OK;
 }
 
+// Y[tokens][rows] = X[tokens][cols] . W^T on the prefill contraction kernel.
+// Scratch (activation tiles, split-K partials, counters) is allocated per call;
+// the call synchronizes `stream` to read back the weight bound and the status.
 extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols, const float *d_x,
                                uint64_t tokens, float *d_y, void *stream)
 {
-    (void)type; (void)d_weights; (void)rows; (void)cols; (void)d_x; (void)tokens; (void)d_y; (void)stream;
-    return fail(nullptr, ATLAS_EINVAL, "the tcgen05 prefill GEMM is not built in this version");
+    if ((type != ATLAS_TYPE_Q4_K && type != ATLAS_TYPE_Q6_K) || !d_weights || !d_x || !d_y || !rows || !cols ||
+        !tokens || cols % 256 || rows > 0x7fffffffu || tokens > 0x7fffffffu || cols > 0x7fffffffu)
+        return fail(nullptr, ATLAS_EINVAL, "bad gemm arguments");
+    if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
+        return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
+    if ((uintptr_t)d_weights & 1u) return fail(nullptr, ATLAS_EINVAL, "weights must be 2-byte aligned");
+    if (((uintptr_t)d_x & 3u) || ((uintptr_t)d_y & 3u)) return fail(nullptr, ATLAS_EINVAL, "x and y must be 4-byte aligned");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    if (device_ok(dev, &sms) != ATLAS_OK) return fail(nullptr, ATLAS_ENODEV, "no sm_100 device");
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint32_t tok_tiles = (uint32_t)((tokens + pf::kTokTile - 1) / pf::kTokTile);
+    const uint32_t tiles = (uint32_t)((rows + pf::kRowTile - 1) / pf::kRowTile);
+    uint32_t terms = 3;
+    if (const char *t = getenv("ATLAS_PREFILL_TERMS")) {
+        const int v = atoi(t);
+        if (v >= 1 && v <= 3) terms = (uint32_t)v;
+    }
+    void *xt = nullptr, *xs = nullptr, *ws = nullptr, *ctr = nullptr, *st = nullptr;
+    const size_t ctr_bytes = (size_t)tiles * tok_tiles * 16;
+    int rc = ATLAS_OK;
+    cudaError_t e = cudaMalloc(&xt, (size_t)tok_tiles * (cols / pf::kKBlock) * pf::kXTileBytes);
+    if (e == cudaSuccess) e = cudaMalloc(&xs, (size_t)tok_tiles * pf::kTokTile * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&ws, (size_t)sms * pf::kTokTile * pf::kRowTile * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&ctr, ctr_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&st, 256);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctr, 0, ctr_bytes, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(st, 0, 256, s);
+    uint32_t bits = 0, status = 0;
+    if (e == cudaSuccess)
+        e = atlas_launch_wbound(type, (const uint8_t *)d_weights, rows * (cols / 256), (uint32_t *)st + 32, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, (uint32_t *)st + 32, 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess)
+        e = atlas_launch_prefill_split(d_x, (uint32_t)cols, (uint32_t)cols, (uint32_t)tokens, tok_tiles * pf::kTokTile,
+                                       nullptr, 0.f, (uint8_t *)xt, (float *)xs, s);
+    if (e == cudaSuccess) {
+        float bound;
+        memcpy(&bound, &bits, 4);
+        pf::GemmArgs a{};
+        a.epi = pf::GEPI_STORE;
+        a.n_seg = 1;
+        a.seg[0] = gseg((const uint8_t *)d_weights, type, (uint32_t)rows, (uint32_t)cols, weight_exponent(bound), nullptr,
+                        d_y, 128, rows, 0, false);
+        a.n_tiles = tiles;
+        a.tok_tiles = tok_tiles;
+        a.kblocks = (uint32_t)(cols / pf::kKBlock);
+        a.ksplit = plan_ksplit(tiles * tok_tiles, a.kblocks, (uint32_t)sms);
+        a.tokens = (uint32_t)tokens;
+        a.terms = terms;
+        a.xt = (const uint8_t *)xt;
+        a.xscale = (const float *)xs;
+        a.ws = (float *)ws;
+        a.ctr = (uint32_t *)ctr;
+        a.status = (uint32_t *)st;
+        const uint64_t units = (uint64_t)tiles * tok_tiles * a.ksplit;
+        e = atlas_launch_prefill_gemm(&a, (int)std::min<uint64_t>(units, (uint64_t)sms), s);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&status, st, 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) rc = fail(nullptr, ATLAS_ECUDA, "gemm: %s", cudaGetErrorString(e));
+    else if (status != kStatusOk) rc = fail(nullptr, ATLAS_ETIMEOUT, "gemm: device status %u", status);
+    cudaFree(xt);
+    cudaFree(xs);
+    cudaFree(ws);
+    cudaFree(ctr);
+    cudaFree(st);
+    return rc;
 }
 
 // ---------------------------------------------------------------------------

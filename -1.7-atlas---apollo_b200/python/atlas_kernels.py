@@ -2,11 +2,16 @@
 
     python -m atlas_kernels gemv --type 14 --rows 151936 --cols 2048 [--reps 20]
     python -m atlas_kernels trace --hidden 2048 --layers 36 --q-heads 16 --kv-heads 2 --ffn 11008 --pos 600
+    python -m atlas_kernels gemm --type 12 --rows 22016 --cols 2048 --tokens 512
+    python -m atlas_kernels prefill --tokens 512
 
 `gemv` times atlas_cuda_gemv with CUDA events (with --reps 1 it runs one warm-up
 and one launch, the shape an ncu capture wants); `trace` runs one decode step
 with device-side timestamps (atlas_cuda_trace_step) and prints the time per
-phase kind. Device buffers come from torch; every kernel is this library's.
+phase kind; `gemm` times atlas_cuda_gemm (per-call scratch allocation
+included); `prefill` times a whole batched prefill of a synthetic model
+(device time of the call, best of --reps). Device buffers come from torch;
+every kernel is this library's.
 """
 import argparse
 import os
@@ -78,9 +83,64 @@ def cmd_trace(a):
               f"(barrier gap {gap / n / 1e3:5.2f} us; slowest CTA stamps {stamps} us)")
 
 
+def cmd_gemm(a):
+    import torch
+    nb = a.rows * a.cols // 256
+    w = atlas_cuda.synth_blocks(a.type, nb, seed=1)
+    d_w = torch.from_numpy(w).cuda()
+    d_x = torch.randn(a.tokens, a.cols, device="cuda")
+    d_y = torch.empty(a.tokens, a.rows, device="cuda")
+    atlas_cuda.gemm(a.type, d_w, a.rows, a.cols, d_x, a.tokens, d_y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        atlas_cuda.gemm(a.type, d_w, a.rows, a.cols, d_x, a.tokens, d_y)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.reps
+    flops = 2.0 * a.rows * a.cols * a.tokens
+    print(f"gemm type {a.type} {a.rows}x{a.cols} x {a.tokens} tokens: {ms * 1e3:.1f} us per call "
+          f"(scratch allocation and split included), {flops / ms / 1e9:.1f} TFLOP/s algorithmic")
+
+
+def cmd_prefill(a):
+    path = os.path.join(tempfile.gettempdir(), f"atlas_trace_{a.hidden}_{a.layers}_{a.ffn}_{a.vocab}.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
+    ids = (np.arange(1, a.tokens + 1, dtype=np.uint32) * 7919) % a.vocab
+    with atlas_cuda.Runtime(path, max_context=a.tokens + 16, max_prefill=a.tokens) as rt:
+        rt.prefill(ids, 0, want_logits=False)
+        best = None
+        for _ in range(a.reps):
+            rt.prefill(ids, 0, want_logits=False)
+            _, ms, _ = rt.stats()
+            best = ms if best is None else min(best, ms)
+    h, f, q, kv, L = a.hidden, a.ffn, a.q_heads * 128, a.kv_heads * 128, a.layers
+    flops = 2.0 * a.tokens * L * (2 * q * h + 2 * kv * h + 3 * f * h)
+    print(f"prefill {a.tokens} tokens: {best:.2f} ms device time, {a.tokens / best * 1e3:.0f} tok/s, "
+          f"{flops / best / 1e9:.1f} TFLOP/s of linear-layer work")
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
+    m = sub.add_parser("gemm")
+    m.add_argument("--type", type=int, default=12)
+    m.add_argument("--rows", type=int, default=22016)
+    m.add_argument("--cols", type=int, default=2048)
+    m.add_argument("--tokens", type=int, default=512)
+    m.add_argument("--reps", type=int, default=10)
+    p = sub.add_parser("prefill")
+    p.add_argument("--hidden", type=int, default=2048)
+    p.add_argument("--layers", type=int, default=36)
+    p.add_argument("--q-heads", type=int, default=16)
+    p.add_argument("--kv-heads", type=int, default=2)
+    p.add_argument("--ffn", type=int, default=11008)
+    p.add_argument("--vocab", type=int, default=151936)
+    p.add_argument("--tokens", type=int, default=512)
+    p.add_argument("--reps", type=int, default=5)
     g = sub.add_parser("gemv")
     g.add_argument("--type", type=int, default=14)
     g.add_argument("--rows", type=int, default=151936)
@@ -95,7 +155,7 @@ def main():
     t.add_argument("--vocab", type=int, default=151936)
     t.add_argument("--pos", type=int, default=600)
     a = ap.parse_args()
-    cmd_gemv(a) if a.cmd == "gemv" else cmd_trace(a)
+    {"gemv": cmd_gemv, "trace": cmd_trace, "gemm": cmd_gemm, "prefill": cmd_prefill}[a.cmd](a)
 
 
 if __name__ == "__main__":
