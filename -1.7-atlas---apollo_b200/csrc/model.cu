@@ -26,6 +26,7 @@ extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, c
 extern "C" size_t atlas_decode_hdr_bytes();
 extern "C" size_t atlas_decode_attn_bytes();
 extern "C" cudaError_t atlas_launch_prefill_gemm(const atlas::pf::GemmArgs *a, int grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_prefill_gemm_pairs(int *pairs);
 extern "C" cudaError_t atlas_launch_prefill_split(const float *x, uint32_t ldx, uint32_t cols, uint32_t tokens,
                                                   uint32_t tok_pad, const float *norm_w, float eps, uint8_t *xt,
                                                   float *xscale, cudaStream_t stream);
@@ -76,11 +77,11 @@ struct AtlasCuda {
     };
     // Batched prefill buffers, sized for desc.max_prefill tokens per chunk.
     struct Prefill {
-        uint32_t cap = 0, tok_pad = 0, terms = 3, max_units = 0;
+        uint32_t cap = 0, tok_pad = 0, terms = 3, max_units = 0, pairs = 0;
         float *x = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *xscale = nullptr, *ws = nullptr;
         float *apart = nullptr;
         uint8_t *xt = nullptr;
-        uint32_t *ctr = nullptr, *actr = nullptr, *units = nullptr, *ids = nullptr, *status = nullptr;
+        uint32_t *actr = nullptr, *units = nullptr, *ids = nullptr, *status = nullptr;
         ProgramBuffers tail;   // final rms_norm + head GEMV + argmax of the last token
     } pf;
     std::vector<W> layers;
@@ -545,15 +546,13 @@ int alloc_prefill(AtlasCuda *h)
     const AtlasModelDesc &d = h->desc;
     AtlasCuda::Prefill &p = h->pf;
     p.cap = d.max_prefill;
-    p.tok_pad = (p.cap + pf::kTokTile - 1) / pf::kTokTile * pf::kTokTile;
+    p.tok_pad = (p.cap + pf::kPairTokens - 1) / pf::kPairTokens * pf::kPairTokens;
     if (const char *t = getenv("ATLAS_PREFILL_TERMS")) {
         const int v = atoi(t);
         if (v >= 1 && v <= 3) p.terms = (uint32_t)v;
     }
     const uint32_t G = (uint32_t)h->sm_count, tok_tiles = p.tok_pad / pf::kTokTile;
     const uint32_t max_cols = std::max(d.hidden, std::max(d.q_dim, d.ffn));
-    const uint32_t qkv_tiles = (d.q_dim + 255) / 256 + 2 * ((d.kv_dim + 255) / 256);
-    const uint32_t max_tiles = std::max(std::max(qkv_tiles, (d.hidden + 255) / 256), (d.ffn + 127) / 128);
     int rc;
     if ((rc = dalloc(h, &p.x, (size_t)p.cap * d.hidden * 4))) return rc;
     if ((rc = dalloc(h, &p.q, (size_t)p.cap * d.q_dim * 4))) return rc;
@@ -561,10 +560,13 @@ int alloc_prefill(AtlasCuda *h)
     if ((rc = dalloc(h, &p.ffn, (size_t)p.cap * d.ffn * 4))) return rc;
     if ((rc = dalloc(h, &p.xt, (size_t)tok_tiles * (max_cols / pf::kKBlock) * pf::kXTileBytes))) return rc;
     if ((rc = dalloc(h, &p.xscale, (size_t)p.tok_pad * 4))) return rc;
-    // split-K partials: a split contraction has at most G units of 128 x 256
+    // split-K partials: a split contraction runs at most one unit per CTA pair,
+    // 2 x 128 x 256 floats each
     if ((rc = dalloc(h, &p.ws, (size_t)G * pf::kTokTile * pf::kRowTile * 4))) return rc;
-    if ((rc = dalloc(h, &p.ctr, (size_t)max_tiles * tok_tiles * 4 * 4))) return rc;
-    CU(h, cudaMemset(p.ctr, 0, (size_t)max_tiles * tok_tiles * 4 * 4));
+    int pairs = 0;
+    if (atlas_prefill_gemm_pairs(&pairs) != cudaSuccess || pairs < 1)
+        return fail(h, ATLAS_ECUDA, "no CTA pair of the prefill contraction kernel fits this device");
+    p.pairs = std::min((uint32_t)pairs, G / 2);
     p.max_units = prefill_max_units(h);
     if ((rc = dalloc(h, &p.apart, (size_t)p.max_units * 64 * 132 * 4))) return rc;
     const size_t actr = (size_t)((p.cap + 7) / 8) * d.kv_heads * 4;
@@ -608,6 +610,7 @@ pf::GemmSeg gseg(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, 
     s.head_stride = head_stride;
     s.tok_stride = tok_stride;
     s.tok_off = tok_off;
+    s.vec4 = (((uintptr_t)out & 15u) == 0 && head_stride % 4 == 0 && tok_stride % 4 == 0) ? 1u : 0u;
     return s;
 }
 
@@ -625,7 +628,6 @@ uint32_t plan_ksplit(uint32_t units, uint32_t kblocks, uint32_t grid)
 int launch_gemm(AtlasCuda *h, pf::GemmArgs &a, uint32_t cols, uint32_t tokens, uint32_t pos0)
 {
     AtlasCuda::Prefill &p = h->pf;
-    const uint32_t G = (uint32_t)h->sm_count;
     uint32_t tiles = 0;
     if (a.epi == pf::GEPI_SWIGLU) {
         tiles = (a.seg[0].rows + 127) / 128;
@@ -636,9 +638,9 @@ int launch_gemm(AtlasCuda *h, pf::GemmArgs &a, uint32_t cols, uint32_t tokens, u
         }
     }
     a.n_tiles = tiles;
-    a.tok_tiles = (tokens + pf::kTokTile - 1) / pf::kTokTile;
+    a.tok_pairs = (tokens + pf::kPairTokens - 1) / pf::kPairTokens;
     a.kblocks = cols / pf::kKBlock;
-    a.ksplit = plan_ksplit(a.n_tiles * a.tok_tiles, a.kblocks, G);
+    a.ksplit = plan_ksplit(a.n_tiles * a.tok_pairs, a.kblocks, p.pairs);
     a.tokens = tokens;
     a.pos0 = pos0;
     a.terms = p.terms;
@@ -646,17 +648,16 @@ int launch_gemm(AtlasCuda *h, pf::GemmArgs &a, uint32_t cols, uint32_t tokens, u
     a.xscale = p.xscale;
     a.rope = reinterpret_cast<const float *>(h->rope);
     a.ws = p.ws;
-    a.ctr = p.ctr;
     a.status = p.status;
-    const uint32_t units = a.n_tiles * a.tok_tiles * a.ksplit;
-    CU(h, atlas_launch_prefill_gemm(&a, (int)std::min(units, G), h->stream));
-    ++h->launches;
+    const uint32_t units = a.n_tiles * a.tok_pairs * a.ksplit;
+    CU(h, atlas_launch_prefill_gemm(&a, 2 * (int)std::min(units, p.pairs), h->stream));
+    h->launches += a.ksplit > 1 ? 2 : 1;   // contraction (+ split-K reduction)
     return ATLAS_OK;
 }
 
 int launch_split(AtlasCuda *h, const float *x, uint32_t cols, uint32_t tokens, const float *norm_w)
 {
-    const uint32_t tok_pad = (tokens + pf::kTokTile - 1) / pf::kTokTile * pf::kTokTile;
+    const uint32_t tok_pad = (tokens + pf::kPairTokens - 1) / pf::kPairTokens * pf::kPairTokens;
     CU(h, atlas_launch_prefill_split(x, cols, cols, tokens, tok_pad, norm_w, h->desc.rms_eps, h->pf.xt, h->pf.xscale,
                                      h->stream));
     ++h->launches;
@@ -978,10 +979,6 @@ int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t p
         cudaMemsetAsync(p.status, 0, 4, h->stream);
         reset_program(h, pb);
         const AtlasModelDesc &d = h->desc;
-        const uint32_t tok_tiles = p.tok_pad / pf::kTokTile;
-        const uint32_t max_tiles = std::max(std::max((d.q_dim + 255) / 256 + 2 * ((d.kv_dim + 255) / 256),
-                                                     (d.hidden + 255) / 256), (d.ffn + 127) / 128);
-        cudaMemsetAsync(p.ctr, 0, (size_t)max_tiles * tok_tiles * 16, h->stream);
         cudaMemsetAsync(p.actr, 0, (size_t)((p.cap + 7) / 8) * d.kv_heads * 4, h->stream);
         cudaStreamSynchronize(h->stream);
         return rc;
@@ -1126,7 +1123,7 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
                                uint64_t tokens, float *d_y, void *stream)
 {
     if ((type != ATLAS_TYPE_Q4_K && type != ATLAS_TYPE_Q6_K) || !d_weights || !d_x || !d_y || !rows || !cols ||
-        !tokens || cols % 256 || rows > 0x7fffffffu || tokens > 0x7fffffffu || cols > 0x7fffffffu)
+        !tokens || cols % 256 || rows > 0x7fffffffu || tokens > 0x7fffffffu || cols > pf::kSplitMaxCols)
         return fail(nullptr, ATLAS_EINVAL, "bad gemm arguments");
     if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
         return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
@@ -1137,22 +1134,23 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
     int sms = 0;
     if (device_ok(dev, &sms) != ATLAS_OK) return fail(nullptr, ATLAS_ENODEV, "no sm_100 device");
     cudaStream_t s = (cudaStream_t)stream;
-    const uint32_t tok_tiles = (uint32_t)((tokens + pf::kTokTile - 1) / pf::kTokTile);
+    const uint32_t tok_pairs = (uint32_t)((tokens + pf::kPairTokens - 1) / pf::kPairTokens);
     const uint32_t tiles = (uint32_t)((rows + pf::kRowTile - 1) / pf::kRowTile);
     uint32_t terms = 3;
     if (const char *t = getenv("ATLAS_PREFILL_TERMS")) {
         const int v = atoi(t);
         if (v >= 1 && v <= 3) terms = (uint32_t)v;
     }
-    void *xt = nullptr, *xs = nullptr, *ws = nullptr, *ctr = nullptr, *st = nullptr;
-    const size_t ctr_bytes = (size_t)tiles * tok_tiles * 16;
+    int pairs = 0;
+    if (atlas_prefill_gemm_pairs(&pairs) != cudaSuccess || pairs < 1)
+        return fail(nullptr, ATLAS_ECUDA, "no CTA pair of the contraction kernel fits this device");
+    pairs = std::min(pairs, sms / 2);
+    void *xt = nullptr, *xs = nullptr, *ws = nullptr, *st = nullptr;
     int rc = ATLAS_OK;
-    cudaError_t e = cudaMalloc(&xt, (size_t)tok_tiles * (cols / pf::kKBlock) * pf::kXTileBytes);
-    if (e == cudaSuccess) e = cudaMalloc(&xs, (size_t)tok_tiles * pf::kTokTile * 4);
+    cudaError_t e = cudaMalloc(&xt, (size_t)2 * tok_pairs * (cols / pf::kKBlock) * pf::kXTileBytes);
+    if (e == cudaSuccess) e = cudaMalloc(&xs, (size_t)tok_pairs * pf::kPairTokens * 4);
     if (e == cudaSuccess) e = cudaMalloc(&ws, (size_t)sms * pf::kTokTile * pf::kRowTile * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&ctr, ctr_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&st, 256);
-    if (e == cudaSuccess) e = cudaMemsetAsync(ctr, 0, ctr_bytes, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(st, 0, 256, s);
     uint32_t bits = 0, status = 0;
     if (e == cudaSuccess)
@@ -1160,7 +1158,7 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
     if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, (uint32_t *)st + 32, 4, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e == cudaSuccess)
-        e = atlas_launch_prefill_split(d_x, (uint32_t)cols, (uint32_t)cols, (uint32_t)tokens, tok_tiles * pf::kTokTile,
+        e = atlas_launch_prefill_split(d_x, (uint32_t)cols, (uint32_t)cols, (uint32_t)tokens, tok_pairs * pf::kPairTokens,
                                        nullptr, 0.f, (uint8_t *)xt, (float *)xs, s);
     if (e == cudaSuccess) {
         float bound;
@@ -1171,18 +1169,17 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
         a.seg[0] = gseg((const uint8_t *)d_weights, type, (uint32_t)rows, (uint32_t)cols, weight_exponent(bound), nullptr,
                         d_y, 128, rows, 0, false);
         a.n_tiles = tiles;
-        a.tok_tiles = tok_tiles;
+        a.tok_pairs = tok_pairs;
         a.kblocks = (uint32_t)(cols / pf::kKBlock);
-        a.ksplit = plan_ksplit(tiles * tok_tiles, a.kblocks, (uint32_t)sms);
+        a.ksplit = plan_ksplit(tiles * tok_pairs, a.kblocks, (uint32_t)pairs);
         a.tokens = (uint32_t)tokens;
         a.terms = terms;
         a.xt = (const uint8_t *)xt;
         a.xscale = (const float *)xs;
         a.ws = (float *)ws;
-        a.ctr = (uint32_t *)ctr;
         a.status = (uint32_t *)st;
-        const uint64_t units = (uint64_t)tiles * tok_tiles * a.ksplit;
-        e = atlas_launch_prefill_gemm(&a, (int)std::min<uint64_t>(units, (uint64_t)sms), s);
+        const uint64_t units = (uint64_t)tiles * tok_pairs * a.ksplit;
+        e = atlas_launch_prefill_gemm(&a, 2 * (int)std::min<uint64_t>(units, (uint64_t)pairs), s);
     }
     if (e == cudaSuccess) e = cudaMemcpyAsync(&status, st, 4, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
@@ -1191,7 +1188,6 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
     cudaFree(xt);
     cudaFree(xs);
     cudaFree(ws);
-    cudaFree(ctr);
     cudaFree(st);
     return rc;
 }

@@ -22,17 +22,20 @@
 namespace atlas {
 namespace pf {
 
-constexpr int kTokTile = 128;          // MMA M: tokens per tile (TMEM lanes)
-constexpr int kRowTile = 256;          // MMA N: weight rows per tile (TMEM columns)
+constexpr int kTokTile = 128;          // tokens per CTA (TMEM lanes)
+constexpr int kPairTokens = 256;       // MMA M over the CTA pair
+constexpr int kRowTile = 256;          // MMA N: weight rows per tile (TMEM columns); 128 per CTA
 constexpr int kKBlock = 64;            // K elements per stage: one 128-byte swizzle row
-constexpr int kStages = 2;
-constexpr uint32_t kATermBytes = kTokTile * 128;   // one operand term of a token tile (16 KB)
-constexpr uint32_t kBTermBytes = kRowTile * 128;   // one operand term of a weight tile (32 KB)
+constexpr int kStages = 3;
+constexpr uint32_t kATermBytes = kTokTile * 128;        // one operand term of a CTA's tokens (16 KB)
+constexpr uint32_t kBTermBytes = (kRowTile / 2) * 128;  // one operand term of a CTA's weight rows (16 KB)
 constexpr uint32_t kStageBytes = 2 * kATermBytes + 2 * kBTermBytes;
-constexpr int kWarps = 14;             // 0 copy, 1 MMA, 2-5 epilogue, 6-13 dequant
+constexpr int kWarps = 22;             // 0 copy, 1 MMA, 2-5 epilogue, 6-21 dequant
+constexpr int kDequantWarps = kWarps - 6;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSeg = 3;
 constexpr uint32_t kXTileBytes = 2 * kATermBytes;  // hi + lo of one (token tile, K block)
+constexpr uint32_t kSplitMaxCols = 57344;          // longest input row the split pass stages
 
 enum GemmEpilogue : uint32_t {
     GEPI_STORE = 0,   // out = acc + bias (optionally RoPE'd)
@@ -58,6 +61,7 @@ struct GemmSeg {
     uint64_t tok_stride;
     uint32_t tok_off;
     uint32_t tile0;        // first row tile of this segment
+    uint32_t vec4;         // out, head_stride and tok_stride keep 16-float groups 16-byte aligned
 };
 
 struct GemmArgs {
@@ -65,8 +69,8 @@ struct GemmArgs {
     uint32_t n_seg;
     uint32_t epi;
     uint32_t n_tiles;      // row tiles over all segments (paired: tiles of 128 + 128 rows)
-    uint32_t tok_tiles;
-    uint32_t ksplit;       // K ranges per tile (split-K with a last-arriver reduction)
+    uint32_t tok_pairs;    // 256-token tiles (one per CTA pair)
+    uint32_t ksplit;       // K ranges per tile (split-K; a reduction kernel sums them)
     uint32_t kblocks;      // cols / 64
     uint32_t tokens;
     uint32_t pos0;         // position of token 0 (RoPE)
@@ -74,8 +78,7 @@ struct GemmArgs {
     const uint8_t *xt;     // activation tiles written by the split kernel
     const float *xscale;   // per token 2^-sx
     const float *rope;     // (cos, sin) table [position][64]
-    float *ws;             // split-K partials
-    uint32_t *ctr;         // per output tile arrival counters (zero between launches)
+    float *ws;             // split-K partials [tile][K range][128 tokens][256 rows]
     uint32_t *status;
 };
 
