@@ -362,8 +362,11 @@ __device__ float stage_x(const Program &pg, const Phase &ph, const Smem &sm)
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) { m = fmaxf(m, sm.h->fred[w]); t += sm.h->dred[w]; }
     // scale so that max|x| lands in [2^13, 2^14): far from fp16 overflow, and
-    // the lo parts of small elements stay normal
-    const float s = (m > 0.f && isfinite(m)) ? exp2f((float)(13 - ilogbf(m))) : 1.0f;
+    // the lo parts of small elements stay normal. The exponent is capped at
+    // 126 so that the scale stays finite for rows of tiny values (a SwiGLU
+    // output of all-negative gates can sit near the fp32 underflow limit);
+    // such rows then contribute ~0, as they do in fp32.
+    const float s = (m > 0.f && isfinite(m)) ? exp2f((float)min(13 - ilogbf(m), 126)) : 1.0f;
     const float inv_rms = norm ? 1.0f / sqrtf((float)(t / (double)n) + pg.rms_eps) : 1.0f;
     float *xs16 = reinterpret_cast<float *>(sm.xarea + (size_t)n * 4u);
     for (uint32_t u = threadIdx.x; u < n / 16u; u += kConsumerWarps * 32) {

@@ -23,7 +23,8 @@
 //               CTA one thread issues the MMAs of every product term once
 //               both SMs' stages are full, and multicasts the stage release
 //               and the finished accumulator to both CTAs; in the odd CTA it
-//               relays the landing of its activation copy to the even CTA;
+//               waits for its own activation copy and dequant warps and
+//               relays one arrival per stage to the even CTA;
 //   warps 2-5   read this CTA's accumulator with tcgen05.ld (lane = token),
 //               undo the power-of-two scales and apply the fused epilogue:
 //               bias, RoPE and the KV-cache store for Q/K/V, residual add
@@ -203,7 +204,8 @@ __host__ __device__ constexpr uint32_t sw128_off(uint32_t row, uint32_t chunk)
 
 struct Bars {
     uint64_t xfull[kStages];   // this CTA's activation copy landed (tx count)
-    uint64_t full[kStages];    // even CTA: the pair's dequant warps + the odd CTA's copy relay
+    uint64_t full[kStages];    // even CTA: its dequant group (8 warps) + the odd CTA's relay
+    uint64_t wfull[kStages];   // odd CTA: its dequant group (8 warps), relayed to the even CTA
     uint64_t empty[kStages];   // both: the MMAs reading the stage completed
     uint64_t acc_full[2];      // both: accumulator complete
     uint64_t acc_empty[2];     // even CTA: the pair's 8 epilogue warps are done reading
@@ -437,7 +439,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_ke
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&bars->xfull[s], 1);
-            mbar_init(&bars->full[s], kDequantWarps + 1);   // one group of 8 warps in each CTA + relay
+            mbar_init(&bars->full[s], kDequantWarps / 2 + 1);   // one group of 8 warps + the relay
+            mbar_init(&bars->wfull[s], kDequantWarps / 2);
             mbar_init(&bars->empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -522,7 +525,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_ke
                 bool ok = true;
                 for (uint32_t kb = un.kb0; kb < un.kb1; ++kb, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                    if (!mbar_wait_cluster(&bars->xfull[s], ph, err)) { ok = false; break; }
+                    if (!mbar_wait_cluster(&bars->xfull[s], ph, err) || !mbar_wait_cluster(&bars->wfull[s], ph, err)) {
+                        ok = false;
+                        break;
+                    }
                     mbar_arrive_cta(&bars->full[s], 0);
                 }
                 if (!ok) break;
@@ -626,10 +632,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_ke
                 }
                 fence_proxy_async();
                 __syncwarp();
-                if (lane == 0) {
-                    if (rank == 0) mbar_arrive(&bars->full[s]);
-                    else mbar_arrive_cta(&bars->full[s], 0);
-                }
+                if (lane == 0) mbar_arrive(rank == 0 ? &bars->full[s] : &bars->wfull[s]);
                 cur = q;
                 return cur.live;
             };
@@ -915,7 +918,10 @@ __global__ void __launch_bounds__(256) split_kernel(const float *x, uint32_t ldx
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fred[i]);
     int e = 0;
     if (amax > 0.f && amax <= FLT_MAX) frexpf(amax, &e);
-    const int sx = amax > 0.f ? 15 - e : 0;
+    // exponent kept in [-126, 126] so that 2^sx and 2^-sx stay finite normal
+    // numbers: a row of tiny values (a SwiGLU output of all-negative gates
+    // can sit near the fp32 underflow limit) then contributes ~0, as in fp32
+    const int sx = amax > 0.f ? max(-126, min(126, 15 - e)) : 0;
     const float p2 = ldexpf(1.0f, sx);
     for (uint32_t ch = threadIdx.x; ch < nch; ch += blockDim.x) {
         const float4 a0 = reinterpret_cast<const float4 *>(rowbuf)[2 * ch];

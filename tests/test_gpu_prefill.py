@@ -127,3 +127,47 @@ def test_prefill_rejects_out_of_vocab(torch_cuda, tiny_model):
         with pytest.raises(atlas_cuda.AtlasError):
             rt.prefill(np.array([1, 2, 1024], np.uint32))
         rt.prefill(np.array([1, 2, 3], np.uint32))   # the handle still works
+
+
+def test_gemm_rows_near_fp32_underflow(torch_cuda, oracle):
+    """Rows whose largest value is tiny (a SwiGLU output with every gate far
+    below zero reaches ~1e-35, subnormals included) or zero: the per-row scale
+    must stay finite and the rows contribute ~0, as they do in fp32."""
+    torch = torch_cuda
+    t, rows, cols = Q6, 512, 11008
+    nb = rows * cols // 256
+    w = atlas_cuda.synth_blocks(t, nb, seed=5, stream=t)
+    W = oracle.dequant(t, w, nb, 256).reshape(rows, cols).astype(np.float64)
+    rng = np.random.default_rng(3)
+    X = rng.standard_normal((6, cols)).astype(np.float32)
+    X[0] *= np.float32(8.3e-35 / np.abs(X[0]).max())          # max just below 2^-113
+    X[1] *= np.float32(1e-39)                                   # subnormal
+    X[2] = 0.0
+    X[3] *= np.float32(1e-30)
+    want = X.astype(np.float64) @ W.T
+    bound = 3e-5 * (np.abs(X).astype(np.float64) @ np.abs(W).T) + 1e-30
+    d_w = torch.from_numpy(w).cuda()
+    d_x = torch.from_numpy(X).cuda()
+    d_y = torch.full((6, rows), float("nan"), dtype=torch.float32, device="cuda")
+    atlas_cuda.gemm(t, d_w, rows, cols, d_x, 6, d_y)
+    torch.cuda.synchronize()
+    got = d_y.cpu().numpy().astype(np.float64)
+    assert np.isfinite(got).all()
+    assert (np.abs(got - want) <= bound).all()
+
+
+def test_gemv_input_near_fp32_underflow(torch_cuda, oracle):
+    torch = torch_cuda
+    t, rows, cols = Q6, 256, 11008
+    w = atlas_cuda.synth_blocks(t, rows * cols // 256, seed=6, stream=t)
+    d_w = torch.from_numpy(w).cuda()
+    for scale in (8.3e-35, 1e-39, 0.0):
+        x = (np.random.default_rng(4).standard_normal(cols) * scale).astype(np.float32)
+        want = oracle.matvec_raw(t, w, rows, cols, x)
+        d_x = torch.from_numpy(x).cuda()
+        d_y = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+        atlas_cuda.gemv(t, d_w, rows, cols, d_x, d_y)
+        torch.cuda.synchronize()
+        got = d_y.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert np.abs(got.astype(np.float64) - want).max() <= 1e-4 * np.abs(want).max() + 1e-30
