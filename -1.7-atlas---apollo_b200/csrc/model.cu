@@ -21,12 +21,14 @@
 #include "quant.cuh"
 
 #include "prefill.h"
+#include "gemv.h"
 
 extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream);
 extern "C" size_t atlas_decode_hdr_bytes();
 extern "C" size_t atlas_decode_attn_bytes();
 extern "C" cudaError_t atlas_launch_prefill_gemm(const atlas::pf::GemmArgs *a, int grid, cudaStream_t stream);
 extern "C" cudaError_t atlas_prefill_gemm_pairs(int *pairs);
+extern "C" cudaError_t atlas_launch_gemv2(const atlas::gv::GemvArgs *a, cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_prefill_split(const float *x, uint32_t ldx, uint32_t cols, uint32_t tokens,
                                                   uint32_t tok_pad, const float *norm_w, float eps, uint8_t *xt,
                                                   float *xscale, cudaStream_t stream);
@@ -489,6 +491,15 @@ int build_decode_program(AtlasCuda *h)
     if (rc) return rc;
     h->decode.pg.advance = 1;
     return ATLAS_OK;
+}
+
+// Rows per CTA of the streaming GEMV: a multiple of 32 (8 warps x 4 rows)
+// giving about two CTAs per SM.
+uint32_t gemv_rows_per_cta(uint32_t rows, uint32_t sms)
+{
+    uint32_t r = (rows + 2 * sms - 1) / (2 * sms);
+    r = (r + 31u) & ~31u;
+    return std::min(256u, std::max(32u, r));
 }
 
 // ------------------------------------------------------------------ prefill --
@@ -1078,7 +1089,7 @@ extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t ro
                                float *d_y, void *stream)
 {
     if ((type != ATLAS_TYPE_Q4_K && type != ATLAS_TYPE_Q6_K) || !d_weights || !d_x || !d_y || !rows || !cols ||
-        cols % 256 || rows > 0xffffffffu || cols > 65536)
+        cols % 256 || rows > 0xffffffffu || cols > 49152)
         return fail(nullptr, ATLAS_EINVAL, "bad gemv arguments");
     if (type == ATLAS_TYPE_Q4_K && ((uintptr_t)d_weights & 15u))
         return fail(nullptr, ATLAS_EINVAL, "Q4_K weights must be 16-byte aligned");
@@ -1089,29 +1100,21 @@ extern "C" int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t ro
     cudaGetDevice(&dev);
     int sms = 0;
     if (dev < 0 || dev >= 16 || device_ok(dev, &sms) != ATLAS_OK) return fail(nullptr, ATLAS_ENODEV, "no sm_100 device");
-    GemvCtx &c = g_gemv_ctx[dev];
-    AtlasCuda tmp;  // error sink for the helpers
-    if (c.device != dev) {
-        c.device = dev;
-        c.sms = sms;
-        c.pb.phases.assign(1, Phase{});
-        // the program buffers live for the rest of the process
-        int rc = finalize_program(&tmp, c.pb, nullptr);
-        if (rc) { c.device = -1; return rc; }
-    }
-    uint32_t n_stages = 0, stage_bytes = 0;
-    if (plan_smem(dev, (uint32_t)cols, n_stages, stage_bytes) != ATLAS_OK)
-        return fail(nullptr, ATLAS_EINVAL, "input length %llu too large", (unsigned long long)cols);
-    Phase ph = gemv_phase((uint32_t)cols, (uint32_t)c.sms, stage_bytes, false,
-                          {seg_of((const uint8_t *)d_weights, type, (uint32_t)rows, (uint32_t)cols, nullptr, d_y)},
-                          d_x, IN_RAW, nullptr, EPI_STORE);
-    Program pg = c.pb.pg;
-    pg.n_stages = n_stages;
-    pg.stage_bytes = stage_bytes;
-    pg.max_cols = (uint32_t)cols;
-    cudaStream_t s = (cudaStream_t)stream;
-    cudaError_t e = cudaMemcpyAsync(c.pb.d_phases, &ph, sizeof(Phase), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = atlas_launch_decode(&pg, c.sms, s);
+    gv::GemvArgs a{};
+    a.seg[0].w = (const uint8_t *)d_weights;
+    a.seg[0].type = type;
+    a.seg[0].rows = (uint32_t)rows;
+    a.seg[0].row_bytes = (cols / 256) * block_bytes(type);
+    a.seg[0].out = d_y;
+    a.n_seg = 1;
+    a.seg_start[0] = 0;
+    a.seg_start[1] = (uint32_t)rows;
+    a.cols = (uint32_t)cols;
+    a.total_rows = (uint32_t)rows;
+    a.rows_per_cta = gemv_rows_per_cta((uint32_t)rows, (uint32_t)sms);
+    a.x = d_x;
+    a.epi = gv::GV_STORE;
+    const cudaError_t e = atlas_launch_gemv2(&a, (cudaStream_t)stream);
     if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
     return ATLAS_OK;
 }

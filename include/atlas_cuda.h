@@ -131,11 +131,10 @@ int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, fl
                        void *stream);
 
 /* y[rows] = W[rows x cols] x[cols] for a Q4_K / Q6_K tensor in device memory
-   (the decode GEMV engine; matvec_rows, src/brain_runtime.c:1133).
-   d_weights: 16-byte aligned for Q4_K, 2-byte for Q6_K; the engine's bulk copies
-   read up to 15 bytes past the last row, which cudaMalloc'd buffers always allow.
-   d_x 16-byte aligned. Calls from several host threads or streams at once are
-   not supported (the kernel's descriptor lives in one per-device buffer). */
+   (matvec_rows, src/brain_runtime.c:1133) on the streaming GEMV kernel: fp32
+   FMAs over the exactly dequantized quants, one launch, no scratch.
+   d_weights: 16-byte aligned for Q4_K, 2-byte for Q6_K; cols a multiple of 256,
+   at most 49152; d_x 16-byte aligned, d_y 4-byte aligned. */
 int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                     const float *d_x, float *d_y, void *stream);
 
@@ -153,9 +152,15 @@ int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_
 int atlas_cuda_gemv_noalloc(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                             const float *d_x, float *d_y, void *stream);
 
-/* Y[tokens x rows] = X[tokens x cols] W^T through the tcgen05 prefill GEMM
-   (batch_matvec_rows, src/brain_runtime_batch.c:1525): X fp32 in, fp16
-   operand tiles, fp32 accumulation. */
+/* Y[tokens x rows] = X[tokens x cols] W^T (all fp32, row-major, device
+   pointers) through the prefill contraction kernel (batch_matvec_rows,
+   src/brain_runtime_batch.c:1525): 2-SM tcgen05 MMA over binary16 hi/lo
+   splits of X and of the dequantized weights (three products, fp32
+   accumulation: fp32-level accuracy). type: ATLAS_TYPE_Q4_K (16-byte aligned
+   weights) or ATLAS_TYPE_Q6_K (2-byte aligned); cols a multiple of 256 and at
+   most 57344. Scratch is allocated per call and the call synchronizes
+   `stream`. ATLAS_EINVAL for bad arguments, ATLAS_ETIMEOUT if a bounded
+   device wait gave up. */
 int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                     const float *d_x, uint64_t tokens, float *d_y, void *stream);
 
