@@ -55,6 +55,11 @@ __device__ __forceinline__ float2 dot4(uint32_t w, float4 xv, float bias, float2
     return acc;
 }
 
+// x is staged in shared memory with 4 floats of padding after every 64 (a
+// lane reads its own 64-value chunk, so the lane stride becomes 272 bytes and
+// a warp's float4 reads hit distinct banks).
+__device__ __forceinline__ uint32_t xpad(uint32_t k) { return k + 4u * (k >> 6); }
+
 // ---------------------------------------------------------------- Q4_K ----
 
 struct RawQ4 {
@@ -86,8 +91,8 @@ __device__ __forceinline__ void k4_sm(uint32_t j, const uint4 &h, float d, float
 __device__ __forceinline__ float dot_q4(const RawQ4 &r, uint32_t ch, const float *xs, const float *gs)
 {
     const uint32_t kq = ch & 3u, base = (ch >> 2) * 256u + 64u * kq;
-    const float4 *xl = reinterpret_cast<const float4 *>(xs + base);        // values 0..31: low nibbles
-    const float4 *xh = reinterpret_cast<const float4 *>(xs + base + 32u);  // values 32..63: high nibbles
+    const float4 *xl = reinterpret_cast<const float4 *>(xs + xpad(base));         // values 0..31: low nibbles
+    const float4 *xh = reinterpret_cast<const float4 *>(xs + xpad(base) + 32u);   // values 32..63: high nibbles
     const uint32_t q[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
     float2 al = make_float2(0.f, 0.f), ah = make_float2(0.f, 0.f);
 #pragma unroll
@@ -138,7 +143,7 @@ __device__ __forceinline__ void load_q6(const uint8_t *row, uint32_t ch, RawQ6 &
 __device__ __forceinline__ float dot_q6(const RawQ6 &r, uint32_t ch, const float *xs)
 {
     const uint32_t kq = ch & 3u, sh = r.dsh >> 16, s4 = 4u * (kq & 1u);
-    const float4 *xv = reinterpret_cast<const float4 *>(xs + (ch >> 2) * 256u + 64u * kq);
+    const float4 *xv = reinterpret_cast<const float4 *>(xs + xpad((ch >> 2) * 256u + 64u * kq));
     float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
     for (int hb = 0; hb < 2; ++hb) {
@@ -252,7 +257,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     if (a.pdl) pdl_wait();
 
     // stage x (rms_norm'ed when norm_w is set) and its 32-value group sums
-    float *xs = smem_f, *gs = smem_f + a.cols;
+    float *xs = smem_f, *gs = smem_f + a.cols + a.cols / 16u;
     float inv = 1.0f;
     if (a.norm_w) {
         double ss = 0.0;
@@ -281,7 +286,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
                 v.z = __fmul_rn(__fmul_rn(v.z, inv), wn.z);
                 v.w = __fmul_rn(__fmul_rn(v.w, inv), wn.w);
             }
-            reinterpret_cast<float4 *>(xs + 32u * g)[i] = v;
+            *reinterpret_cast<float4 *>(xs + xpad(32u * g + 4u * (uint32_t)i)) = v;
             s += (v.x + v.y) + (v.z + v.w);
         }
         gs[g] = s;
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
 
 using namespace atlas::gv;
 
-extern "C" size_t atlas_gemv2_smem(uint32_t cols) { return (size_t)cols * 4u + (size_t)cols / 32u * 4u; }
+extern "C" size_t atlas_gemv2_smem(uint32_t cols) { return ((size_t)cols + cols / 16u + cols / 32u) * 4u; }
 
 extern "C" cudaError_t atlas_launch_gemv2(const GemvArgs *a, cudaStream_t stream)
 {

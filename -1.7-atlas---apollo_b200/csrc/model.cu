@@ -22,6 +22,7 @@
 
 #include "prefill.h"
 #include "gemv.h"
+#include "decode2.h"
 
 extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream);
 extern "C" size_t atlas_decode_hdr_bytes();
@@ -36,6 +37,15 @@ extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t 
                                                   uint32_t type, uint64_t row_bytes, uint32_t hidden, float *x,
                                                   cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_prefill_attn(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
+extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots);
+extern "C" size_t atlas_d2_attn_smem(uint32_t splits);
+extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
+extern "C" cudaError_t atlas_d2_launch_mv(const atlas::d2::MvArgs *a, uint32_t grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_d2_launch_attn(const atlas::d2::AttnArgs *a, uint32_t grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,
+                                             uint32_t vocab, float *x, atlas::d2::DecState *st, cudaStream_t stream);
+extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n,
+                                              atlas::d2::DecState *st, cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_wbound(uint32_t type, const uint8_t *blocks, uint64_t nblocks, uint32_t *out_bits,
                                            cudaStream_t stream);
 
@@ -99,6 +109,16 @@ struct AtlasCuda {
     uint32_t *d_out_ids = nullptr;
     uint32_t out_ids_cap = 0;
     ProgramBuffers decode;
+    // Graph decode step (decode2.cu): one CUDA graph of PDL-chained kernels.
+    struct Graph2 {
+        bool on = false;
+        d2::DecState *st = nullptr;
+        float *bpart = nullptr, *apart = nullptr;
+        uint32_t *tctr = nullptr, *actr = nullptr, *status = nullptr;
+        uint32_t tctr_n = 0, splits = 0, kernels = 0;
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+    } g2;
     uint64_t launches = 0;
     double last_ms = 0.0;
     double total_ms = 0.0;
@@ -417,9 +437,288 @@ int run_program(AtlasCuda *h, ProgramBuffers &pb, uint32_t token, uint32_t pos, 
     return ATLAS_OK;
 }
 
+// ------------------------------------------------ graph decode step ------
+
+// Shared memory a kernel may take so that two CTAs (this kernel's and its
+// successor's) fit on one SM: (228 KB - 2 x 1 KB reserved) / 2.
+constexpr uint32_t kHalfSmBytes = 115712;
+
+struct MvPlan {
+    d2::MvArgs a{};
+    uint32_t grid = 0;
+};
+
+d2::MvSeg mvseg(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, const float *bias, float *out)
+{
+    d2::MvSeg s{};
+    s.w = w;
+    s.type = type;
+    s.rows = rows;
+    s.row_bytes = (uint64_t)(cols / 256u) * block_bytes(type);
+    s.bias = bias;
+    s.out = out;
+    return s;
+}
+
+// Task ranges and ring plan of one mv launch shape. Segments get CTAs in
+// proportion to their bytes; inside a segment (or the gate/up pair) every CTA
+// takes an equal share of the 16-row x 256-element tasks (+-1). The ring slot
+// holds `st` tasks; `st` and the ring depth are the largest that keep the
+// launch within half an SM's shared memory with at least 3 slots.
+int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initializer_list<d2::MvSeg> segs, uint32_t epi)
+{
+    d2::MvArgs &a = p.a;
+    a = d2::MvArgs{};
+    a.cols = cols;
+    a.nb = cols / 256u;
+    a.paired = paired ? 1u : 0u;
+    a.epi = epi;
+    for (const d2::MvSeg &sg : segs) {
+        if (a.n_seg == 3) return fail(h, ATLAS_EINVAL, "mv: too many segments");
+        if ((sg.type != 12u && sg.type != 14u) || sg.rows % 16u || !sg.rows)
+            return fail(h, ATLAS_EINVAL, "mv: segment type %u rows %u unsupported", sg.type, sg.rows);
+        a.seg[a.n_seg++] = sg;
+    }
+    if (!cols || cols % 256u || (paired && (a.n_seg != 2 || a.seg[0].rows != a.seg[1].rows)))
+        return fail(h, ATLAS_EINVAL, "mv: bad shape");
+    const uint32_t G = (uint32_t)h->sm_count;
+    const uint32_t P = paired ? 2u : 1u, TP = a.nb * P;
+    std::vector<uint32_t> cta_n, tasks;
+    if (paired) {
+        tasks.push_back(a.seg[0].rows / 16u * TP);
+        cta_n.push_back(std::min(G, tasks[0]));
+    } else {
+        double total = 0;
+        for (uint32_t s = 0; s < a.n_seg; ++s) total += (double)a.seg[s].rows * (double)a.seg[s].row_bytes;
+        uint32_t used = 0;
+        for (uint32_t s = 0; s < a.n_seg; ++s) {
+            tasks.push_back(a.seg[s].rows / 16u * a.nb);
+            const double share = (double)G * (double)a.seg[s].rows * (double)a.seg[s].row_bytes / total;
+            uint32_t n = (uint32_t)std::max(1.0, std::floor(share + 0.5));
+            n = std::min(n, tasks[s]);
+            cta_n.push_back(n);
+            used += n;
+        }
+        while (used > G) {
+            size_t big = 0;
+            for (size_t s = 1; s < cta_n.size(); ++s)
+                if (cta_n[s] > cta_n[big]) big = s;
+            if (cta_n[big] <= 1) return fail(h, ATLAS_EINVAL, "mv: more segments than SMs");
+            --cta_n[big];
+            --used;
+        }
+    }
+    std::vector<d2::MvCta> ctas;
+    uint32_t tile0 = 0;
+    for (size_t s = 0; s < cta_n.size(); ++s) {
+        a.seg_cta0[s] = (uint32_t)ctas.size();
+        a.seg_tile0[s] = tile0;
+        tile0 += paired ? a.seg[0].rows / 16u : a.seg[s].rows / 16u;
+        for (uint32_t c = 0; c < cta_n[s]; ++c) {
+            d2::MvCta e{};
+            e.seg = (uint32_t)s;
+            e.j0 = (uint32_t)((uint64_t)tasks[s] * c / cta_n[s]);
+            e.j1 = (uint32_t)((uint64_t)tasks[s] * (c + 1) / cta_n[s]);
+            ctas.push_back(e);
+        }
+    }
+    a.seg_cta0[cta_n.size()] = (uint32_t)ctas.size();
+    p.grid = (uint32_t)ctas.size();
+    if (tile0 > h->g2.tctr_n) return fail(h, ATLAS_EINVAL, "mv: tile counter buffer too small");
+    // ring plan
+    uint32_t bb = 0;
+    for (uint32_t s = 0; s < a.n_seg; ++s) bb = std::max(bb, block_bytes(a.seg[s].type));
+    // A warp runs at most (nslot + 1) * st tasks ahead of the slowest warp,
+    // so tslots > (nslot + 1) * st / TP + 1 open-tile slots never collide.
+    auto tslots_of = [&](uint32_t nslot, uint32_t st) { return (nslot + 1u) * st / TP + 2u; };
+    bool ok = false;
+    for (uint32_t budget : {kHalfSmBytes, 227u * 1024u}) {
+        for (uint32_t st : {8u, 4u, 2u, 1u}) {
+            const uint32_t npmax = std::min(st, (st - 1u) / a.nb + 2u);
+            if (npmax > (uint32_t)d2::kMvMaxPortions) continue;
+            const uint32_t slot = (16u * (st * bb + npmax * 48u) + 127u) & ~127u;
+            uint32_t nslot = d2::kMvMaxSlots;
+            while (nslot && (tslots_of(nslot, st) > (uint32_t)d2::kMvMaxTileSlots ||
+                             atlas_d2_mv_smem(cols, nslot, slot, tslots_of(nslot, st)) > budget))
+                --nslot;
+            if (nslot >= 3u || (st == 1u && nslot >= 2u)) {
+                a.st = st;
+                a.nslot = nslot;
+                a.slot_bytes = slot;
+                a.tslots = tslots_of(nslot, st);
+                ok = true;
+                break;
+            }
+        }
+        if (ok) break;
+    }
+    if (!ok) return fail(h, ATLAS_EINVAL, "mv: no shared-memory plan for %u columns", cols);
+    a.smem_bytes = (uint32_t)atlas_d2_mv_smem(cols, a.nslot, a.slot_bytes, a.tslots);
+    d2::MvCta *dc = nullptr;
+    int rc = dalloc(h, &dc, ctas.size() * sizeof(d2::MvCta));
+    if (rc) return rc;
+    CU(h, cudaMemcpy(dc, ctas.data(), ctas.size() * sizeof(d2::MvCta), cudaMemcpyHostToDevice));
+    a.cta = dc;
+    a.eps = h->desc.rms_eps;
+    a.bpart = h->g2.bpart;
+    a.tctr = h->g2.tctr;
+    a.pmax = h->pmax;
+    a.pidx = h->pidx;
+    a.status = h->g2.status;
+    a.pdl = 1u;
+    return ATLAS_OK;
+}
+
+// Capture one decode step as a CUDA graph of PDL-chained kernels.
+int build_graph2(AtlasCuda *h)
+{
+    const AtlasModelDesc &d = h->desc;
+    AtlasCuda::Graph2 &g = h->g2;
+    const uint32_t G = (uint32_t)h->sm_count, group = d.q_heads / d.kv_heads;
+    if (group > d2::kAttnMaxGroup) return fail(h, ATLAS_EINVAL, "graph decode: more than 8 query heads per KV head");
+    int rc = dalloc(h, &g.st, sizeof(d2::DecState));
+    if (rc) return rc;
+    CU(h, cudaMemset(g.st, 0, sizeof(d2::DecState)));
+    g.status = &g.st->status;
+    if ((rc = dalloc(h, &g.bpart, (size_t)G * 64u * sizeof(float)))) return rc;
+    g.tctr_n = std::max(d.vocab, std::max(d.ffn, d.q_dim + 2u * d.kv_dim)) / 16u + 64u;
+    if ((rc = dalloc(h, &g.tctr, (size_t)g.tctr_n * 4u))) return rc;
+    CU(h, cudaMemset(g.tctr, 0, (size_t)g.tctr_n * 4u));
+    g.splits = std::max(1u, std::min(G / d.kv_heads, 160u));
+    if ((rc = dalloc(h, &g.apart, (size_t)d.kv_heads * g.splits * group * d2::kRec * sizeof(float)))) return rc;
+    if ((rc = dalloc(h, &g.actr, (size_t)d.kv_heads * 4u))) return rc;
+    CU(h, cudaMemset(g.actr, 0, (size_t)d.kv_heads * 4u));
+
+    const AtlasCuda::W &w0 = h->layers[0];
+    MvPlan qkv, o, gu, dn, hd;
+    if ((rc = plan_mv(h, qkv, d.hidden, false,
+                      {mvseg(w0.q, w0.tq, d.q_dim, d.hidden, w0.bq, h->q), mvseg(w0.k, w0.tk, d.kv_dim, d.hidden, w0.bk, h->k),
+                       mvseg(w0.v, w0.tv, d.kv_dim, d.hidden, w0.bv, h->v)},
+                      d2::MV_STORE)))
+        return rc;
+    if ((rc = plan_mv(h, o, d.q_dim, false, {mvseg(w0.o, w0.to, d.hidden, d.q_dim, nullptr, h->x)}, d2::MV_RESID)))
+        return rc;
+    if ((rc = plan_mv(h, gu, d.hidden, true,
+                      {mvseg(w0.gate, w0.tg, d.ffn, d.hidden, nullptr, h->ffn), mvseg(w0.up, w0.tu, d.ffn, d.hidden, nullptr, nullptr)},
+                      d2::MV_SWIGLU)))
+        return rc;
+    if ((rc = plan_mv(h, dn, d.ffn, false, {mvseg(w0.down, w0.td, d.hidden, d.ffn, nullptr, h->x)}, d2::MV_RESID)))
+        return rc;
+    if ((rc = plan_mv(h, hd, d.hidden, false, {mvseg(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)},
+                      d2::MV_LOGITS)))
+        return rc;
+    qkv.a.x = h->x;
+    o.a.x = h->att;
+    gu.a.x = h->x;
+    dn.a.x = h->ffn;
+    hd.a.x = h->x;
+    hd.a.norm_w = h->out_norm;
+    size_t mv_smem = 0;
+    for (const MvPlan *p : {&qkv, &o, &gu, &dn, &hd}) mv_smem = std::max<size_t>(mv_smem, p->a.smem_bytes);
+    CU(h, atlas_d2_setup(mv_smem, atlas_d2_attn_smem(g.splits)));
+
+    d2::AttnArgs at{};
+    at.q = h->q;
+    at.k = h->k;
+    at.v = h->v;
+    at.att = h->att;
+    at.part = g.apart;
+    at.ctr = g.actr;
+    at.rope = h->rope;
+    at.st = g.st;
+    at.q_heads = d.q_heads;
+    at.kv_heads = d.kv_heads;
+    at.max_context = d.max_context;
+    at.splits = g.splits;
+    at.kv_fp16 = d.kv_fp16 ? 1u : 0u;
+
+    const uint64_t embd_row = (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
+    CU(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    uint32_t kernels = 0;
+    cudaError_t e = atlas_d2_launch_embed(h->embd, embd_row, h->t_embd, d.hidden, d.vocab, h->x, g.st, h->stream);
+    ++kernels;
+    for (uint32_t l = 0; l < d.layers && e == cudaSuccess; ++l) {
+        const AtlasCuda::W &w = h->layers[l];
+        d2::MvArgs a = qkv.a;
+        a.seg[0].w = w.q; a.seg[0].bias = w.bq;
+        a.seg[1].w = w.k; a.seg[1].bias = w.bk;
+        a.seg[2].w = w.v; a.seg[2].bias = w.bv;
+        a.norm_w = w.attn_norm;
+        if ((e = atlas_d2_launch_mv(&a, qkv.grid, h->stream)) != cudaSuccess) break;
+        at.k_cache = w.kc;
+        at.v_cache = w.vc;
+        if ((e = atlas_d2_launch_attn(&at, d.kv_heads * g.splits, h->stream)) != cudaSuccess) break;
+        a = o.a;
+        a.seg[0].w = w.o;
+        if ((e = atlas_d2_launch_mv(&a, o.grid, h->stream)) != cudaSuccess) break;
+        a = gu.a;
+        a.seg[0].w = w.gate;
+        a.seg[1].w = w.up;
+        a.norm_w = w.ffn_norm;
+        if ((e = atlas_d2_launch_mv(&a, gu.grid, h->stream)) != cudaSuccess) break;
+        a = dn.a;
+        a.seg[0].w = w.down;
+        if ((e = atlas_d2_launch_mv(&a, dn.grid, h->stream)) != cudaSuccess) break;
+        kernels += 5;
+    }
+    if (e == cudaSuccess) { e = atlas_d2_launch_mv(&hd.a, hd.grid, h->stream); ++kernels; }
+    if (e == cudaSuccess) { e = atlas_d2_launch_argmax(h->pmax, h->pidx, hd.grid, g.st, h->stream); ++kernels; }
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return fail(h, ATLAS_ECUDA, "graph capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    g.graph = graph;
+    CU(h, cudaGraphInstantiate(&g.exec, graph, 0));
+    g.kernels = kernels;
+    g.on = true;
+    return ATLAS_OK;
+}
+
+// `steps` replays of the step graph from (token, pos); out_ids_dev receives
+// the picks when set (advance mode), else one step's pick is returned.
+int run_graph2(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
+               float *last_logit)
+{
+    AtlasCuda::Graph2 &g = h->g2;
+    d2::DecState init{};
+    init.pos = pos;
+    init.token = token;
+    init.max_steps = out_ids_dev ? steps : 0u;
+    init.advance = 1u;
+    init.out_ids = out_ids_dev;
+    CU(h, cudaMemcpyAsync(g.st, &init, sizeof(init), cudaMemcpyHostToDevice, h->stream));
+    CU(h, cudaEventRecord(h->ev0, h->stream));
+    for (uint32_t i = 0; i < steps; ++i) CU(h, cudaGraphLaunch(g.exec, h->stream));
+    CU(h, cudaEventRecord(h->ev1, h->stream));
+    h->launches += (uint64_t)steps * g.kernels;
+    d2::DecState out{};
+    CU(h, cudaMemcpyAsync(&out, g.st, sizeof(out), cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->last_ms = ms;
+    h->total_ms += ms;
+    if (out.status != kStatusOk) {
+        const int rc = status_to_code(h, out.status);
+        // clear what a failed step may have left behind
+        const AtlasModelDesc &d = h->desc;
+        cudaMemsetAsync(g.tctr, 0, (size_t)g.tctr_n * 4u, h->stream);
+        cudaMemsetAsync(g.actr, 0, (size_t)d.kv_heads * 4u, h->stream);
+        cudaMemsetAsync(g.st, 0, sizeof(d2::DecState), h->stream);
+        cudaStreamSynchronize(h->stream);
+        return rc;
+    }
+    if (last_token) *last_token = out.next_token;
+    if (last_logit) *last_logit = out.next_logit;
+    return ATLAS_OK;
+}
+
 int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
                float *last_logit)
 {
+    if (h->g2.on) return run_graph2(h, token, pos, steps, out_ids_dev, last_token, last_logit);
     return run_program(h, h->decode, token, pos, steps, out_ids_dev, last_token, last_logit);
 }
 
@@ -799,6 +1098,8 @@ void atlas_cuda_destroy(AtlasCuda *h)
 {
     if (!h) return;
     if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->g2.exec) cudaGraphExecDestroy(h->g2.exec);
+    if (h->g2.graph) cudaGraphDestroy(h->g2.graph);
     for (void *p : h->allocs) cudaFree(p);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
@@ -901,6 +1202,11 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
             TRY(fail(h, ATLAS_ECUDA, "rope upload failed"));
     }
     TRY(build_decode_program(h));
+    {
+        // graph decode step unless the persistent decode kernel is asked for
+        const char *eng = getenv("ATLAS_DECODE_ENGINE");
+        if (!eng || strcmp(eng, "persistent") != 0) TRY(build_graph2(h));
+    }
     TRY(alloc_prefill(h));
     if (cudaDeviceSynchronize() != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "device sync failed"));
 #undef TRY
