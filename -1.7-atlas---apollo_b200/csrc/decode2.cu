@@ -12,9 +12,9 @@
 // activations, so HBM keeps streaming across kernel boundaries.
 //
 // mv kernel (dequant-GEMV, one CTA per SM): a producer warp copies the raw
-// Q4_K / Q6_K rows of the CTA's task range into a shared-memory ring with 1-D
-// bulk copies, one copy per row piece, rows placed at an odd multiple of 16
-// bytes apart so that the 8 row groups of a warp hit distinct banks. Eight
+// Q4_K / Q6_K rows of the CTA's task range into a shared-memory ring with
+// 1-D bulk copies of row pairs, placed an odd multiple of 16 bytes apart so
+// that the 8 row groups of a warp hit distinct banks. Eight
 // consumer warps stage the input (rms_norm'ed, split into fp16 hi/lo), then run
 // the tensor-core tiles of tc_tiles.cuh on their tasks (16 rows x 256
 // elements each) and reduce the tiles' row sums in a fixed order: inside the
@@ -48,7 +48,8 @@ __host__ __device__ constexpr uint32_t odd16(uint32_t v)
 }
 
 // Dynamic shared memory of an mv CTA:
-//   MvHdr | tile area: tcnt[tslots], tpart[tslots][2][kMvWarps][16] | x area | ring
+//   MvHdr | tile area: tcnt[tslots], tpart[tslots][2][kMvWarps][kMvRows]
+//         | slot descriptors | x area | ring
 struct __align__(16) MvHdr {
     uint64_t full[kMvMaxSlots];
     uint64_t empty[kMvMaxSlots];
@@ -58,64 +59,74 @@ struct __align__(16) MvHdr {
     uint32_t aidx[kMvWarps];
     uint32_t *tcnt;    // arrivals per open tile slot
     float *tpart;      // per-warp row sums of open tiles
+    uint4 *desc;       // [nslot][8] task descriptors
+    uint8_t *lead;     // [nslot][kMvMaxPortions][16] copy misalignments
 };
 
 __host__ __device__ constexpr uint32_t mv_hdr_bytes() { return align128((uint32_t)sizeof(MvHdr)); }
 __host__ __device__ constexpr uint32_t mv_tcnt_bytes(uint32_t tslots) { return (tslots * 4u + 15u) & ~15u; }
 __host__ __device__ constexpr uint32_t mv_tile_bytes(uint32_t tslots)
 {
-    return align128(mv_tcnt_bytes(tslots) + tslots * 2u * kMvWarps * 16u * 4u);
+    return align128(mv_tcnt_bytes(tslots) + tslots * 2u * kMvWarps * kMvRows * 4u);
+}
+// Per ring slot: one descriptor per task - ring offset of the task's block in
+// the run's first copy, copy stride | row stride << 16, tile, segment | run
+// << 4 | log2 copies << 8 | block << 16 - and the copies' misalignments.
+__host__ __device__ constexpr uint32_t mv_desc_bytes(uint32_t nslot)
+{
+    return align128(nslot * (8u * 16u + kMvMaxPortions * 16u));
 }
 __host__ __device__ constexpr uint32_t mv_x_bytes(uint32_t cols) { return align128(cols * 4u + cols / 16u * 4u); }
 
 __device__ __forceinline__ float *tpart_at(const MvHdr *h, uint32_t ts, uint32_t s, uint32_t w)
 {
-    return h->tpart + ((ts * 2u + s) * kMvWarps + w) * 16u;
+    return h->tpart + ((ts * 2u + s) * kMvWarps + w) * kMvRows;
 }
 
-// One (tile, segment) run of block columns inside a ring slot; its 16 rows sit
-// at off + i * stride (+ the row piece's misalignment `lead`).
+// One (tile, segment) run of n block columns inside a ring slot. A run of
+// whole rows (n == nb) is copied as C = seg.copies bulk copies of R = 16 / C
+// adjacent rows (the rows are adjacent in memory), a partial run row by row
+// (C = 16, R = 1). Copy q sits at off + q * cstride, cstride an odd multiple
+// of 16 bytes, its rows rstride (= row_bytes) apart after the copy's
+// misalignment lead_q. MMA row m of the tile is row (m % C) * R + m / C: the
+// 8 rows an MMA row group reads come from different copies (distinct banks),
+// or - where the host saw that rows of one copy already fall in distinct
+// banks - from one copy.
 struct Portion {
-    uint32_t t, s, b0, n, off, stride, j;   // j: first task of the run
+    uint32_t t, s, b0, n, off, cstride, rstride, c, j;   // c = log2 C, j: first task of the run
 };
 
 __device__ __forceinline__ uint32_t mv_bb(uint32_t type) { return type == 12u ? 144u : 210u; }
 
-// Runs of the slot holding tasks [js, je) of segment `segi` (or of the pair).
-__device__ __forceinline__ uint32_t slot_portions(const MvArgs &a, uint32_t segi, uint32_t js, uint32_t je,
-                                                  Portion (&pr)[kMvMaxPortions])
-{
-    const uint32_t P = a.paired ? 2u : 1u, TP = a.nb * P;
-    uint32_t j = js, off = 0, np = 0;
-#pragma unroll
-    for (int q = 0; q < kMvMaxPortions; ++q) {
-        if (j >= je) break;
-        const uint32_t t = j / TP, r = j % TP;
-        const uint32_t s = a.paired ? r / a.nb : segi;
-        const uint32_t b0 = r % a.nb, n = min(a.nb - b0, je - j);
-        const uint32_t stride = odd16(n * mv_bb(a.seg[s].type) + 15u);
-        pr[q] = Portion{t, s, b0, n, off, stride, j};
-        off += 16u * stride;
-        j += n;
-        ++np;
-    }
-    return np;
-}
+__host__ __device__ constexpr uint32_t ceil16(uint32_t v) { return (v + 15u) & ~15u; }
 
-// Global address of row i of a run (the bulk copy starts at it rounded down to 16 bytes).
-__device__ __forceinline__ const uint8_t *run_row(const MvArgs &a, const Portion &p, uint32_t i)
+__device__ __forceinline__ uint32_t log2u(uint32_t v) { return 31u - (uint32_t)__clz(v); }
+
+__device__ __forceinline__ Portion pick(const Portion (&pr)[kMvMaxPortions], uint32_t p)
 {
-    const MvSeg &sg = a.seg[p.s];
-    return sg.w + (uint64_t)(16u * p.t + i) * sg.row_bytes + (uint64_t)p.b0 * mv_bb(sg.type);
+    Portion q = pr[0];
+#pragma unroll
+    for (int v = 1; v < kMvMaxPortions; ++v)
+        if ((uint32_t)v == p) q = pr[v];
+    return q;
 }
 
 // ----------------------------------------------------------- producer ----
 
+// One pass per ring slot: wait until the slot is free, lay out its runs from
+// a (tile, segment, block) cursor (no divisions), write the descriptors of its
+// tasks and the copies' misalignments, then every copying lane announces its
+// own bytes and issues its bulk copy; lane 0's arrival publishes the
+// descriptors. A bulk copy costs tens of nanoseconds of the SM's copy engine
+// whatever its size, so whole-row runs go in few large copies.
 __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCta &c, volatile uint32_t *err)
 {
     const uint32_t lane = threadIdx.x & 31u;
     const uint64_t policy = policy_evict_first();
-    const uint32_t nslots = (c.j1 - c.j0 + a.st - 1u) / a.st;
+    const uint32_t P = a.paired ? 2u : 1u, TP = a.nb * P;
+    const uint32_t L = c.j1 - c.j0, nslots = (L + a.st - 1u) / a.st;
+    uint32_t ct = c.j0 / TP, cs = a.paired ? 0u : c.seg, cb = 0u;   // ranges start on a tile
+    uint32_t j = 0;                                                 // task position in the range
     for (uint32_t k = 0; k < nslots; ++k) {
         const uint32_t ri = k % a.nslot;
         if (k >= a.nslot) {
@@ -124,36 +135,65 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
         }
-        const uint32_t js = c.j0 + k * a.st, je = min(c.j1, js + a.st);
+        const uint32_t js = j, je = min(L, js + a.st);
         Portion pr[kMvMaxPortions];
-        const uint32_t np = slot_portions(a, c.seg, js, je, pr);
-        uint8_t *slot = ring + (size_t)ri * a.slot_bytes;
-        // lane L copies rows L and L + 32 of the slot's runs (16 rows per run)
-        const uint8_t *src[2];
-        uint8_t *dst[2];
-        uint32_t nbytes[2] = {0u, 0u};
+        uint32_t np = 0, off = 0;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const uint32_t idx = lane + 32u * (uint32_t)u, p = idx / 16u, i = idx % 16u;
-            if (p >= np) continue;
-            Portion q = pr[0];
+        for (int q = 0; q < kMvMaxPortions; ++q) {
+            if (j >= je) break;
+            const MvSeg &sg = a.seg[cs];
+            const uint32_t n = min(a.nb - cb, je - j);
+            const bool whole = n == a.nb;
+            const uint32_t C = whole ? sg.copies : 16u;
+            const uint32_t rstride = (uint32_t)sg.row_bytes;
+            const uint32_t cstride = whole ? odd16((16u / C) * rstride + 15u) : odd16(n * mv_bb(sg.type) + 15u);
+            pr[q] = Portion{ct, cs, cb, n, off, cstride, rstride, log2u(C), j};
+            off += C * cstride;
+            j += n;
+            ++np;
+            cb += n;
+            if (cb == a.nb) {
+                cb = 0u;
+                if (a.paired && cs == 0u) {
+                    cs = 1u;
+                } else {
+                    if (a.paired) cs = 0u;
+                    ++ct;
+                }
+            }
+        }
+        uint8_t *slot = ring + (size_t)ri * a.slot_bytes;
+        if (lane < je - js) {
+            const uint32_t jt = js + lane;
+            uint32_t p = 0;
 #pragma unroll
             for (int v = 1; v < kMvMaxPortions; ++v)
-                if ((uint32_t)v == p) q = pr[v];
-            const uint8_t *g = run_row(a, q, i);
-            const uint32_t lead = (uint32_t)(reinterpret_cast<uintptr_t>(g) & 15u);
-            src[u] = g - lead;
-            dst[u] = slot + q.off + i * q.stride;
-            nbytes[u] = (lead + q.n * mv_bb(a.seg[q.s].type) + 15u) & ~15u;
+                if ((uint32_t)v < np && jt >= pr[v].j) p = (uint32_t)v;
+            const Portion q = pick(pr, p);
+            const uint32_t b = q.b0 + (jt - q.j);
+            const uint32_t base = ri * a.slot_bytes + q.off + (b - q.b0) * mv_bb(a.seg[q.s].type);
+            h->desc[ri * 8u + lane] =
+                make_uint4(base, q.cstride | (q.rstride << 16), q.t, q.s | (p << 4) | (q.c << 8) | (b << 16));
         }
-        uint32_t total = nbytes[0] + nbytes[1];
+        // lane L: copy L % 16 of runs L / 16 and L / 16 + 2
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-        if (lane == 0) mbar_arrive_expect_tx(&h->full[ri], total);
-        __syncwarp();
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-            if (nbytes[u]) bulk_g2s_hint(dst[u], src[u], nbytes[u], &h->full[ri], policy);
+        for (uint32_t u = 0; u < 2; ++u) {
+            const uint32_t p = lane / 16u + 2u * u, i = lane % 16u;
+            if (p >= np) continue;
+            const Portion q = pick(pr, p);
+            const uint32_t C = 1u << q.c, R = 16u / C;
+            if (i >= C) continue;
+            const MvSeg &sg = a.seg[q.s];
+            const uint8_t *g = sg.w + (uint64_t)((uint32_t)kMvRows * q.t + i * R) * sg.row_bytes +
+                               (uint64_t)q.b0 * mv_bb(sg.type);
+            const uint32_t lead = (uint32_t)(reinterpret_cast<uintptr_t>(g) & 15u);
+            const uint32_t nbytes = ceil16(lead + (C == 16u ? q.n * mv_bb(sg.type) : R * q.rstride));
+            h->lead[(ri * (uint32_t)kMvMaxPortions + p) * 16u + i] = (uint8_t)lead;
+            mbar_expect_tx(&h->full[ri], nbytes);
+            bulk_g2s_hint(slot + q.off + i * q.cstride, g - lead, nbytes, &h->full[ri], policy);
+        }
+        __syncwarp();   // descriptors and leads of all lanes before lane 0's release
+        if (lane == 0) mbar_arrive(&h->full[ri]);
     }
     // every issued copy lands before the CTA may exit
     if (lane == 0) {
@@ -170,29 +210,43 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
 // of two putting max|x| in [2^13, 2^14). The rms_norm factor is a scalar, so
 // it is applied to the row sums instead: W (x w inv) = inv * W (x w), with
 // the sum of squares in double as src/brain_runtime.c:1345-1360. Returns the
-// factor for the row sums: inv_rms / xscale.
+// factor for the row sums: inv_rms / xscale. Pass 1 keeps eight 16-byte loads
+// per thread in flight (x comes from L2); pass 2 converts one 4-element group
+// per thread and step, the 16-element sums reduced across 4 adjacent lanes.
 __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
 {
-    const uint32_t n = a.cols;
+    const uint32_t n4 = a.cols / 4u;
     const bool norm = a.norm_w != nullptr;
     float4 *xf = reinterpret_cast<float4 *>(xarea);
     float mx = 0.f;
     double ss = 0.0;
     constexpr uint32_t kStride = kMvWarps * 32;
-    for (uint32_t i0 = threadIdx.x; i0 < n / 4u; i0 += 4u * kStride) {
-        float4 v[4], w[4];
+    constexpr int kDepth = 8;
+    // the norm weights of the first round do not depend on the preceding
+    // kernel: load them before waiting for it
+    float4 w[kDepth];
+    if (norm) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kDepth; ++j) {
+            const uint32_t i = threadIdx.x + (uint32_t)j * kStride;
+            if (i < n4) w[j] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
+        }
+    }
+    if (a.pdl) pdl_wait();
+    for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += kDepth * kStride) {
+        float4 v[kDepth];
+#pragma unroll
+        for (int j = 0; j < kDepth; ++j) {
             const uint32_t i = i0 + (uint32_t)j * kStride;
-            if (i < n / 4u) {
+            if (i < n4) {
                 v[j] = __ldcg(reinterpret_cast<const float4 *>(a.x) + i);
-                if (norm) w[j] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
+                if (norm && i0 != threadIdx.x) w[j] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kDepth; ++j) {
             const uint32_t i = i0 + (uint32_t)j * kStride;
-            if (i >= n / 4u) continue;
+            if (i >= n4) continue;
             float4 x = v[j];
             if (norm) {
                 ss += (double)x.x * (double)x.x;
@@ -208,7 +262,7 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (norm) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     if (lane == 0) { h->fred[warp] = mx; h->dred[warp] = ss; }
@@ -220,31 +274,30 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
     // exponent capped at 126: rows of tiny values (a SwiGLU output of
     // all-negative gates) keep a finite scale and contribute ~0, as in fp32
     const float s = (m > 0.f && isfinite(m)) ? exp2f((float)min(13 - ilogbf(m), 126)) : 1.0f;
-    const float inv_rms = norm ? 1.0f / sqrtf((float)(t / (double)n) + a.eps) : 1.0f;
-    float *xs16 = reinterpret_cast<float *>(xarea + (size_t)n * 4u);
-    for (uint32_t u = threadIdx.x; u < n / 16u; u += kStride) {
+    const float inv_rms = norm ? 1.0f / sqrtf((float)(t / (double)a.cols) + a.eps) : 1.0f;
+    float *xs16 = reinterpret_cast<float *>(xarea + (size_t)a.cols * 4u);
+    // n4 is a multiple of 4 (cols % 256 == 0) and the stride of 256 keeps the
+    // four groups of a 16-element sum in lanes 4k..4k+3 of one warp
+    for (uint32_t i = threadIdx.x; i < n4; i += kStride) {
+        const float4 v = xf[i];
+        const float e[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+        __half hi[4], lo[4];
         float sum = 0.f;
-        uint4 pk[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float4 v = xf[4 * u + q];
-            const float e[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
-            __half hi[4], lo[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                hi[i] = __float2half_rn(e[i]);
-                lo[i] = __float2half_rn(e[i] - __half2float(hi[i]));
-                sum += e[i];
-            }
-            pk[q].x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
-            pk[q].y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
-            pk[q].z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
-            pk[q].w = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+            hi[q] = __float2half_rn(e[q]);
+            lo[q] = __float2half_rn(e[q] - __half2float(hi[q]));
+            sum += e[q];
         }
-        // in place: unit u's 64 bytes are only read by this thread
-#pragma unroll
-        for (int q = 0; q < 4; ++q) reinterpret_cast<uint4 *>(xarea)[4 * u + q] = pk[q];
-        xs16[u] = sum;
+        uint4 pk;
+        pk.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
+        pk.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
+        pk.z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
+        pk.w = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+        reinterpret_cast<uint4 *>(xarea)[i] = pk;   // in place: group i is only touched by this thread
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if ((lane & 3u) == 0u) xs16[i / 4u] = sum;
     }
     mv_sync();
     return inv_rms / s;
@@ -257,49 +310,56 @@ struct MvBest {
     uint32_t i;
 };
 
-// largest CTA of segment `segi` whose range starts at or before task j
-__device__ __forceinline__ uint32_t cta_of(const MvArgs &a, uint32_t segi, uint32_t j)
+// Epilogue of tile t: lane i < 16 holds row i (v0; paired: v0 = gate, v1 =
+// up); `pre` is the row's bias (store) or residual (residual add), loaded
+// when the warp started the tile.
+__device__ __forceinline__ void mv_finish(const MvArgs &a, uint32_t segi, uint32_t t, float v0, float v1, float pre,
+                                          uint32_t lane, MvBest &best)
 {
-    uint32_t lo = a.seg_cta0[segi], hi = a.seg_cta0[segi + 1] - 1u;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi + 1u) / 2u;
-        if (__ldg(&a.cta[mid].j0) <= j) lo = mid;
-        else hi = mid - 1u;
-    }
-    return lo;
-}
-
-// Epilogue of tile t. Lane i < 16 holds row i (paired: the gate sum; lane
-// 16 + i the up sum of the same row).
-__device__ __forceinline__ void mv_finish(const MvArgs &a, uint32_t segi, uint32_t t, float v, uint32_t lane,
-                                          MvBest &best)
-{
-    const uint32_t row = 16u * t + (lane & 15u);
+    const uint32_t row = (uint32_t)kMvRows * t + lane;
     if (a.epi == MV_SWIGLU) {
-        const float up = __shfl_down_sync(0xffffffffu, v, 16);
-        if (lane < 16u) a.seg[0].out[row] = (v / (1.0f + expf(-v))) * up;   // src/brain_runtime.c:1755-1758
+        a.seg[0].out[row] = (v0 / (1.0f + expf(-v0))) * v1;   // src/brain_runtime.c:1755-1758
         return;
     }
-    if (lane >= 16u) return;
     const MvSeg &sg = a.seg[segi];
     if (a.epi == MV_RESID) {
-        sg.out[row] = __ldcg(sg.out + row) + v;   // src/brain_runtime.c:1745, :1762
+        sg.out[row] = pre + v0;   // src/brain_runtime.c:1745, :1762
         return;
     }
-    const float r = sg.bias ? v + __ldg(sg.bias + row) : v;
+    const float r = sg.bias ? v0 + pre : v0;
     sg.out[row] = r;
     if (a.epi == MV_LOGITS && (r > best.v || (r == best.v && row < best.i))) { best.v = r; best.i = row; }
 }
 
-// The warp's row sums of tile t are complete. Publish them; the last of the
-// CTA's warps with tasks in the tile adds them up in warp order and finishes
-// the tile - or, for a tile shared with neighbouring CTAs, publishes the
-// CTA's sums and the last CTA to arrive adds those up in CTA order.
-__device__ void mv_flush(const MvArgs &a, MvHdr *h, const MvCta &c, uint32_t t, const float (&acc)[2][2],
-                         float out_scale, MvBest &best)
+// Epilogue operand of row lane of tile t (lanes < 16), read early.
+__device__ __forceinline__ float mv_pre(const MvArgs &a, uint32_t segi, uint32_t t, uint32_t lane)
+{
+    if (lane >= 16u) return 0.f;
+    const MvSeg &sg = a.seg[segi];
+    const uint32_t row = (uint32_t)kMvRows * t + lane;
+    if (a.epi == MV_RESID) return __ldcg(sg.out + row);
+    if (a.epi == MV_STORE && sg.bias) return __ldg(sg.bias + row);
+    return 0.f;
+}
+
+// Weight row (within the tile) of MMA row m when the run's rows come in
+// 1 << c copies: copy m % C, row m / C of the copy.
+__device__ __forceinline__ uint32_t mv_wrow(uint32_t m, uint32_t c)
+{
+    return (m & ((1u << c) - 1u)) * (16u >> c) + (m >> c);
+}
+
+// The warp's row sums of tile t are complete (acc[s][0]: MMA row g, acc[s][1]:
+// MMA row g + 8 of segment s, this lane's share; lc[s]: the copy layout of
+// segment s in this tile - one whole-row run, or partial runs only). Publish them; the last of
+// the CTA's warps with tasks in the tile adds them up in warp order and
+// finishes the tile.
+__device__ void mv_flush(const MvArgs &a, MvHdr *h, const MvCta &c, uint32_t t, const uint32_t (&lc)[2],
+                         const float (&acc)[2][2], float out_scale, float pre, MvBest &best)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, g = lane >> 2;
-    const uint32_t P = a.paired ? 2u : 1u, TP = a.nb * P, ts = t % a.tslots;
+    const uint32_t P = a.paired ? 2u : 1u, TP = a.nb * P;
+    const uint32_t ts = (t - c.j0 / TP) % a.tslots;   // tiles are opened in order
 #pragma unroll
     for (uint32_t s = 0; s < 2; ++s) {
         if (s >= P) break;
@@ -310,12 +370,11 @@ __device__ void mv_flush(const MvArgs &a, MvHdr *h, const MvCta &c, uint32_t t, 
         v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
         if ((lane & 3u) == 0u) {
             float *tp = tpart_at(h, ts, s, warp);
-            tp[g] = v0;
-            tp[g + 8u] = v1;
+            tp[mv_wrow(g, lc[s])] = v0;
+            tp[mv_wrow(g + 8u, lc[s])] = v1;
         }
     }
-    const uint32_t a0 = max(c.j0, t * TP), a1 = min(c.j1, (t + 1u) * TP), n = a1 - a0;
-    const uint32_t expect = min(n, (uint32_t)kMvWarps);
+    const uint32_t expect = min(TP, (uint32_t)kMvWarps);
     __syncwarp();
     uint32_t last = 0;
     if (lane == 0) {
@@ -325,114 +384,193 @@ __device__ void mv_flush(const MvArgs &a, MvHdr *h, const MvCta &c, uint32_t t, 
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) return;
     __threadfence_block();
-    const uint32_t i = lane & 15u, s = lane >> 4;
-    float v = 0.f;
-    if (s < P) {
-        const uint32_t w0 = (a0 - c.j0) % kMvWarps;
+    const uint32_t i = lane & 15u;
+    float v[2] = {0.f, 0.f};
+    const uint32_t w0 = (t * TP - c.j0) % kMvWarps;
+#pragma unroll
+    for (uint32_t s = 0; s < 2; ++s) {
+        if (s >= P) break;
         const volatile float *tp = tpart_at(h, ts, s, 0) + i;
 #pragma unroll
         for (uint32_t w = 0; w < (uint32_t)kMvWarps; ++w)
-            if (n >= (uint32_t)kMvWarps || ((w + kMvWarps - w0) % kMvWarps) < n) v += tp[w * 16u];
-        v *= out_scale;
+            if (TP >= (uint32_t)kMvWarps || ((w + kMvWarps - w0) % kMvWarps) < TP) v[s] += tp[w * (uint32_t)kMvRows];
+        v[s] *= out_scale;
     }
     __syncwarp();
     if (lane == 0) h->tcnt[ts] = 0u;
-    if (t * TP >= c.j0 && (t + 1u) * TP <= c.j1) {
-        mv_finish(a, c.seg, t, v, lane, best);
-        return;
-    }
-    // tile shared with neighbouring CTAs
-    const uint32_t side = (t == c.j0 / TP) ? 0u : 1u;
-    if (s < P) a.bpart[((size_t)blockIdx.x * 2u + side) * 32u + s * 16u + i] = v;
-    __threadfence();
-    __syncwarp();
-    const uint32_t cf = cta_of(a, c.seg, t * TP), cl = cta_of(a, c.seg, (t + 1u) * TP - 1u);
-    uint32_t *ctr = a.tctr + a.seg_tile0[c.seg] + t;
-    uint32_t done = 0;
-    if (lane == 0) done = (atom_acq_rel_add(ctr, 1u) == cl - cf) ? 1u : 0u;
-    done = __shfl_sync(0xffffffffu, done, 0);
-    if (!done) return;
-    __syncwarp();
-    __threadfence();
-    float tot = 0.f;
-    if (s < P)
-        for (uint32_t cc = cf; cc <= cl; ++cc) {
-            const uint32_t sd = (t == __ldg(&a.cta[cc].j0) / TP) ? 0u : 1u;
-            tot += __ldcg(a.bpart + ((size_t)cc * 2u + sd) * 32u + s * 16u + i);
-        }
-    if (lane == 0) *ctr = 0u;
-    mv_finish(a, c.seg, t, tot, lane, best);
+    if (lane < 16u) mv_finish(a, c.seg, t, v[0], v[1], pre, lane, best);
 }
 
-// Consumer warp: tasks c.j0 + warp + 8m, each one 16-row x 256-element tile
-// of the staged slot. Returns false after a failed wait (status recorded).
+__device__ __forceinline__ void ldmatrix_x4(const void *p, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_addr(p)));
+}
+
+// Address of MMA row m of a run's block: copy m % C at cstride, row m / C
+// of the copy at rstride (Q4_K rows are 16-byte aligned: no misalignment).
+__device__ __forceinline__ const uint8_t *q4_row(const uint8_t *blk, uint32_t m, uint32_t lc, uint32_t cstride,
+                                                 uint32_t rstride)
+{
+    return blk + (m & ((1u << lc) - 1u)) * cstride + (m >> lc) * rstride;
+}
+
+// One Q4_K task (16 rows x 256 elements) for lane (g, t): MMA rows g and
+// g + 8 (q4_row). The arithmetic of q4k_tiles (tc_tiles.cuh); the 128 quant
+// bytes of the rows come in with four ldmatrix.x4 (a matrix = 8 rows x 16
+// bytes), which hand lane (g, t) word t of each 16-byte chunk of its rows:
+// exactly the A-fragment word.
+__device__ __forceinline__ void q4k_task(const uint8_t *blk, uint32_t lc, uint32_t cstride, uint32_t rstride,
+                                         const uint8_t *xb, const float *xs, uint32_t lane, float &o0, float &o1)
+{
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    uint32_t W[8][2];
+    {
+        // lane i addresses row i & 7 of matrix i >> 3 = (row half, chunk pair)
+        const uint32_t m = lane >> 3;
+        const uint8_t *rb = q4_row(blk, (lane & 7u) + 8u * (m & 1u), lc, cstride, rstride) + 16u + 16u * (m >> 1);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            ldmatrix_x4(rb + 32u * (uint32_t)q, W[2 * q][0], W[2 * q][1], W[2 * q + 1][0], W[2 * q + 1][1]);
+    }
+    float dsc[2][2], dmn[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint4 hd = *reinterpret_cast<const uint4 *>(q4_row(blk, g + 8u * (uint32_t)r, lc, cstride, rstride));
+        const float d = h2f((uint16_t)(hd.x & 0xffffu)), dm = h2f((uint16_t)(hd.x >> 16));
+        const uint32_t sh = 8u * t;
+        const uint32_t y = (hd.y >> sh) & 255u, z = (hd.z >> sh) & 255u, w = (hd.w >> sh) & 255u;
+        dsc[r][0] = d * (float)(y & 63u);                        // sub-block j = t
+        dmn[r][0] = dm * (float)(z & 63u);
+        dsc[r][1] = d * (float)((w & 15u) | ((y >> 6) << 4));    // j = t + 4
+        dmn[r][1] = dm * (float)((w >> 4) | ((z >> 6) << 4));
+    }
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t podd = (g & 1u) * 8u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        float dlo[4], dhi[4];
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp) {
+            const uint32_t w0 = W[2 * c + hp][0], w1 = W[2 * c + hp][1];
+            const uint32_t l0 = w0 & 0x0f0f0f0fu, h0 = (w0 >> 4) & 0x0f0f0f0fu;
+            const uint32_t l1 = w1 & 0x0f0f0f0fu, h1 = (w1 >> 4) & 0x0f0f0f0fu;
+            const uint2 blo = *reinterpret_cast<const uint2 *>(xb + (16u * c + 4u * hp + t) * 16u + podd);
+            const uint2 bhi = *reinterpret_cast<const uint2 *>(xb + (16u * c + 8u + 4u * hp + t) * 16u + podd);
+            if (hp == 0) {
+                mma16816(dlo, sub2(l0, 0x4140), sub2(l1, 0x4140), sub2(l0, 0x4342), sub2(l1, 0x4342), blo, zero);
+                mma16816(dhi, sub2(h0, 0x4140), sub2(h1, 0x4140), sub2(h0, 0x4342), sub2(h1, 0x4342), bhi, zero);
+            } else {
+                const float clo[4] = {dlo[0], dlo[1], dlo[2], dlo[3]};
+                const float chi[4] = {dhi[0], dhi[1], dhi[2], dhi[3]};
+                mma16816(dlo, sub2(l0, 0x4140), sub2(l1, 0x4140), sub2(l0, 0x4342), sub2(l1, 0x4342), blo, clo);
+                mma16816(dhi, sub2(h0, 0x4140), sub2(h1, 0x4140), sub2(h0, 0x4342), sub2(h1, 0x4342), bhi, chi);
+            }
+        }
+        // this lane's sub-block in chunk c, if any: j = 2c + (t & 1) with (c & 1) == (t >> 1)
+        if ((uint32_t)(c & 1) == (t >> 1)) {
+            const int slot = c >> 1, j = 2 * c + (int)(t & 1u);
+            const float *D = (t & 1u) ? dhi : dlo;
+            const float sx = xs[2 * j] + xs[2 * j + 1];
+            o0 += dsc[0][slot] * ((D[0] + D[1]) * kTwo24) - dmn[0][slot] * sx;
+            o1 += dsc[1][slot] * ((D[2] + D[3]) * kTwo24) - dmn[1][slot] * sx;
+        }
+    }
+}
+
+// Consumer warp w: task u = w % st of every (8 / st)-th slot starting at
+// slot w / st - i.e. positions w + 8m of the CTA's task order; the
+// producer's descriptor gives the task's tile, block and place in the ring.
+// Returns false after a failed wait (status recorded).
 __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uint8_t *ring, const MvCta &c,
                             volatile uint32_t *err, MvBest &best)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const int g = (int)(lane >> 2), t4 = (int)(lane & 3u);
-    if (a.pdl) pdl_wait();
-    const float out_scale = mv_stage_x(a, h, xarea);
+    const float out_scale = mv_stage_x(a, h, xarea);   // waits for the preceding kernel
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
+    const uint32_t step = kMvWarps / a.st, u = warp % a.st;
+    uint32_t ri = warp / a.st, ph = 0;
+    while (ri >= a.nslot) { ri -= a.nslot; ph ^= 1u; }
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    uint32_t cur = 0xffffffffu;
-    for (uint32_t j = c.j0 + warp; j < c.j1; j += kMvWarps) {
-        const uint32_t k = (j - c.j0) / a.st, ri = k % a.nslot;
+    uint32_t cur = 0xffffffffu, cur_lc[2] = {0u, 0u};
+    float pre = 0.f;
+    for (uint32_t i = warp; i < c.j1 - c.j0; i += kMvWarps) {   // task positions w + 8m
         uint32_t ok = 1u;
-        if (lane == 0) ok = mbar_wait(&h->full[ri], (k / a.nslot) & 1u, err) ? 1u : 0u;
+        if (lane == 0) ok = mbar_wait(&h->full[ri], ph, err) ? 1u : 0u;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) return false;
-        const uint32_t js = c.j0 + k * a.st, je = min(c.j1, js + a.st);
-        Portion pr[kMvMaxPortions];
-        const uint32_t np = slot_portions(a, c.seg, js, je, pr);
-        Portion q = pr[0];
-#pragma unroll
-        for (int u = 1; u < kMvMaxPortions; ++u)
-            if ((uint32_t)u < np && j >= pr[u].j) q = pr[u];
-        const uint32_t b = q.b0 + (j - q.j);
-        if (q.t != cur) {
-            if (cur != 0xffffffffu) mv_flush(a, h, c, cur, acc, out_scale, best);
-            cur = q.t;
+        const uint4 dsc = h->desc[ri * 8u + u];
+        const uint32_t t = dsc.z, s = dsc.w & 15u, run = (dsc.w >> 4) & 15u, lc = (dsc.w >> 8) & 15u, b = dsc.w >> 16;
+        const uint32_t cstride = dsc.y & 0xffffu, rstride = dsc.y >> 16;
+        if (t != cur) {
+            if (cur != 0xffffffffu) mv_flush(a, h, c, cur, cur_lc, acc, out_scale, pre, best);
+            cur = t;
             acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+            pre = mv_pre(a, c.seg, t, lane);
         }
-        const MvSeg &sg = a.seg[q.s];
-        const uint32_t bb = mv_bb(sg.type);
-        const uint8_t *slot = ring + (size_t)ri * a.slot_bytes + q.off + (b - q.b0) * bb;
-        const uint32_t l0 = (uint32_t)(reinterpret_cast<uintptr_t>(run_row(a, q, (uint32_t)g)) & 15u);
-        const uint32_t l1 = (uint32_t)(reinterpret_cast<uintptr_t>(run_row(a, q, (uint32_t)g + 8u)) & 15u);
-        const uint8_t *r0[1] = {slot + (uint32_t)g * q.stride + l0};
-        const uint8_t *r1[1] = {slot + ((uint32_t)g + 8u) * q.stride + l1};
-        const uint8_t *xb[1] = {xarea + (size_t)b * 1024u};
-        const float *xs[1] = {xs16 + (size_t)b * 16u};
-        float o0[1] = {0.f}, o1[1] = {0.f};
-        if (sg.type == 12u) q4k_tiles<1, true>(r0, r1, xb, xs, g, t4, o0, o1);
-        else q6k_tiles<1, true>(r0, r1, xb, xs, g, t4, o0, o1);
+        // a segment of a tile comes as one whole run or as partial runs only
+        if (a.paired && (s & 1u)) cur_lc[1] = lc;
+        else cur_lc[0] = lc;
+        const uint8_t *blk = ring + dsc.x;
+        const uint8_t *xb = xarea + (size_t)b * 1024u;
+        const float *xs = xs16 + (size_t)b * 16u;
+        float o0 = 0.f, o1 = 0.f;
+        if (a.seg[s].type == 12u) {
+            q4k_task(blk, lc, cstride, rstride, xb, xs, lane, o0, o1);
+        } else {
+            const uint8_t *ld = h->lead + (ri * (uint32_t)kMvMaxPortions + run) * 16u;
+            const uint32_t m0 = (uint32_t)g, m1 = (uint32_t)g + 8u, cm = (1u << lc) - 1u;
+            const uint8_t *r0[1] = {blk + (m0 & cm) * cstride + ld[m0 & cm] + (m0 >> lc) * rstride};
+            const uint8_t *r1[1] = {blk + (m1 & cm) * cstride + ld[m1 & cm] + (m1 >> lc) * rstride};
+            const uint8_t *xbs[1] = {xb};
+            const float *xss[1] = {xs};
+            float p0[1] = {0.f}, p1[1] = {0.f};
+            q6k_tiles<1, true>(r0, r1, xbs, xss, g, t4, p0, p1);
+            o0 = p0[0];
+            o1 = p1[0];
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&h->empty[ri]);
-        if (a.paired && (q.s & 1u)) {
-            acc[1][0] += o0[0];
-            acc[1][1] += o1[0];
+        if (a.paired && (s & 1u)) {
+            acc[1][0] += o0;
+            acc[1][1] += o1;
         } else {
-            acc[0][0] += o0[0];
-            acc[0][1] += o1[0];
+            acc[0][0] += o0;
+            acc[0][1] += o1;
+        }
+        ri += step;
+        while (ri >= a.nslot) {
+            ri -= a.nslot;
+            ph ^= 1u;
         }
     }
-    if (cur != 0xffffffffu) mv_flush(a, h, c, cur, acc, out_scale, best);
+    if (cur != 0xffffffffu) mv_flush(a, h, c, cur, cur_lc, acc, out_scale, pre, best);
     return true;
 }
 
-__global__ void __launch_bounds__(kMvThreads, 2) mv_kernel(const __grid_constant__ MvArgs a)
+__global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     MvHdr *h = reinterpret_cast<MvHdr *>(smem);
     uint8_t *tiles = smem + mv_hdr_bytes();
-    uint8_t *xarea = tiles + mv_tile_bytes(a.tslots);
+    uint8_t *descs = tiles + mv_tile_bytes(a.tslots);
+    uint8_t *xarea = descs + mv_desc_bytes(a.nslot);
     uint8_t *ring = xarea + mv_x_bytes(a.cols);
     const MvCta c = a.cta[blockIdx.x];
     volatile uint32_t *err = a.status;
+    // a consumer waits for a slot kMvWarps / st slots after its previous one:
+    // with fewer ring entries its parity wait would alias an older phase
+    if (a.st == 0u || a.nslot > (uint32_t)kMvMaxSlots || a.nslot * a.st < (uint32_t)kMvWarps) {
+        if (threadIdx.x == 0) atomicCAS(a.status, kStatusOk, kStatusBadArgument);
+        return;
+    }
     if (threadIdx.x == 0) {
         h->tcnt = reinterpret_cast<uint32_t *>(tiles);
         h->tpart = reinterpret_cast<float *>(tiles + mv_tcnt_bytes(a.tslots));
+        h->desc = reinterpret_cast<uint4 *>(descs);
+        h->lead = descs + a.nslot * 8u * 16u;
         for (uint32_t i = 0; i < a.nslot; ++i) {
             mbar_init(&h->full[i], 1u);
             mbar_init(&h->empty[i], a.st);
@@ -759,7 +897,8 @@ cudaError_t launch_ex(const void *fn, void **args, dim3 grid, dim3 block, size_t
 
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots)
 {
-    return (size_t)mv_hdr_bytes() + mv_tile_bytes(tslots) + mv_x_bytes(cols) + (size_t)nslot * slot_bytes;
+    return (size_t)mv_hdr_bytes() + mv_tile_bytes(tslots) + mv_desc_bytes(nslot) + mv_x_bytes(cols) +
+           (size_t)nslot * slot_bytes;
 }
 
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits)

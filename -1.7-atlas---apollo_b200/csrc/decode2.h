@@ -33,10 +33,10 @@ struct DecState {
 // Work is counted in tasks: one task = 16 rows x one 256-element block column.
 // Task j of a segment covers tile t = j / nb (rows 16t..16t+15), block j % nb;
 // a paired (SwiGLU) kernel interleaves the gate and up segments per tile:
-// t = j / (2 nb), segment (j / nb) & 1. Every CTA owns a contiguous task range
-// of one segment (or of the pair); CTA-interior tiles are finished in shared
-// memory, tiles shared by neighbouring CTAs through `bpart` and a per-tile
-// arrival counter.
+// t = j / (2 nb), segment (j / nb) & 1. Every CTA owns a contiguous range of
+// whole tiles of one segment (or of the pair), so every tile is finished
+// inside one CTA, in shared memory.
+constexpr int kMvRows = 16;                       // rows per tile (one MMA row tile)
 constexpr int kMvWarps = 8;                       // consumer warps; warp w takes tasks j0 + w + 8m
 constexpr int kMvThreads = (kMvWarps + 1) * 32;   // + one producer warp
 constexpr int kMvMaxSlots = 8;
@@ -49,14 +49,16 @@ struct MvSeg {
     const uint8_t *w;      // row 0 of the raw GGUF tensor
     uint64_t row_bytes;
     uint32_t type;         // 12 = Q4_K, 14 = Q6_K
-    uint32_t rows;         // multiple of 16
+    uint32_t rows;         // multiple of kMvRows
     const float *bias;     // optional (MV_STORE)
     float *out;
+    uint32_t copies;       // bulk copies per whole-row run of 16 rows: 1, 2, 4 or 8
+    uint32_t pad_;
 };
 
 struct MvCta {
     uint32_t seg;          // segment (0 when paired)
-    uint32_t j0, j1;       // task range
+    uint32_t j0, j1;       // task range (whole tiles)
     uint32_t pad_;
 };
 
@@ -69,14 +71,10 @@ struct MvArgs {
     uint32_t slot_bytes;
     uint32_t tslots;       // open-tile slots: > (nslot + 1) * st / tasks per tile + 1
     uint32_t smem_bytes;   // dynamic shared memory of the launch
-    uint32_t seg_cta0[4];  // CTAs of segment s: [seg_cta0[s], seg_cta0[s + 1])
-    uint32_t seg_tile0[4]; // first entry of segment s in tctr
     const MvCta *cta;      // [gridDim.x]
     const float *x;        // input vector (cols floats)
     const float *norm_w;   // rms_norm weight, or null
     float eps;
-    float *bpart;          // [gridDim.x][2 sides][2 segments][16 rows]
-    uint32_t *tctr;        // per-tile arrival counters (zero between launches)
     float *pmax;           // MV_LOGITS: per-CTA maximum and its row
     uint32_t *pidx;
     uint32_t *status;

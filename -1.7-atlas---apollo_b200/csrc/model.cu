@@ -113,9 +113,9 @@ struct AtlasCuda {
     struct Graph2 {
         bool on = false;
         d2::DecState *st = nullptr;
-        float *bpart = nullptr, *apart = nullptr;
-        uint32_t *tctr = nullptr, *actr = nullptr, *status = nullptr;
-        uint32_t tctr_n = 0, splits = 0, kernels = 0;
+        float *apart = nullptr;
+        uint32_t *actr = nullptr, *status = nullptr;
+        uint32_t splits = 0, kernels = 0;
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
     } g2;
@@ -460,11 +460,34 @@ d2::MvSeg mvseg(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, c
     return s;
 }
 
+// Bulk copies per whole-row run of 16 rows (decode2.cu): the fewest of 1, 2,
+// 4, 8 whose layout puts the 8 rows of an MMA row group (rows m = 0..7 or
+// 8..15 -> copy m % C, row m / C of the copy) in shared-memory bank groups
+// that collide at most twice.
+uint32_t mv_copies(uint64_t row_bytes)
+{
+    auto odd16 = [](uint64_t v) { return 16u * (((v + 15u) / 16u) | 1u); };
+    for (uint32_t C : {1u, 2u, 4u, 8u}) {
+        const uint64_t R = 16u / C, cst = odd16(R * row_bytes + 15u);
+        uint32_t worst = 0;
+        for (uint32_t half = 0; half < 2; ++half) {
+            uint32_t hits[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (uint32_t m = 8 * half; m < 8 * half + 8; ++m) {
+                const uint64_t addr = (m % C) * cst + (m / C) * row_bytes;
+                worst = std::max(worst, ++hits[(addr / 16u) % 8u]);
+            }
+        }
+        if (worst <= 2u) return C;
+    }
+    return 8u;
+}
+
 // Task ranges and ring plan of one mv launch shape. Segments get CTAs in
 // proportion to their bytes; inside a segment (or the gate/up pair) every CTA
-// takes an equal share of the 16-row x 256-element tasks (+-1). The ring slot
-// holds `st` tasks; `st` and the ring depth are the largest that keep the
-// launch within half an SM's shared memory with at least 3 slots.
+// takes an equal share (+-1) of whole 16-row tiles, so no tile spans two CTAs.
+// The ring slot holds `st` tasks; `st` and the ring depth are the largest
+// that keep the launch within half an SM's shared memory with at least 3
+// slots.
 int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initializer_list<d2::MvSeg> segs, uint32_t epi)
 {
     d2::MvArgs &a = p.a;
@@ -475,27 +498,31 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     a.epi = epi;
     for (const d2::MvSeg &sg : segs) {
         if (a.n_seg == 3) return fail(h, ATLAS_EINVAL, "mv: too many segments");
-        if ((sg.type != 12u && sg.type != 14u) || sg.rows % 16u || !sg.rows)
+        if ((sg.type != 12u && sg.type != 14u) || sg.rows % (uint32_t)d2::kMvRows || !sg.rows)
             return fail(h, ATLAS_EINVAL, "mv: segment type %u rows %u unsupported", sg.type, sg.rows);
-        a.seg[a.n_seg++] = sg;
+        if (sg.type == 12u && (reinterpret_cast<uintptr_t>(sg.w) & 15u))
+            return fail(h, ATLAS_EINVAL, "mv: Q4_K tensor not 16-byte aligned");
+        a.seg[a.n_seg] = sg;
+        a.seg[a.n_seg].copies = mv_copies(sg.row_bytes);
+        ++a.n_seg;
     }
     if (!cols || cols % 256u || (paired && (a.n_seg != 2 || a.seg[0].rows != a.seg[1].rows)))
         return fail(h, ATLAS_EINVAL, "mv: bad shape");
     const uint32_t G = (uint32_t)h->sm_count;
     const uint32_t P = paired ? 2u : 1u, TP = a.nb * P;
-    std::vector<uint32_t> cta_n, tasks;
+    std::vector<uint32_t> cta_n, tiles;
     if (paired) {
-        tasks.push_back(a.seg[0].rows / 16u * TP);
-        cta_n.push_back(std::min(G, tasks[0]));
+        tiles.push_back(a.seg[0].rows / (uint32_t)d2::kMvRows);
+        cta_n.push_back(std::min(G, tiles[0]));
     } else {
         double total = 0;
         for (uint32_t s = 0; s < a.n_seg; ++s) total += (double)a.seg[s].rows * (double)a.seg[s].row_bytes;
         uint32_t used = 0;
         for (uint32_t s = 0; s < a.n_seg; ++s) {
-            tasks.push_back(a.seg[s].rows / 16u * a.nb);
+            tiles.push_back(a.seg[s].rows / (uint32_t)d2::kMvRows);
             const double share = (double)G * (double)a.seg[s].rows * (double)a.seg[s].row_bytes / total;
             uint32_t n = (uint32_t)std::max(1.0, std::floor(share + 0.5));
-            n = std::min(n, tasks[s]);
+            n = std::min(n, tiles[s]);
             cta_n.push_back(n);
             used += n;
         }
@@ -509,39 +536,54 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
         }
     }
     std::vector<d2::MvCta> ctas;
-    uint32_t tile0 = 0;
-    for (size_t s = 0; s < cta_n.size(); ++s) {
-        a.seg_cta0[s] = (uint32_t)ctas.size();
-        a.seg_tile0[s] = tile0;
-        tile0 += paired ? a.seg[0].rows / 16u : a.seg[s].rows / 16u;
+    for (size_t s = 0; s < cta_n.size(); ++s)
         for (uint32_t c = 0; c < cta_n[s]; ++c) {
             d2::MvCta e{};
             e.seg = (uint32_t)s;
-            e.j0 = (uint32_t)((uint64_t)tasks[s] * c / cta_n[s]);
-            e.j1 = (uint32_t)((uint64_t)tasks[s] * (c + 1) / cta_n[s]);
+            e.j0 = (uint32_t)((uint64_t)tiles[s] * c / cta_n[s]) * TP;
+            e.j1 = (uint32_t)((uint64_t)tiles[s] * (c + 1) / cta_n[s]) * TP;
             ctas.push_back(e);
         }
-    }
-    a.seg_cta0[cta_n.size()] = (uint32_t)ctas.size();
     p.grid = (uint32_t)ctas.size();
-    if (tile0 > h->g2.tctr_n) return fail(h, ATLAS_EINVAL, "mv: tile counter buffer too small");
     // ring plan
-    uint32_t bb = 0;
-    for (uint32_t s = 0; s < a.n_seg; ++s) bb = std::max(bb, block_bytes(a.seg[s].type));
+    auto odd16 = [](uint32_t v) { return 16u * (((v + 15u) / 16u) | 1u); };
+    // bytes of a run of n blocks (decode2.cu mv_producer), largest over the segments
+    auto run_bytes = [&](uint32_t n) {
+        uint32_t m = 0;
+        for (uint32_t s = 0; s < a.n_seg; ++s) {
+            const d2::MvSeg &sg = a.seg[s];
+            const uint32_t bb = block_bytes(sg.type), rb = (uint32_t)sg.row_bytes;
+            m = std::max(m, n == a.nb ? sg.copies * odd16((16u / sg.copies) * rb + 15u) : 16u * odd16(n * bb + 15u));
+        }
+        return m;
+    };
     // A warp runs at most (nslot + 1) * st tasks ahead of the slowest warp,
     // so tslots > (nslot + 1) * st / TP + 1 open-tile slots never collide.
     auto tslots_of = [&](uint32_t nslot, uint32_t st) { return (nslot + 1u) * st / TP + 2u; };
     bool ok = false;
     for (uint32_t budget : {kHalfSmBytes, 227u * 1024u}) {
         for (uint32_t st : {8u, 4u, 2u, 1u}) {
+            // runs in a slot: a partial first run, whole rows, a partial last one
             const uint32_t npmax = std::min(st, (st - 1u) / a.nb + 2u);
             if (npmax > (uint32_t)d2::kMvMaxPortions) continue;
-            const uint32_t slot = (16u * (st * bb + npmax * 48u) + 127u) & ~127u;
+            uint32_t worst = 0;   // over where the slot's first run starts
+            for (uint32_t r1 = 1; r1 <= std::min(st, a.nb); ++r1) {
+                uint32_t sum = run_bytes(r1), left = st - r1;
+                while (left) {
+                    const uint32_t n = std::min(a.nb, left);
+                    sum += run_bytes(n);
+                    left -= n;
+                }
+                worst = std::max(worst, sum);
+            }
+            const uint32_t slot = (worst + 127u) & ~127u;
             uint32_t nslot = d2::kMvMaxSlots;
             while (nslot && (tslots_of(nslot, st) > (uint32_t)d2::kMvMaxTileSlots ||
                              atlas_d2_mv_smem(cols, nslot, slot, tslots_of(nslot, st)) > budget))
                 --nslot;
-            if (nslot >= 3u || (st == 1u && nslot >= 2u)) {
+            // a warp's next slot is kMvWarps / st slots on; it may be at most
+            // one ring round ahead of the slots still in use (mbarrier parity)
+            if (nslot >= std::max(3u, (uint32_t)d2::kMvWarps / st)) {
                 a.st = st;
                 a.nslot = nslot;
                 a.slot_bytes = slot;
@@ -560,8 +602,6 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     CU(h, cudaMemcpy(dc, ctas.data(), ctas.size() * sizeof(d2::MvCta), cudaMemcpyHostToDevice));
     a.cta = dc;
     a.eps = h->desc.rms_eps;
-    a.bpart = h->g2.bpart;
-    a.tctr = h->g2.tctr;
     a.pmax = h->pmax;
     a.pidx = h->pidx;
     a.status = h->g2.status;
@@ -580,10 +620,6 @@ int build_graph2(AtlasCuda *h)
     if (rc) return rc;
     CU(h, cudaMemset(g.st, 0, sizeof(d2::DecState)));
     g.status = &g.st->status;
-    if ((rc = dalloc(h, &g.bpart, (size_t)G * 64u * sizeof(float)))) return rc;
-    g.tctr_n = std::max(d.vocab, std::max(d.ffn, d.q_dim + 2u * d.kv_dim)) / 16u + 64u;
-    if ((rc = dalloc(h, &g.tctr, (size_t)g.tctr_n * 4u))) return rc;
-    CU(h, cudaMemset(g.tctr, 0, (size_t)g.tctr_n * 4u));
     g.splits = std::max(1u, std::min(G / d.kv_heads, 160u));
     if ((rc = dalloc(h, &g.apart, (size_t)d.kv_heads * g.splits * group * d2::kRec * sizeof(float)))) return rc;
     if ((rc = dalloc(h, &g.actr, (size_t)d.kv_heads * 4u))) return rc;
@@ -704,7 +740,6 @@ int run_graph2(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
         const int rc = status_to_code(h, out.status);
         // clear what a failed step may have left behind
         const AtlasModelDesc &d = h->desc;
-        cudaMemsetAsync(g.tctr, 0, (size_t)g.tctr_n * 4u, h->stream);
         cudaMemsetAsync(g.actr, 0, (size_t)d.kv_heads * 4u, h->stream);
         cudaMemsetAsync(g.st, 0, sizeof(d2::DecState), h->stream);
         cudaStreamSynchronize(h->stream);

@@ -116,7 +116,9 @@ __device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const 
 // NT independent 16-row x 256-element Q6_K tiles (blocks at even, not
 // necessarily 4-aligned addresses). Lane t keeps the 16-element groups with
 // k == t: one scale per (h, hp) and row, selected outside the k loop.
-template <int NT, bool FULL>
+// SAME_X: all NT tiles use the block column of xb[0] / xs[0] (row tiles of
+// one block column), so the B fragments are loaded once.
+template <int NT, bool FULL, bool SAME_X = false>
 __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const uint8_t *const (&r1)[NT],
                                           const uint8_t *const (&xb)[NT], const float *const (&xs)[NT], int g, int t,
                                           float (&o0)[NT], float (&o1)[NT])
@@ -163,7 +165,7 @@ __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const 
                         v0 = ((x0 >> sa) & 0x0f0f0f0fu) | ((Q0[n] << qs) & 0x30303030u);
                         v1 = ((x1 >> sa) & 0x0f0f0f0fu) | ((Q1[n] << qs) & 0x30303030u);
                     }
-                    const uint2 b = *reinterpret_cast<const uint2 *>(xb[n] + (e0 / 4u + (uint32_t)t) * 16u + podd);
+                    const uint2 b = *reinterpret_cast<const uint2 *>(xb[SAME_X ? 0 : n] + (e0 / 4u + (uint32_t)t) * 16u + podd);
                     float dd[4];
                     mma16816(dd, sub2(v0, 0x4140), sub2(v1, 0x4140), sub2(v0, 0x4342), sub2(v1, 0x4342), b, zero);
                     const bool mine = k == t;
@@ -173,7 +175,7 @@ __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const 
             }
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-                const float sx = 32.0f * xs[n][8u * h + 2u * (uint32_t)t + hp];
+                const float sx = 32.0f * xs[SAME_X ? 0 : n][8u * h + 2u * (uint32_t)t + hp];
                 o0[n] += s0[n] * ((keep[n][0] + keep[n][1]) * kTwo24 - sx);
                 o1[n] += s1[n] * ((keep[n][2] + keep[n][3]) * kTwo24 - sx);
             }
