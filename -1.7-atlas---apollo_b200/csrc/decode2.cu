@@ -608,19 +608,21 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
 // ---------------------------------------------------------- attention ----
 
 struct __align__(16) AttnSmem {
-    float4 q[kAttnMaxGroup][32];   // RoPE'd queries of the group (128 dims)
-    float4 k[kAttnTile][32];       // staged K rows
-    float4 v[kAttnTile][32];       // staged V rows
-    float4 knew[32], vnew[32];     // the current token's RoPE'd k and its v
+    float4 q[kAttnMaxGroup][32];        // RoPE'd queries of the group (128 dims)
+    uint8_t k[kAttnTile * 512];         // staged K rows, as stored in the cache (fp32 or fp16)
+    uint8_t v[kAttnTile * 512];         // staged V rows
+    float4 knew[32], vnew[32];          // the current token's RoPE'd k and its v
     float cden[kAttnMaxGroup];
+    uint64_t bar;                       // tile arrival
     uint32_t flag;
 };
 // followed by the combine weights cw[splits][kAttnMaxGroup]
 
-__device__ __forceinline__ float4 kv_load4(const void *cache, size_t row, uint32_t c4, bool f16)
+// 4 elements d4 of a staged cache row (fp32 or fp16 rows)
+__device__ __forceinline__ float4 kv_row4(const uint8_t *row, uint32_t d4, bool f16)
 {
-    if (!f16) return __ldcg(reinterpret_cast<const float4 *>(cache) + row * 32u + c4);
-    const uint2 hb = __ldcg(reinterpret_cast<const uint2 *>(cache) + row * 32u + c4);
+    if (!f16) return reinterpret_cast<const float4 *>(row)[d4];
+    const uint2 hb = reinterpret_cast<const uint2 *>(row)[d4];
     const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&hb.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&hb.y));
     return make_float4(a.x, a.y, b.x, b.y);
@@ -635,20 +637,22 @@ __device__ __forceinline__ float warp_maxf(float v)
 
 // Split-K flash-decode over the KV cache (gqa_single_token,
 // src/brain_runtime.c:1482-1528), one CTA per (KV head, split). The splits in
-// use grow with the context (at least kAttnMinSpan positions each); every
-// warp takes one query head of the group: scores one position per lane (q . k
-// over 128 dims read in a lane-rotated order, conflict-free), online softmax,
-// P.V with lane = 4 output dims. The split holding the current position
-// applies RoPE to the fresh k and appends k and v to the cache
-// (src/brain_runtime.c:1496-1500). The last split of a KV head to finish
-// combines all splits' (max, sum, acc) records.
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constant__ AttnArgs a)
+// use grow with the context (at least kAttnMinSpan positions each). A split's
+// cached K and V rows are contiguous in the cache, so each tile of up to
+// kAttnTile positions arrives as two bulk copies; the first is issued before
+// waiting for the preceding kernel (cached rows and the step's position were
+// written by earlier steps). Every warp takes one query head of the group,
+// lane = 4 of the 128 dimensions: one warp reduction per position's score,
+// online softmax per chunk of 32 positions, P.V. The
+// split holding the current position applies RoPE to the fresh k and
+// appends k and v to the cache (src/brain_runtime.c:1496-1500). The last
+// split of a KV head to finish combines all splits' (max, sum, acc) records.
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem_a[];
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
     float *cw = reinterpret_cast<float *>(smem_a + sizeof(AttnSmem));
     pdl_launch();
-    pdl_wait();
     const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
     if (pos >= a.max_context) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&a.st->status, kStatusOk, kStatusBadArgument);
@@ -664,7 +668,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     const uint32_t t0 = min(s * span, n), t1 = min(n, t0 + span);
     const bool has_pos = t0 <= pos && pos < t1;
     const bool f16 = a.kv_fp16 != 0u;
+    const uint32_t rowb = f16 ? 256u : 512u;
     const float scale = 1.0f / sqrtf(128.0f);
+    volatile uint32_t *err = &a.st->status;
+    const size_t head_row0 = (size_t)kvh * a.max_context;
+    // tile [tb, tb + kAttnTile) of the split: cached rows [tb, min(te, pos)) by bulk copies
+    auto issue = [&](uint32_t tb) {
+        const uint32_t te = min(tb + kAttnTile, t1), ce = max(tb, min(te, pos));
+        const uint32_t bytes = (ce - tb) * rowb;
+        mbar_arrive_expect_tx(&sm.bar, 2u * bytes);
+        if (bytes) {
+            bulk_g2s(sm.k, reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar);
+            bulk_g2s(sm.v, reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar);
+        }
+    };
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.bar, 1u);
+        fence_mbar_init();
+        if (t0 < t1) issue(t0);
+    }
+    __syncthreads();
+    pdl_wait();
     float *qf = reinterpret_cast<float *>(sm.q);
     for (uint32_t i = threadIdx.x; i < group * 64u; i += kAttnThreads) {
         const uint32_t hq = i >> 6, p = i & 63u;
@@ -687,7 +711,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     }
     __syncthreads();
     if (has_pos && threadIdx.x < 128u) {
-        const size_t off = ((size_t)kvh * a.max_context + pos) * 128u + threadIdx.x;
+        const size_t off = (head_row0 + pos) * 128u + threadIdx.x;
         const float kv = reinterpret_cast<const float *>(sm.knew)[threadIdx.x];
         const float vv = reinterpret_cast<const float *>(sm.vnew)[threadIdx.x];
         if (f16) {
@@ -700,47 +724,36 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     }
     float m = -FLT_MAX, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const size_t head_row0 = (size_t)kvh * a.max_context;
-    for (uint32_t tb = t0; tb < t1; tb += kAttnTile) {
-        const uint32_t te = min(tb + kAttnTile, t1), ce = max(tb, min(te, pos));
-        for (uint32_t idx = threadIdx.x; idx < (ce - tb) * 32u; idx += kAttnThreads) {
-            const uint32_t r = idx >> 5, c4 = idx & 31u;
-            sm.k[r][c4] = kv_load4(a.k_cache, head_row0 + tb + r, c4, f16);
-            sm.v[r][c4] = kv_load4(a.v_cache, head_row0 + tb + r, c4, f16);
-        }
-        if (pos >= tb && pos < te && threadIdx.x < 32u) {
-            sm.k[pos - tb][threadIdx.x] = sm.knew[threadIdx.x];
-            sm.v[pos - tb][threadIdx.x] = sm.vnew[threadIdx.x];
-        }
-        __syncthreads();
+    uint32_t phase = 0;
+    for (uint32_t tb = t0; tb < t1; tb += kAttnTile, phase ^= 1u) {
+        const uint32_t te = min(tb + kAttnTile, t1);
+        mbar_wait(&sm.bar, phase, err);
         if (warp < group) {
+            // lane = 4 of the 128 dimensions; scores of up to 32 positions,
+            // one warp reduction each (lane p keeps position p's score), then
+            // an online-softmax update and P.V for the chunk
+            const float4 qv = sm.q[warp][lane];
             for (uint32_t sb = tb; sb < te; sb += 32u) {
-                const uint32_t p = sb + lane;
-                const bool valid = p < te;
+                const uint32_t np = min(32u, te - sb);
                 float sc = -FLT_MAX;
-                if (valid) {
-                    float dot = 0.f;
-#pragma unroll 8
-                    for (uint32_t i = 0; i < 32u; ++i) {
-                        const uint32_t d4 = (i + lane) & 31u;
-                        const float4 qv = sm.q[warp][d4];
-                        const float4 kv = sm.k[p - tb][d4];
-                        dot = fmaf(qv.x, kv.x, dot);
-                        dot = fmaf(qv.y, kv.y, dot);
-                        dot = fmaf(qv.z, kv.z, dot);
-                        dot = fmaf(qv.w, kv.w, dot);
-                    }
-                    sc = dot * scale;
+#pragma unroll 4
+                for (uint32_t jj = 0; jj < np; ++jj) {
+                    const uint32_t p = sb + jj;
+                    const float4 kv = p == pos ? sm.knew[lane] : kv_row4(sm.k + (size_t)(p - tb) * rowb, lane, f16);
+                    float d = fmaf(qv.x, kv.x, qv.y * kv.y) + fmaf(qv.z, kv.z, qv.w * kv.w);
+                    d = warp_sum(d);
+                    if (lane == jj) sc = d * scale;
                 }
                 const float mn = fmaxf(m, warp_maxf(sc));
                 const float corr = expf(m - mn);
-                const float w = valid ? expf(sc - mn) : 0.f;
+                const float w = lane < np ? expf(sc - mn) : 0.f;
                 l = l * corr + warp_sum(w);
                 acc.x *= corr; acc.y *= corr; acc.z *= corr; acc.w *= corr;
-                const uint32_t np = min(32u, te - sb);
+#pragma unroll 4
                 for (uint32_t jj = 0; jj < np; ++jj) {
                     const float wj = __shfl_sync(0xffffffffu, w, (int)jj);
-                    const float4 vv = sm.v[sb + jj - tb][lane];
+                    const uint32_t pj = sb + jj;
+                    const float4 vv = pj == pos ? sm.vnew[lane] : kv_row4(sm.v + (size_t)(pj - tb) * rowb, lane, f16);
                     acc.x = fmaf(wj, vv.x, acc.x);
                     acc.y = fmaf(wj, vv.y, acc.y);
                     acc.z = fmaf(wj, vv.z, acc.z);
@@ -749,7 +762,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
                 m = mn;
             }
         }
-        __syncthreads();
+        __syncthreads();   // tile consumed: the buffers may be refilled
+        if (threadIdx.x == 0 && tb + kAttnTile < t1) issue(tb + kAttnTile);
     }
     if (warp < group) {
         float *dst = a.part + (((size_t)kvh * a.splits + s) * group + warp) * kRec;
@@ -766,19 +780,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     __syncthreads();
     if (!sm.flag) return;
     __threadfence();
-    // combine: weights exp(m_s - M) per split and head, then the weighted sums
+    // combine: weights exp(m_s - M) per split and head, then the weighted
+    // sums; every thread issues its loads of the partial records 16 splits
+    // at a time (they come from L2)
     for (uint32_t hq = warp; hq < group; hq += kAttnThreads / 32u) {
-        float M = -FLT_MAX;
-        for (uint32_t q = lane; q < ns; q += 32u)
+        float2 ml[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint32_t q = lane + 32u * (uint32_t)r;
+            ml[r] = q < ns ? __ldcg(reinterpret_cast<const float2 *>(a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u))
+                           : make_float2(-FLT_MAX, 0.f);
+        }
+        float M = fmaxf(ml[0].x, ml[1].x);
+        for (uint32_t q = lane + 64u; q < ns; q += 32u)
             M = fmaxf(M, __ldcg(a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u));
         M = warp_maxf(M);
         float den = 0.f;
         for (uint32_t q = lane; q < ns; q += 32u) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(
-                a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u));
-            const float w = expf(ml.x - M);
+            const float2 v = q < 32u ? ml[0] : q < 64u ? ml[1]
+                                     : __ldcg(reinterpret_cast<const float2 *>(a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u));
+            const float w = expf(v.x - M);
             cw[q * kAttnMaxGroup + hq] = w;
-            den += w * ml.y;
+            den += w * v.y;
         }
         den = warp_sum(den);
         if (lane == 0) sm.cden[hq] = den;
@@ -787,15 +810,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     for (uint32_t i = threadIdx.x; i < group * 32u; i += kAttnThreads) {
         const uint32_t hq = i >> 5, d4 = i & 31u;
         float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t q0 = 0; q0 < ns; q0 += 8u) {
-            float4 v[8];
+        for (uint32_t q0 = 0; q0 < ns; q0 += 16u) {
+            float4 v[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 16; ++j)
                 if (q0 + j < ns)
                     v[j] = __ldcg(reinterpret_cast<const float4 *>(
                         a.part + (((size_t)kvh * a.splits + q0 + j) * group + hq) * kRec) + d4);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 16; ++j)
                 if (q0 + j < ns) {
                     const float w = cw[(q0 + j) * kAttnMaxGroup + hq];
                     num.x = fmaf(w, v[j].x, num.x);

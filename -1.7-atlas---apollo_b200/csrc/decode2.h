@@ -85,7 +85,7 @@ struct MvArgs {
 
 constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kAttnTile = 64;      // cached positions staged per tile
-constexpr uint32_t kAttnMinSpan = 32;   // positions per split, at least
+constexpr uint32_t kAttnMinSpan = 16;   // positions per split, at least
 constexpr uint32_t kAttnMaxGroup = 8;   // query heads per KV head (one warp each)
 constexpr uint32_t kRec = 132;          // partial record: acc[128], max, sum, 2 pad
 
