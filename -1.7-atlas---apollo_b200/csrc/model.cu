@@ -560,8 +560,13 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     // A warp runs at most (nslot + 1) * st tasks ahead of the slowest warp,
     // so tslots > (nslot + 1) * st / TP + 1 open-tile slots never collide.
     auto tslots_of = [&](uint32_t nslot, uint32_t st) { return (nslot + 1u) * st / TP + 2u; };
+    // Rows longer than 8 blocks are staged in K-slices, one bulk copy per row
+    // piece: such launches take the whole SM so that the pieces can be 8
+    // blocks long (a bulk copy costs the copy engine tens of nanoseconds
+    // whatever its size), giving up co-residency with their neighbours.
+    const uint32_t budgets[2] = {a.nb > 8u ? 227u * 1024u : kHalfSmBytes, 227u * 1024u};
     bool ok = false;
-    for (uint32_t budget : {kHalfSmBytes, 227u * 1024u}) {
+    for (uint32_t budget : budgets) {
         for (uint32_t st : {8u, 4u, 2u, 1u}) {
             // runs in a slot: a partial first run, whole rows, a partial last one
             const uint32_t npmax = std::min(st, (st - 1u) / a.nb + 2u);
