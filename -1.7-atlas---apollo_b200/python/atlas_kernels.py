@@ -123,6 +123,26 @@ def cmd_prefill(a):
           f"{flops / best / 1e9:.1f} TFLOP/s of linear-layer work")
 
 
+def cmd_decode(a):
+    """Prefill a random prompt, then `steps` greedy decode steps through the
+    graph decode step; prints the device time per token of a 64-step run
+    unless --steps-only (then only the `steps` steps run: a capture target)."""
+    path = os.path.join(tempfile.gettempdir(), f"atlas_trace_{a.hidden}_{a.layers}_{a.ffn}_{a.vocab}.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
+    ids = np.random.default_rng(1).integers(0, a.vocab, a.prompt).astype(np.uint32)
+    with atlas_cuda.Runtime(path, max_context=a.prompt + a.steps + 80, max_prefill=a.prompt) as rt:
+        _, first = rt.prefill(ids, 0, want_logits=False)
+        rt.generate(first, a.prompt, a.steps)
+        if a.steps_only:
+            return
+        d0 = rt.stats()[2]
+        rt.generate(first, a.prompt, 64)
+        ms = (rt.stats()[2] - d0) / 64
+    print(f"decode at position {a.prompt}: {ms:.4f} ms per token, {1e3 / ms:.1f} tok/s")
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -154,8 +174,18 @@ def main():
     t.add_argument("--ffn", type=int, default=11008)
     t.add_argument("--vocab", type=int, default=151936)
     t.add_argument("--pos", type=int, default=600)
+    dcd = sub.add_parser("decode")
+    dcd.add_argument("--hidden", type=int, default=2048)
+    dcd.add_argument("--layers", type=int, default=36)
+    dcd.add_argument("--q-heads", type=int, default=16)
+    dcd.add_argument("--kv-heads", type=int, default=2)
+    dcd.add_argument("--ffn", type=int, default=11008)
+    dcd.add_argument("--vocab", type=int, default=151936)
+    dcd.add_argument("--prompt", type=int, default=512)
+    dcd.add_argument("--steps", type=int, default=3)
+    dcd.add_argument("--steps-only", action="store_true")
     a = ap.parse_args()
-    {"gemv": cmd_gemv, "trace": cmd_trace, "gemm": cmd_gemm, "prefill": cmd_prefill}[a.cmd](a)
+    {"gemv": cmd_gemv, "trace": cmd_trace, "gemm": cmd_gemm, "prefill": cmd_prefill, "decode": cmd_decode}[a.cmd](a)
 
 
 if __name__ == "__main__":
