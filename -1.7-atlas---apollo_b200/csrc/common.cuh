@@ -24,6 +24,7 @@ enum : uint32_t {
     kStatusStageTimeout = 2,     // an mbarrier (bulk-copy stage) never completed
     kStatusBadArgument = 3,      // device-side argument check failed
     kStatusCombineTimeout = 4,   // attention split combine never saw all splits
+    kStatusPeerTimeout = 5,      // a tensor-parallel peer's arrivals never came
 };
 
 // Wall-clock bound of one wait (globaltimer, ns): far above any legitimate
@@ -165,6 +166,37 @@ __device__ __forceinline__ uint32_t atom_acq_rel_add(uint32_t *p, uint32_t v)
     uint32_t old;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
+}
+
+// System scope (another GPU writes the counter over NVLink).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v)
+{
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *ctr >= target (mod 2^32), acquire at system scope.
+__device__ __forceinline__ bool wait_counter_sys(const uint32_t *ctr, uint32_t target, volatile uint32_t *err)
+{
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        if ((int32_t)(ld_acquire_sys(ctr) - target) >= 0) return true;
+        if (*err != kStatusOk) return false;
+        if (i > 32) {
+            __nanosleep(32);
+            const uint64_t now = global_ns();
+            if (!t0) t0 = now;
+            else if (now - t0 > kWaitLimitNs) break;
+        }
+    }
+    atomicCAS(const_cast<uint32_t *>(err), kStatusOk, kStatusPeerTimeout);
+    return false;
 }
 
 // Bounded wait until *ctr >= target (acquire). False on timeout / prior error.

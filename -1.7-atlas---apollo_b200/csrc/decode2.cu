@@ -233,6 +233,22 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
         }
     }
     if (a.pdl) pdl_wait();
+    // tensor parallel: the partial rows of the preceding row-split projection
+    // from every rank, then x = a.x + slot 0 + slot 1 + ... in rank order
+    const float4 *red = nullptr;
+    uint32_t own0 = 0, own1 = 0;
+    if (a.in_red) {
+        if (threadIdx.x == 0) {
+            const uint32_t epoch = *reinterpret_cast<volatile const uint32_t *>(&a.dstate->epoch);
+            const uint32_t k = epoch * a.seq_mul + a.seq_add;
+            wait_counter_sys(reinterpret_cast<const uint32_t *>(a.peer[a.rank] + a.in_cnt), k * a.in_arrivals,
+                             a.status);
+        }
+        mv_sync();
+        red = reinterpret_cast<const float4 *>(a.peer[a.rank] + a.in_red);
+        own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
+        own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
+    }
     for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += kDepth * kStride) {
         float4 v[kDepth];
 #pragma unroll
@@ -241,6 +257,34 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
             if (i < n4) {
                 v[j] = __ldcg(reinterpret_cast<const float4 *>(a.x) + i);
                 if (norm && i0 != threadIdx.x) w[j] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
+            }
+        }
+        if (red) {
+            for (uint32_t r = 0; r < a.tp; ++r) {
+#pragma unroll
+                for (int j = 0; j < kDepth; ++j) {
+                    const uint32_t i = i0 + (uint32_t)j * kStride;
+                    if (i < n4) {
+                        const float4 p = __ldcg(red + (size_t)r * n4 + i);
+                        v[j].x += p.x; v[j].y += p.y; v[j].z += p.z; v[j].w += p.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kDepth; ++j) {
+                const uint32_t i = i0 + (uint32_t)j * kStride;
+                if (i >= own0 && i < own1 && a.xout) reinterpret_cast<float4 *>(a.xout)[i] = v[j];
+            }
+        }
+        if (a.x_hi) {
+            // the rank's slice of the attention output inside its o blocks
+#pragma unroll
+            for (int j = 0; j < kDepth; ++j) {
+                const uint32_t e = 4u * (i0 + (uint32_t)j * kStride);
+                if (e + 0u < a.x_lo || e + 0u >= a.x_hi) v[j].x = 0.f;
+                if (e + 1u < a.x_lo || e + 1u >= a.x_hi) v[j].y = 0.f;
+                if (e + 2u < a.x_lo || e + 2u >= a.x_hi) v[j].z = 0.f;
+                if (e + 3u < a.x_lo || e + 3u >= a.x_hi) v[j].w = 0.f;
             }
         }
 #pragma unroll
@@ -324,6 +368,13 @@ __device__ __forceinline__ void mv_finish(const MvArgs &a, uint32_t segi, uint32
     const MvSeg &sg = a.seg[segi];
     if (a.epi == MV_RESID) {
         sg.out[row] = pre + v0;   // src/brain_runtime.c:1745, :1762
+        return;
+    }
+    if (a.epi == MV_PART) {
+        // this rank's partial row into its slot at every rank (the residual
+        // is added by the consumer's staging)
+        for (uint32_t p = 0; p < a.tp; ++p)
+            reinterpret_cast<float *>(a.peer[p] + a.out_red)[(size_t)a.rank * sg.rows + row] = v0;
         return;
     }
     const float r = sg.bias ? v0 + pre : v0;
@@ -586,6 +637,15 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
     }
     MvBest best{-FLT_MAX, 0xffffffffu};
     mv_consumer(a, h, xarea, ring, c, err, best);
+    if (a.epi == MV_PART) {
+        // every pushing thread orders its own remote stores, then one arrival
+        // per CTA at every rank
+        __threadfence_system();
+        mv_sync();
+        if (threadIdx.x == 0)
+            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        return;
+    }
     if (a.epi != MV_LOGITS) return;
     // one (max, row) per CTA; the argmax kernel reduces them
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -600,8 +660,20 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
     if (threadIdx.x == 0) {
         for (int w = 1; w < kMvWarps; ++w)
             if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
-        a.pmax[blockIdx.x] = best.v;
-        a.pidx[blockIdx.x] = best.i;
+        if (a.tp > 1u) {
+            // (max, global row) into this rank's slot at every rank
+            for (uint32_t p = 0; p < a.tp; ++p) {
+                reinterpret_cast<float *>(a.peer[p] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
+                reinterpret_cast<uint32_t *>(a.peer[p] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
+                                                                                            blockIdx.x] =
+                    a.row_base + best.i;
+            }
+            __threadfence_system();
+            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        } else {
+            a.pmax[blockIdx.x] = best.v;
+            a.pidx[blockIdx.x] = best.i;
+        }
     }
 }
 
@@ -855,14 +927,22 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t *embd, uint64_
 
 // Greedy pick over the head's per-CTA (max, row) partials, lowest row among
 // equal maxima (atlas_sample_token's greedy branch, src/brain_runtime.c:1783);
-// then advance the step state.
+// then advance the step state. Tensor parallel: the partials of every rank,
+// once the head counter `cnt` has seen this step's `arrivals`.
 __global__ void __launch_bounds__(256) argmax_kernel(const float *pmax, const uint32_t *pidx, uint32_t n,
-                                                     DecState *st)
+                                                     DecState *st, const uint32_t *cnt, uint32_t arrivals)
 {
     __shared__ float bv[8];
     __shared__ uint32_t bi[8];
     pdl_launch();
     pdl_wait();
+    if (cnt) {
+        if (threadIdx.x == 0) {
+            const uint32_t epoch = *reinterpret_cast<volatile const uint32_t *>(&st->epoch);
+            wait_counter_sys(cnt, (epoch + 1u) * arrivals, &st->status);
+        }
+        __syncthreads();
+    }
     float best = -FLT_MAX;
     uint32_t idx = 0xffffffffu;
     for (uint32_t i = threadIdx.x; i < n; i += 256u) {
@@ -886,10 +966,12 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *pmax, const ui
     st->next_logit = best;
     if (st->out_ids && st->step < st->max_steps) st->out_ids[st->step] = idx;
     if (st->advance) {
-        st->token = idx;
+        // prompt mode: the next prompt token instead of the pick
+        st->token = (st->in_ids && st->step + 1u < st->n_in) ? st->in_ids[st->step + 1u] : idx;
         st->pos = st->pos + 1u;
         st->step = st->step + 1u;
     }
+    st->epoch = st->epoch + 1u;
 }
 
 }  // namespace d2
@@ -960,8 +1042,8 @@ extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_b
 }
 
 extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n, DecState *st,
-                                              cudaStream_t stream)
+                                              const uint32_t *cnt, uint32_t arrivals, cudaStream_t stream)
 {
-    void *args[] = {&pmax, &pidx, &n, &st};
+    void *args[] = {&pmax, &pidx, &n, &st, &cnt, &arrivals};
     return launch_ex((const void *)argmax_kernel, args, dim3(1), dim3(256), 0, stream, true);
 }

@@ -26,7 +26,39 @@ struct DecState {
     uint32_t max_steps;    // capacity of out_ids
     uint32_t advance;      // 1: after the pick, token = pick, pos += 1, step += 1
     uint32_t *out_ids;     // optional device array of picks
+    const uint32_t *in_ids;  // prompt mode: the token after step s is in_ids[s + 1] while s + 1 < n_in
+    uint32_t n_in;
+    uint32_t epoch;        // steps completed since creation (tensor-parallel exchange sequence)
 };
+
+// ------------------------------------------------ tensor-parallel exchange --
+//
+// Every rank owns one exchange area in device memory, mapped into the other
+// ranks' processes. Row-split projections (o, down) push their partial rows
+// into every rank's area, at the slot of the pushing rank, and count one
+// arrival per CTA at every rank; the next kernel's input staging waits for
+// all arrivals of that occurrence and sums the slots in rank order, so every
+// rank computes the same x. The head pushes its per-CTA (max, row) pairs the
+// same way for the argmax. Counters only grow: occurrence k of a stage is
+// complete when the counter reaches k * arrivals (mod 2^32).
+constexpr uint32_t kTpMax = 8;
+constexpr uint32_t kTpPStride = 256;    // per-rank (max, row) slots, >= CTAs of the head launch
+constexpr uint32_t kTpCntO = 0, kTpCntDn = 4, kTpCntHead = 8;   // counter byte offsets
+
+struct TpLayout {
+    uint32_t red_o, red_dn, pmax, pidx, bytes;   // byte offsets / total size
+};
+
+__host__ __device__ inline TpLayout tp_layout(uint32_t tp, uint32_t hidden)
+{
+    TpLayout l{};
+    l.red_o = 128u;
+    l.red_dn = l.red_o + ((tp * hidden * 4u + 127u) & ~127u);
+    l.pmax = l.red_dn + ((tp * hidden * 4u + 127u) & ~127u);
+    l.pidx = l.pmax + tp * kTpPStride * 4u;
+    l.bytes = l.pidx + tp * kTpPStride * 4u;
+    return l;
+}
 
 // ------------------------------------------------------------ mv kernel ----
 //
@@ -43,7 +75,8 @@ constexpr int kMvMaxSlots = 8;
 constexpr int kMvMaxTileSlots = 128;              // open tiles tracked in shared memory, at most
 constexpr int kMvMaxPortions = 4;                 // (tile, segment) runs in one slot
 
-enum MvEpi : uint32_t { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_LOGITS = 3 };
+// MV_PART: partial rows of a row-split projection, pushed to every rank
+enum MvEpi : uint32_t { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_LOGITS = 3, MV_PART = 4 };
 
 struct MvSeg {
     const uint8_t *w;      // row 0 of the raw GGUF tensor
@@ -79,6 +112,19 @@ struct MvArgs {
     uint32_t *pidx;
     uint32_t *status;
     uint32_t pdl;          // launched as a programmatic dependent
+    // tensor parallel (tp > 1)
+    uint8_t *peer[kTpMax];   // exchange areas of the ranks, as mapped in this process
+    uint32_t tp, rank;
+    const DecState *dstate;  // epoch of the current step
+    // input staging: x = a.x + sum over ranks of the receive slots at in_red,
+    // once in_cnt has seen occurrence epoch * seq_mul + seq_add; the sum is
+    // written back to xout (each CTA its share). in_red == 0: no exchange.
+    uint32_t in_red, in_cnt, in_arrivals, seq_mul, seq_add;
+    float *xout;
+    uint32_t x_lo, x_hi;     // x_hi > 0: staged elements outside [x_lo, x_hi) are zero
+    // MV_PART / MV_LOGITS pushes: receive offset and counter at every rank
+    uint32_t out_red, out_cnt;
+    uint32_t row_base;       // MV_LOGITS: global index of row 0
 };
 
 // ------------------------------------------------------ attention kernel ----

@@ -8,6 +8,7 @@
 // attention split partials; a RoPE (cos, sin) table built on the host with the
 // reference's own powf / cosf / sinf (src/brain_runtime.c:1383-1387).
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstddef>
 #include <cstdarg>
@@ -45,7 +46,8 @@ extern "C" cudaError_t atlas_d2_launch_attn(const atlas::d2::AttnArgs *a, uint32
 extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,
                                              uint32_t vocab, float *x, atlas::d2::DecState *st, cudaStream_t stream);
 extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n,
-                                              atlas::d2::DecState *st, cudaStream_t stream);
+                                              atlas::d2::DecState *st, const uint32_t *cnt, uint32_t arrivals,
+                                              cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_wbound(uint32_t type, const uint8_t *blocks, uint64_t nblocks, uint32_t *out_bits,
                                            cudaStream_t stream);
 
@@ -124,6 +126,17 @@ struct AtlasCuda {
     double total_ms = 0.0;
     uint32_t n_stages = 0, stage_bytes = 0, max_cols = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // Tensor parallel: this rank's slice, the exchange areas (own and the
+    // peers' mappings), the second residual buffer, prompt ids for prompt mode.
+    int tp = 1, rank = 0;
+    AtlasTpSlice sl{};
+    uint8_t *xchg = nullptr;
+    uint8_t *peer[d2::kTpMax] = {};
+    bool peer_mapped[d2::kTpMax] = {};
+    float *x2 = nullptr;
+    uint32_t *d_in_ids = nullptr;
+    uint32_t in_cap = 0;
+    bool broken = false;   // a failed tensor-parallel step left the ranks out of step
 };
 
 namespace {
@@ -195,9 +208,47 @@ uint64_t elems(const AtlasTensorDesc *t)
     return e;
 }
 
-// Matrix tensor [rows x cols] of a supported GEMV type, uploaded unchanged.
-int upload_matrix(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, uint64_t rows, const uint8_t **dev,
-                  uint32_t *type)
+// Tensor-parallel slice of rank `rank` of `size`: KV heads (with their query
+// heads) split evenly; attn_output columns = the rank's attention-output
+// elements, widened to whole 256-blocks (a block shared by two ranks is read
+// by both, each zeroing the other's elements); FFN rows in whole 256-blocks
+// (ffn_down's columns follow them); output-head rows in whole 16-row tiles.
+// Returns a static reason string, or nullptr when the shape splits.
+const char *tp_slice_of(const AtlasModelDesc &d, int rank, int size, AtlasTpSlice &s)
+{
+    s = AtlasTpSlice{};
+    if (size != 1 && size != 2 && size != 4 && size != 8) return "tp_size must be 1, 2, 4 or 8";
+    if (rank < 0 || rank >= size) return "tp_rank out of range";
+    if (!d.kv_heads || d.kv_heads % (uint32_t)size) return "kv_heads is not a multiple of tp_size";
+    if (!d.q_heads || d.q_heads % d.kv_heads) return "q_heads is not a multiple of kv_heads";
+    const uint32_t nbf = d.ffn / 256u, tiles = d.vocab / 16u;
+    if (d.ffn % 256u || nbf < (uint32_t)size) return "ffn is too small to split";
+    if (d.vocab % 16u || tiles < (uint32_t)size) return "vocab is not a multiple of 16 rows per rank";
+    const uint32_t r = (uint32_t)rank, n = (uint32_t)size, group = d.q_heads / d.kv_heads;
+    s.kv_heads = d.kv_heads / n;
+    s.kv_head0 = r * s.kv_heads;
+    s.q_heads = s.kv_heads * group;
+    s.q_head0 = s.kv_head0 * group;
+    const uint32_t q0 = s.q_head0 * 128u, q1 = q0 + s.q_heads * 128u;
+    s.o_block0 = q0 / 256u;
+    s.o_blocks = (q1 + 255u) / 256u - s.o_block0;
+    s.o_lo = q0 - 256u * s.o_block0;
+    s.o_hi = q1 - 256u * s.o_block0;
+    const uint32_t f0 = (uint32_t)((uint64_t)nbf * r / n), f1 = (uint32_t)((uint64_t)nbf * (r + 1u) / n);
+    s.ffn_row0 = 256u * f0;
+    s.ffn_rows = 256u * (f1 - f0);
+    const uint32_t v0 = (uint32_t)((uint64_t)tiles * r / n), v1 = (uint32_t)((uint64_t)tiles * (r + 1u) / n);
+    s.vocab_row0 = 16u * v0;
+    s.vocab_rows = 16u * (v1 - v0);
+    return nullptr;
+}
+
+// Rows [row0, row0 + nrows) and 256-column blocks [b0, b0 + nblk) of a matrix
+// tensor [rows x cols] of a supported GEMV type. The blocks are uploaded
+// unchanged; a block-column slice (a tensor-parallel rank's share of a
+// row-split projection) is packed row after row.
+int upload_matrix_part(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, uint64_t rows, uint64_t row0,
+                       uint64_t nrows, uint64_t b0, uint64_t nblk, const uint8_t **dev, uint32_t *type)
 {
     if (!t) return fail(h, ATLAS_EINVAL, "missing matrix tensor");
     if (t->type != ATLAS_TYPE_Q4_K && t->type != ATLAS_TYPE_Q6_K)
@@ -207,20 +258,38 @@ int upload_matrix(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, uint64_
         return fail(h, ATLAS_EINVAL, "%s: dims %llu x %llu, expected %llu x %llu", t->name,
                     (unsigned long long)t->dims[0], (unsigned long long)t->dims[1], (unsigned long long)cols,
                     (unsigned long long)rows);
-    const uint64_t bytes = rows * (cols / 256) * block_bytes(t->type);
+    const uint64_t nb = cols / 256, bb = block_bytes(t->type), rb = nb * bb;
+    if (row0 + nrows > rows || b0 + nblk > nb || !nrows || !nblk) return fail(h, ATLAS_EINVAL, "%s: bad slice", t->name);
+    const uint64_t bytes = nrows * nblk * bb;
     uint8_t *d = nullptr;
     int rc = dalloc(h, &d, bytes);
     if (rc) return rc;
-    CU(h, cudaMemcpy(d, t->data, bytes, cudaMemcpyHostToDevice));
+    const uint8_t *src = static_cast<const uint8_t *>(t->data) + row0 * rb;
+    if (nblk == nb) {
+        CU(h, cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice));
+    } else {
+        std::vector<uint8_t> tmp(bytes);
+        for (uint64_t r = 0; r < nrows; ++r) memcpy(&tmp[r * nblk * bb], src + r * rb + b0 * bb, nblk * bb);
+        CU(h, cudaMemcpy(d, tmp.data(), bytes, cudaMemcpyHostToDevice));
+    }
     *dev = d;
     *type = t->type;
     return ATLAS_OK;
 }
 
+// Matrix tensor [rows x cols] of a supported GEMV type, uploaded unchanged.
+int upload_matrix(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, uint64_t rows, const uint8_t **dev,
+                  uint32_t *type)
+{
+    return upload_matrix_part(h, t, cols, rows, 0, rows, 0, cols / 256, dev, type);
+}
+
 // F32 or F16 vector of n elements -> fp32 on the device (load_f32_vector,
 // src/brain_runtime.c:1280-1309).
-int upload_vector(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t n, const float **dev)
+int upload_vector(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t n, const float **dev, uint64_t off = 0,
+                  uint64_t count = 0)
 {
+    if (!count) count = n;
     if (!t || elems(t) != n) return fail(h, ATLAS_EINVAL, "%s: vector of %llu elements expected", t ? t->name : "?",
                                          (unsigned long long)n);
     std::vector<float> tmp(n);
@@ -244,10 +313,11 @@ int upload_vector(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t n, const floa
     } else {
         return fail(h, ATLAS_EINVAL, "%s: vector type %u unsupported", t->name, t->type);
     }
+    if (off + count > n) return fail(h, ATLAS_EINVAL, "%s: bad vector slice", t->name);
     float *d = nullptr;
-    int rc = dalloc(h, &d, n * 4);
+    int rc = dalloc(h, &d, count * 4);
     if (rc) return rc;
-    CU(h, cudaMemcpy(d, tmp.data(), n * 4, cudaMemcpyHostToDevice));
+    CU(h, cudaMemcpy(d, tmp.data() + off, count * 4, cudaMemcpyHostToDevice));
     *dev = d;
     return ATLAS_OK;
 }
@@ -392,6 +462,8 @@ int status_to_code(AtlasCuda *h, uint32_t st)
     if (st == kStatusOk) return ATLAS_OK;
     if (st == kStatusBarrierTimeout) return fail(h, ATLAS_ETIMEOUT, "device phase barrier timed out (status %u)", st);
     if (st == kStatusStageTimeout) return fail(h, ATLAS_ETIMEOUT, "device copy stage timed out (status %u)", st);
+    if (st == kStatusCombineTimeout) return fail(h, ATLAS_ETIMEOUT, "attention split combine timed out (status %u)", st);
+    if (st == kStatusPeerTimeout) return fail(h, ATLAS_ENCCL, "a tensor-parallel peer did not arrive (status %u)", st);
     return fail(h, ATLAS_ECUDA, "device reported status %u", st);
 }
 
@@ -614,46 +686,96 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     return ATLAS_OK;
 }
 
-// Capture one decode step as a CUDA graph of PDL-chained kernels.
+// Capture one decode step as a CUDA graph of PDL-chained kernels. With
+// tensor parallelism the shapes are the rank's slice; o and down push partial
+// rows (MV_PART) that the next kernel's staging sums in rank order, with the
+// residual kept in two buffers: qkv stages x2 + down partials into x,
+// gate/up stages x + o partials into x2.
 int build_graph2(AtlasCuda *h)
 {
     const AtlasModelDesc &d = h->desc;
+    const AtlasTpSlice &sl = h->sl;
     AtlasCuda::Graph2 &g = h->g2;
-    const uint32_t G = (uint32_t)h->sm_count, group = d.q_heads / d.kv_heads;
+    const uint32_t G = (uint32_t)h->sm_count, group = d.q_heads / d.kv_heads, tp = (uint32_t)h->tp;
+    const uint32_t lq = sl.q_heads * 128u, lkv = sl.kv_heads * 128u;
     if (group > d2::kAttnMaxGroup) return fail(h, ATLAS_EINVAL, "graph decode: more than 8 query heads per KV head");
     int rc = dalloc(h, &g.st, sizeof(d2::DecState));
     if (rc) return rc;
     CU(h, cudaMemset(g.st, 0, sizeof(d2::DecState)));
     g.status = &g.st->status;
-    g.splits = std::max(1u, std::min(G / d.kv_heads, 160u));
-    if ((rc = dalloc(h, &g.apart, (size_t)d.kv_heads * g.splits * group * d2::kRec * sizeof(float)))) return rc;
-    if ((rc = dalloc(h, &g.actr, (size_t)d.kv_heads * 4u))) return rc;
-    CU(h, cudaMemset(g.actr, 0, (size_t)d.kv_heads * 4u));
+    g.splits = std::max(1u, std::min(G / sl.kv_heads, 160u));
+    if ((rc = dalloc(h, &g.apart, (size_t)sl.kv_heads * g.splits * group * d2::kRec * sizeof(float)))) return rc;
+    if ((rc = dalloc(h, &g.actr, (size_t)sl.kv_heads * 4u))) return rc;
+    CU(h, cudaMemset(g.actr, 0, (size_t)sl.kv_heads * 4u));
 
     const AtlasCuda::W &w0 = h->layers[0];
+    const uint32_t o_cols = sl.o_blocks * 256u;
+    const uint32_t part = tp > 1 ? (uint32_t)d2::MV_PART : (uint32_t)d2::MV_RESID;
     MvPlan qkv, o, gu, dn, hd;
     if ((rc = plan_mv(h, qkv, d.hidden, false,
-                      {mvseg(w0.q, w0.tq, d.q_dim, d.hidden, w0.bq, h->q), mvseg(w0.k, w0.tk, d.kv_dim, d.hidden, w0.bk, h->k),
-                       mvseg(w0.v, w0.tv, d.kv_dim, d.hidden, w0.bv, h->v)},
+                      {mvseg(w0.q, w0.tq, lq, d.hidden, w0.bq, h->q), mvseg(w0.k, w0.tk, lkv, d.hidden, w0.bk, h->k),
+                       mvseg(w0.v, w0.tv, lkv, d.hidden, w0.bv, h->v)},
                       d2::MV_STORE)))
         return rc;
-    if ((rc = plan_mv(h, o, d.q_dim, false, {mvseg(w0.o, w0.to, d.hidden, d.q_dim, nullptr, h->x)}, d2::MV_RESID)))
-        return rc;
+    if ((rc = plan_mv(h, o, o_cols, false, {mvseg(w0.o, w0.to, d.hidden, o_cols, nullptr, h->x)}, part))) return rc;
     if ((rc = plan_mv(h, gu, d.hidden, true,
-                      {mvseg(w0.gate, w0.tg, d.ffn, d.hidden, nullptr, h->ffn), mvseg(w0.up, w0.tu, d.ffn, d.hidden, nullptr, nullptr)},
+                      {mvseg(w0.gate, w0.tg, sl.ffn_rows, d.hidden, nullptr, h->ffn),
+                       mvseg(w0.up, w0.tu, sl.ffn_rows, d.hidden, nullptr, nullptr)},
                       d2::MV_SWIGLU)))
         return rc;
-    if ((rc = plan_mv(h, dn, d.ffn, false, {mvseg(w0.down, w0.td, d.hidden, d.ffn, nullptr, h->x)}, d2::MV_RESID)))
+    if ((rc = plan_mv(h, dn, sl.ffn_rows, false, {mvseg(w0.down, w0.td, d.hidden, sl.ffn_rows, nullptr, h->x)}, part)))
         return rc;
-    if ((rc = plan_mv(h, hd, d.hidden, false, {mvseg(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)},
+    if ((rc = plan_mv(h, hd, d.hidden, false, {mvseg(h->head, h->t_head, sl.vocab_rows, d.hidden, nullptr, h->logits)},
                       d2::MV_LOGITS)))
         return rc;
     qkv.a.x = h->x;
-    o.a.x = h->att;
+    o.a.x = h->att + (size_t)sl.o_block0 * 256u;
     gu.a.x = h->x;
     dn.a.x = h->ffn;
     hd.a.x = h->x;
     hd.a.norm_w = h->out_norm;
+    uint32_t arr_o = 0, arr_dn = 0, arr_hd = 0;
+    if (tp > 1) {
+        // arrivals per occurrence: one per CTA of every rank; o and down have
+        // the same rows (hidden) on every rank, head grids follow the slices
+        if (o.grid != std::min(G, d.hidden / 16u) || dn.grid != o.grid)
+            return fail(h, ATLAS_EINVAL, "tensor parallel: unexpected o / down grid");
+        arr_o = tp * o.grid;
+        arr_dn = tp * dn.grid;
+        for (uint32_t r = 0; r < tp; ++r) {
+            AtlasTpSlice rs{};
+            tp_slice_of(d, (int)r, (int)tp, rs);
+            arr_hd += std::min(G, rs.vocab_rows / 16u);
+        }
+        if (hd.grid != std::min(G, sl.vocab_rows / 16u) || hd.grid > d2::kTpPStride)
+            return fail(h, ATLAS_EINVAL, "tensor parallel: unexpected head grid");
+        const d2::TpLayout xl = d2::tp_layout(tp, d.hidden);
+        for (MvPlan *p : {&qkv, &o, &gu, &dn, &hd}) {
+            for (uint32_t r = 0; r < tp; ++r) p->a.peer[r] = h->peer[r];
+            p->a.tp = tp;
+            p->a.rank = (uint32_t)h->rank;
+            p->a.dstate = g.st;
+            p->a.seq_mul = d.layers;
+        }
+        o.a.x_lo = sl.o_lo;
+        o.a.x_hi = sl.o_hi;
+        o.a.out_red = xl.red_o;
+        o.a.out_cnt = d2::kTpCntO;
+        dn.a.out_red = xl.red_dn;
+        dn.a.out_cnt = d2::kTpCntDn;
+        gu.a.in_red = xl.red_o;
+        gu.a.in_cnt = d2::kTpCntO;
+        gu.a.in_arrivals = arr_o;
+        gu.a.xout = h->x2;
+        hd.a.x = h->x2;
+        hd.a.in_red = xl.red_dn;
+        hd.a.in_cnt = d2::kTpCntDn;
+        hd.a.in_arrivals = arr_dn;
+        hd.a.seq_add = d.layers;
+        hd.a.out_red = xl.pmax;
+        hd.a.out_cnt = d2::kTpCntHead;
+        hd.a.row_base = sl.vocab_row0;
+    }
     size_t mv_smem = 0;
     for (const MvPlan *p : {&qkv, &o, &gu, &dn, &hd}) mv_smem = std::max<size_t>(mv_smem, p->a.smem_bytes);
     CU(h, atlas_d2_setup(mv_smem, atlas_d2_attn_smem(g.splits)));
@@ -662,13 +784,13 @@ int build_graph2(AtlasCuda *h)
     at.q = h->q;
     at.k = h->k;
     at.v = h->v;
-    at.att = h->att;
+    at.att = h->att + (size_t)sl.q_head0 * 128u;
     at.part = g.apart;
     at.ctr = g.actr;
     at.rope = h->rope;
     at.st = g.st;
-    at.q_heads = d.q_heads;
-    at.kv_heads = d.kv_heads;
+    at.q_heads = sl.q_heads;
+    at.kv_heads = sl.kv_heads;
     at.max_context = d.max_context;
     at.splits = g.splits;
     at.kv_fp16 = d.kv_fp16 ? 1u : 0u;
@@ -685,10 +807,20 @@ int build_graph2(AtlasCuda *h)
         a.seg[1].w = w.k; a.seg[1].bias = w.bk;
         a.seg[2].w = w.v; a.seg[2].bias = w.bv;
         a.norm_w = w.attn_norm;
+        if (tp > 1 && l > 0) {
+            // x = x2 + the down partials of layer l - 1 (occurrence epoch * L + l)
+            const d2::TpLayout xl = d2::tp_layout(tp, d.hidden);
+            a.x = h->x2;
+            a.in_red = xl.red_dn;
+            a.in_cnt = d2::kTpCntDn;
+            a.in_arrivals = arr_dn;
+            a.seq_add = l;
+            a.xout = h->x;
+        }
         if ((e = atlas_d2_launch_mv(&a, qkv.grid, h->stream)) != cudaSuccess) break;
         at.k_cache = w.kc;
         at.v_cache = w.vc;
-        if ((e = atlas_d2_launch_attn(&at, d.kv_heads * g.splits, h->stream)) != cudaSuccess) break;
+        if ((e = atlas_d2_launch_attn(&at, sl.kv_heads * g.splits, h->stream)) != cudaSuccess) break;
         a = o.a;
         a.seg[0].w = w.o;
         if ((e = atlas_d2_launch_mv(&a, o.grid, h->stream)) != cudaSuccess) break;
@@ -696,6 +828,7 @@ int build_graph2(AtlasCuda *h)
         a.seg[0].w = w.gate;
         a.seg[1].w = w.up;
         a.norm_w = w.ffn_norm;
+        a.seq_add = l + 1u;
         if ((e = atlas_d2_launch_mv(&a, gu.grid, h->stream)) != cudaSuccess) break;
         a = dn.a;
         a.seg[0].w = w.down;
@@ -703,7 +836,17 @@ int build_graph2(AtlasCuda *h)
         kernels += 5;
     }
     if (e == cudaSuccess) { e = atlas_d2_launch_mv(&hd.a, hd.grid, h->stream); ++kernels; }
-    if (e == cudaSuccess) { e = atlas_d2_launch_argmax(h->pmax, h->pidx, hd.grid, g.st, h->stream); ++kernels; }
+    if (e == cudaSuccess) {
+        if (tp > 1) {
+            const d2::TpLayout xl = d2::tp_layout(tp, d.hidden);
+            e = atlas_d2_launch_argmax(reinterpret_cast<const float *>(h->xchg + xl.pmax),
+                                       reinterpret_cast<const uint32_t *>(h->xchg + xl.pidx), tp * d2::kTpPStride, g.st,
+                                       reinterpret_cast<const uint32_t *>(h->xchg + d2::kTpCntHead), arr_hd, h->stream);
+        } else {
+            e = atlas_d2_launch_argmax(h->pmax, h->pidx, hd.grid, g.st, nullptr, 0u, h->stream);
+        }
+        ++kernels;
+    }
     cudaGraph_t graph = nullptr;
     const cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
     if (e != cudaSuccess || e2 != cudaSuccess) {
@@ -718,18 +861,25 @@ int build_graph2(AtlasCuda *h)
 }
 
 // `steps` replays of the step graph from (token, pos); out_ids_dev receives
-// the picks when set (advance mode), else one step's pick is returned.
+// the picks when set (advance mode), else one step's pick is returned. With
+// in_ids_dev (prompt mode) the token after step s is in_ids_dev[s + 1] while
+// there is one. The state's epoch (the exchange sequence) is never rewritten.
 int run_graph2(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
-               float *last_logit)
+               float *last_logit, const uint32_t *in_ids_dev = nullptr, uint32_t n_in = 0)
 {
     AtlasCuda::Graph2 &g = h->g2;
+    if (h->broken)
+        return fail(h, ATLAS_ENCCL, "an earlier tensor-parallel step failed; recreate the handles of all ranks");
+    if (!g.on) return fail(h, ATLAS_EINVAL, "the decode step is not built (tensor parallel: call atlas_cuda_tp_connect)");
     d2::DecState init{};
     init.pos = pos;
     init.token = token;
     init.max_steps = out_ids_dev ? steps : 0u;
     init.advance = 1u;
     init.out_ids = out_ids_dev;
-    CU(h, cudaMemcpyAsync(g.st, &init, sizeof(init), cudaMemcpyHostToDevice, h->stream));
+    init.in_ids = in_ids_dev;
+    init.n_in = n_in;
+    CU(h, cudaMemcpyAsync(g.st, &init, offsetof(d2::DecState, epoch), cudaMemcpyHostToDevice, h->stream));
     CU(h, cudaEventRecord(h->ev0, h->stream));
     for (uint32_t i = 0; i < steps; ++i) CU(h, cudaGraphLaunch(g.exec, h->stream));
     CU(h, cudaEventRecord(h->ev1, h->stream));
@@ -742,10 +892,16 @@ int run_graph2(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
     h->last_ms = ms;
     h->total_ms += ms;
     if (out.status != kStatusOk) {
+        if (h->tp > 1) {
+            // the ranks' exchange counters no longer agree
+            h->broken = true;
+            if (out.status == kStatusPeerTimeout)
+                return fail(h, ATLAS_ENCCL, "a tensor-parallel peer did not arrive (status %u)", out.status);
+            return status_to_code(h, out.status);
+        }
         const int rc = status_to_code(h, out.status);
         // clear what a failed step may have left behind
-        const AtlasModelDesc &d = h->desc;
-        cudaMemsetAsync(g.actr, 0, (size_t)d.kv_heads * 4u, h->stream);
+        cudaMemsetAsync(g.actr, 0, (size_t)h->sl.kv_heads * 4u, h->stream);
         cudaMemsetAsync(g.st, 0, sizeof(d2::DecState), h->stream);
         cudaStreamSynchronize(h->stream);
         return rc;
@@ -758,7 +914,7 @@ int run_graph2(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
 int run_decode(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint32_t *out_ids_dev, uint32_t *last_token,
                float *last_logit)
 {
-    if (h->g2.on) return run_graph2(h, token, pos, steps, out_ids_dev, last_token, last_logit);
+    if (h->g2.on || h->tp > 1) return run_graph2(h, token, pos, steps, out_ids_dev, last_token, last_logit);
     return run_program(h, h->decode, token, pos, steps, out_ids_dev, last_token, last_logit);
 }
 
@@ -1140,6 +1296,8 @@ void atlas_cuda_destroy(AtlasCuda *h)
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->g2.exec) cudaGraphExecDestroy(h->g2.exec);
     if (h->g2.graph) cudaGraphDestroy(h->g2.graph);
+    for (int r = 0; r < (int)d2::kTpMax; ++r)
+        if (h->peer_mapped[r]) cudaIpcCloseMemHandle(h->peer[r]);
     for (void *p : h->allocs) cudaFree(p);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
@@ -1161,8 +1319,17 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
         !d.vocab || d.max_context < 2)
         return fail(nullptr, ATLAS_EINVAL, "unsupported model shape (head_dim must be 128, dims multiples of 256)");
     if (d.has_qk_norm) return fail(nullptr, ATLAS_EINVAL, "qwen3 q/k norm is not supported yet");
-    if (d.tp_size > 1) return fail(nullptr, ATLAS_EINVAL, "tensor parallel handles are created by atlas_cuda_create_tp");
+    const int tp = d.tp_size > 1 ? d.tp_size : 1;
+    AtlasTpSlice sl{0u, d.q_heads, 0u, d.kv_heads, 0u, d.q_dim / 256u, 0u, d.q_dim, 0u, d.ffn, 0u, d.vocab};
+    if (tp > 1) {
+        if (const char *why = tp_slice_of(d, d.tp_rank, tp, sl))
+            return fail(nullptr, ATLAS_EINVAL, "tensor parallel: %s", why);
+        if (d.kv_fp16) return fail(nullptr, ATLAS_EINVAL, "tensor parallel: fp32 KV cache only");
+    }
     AtlasCuda *h = new AtlasCuda();
+    h->tp = tp;
+    h->rank = tp > 1 ? d.tp_rank : 0;
+    h->sl = sl;
     h->desc = d;
     if (h->desc.rms_eps <= 0.f) h->desc.rms_eps = 1e-6f;
     if (h->desc.rope_base <= 0.f) h->desc.rope_base = 1000000.0f;
@@ -1181,31 +1348,38 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     TRY(upload_matrix(h, emb, d.hidden, d.vocab, &h->embd, &h->t_embd));
     const AtlasTensorDesc *outw = find(tensors, n_tensors, "output.weight");
     if (!outw || (outw->data == emb->data && outw->type == emb->type)) {
-        h->head = h->embd;  // tied embeddings: one device copy
+        // tied embeddings: one device copy (a rank's head rows are a row range of it)
+        h->head = h->embd + (uint64_t)sl.vocab_row0 * (d.hidden / 256u) * block_bytes(h->t_embd);
         h->t_head = h->t_embd;
     } else {
-        TRY(upload_matrix(h, outw, d.hidden, d.vocab, &h->head, &h->t_head));
+        TRY(upload_matrix_part(h, outw, d.hidden, d.vocab, sl.vocab_row0, sl.vocab_rows, 0, d.hidden / 256u,
+                               &h->head, &h->t_head));
     }
     TRY(upload_vector(h, find(tensors, n_tensors, "output_norm.weight"), d.hidden, &h->out_norm));
     h->layers.resize(d.layers);
     const size_t esz = d.kv_fp16 ? 2 : 4;
-    const size_t kv_layer = (size_t)d.kv_heads * d.max_context * d.head_dim * esz;
+    const size_t kv_layer = (size_t)sl.kv_heads * d.max_context * d.head_dim * esz;
+    const uint32_t hb = d.hidden / 256u, lq = sl.q_heads * 128u, lkv = sl.kv_heads * 128u;
     for (uint32_t l = 0; l < d.layers; ++l) {
         AtlasCuda::W &w = h->layers[l];
 #define TN(suffix) (snprintf(name, sizeof(name), "blk.%u." suffix, l), find(tensors, n_tensors, name))
-        TRY(upload_matrix(h, TN("attn_q.weight"), d.hidden, d.q_dim, &w.q, &w.tq));
-        TRY(upload_matrix(h, TN("attn_k.weight"), d.hidden, d.kv_dim, &w.k, &w.tk));
-        TRY(upload_matrix(h, TN("attn_v.weight"), d.hidden, d.kv_dim, &w.v, &w.tv));
-        TRY(upload_matrix(h, TN("attn_output.weight"), d.q_dim, d.hidden, &w.o, &w.to));
-        TRY(upload_matrix(h, TN("ffn_gate.weight"), d.hidden, d.ffn, &w.gate, &w.tg));
-        TRY(upload_matrix(h, TN("ffn_up.weight"), d.hidden, d.ffn, &w.up, &w.tu));
-        TRY(upload_matrix(h, TN("ffn_down.weight"), d.ffn, d.hidden, &w.down, &w.td));
+        // the rank's share (the whole tensor without tensor parallelism)
+        TRY(upload_matrix_part(h, TN("attn_q.weight"), d.hidden, d.q_dim, sl.q_head0 * 128u, lq, 0, hb, &w.q, &w.tq));
+        TRY(upload_matrix_part(h, TN("attn_k.weight"), d.hidden, d.kv_dim, sl.kv_head0 * 128u, lkv, 0, hb, &w.k, &w.tk));
+        TRY(upload_matrix_part(h, TN("attn_v.weight"), d.hidden, d.kv_dim, sl.kv_head0 * 128u, lkv, 0, hb, &w.v, &w.tv));
+        TRY(upload_matrix_part(h, TN("attn_output.weight"), d.q_dim, d.hidden, 0, d.hidden, sl.o_block0, sl.o_blocks,
+                               &w.o, &w.to));
+        TRY(upload_matrix_part(h, TN("ffn_gate.weight"), d.hidden, d.ffn, sl.ffn_row0, sl.ffn_rows, 0, hb, &w.gate,
+                               &w.tg));
+        TRY(upload_matrix_part(h, TN("ffn_up.weight"), d.hidden, d.ffn, sl.ffn_row0, sl.ffn_rows, 0, hb, &w.up, &w.tu));
+        TRY(upload_matrix_part(h, TN("ffn_down.weight"), d.ffn, d.hidden, 0, d.hidden, sl.ffn_row0 / 256u,
+                               sl.ffn_rows / 256u, &w.down, &w.td));
         TRY(upload_vector(h, TN("attn_norm.weight"), d.hidden, &w.attn_norm));
         TRY(upload_vector(h, TN("ffn_norm.weight"), d.hidden, &w.ffn_norm));
         // optional_bias: absent biases are skipped (src/brain_runtime.c:1540-1546)
-        if (TN("attn_q.bias")) TRY(upload_vector(h, TN("attn_q.bias"), d.q_dim, &w.bq));
-        if (TN("attn_k.bias")) TRY(upload_vector(h, TN("attn_k.bias"), d.kv_dim, &w.bk));
-        if (TN("attn_v.bias")) TRY(upload_vector(h, TN("attn_v.bias"), d.kv_dim, &w.bv));
+        if (TN("attn_q.bias")) TRY(upload_vector(h, TN("attn_q.bias"), d.q_dim, &w.bq, sl.q_head0 * 128u, lq));
+        if (TN("attn_k.bias")) TRY(upload_vector(h, TN("attn_k.bias"), d.kv_dim, &w.bk, sl.kv_head0 * 128u, lkv));
+        if (TN("attn_v.bias")) TRY(upload_vector(h, TN("attn_v.bias"), d.kv_dim, &w.bv, sl.kv_head0 * 128u, lkv));
 #undef TN
         TRY(dalloc(h, &w.kc, kv_layer));
         TRY(dalloc(h, &w.vc, kv_layer));
@@ -1213,12 +1387,28 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     uint32_t big = d.ffn > d.q_dim ? d.ffn : d.q_dim;
     if (d.hidden > big) big = d.hidden;
     TRY(dalloc(h, &h->x, d.hidden * 4));
-    TRY(dalloc(h, &h->q, d.q_dim * 4));
-    TRY(dalloc(h, &h->k, d.kv_dim * 4));
-    TRY(dalloc(h, &h->v, d.kv_dim * 4));
-    TRY(dalloc(h, &h->att, d.q_dim * 4));
-    TRY(dalloc(h, &h->ffn, (size_t)d.ffn * 4));
-    TRY(dalloc(h, &h->logits, (size_t)d.vocab * 4));
+    TRY(dalloc(h, &h->q, lq * 4));
+    TRY(dalloc(h, &h->k, lkv * 4));
+    TRY(dalloc(h, &h->v, lkv * 4));
+    TRY(dalloc(h, &h->att, d.q_dim * 4));   // all heads' positions; a rank writes its own heads only
+    if (cudaMemset(h->att, 0, d.q_dim * 4) != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "memset failed"));
+    TRY(dalloc(h, &h->ffn, (size_t)sl.ffn_rows * 4));
+    TRY(dalloc(h, &h->logits, (size_t)sl.vocab_rows * 4));
+    if (tp > 1) {
+        TRY(dalloc(h, &h->x2, d.hidden * 4));
+        const d2::TpLayout xl = d2::tp_layout((uint32_t)tp, d.hidden);
+        TRY(dalloc(h, &h->xchg, xl.bytes));
+        std::vector<uint8_t> init(xl.bytes, 0);
+        for (uint32_t i = 0; i < (uint32_t)tp * d2::kTpPStride; ++i) {
+            const float lo = -FLT_MAX;
+            const uint32_t none = 0xffffffffu;
+            memcpy(&init[xl.pmax + 4u * i], &lo, 4);
+            memcpy(&init[xl.pidx + 4u * i], &none, 4);
+        }
+        if (cudaMemcpy(h->xchg, init.data(), xl.bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+            TRY(fail(h, ATLAS_ECUDA, "exchange area upload failed"));
+        h->peer[h->rank] = h->xchg;
+    }
     size_t nsplit_max = (d.max_context + kAttnChunk - 1) / kAttnChunk + 1;
     if (nsplit_max > (size_t)kMaxSplits) nsplit_max = kMaxSplits;
     TRY(dalloc(h, &h->part, (size_t)d.kv_heads * nsplit_max * (d.q_heads / d.kv_heads) * (d.head_dim + 4) * 4));
@@ -1241,13 +1431,14 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
         if (cudaMemcpy(h->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
             TRY(fail(h, ATLAS_ECUDA, "rope upload failed"));
     }
-    TRY(build_decode_program(h));
-    {
+    if (tp == 1) {
+        TRY(build_decode_program(h));
         // graph decode step unless the persistent decode kernel is asked for
         const char *eng = getenv("ATLAS_DECODE_ENGINE");
         if (!eng || strcmp(eng, "persistent") != 0) TRY(build_graph2(h));
+        TRY(alloc_prefill(h));
     }
-    TRY(alloc_prefill(h));
+    // tensor parallel: the decode step is built by atlas_cuda_tp_connect
     if (cudaDeviceSynchronize() != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "device sync failed"));
 #undef TRY
     *out = h;
@@ -1264,7 +1455,9 @@ int atlas_cuda_decode(AtlasCuda *h, uint32_t id, uint32_t pos, float *logits, ui
     int rc = run_decode(h, id, pos, 1, nullptr, &next, nullptr);
     if (rc) return rc;
     if (logits) {
-        CU(h, cudaMemcpyAsync(logits, h->logits, (size_t)h->desc.vocab * 4, cudaMemcpyDeviceToHost, h->stream));
+        // the rank's vocab slice (all of it without tensor parallelism)
+        CU(h, cudaMemcpyAsync(logits + h->sl.vocab_row0, h->logits, (size_t)h->sl.vocab_rows * 4,
+                              cudaMemcpyDeviceToHost, h->stream));
         CU(h, cudaStreamSynchronize(h->stream));
     }
     if (argmax) *argmax = next;
@@ -1305,6 +1498,28 @@ int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t p
     for (uint32_t i = 0; i < n; ++i)
         if (ids[i] >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab %u", ids[i], h->desc.vocab);
     if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    if (h->tp > 1) {
+        // tensor parallel: the prompt token by token through the decode step
+        // (prompt mode: no host work between tokens)
+        if (n > h->in_cap) {
+            uint32_t *p = nullptr;
+            int rc = dalloc(h, &p, (size_t)n * 4);
+            if (rc) return rc;
+            h->d_in_ids = p;
+            h->in_cap = n;
+        }
+        CU(h, cudaMemcpyAsync(h->d_in_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, h->stream));
+        uint32_t next = 0;
+        int rc = run_graph2(h, ids[0], pos0, n, nullptr, &next, nullptr, h->d_in_ids, n);
+        if (rc) return rc;
+        if (last_logits) {
+            CU(h, cudaMemcpyAsync(last_logits + h->sl.vocab_row0, h->logits, (size_t)h->sl.vocab_rows * 4,
+                                  cudaMemcpyDeviceToHost, h->stream));
+            CU(h, cudaStreamSynchronize(h->stream));
+        }
+        if (argmax) *argmax = next;
+        return ATLAS_OK;
+    }
     AtlasCuda::Prefill &p = h->pf;
     CU(h, cudaEventRecord(h->ev0, h->stream));
     for (uint32_t off = 0; off < n; off += p.cap) {
@@ -1348,10 +1563,54 @@ int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t p
     return ATLAS_OK;
 }
 
+int atlas_cuda_tp_slice(const AtlasModelDesc *desc, int rank, int size, AtlasTpSlice *out)
+{
+    if (!desc || !out) return fail(nullptr, ATLAS_EINVAL, "null argument");
+    if (const char *why = tp_slice_of(*desc, rank, size, *out)) return fail(nullptr, ATLAS_EINVAL, "tensor parallel: %s", why);
+    return ATLAS_OK;
+}
+
+int atlas_cuda_tp_handle(AtlasCuda *h, void *out)
+{
+    if (!h || !out) return fail(h, ATLAS_EINVAL, "null argument");
+    if (h->tp < 2 || !h->xchg) return fail(h, ATLAS_EINVAL, "not a tensor-parallel handle");
+    static_assert(sizeof(cudaIpcMemHandle_t) == ATLAS_TP_HANDLE_BYTES, "IPC handle size");
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    cudaIpcMemHandle_t mh;
+    CU(h, cudaIpcGetMemHandle(&mh, h->xchg));
+    memcpy(out, &mh, sizeof(mh));
+    return ATLAS_OK;
+}
+
+int atlas_cuda_tp_connect(AtlasCuda *h, const void *handles)
+{
+    if (!h || !handles) return fail(h, ATLAS_EINVAL, "null argument");
+    if (h->tp < 2) return fail(h, ATLAS_EINVAL, "not a tensor-parallel handle");
+    if (h->g2.on) return fail(h, ATLAS_EINVAL, "already connected");
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    for (int r = 0; r < h->tp; ++r) {
+        if (r == h->rank) continue;
+        cudaIpcMemHandle_t mh;
+        memcpy(&mh, hb + (size_t)r * ATLAS_TP_HANDLE_BYTES, sizeof(mh));
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, mh, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return fail(h, ATLAS_ECUDA, "mapping rank %d's exchange area failed: %s", r, cudaGetErrorString(e));
+        h->peer[r] = static_cast<uint8_t *>(p);
+        h->peer_mapped[r] = true;
+    }
+    const int rc = build_graph2(h);
+    if (rc) return rc;
+    CU(h, cudaDeviceSynchronize());
+    return ATLAS_OK;
+}
+
 int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out_ns, size_t cap, uint32_t *n_ctas,
                           uint32_t *n_phases, uint32_t *phase_kinds)
 {
     if (!h) return fail(h, ATLAS_EINVAL, "null handle");
+    if (h->tp > 1) return fail(h, ATLAS_EINVAL, "tracing covers the single-GPU persistent engine only");
     const size_t np = h->decode.phases.size(), per = (size_t)h->sm_count * np, need = per * 12;
     if (n_ctas) *n_ctas = (uint32_t)h->sm_count;
     if (n_phases) *n_phases = (uint32_t)np;

@@ -284,7 +284,8 @@ int atlas_rt_open(const char *path, const AtlasRtOptions *opt, AtlasRuntime **ou
     d.kv_heads = s->kv_heads; d.head_dim = s->head_dim; d.ffn = s->ffn_size; d.layers = s->layers;
     d.vocab = s->vocab_size; d.max_context = s->max_context; d.max_prefill = o.max_prefill;
     d.rope_base = s->rope_base; d.rms_eps = 1.0e-6f; d.has_qk_norm = s->has_qk_norm;
-    d.kv_fp16 = o.kv_fp16; d.device = o.device; d.tp_rank = 0; d.tp_size = 1;
+    d.kv_fp16 = o.kv_fp16; d.device = o.device;
+    d.tp_rank = o.tp_size > 1 ? o.tp_rank : 0; d.tp_size = o.tp_size > 1 ? o.tp_size : 1;
     rc = atlas_cuda_create(&d, td, n, &rt->dev);
     free(td);
     if (rc) rt_fail(rt, rc, "%s", atlas_cuda_last_error(NULL));

@@ -27,7 +27,8 @@ EXPORTS = [
     "atlas_cuda_create", "atlas_cuda_destroy", "atlas_cuda_last_error", "atlas_cuda_prefill",
     "atlas_cuda_decode", "atlas_cuda_generate", "atlas_cuda_stats", "atlas_cuda_dequant",
     "atlas_cuda_gemv", "atlas_cuda_gemm", "atlas_cuda_device_info", "atlas_cuda_trace_step",
-    "atlas_cuda_device_ms", "atlas_cuda_gemv_noalloc",
+    "atlas_cuda_device_ms", "atlas_cuda_gemv_noalloc", "atlas_cuda_tp_slice", "atlas_cuda_tp_handle",
+    "atlas_cuda_tp_connect",
     "brain_gpu_init", "brain_gpu_matvec_batch", "brain_gpu_matvec", "brain_gpu_shutdown",
     "atlas_rt_open", "atlas_rt_close", "atlas_rt_error", "atlas_rt_shape", "atlas_rt_data_base",
     "atlas_rt_find_tensor", "atlas_rt_file_bytes", "atlas_rt_device", "atlas_rt_forward_token",
@@ -63,7 +64,30 @@ class TensorInfo(ctypes.Structure):
 
 class RtOptions(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("max_context", ctypes.c_uint32), ("max_prefill", ctypes.c_uint32),
-                ("kv_fp16", ctypes.c_int32), ("no_device", ctypes.c_int32)]
+                ("kv_fp16", ctypes.c_int32), ("no_device", ctypes.c_int32), ("tp_rank", ctypes.c_int32),
+                ("tp_size", ctypes.c_int32)]
+
+
+class ModelDesc(ctypes.Structure):
+    """AtlasModelDesc (include/atlas_cuda.h)."""
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                ("hidden", "q_dim", "kv_dim", "q_heads", "kv_heads", "head_dim", "ffn", "layers", "vocab",
+                 "max_context", "max_prefill")] + [
+        ("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)] + [
+        (n, ctypes.c_int32) for n in ("has_qk_norm", "kv_fp16", "device", "tp_rank", "tp_size")]
+
+
+class TpSlice(ctypes.Structure):
+    """AtlasTpSlice: one tensor-parallel rank's share of the model."""
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                ("q_head0", "q_heads", "kv_head0", "kv_heads", "o_block0", "o_blocks", "o_lo", "o_hi",
+                 "ffn_row0", "ffn_rows", "vocab_row0", "vocab_rows")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+TP_HANDLE_BYTES = 64
 
 
 class BrainGpuMatvec(ctypes.Structure):
@@ -95,6 +119,9 @@ def lib() -> ctypes.CDLL:
         L.atlas_cuda_stats.argtypes = [P, P, P]
         L.atlas_cuda_device_ms.argtypes = [P, P]
         L.atlas_cuda_trace_step.argtypes = [P, U32, U32, P, ctypes.c_size_t, P, P, P]
+        L.atlas_cuda_tp_slice.argtypes = [P, I32, I32, P]
+        L.atlas_cuda_tp_handle.argtypes = [P, P]
+        L.atlas_cuda_tp_connect.argtypes = [P, P]
         L.atlas_rt_open.argtypes = [ctypes.c_char_p, P, P]
         L.atlas_rt_close.argtypes = [P]
         L.atlas_rt_error.restype = ctypes.c_char_p
@@ -160,9 +187,10 @@ class Runtime:
     """Reference-shaped model API: open a GGUF, forward tokens, prefill, generate."""
 
     def __init__(self, path: str, *, device: int = 0, max_context: int = 0, max_prefill: int = 0,
-                 kv_fp16: bool = False, no_device: bool = False):
+                 kv_fp16: bool = False, no_device: bool = False, tp_rank: int = 0, tp_size: int = 1):
         self._h = ctypes.c_void_p()
-        opt = RtOptions(device, max_context, max_prefill, int(kv_fp16), int(no_device))
+        opt = RtOptions(device, max_context, max_prefill, int(kv_fp16), int(no_device), tp_rank, tp_size)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         rc = lib().atlas_rt_open(path.encode(), ctypes.byref(opt), ctypes.byref(self._h))
         if rc != ATLAS_OK:
             msg = lib().atlas_rt_error(self._h).decode()
@@ -221,6 +249,27 @@ class Runtime:
                                           _ptr(kinds)), "trace_step", dev)
         return buf[:per * 4].reshape(nc.value, nph.value, 4), buf[per * 4:].reshape(nc.value, nph.value, 8), kinds
 
+    def tp_slice(self) -> TpSlice:
+        """This rank's share of the model (the whole model without tensor parallelism)."""
+        s = self.shape
+        return tp_slice(dict(hidden=s.hidden_size, q_heads=s.q_heads, kv_heads=s.kv_heads, ffn=s.ffn_size,
+                             vocab=s.vocab_size), self.tp_rank, self.tp_size)
+
+    def tp_handle(self) -> bytes:
+        """The exchange area of this rank, to hand to every other rank."""
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        dev = lib().atlas_rt_device(self._h)
+        check(lib().atlas_cuda_tp_handle(dev, buf), "atlas_cuda_tp_handle", dev)
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """handles: every rank's tp_handle() in rank order; builds the decode step."""
+        if len(handles) != self.tp_size or any(len(b) != TP_HANDLE_BYTES for b in handles):
+            raise ValueError("tp_connect needs tp_size handles of TP_HANDLE_BYTES bytes")
+        buf = ctypes.create_string_buffer(b"".join(handles), TP_HANDLE_BYTES * self.tp_size)
+        dev = lib().atlas_rt_device(self._h)
+        check(lib().atlas_cuda_tp_connect(dev, buf), "atlas_cuda_tp_connect", dev)
+
     def stats(self):
         """(kernel launches since creation, device ms of the last call, device ms of all calls)."""
         n = ctypes.c_uint64()
@@ -247,6 +296,26 @@ class Runtime:
             self.close()
         except Exception:
             pass
+
+
+def tp_slice(shape: dict, rank: int, size: int) -> TpSlice:
+    """atlas_cuda_tp_slice for a shape given as hidden / q_heads / kv_heads / ffn / vocab."""
+    d = ModelDesc()
+    d.hidden, d.q_heads, d.kv_heads, d.ffn, d.vocab = (shape[k] for k in ("hidden", "q_heads", "kv_heads", "ffn",
+                                                                           "vocab"))
+    d.head_dim, d.q_dim, d.kv_dim = 128, 128 * d.q_heads, 128 * d.kv_heads
+    out = TpSlice()
+    check(lib().atlas_cuda_tp_slice(ctypes.byref(d), rank, size, ctypes.byref(out)), "atlas_cuda_tp_slice")
+    return out
+
+
+def connect_tp(rt: "Runtime", group=None) -> None:
+    """Exchange the ranks' handles through torch.distributed (any backend:
+    the handles are 64 host bytes each) and connect this rank's runtime."""
+    import torch.distributed as dist
+    handles = [None] * rt.tp_size
+    dist.all_gather_object(handles, rt.tp_handle(), group=group)
+    rt.tp_connect(handles)
 
 
 def dequant(type_id: int, d_blocks, nblocks: int, d_out, stream: int = 0) -> None:

@@ -48,10 +48,13 @@ def cmd_gemv(a):
 
 
 def cmd_trace(a):
-    path = os.path.join(tempfile.gettempdir(), f"atlas_trace_{a.hidden}_{a.layers}_{a.ffn}_{a.vocab}.gguf")
+    tag = "u" if a.untied else "t"
+    path = os.path.join(tempfile.gettempdir(),
+                        f"atlas_trace_{a.hidden}_{a.layers}_{a.q_heads}_{a.kv_heads}_{a.ffn}_{a.vocab}{tag}.gguf")
     if not os.path.exists(path):
         atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
-                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1,
+                                        tied=not a.untied)
     with atlas_cuda.Runtime(path, max_context=a.pos + 16) as rt:
         rt.prefill(np.arange(1, a.pos + 1, dtype=np.uint32) % a.vocab, 0, want_logits=False)
         tr, ext, kinds = rt.trace_step(7, a.pos)
@@ -105,10 +108,13 @@ def cmd_gemm(a):
 
 
 def cmd_prefill(a):
-    path = os.path.join(tempfile.gettempdir(), f"atlas_trace_{a.hidden}_{a.layers}_{a.ffn}_{a.vocab}.gguf")
+    tag = "u" if a.untied else "t"
+    path = os.path.join(tempfile.gettempdir(),
+                        f"atlas_trace_{a.hidden}_{a.layers}_{a.q_heads}_{a.kv_heads}_{a.ffn}_{a.vocab}{tag}.gguf")
     if not os.path.exists(path):
         atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
-                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1,
+                                        tied=not a.untied)
     ids = (np.arange(1, a.tokens + 1, dtype=np.uint32) * 7919) % a.vocab
     with atlas_cuda.Runtime(path, max_context=a.tokens + 16, max_prefill=a.tokens) as rt:
         rt.prefill(ids, 0, want_logits=False)
@@ -127,10 +133,13 @@ def cmd_decode(a):
     """Prefill a random prompt, then `steps` greedy decode steps through the
     graph decode step; prints the device time per token of a 64-step run
     unless --steps-only (then only the `steps` steps run: a capture target)."""
-    path = os.path.join(tempfile.gettempdir(), f"atlas_trace_{a.hidden}_{a.layers}_{a.ffn}_{a.vocab}.gguf")
+    tag = "u" if a.untied else "t"
+    path = os.path.join(tempfile.gettempdir(),
+                        f"atlas_trace_{a.hidden}_{a.layers}_{a.q_heads}_{a.kv_heads}_{a.ffn}_{a.vocab}{tag}.gguf")
     if not os.path.exists(path):
         atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
-                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1)
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1,
+                                        tied=not a.untied)
     ids = np.random.default_rng(1).integers(0, a.vocab, a.prompt).astype(np.uint32)
     with atlas_cuda.Runtime(path, max_context=a.prompt + a.steps + 80, max_prefill=a.prompt) as rt:
         _, first = rt.prefill(ids, 0, want_logits=False)
@@ -161,6 +170,7 @@ def main():
     p.add_argument("--vocab", type=int, default=151936)
     p.add_argument("--tokens", type=int, default=512)
     p.add_argument("--reps", type=int, default=5)
+    p.add_argument("--untied", action="store_true", help="separate Q6_K output head")
     g = sub.add_parser("gemv")
     g.add_argument("--type", type=int, default=14)
     g.add_argument("--rows", type=int, default=151936)
@@ -174,6 +184,7 @@ def main():
     t.add_argument("--ffn", type=int, default=11008)
     t.add_argument("--vocab", type=int, default=151936)
     t.add_argument("--pos", type=int, default=600)
+    t.add_argument("--untied", action="store_true", help="separate Q6_K output head")
     dcd = sub.add_parser("decode")
     dcd.add_argument("--hidden", type=int, default=2048)
     dcd.add_argument("--layers", type=int, default=36)
@@ -184,6 +195,7 @@ def main():
     dcd.add_argument("--prompt", type=int, default=512)
     dcd.add_argument("--steps", type=int, default=3)
     dcd.add_argument("--steps-only", action="store_true")
+    dcd.add_argument("--untied", action="store_true", help="separate Q6_K output head")
     a = ap.parse_args()
     {"gemv": cmd_gemv, "trace": cmd_trace, "gemm": cmd_gemm, "prefill": cmd_prefill, "decode": cmd_decode}[a.cmd](a)
 

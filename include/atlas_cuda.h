@@ -33,7 +33,7 @@ enum {
     ATLAS_ENOMEM = -3,   /* device or host allocation failed */
     ATLAS_ECUDA = -4,    /* a CUDA runtime call failed */
     ATLAS_ETIMEOUT = -5, /* a bounded device-side wait ran out (status read back, context intact) */
-    ATLAS_ENCCL = -6,    /* a collective failed */
+    ATLAS_ENCCL = -6,    /* a tensor-parallel exchange failed (a peer never arrived) */
     ATLAS_ERANGE = -7    /* position / token / size beyond what the handle was created for */
 };
 
@@ -72,9 +72,8 @@ typedef struct {
     int32_t has_qk_norm;   /* qwen3 per-head q/k RMSNorm (src/brain_runtime.c:1727-1737) */
     int32_t kv_fp16;       /* 0: fp32 KV cache (default), 1: fp16 KV cache (see below) */
     int32_t device;        /* CUDA device ordinal */
-    int32_t tp_rank;       /* tensor-parallel rank, 0..tp_size-1 */
-    int32_t tp_size;       /* 1, 2, 4 or 8; >1 needs nccl_comm */
-    void *nccl_comm;       /* ncclComm_t spanning the tp_size ranks, or NULL */
+    int32_t tp_rank;       /* tensor-parallel rank, 0..tp_size-1 (one process per GPU) */
+    int32_t tp_size;       /* 1, or 2 / 4 / 8 when kv_heads % tp_size == 0 (see atlas_cuda_tp_*) */
 } AtlasModelDesc;
 
 /* KV-cache precision: the reference keeps K and V in fp32 (src/brain_runtime.c:2019-2020).
@@ -121,6 +120,43 @@ int atlas_cuda_device_ms(const AtlasCuda *h, double *total_ms);
    n_ctas / n_phases / phase_kinds (kind * 16 + epilogue) describe the layout. */
 int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out_ns, size_t cap,
                           uint32_t *n_ctas, uint32_t *n_phases, uint32_t *phase_kinds);
+
+/* ---- tensor parallelism (one process per GPU, tp_size ranks) ----
+
+   The layout of the reference's forward_token across ranks: query heads with
+   their KV heads (and the KV cache) split by KV head; attn_q/k/v, ffn_gate/up
+   and the output head split by rows; attn_output and ffn_down split by their
+   256-column blocks, each rank summing its partial rows; every partial sum
+   is exchanged over peer memory (NVLink) inside the decode kernels and added
+   in rank order, so all ranks hold the same residual stream and pick the
+   same token. Create the handle with desc.tp_rank / tp_size, export its
+   exchange area with atlas_cuda_tp_handle, give every rank all ranks'
+   handles (rank order) through atlas_cuda_tp_connect, then call
+   prefill / decode / generate on every rank with the same arguments.
+   Logits outputs receive only the rank's vocab slice (vocab_row0 ..
+   vocab_row0 + vocab_rows - 1; other entries are left untouched). Prompts
+   run token by token through the decode step. A failed step (ATLAS_ENCCL /
+   ATLAS_ETIMEOUT) leaves the ranks out of step: destroy and recreate all.
+   Destroy the handles only after every rank finished its last call. */
+
+typedef struct {
+    uint32_t q_head0, q_heads;        /* query heads of the rank */
+    uint32_t kv_head0, kv_heads;      /* KV heads (and their cache) */
+    uint32_t o_block0, o_blocks;      /* 256-column blocks of attn_output.weight the rank reads */
+    uint32_t o_lo, o_hi;              /* the rank's attention-output elements inside those blocks */
+    uint32_t ffn_row0, ffn_rows;      /* ffn_gate / ffn_up rows, = ffn_down columns (256-multiples) */
+    uint32_t vocab_row0, vocab_rows;  /* output.weight rows: the rank's logits */
+} AtlasTpSlice;
+
+#define ATLAS_TP_HANDLE_BYTES 64
+
+/* The slice of rank `rank` of `size` for a model shape (no device needed). */
+int atlas_cuda_tp_slice(const AtlasModelDesc *desc, int rank, int size, AtlasTpSlice *out);
+/* The handle's exchange area as ATLAS_TP_HANDLE_BYTES bytes to give the other ranks. */
+int atlas_cuda_tp_handle(AtlasCuda *h, void *out);
+/* handles: tp_size * ATLAS_TP_HANDLE_BYTES bytes in rank order (this rank's own
+   entry included). Maps the peers' exchange areas and builds the decode step. */
+int atlas_cuda_tp_connect(AtlasCuda *h, const void *handles);
 
 /* ---- stateless kernels over caller-owned DEVICE memory (parity tests) ---- */
 

@@ -52,6 +52,8 @@ typedef struct {
     uint32_t max_prefill;  /* 0: 512 */
     int32_t kv_fp16;       /* 1: fp16 KV cache instead of fp32 (atlas_cuda.h) */
     int32_t no_device;     /* 1: parse only (no GPU work) */
+    int32_t tp_rank;       /* tensor parallel: this process's rank ... */
+    int32_t tp_size;       /* ... of tp_size (0 or 1: one GPU); see atlas_cuda_tp_* */
 } AtlasRtOptions;
 
 int atlas_rt_open(const char *path, const AtlasRtOptions *opt, AtlasRuntime **out);

@@ -109,3 +109,40 @@ def test_cfg0_full_size_matches_reference(torch_cuda, model_dir):
         picks = rt.generate(am1, len(prompt) + 1, 30)
         got = np.concatenate([[am, am1], picks]).astype(np.uint32)
         np.testing.assert_array_equal(got, g["picks"])
+
+
+WIDE = {
+    # Qwen2.5-7B and -14B layer widths (2 of their 28 / 48 layers), untied Q6_K head
+    "7b_width": dict(hidden=3584, layers=2, q_heads=28, kv_heads=4, ffn=18944, vocab=152064,
+                     context_length=1024, seed=77),
+    "14b_width": dict(hidden=5120, layers=2, q_heads=40, kv_heads=8, ffn=13824, vocab=152064,
+                      context_length=1024, seed=78),
+}
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", sorted(WIDE))
+def test_wide_shapes_match_oracle(torch_cuda, oracle, model_dir, name):
+    """Full-width layers of the 7B / 14B shapes (rows longer than 8 blocks on every
+    projection, 7 and 5 query heads per KV head, vocab 152064): prompt logits and
+    32 greedy steps against the oracle."""
+    cfg = WIDE[name]
+    p = os.path.join(str(model_dir), f"{name}.gguf")
+    if not os.path.exists(p):
+        atlas_cuda.write_synthetic_gguf(p, tied=False, **cfg)
+    m = oracle.open(p)
+    m.begin(128)
+    prompt = np.random.default_rng(cfg["seed"]).integers(0, cfg["vocab"], 12).astype(np.uint32)
+    for i, t in enumerate(prompt):
+        want = m.forward(int(t), i, i + 1 == len(prompt))
+    want_picks, lg = [], want
+    for s in range(32):
+        want_picks.append(m.argmax(lg))
+        if s < 31:
+            lg = m.forward(want_picks[-1], len(prompt) + s)
+    with atlas_cuda.Runtime(p, max_context=128) as rt:
+        got, am = rt.prefill(prompt)
+        _close(got, want, 1e-3)
+        assert am == want_picks[0]
+        picks = rt.generate(am, len(prompt), 31)
+        np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
