@@ -152,6 +152,62 @@ def cmd_decode(a):
     print(f"decode at position {a.prompt}: {ms:.4f} ms per token, {1e3 / ms:.1f} tok/s")
 
 
+def cmd_tp(a):
+    """Tensor-parallel decode, one rank per process (launch under
+    torch.distributed.run): prefill a random prompt through the TP prompt mode,
+    then time `steps` greedy decode steps; rank 0 prints each rank's device
+    time per token and the per-GPU HBM rate of the rank's share."""
+    import datetime
+    import torch.distributed as dist
+    if "RANK" not in os.environ:   # one rank without a launcher
+        import socket
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        os.environ.update(RANK="0", WORLD_SIZE="1", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    path = os.path.join(tempfile.gettempdir(),
+                        f"atlas_trace_{a.hidden}_{a.layers}_{a.q_heads}_{a.kv_heads}_{a.ffn}_{a.vocab}u.gguf")
+    if rank == 0 and not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, hidden=a.hidden, layers=a.layers, q_heads=a.q_heads,
+                                        kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1, tied=False)
+    dist.barrier()
+    ids = np.random.default_rng(1).integers(0, a.vocab, a.prompt).astype(np.uint32)
+    rt = atlas_cuda.Runtime(path, device=int(os.environ.get("LOCAL_RANK", rank)),
+                            max_context=a.prompt + 2 * a.steps + 8, tp_rank=rank, tp_size=world)
+    if world > 1:
+        atlas_cuda.connect_tp(rt)
+    dist.barrier()
+    _, first = rt.prefill(ids, 0, want_logits=False)
+    prompt_ms = rt.stats()[1]
+    picks = rt.generate(first, a.prompt, a.steps)           # warm-up
+    rt.generate(int(picks[-1]), a.prompt + a.steps, a.steps)
+    ms = rt.stats()[1] / a.steps
+    sl = rt.tp_slice()
+    h, f, q, kv, L = a.hidden, a.ffn, a.q_heads * 128, a.kv_heads * 128, a.layers
+    q4, q6 = 144 / 256, 210 / 256
+    # this rank's weight bytes per token (o and down: its blocks) + its KV read at the mean position
+    lq, lkv = sl.q_heads * 128, sl.kv_heads * 128
+    layer = (lq + lkv) * h * q4 + lkv * h * q6 + h * sl.o_blocks * 256 * q4 + 2 * sl.ffn_rows * h * q4 + \
+        h * sl.ffn_rows * q6
+    pos = a.prompt + 1.5 * a.steps
+    rank_bytes = L * layer + sl.vocab_rows * h * q6 + L * 2 * lkv * 4 * pos
+    got = [None] * world
+    dist.all_gather_object(got, (ms, rank_bytes, prompt_ms))
+    dist.barrier()
+    rt.close()
+    if rank == 0:
+        worst = max(g[0] for g in got)
+        print(f"tp {world}: {h}x{L} layers, q/kv heads {a.q_heads}/{kv // 128}, ffn {f}, vocab {a.vocab}")
+        for r, (m, b, pm) in enumerate(got):
+            print(f"  rank {r}: {m:.4f} ms per token, {b / 1e9:.3f} GB per token -> {b / m / 1e6:.0f} GB/s "
+                  f"(prompt {a.prompt} tokens {pm:.1f} ms)")
+        print(f"decode {1e3 / worst:.1f} tok/s (slowest rank {worst:.4f} ms per token)")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -196,8 +252,18 @@ def main():
     dcd.add_argument("--steps", type=int, default=3)
     dcd.add_argument("--steps-only", action="store_true")
     dcd.add_argument("--untied", action="store_true", help="separate Q6_K output head")
+    tpp = sub.add_parser("tp")
+    tpp.add_argument("--hidden", type=int, default=3584)
+    tpp.add_argument("--layers", type=int, default=28)
+    tpp.add_argument("--q-heads", type=int, default=28)
+    tpp.add_argument("--kv-heads", type=int, default=4)
+    tpp.add_argument("--ffn", type=int, default=18944)
+    tpp.add_argument("--vocab", type=int, default=152064)
+    tpp.add_argument("--prompt", type=int, default=512)
+    tpp.add_argument("--steps", type=int, default=64)
     a = ap.parse_args()
-    {"gemv": cmd_gemv, "trace": cmd_trace, "gemm": cmd_gemm, "prefill": cmd_prefill, "decode": cmd_decode}[a.cmd](a)
+    {"gemv": cmd_gemv, "trace": cmd_trace, "gemm": cmd_gemm, "prefill": cmd_prefill, "decode": cmd_decode,
+     "tp": cmd_tp}[a.cmd](a)
 
 
 if __name__ == "__main__":
