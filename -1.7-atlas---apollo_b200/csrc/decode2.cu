@@ -65,9 +65,12 @@ struct __align__(16) MvHdr {
 
 __host__ __device__ constexpr uint32_t mv_hdr_bytes() { return align128((uint32_t)sizeof(MvHdr)); }
 __host__ __device__ constexpr uint32_t mv_tcnt_bytes(uint32_t tslots) { return (tslots * 4u + 15u) & ~15u; }
+// per-warp partial rows of an open tile, rows kTpRow floats apart so that the
+// cooperative finish (lane = (warp k, row, segment)) reads distinct banks
+constexpr uint32_t kTpRow = kMvRows + 1u;
 __host__ __device__ constexpr uint32_t mv_tile_bytes(uint32_t tslots)
 {
-    return align128(mv_tcnt_bytes(tslots) + tslots * 2u * kMvWarps * kMvRows * 4u);
+    return align128(mv_tcnt_bytes(tslots) + tslots * 2u * kMvWarps * kTpRow * 4u);
 }
 // Per ring slot: one descriptor per task - ring offset of the task's block in
 // the run's first copy, copy stride | row stride << 16, tile, segment | run
@@ -80,7 +83,7 @@ __host__ __device__ constexpr uint32_t mv_x_bytes(uint32_t cols) { return align1
 
 __device__ __forceinline__ float *tpart_at(const MvHdr *h, uint32_t ts, uint32_t s, uint32_t w)
 {
-    return h->tpart + ((ts * 2u + s) * kMvWarps + w) * kMvRows;
+    return h->tpart + ((ts * 2u + s) * kMvWarps + w) * kTpRow;
 }
 
 // One (tile, segment) run of n block columns inside a ring slot. A run of
@@ -444,7 +447,7 @@ __device__ void mv_flush(const MvArgs &a, MvHdr *h, const MvCta &c, uint32_t t, 
         const volatile float *tp = tpart_at(h, ts, s, 0) + i;
 #pragma unroll
         for (uint32_t w = 0; w < (uint32_t)kMvWarps; ++w)
-            if (TP >= (uint32_t)kMvWarps || ((w + kMvWarps - w0) % kMvWarps) < TP) v[s] += tp[w * (uint32_t)kMvRows];
+            if (TP >= (uint32_t)kMvWarps || ((w + kMvWarps - w0) % kMvWarps) < TP) v[s] += tp[w * kTpRow];
         v[s] *= out_scale;
     }
     __syncwarp();
@@ -547,14 +550,24 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     uint32_t cur = 0xffffffffu, cur_lc[2] = {0u, 0u};
     float pre = 0.f;
-    for (uint32_t i = warp; i < c.j1 - c.j0; i += kMvWarps) {   // task positions w + 8m
+    uint32_t ready = 0u;        // lane 0: this slot's copies were already seen complete
+    const uint32_t L = c.j1 - c.j0;
+    for (uint32_t i = warp; i < L; i += kMvWarps) {   // task positions w + 8m
         uint32_t ok = 1u;
-        if (lane == 0) ok = mbar_wait(&h->full[ri], ph, err) ? 1u : 0u;
+        if (lane == 0 && !ready) ok = mbar_wait(&h->full[ri], ph, err) ? 1u : 0u;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) return false;
         const uint4 dsc = h->desc[ri * 8u + u];
         const uint32_t t = dsc.z, s = dsc.w & 15u, run = (dsc.w >> 4) & 15u, lc = (dsc.w >> 8) & 15u, b = dsc.w >> 16;
         const uint32_t cstride = dsc.y & 0xffffu, rstride = dsc.y >> 16;
+        // probe the next slot now; the answer is used one task later
+        uint32_t rn = ri + step, pn = ph;
+        while (rn >= a.nslot) {
+            rn -= a.nslot;
+            pn ^= 1u;
+        }
+        ready = 0u;
+        if (lane == 0 && i + kMvWarps < L) ready = mbar_test(&h->full[rn], pn) ? 1u : 0u;
         if (t != cur) {
             if (cur != 0xffffffffu) mv_flush(a, h, c, cur, cur_lc, acc, out_scale, pre, best);
             cur = t;
@@ -591,11 +604,8 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
             acc[0][0] += o0;
             acc[0][1] += o1;
         }
-        ri += step;
-        while (ri >= a.nslot) {
-            ri -= a.nslot;
-            ph ^= 1u;
-        }
+        ri = rn;
+        ph = pn;
     }
     if (cur != 0xffffffffu) mv_flush(a, h, c, cur, cur_lc, acc, out_scale, pre, best);
     return true;
