@@ -741,7 +741,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
         return;
     }
     const uint32_t n = pos + 1u;
-    const uint32_t ns = min(a.splits, (n + kAttnMinSpan - 1u) / kAttnMinSpan);
+    const uint32_t ms = a.min_span ? a.min_span : kAttnMinSpan;
+    const uint32_t ns = min(a.splits, (n + ms - 1u) / ms);
     const uint32_t span = (n + ns - 1u) / ns;
     const uint32_t kvh = blockIdx.x / a.splits, s = blockIdx.x % a.splits;
     if (s >= ns) return;
@@ -984,6 +985,46 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *pmax, const ui
     st->epoch = st->epoch + 1u;
 }
 
+// ------------------------------------------- prefill all-reduce (TP) ----
+
+// Reduce-scatter + all-gather of a prefill chunk's partial rows over peer
+// memory, one cooperative launch (all CTAs resident: they wait on counters
+// that this GPU's CTAs also feed). Every rank takes an equal slice of the
+// float4 elements, adds the ranks' partials in rank order to its residual
+// and stores the sums into every rank's residual; the ready counter (one
+// arrival per rank) says every partial is written, the done counter (one
+// arrival per CTA of every rank) says every slice has landed and nobody
+// reads this rank's partials any more.
+__global__ void __launch_bounds__(256) tp_allreduce_kernel(const __grid_constant__ TpReduceArgs a)
+{
+    uint8_t *own = a.peer[a.rank];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        __threadfence_system();
+        for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + kTpCntReady), 1u);
+    }
+    if (threadIdx.x == 0)
+        wait_counter_sys(reinterpret_cast<const uint32_t *>(own + kTpCntReady), a.seq * a.tp, a.status);
+    __syncthreads();
+    const uint32_t s0 = (uint32_t)((uint64_t)a.n4 * a.rank / a.tp), s1 = (uint32_t)((uint64_t)a.n4 * (a.rank + 1u) / a.tp);
+    const float4 *xr = reinterpret_cast<const float4 *>(own + a.px);
+    for (uint32_t e = s0 + blockIdx.x * blockDim.x + threadIdx.x; e < s1; e += gridDim.x * blockDim.x) {
+        float4 v = __ldcg(xr + e);
+        for (uint32_t q = 0; q < a.tp; ++q) {
+            const float4 *pq = reinterpret_cast<const float4 *>(a.peer[q] + a.part) + e;
+            const float4 w = q == a.rank ? __ldcg(pq) : __ldcv(pq);
+            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+        }
+        for (uint32_t p = 0; p < a.tp; ++p) reinterpret_cast<float4 *>(a.peer[p] + a.px)[e] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + kTpCntDone), 1u);
+        wait_counter_sys(reinterpret_cast<const uint32_t *>(own + kTpCntDone), a.seq * a.tp * gridDim.x, a.status);
+    }
+    __syncthreads();
+}
+
 }  // namespace d2
 }  // namespace atlas
 
@@ -1056,4 +1097,12 @@ extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t 
 {
     void *args[] = {&pmax, &pidx, &n, &st, &cnt, &arrivals};
     return launch_ex((const void *)argmax_kernel, args, dim3(1), dim3(256), 0, stream, true);
+}
+
+// grid: CTAs of the cooperative launch (the same on every rank)
+extern "C" cudaError_t atlas_tp_allreduce(const TpReduceArgs *a, uint32_t grid, cudaStream_t stream)
+{
+    TpReduceArgs copy = *a;
+    void *args[] = {&copy};
+    return cudaLaunchCooperativeKernel((const void *)tp_allreduce_kernel, dim3(grid), dim3(256), args, 0, stream);
 }

@@ -43,22 +43,41 @@ struct DecState {
 // complete when the counter reaches k * arrivals (mod 2^32).
 constexpr uint32_t kTpMax = 8;
 constexpr uint32_t kTpPStride = 256;    // per-rank (max, row) slots, >= CTAs of the head launch
-constexpr uint32_t kTpCntO = 0, kTpCntDn = 4, kTpCntHead = 8;   // counter byte offsets
+constexpr uint32_t kTpCntO = 0, kTpCntDn = 4, kTpCntHead = 8;   // counter byte offsets (decode)
+constexpr uint32_t kTpCntReady = 12, kTpCntDone = 16;            // prefill exchange counters
 
+// Decode slots, then the prefill regions: the rank's partial rows of a
+// row-split contraction [tmax][hidden] and the residual stream [tmax][hidden]
+// (peers write their reduced slices into it).
 struct TpLayout {
-    uint32_t red_o, red_dn, pmax, pidx, bytes;   // byte offsets / total size
+    uint32_t red_o, red_dn, pmax, pidx;
+    uint64_t part, px, bytes;   // byte offsets / total size
 };
 
-__host__ __device__ inline TpLayout tp_layout(uint32_t tp, uint32_t hidden)
+__host__ __device__ inline TpLayout tp_layout(uint32_t tp, uint32_t hidden, uint32_t tmax = 0)
 {
     TpLayout l{};
     l.red_o = 128u;
     l.red_dn = l.red_o + ((tp * hidden * 4u + 127u) & ~127u);
     l.pmax = l.red_dn + ((tp * hidden * 4u + 127u) & ~127u);
     l.pidx = l.pmax + tp * kTpPStride * 4u;
-    l.bytes = l.pidx + tp * kTpPStride * 4u;
+    l.part = (l.pidx + tp * kTpPStride * 4u + 255u) & ~255u;
+    l.px = l.part + (((uint64_t)tmax * hidden * 4u + 255u) & ~uint64_t(255));
+    l.bytes = l.px + (uint64_t)tmax * hidden * 4u;
     return l;
 }
+
+// One all-reduce of a prefill chunk's partial rows (tokens x hidden floats):
+// every rank adds all ranks' partials, in rank order, to its residual slice
+// and writes the sums into every rank's residual.
+struct TpReduceArgs {
+    uint8_t *peer[kTpMax];
+    uint32_t tp, rank;
+    uint64_t part, px;          // region offsets (TpLayout)
+    uint32_t n4;                // float4 elements (tokens * hidden / 4)
+    uint32_t seq;               // occurrence number of this all-reduce (1, 2, ...)
+    uint32_t *status;
+};
 
 // ------------------------------------------------------------ mv kernel ----
 //
@@ -144,6 +163,7 @@ struct AttnArgs {
     const float2 *rope;         // (cos, sin) [position][64]
     DecState *st;
     uint32_t q_heads, kv_heads, max_context, splits, kv_fp16;
+    uint32_t min_span;          // cached positions per split, at least (0: kAttnMinSpan)
 };
 
 }  // namespace d2

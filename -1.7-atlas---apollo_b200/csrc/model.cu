@@ -48,6 +48,7 @@ extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_b
 extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n,
                                               atlas::d2::DecState *st, const uint32_t *cnt, uint32_t arrivals,
                                               cudaStream_t stream);
+extern "C" cudaError_t atlas_tp_allreduce(const atlas::d2::TpReduceArgs *a, uint32_t grid, cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_wbound(uint32_t type, const uint8_t *blocks, uint64_t nblocks, uint32_t *out_bits,
                                            cudaStream_t stream);
 
@@ -136,6 +137,7 @@ struct AtlasCuda {
     float *x2 = nullptr;
     uint32_t *d_in_ids = nullptr;
     uint32_t in_cap = 0;
+    uint32_t pf_seq = 0;   // prefill all-reduces run so far (their exchange occurrence numbers)
     bool broken = false;   // a failed tensor-parallel step left the ranks out of step
 };
 
@@ -794,6 +796,7 @@ int build_graph2(AtlasCuda *h)
     at.max_context = d.max_context;
     at.splits = g.splits;
     at.kv_fp16 = d.kv_fp16 ? 1u : 0u;
+    if (const char *e = getenv("ATLAS_ATTN_MIN_SPAN")) at.min_span = (uint32_t)std::max(1, atoi(e));
 
     const uint64_t embd_row = (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
     CU(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
@@ -1019,11 +1022,13 @@ int compute_weight_exponents(AtlasCuda *h)
     CU(h, cudaMemsetAsync(bits, 0, n * 4, h->stream));
     for (uint32_t l = 0; l < d.layers; ++l) {
         const AtlasCuda::W &w = h->layers[l];
+        const AtlasTpSlice &sl = h->sl;
+        const uint64_t lq = sl.q_heads * 128ull, lkv = sl.kv_heads * 128ull;
         const struct { const uint8_t *p; uint32_t t; uint64_t elems; } m[7] = {
-            {w.q, w.tq, (uint64_t)d.q_dim * d.hidden},   {w.k, w.tk, (uint64_t)d.kv_dim * d.hidden},
-            {w.v, w.tv, (uint64_t)d.kv_dim * d.hidden},  {w.o, w.to, (uint64_t)d.hidden * d.q_dim},
-            {w.gate, w.tg, (uint64_t)d.ffn * d.hidden}, {w.up, w.tu, (uint64_t)d.ffn * d.hidden},
-            {w.down, w.td, (uint64_t)d.hidden * d.ffn}};
+            {w.q, w.tq, lq * d.hidden},   {w.k, w.tk, lkv * d.hidden},
+            {w.v, w.tv, lkv * d.hidden},  {w.o, w.to, (uint64_t)d.hidden * sl.o_blocks * 256u},
+            {w.gate, w.tg, (uint64_t)sl.ffn_rows * d.hidden}, {w.up, w.tu, (uint64_t)sl.ffn_rows * d.hidden},
+            {w.down, w.td, (uint64_t)d.hidden * sl.ffn_rows}};
         for (int i = 0; i < 7; ++i)
             CU(h, atlas_launch_wbound(m[i].t, m[i].p, m[i].elems / 256, bits + l * 7 + i, h->stream));
     }
@@ -1059,11 +1064,20 @@ int alloc_prefill(AtlasCuda *h)
     }
     const uint32_t G = (uint32_t)h->sm_count, tok_tiles = p.tok_pad / pf::kTokTile;
     const uint32_t max_cols = std::max(d.hidden, std::max(d.q_dim, d.ffn));
+    const AtlasTpSlice &sl = h->sl;
     int rc;
-    if ((rc = dalloc(h, &p.x, (size_t)p.cap * d.hidden * 4))) return rc;
-    if ((rc = dalloc(h, &p.q, (size_t)p.cap * d.q_dim * 4))) return rc;
+    if (h->tp > 1) {
+        // the residual stream lives in the exchange area: peers write their reduced slices into it
+        const d2::TpLayout xl = d2::tp_layout((uint32_t)h->tp, d.hidden, d.max_prefill);
+        p.x = reinterpret_cast<float *>(h->xchg + xl.px);
+    } else if ((rc = dalloc(h, &p.x, (size_t)p.cap * d.hidden * 4))) {
+        return rc;
+    }
+    if ((rc = dalloc(h, &p.q, (size_t)p.cap * sl.q_heads * 128u * 4))) return rc;
+    // all heads' positions (a rank writes its own heads; the others stay zero)
     if ((rc = dalloc(h, &p.att, (size_t)p.cap * d.q_dim * 4))) return rc;
-    if ((rc = dalloc(h, &p.ffn, (size_t)p.cap * d.ffn * 4))) return rc;
+    CU(h, cudaMemset(p.att, 0, (size_t)p.cap * d.q_dim * 4));
+    if ((rc = dalloc(h, &p.ffn, (size_t)p.cap * sl.ffn_rows * 4))) return rc;
     if ((rc = dalloc(h, &p.xt, (size_t)tok_tiles * (max_cols / pf::kKBlock) * pf::kXTileBytes))) return rc;
     if ((rc = dalloc(h, &p.xscale, (size_t)p.tok_pad * 4))) return rc;
     // split-K partials: a split contraction runs at most one unit per CTA pair,
@@ -1082,6 +1096,8 @@ int alloc_prefill(AtlasCuda *h)
     if ((rc = dalloc(h, &p.ids, (size_t)p.cap * 4))) return rc;
     if ((rc = dalloc(h, &p.status, 256))) return rc;
     CU(h, cudaMemset(p.status, 0, 256));
+    // tensor parallel: the last prompt token runs through the decode step
+    if (h->tp > 1) return compute_weight_exponents(h);
     // tail program: rms_norm + head GEMV + argmax over x (the last token's row)
     std::vector<Phase> &P = p.tail.phases;
     Phase hd = gemv_phase(d.hidden, G, h->stage_bytes, false,
@@ -1161,11 +1177,11 @@ int launch_gemm(AtlasCuda *h, pf::GemmArgs &a, uint32_t cols, uint32_t tokens, u
     return ATLAS_OK;
 }
 
-int launch_split(AtlasCuda *h, const float *x, uint32_t cols, uint32_t tokens, const float *norm_w)
+int launch_split(AtlasCuda *h, const float *x, uint32_t cols, uint32_t tokens, const float *norm_w, uint32_t ldx = 0)
 {
     const uint32_t tok_pad = (tokens + pf::kPairTokens - 1) / pf::kPairTokens * pf::kPairTokens;
-    CU(h, atlas_launch_prefill_split(x, cols, cols, tokens, tok_pad, norm_w, h->desc.rms_eps, h->pf.xt, h->pf.xscale,
-                                     h->stream));
+    CU(h, atlas_launch_prefill_split(x, ldx ? ldx : cols, cols, tokens, tok_pad, norm_w, h->desc.rms_eps, h->pf.xt,
+                                     h->pf.xscale, h->stream));
     ++h->launches;
     return ATLAS_OK;
 }
@@ -1176,16 +1192,17 @@ int launch_split(AtlasCuda *h, const float *x, uint32_t cols, uint32_t tokens, c
 int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
 {
     const AtlasModelDesc &d = h->desc;
+    const AtlasTpSlice &sl = h->sl;
     const uint32_t G = (uint32_t)h->sm_count, qt_n = (n + 7) / 8;
     uint64_t chunks = 0;
     for (uint32_t qt = 0; qt < qt_n; ++qt) chunks += (pos0 + std::min(8 * qt + 8, n) + 63) / 64;
-    chunks *= d.kv_heads;
+    chunks *= sl.kv_heads;
     uint32_t span_chunks = (uint32_t)std::max<uint64_t>(1, (chunks + 3 * G - 1) / (3 * G));
     std::vector<uint32_t> tab;
     for (;;) {
         tab.clear();
         const uint32_t span = 64 * span_chunks;
-        for (uint32_t g = 0; g < d.kv_heads; ++g)
+        for (uint32_t g = 0; g < sl.kv_heads; ++g)
             for (uint32_t qt = 0; qt < qt_n; ++qt) {
                 const uint32_t kend = pos0 + std::min(8 * qt + 8, n), parts = (kend + span - 1) / span;
                 for (uint32_t s = 0; s < parts; ++s) tab.push_back(g | (qt << 8) | (s << 20));
@@ -1198,14 +1215,17 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
     CU(h, cudaStreamSynchronize(h->stream));
     a = pf::AttnArgs{};
     a.q = h->pf.q;
-    a.out = h->pf.att;
+    // the rank's heads at their places in the all-heads rows
+    a.out = h->pf.att + (size_t)sl.q_head0 * 128u;
+    a.out_stride = d.q_dim;
+    a.kv_f16 = d.kv_fp16 ? 1u : 0u;
     a.part = h->pf.apart;
     a.ctr = h->pf.actr;
     a.status = h->pf.status;
     a.tokens = n;
     a.pos0 = pos0;
-    a.q_heads = d.q_heads;
-    a.kv_heads = d.kv_heads;
+    a.q_heads = sl.q_heads;
+    a.kv_heads = sl.kv_heads;
     a.max_context = d.max_context;
     a.q_tiles = qt_n;
     a.span = 64 * span_chunks;
@@ -1220,7 +1240,10 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
 int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
 {
     const AtlasModelDesc &d = h->desc;
+    const AtlasTpSlice &sl = h->sl;
     AtlasCuda::Prefill &p = h->pf;
+    const bool tp = h->tp > 1;
+    const uint32_t lq = sl.q_heads * 128u, lkv = sl.kv_heads * 128u, o_cols = sl.o_blocks * 256u;
     CU(h, cudaMemcpyAsync(p.ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, h->stream));
     CU(h, atlas_launch_prefill_embed(p.ids, n, h->embd, h->t_embd,
                                      (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd), d.hidden,
@@ -1229,6 +1252,27 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
     pf::AttnArgs at;
     int rc = plan_attention(h, n, pos0, at);
     if (rc) return rc;
+    // tensor parallel: o and down leave partial rows in the exchange area, the
+    // all-reduce adds every rank's to the residual
+    d2::TpReduceArgs ar{};
+    float *part = nullptr;
+    if (tp) {
+        const d2::TpLayout xl = d2::tp_layout((uint32_t)h->tp, d.hidden, d.max_prefill);
+        for (int r = 0; r < h->tp; ++r) ar.peer[r] = h->peer[r];
+        ar.tp = (uint32_t)h->tp;
+        ar.rank = (uint32_t)h->rank;
+        ar.part = xl.part;
+        ar.px = xl.px;
+        ar.n4 = n * d.hidden / 4u;
+        ar.status = p.status;
+        part = reinterpret_cast<float *>(h->xchg + xl.part);
+    }
+    auto allreduce = [&]() -> int {
+        ar.seq = ++h->pf_seq;
+        CU(h, atlas_tp_allreduce(&ar, (uint32_t)h->sm_count, h->stream));
+        ++h->launches;
+        return ATLAS_OK;
+    };
     const uint64_t cache_head = (uint64_t)d.max_context * d.head_dim;
     for (uint32_t l = 0; l < d.layers; ++l) {
         const AtlasCuda::W &w = h->layers[l];
@@ -1238,37 +1282,42 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
         pf::GemmArgs g{};
         g.epi = pf::GEPI_STORE;
         g.n_seg = 3;
-        g.seg[0] = gseg(w.q, w.tq, d.q_dim, d.hidden, w.eq, w.bq, p.q, 128, d.q_dim, 0, true);
-        g.seg[1] = gseg(w.k, w.tk, d.kv_dim, d.hidden, w.ek, w.bk, kc, cache_head, d.head_dim, pos0, true);
-        g.seg[2] = gseg(w.v, w.tv, d.kv_dim, d.hidden, w.ev, w.bv, vc, cache_head, d.head_dim, pos0, false);
+        g.seg[0] = gseg(w.q, w.tq, lq, d.hidden, w.eq, w.bq, p.q, 128, lq, 0, true);
+        g.seg[1] = gseg(w.k, w.tk, lkv, d.hidden, w.ek, w.bk, kc, cache_head, d.head_dim, pos0, true);
+        g.seg[2] = gseg(w.v, w.tv, lkv, d.hidden, w.ev, w.bv, vc, cache_head, d.head_dim, pos0, false);
+        g.seg[1].f16 = g.seg[2].f16 = d.kv_fp16 ? 1u : 0u;   // element offsets either way
         if ((rc = launch_gemm(h, g, d.hidden, n, pos0))) return rc;
         at.k_cache = kc;
         at.v_cache = vc;
         CU(h, atlas_launch_prefill_attn(&at, (int)std::min<uint32_t>(at.n_units, (uint32_t)h->sm_count), h->stream));
         ++h->launches;
-        if ((rc = launch_split(h, p.att, d.q_dim, n, nullptr))) return rc;
+        // the rank's attn_output blocks (other ranks' heads in them are zero)
+        if ((rc = launch_split(h, p.att + (size_t)sl.o_block0 * 256u, o_cols, n, nullptr, d.q_dim))) return rc;
         g = pf::GemmArgs{};
-        g.epi = pf::GEPI_RESID;
+        g.epi = tp ? pf::GEPI_STORE : pf::GEPI_RESID;
         g.n_seg = 1;
-        g.seg[0] = gseg(w.o, w.to, d.hidden, d.q_dim, w.eo, nullptr, p.x, 128, d.hidden, 0, false);
-        if ((rc = launch_gemm(h, g, d.q_dim, n, pos0))) return rc;
+        g.seg[0] = gseg(w.o, w.to, d.hidden, o_cols, w.eo, nullptr, tp ? part : p.x, 128, d.hidden, 0, false);
+        if ((rc = launch_gemm(h, g, o_cols, n, pos0))) return rc;
+        if (tp && (rc = allreduce())) return rc;
         // feed-forward block: rms_norm -> gate, up -> SwiGLU -> down (+residual)
         if ((rc = launch_split(h, p.x, d.hidden, n, w.ffn_norm))) return rc;
         g = pf::GemmArgs{};
         g.epi = pf::GEPI_SWIGLU;
         g.n_seg = 2;
-        g.seg[0] = gseg(w.gate, w.tg, d.ffn, d.hidden, w.eg, nullptr, p.ffn, 128, d.ffn, 0, false);
-        g.seg[1] = gseg(w.up, w.tu, d.ffn, d.hidden, w.eu, nullptr, nullptr, 0, 0, 0, false);
+        g.seg[0] = gseg(w.gate, w.tg, sl.ffn_rows, d.hidden, w.eg, nullptr, p.ffn, 128, sl.ffn_rows, 0, false);
+        g.seg[1] = gseg(w.up, w.tu, sl.ffn_rows, d.hidden, w.eu, nullptr, nullptr, 0, 0, 0, false);
         if ((rc = launch_gemm(h, g, d.hidden, n, pos0))) return rc;
-        if ((rc = launch_split(h, p.ffn, d.ffn, n, nullptr))) return rc;
+        if ((rc = launch_split(h, p.ffn, sl.ffn_rows, n, nullptr))) return rc;
         g = pf::GemmArgs{};
-        g.epi = pf::GEPI_RESID;
+        g.epi = tp ? pf::GEPI_STORE : pf::GEPI_RESID;
         g.n_seg = 1;
-        g.seg[0] = gseg(w.down, w.td, d.hidden, d.ffn, w.ed, nullptr, p.x, 128, d.hidden, 0, false);
-        if ((rc = launch_gemm(h, g, d.ffn, n, pos0))) return rc;
+        g.seg[0] = gseg(w.down, w.td, d.hidden, sl.ffn_rows, w.ed, nullptr, tp ? part : p.x, 128, d.hidden, 0, false);
+        if ((rc = launch_gemm(h, g, sl.ffn_rows, n, pos0))) return rc;
+        if (tp && (rc = allreduce())) return rc;
     }
-    CU(h, cudaMemcpyAsync(h->x, p.x + (size_t)(n - 1) * d.hidden, (size_t)d.hidden * 4, cudaMemcpyDeviceToDevice,
-                          h->stream));
+    if (!tp)
+        CU(h, cudaMemcpyAsync(h->x, p.x + (size_t)(n - 1) * d.hidden, (size_t)d.hidden * 4, cudaMemcpyDeviceToDevice,
+                              h->stream));
     return ATLAS_OK;
 }
 
@@ -1396,16 +1445,17 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     TRY(dalloc(h, &h->logits, (size_t)sl.vocab_rows * 4));
     if (tp > 1) {
         TRY(dalloc(h, &h->x2, d.hidden * 4));
-        const d2::TpLayout xl = d2::tp_layout((uint32_t)tp, d.hidden);
+        const d2::TpLayout xl = d2::tp_layout((uint32_t)tp, d.hidden, h->desc.max_prefill);
         TRY(dalloc(h, &h->xchg, xl.bytes));
-        std::vector<uint8_t> init(xl.bytes, 0);
+        if (cudaMemset(h->xchg, 0, xl.bytes) != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "memset failed"));
+        std::vector<uint8_t> init((size_t)(xl.part - xl.pmax), 0);
         for (uint32_t i = 0; i < (uint32_t)tp * d2::kTpPStride; ++i) {
             const float lo = -FLT_MAX;
             const uint32_t none = 0xffffffffu;
-            memcpy(&init[xl.pmax + 4u * i], &lo, 4);
-            memcpy(&init[xl.pidx + 4u * i], &none, 4);
+            memcpy(&init[4u * i], &lo, 4);
+            memcpy(&init[xl.pidx - xl.pmax + 4u * i], &none, 4);
         }
-        if (cudaMemcpy(h->xchg, init.data(), xl.bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (cudaMemcpy(h->xchg + xl.pmax, init.data(), init.size(), cudaMemcpyHostToDevice) != cudaSuccess)
             TRY(fail(h, ATLAS_ECUDA, "exchange area upload failed"));
         h->peer[h->rank] = h->xchg;
     }
@@ -1436,8 +1486,8 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
         // graph decode step unless the persistent decode kernel is asked for
         const char *eng = getenv("ATLAS_DECODE_ENGINE");
         if (!eng || strcmp(eng, "persistent") != 0) TRY(build_graph2(h));
-        TRY(alloc_prefill(h));
     }
+    TRY(alloc_prefill(h));
     // tensor parallel: the decode step is built by atlas_cuda_tp_connect
     if (cudaDeviceSynchronize() != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "device sync failed"));
 #undef TRY
@@ -1499,19 +1549,33 @@ int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t p
         if (ids[i] >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab %u", ids[i], h->desc.vocab);
     if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
     if (h->tp > 1) {
-        // tensor parallel: the prompt token by token through the decode step
-        // (prompt mode: no host work between tokens)
-        if (n > h->in_cap) {
-            uint32_t *p = nullptr;
-            int rc = dalloc(h, &p, (size_t)n * 4);
+        // tensor parallel: all but the last token through the batched
+        // contractions (partial rows all-reduced over peer memory), then the
+        // last one through the decode step (its layers, the split head and
+        // the greedy pick across ranks)
+        if (h->broken) return fail(h, ATLAS_ENCCL, "an earlier tensor-parallel step failed; recreate all ranks");
+        if (!h->g2.on) return fail(h, ATLAS_EINVAL, "tensor parallel: call atlas_cuda_tp_connect first");
+        AtlasCuda::Prefill &p = h->pf;
+        CU(h, cudaEventRecord(h->ev0, h->stream));
+        for (uint32_t off = 0; off + 1 < n; off += p.cap) {
+            const int rc = prefill_chunk(h, ids + off, std::min(p.cap, n - 1 - off), pos0 + off);
             if (rc) return rc;
-            h->d_in_ids = p;
-            h->in_cap = n;
         }
-        CU(h, cudaMemcpyAsync(h->d_in_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, h->stream));
+        CU(h, cudaEventRecord(h->ev1, h->stream));
+        uint32_t st = 0;
+        CU(h, cudaMemcpyAsync(&st, p.status, 4, cudaMemcpyDeviceToHost, h->stream));
+        CU(h, cudaStreamSynchronize(h->stream));
+        float pms = 0.f;
+        cudaEventElapsedTime(&pms, h->ev0, h->ev1);
+        if (st != kStatusOk) {
+            h->broken = true;
+            return status_to_code(h, st);
+        }
         uint32_t next = 0;
-        int rc = run_graph2(h, ids[0], pos0, n, nullptr, &next, nullptr, h->d_in_ids, n);
+        int rc = run_graph2(h, ids[n - 1], pos0 + n - 1, 1, nullptr, &next, nullptr);
         if (rc) return rc;
+        h->last_ms += pms;
+        h->total_ms += pms;
         if (last_logits) {
             CU(h, cudaMemcpyAsync(last_logits + h->sl.vocab_row0, h->logits, (size_t)h->sl.vocab_rows * 4,
                                   cudaMemcpyDeviceToHost, h->stream));

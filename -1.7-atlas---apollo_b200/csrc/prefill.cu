@@ -422,6 +422,42 @@ __device__ __forceinline__ void load8(const float *p, float (&y)[8], uint32_t n,
     }
 }
 
+__device__ __forceinline__ float4 h4_to_f4(uint2 u)
+{
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// Store n of 8 values at element e of a segment's output (fp32, or binary16
+// for an fp16 KV cache).
+__device__ __forceinline__ void put8(const GemmSeg &g, size_t e, const float (&y)[8], uint32_t n)
+{
+    if (!g.f16) {
+        store8(g.out + e, y, n, g.vec4 != 0);
+        return;
+    }
+    __half *p = reinterpret_cast<__half *>(g.out) + e;
+    if (g.vec4 && n == 8u) {
+        uint4 u;
+        u.x = pack_h2(y[0], y[1]);
+        u.y = pack_h2(y[2], y[3]);
+        u.z = pack_h2(y[4], y[5]);
+        u.w = pack_h2(y[6], y[7]);
+        *reinterpret_cast<uint4 *>(p) = u;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if ((uint32_t)j < n) p[j] = __float2half_rn(y[j]);
+    }
+}
+
+__device__ __forceinline__ void put1(const GemmSeg &g, size_t e, float y)
+{
+    if (g.f16) reinterpret_cast<__half *>(g.out)[e] = __float2half_rn(y);
+    else g.out[e] = y;
+}
+
 // --------------------------------------------------------------- kernel ----
 
 template <int TERMS>
@@ -723,8 +759,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_ke
                                 va[j] = __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y));
                                 vb[j] = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
                             }
-                            store8(o + (ra >> 7) * g.head_stride + (ra & 127u), va, na, g.vec4 != 0);
-                            store8(o + (rb >> 7) * g.head_stride + (rb & 127u), vb, nb, g.vec4 != 0);
+                            const size_t et = (size_t)(t + g.tok_off) * g.tok_stride;
+                            put8(g, et + (ra >> 7) * g.head_stride + (ra & 127u), va, na);
+                            put8(g, et + (rb >> 7) * g.head_stride + (rb & 127u), vb, nb);
                         }
                 } else {
                     for (uint32_t c = 0; c < (uint32_t)kRowTile; c += 8) {
@@ -739,12 +776,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_ke
                             load8(p, x, n, g.vec4 != 0);   // residual stream, src/brain_runtime.c:1745, :1762
 #pragma unroll
                             for (int j = 0; j < 8; ++j) v[j] = x[j] + v[j] * s;
+                            store8(p, v, n, g.vec4 != 0);
                         } else {
 #pragma unroll
                             for (int j = 0; j < 8; ++j)
                                 v[j] = v[j] * s + ((g.bias && (uint32_t)j < n) ? __ldg(g.bias + r0 + j) : 0.f);
+                            put8(g, (size_t)(t + g.tok_off) * g.tok_stride + (r0 >> 7) * g.head_stride + (r0 & 127u), v, n);
                         }
-                        store8(p, v, n, g.vec4 != 0);
                     }
                 }
             }
@@ -825,8 +863,9 @@ __global__ void __launch_bounds__(256) splitk_kernel(const __grid_constant__ Gem
                 const float2 r = __ldg(cs + ((c + (uint32_t)j) & 63u));
                 const float x0 = va[j] * s + (g.bias ? __ldg(g.bias + ra) : 0.f);
                 const float x1 = vb[j] * s + (g.bias ? __ldg(g.bias + rb) : 0.f);
-                o[(ra >> 7) * g.head_stride + (ra & 127u)] = __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y));
-                o[(rb >> 7) * g.head_stride + (rb & 127u)] = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
+                const size_t et = (size_t)(t + g.tok_off) * g.tok_stride;
+                put1(g, et + (ra >> 7) * g.head_stride + (ra & 127u), __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y)));
+                put1(g, et + (rb >> 7) * g.head_stride + (rb & 127u), __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x)));
             }
             continue;
         }
@@ -842,7 +881,7 @@ __global__ void __launch_bounds__(256) splitk_kernel(const __grid_constant__ Gem
             float y = va[j] * s;
             if (a.epi == GEPI_RESID) y = prev[j] + y;   // src/brain_runtime.c:1745, :1762
             else if (g.bias) y += __ldg(g.bias + r);
-            o[(r >> 7) * g.head_stride + (r & 127u)] = y;
+            put1(g, (size_t)(t + g.tok_off) * g.tok_stride + (r >> 7) * g.head_stride + (r & 127u), y);
         }
     }
 }
@@ -980,6 +1019,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(const __grid_constant__ At
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw);
     const uint32_t tid = threadIdx.x, ty = tid >> 4, tx = tid & 15u;
     const uint32_t group = a.q_heads / a.kv_heads, qdim = a.q_heads * 128u;
+    const uint32_t ostride = a.out_stride ? a.out_stride : qdim;
     const float scale = 1.0f / sqrtf(128.0f);
     for (uint32_t u = blockIdx.x; u < a.n_units; u += gridDim.x) {
         const uint32_t code = a.unit_tab[u];
@@ -1012,8 +1052,13 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(const __grid_constant__ At
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (pos < k1) {
                 const size_t off = ((size_t)g * a.max_context + pos) * 128u;
-                kv = __ldcg(reinterpret_cast<const float4 *>(a.k_cache + off) + d4);
-                vv = __ldcg(reinterpret_cast<const float4 *>(a.v_cache + off) + d4);
+                if (a.kv_f16) {
+                    kv = h4_to_f4(__ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(a.k_cache) + off) + d4));
+                    vv = h4_to_f4(__ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(a.v_cache) + off) + d4));
+                } else {
+                    kv = __ldcg(reinterpret_cast<const float4 *>(a.k_cache + off) + d4);
+                    vv = __ldcg(reinterpret_cast<const float4 *>(a.v_cache + off) + d4);
+                }
             }
             *reinterpret_cast<float4 *>(&sm.k[j][4 * d4]) = kv;
             *reinterpret_cast<float4 *>(&sm.v[j][4 * d4]) = vv;
@@ -1093,7 +1138,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(const __grid_constant__ At
             for (int r = 0; r < 4; ++r) {
                 const uint32_t row = 4 * ty + (uint32_t)r, qi = row / group, h = row % group;
                 if (row >= kQT * group || t0 + qi >= t1) continue;
-                float *dst = a.out + (size_t)(t0 + qi) * qdim + (size_t)(g * group + h) * 128u + 8u * tx;
+                float *dst = a.out + (size_t)(t0 + qi) * ostride + (size_t)(g * group + h) * 128u + 8u * tx;
                 const float inv = l[r] > 0.f ? 1.0f / l[r] : 0.f;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) dst[j] = o[r][j] * inv;
@@ -1139,7 +1184,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(const __grid_constant__ At
                 for (int j = 0; j < 8; ++j) acc[j] = fmaf(f, __ldcg(rec + 8 * tx + j), acc[j]);
             }
             const float inv = L > 0.f ? 1.0f / L : 0.f;
-            float *dst = a.out + (size_t)(t0 + qi) * qdim + (size_t)(g * group + h) * 128u + 8u * tx;
+            float *dst = a.out + (size_t)(t0 + qi) * ostride + (size_t)(g * group + h) * 128u + 8u * tx;
 #pragma unroll
             for (int j = 0; j < 8; ++j) dst[j] = acc[j] * inv;
         }

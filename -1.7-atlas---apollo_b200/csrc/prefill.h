@@ -62,6 +62,7 @@ struct GemmSeg {
     uint32_t tok_off;
     uint32_t tile0;        // first row tile of this segment
     uint32_t vec4;         // out, head_stride and tok_stride keep 16-float groups 16-byte aligned
+    uint32_t f16;          // out holds binary16 (an fp16 KV cache); offsets count elements
 };
 
 struct GemmArgs {
@@ -97,6 +98,8 @@ struct AttnArgs {
     uint32_t n_units;
     const uint32_t *unit_tab;   // per unit: g | query tile << 8 | span index << 20;
                                 // the spans of one (g, tile) are consecutive
+    uint32_t out_stride;        // floats between tokens of out (0: q_heads * 128)
+    uint32_t kv_f16;            // the KV cache holds binary16
 };
 
 }  // namespace pf

@@ -141,14 +141,17 @@ def cmd_decode(a):
                                         kv_heads=a.kv_heads, ffn=a.ffn, vocab=a.vocab, seed=1,
                                         tied=not a.untied)
     ids = np.random.default_rng(1).integers(0, a.vocab, a.prompt).astype(np.uint32)
-    with atlas_cuda.Runtime(path, max_context=a.prompt + a.steps + 80, max_prefill=a.prompt) as rt:
+    with atlas_cuda.Runtime(path, max_context=a.prompt + a.steps + 80, max_prefill=min(a.prompt, a.chunk),
+                            kv_fp16=a.kv_fp16) as rt:
         _, first = rt.prefill(ids, 0, want_logits=False)
+        pre_ms = rt.stats()[1]
         rt.generate(first, a.prompt, a.steps)
         if a.steps_only:
             return
         d0 = rt.stats()[2]
         rt.generate(first, a.prompt, 64)
         ms = (rt.stats()[2] - d0) / 64
+    print(f"prefill {a.prompt} tokens: {pre_ms:.2f} ms ({a.prompt / pre_ms * 1e3:.0f} tok/s)")
     print(f"decode at position {a.prompt}: {ms:.4f} ms per token, {1e3 / ms:.1f} tok/s")
 
 
@@ -252,6 +255,8 @@ def main():
     dcd.add_argument("--steps", type=int, default=3)
     dcd.add_argument("--steps-only", action="store_true")
     dcd.add_argument("--untied", action="store_true", help="separate Q6_K output head")
+    dcd.add_argument("--kv-fp16", action="store_true", help="fp16 KV cache")
+    dcd.add_argument("--chunk", type=int, default=512, help="prefill chunk (max_prefill)")
     tpp = sub.add_parser("tp")
     tpp.add_argument("--hidden", type=int, default=3584)
     tpp.add_argument("--layers", type=int, default=28)

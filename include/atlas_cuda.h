@@ -135,7 +135,9 @@ int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out
    prefill / decode / generate on every rank with the same arguments.
    Logits outputs receive only the rank's vocab slice (vocab_row0 ..
    vocab_row0 + vocab_rows - 1; other entries are left untouched). Prompts
-   run token by token through the decode step. A failed step (ATLAS_ENCCL /
+   run batched on every rank's shards (the partial rows of attn_output and
+   ffn_down all-reduced over peer memory), their last token through the
+   decode step. A failed step (ATLAS_ENCCL /
    ATLAS_ETIMEOUT) leaves the ranks out of step: destroy and recreate all.
    Destroy the handles only after every rank finished its last call. */
 

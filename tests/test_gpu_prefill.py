@@ -171,3 +171,22 @@ def test_gemv_input_near_fp32_underflow(torch_cuda, oracle):
         got = d_y.cpu().numpy()
         assert np.isfinite(got).all()
         assert np.abs(got.astype(np.float64) - want).max() <= 1e-4 * np.abs(want).max() + 1e-30
+
+
+def test_prefill_fp16_kv_cache_matches_decode_loop(torch_cuda, small_model):
+    """fp16 KV cache: the batched prefill (K/V stored as binary16 by the
+    contraction epilogue, read back as binary16 by the prompt attention, in
+    chunks that straddle the cache) matches a token-by-token decode loop over
+    the same fp16 cache, and generation continues from either identically."""
+    prompt = np.random.default_rng(3).integers(0, 4096, 150).astype(np.uint32)
+    with atlas_cuda.Runtime(small_model, max_context=256, max_prefill=64, kv_fp16=True) as rt:
+        lg, am = rt.prefill(prompt)
+        a = rt.generate(am, len(prompt), 8)
+    with atlas_cuda.Runtime(small_model, max_context=256, max_prefill=64, kv_fp16=True) as rt:
+        for i, t in enumerate(prompt):
+            want, am2 = rt.forward(int(t), i, i + 1 == len(prompt))
+        b = rt.generate(am2, len(prompt), 8)
+    err = np.abs(lg.astype(np.float64) - want).max()
+    assert err <= 1e-3 * np.abs(want).max(), f"max|dlogit| {err}"
+    assert am == am2
+    np.testing.assert_array_equal(a, b)
