@@ -691,11 +691,11 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
 
 struct __align__(16) AttnSmem {
     float4 q[kAttnMaxGroup][32];        // RoPE'd queries of the group (128 dims)
-    uint8_t k[kAttnTile * 512];         // staged K rows, as stored in the cache (fp32 or fp16)
-    uint8_t v[kAttnTile * 512];         // staged V rows
+    uint8_t k[2][kAttnTile * 512];      // staged K rows, as stored in the cache (fp32 or fp16), two tiles
+    uint8_t v[2][kAttnTile * 512];      // staged V rows
     float4 knew[32], vnew[32];          // the current token's RoPE'd k and its v
     float cden[kAttnMaxGroup];
-    uint64_t bar;                       // tile arrival
+    uint64_t bar[2];                    // tile arrival, per buffer
     uint32_t flag;
 };
 // followed by the combine weights cw[splits][kAttnMaxGroup]
@@ -721,9 +721,10 @@ __device__ __forceinline__ float warp_maxf(float v)
 // src/brain_runtime.c:1482-1528), one CTA per (KV head, split). The splits in
 // use grow with the context (at least kAttnMinSpan positions each). A split's
 // cached K and V rows are contiguous in the cache, so each tile of up to
-// kAttnTile positions arrives as two bulk copies; the first is issued before
-// waiting for the preceding kernel (cached rows and the step's position were
-// written by earlier steps). Every warp takes one query head of the group,
+// kAttnTile positions arrives as two bulk copies into one of two buffers: the
+// tile after the current one is always in flight, and the first two are
+// issued before waiting for the preceding kernel (cached rows and the step's
+// position were written by earlier steps). Every warp takes one query head of the group,
 // lane = 4 of the 128 dimensions: one warp reduction per position's score,
 // online softmax per chunk of 32 positions, P.V. The
 // split holding the current position applies RoPE to the fresh k and
@@ -755,20 +756,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
     const float scale = 1.0f / sqrtf(128.0f);
     volatile uint32_t *err = &a.st->status;
     const size_t head_row0 = (size_t)kvh * a.max_context;
-    // tile [tb, tb + kAttnTile) of the split: cached rows [tb, min(te, pos)) by bulk copies
-    auto issue = [&](uint32_t tb) {
+    // tile [tb, tb + kAttnTile) of the split into buffer b: cached rows
+    // [tb, min(te, pos)) by bulk copies; two tiles are in flight
+    auto issue = [&](uint32_t tb, uint32_t b) {
         const uint32_t te = min(tb + kAttnTile, t1), ce = max(tb, min(te, pos));
         const uint32_t bytes = (ce - tb) * rowb;
-        mbar_arrive_expect_tx(&sm.bar, 2u * bytes);
+        mbar_arrive_expect_tx(&sm.bar[b], 2u * bytes);
         if (bytes) {
-            bulk_g2s(sm.k, reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar);
-            bulk_g2s(sm.v, reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar);
+            bulk_g2s(sm.k[b], reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar[b]);
+            bulk_g2s(sm.v[b], reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar[b]);
         }
     };
     if (threadIdx.x == 0) {
-        mbar_init(&sm.bar, 1u);
+        mbar_init(&sm.bar[0], 1u);
+        mbar_init(&sm.bar[1], 1u);
         fence_mbar_init();
-        if (t0 < t1) issue(t0);
+        if (t0 < t1) issue(t0, 0u);
+        if (t0 + kAttnTile < t1) issue(t0 + kAttnTile, 1u);
     }
     __syncthreads();
     pdl_wait();
@@ -807,10 +811,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
     }
     float m = -FLT_MAX, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    uint32_t phase = 0;
-    for (uint32_t tb = t0; tb < t1; tb += kAttnTile, phase ^= 1u) {
-        const uint32_t te = min(tb + kAttnTile, t1);
-        mbar_wait(&sm.bar, phase, err);
+    uint32_t it = 0;
+    for (uint32_t tb = t0; tb < t1; tb += kAttnTile, ++it) {
+        const uint32_t te = min(tb + kAttnTile, t1), b = it & 1u;
+        const uint8_t *kt = sm.k[b], *vt = sm.v[b];
+        mbar_wait(&sm.bar[b], (it >> 1) & 1u, err);
         if (warp < group) {
             // lane = 4 of the 128 dimensions; scores of up to 32 positions,
             // one warp reduction each (lane p keeps position p's score), then
@@ -822,7 +827,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
 #pragma unroll 4
                 for (uint32_t jj = 0; jj < np; ++jj) {
                     const uint32_t p = sb + jj;
-                    const float4 kv = p == pos ? sm.knew[lane] : kv_row4(sm.k + (size_t)(p - tb) * rowb, lane, f16);
+                    const float4 kv = p == pos ? sm.knew[lane] : kv_row4(kt + (size_t)(p - tb) * rowb, lane, f16);
                     float d = fmaf(qv.x, kv.x, qv.y * kv.y) + fmaf(qv.z, kv.z, qv.w * kv.w);
                     d = warp_sum(d);
                     if (lane == jj) sc = d * scale;
@@ -836,7 +841,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
                 for (uint32_t jj = 0; jj < np; ++jj) {
                     const float wj = __shfl_sync(0xffffffffu, w, (int)jj);
                     const uint32_t pj = sb + jj;
-                    const float4 vv = pj == pos ? sm.vnew[lane] : kv_row4(sm.v + (size_t)(pj - tb) * rowb, lane, f16);
+                    const float4 vv = pj == pos ? sm.vnew[lane] : kv_row4(vt + (size_t)(pj - tb) * rowb, lane, f16);
                     acc.x = fmaf(wj, vv.x, acc.x);
                     acc.y = fmaf(wj, vv.y, acc.y);
                     acc.z = fmaf(wj, vv.z, acc.z);
@@ -845,8 +850,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
                 m = mn;
             }
         }
-        __syncthreads();   // tile consumed: the buffers may be refilled
-        if (threadIdx.x == 0 && tb + kAttnTile < t1) issue(tb + kAttnTile);
+        __syncthreads();   // tile consumed: its buffer takes the tile after next
+        if (threadIdx.x == 0 && tb + 2u * kAttnTile < t1) issue(tb + 2u * kAttnTile, b);
     }
     if (warp < group) {
         float *dst = a.part + (((size_t)kvh * a.splits + s) * group + warp) * kRec;

@@ -149,7 +149,7 @@ struct MvArgs {
 // ------------------------------------------------------ attention kernel ----
 
 constexpr uint32_t kAttnThreads = 256;
-constexpr uint32_t kAttnTile = 64;      // cached positions staged per tile
+constexpr uint32_t kAttnTile = 32;      // cached positions staged per tile (two tiles in flight)
 constexpr uint32_t kAttnMinSpan = 16;   // positions per split, at least
 constexpr uint32_t kAttnMaxGroup = 8;   // query heads per KV head (one warp each)
 constexpr uint32_t kRec = 132;          // partial record: acc[128], max, sum, 2 pad

@@ -705,7 +705,8 @@ int build_graph2(AtlasCuda *h)
     if (rc) return rc;
     CU(h, cudaMemset(g.st, 0, sizeof(d2::DecState)));
     g.status = &g.st->status;
-    g.splits = std::max(1u, std::min(G / sl.kv_heads, 160u));
+    // two attention CTAs fit on an SM: up to two splits per SM and KV head
+    g.splits = std::max(1u, std::min(2u * G / sl.kv_heads, 160u));
     if ((rc = dalloc(h, &g.apart, (size_t)sl.kv_heads * g.splits * group * d2::kRec * sizeof(float)))) return rc;
     if ((rc = dalloc(h, &g.actr, (size_t)sl.kv_heads * 4u))) return rc;
     CU(h, cudaMemset(g.actr, 0, (size_t)sl.kv_heads * 4u));

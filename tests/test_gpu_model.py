@@ -146,3 +146,29 @@ def test_wide_shapes_match_oracle(torch_cuda, oracle, model_dir, name):
         assert am == want_picks[0]
         picks = rt.generate(am, len(prompt), 31)
         np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
+
+
+@pytest.mark.slow
+def test_long_splits_match_oracle(torch_cuda, oracle, tiny_model, monkeypatch):
+    """Decode attention with many K/V tiles per split (the double-buffered
+    tile loop): a 1400-token prompt with splits of >= 192 positions (6 tiles
+    each), then 8 greedy steps, against the oracle."""
+    monkeypatch.setenv("ATLAS_ATTN_MIN_SPAN", "192")
+    prompt = np.random.default_rng(11).integers(0, 1024, 1400).astype(np.uint32)
+    m = oracle.open(tiny_model)
+    m.begin(1500)
+    for i, t in enumerate(prompt):
+        want = m.forward(int(t), i, i + 1 == len(prompt))
+    want_picks, lg = [], want
+    for s in range(8):
+        want_picks.append(m.argmax(lg))
+        if s < 7:
+            lg = m.forward(want_picks[-1], len(prompt) + s)
+    with atlas_cuda.Runtime(tiny_model, max_context=1500) as rt:
+        got, am = rt.prefill(prompt)
+        _close(got, want, 1e-3)
+        assert am == want_picks[0]
+        _, am1 = rt.forward(am, len(prompt))
+        picks = rt.generate(am1, len(prompt) + 1, 6)
+        np.testing.assert_array_equal(np.concatenate([[am, am1], picks]).astype(np.uint32),
+                                      np.array(want_picks, np.uint32))
