@@ -5,11 +5,14 @@
 // from one CUDA graph per token.
 //
 // Every kernel first lets its successor launch (griddepcontrol.launch_dependents)
-// and only then waits for its predecessor (griddepcontrol.wait). A kernel is
-// sized to take at most half of an SM, so the successor's CTAs become resident
-// while the current kernel runs and their producer warps stream the next
-// weights into shared memory ahead of time: weights never depend on the
-// activations, so HBM keeps streaming across kernel boundaries.
+// and only then waits for its predecessor (griddepcontrol.wait). A successor
+// CTA becomes resident on an SM as soon as resources there allow - for two
+// mv kernels, when the predecessor's CTA on that SM exits (at 112 registers
+// per thread the register banks hold one 9-warp mv CTA per SM) - and its
+// producer warp starts streaming weights at once: weights never depend on
+// the activations, so HBM keeps streaming while other SMs finish the
+// predecessor. (A 96-register build that fits two mv CTAs per SM ran the 3B
+// step 16 % slower: co-resident CTAs compete for issue slots.)
 //
 // mv kernel (dequant-GEMV, one CTA per SM): a producer warp copies the raw
 // Q4_K / Q6_K rows of the CTA's task range into a shared-memory ring with
