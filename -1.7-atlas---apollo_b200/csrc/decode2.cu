@@ -698,6 +698,7 @@ struct __align__(16) AttnSmem {
     uint8_t v[2][kAttnTile * 512];      // staged V rows
     float4 knew[32], vnew[32];          // the current token's RoPE'd k and its v
     float cden[kAttnMaxGroup];
+    float qinv[kAttnMaxGroup + 1];      // qwen3: 1 / rms of each query head and (last) of the new k
     uint64_t bar[2];                    // tile arrival, per buffer
     uint32_t flag;
 };
@@ -779,11 +780,32 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
     }
     __syncthreads();
     pdl_wait();
+    const bool qkn = a.q_norm != nullptr;
+    if (qkn) {
+        // qwen3 per-head RMSNorm before RoPE (src/brain_runtime.c:1727-1737,
+        // rms_norm :1338-1371): warp w takes query head w, and the new k
+        // (index group) where this split appends it
+        for (uint32_t hh = warp; hh <= group; hh += kAttnThreads / 32u) {
+            if (hh == group && !has_pos) break;
+            const float *src = hh < group ? a.q + (size_t)(kvh * group + hh) * 128u : a.k + (size_t)kvh * 128u;
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(src) + lane);
+            double ss = (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) sm.qinv[hh] = 1.0f / sqrtf((float)(ss / 128.0) + a.eps);
+        }
+        __syncthreads();
+    }
     float *qf = reinterpret_cast<float *>(sm.q);
     for (uint32_t i = threadIdx.x; i < group * 64u; i += kAttnThreads) {
         const uint32_t hq = i >> 6, p = i & 63u;
         const float *qh = a.q + (size_t)(kvh * group + hq) * 128u;
-        const float qa = __ldcg(qh + p), qb = __ldcg(qh + p + 64u);
+        float qa = __ldcg(qh + p), qb = __ldcg(qh + p + 64u);
+        if (qkn) {
+            const float inv = sm.qinv[hq];
+            qa = __fmul_rn(__fmul_rn(qa, inv), __ldg(a.q_norm + p));
+            qb = __fmul_rn(__fmul_rn(qb, inv), __ldg(a.q_norm + p + 64u));
+        }
         const float2 cs = __ldg(a.rope + (size_t)pos * 64u + p);
         qf[hq * 128u + p] = qa * cs.x - qb * cs.y;   // src/brain_runtime.c:1391-1393
         qf[hq * 128u + p + 64u] = qa * cs.y + qb * cs.x;
@@ -792,7 +814,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
         float *kn = reinterpret_cast<float *>(sm.knew), *vn = reinterpret_cast<float *>(sm.vnew);
         const float *kh = a.k + (size_t)kvh * 128u;
         for (uint32_t p = threadIdx.x; p < 64u; p += kAttnThreads) {
-            const float ka = __ldcg(kh + p), kb = __ldcg(kh + p + 64u);
+            float ka = __ldcg(kh + p), kb = __ldcg(kh + p + 64u);
+            if (qkn) {
+                const float inv = sm.qinv[group];
+                ka = __fmul_rn(__fmul_rn(ka, inv), __ldg(a.k_norm + p));
+                kb = __fmul_rn(__fmul_rn(kb, inv), __ldg(a.k_norm + p + 64u));
+            }
             const float2 cs = __ldg(a.rope + (size_t)pos * 64u + p);
             kn[p] = ka * cs.x - kb * cs.y;
             kn[p + 64u] = ka * cs.y + kb * cs.x;

@@ -164,6 +164,8 @@ struct AttnArgs {
     DecState *st;
     uint32_t q_heads, kv_heads, max_context, splits, kv_fp16;
     uint32_t min_span;          // cached positions per split, at least (0: kAttnMinSpan)
+    const float *q_norm, *k_norm;   // qwen3: per-head RMSNorm weights [128] of q and k, or null
+    float eps;
 };
 
 }  // namespace d2

@@ -48,6 +48,11 @@ extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_b
 extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n,
                                               atlas::d2::DecState *st, const uint32_t *cnt, uint32_t arrivals,
                                               cudaStream_t stream);
+extern "C" cudaError_t atlas_launch_prefill_qknorm(float *q, uint32_t q_heads, const float *kin, void *kcache,
+                                                   uint32_t kv_heads, uint32_t max_context, uint32_t pos0,
+                                                   uint32_t tokens, const float *qn, const float *kn,
+                                                   const float2 *rope, float eps, uint32_t kv_f16,
+                                                   cudaStream_t stream);
 extern "C" cudaError_t atlas_tp_allreduce(const atlas::d2::TpReduceArgs *a, uint32_t grid, cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_wbound(uint32_t type, const uint8_t *blocks, uint64_t nblocks, uint32_t *out_bits,
                                            cudaStream_t stream);
@@ -85,6 +90,7 @@ struct AtlasCuda {
         const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
         uint32_t tq = 0, tk = 0, tv = 0, to = 0, tg = 0, tu = 0, td = 0;
         const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+        const float *qn = nullptr, *kn = nullptr;   // qwen3 per-head q / k RMSNorm weights [head_dim]
         void *kc = nullptr, *vc = nullptr;
         // prefill: power-of-two exponents that bring each tensor's weights into
         // [2^14, 2^15) before the binary16 split
@@ -95,6 +101,7 @@ struct AtlasCuda {
         uint32_t cap = 0, tok_pad = 0, terms = 3, max_units = 0, pairs = 0;
         float *x = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *xscale = nullptr, *ws = nullptr;
         float *apart = nullptr;
+        float *kq = nullptr;   // qwen3: the chunk's keys before their norm and RoPE
         uint8_t *xt = nullptr;
         uint32_t *actr = nullptr, *units = nullptr, *ids = nullptr, *status = nullptr;
         ProgramBuffers tail;   // final rms_norm + head GEMV + argmax of the last token
@@ -797,6 +804,7 @@ int build_graph2(AtlasCuda *h)
     at.max_context = d.max_context;
     at.splits = g.splits;
     at.kv_fp16 = d.kv_fp16 ? 1u : 0u;
+    at.eps = d.rms_eps;
     if (const char *e = getenv("ATLAS_ATTN_MIN_SPAN")) at.min_span = (uint32_t)std::max(1, atoi(e));
 
     const uint64_t embd_row = (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
@@ -824,6 +832,8 @@ int build_graph2(AtlasCuda *h)
         if ((e = atlas_d2_launch_mv(&a, qkv.grid, h->stream)) != cudaSuccess) break;
         at.k_cache = w.kc;
         at.v_cache = w.vc;
+        at.q_norm = w.qn;
+        at.k_norm = w.kn;
         if ((e = atlas_d2_launch_attn(&at, sl.kv_heads * g.splits, h->stream)) != cudaSuccess) break;
         a = o.a;
         a.seg[0].w = w.o;
@@ -1079,6 +1089,7 @@ int alloc_prefill(AtlasCuda *h)
     if ((rc = dalloc(h, &p.att, (size_t)p.cap * d.q_dim * 4))) return rc;
     CU(h, cudaMemset(p.att, 0, (size_t)p.cap * d.q_dim * 4));
     if ((rc = dalloc(h, &p.ffn, (size_t)p.cap * sl.ffn_rows * 4))) return rc;
+    if (d.has_qk_norm && (rc = dalloc(h, &p.kq, (size_t)p.cap * sl.kv_heads * 128u * 4))) return rc;
     if ((rc = dalloc(h, &p.xt, (size_t)tok_tiles * (max_cols / pf::kKBlock) * pf::kXTileBytes))) return rc;
     if ((rc = dalloc(h, &p.xscale, (size_t)p.tok_pad * 4))) return rc;
     // split-K partials: a split contraction runs at most one unit per CTA pair,
@@ -1283,11 +1294,20 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
         pf::GemmArgs g{};
         g.epi = pf::GEPI_STORE;
         g.n_seg = 3;
-        g.seg[0] = gseg(w.q, w.tq, lq, d.hidden, w.eq, w.bq, p.q, 128, lq, 0, true);
-        g.seg[1] = gseg(w.k, w.tk, lkv, d.hidden, w.ek, w.bk, kc, cache_head, d.head_dim, pos0, true);
+        const bool qkn = d.has_qk_norm != 0;
+        g.seg[0] = gseg(w.q, w.tq, lq, d.hidden, w.eq, w.bq, p.q, 128, lq, 0, !qkn);
+        g.seg[1] = qkn ? gseg(w.k, w.tk, lkv, d.hidden, w.ek, w.bk, p.kq, 128, lkv, 0, false)
+                       : gseg(w.k, w.tk, lkv, d.hidden, w.ek, w.bk, kc, cache_head, d.head_dim, pos0, true);
         g.seg[2] = gseg(w.v, w.tv, lkv, d.hidden, w.ev, w.bv, vc, cache_head, d.head_dim, pos0, false);
-        g.seg[1].f16 = g.seg[2].f16 = d.kv_fp16 ? 1u : 0u;   // element offsets either way
+        if (!qkn) g.seg[1].f16 = d.kv_fp16 ? 1u : 0u;   // element offsets either way
+        g.seg[2].f16 = d.kv_fp16 ? 1u : 0u;
         if ((rc = launch_gemm(h, g, d.hidden, n, pos0))) return rc;
+        if (qkn) {
+            // qwen3: per-head RMSNorm, then RoPE; keys into the cache
+            CU(h, atlas_launch_prefill_qknorm(p.q, sl.q_heads, p.kq, w.kc, sl.kv_heads, d.max_context, pos0, n, w.qn,
+                                              w.kn, h->rope, d.rms_eps, d.kv_fp16 ? 1u : 0u, h->stream));
+            ++h->launches;
+        }
         at.k_cache = kc;
         at.v_cache = vc;
         CU(h, atlas_launch_prefill_attn(&at, (int)std::min<uint32_t>(at.n_units, (uint32_t)h->sm_count), h->stream));
@@ -1368,7 +1388,6 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
         d.kv_dim != d.kv_heads * d.head_dim || d.hidden % 256 || d.ffn % 256 || d.q_dim % 256 || !d.layers ||
         !d.vocab || d.max_context < 2)
         return fail(nullptr, ATLAS_EINVAL, "unsupported model shape (head_dim must be 128, dims multiples of 256)");
-    if (d.has_qk_norm) return fail(nullptr, ATLAS_EINVAL, "qwen3 q/k norm is not supported yet");
     const int tp = d.tp_size > 1 ? d.tp_size : 1;
     AtlasTpSlice sl{0u, d.q_heads, 0u, d.kv_heads, 0u, d.q_dim / 256u, 0u, d.q_dim, 0u, d.ffn, 0u, d.vocab};
     if (tp > 1) {
@@ -1430,6 +1449,11 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
         if (TN("attn_q.bias")) TRY(upload_vector(h, TN("attn_q.bias"), d.q_dim, &w.bq, sl.q_head0 * 128u, lq));
         if (TN("attn_k.bias")) TRY(upload_vector(h, TN("attn_k.bias"), d.kv_dim, &w.bk, sl.kv_head0 * 128u, lkv));
         if (TN("attn_v.bias")) TRY(upload_vector(h, TN("attn_v.bias"), d.kv_dim, &w.bv, sl.kv_head0 * 128u, lkv));
+        if (d.has_qk_norm) {
+            // qwen3 (src/brain_runtime.c:1727-1737): one weight vector per head dimension
+            TRY(upload_vector(h, TN("attn_q_norm.weight"), d.head_dim, &w.qn));
+            TRY(upload_vector(h, TN("attn_k_norm.weight"), d.head_dim, &w.kn));
+        }
 #undef TN
         TRY(dalloc(h, &w.kc, kv_layer));
         TRY(dalloc(h, &w.vc, kv_layer));
@@ -1485,8 +1509,9 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     if (tp == 1) {
         TRY(build_decode_program(h));
         // graph decode step unless the persistent decode kernel is asked for
+        // (qwen3's q/k norm exists in the graph step only)
         const char *eng = getenv("ATLAS_DECODE_ENGINE");
-        if (!eng || strcmp(eng, "persistent") != 0) TRY(build_graph2(h));
+        if (!eng || strcmp(eng, "persistent") != 0 || d.has_qk_norm) TRY(build_graph2(h));
     }
     TRY(alloc_prefill(h));
     // tensor parallel: the decode step is built by atlas_cuda_tp_connect
@@ -1675,7 +1700,8 @@ int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out
                           uint32_t *n_phases, uint32_t *phase_kinds)
 {
     if (!h) return fail(h, ATLAS_EINVAL, "null handle");
-    if (h->tp > 1) return fail(h, ATLAS_EINVAL, "tracing covers the single-GPU persistent engine only");
+    if (h->tp > 1 || h->desc.has_qk_norm)
+        return fail(h, ATLAS_EINVAL, "tracing covers the single-GPU persistent engine (qwen2) only");
     const size_t np = h->decode.phases.size(), per = (size_t)h->sm_count * np, need = per * 12;
     if (n_ctas) *n_ctas = (uint32_t)h->sm_count;
     if (n_phases) *n_phases = (uint32_t)np;

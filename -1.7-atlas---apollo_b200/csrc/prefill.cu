@@ -1290,6 +1290,61 @@ extern "C" cudaError_t atlas_launch_prefill_gemm(const GemmArgs *a, int grid, cu
     return cudaGetLastError();
 }
 
+// qwen3 per-head q/k RMSNorm then RoPE over a prompt chunk
+// (src/brain_runtime.c:1727-1737, rms_norm :1338-1371, rope :1377-1401): one
+// CTA of 64 threads per (token, head); thread p holds the RoPE pair (p, p + 64).
+// Query heads are normalized in place in q [tokens][q_heads * 128]; key heads
+// are read from kin [tokens][kv_heads * 128] and written into the KV cache at
+// positions pos0 + t (binary16 when kv_f16).
+__global__ void __launch_bounds__(64) qk_norm_rope_kernel(float *q, uint32_t q_heads, const float *kin, void *kcache,
+                                                          uint32_t kv_heads, uint32_t max_context, uint32_t pos0,
+                                                          const float *qn, const float *kn, const float2 *rope,
+                                                          float eps, uint32_t kv_f16)
+{
+    __shared__ double red[2];
+    const uint32_t t = blockIdx.x, hh = blockIdx.y, p = threadIdx.x;
+    const bool isq = hh < q_heads;
+    const float *src = isq ? q + ((size_t)t * q_heads + hh) * 128u : kin + ((size_t)t * kv_heads + (hh - q_heads)) * 128u;
+    const float *w = isq ? qn : kn;
+    const float a = src[p], b = src[p + 64u];
+    double ss = (double)a * a + (double)b * b;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((p & 31u) == 0u) red[p >> 5] = ss;
+    __syncthreads();
+    const float inv = 1.0f / sqrtf((float)((red[0] + red[1]) / 128.0) + eps);
+    const float x0 = __fmul_rn(__fmul_rn(a, inv), w[p]), x1 = __fmul_rn(__fmul_rn(b, inv), w[p + 64u]);
+    const float2 r = rope[(size_t)(pos0 + t) * 64u + p];
+    const float y0 = __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y));
+    const float y1 = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
+    if (isq) {
+        float *dst = q + ((size_t)t * q_heads + hh) * 128u;
+        dst[p] = y0;
+        dst[p + 64u] = y1;
+        return;
+    }
+    const size_t off = ((size_t)(hh - q_heads) * max_context + pos0 + t) * 128u;
+    if (kv_f16) {
+        reinterpret_cast<__half *>(kcache)[off + p] = __float2half_rn(y0);
+        reinterpret_cast<__half *>(kcache)[off + p + 64u] = __float2half_rn(y1);
+    } else {
+        reinterpret_cast<float *>(kcache)[off + p] = y0;
+        reinterpret_cast<float *>(kcache)[off + p + 64u] = y1;
+    }
+}
+
+extern "C" cudaError_t atlas_launch_prefill_qknorm(float *q, uint32_t q_heads, const float *kin, void *kcache,
+                                                   uint32_t kv_heads, uint32_t max_context, uint32_t pos0,
+                                                   uint32_t tokens, const float *qn, const float *kn,
+                                                   const float2 *rope, float eps, uint32_t kv_f16,
+                                                   cudaStream_t stream)
+{
+    qk_norm_rope_kernel<<<dim3(tokens, q_heads + kv_heads), 64, 0, stream>>>(q, q_heads, kin, kcache, kv_heads,
+                                                                            max_context, pos0, qn, kn, rope, eps,
+                                                                            kv_f16);
+    return cudaGetLastError();
+}
+
 extern "C" cudaError_t atlas_launch_prefill_split(const float *x, uint32_t ldx, uint32_t cols, uint32_t tokens,
                                                   uint32_t tok_pad, const float *norm_w, float eps, uint8_t *xt,
                                                   float *xscale, cudaStream_t stream)

@@ -247,7 +247,7 @@ static uint64_t tensor_bytes(uint32_t type, uint64_t cols, uint64_t rows)
 static int build_plan(const AtlasSynthConfig *c, Plan **out, int *count)
 {
     uint32_t H = c->hidden, qd = c->q_heads * c->head_dim, kvd = c->kv_heads * c->head_dim;
-    int n = 3 + (int)c->layers * (c->qkv_bias ? 12 : 9) + 1;
+    int n = 3 + (int)c->layers * ((c->qkv_bias ? 12 : 9) + (c->qk_norm ? 2 : 0)) + 1;
     Plan *p = (Plan *)calloc((size_t)n, sizeof(Plan));
     if (!p) return -1;
     int k = 0;
@@ -275,6 +275,10 @@ static int build_plan(const AtlasSynthConfig *c, Plan **out, int *count)
             LADD("attn_q.bias", T_F32, qd, 1, 2);
             LADD("attn_k.bias", T_F32, kvd, 1, 2);
             LADD("attn_v.bias", T_F32, kvd, 1, 2);
+        }
+        if (c->qk_norm) {
+            LADD("attn_q_norm.weight", T_F32, c->head_dim, 1, 1);
+            LADD("attn_k_norm.weight", T_F32, c->head_dim, 1, 1);
         }
         LADD("attn_output.weight", T_Q4K, qd, H, 0);
         LADD("ffn_norm.weight", T_F32, H, 1, 1);
@@ -314,17 +318,21 @@ static Buf build_header(const AtlasSynthConfig *c, const Plan *p, int n)
     put_u32(&b, 3);
     put_u64(&b, (uint64_t)n);
     put_u64(&b, 14);
-    kv_str(&b, "general.architecture", "qwen2");
+    const char *arch = c->qk_norm ? "qwen3" : "qwen2";
+    char key[96];
+#define KEY(SUFFIX) (snprintf(key, sizeof(key), "%s.%s", arch, SUFFIX), key)
+    kv_str(&b, "general.architecture", arch);
     kv_str(&b, "general.name", "atlas-synthetic");
     kv_u32(&b, "general.alignment", ALIGN);
-    kv_u32(&b, "qwen2.block_count", c->layers);
-    kv_u32(&b, "qwen2.context_length", c->context_length);
-    kv_u32(&b, "qwen2.embedding_length", c->hidden);
-    kv_u32(&b, "qwen2.feed_forward_length", c->ffn);
-    kv_u32(&b, "qwen2.attention.head_count", c->q_heads);
-    kv_u32(&b, "qwen2.attention.head_count_kv", c->kv_heads);
-    kv_f32(&b, "qwen2.rope.freq_base", c->rope_base);
-    kv_f32(&b, "qwen2.attention.layer_norm_rms_epsilon", 1e-6f);
+    kv_u32(&b, KEY("block_count"), c->layers);
+    kv_u32(&b, KEY("context_length"), c->context_length);
+    kv_u32(&b, KEY("embedding_length"), c->hidden);
+    kv_u32(&b, KEY("feed_forward_length"), c->ffn);
+    kv_u32(&b, KEY("attention.head_count"), c->q_heads);
+    kv_u32(&b, KEY("attention.head_count_kv"), c->kv_heads);
+    kv_f32(&b, KEY("rope.freq_base"), c->rope_base);
+    kv_f32(&b, KEY("attention.layer_norm_rms_epsilon"), 1e-6f);
+#undef KEY
     kv_str(&b, "tokenizer.ggml.model", "gpt2");
     put_vocab(&b, c->vocab);
     for (int i = 0; i < n; ++i) {

@@ -47,7 +47,7 @@ class SynthConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in
                 ("hidden", "layers", "q_heads", "kv_heads", "head_dim", "ffn", "vocab", "context_length")] + [
         ("rope_base", ctypes.c_float), ("tied", ctypes.c_int32), ("qkv_bias", ctypes.c_int32),
-        ("threads", ctypes.c_int32), ("seed", ctypes.c_uint64)]
+        ("threads", ctypes.c_int32), ("seed", ctypes.c_uint64), ("qk_norm", ctypes.c_int32)]
 
 
 class Shape(ctypes.Structure):
@@ -166,9 +166,11 @@ def _ptr(a) -> ctypes.c_void_p:
 
 def write_synthetic_gguf(path: str, *, hidden: int, layers: int, q_heads: int, kv_heads: int, ffn: int, vocab: int,
                          head_dim: int = 128, context_length: int = 32768, rope_base: float = 1e6,
-                         tied: bool = True, qkv_bias: bool = True, seed: int = 0, threads: int = 0) -> int:
+                         tied: bool = True, qkv_bias: bool = True, seed: int = 0, threads: int = 0,
+                         qk_norm: bool = False) -> int:
+    """qk_norm: a qwen3 file (per-head q/k RMSNorm weights)."""
     cfg = SynthConfig(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, context_length, rope_base,
-                      int(tied), int(qkv_bias), threads, seed)
+                      int(tied), int(qkv_bias), threads, seed, int(qk_norm))
     rc = lib().atlas_synth_write_gguf(ctypes.byref(cfg), path.encode())
     if rc != 0:
         raise RuntimeError(f"synthetic GGUF write failed: {path}")

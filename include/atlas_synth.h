@@ -45,6 +45,8 @@ typedef struct {
     int32_t qkv_bias;         /* 1: emit attn_q/k/v.bias */
     int32_t threads;          /* 0: all cores */
     uint64_t seed;
+    int32_t qk_norm;          /* 1: a qwen3 file (architecture "qwen3", per-head
+                                 blk.N.attn_q_norm / attn_k_norm.weight, head_dim floats) */
 } AtlasSynthConfig;
 
 /* Writes the model to `path`. Returns 0 on success, -1 on failure (errno-style

@@ -71,6 +71,15 @@ def tiny_untied_model(model_dir):
 
 
 @pytest.fixture(scope="session")
+def tiny_qwen3_model(model_dir):
+    """qwen3: per-head q/k RMSNorm, no q/k/v bias."""
+    path = os.path.join(str(model_dir), "tiny_qwen3.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, tied=True, qkv_bias=False, qk_norm=True, **dict(TINY, seed=2468))
+    return path
+
+
+@pytest.fixture(scope="session")
 def small_model(model_dir):
     return _model(model_dir, "small", SMALL)
 

@@ -172,3 +172,32 @@ def test_long_splits_match_oracle(torch_cuda, oracle, tiny_model, monkeypatch):
         picks = rt.generate(am1, len(prompt) + 1, 6)
         np.testing.assert_array_equal(np.concatenate([[am, am1], picks]).astype(np.uint32),
                                       np.array(want_picks, np.uint32))
+
+
+def test_qwen3_qk_norm_matches_oracle(torch_cuda, oracle, tiny_qwen3_model):
+    """qwen3 (per-head q/k RMSNorm before RoPE, src/brain_runtime.c:1727-1737):
+    token-by-token decode logits, a chunked batched prefill and 32 greedy
+    steps against the oracle (itself pinned to the reference for qwen3)."""
+    m = oracle.open(tiny_qwen3_model)
+    m.begin(128)
+    prompt = np.random.default_rng(21).integers(0, 1024, 40).astype(np.uint32)
+    with atlas_cuda.Runtime(tiny_qwen3_model, max_context=128) as rt:
+        for pos, tok in enumerate(prompt[:6]):
+            got, am = rt.forward(int(tok), pos)
+            want = m.forward(int(tok), pos)
+            _close(got, want, 1e-3)
+            assert am == m.argmax(want)
+    m.begin(128)
+    for i, t in enumerate(prompt):
+        want = m.forward(int(t), i, i + 1 == len(prompt))
+    want_picks, lg = [], want
+    for s in range(32):
+        want_picks.append(m.argmax(lg))
+        if s < 31:
+            lg = m.forward(want_picks[-1], len(prompt) + s)
+    with atlas_cuda.Runtime(tiny_qwen3_model, max_context=128, max_prefill=16) as rt:
+        got, am = rt.prefill(prompt)
+        _close(got, want, 1e-3)
+        assert am == want_picks[0]
+        picks = rt.generate(am, len(prompt), 31)
+        np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))

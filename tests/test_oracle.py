@@ -83,6 +83,18 @@ def test_oracle_forward_matches_reference_untied(oracle, ref, tiny_untied_model)
     r.close()
 
 
+def test_oracle_forward_matches_reference_qwen3(oracle, ref, tiny_qwen3_model):
+    """qwen3 per-head q/k RMSNorm (src/brain_runtime.c:1727-1737): the oracle's
+    logits equal the reference's bit for bit."""
+    m = oracle.open(tiny_qwen3_model)
+    assert m.qk_norm == 1
+    m.begin(64)
+    r = ref.open(tiny_qwen3_model)
+    for pos, tok in enumerate([1, 900, 44, 1000, 2, 17]):
+        np.testing.assert_array_equal(m.forward(tok, pos), r.forward(tok, pos))
+    r.close()
+
+
 @pytest.mark.slow
 def test_oracle_cfg0_prompt_logits(oracle, model_dir):
     """Full-size Qwen2-1.5B shape: the oracle reproduces the reference's logits."""
