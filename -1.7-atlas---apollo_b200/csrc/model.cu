@@ -37,7 +37,7 @@ extern "C" cudaError_t atlas_launch_prefill_split(const float *x, uint32_t ldx, 
 extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t tokens, const uint8_t *embd,
                                                   uint32_t type, uint64_t row_bytes, uint32_t hidden, float *x,
                                                   cudaStream_t stream);
-extern "C" cudaError_t atlas_launch_prefill_attn(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_launch_prefill_attn_tc(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots);
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits);
 extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
@@ -1100,7 +1100,7 @@ int alloc_prefill(AtlasCuda *h)
         return fail(h, ATLAS_ECUDA, "no CTA pair of the prefill contraction kernel fits this device");
     p.pairs = std::min((uint32_t)pairs, G / 2);
     p.max_units = prefill_max_units(h);
-    if ((rc = dalloc(h, &p.apart, (size_t)p.max_units * 64 * 132 * 4))) return rc;
+    if ((rc = dalloc(h, &p.apart, (size_t)p.max_units * 128 * 132 * 4))) return rc;
     const size_t actr = (size_t)((p.cap + 7) / 8) * d.kv_heads * 4;
     if ((rc = dalloc(h, &p.actr, actr))) return rc;
     CU(h, cudaMemset(p.actr, 0, actr));
@@ -1205,9 +1205,11 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
 {
     const AtlasModelDesc &d = h->desc;
     const AtlasTpSlice &sl = h->sl;
-    const uint32_t G = (uint32_t)h->sm_count, qt_n = (n + 7) / 8;
+    // units of 128 query rows: qt tokens x group heads
+    const uint32_t group = d.q_heads / d.kv_heads, qtok = std::max(1u, 128u / group);
+    const uint32_t G = (uint32_t)h->sm_count, qt_n = (n + qtok - 1) / qtok;
     uint64_t chunks = 0;
-    for (uint32_t qt = 0; qt < qt_n; ++qt) chunks += (pos0 + std::min(8 * qt + 8, n) + 63) / 64;
+    for (uint32_t qt = 0; qt < qt_n; ++qt) chunks += (pos0 + std::min(qtok * qt + qtok, n) + 63) / 64;
     chunks *= sl.kv_heads;
     uint32_t span_chunks = (uint32_t)std::max<uint64_t>(1, (chunks + 3 * G - 1) / (3 * G));
     std::vector<uint32_t> tab;
@@ -1216,7 +1218,7 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
         const uint32_t span = 64 * span_chunks;
         for (uint32_t g = 0; g < sl.kv_heads; ++g)
             for (uint32_t qt = 0; qt < qt_n; ++qt) {
-                const uint32_t kend = pos0 + std::min(8 * qt + 8, n), parts = (kend + span - 1) / span;
+                const uint32_t kend = pos0 + std::min(qtok * qt + qtok, n), parts = (kend + span - 1) / span;
                 for (uint32_t s = 0; s < parts; ++s) tab.push_back(g | (qt << 8) | (s << 20));
             }
         if (tab.size() <= h->pf.max_units && (d.max_context + span - 1) / span < 4096) break;
@@ -1231,6 +1233,7 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
     a.out = h->pf.att + (size_t)sl.q_head0 * 128u;
     a.out_stride = d.q_dim;
     a.kv_f16 = d.kv_fp16 ? 1u : 0u;
+    a.q_tokens = qtok;
     a.part = h->pf.apart;
     a.ctr = h->pf.actr;
     a.status = h->pf.status;
@@ -1310,7 +1313,8 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
         }
         at.k_cache = kc;
         at.v_cache = vc;
-        CU(h, atlas_launch_prefill_attn(&at, (int)std::min<uint32_t>(at.n_units, (uint32_t)h->sm_count), h->stream));
+        CU(h, atlas_launch_prefill_attn_tc(&at, (int)std::min<uint32_t>(at.n_units, (uint32_t)h->sm_count),
+                                           h->stream));
         ++h->launches;
         // the rank's attn_output blocks (other ranks' heads in them are zero)
         if ((rc = launch_split(h, p.att + (size_t)sl.o_block0 * 256u, o_cols, n, nullptr, d.q_dim))) return rc;

@@ -994,203 +994,7 @@ __global__ void embed_kernel(const uint32_t *ids, uint32_t tokens, const uint8_t
         x[(size_t)t * hidden + i] = deq_elem(type, row + (size_t)(i / be) * bb, (int)(i % be));
 }
 
-// ------------------------------------------------------------ attention ----
-
-// Causal GQA attention for prompt tokens (gqa_single_token per token,
-// src/brain_runtime.c:1482-1528). A unit is (kv head g, tile of kQT query
-// tokens, span of cached positions): the kQT x group query rows walk the
-// span kKC keys at a time through shared memory (fp32 scores, online softmax,
-// P.V); a (g, tile) whose keys fit one span writes its output directly,
-// otherwise each span stores (acc, max, sum) and the last span to finish
-// merges them.
-constexpr uint32_t kQT = 8, kKC = 64, kRows = 64, kQPad = 132, kPPad = 68, kRec = 132;
-
-struct AttnSmem {
-    float q[kRows][kQPad];
-    float k[kKC][kQPad];
-    float v[kKC][128];
-    float p[kRows][kPPad];
-    uint32_t flag;
-};
-
-__global__ void __launch_bounds__(256, 1) attn_kernel(const __grid_constant__ AttnArgs a)
-{
-    extern __shared__ uint8_t smem_raw[];
-    AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw);
-    const uint32_t tid = threadIdx.x, ty = tid >> 4, tx = tid & 15u;
-    const uint32_t group = a.q_heads / a.kv_heads, qdim = a.q_heads * 128u;
-    const uint32_t ostride = a.out_stride ? a.out_stride : qdim;
-    const float scale = 1.0f / sqrtf(128.0f);
-    for (uint32_t u = blockIdx.x; u < a.n_units; u += gridDim.x) {
-        const uint32_t code = a.unit_tab[u];
-        const uint32_t g = code & 0xffu, qt = (code >> 8) & 0xfffu, part = code >> 20;
-        const uint32_t t0 = qt * kQT, t1 = min(t0 + kQT, a.tokens);
-        const uint32_t kend = a.pos0 + t1;                       // keys [0, kend) for this tile
-        const uint32_t nparts = (kend + a.span - 1) / a.span;
-        const uint32_t k0 = part * a.span, k1 = min(k0 + a.span, kend);
-        __syncthreads();   // previous unit done with shared memory
-        // queries (rows r = qi * group + h)
-        for (uint32_t i = tid; i < kRows * 32u; i += 256u) {
-            const uint32_t r = i >> 5, d4 = i & 31u, qi = r / group, h = r % group;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (r < kQT * group && t0 + qi < t1)
-                v = __ldcg(reinterpret_cast<const float4 *>(a.q + (size_t)(t0 + qi) * qdim + (size_t)(g * group + h) * 128u) + d4);
-            *reinterpret_cast<float4 *>(&sm.q[r][4 * d4]) = v;
-        }
-        float m[4], l[4], o[4][8];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            m[r] = -FLT_MAX;
-            l[r] = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[r][j] = 0.f;
-        }
-        for (uint32_t p0 = k0; p0 < k1; p0 += kKC) {
-        if (p0 != k0) __syncthreads();   // previous chunk's K / V / P consumed
-        for (uint32_t i = tid; i < kKC * 32u; i += 256u) {
-            const uint32_t j = i >> 5, d4 = i & 31u, pos = p0 + j;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (pos < k1) {
-                const size_t off = ((size_t)g * a.max_context + pos) * 128u;
-                if (a.kv_f16) {
-                    kv = h4_to_f4(__ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(a.k_cache) + off) + d4));
-                    vv = h4_to_f4(__ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(a.v_cache) + off) + d4));
-                } else {
-                    kv = __ldcg(reinterpret_cast<const float4 *>(a.k_cache + off) + d4);
-                    vv = __ldcg(reinterpret_cast<const float4 *>(a.v_cache + off) + d4);
-                }
-            }
-            *reinterpret_cast<float4 *>(&sm.k[j][4 * d4]) = kv;
-            *reinterpret_cast<float4 *>(&sm.v[j][4 * d4]) = vv;
-        }
-        __syncthreads();
-        // scores: rows 4ty..4ty+3, keys tx + 16i
-        float s[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) s[r][i] = 0.f;
-#pragma unroll 4
-        for (uint32_t d = 0; d < 128u; d += 4) {
-            float4 qv[4], kv[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) qv[r] = *reinterpret_cast<const float4 *>(&sm.q[4 * ty + r][d]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) kv[i] = *reinterpret_cast<const float4 *>(&sm.k[tx + 16 * i][d]);
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    s[r][i] = fmaf(qv[r].x, kv[i].x, s[r][i]);
-                    s[r][i] = fmaf(qv[r].y, kv[i].y, s[r][i]);
-                    s[r][i] = fmaf(qv[r].z, kv[i].z, s[r][i]);
-                    s[r][i] = fmaf(qv[r].w, kv[i].w, s[r][i]);
-                }
-        }
-        // online softmax (src/brain_runtime.c:1430-1476 computes the same
-        // weights in one pass over all scores)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const uint32_t row = 4 * ty + (uint32_t)r, qi = row / group;
-            const uint32_t qpos = a.pos0 + t0 + qi;   // causal: keys <= qpos
-            float mx = m[r];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t pos = p0 + tx + 16u * (uint32_t)i;
-                const bool ok = row < kQT * group && t0 + qi < t1 && pos <= qpos && pos < k1;
-                s[r][i] = ok ? s[r][i] * scale : -INFINITY;
-                mx = fmaxf(mx, s[r][i]);
-            }
-#pragma unroll
-            for (int sh = 8; sh > 0; sh >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, sh));
-            const float corr = expf(m[r] - mx);
-            float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float pv = s[r][i] == -INFINITY ? 0.f : expf(s[r][i] - mx);
-                sm.p[4 * ty + r][tx + 16 * i] = pv;
-                sum += pv;
-            }
-#pragma unroll
-            for (int sh = 8; sh > 0; sh >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, sh);
-            m[r] = mx;
-            l[r] = fmaf(l[r], corr, sum);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[r][j] *= corr;
-        }
-        __syncthreads();
-        // P.V: rows 4ty..4ty+3, dims 8tx..8tx+7
-        for (uint32_t j = 0; j < kKC; ++j) {
-            const float4 v0 = *reinterpret_cast<const float4 *>(&sm.v[j][8 * tx]);
-            const float4 v1 = *reinterpret_cast<const float4 *>(&sm.v[j][8 * tx + 4]);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const float pv = sm.p[4 * ty + r][j];
-                o[r][0] = fmaf(pv, v0.x, o[r][0]); o[r][1] = fmaf(pv, v0.y, o[r][1]);
-                o[r][2] = fmaf(pv, v0.z, o[r][2]); o[r][3] = fmaf(pv, v0.w, o[r][3]);
-                o[r][4] = fmaf(pv, v1.x, o[r][4]); o[r][5] = fmaf(pv, v1.y, o[r][5]);
-                o[r][6] = fmaf(pv, v1.z, o[r][6]); o[r][7] = fmaf(pv, v1.w, o[r][7]);
-            }
-        }
-        }   // key chunks of the span
-        if (nparts == 1) {
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t row = 4 * ty + (uint32_t)r, qi = row / group, h = row % group;
-                if (row >= kQT * group || t0 + qi >= t1) continue;
-                float *dst = a.out + (size_t)(t0 + qi) * ostride + (size_t)(g * group + h) * 128u + 8u * tx;
-                const float inv = l[r] > 0.f ? 1.0f / l[r] : 0.f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) dst[j] = o[r][j] * inv;
-            }
-            continue;
-        }
-        // partial record of this span: acc[128], max, sum per row
-        const uint32_t u0 = u - part;   // the tile's spans are consecutive units
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const uint32_t row = 4 * ty + (uint32_t)r;
-            float *rec = a.part + ((size_t)u * kRows + row) * kRec;
-#pragma unroll
-            for (int j = 0; j < 8; j += 4)
-                __stcg(reinterpret_cast<float4 *>(rec + 8 * tx + j), make_float4(o[r][j], o[r][j + 1], o[r][j + 2], o[r][j + 3]));
-            if (tx == 0) { __stcg(rec + 128, m[r]); __stcg(rec + 129, l[r]); }
-        }
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) {
-            const uint32_t old = atom_acq_rel_add(a.ctr + g * a.q_tiles + qt, 1u);
-            sm.flag = (old == nparts - 1u) ? 1u : 0u;
-        }
-        __syncthreads();
-        if (!sm.flag) continue;
-        __threadfence();
-        // merge: rows 4ty..4ty+3, dims 8tx..8tx+7
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const uint32_t row = 4 * ty + (uint32_t)r, qi = row / group, h = row % group;
-            if (row >= kQT * group || t0 + qi >= t1) continue;
-            float M = -FLT_MAX;
-            for (uint32_t c = 0; c < nparts; ++c) M = fmaxf(M, __ldcg(a.part + ((size_t)(u0 + c) * kRows + row) * kRec + 128));
-            float L = 0.f, acc[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-            for (uint32_t c = 0; c < nparts; ++c) {
-                const float *rec = a.part + ((size_t)(u0 + c) * kRows + row) * kRec;
-                const float mc = __ldcg(rec + 128);
-                const float f = mc == -FLT_MAX ? 0.f : expf(mc - M);
-                L = fmaf(f, __ldcg(rec + 129), L);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = fmaf(f, __ldcg(rec + 8 * tx + j), acc[j]);
-            }
-            const float inv = L > 0.f ? 1.0f / L : 0.f;
-            float *dst = a.out + (size_t)(t0 + qi) * ostride + (size_t)(g * group + h) * 128u + 8u * tx;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = acc[j] * inv;
-        }
-        if (tid == 0) a.ctr[g * a.q_tiles + qt] = 0;
-    }
-}
+// Prompt attention: prefill_attn.cu (tensor cores).
 
 // ------------------------------------------------- weight scale bound ------
 
@@ -1223,7 +1027,6 @@ using namespace atlas;
 using namespace atlas::pf;
 
 extern "C" size_t atlas_prefill_gemm_smem() { return kGemmSmem; }
-extern "C" size_t atlas_prefill_attn_smem() { return sizeof(AttnSmem); }
 
 namespace {
 
@@ -1366,18 +1169,6 @@ extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t 
                                                   cudaStream_t stream)
 {
     embed_kernel<<<tokens, 256, 0, stream>>>(ids, tokens, embd, type, row_bytes, hidden, x);
-    return cudaGetLastError();
-}
-
-extern "C" cudaError_t atlas_launch_prefill_attn(const AttnArgs *a, int grid, cudaStream_t stream)
-{
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    attn_kernel<<<grid, 256, sizeof(AttnSmem), stream>>>(*a);
     return cudaGetLastError();
 }
 

@@ -93,13 +93,14 @@ struct AttnArgs {
     uint32_t *ctr;         // per (kv head, query tile) arrival counters
     uint32_t *status;
     uint32_t tokens, pos0, q_heads, kv_heads, max_context;
-    uint32_t q_tiles;      // ceil(T / 8)
+    uint32_t q_tiles;      // ceil(T / q_tokens)
     uint32_t span;         // cached positions per unit (multiple of 64)
     uint32_t n_units;
     const uint32_t *unit_tab;   // per unit: g | query tile << 8 | span index << 20;
                                 // the spans of one (g, tile) are consecutive
     uint32_t out_stride;        // floats between tokens of out (0: q_heads * 128)
     uint32_t kv_f16;            // the KV cache holds binary16
+    uint32_t q_tokens;          // query tokens per unit (128 / group: 128 query rows)
 };
 
 }  // namespace pf
