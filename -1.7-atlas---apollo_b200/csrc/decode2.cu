@@ -219,7 +219,10 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
 // factor for the row sums: inv_rms / xscale. Pass 1 keeps eight 16-byte loads
 // per thread in flight (x comes from L2); pass 2 converts one 4-element group
 // per thread and step, the 16-element sums reduced across 4 adjacent lanes.
-__device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
+// q4_order: the CTA's tasks are Q4_K - each 4-element group is stored as
+// (x0, x2, x1, x3), the order in which q4k_task pairs the nibbles of a quant
+// word (bytes 0 and 2, bytes 1 and 3) without byte permutes.
+__device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea, bool q4_order)
 {
     const uint32_t n4 = a.cols / 4u;
     const bool norm = a.norm_w != nullptr;
@@ -340,10 +343,11 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea)
             sum += e[q];
         }
         uint4 pk;
-        pk.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
-        pk.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
-        pk.z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
-        pk.w = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+        const int e1 = q4_order ? 2 : 1, e2 = q4_order ? 1 : 2;
+        pk.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[e1]) << 16);
+        pk.y = (uint32_t)__half_as_ushort(hi[e2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
+        pk.z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[e1]) << 16);
+        pk.w = (uint32_t)__half_as_ushort(lo[e2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
         reinterpret_cast<uint4 *>(xarea)[i] = pk;   // in place: group i is only touched by this thread
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
@@ -510,28 +514,33 @@ __device__ __forceinline__ void q4k_task(const uint8_t *blk, uint32_t lc, uint32
         float dlo[4], dhi[4];
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp) {
+            // 16-bit lanes straight from the quant words: bytes (0, 2) and
+            // (1, 3) of each word (the x groups are staged in that order);
+            // low nibbles as subnormals q 2^-24, high nibbles in place as
+            // 16 q 2^-24 (exact; the 16 is taken out with the scale)
             const uint32_t w0 = W[2 * c + hp][0], w1 = W[2 * c + hp][1];
-            const uint32_t l0 = w0 & 0x0f0f0f0fu, h0 = (w0 >> 4) & 0x0f0f0f0fu;
-            const uint32_t l1 = w1 & 0x0f0f0f0fu, h1 = (w1 >> 4) & 0x0f0f0f0fu;
+            const uint32_t v0 = w0 >> 8, v1 = w1 >> 8;
             const uint2 blo = *reinterpret_cast<const uint2 *>(xb + (16u * c + 4u * hp + t) * 16u + podd);
             const uint2 bhi = *reinterpret_cast<const uint2 *>(xb + (16u * c + 8u + 4u * hp + t) * 16u + podd);
+            const uint32_t kl = 0x000f000fu, kh = 0x00f000f0u;
             if (hp == 0) {
-                mma16816(dlo, sub2(l0, 0x4140), sub2(l1, 0x4140), sub2(l0, 0x4342), sub2(l1, 0x4342), blo, zero);
-                mma16816(dhi, sub2(h0, 0x4140), sub2(h1, 0x4140), sub2(h0, 0x4342), sub2(h1, 0x4342), bhi, zero);
+                mma16816(dlo, w0 & kl, w1 & kl, v0 & kl, v1 & kl, blo, zero);
+                mma16816(dhi, w0 & kh, w1 & kh, v0 & kh, v1 & kh, bhi, zero);
             } else {
                 const float clo[4] = {dlo[0], dlo[1], dlo[2], dlo[3]};
                 const float chi[4] = {dhi[0], dhi[1], dhi[2], dhi[3]};
-                mma16816(dlo, sub2(l0, 0x4140), sub2(l1, 0x4140), sub2(l0, 0x4342), sub2(l1, 0x4342), blo, clo);
-                mma16816(dhi, sub2(h0, 0x4140), sub2(h1, 0x4140), sub2(h0, 0x4342), sub2(h1, 0x4342), bhi, chi);
+                mma16816(dlo, w0 & kl, w1 & kl, v0 & kl, v1 & kl, blo, clo);
+                mma16816(dhi, w0 & kh, w1 & kh, v0 & kh, v1 & kh, bhi, chi);
             }
         }
         // this lane's sub-block in chunk c, if any: j = 2c + (t & 1) with (c & 1) == (t >> 1)
         if ((uint32_t)(c & 1) == (t >> 1)) {
             const int slot = c >> 1, j = 2 * c + (int)(t & 1u);
             const float *D = (t & 1u) ? dhi : dlo;
+            const float unit = (t & 1u) ? kTwo24 * 0.0625f : kTwo24;   // high nibbles came as 16 q
             const float sx = xs[2 * j] + xs[2 * j + 1];
-            o0 += dsc[0][slot] * ((D[0] + D[1]) * kTwo24) - dmn[0][slot] * sx;
-            o1 += dsc[1][slot] * ((D[2] + D[3]) * kTwo24) - dmn[1][slot] * sx;
+            o0 += dsc[0][slot] * ((D[0] + D[1]) * unit) - dmn[0][slot] * sx;
+            o1 += dsc[1][slot] * ((D[2] + D[3]) * unit) - dmn[1][slot] * sx;
         }
     }
 }
@@ -545,7 +554,8 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const int g = (int)(lane >> 2), t4 = (int)(lane & 3u);
-    const float out_scale = mv_stage_x(a, h, xarea);   // waits for the preceding kernel
+    // waits for the preceding kernel; a CTA's tasks are all of its segment's type
+    const float out_scale = mv_stage_x(a, h, xarea, a.seg[c.seg].type == 12u);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
     const uint32_t step = kMvWarps / a.st, u = warp % a.st;
     uint32_t ri = warp / a.st, ph = 0;
