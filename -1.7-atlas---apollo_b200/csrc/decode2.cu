@@ -80,7 +80,7 @@ __host__ __device__ constexpr uint32_t mv_tile_bytes(uint32_t tslots)
 // << 4 | log2 copies << 8 | block << 16 - and the copies' misalignments.
 __host__ __device__ constexpr uint32_t mv_desc_bytes(uint32_t nslot)
 {
-    return align128(nslot * (8u * 16u + kMvMaxPortions * 16u));
+    return align128(nslot * (kMvMaxSt * 16u + kMvMaxPortions * 16u));
 }
 __host__ __device__ constexpr uint32_t mv_x_bytes(uint32_t cols) { return align128(cols * 4u + cols / 16u * 4u); }
 
@@ -178,7 +178,7 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
             const Portion q = pick(pr, p);
             const uint32_t b = q.b0 + (jt - q.j);
             const uint32_t base = ri * a.slot_bytes + q.off + (b - q.b0) * mv_bb(a.seg[q.s].type);
-            h->desc[ri * 8u + lane] =
+            h->desc[ri * kMvMaxSt + lane] =
                 make_uint4(base, q.cstride | (q.rstride << 16), q.t, q.s | (p << 4) | (q.c << 8) | (b << 16));
         }
         // lane L: copy L % 16 of runs L / 16 and L / 16 + 2
@@ -545,9 +545,10 @@ __device__ __forceinline__ void q4k_task(const uint8_t *blk, uint32_t lc, uint32
     }
 }
 
-// Consumer warp w: task u = w % st of every (8 / st)-th slot starting at
-// slot w / st - i.e. positions w + 8m of the CTA's task order; the
-// producer's descriptor gives the task's tile, block and place in the ring.
+// Consumer warp w: positions w + 8m of the CTA's task order - task u = w % st
+// of every (8 / st)-th slot starting at slot w / st when st <= 8, tasks w and
+// w + 8 of every slot when st = 16; the producer's descriptor gives the
+// task's tile, block and place in the ring.
 // Returns false after a failed wait (status recorded).
 __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uint8_t *ring, const MvCta &c,
                             volatile uint32_t *err, MvBest &best)
@@ -557,8 +558,9 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
     // waits for the preceding kernel; a CTA's tasks are all of its segment's type
     const float out_scale = mv_stage_x(a, h, xarea, a.seg[c.seg].type == 12u);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
-    const uint32_t step = kMvWarps / a.st, u = warp % a.st;
-    uint32_t ri = warp / a.st, ph = 0;
+    const uint32_t per = a.st > (uint32_t)kMvWarps ? a.st / kMvWarps : 1u;    // tasks per slot visit
+    const uint32_t step = a.st > (uint32_t)kMvWarps ? 1u : kMvWarps / a.st, u = warp % a.st;
+    uint32_t ri = warp / a.st, ph = 0, qi = 0;
     while (ri >= a.nslot) { ri -= a.nslot; ph ^= 1u; }
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     uint32_t cur = 0xffffffffu, cur_lc[2] = {0u, 0u};
@@ -567,10 +569,10 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
     const uint32_t L = c.j1 - c.j0;
     for (uint32_t i = warp; i < L; i += kMvWarps) {   // task positions w + 8m
         uint32_t ok = 1u;
-        if (lane == 0 && !ready) ok = mbar_wait(&h->full[ri], ph, err) ? 1u : 0u;
+        if (qi == 0u && lane == 0 && !ready) ok = mbar_wait(&h->full[ri], ph, err) ? 1u : 0u;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) return false;
-        const uint4 dsc = h->desc[ri * 8u + u];
+        const uint4 dsc = h->desc[ri * kMvMaxSt + u + (uint32_t)kMvWarps * qi];
         const uint32_t t = dsc.z, s = dsc.w & 15u, run = (dsc.w >> 4) & 15u, lc = (dsc.w >> 8) & 15u, b = dsc.w >> 16;
         const uint32_t cstride = dsc.y & 0xffffu, rstride = dsc.y >> 16;
         // probe the next slot now; the answer is used one task later
@@ -579,8 +581,12 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
             rn -= a.nslot;
             pn ^= 1u;
         }
-        ready = 0u;
-        if (lane == 0 && i + kMvWarps < L) ready = mbar_test(&h->full[rn], pn) ? 1u : 0u;
+        // a warp's last task of this slot visit releases the slot
+        const bool last = qi + 1u == per || i + kMvWarps >= L;
+        if (qi == 0u) {
+            ready = 0u;
+            if (lane == 0 && i + per * kMvWarps < L) ready = mbar_test(&h->full[rn], pn) ? 1u : 0u;
+        }
         if (t != cur) {
             if (cur != 0xffffffffu) mv_flush(a, h, c, cur, cur_lc, acc, out_scale, pre, best);
             cur = t;
@@ -609,7 +615,7 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
             o1 = p1[0];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&h->empty[ri]);
+        if (last && lane == 0) mbar_arrive(&h->empty[ri]);
         if (a.paired && (s & 1u)) {
             acc[1][0] += o0;
             acc[1][1] += o1;
@@ -617,8 +623,13 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
             acc[0][0] += o0;
             acc[0][1] += o1;
         }
-        ri = rn;
-        ph = pn;
+        if (last) {
+            ri = rn;
+            ph = pn;
+            qi = 0u;
+        } else {
+            ++qi;
+        }
     }
     if (cur != 0xffffffffu) mv_flush(a, h, c, cur, cur_lc, acc, out_scale, pre, best);
     return true;
@@ -636,7 +647,7 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
     volatile uint32_t *err = a.status;
     // a consumer waits for a slot kMvWarps / st slots after its previous one:
     // with fewer ring entries its parity wait would alias an older phase
-    if (a.st == 0u || a.nslot > (uint32_t)kMvMaxSlots || a.nslot * a.st < (uint32_t)kMvWarps) {
+    if (a.st == 0u || a.st > kMvMaxSt || a.nslot > (uint32_t)kMvMaxSlots || a.nslot * a.st < (uint32_t)kMvWarps) {
         if (threadIdx.x == 0) atomicCAS(a.status, kStatusOk, kStatusBadArgument);
         return;
     }
@@ -644,10 +655,10 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
         h->tcnt = reinterpret_cast<uint32_t *>(tiles);
         h->tpart = reinterpret_cast<float *>(tiles + mv_tcnt_bytes(a.tslots));
         h->desc = reinterpret_cast<uint4 *>(descs);
-        h->lead = descs + a.nslot * 8u * 16u;
+        h->lead = descs + a.nslot * kMvMaxSt * 16u;
         for (uint32_t i = 0; i < a.nslot; ++i) {
             mbar_init(&h->full[i], 1u);
-            mbar_init(&h->empty[i], a.st);
+            mbar_init(&h->empty[i], min(a.st, (uint32_t)kMvWarps));   // one arrival per warp with tasks in it
         }
         for (uint32_t i = 0; i < a.tslots; ++i) h->tcnt[i] = 0u;
         fence_mbar_init();

@@ -93,6 +93,7 @@ constexpr int kMvThreads = (kMvWarps + 1) * 32;   // + one producer warp
 constexpr int kMvMaxSlots = 8;
 constexpr int kMvMaxTileSlots = 128;              // open tiles tracked in shared memory, at most
 constexpr int kMvMaxPortions = 4;                 // (tile, segment) runs in one slot
+constexpr uint32_t kMvMaxSt = 16;                 // tasks per ring slot, at most (16: two per warp)
 
 // MV_PART: partial rows of a row-split projection, pushed to every rank
 enum MvEpi : uint32_t { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_LOGITS = 3, MV_PART = 4 };
@@ -118,7 +119,7 @@ struct MvArgs {
     MvSeg seg[3];
     uint32_t n_seg, paired, nb, cols;
     uint32_t epi;
-    uint32_t st;           // tasks per ring slot (1, 2, 4 or 8)
+    uint32_t st;           // tasks per ring slot (1, 2, 4, 8 or 16)
     uint32_t nslot;        // ring depth
     uint32_t slot_bytes;
     uint32_t tslots;       // open-tile slots: > (nslot + 1) * st / tasks per tile + 1

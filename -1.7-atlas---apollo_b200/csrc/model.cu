@@ -647,8 +647,11 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     // whatever its size), giving up co-residency with their neighbours.
     const uint32_t budgets[2] = {a.nb > 8u ? 227u * 1024u : kHalfSmBytes, 227u * 1024u};
     bool ok = false;
-    for (uint32_t budget : budgets) {
-        for (uint32_t st : {8u, 4u, 2u, 1u}) {
+    // The largest slot wins (per-slot costs - descriptors, copy issue,
+    // barrier round trips - dominate small slots), on the whole SM if it
+    // must: mv CTAs do not share an SM anyway (registers)
+    for (uint32_t st : {16u, 8u, 4u, 2u, 1u}) {
+        for (uint32_t budget : budgets) {
             // runs in a slot: a partial first run, whole rows, a partial last one
             const uint32_t npmax = std::min(st, (st - 1u) / a.nb + 2u);
             if (npmax > (uint32_t)d2::kMvMaxPortions) continue;
