@@ -713,17 +713,28 @@ __global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
 
 // ---------------------------------------------------------- attention ----
 
-struct __align__(16) AttnSmem {
-    float4 q[kAttnMaxGroup][32];        // RoPE'd queries of the group (128 dims)
+constexpr uint32_t kAttnWarps = kAttnThreads / 32u;
+constexpr uint32_t kAttnPer = kAttnTile / kAttnWarps;   // positions of a tile per warp
+
+struct AttnTiles {
     uint8_t k[2][kAttnTile * 512];      // staged K rows, as stored in the cache (fp32 or fp16), two tiles
     uint8_t v[2][kAttnTile * 512];      // staged V rows
+};
+
+struct __align__(16) AttnSmem {
+    float4 q[kAttnMaxGroup][32];        // RoPE'd queries of the group (128 dims)
+    union {
+        AttnTiles tl;
+        float wrec[kAttnWarps][kAttnMaxGroup][kRec];   // after the last tile: every warp's (acc, max, sum) per head
+    } u;
     float4 knew[32], vnew[32];          // the current token's RoPE'd k and its v
-    float cden[kAttnMaxGroup];
+    float rec[kAttnMaxGroup][kRec];     // this split's (acc[128], max, sum) per query head, read by the cluster
+    float cw[32];                       // last merge: weight of each cluster record
     float qinv[kAttnMaxGroup + 1];      // qwen3: 1 / rms of each query head and (last) of the new k
+    float cden;
     uint64_t bar[2];                    // tile arrival, per buffer
     uint32_t flag;
 };
-// followed by the combine weights cw[splits][kAttnMaxGroup]
 
 // 4 elements d4 of a staged cache row (fp32 or fp16 rows)
 __device__ __forceinline__ float4 kv_row4(const uint8_t *row, uint32_t d4, bool f16)
@@ -742,24 +753,79 @@ __device__ __forceinline__ float warp_maxf(float v)
     return v;
 }
 
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of every CTA of the cluster; shared-memory writes before it
+// are visible to the cluster's reads after it.
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The float at the same shared-memory offset as p in CTA `cta` of the cluster.
+__device__ __forceinline__ float ld_cluster(const float *p, uint32_t cta)
+{
+    uint32_t r;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(cta));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+    return v;
+}
+
+// Sums over the warp of GP values at once. Slot i of lane l holds the lane's
+// part of head i ^ (l >> (5 - log2 GP)); each of the first log2 GP levels
+// keeps half of the slots and adds the partner lane's matching slot, the
+// remaining levels are plain. Lane l ends with the sum of head
+// l >> (5 - log2 GP); every addition is own + partner of a butterfly over
+// lane distances 16, 8, 4, 2, 1, as in warp_sum.
+template <int GP>
+__device__ __forceinline__ float head_sums(float (&p)[GP])
+{
+    int lev = 0;
+#pragma unroll
+    for (int n = GP; n > 1; n >>= 1, ++lev) {
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) p[i] += __shfl_xor_sync(0xffffffffu, p[i + n / 2], 16 >> lev);
+    }
+    float v = p[0];
+#pragma unroll
+    for (int o = 16 >> lev; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 // Split-K flash-decode over the KV cache (gqa_single_token,
-// src/brain_runtime.c:1482-1528), one CTA per (KV head, split). The splits in
-// use grow with the context (at least kAttnMinSpan positions each). A split's
+// src/brain_runtime.c:1482-1528). One CTA per (KV head, split); the splits in
+// use grow with the context (at least kAttnMinSpan positions each) and come
+// in clusters of kAttnCluster consecutive splits of one KV head. A split's
 // cached K and V rows are contiguous in the cache, so each tile of up to
 // kAttnTile positions arrives as two bulk copies into one of two buffers: the
 // tile after the current one is always in flight, and the first two are
 // issued before waiting for the preceding kernel (cached rows and the step's
-// position were written by earlier steps). Every warp takes one query head of the group,
-// lane = 4 of the 128 dimensions: one warp reduction per position's score,
-// online softmax per chunk of 32 positions, P.V. The
-// split holding the current position applies RoPE to the fresh k and
-// appends k and v to the cache (src/brain_runtime.c:1496-1500). The last
-// split of a KV head to finish combines all splits' (max, sum, acc) records.
+// position were written by earlier steps). The split holding the current
+// position applies RoPE to the fresh k and appends k and v to the cache
+// (src/brain_runtime.c:1496-1500).
+//
+// Warp w takes kAttnPer positions of every tile and all GP (>= group) query
+// heads of the KV head: lane = 4 of the 128 dimensions for the scores (one
+// K row read serves every head; head_sums reduces all heads' dot products in
+// one pass), then lane = (head, j) for the online softmax and P.V, holding
+// float4s j, j + 32 / GP, ... of its head (the head's lanes read adjacent
+// float4s of a V row: no bank conflicts). The warps' states merge into the
+// split's record per head; the cluster's CTA r merges head r over the
+// cluster's records (distributed
+// shared memory). With one cluster that is the output; otherwise the cluster
+// record goes to global memory and the last cluster to finish a head merges
+// all clusters' records of that head.
+template <int GP>
 __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem_a[];
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
-    float *cw = reinterpret_cast<float *>(smem_a + sizeof(AttnSmem));
     pdl_launch();
     const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
     if (pos >= a.max_context) {
@@ -768,10 +834,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
     }
     const uint32_t n = pos + 1u;
     const uint32_t ms = a.min_span ? a.min_span : kAttnMinSpan;
-    const uint32_t ns = min(a.splits, (n + ms - 1u) / ms);
+    // splits in use: whole clusters (a.splits is a multiple of the cluster size)
+    const uint32_t ns = min(a.splits, ((n + ms - 1u) / ms + kAttnCluster - 1u) / kAttnCluster * kAttnCluster);
     const uint32_t span = (n + ns - 1u) / ns;
     const uint32_t kvh = blockIdx.x / a.splits, s = blockIdx.x % a.splits;
-    if (s >= ns) return;
+    if (s >= ns) return;   // the whole cluster leaves
+    const uint32_t ncl = ns / kAttnCluster, cl = s / kAttnCluster;
     const uint32_t group = a.q_heads / a.kv_heads;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t t0 = min(s * span, n), t1 = min(n, t0 + span);
@@ -788,8 +856,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
         const uint32_t bytes = (ce - tb) * rowb;
         mbar_arrive_expect_tx(&sm.bar[b], 2u * bytes);
         if (bytes) {
-            bulk_g2s(sm.k[b], reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar[b]);
-            bulk_g2s(sm.v[b], reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes, &sm.bar[b]);
+            bulk_g2s(sm.u.tl.k[b], reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes,
+                     &sm.bar[b]);
+            bulk_g2s(sm.u.tl.v[b], reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes,
+                     &sm.bar[b]);
         }
     };
     if (threadIdx.x == 0) {
@@ -806,7 +876,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
         // qwen3 per-head RMSNorm before RoPE (src/brain_runtime.c:1727-1737,
         // rms_norm :1338-1371): warp w takes query head w, and the new k
         // (index group) where this split appends it
-        for (uint32_t hh = warp; hh <= group; hh += kAttnThreads / 32u) {
+        for (uint32_t hh = warp; hh <= group; hh += kAttnWarps) {
             if (hh == group && !has_pos) break;
             const float *src = hh < group ? a.q + (size_t)(kvh * group + hh) * 128u : a.k + (size_t)kvh * 128u;
             const float4 v = __ldcg(reinterpret_cast<const float4 *>(src) + lane);
@@ -860,116 +930,175 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
             reinterpret_cast<float *>(a.v_cache)[off] = vv;
         }
     }
+    constexpr uint32_t kL = GP == 8 ? 3u : GP == 4 ? 2u : GP == 2 ? 1u : 0u;
+    const uint32_t hm = lane >> (5u - kL);                       // this lane's head after head_sums
+    constexpr uint32_t kHs = 32u >> kL;                          // lanes per head
+    const uint32_t hl = lane & (kHs - 1u);                       // its place among them: float4s hl + kHs i
+    float4 qr[GP];
+#pragma unroll
+    for (int i = 0; i < GP; ++i) {
+        const uint32_t hh = (uint32_t)i ^ hm;
+        qr[i] = hh < group ? sm.q[hh][lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float m = -FLT_MAX, l = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 acc[GP];
+#pragma unroll
+    for (int i = 0; i < GP; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     uint32_t it = 0;
     for (uint32_t tb = t0; tb < t1; tb += kAttnTile, ++it) {
         const uint32_t te = min(tb + kAttnTile, t1), b = it & 1u;
-        const uint8_t *kt = sm.k[b], *vt = sm.v[b];
+        const uint8_t *kt = sm.u.tl.k[b], *vt = sm.u.tl.v[b];
         mbar_wait(&sm.bar[b], (it >> 1) & 1u, err);
-        if (warp < group) {
-            // lane = 4 of the 128 dimensions; scores of up to 32 positions,
-            // one warp reduction each (lane p keeps position p's score), then
-            // an online-softmax update and P.V for the chunk
-            const float4 qv = sm.q[warp][lane];
-            for (uint32_t sb = tb; sb < te; sb += 32u) {
-                const uint32_t np = min(32u, te - sb);
-                float sc = -FLT_MAX;
-#pragma unroll 4
-                for (uint32_t jj = 0; jj < np; ++jj) {
-                    const uint32_t p = sb + jj;
-                    const float4 kv = p == pos ? sm.knew[lane] : kv_row4(kt + (size_t)(p - tb) * rowb, lane, f16);
-                    float d = fmaf(qv.x, kv.x, qv.y * kv.y) + fmaf(qv.z, kv.z, qv.w * kv.w);
-                    d = warp_sum(d);
-                    if (lane == jj) sc = d * scale;
-                }
-                const float mn = fmaxf(m, warp_maxf(sc));
-                const float corr = expf(m - mn);
-                const float w = lane < np ? expf(sc - mn) : 0.f;
-                l = l * corr + warp_sum(w);
-                acc.x *= corr; acc.y *= corr; acc.z *= corr; acc.w *= corr;
-#pragma unroll 4
-                for (uint32_t jj = 0; jj < np; ++jj) {
-                    const float wj = __shfl_sync(0xffffffffu, w, (int)jj);
-                    const uint32_t pj = sb + jj;
-                    const float4 vv = pj == pos ? sm.vnew[lane] : kv_row4(vt + (size_t)(pj - tb) * rowb, lane, f16);
-                    acc.x = fmaf(wj, vv.x, acc.x);
-                    acc.y = fmaf(wj, vv.y, acc.y);
-                    acc.z = fmaf(wj, vv.z, acc.z);
-                    acc.w = fmaf(wj, vv.w, acc.w);
-                }
-                m = mn;
+        const uint32_t p0 = tb + kAttnPer * warp;   // this warp's positions p0 .. p0 + kAttnPer - 1
+        float sc[kAttnPer];
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnPer; ++j) {
+            const uint32_t p = p0 + j;
+            sc[j] = -FLT_MAX;
+            if (p < te) {
+                const float4 kv = p == pos ? sm.knew[lane] : kv_row4(kt + (size_t)(p - tb) * rowb, lane, f16);
+                float d[GP];
+#pragma unroll
+                for (int i = 0; i < GP; ++i)
+                    d[i] = fmaf(qr[i].x, kv.x, qr[i].y * kv.y) + fmaf(qr[i].z, kv.z, qr[i].w * kv.w);
+                sc[j] = head_sums<GP>(d) * scale;
             }
         }
+        float mc = sc[0];
+#pragma unroll
+        for (uint32_t j = 1; j < kAttnPer; ++j) mc = fmaxf(mc, sc[j]);
+        const float mn = fmaxf(m, mc);
+        const float corr = expf(m - mn);
+        float w[kAttnPer], ws = 0.f;
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnPer; ++j) {
+            w[j] = p0 + j < te ? expf(sc[j] - mn) : 0.f;
+            ws += w[j];
+        }
+        l = l * corr + ws;
+#pragma unroll
+        for (int i = 0; i < GP; ++i) {
+            acc[i].x *= corr;
+            acc[i].y *= corr;
+            acc[i].z *= corr;
+            acc[i].w *= corr;
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnPer; ++j) {
+            const uint32_t p = p0 + j;
+            if (p < te) {
+                const uint8_t *vr = vt + (size_t)(p - tb) * rowb;
+#pragma unroll
+                for (int i = 0; i < GP; ++i) {
+                    const uint32_t d4 = hl + kHs * (uint32_t)i;   // the head's lanes read adjacent float4s
+                    const float4 vv = p == pos ? sm.vnew[d4] : kv_row4(vr, d4, f16);
+                    acc[i].x = fmaf(w[j], vv.x, acc[i].x);
+                    acc[i].y = fmaf(w[j], vv.y, acc[i].y);
+                    acc[i].z = fmaf(w[j], vv.z, acc[i].z);
+                    acc[i].w = fmaf(w[j], vv.w, acc[i].w);
+                }
+            }
+        }
+        m = mn;
         __syncthreads();   // tile consumed: its buffer takes the tile after next
         if (threadIdx.x == 0 && tb + 2u * kAttnTile < t1) issue(tb + 2u * kAttnTile, b);
     }
-    if (warp < group) {
-        float *dst = a.part + (((size_t)kvh * a.splits + s) * group + warp) * kRec;
-        reinterpret_cast<float4 *>(dst)[lane] = acc;
-        if (lane == 0) { dst[128] = m; dst[129] = l; }
+    // every copy was consumed: the tile buffers hold the warps' states now
+    if (hm < group) {
+        float *dst = sm.u.wrec[warp][hm];
+#pragma unroll
+        for (int i = 0; i < GP; ++i) reinterpret_cast<float4 *>(dst)[hl + kHs * (uint32_t)i] = acc[i];
+        if (hl == 0u) {
+            dst[128] = m;
+            dst[129] = l;
+        }
+    }
+    __syncthreads();
+    {
+        const uint32_t hh = threadIdx.x >> 5, d4 = lane;   // 8 heads x 32 float4
+        if (hh < group) {
+            float M = -FLT_MAX;
+#pragma unroll
+            for (uint32_t w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm.u.wrec[w][hh][128]);
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            float L = 0.f;
+#pragma unroll
+            for (uint32_t w = 0; w < kAttnWarps; ++w) {
+                const float e = expf(sm.u.wrec[w][hh][128] - M);
+                const float4 v = reinterpret_cast<const float4 *>(sm.u.wrec[w][hh])[d4];
+                L = fmaf(e, sm.u.wrec[w][hh][129], L);
+                o.x = fmaf(e, v.x, o.x);
+                o.y = fmaf(e, v.y, o.y);
+                o.z = fmaf(e, v.z, o.z);
+                o.w = fmaf(e, v.w, o.w);
+            }
+            reinterpret_cast<float4 *>(sm.rec[hh])[d4] = o;
+            if (d4 == 0u) {
+                sm.rec[hh][128] = M;
+                sm.rec[hh][129] = L;
+            }
+        }
+    }
+    cluster_sync_all();
+    // CTA r of the cluster merges head r over the cluster's records; thread = dimension
+    const uint32_t hh = cluster_ctarank();
+    const bool merges = hh < group;
+    float o = 0.f, L = 0.f, M = -FLT_MAX;
+    if (merges && threadIdx.x < 128u) {
+        float mc[kAttnCluster];
+#pragma unroll
+        for (uint32_t c = 0; c < kAttnCluster; ++c) {
+            mc[c] = ld_cluster(&sm.rec[hh][128], c);
+            M = fmaxf(M, mc[c]);
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < kAttnCluster; ++c) {
+            const float e = expf(mc[c] - M);
+            L = fmaf(e, ld_cluster(&sm.rec[hh][129], c), L);
+            o = fmaf(e, ld_cluster(&sm.rec[hh][threadIdx.x], c), o);
+        }
+    }
+    cluster_sync_all();   // no CTA leaves while the cluster may still read its records
+    if (!merges) return;
+    float *out = a.att + (size_t)(kvh * group + hh) * 128u;
+    if (ncl == 1u) {
+        if (threadIdx.x < 128u) out[threadIdx.x] = o * (L > 0.f ? 1.0f / L : 0.f);
+        return;
+    }
+    float *crec = a.part + (((size_t)kvh * (a.splits / kAttnCluster) + cl) * group + hh) * kRec;
+    if (threadIdx.x < 128u) crec[threadIdx.x] = o;
+    if (threadIdx.x == 0) {
+        crec[128] = M;
+        crec[129] = L;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        const uint32_t old = atom_acq_rel_add(a.ctr + kvh, 1u);
-        sm.flag = (old == ns - 1u) ? 1u : 0u;
-        if (sm.flag) a.ctr[kvh] = 0u;
+        uint32_t *ctr = a.ctr + kvh * group + hh;
+        const uint32_t old = atom_acq_rel_add(ctr, 1u);
+        sm.flag = (old == ncl - 1u) ? 1u : 0u;
+        if (sm.flag) *ctr = 0u;
     }
     __syncthreads();
     if (!sm.flag) return;
     __threadfence();
-    // combine: weights exp(m_s - M) per split and head, then the weighted
-    // sums; every thread issues its loads of the partial records 16 splits
-    // at a time (they come from L2)
-    for (uint32_t hq = warp; hq < group; hq += kAttnThreads / 32u) {
-        float2 ml[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const uint32_t q = lane + 32u * (uint32_t)r;
-            ml[r] = q < ns ? __ldcg(reinterpret_cast<const float2 *>(a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u))
-                           : make_float2(-FLT_MAX, 0.f);
-        }
-        float M = fmaxf(ml[0].x, ml[1].x);
-        for (uint32_t q = lane + 64u; q < ns; q += 32u)
-            M = fmaxf(M, __ldcg(a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u));
-        M = warp_maxf(M);
-        float den = 0.f;
-        for (uint32_t q = lane; q < ns; q += 32u) {
-            const float2 v = q < 32u ? ml[0] : q < 64u ? ml[1]
-                                     : __ldcg(reinterpret_cast<const float2 *>(a.part + (((size_t)kvh * a.splits + q) * group + hq) * kRec + 128u));
-            const float w = expf(v.x - M);
-            cw[q * kAttnMaxGroup + hq] = w;
-            den += w * v.y;
-        }
-        den = warp_sum(den);
-        if (lane == 0) sm.cden[hq] = den;
+    // the last cluster of head hh merges every cluster's record of it
+    const float *rec0 = a.part + ((size_t)kvh * (a.splits / kAttnCluster) * group + hh) * kRec;
+    const size_t cstride = (size_t)group * kRec;
+    if (warp == 0) {
+        const float mcl = lane < ncl ? __ldcg(rec0 + lane * cstride + 128u) : -FLT_MAX;
+        const float Mx = warp_maxf(mcl);
+        const float e = lane < ncl ? expf(mcl - Mx) : 0.f;
+        const float den = warp_sum(lane < ncl ? e * __ldcg(rec0 + lane * cstride + 129u) : 0.f);
+        sm.cw[lane] = e;
+        if (lane == 0) sm.cden = den;
     }
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < group * 32u; i += kAttnThreads) {
-        const uint32_t hq = i >> 5, d4 = i & 31u;
-        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t q0 = 0; q0 < ns; q0 += 16u) {
-            float4 v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (q0 + j < ns)
-                    v[j] = __ldcg(reinterpret_cast<const float4 *>(
-                        a.part + (((size_t)kvh * a.splits + q0 + j) * group + hq) * kRec) + d4);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (q0 + j < ns) {
-                    const float w = cw[(q0 + j) * kAttnMaxGroup + hq];
-                    num.x = fmaf(w, v[j].x, num.x);
-                    num.y = fmaf(w, v[j].y, num.y);
-                    num.z = fmaf(w, v[j].z, num.z);
-                    num.w = fmaf(w, v[j].w, num.w);
-                }
-        }
-        const float den = sm.cden[hq];
-        const float inv = den > 0.f ? 1.0f / den : 0.f;
-        reinterpret_cast<float4 *>(a.att + (size_t)(kvh * group + hq) * 128u)[d4] =
-            make_float4(num.x * inv, num.y * inv, num.z * inv, num.w * inv);
+    if (threadIdx.x < 128u) {
+        float num = 0.f;
+        for (uint32_t c = 0; c < ncl; ++c) num = fmaf(sm.cw[c], __ldcg(rec0 + c * cstride + threadIdx.x), num);
+        const float den = sm.cden;
+        out[threadIdx.x] = num * (den > 0.f ? 1.0f / den : 0.f);
     }
 }
 
@@ -1090,19 +1219,37 @@ using namespace atlas::d2;
 
 namespace {
 
-cudaError_t launch_ex(const void *fn, void **args, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl)
+// cluster > 1: clusters of that many consecutive CTAs (grid.x a multiple of it)
+cudaError_t launch_ex(const void *fn, void **args, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      uint32_t cluster = 1)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = at;
     cfg.numAttrs = 1;
+    if (cluster > 1) {
+        at[1].id = cudaLaunchAttributeClusterDimension;
+        at[1].val.clusterDim.x = cluster;
+        at[1].val.clusterDim.y = 1;
+        at[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+    }
     return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// attention instance for `group` query heads per KV head (rounded up to a power of two)
+const void *attn_fn(uint32_t group)
+{
+    if (group <= 1u) return (const void *)attn_kernel<1>;
+    if (group <= 2u) return (const void *)attn_kernel<2>;
+    if (group <= 4u) return (const void *)attn_kernel<4>;
+    return (const void *)attn_kernel<8>;
 }
 
 }  // namespace
@@ -1113,9 +1260,33 @@ extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_
            (size_t)nslot * slot_bytes;
 }
 
+// Clusters of the attention launch (kAttnCluster CTAs each) that fit on the
+// device at once, for `group` query heads per KV head; 0 on error.
+extern "C" int atlas_d2_attn_max_clusters(uint32_t group)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kAttnCluster * 64u);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kAttnCluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaFuncSetAttribute(attn_fn(group), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem)) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, attn_fn(group), &cfg) != cudaSuccess)
+        return 0;
+    return n;
+}
+
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits)
 {
-    return sizeof(AttnSmem) + (size_t)splits * kAttnMaxGroup * sizeof(float);
+    (void)splits;
+    return sizeof(AttnSmem);
 }
 
 // Raise the kernels' dynamic shared-memory limits (call before any capture).
@@ -1123,7 +1294,11 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
 {
     cudaError_t e = cudaFuncSetAttribute(mv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem);
+    for (uint32_t g = 1; g <= kAttnMaxGroup; g *= 2u)
+        if ((e = cudaFuncSetAttribute(attn_fn(g), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem)) !=
+            cudaSuccess)
+            return e;
+    return cudaSuccess;
 }
 
 extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaStream_t stream)
@@ -1137,8 +1312,12 @@ extern "C" cudaError_t atlas_d2_launch_attn(const AttnArgs *a, uint32_t grid, cu
 {
     AttnArgs copy = *a;
     void *args[] = {&copy};
-    return launch_ex((const void *)attn_kernel, args, dim3(grid), dim3(kAttnThreads), atlas_d2_attn_smem(a->splits),
-                     stream, true);
+    const uint32_t group = a->q_heads / a->kv_heads;
+    if (group == 0u || group > kAttnMaxGroup || a->splits % kAttnCluster != 0u || a->splits / kAttnCluster > 32u ||
+        grid != a->kv_heads * a->splits)
+        return cudaErrorInvalidValue;
+    return launch_ex(attn_fn(group), args, dim3(grid), dim3(kAttnThreads), atlas_d2_attn_smem(a->splits), stream, true,
+                     kAttnCluster);
 }
 
 extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,

@@ -152,6 +152,7 @@ struct MvArgs {
 constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kAttnTile = 32;      // cached positions staged per tile (two tiles in flight)
 constexpr uint32_t kAttnMinSpan = 16;   // positions per split, at least
+constexpr uint32_t kAttnCluster = 8;    // consecutive splits of a KV head merged in one thread-block cluster
 constexpr uint32_t kAttnMaxGroup = 8;   // query heads per KV head (one warp each)
 constexpr uint32_t kRec = 132;          // partial record: acc[128], max, sum, 2 pad
 
@@ -159,8 +160,8 @@ struct AttnArgs {
     const float *q, *k, *v;     // projections of the current token (+bias, no RoPE)
     void *k_cache, *v_cache;    // this layer's [kv_heads][max_context][128]
     float *att;                 // [q_heads][128]
-    float *part;                // [kv_heads][splits][group][kRec]
-    uint32_t *ctr;              // per KV head, zero between launches
+    float *part;                // cluster records [kv_heads][splits / kAttnCluster][group][kRec]
+    uint32_t *ctr;              // per query head, zero between launches
     const float2 *rope;         // (cos, sin) [position][64]
     DecState *st;
     uint32_t q_heads, kv_heads, max_context, splits, kv_fp16;

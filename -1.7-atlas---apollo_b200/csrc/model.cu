@@ -40,6 +40,7 @@ extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t 
 extern "C" cudaError_t atlas_launch_prefill_attn_tc(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots);
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits);
+extern "C" int atlas_d2_attn_max_clusters(uint32_t group);
 extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
 extern "C" cudaError_t atlas_d2_launch_mv(const atlas::d2::MvArgs *a, uint32_t grid, cudaStream_t stream);
 extern "C" cudaError_t atlas_d2_launch_attn(const atlas::d2::AttnArgs *a, uint32_t grid, cudaStream_t stream);
@@ -715,11 +716,18 @@ int build_graph2(AtlasCuda *h)
     if (rc) return rc;
     CU(h, cudaMemset(g.st, 0, sizeof(d2::DecState)));
     g.status = &g.st->status;
-    // two attention CTAs fit on an SM: up to two splits per SM and KV head
-    g.splits = std::max(1u, std::min(2u * G / sl.kv_heads, 160u));
-    if ((rc = dalloc(h, &g.apart, (size_t)sl.kv_heads * g.splits * group * d2::kRec * sizeof(float)))) return rc;
-    if ((rc = dalloc(h, &g.actr, (size_t)sl.kv_heads * 4u))) return rc;
-    CU(h, cudaMemset(g.actr, 0, (size_t)sl.kv_heads * 4u));
+    // two attention CTAs fit on an SM: up to two splits per SM and KV head,
+    // in whole clusters, and at most 3/4 of the clusters the device holds at
+    // once (a second wave doubles the launch at long contexts; a full first
+    // wave waits for the last free SMs of a GPC as the preceding kernel drains)
+    const uint32_t C = d2::kAttnCluster;
+    g.splits = std::max(C, std::min(2u * G / sl.kv_heads, 160u) / C * C);
+    const int max_cl = atlas_d2_attn_max_clusters(group);
+    if (max_cl > 0) g.splits = std::max(C, std::min(g.splits, (uint32_t)max_cl * 3u / 4u / sl.kv_heads * C));
+    if (const char *e = getenv("ATLAS_ATTN_SPLITS")) g.splits = std::max(C, std::min(160u, (uint32_t)atoi(e)) / C * C);
+    if ((rc = dalloc(h, &g.apart, (size_t)sl.kv_heads * (g.splits / C) * group * d2::kRec * sizeof(float)))) return rc;
+    if ((rc = dalloc(h, &g.actr, (size_t)sl.q_heads * 4u))) return rc;
+    CU(h, cudaMemset(g.actr, 0, (size_t)sl.q_heads * 4u));
 
     const AtlasCuda::W &w0 = h->layers[0];
     const uint32_t o_cols = sl.o_blocks * 256u;
@@ -918,7 +926,7 @@ int run_graph2(AtlasCuda *h, uint32_t token, uint32_t pos, uint32_t steps, uint3
         }
         const int rc = status_to_code(h, out.status);
         // clear what a failed step may have left behind
-        cudaMemsetAsync(g.actr, 0, (size_t)h->sl.kv_heads * 4u, h->stream);
+        cudaMemsetAsync(g.actr, 0, (size_t)h->sl.q_heads * 4u, h->stream);
         cudaMemsetAsync(g.st, 0, sizeof(d2::DecState), h->stream);
         cudaStreamSynchronize(h->stream);
         return rc;

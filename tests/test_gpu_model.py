@@ -149,11 +149,13 @@ def test_wide_shapes_match_oracle(torch_cuda, oracle, model_dir, name):
 
 
 @pytest.mark.slow
-def test_long_splits_match_oracle(torch_cuda, oracle, tiny_model, monkeypatch):
-    """Decode attention with many K/V tiles per split (the double-buffered
-    tile loop): a 1400-token prompt with splits of >= 192 positions (6 tiles
-    each), then 8 greedy steps, against the oracle."""
-    monkeypatch.setenv("ATLAS_ATTN_MIN_SPAN", "192")
+@pytest.mark.parametrize("min_span", ["192", "8"])
+def test_long_splits_match_oracle(torch_cuda, oracle, tiny_model, monkeypatch, min_span):
+    """Decode attention over a 1400-token prompt, then 8 greedy steps, against
+    the oracle: splits of >= 192 positions (one cluster of 8 splits, 6 K/V
+    tiles each: the double-buffered tile loop) and of >= 8 positions (18
+    clusters: the merge of cluster records in global memory)."""
+    monkeypatch.setenv("ATLAS_ATTN_MIN_SPAN", min_span)
     prompt = np.random.default_rng(11).integers(0, 1024, 1400).astype(np.uint32)
     m = oracle.open(tiny_model)
     m.begin(1500)
