@@ -1210,8 +1210,13 @@ int launch_split(AtlasCuda *h, const float *x, uint32_t cols, uint32_t tokens, c
 }
 
 // Attention units for `n` prompt tokens at positions pos0..pos0+n-1: per KV
-// head and tile of 8 queries, the cached positions [0, pos0 + tile end) cut
-// into spans sized so that all units make about three waves over the SMs.
+// head and tile of 128 / group queries, the cached positions
+// [0, pos0 + tile end) cut into spans of whole 64-key chunks. When one unit
+// per tile fits in one wave over the SMs, the spans are the shortest that
+// keep all units in one wave (every unit loads and splits its 128 query rows,
+// so short spans pay that again and again: at 512 tokens of the 3B shape,
+// 192-key spans take 1.72 ms for 4 layers where 64-key spans took 1.84);
+// otherwise they are sized so that all units make about three waves.
 int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
 {
     const AtlasModelDesc &d = h->desc;
@@ -1220,9 +1225,25 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
     const uint32_t group = d.q_heads / d.kv_heads, qtok = std::max(1u, 128u / group);
     const uint32_t G = (uint32_t)h->sm_count, qt_n = (n + qtok - 1) / qtok;
     uint64_t chunks = 0;
-    for (uint32_t qt = 0; qt < qt_n; ++qt) chunks += (pos0 + std::min(qtok * qt + qtok, n) + 63) / 64;
+    uint32_t max_chunks = 1;
+    for (uint32_t qt = 0; qt < qt_n; ++qt) {
+        const uint32_t c = (pos0 + std::min(qtok * qt + qtok, n) + 63) / 64;
+        chunks += c;
+        max_chunks = std::max(max_chunks, c);
+    }
     chunks *= sl.kv_heads;
     uint32_t span_chunks = (uint32_t)std::max<uint64_t>(1, (chunks + 3 * G - 1) / (3 * G));
+    if ((uint64_t)qt_n * sl.kv_heads <= G) {
+        auto units = [&](uint32_t sc) {
+            uint64_t u = 0;
+            for (uint32_t qt = 0; qt < qt_n; ++qt)
+                u += ((pos0 + std::min(qtok * qt + qtok, n) + 63) / 64 + sc - 1) / sc;
+            return u * sl.kv_heads;
+        };
+        span_chunks = 1;
+        while (span_chunks < max_chunks && units(span_chunks) > G) ++span_chunks;
+    }
+    if (const char *e = getenv("ATLAS_PF_ATTN_SPAN_CHUNKS")) span_chunks = (uint32_t)std::max(1, atoi(e));
     std::vector<uint32_t> tab;
     for (;;) {
         tab.clear();
