@@ -721,10 +721,18 @@ struct AttnTiles {
     uint8_t v[2][kAttnTile * 512];      // staged V rows
 };
 
+// attn_tc16_kernel: tiles of 64 fp16 rows, padded to 272 bytes
+constexpr uint32_t kTcTile = 64, kTcRowH = 136;
+struct AttnTcTiles {
+    __half k[2][kTcTile][kTcRowH];
+    __half v[2][kTcTile][kTcRowH];
+};
+
 struct __align__(16) AttnSmem {
     float4 q[kAttnMaxGroup][32];        // RoPE'd queries of the group (128 dims)
     union {
         AttnTiles tl;
+        AttnTcTiles tc;
         float wrec[kAttnWarps][kAttnMaxGroup][kRec];   // after the last tile: every warp's (acc, max, sum) per head
     } u;
     float4 knew[32], vnew[32];          // the current token's RoPE'd k and its v
@@ -821,56 +829,13 @@ __device__ __forceinline__ float head_sums(float (&p)[GP])
 // shared memory). With one cluster that is the output; otherwise the cluster
 // record goes to global memory and the last cluster to finish a head merges
 // all clusters' records of that head.
-template <int GP>
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a)
+// After the predecessor wait: the group's queries (qwen3 norm, RoPE) into
+// shared memory, and in the split that owns the current position the new k
+// (norm, RoPE) and v, appended to the cache. All threads.
+__device__ __forceinline__ void attn_stage_qkv(const AttnArgs &a, AttnSmem &sm, uint32_t kvh, uint32_t group,
+                                               uint32_t pos, bool has_pos, bool f16, size_t head_row0)
 {
-    extern __shared__ __align__(16) uint8_t smem_a[];
-    AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
-    pdl_launch();
-    const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
-    if (pos >= a.max_context) {
-        if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&a.st->status, kStatusOk, kStatusBadArgument);
-        return;
-    }
-    const uint32_t n = pos + 1u;
-    const uint32_t ms = a.min_span ? a.min_span : kAttnMinSpan;
-    // splits in use: whole clusters (a.splits is a multiple of the cluster size)
-    const uint32_t ns = min(a.splits, ((n + ms - 1u) / ms + kAttnCluster - 1u) / kAttnCluster * kAttnCluster);
-    const uint32_t span = (n + ns - 1u) / ns;
-    const uint32_t kvh = blockIdx.x / a.splits, s = blockIdx.x % a.splits;
-    if (s >= ns) return;   // the whole cluster leaves
-    const uint32_t ncl = ns / kAttnCluster, cl = s / kAttnCluster;
-    const uint32_t group = a.q_heads / a.kv_heads;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t t0 = min(s * span, n), t1 = min(n, t0 + span);
-    const bool has_pos = t0 <= pos && pos < t1;
-    const bool f16 = a.kv_fp16 != 0u;
-    const uint32_t rowb = f16 ? 256u : 512u;
-    const float scale = 1.0f / sqrtf(128.0f);
-    volatile uint32_t *err = &a.st->status;
-    const size_t head_row0 = (size_t)kvh * a.max_context;
-    // tile [tb, tb + kAttnTile) of the split into buffer b: cached rows
-    // [tb, min(te, pos)) by bulk copies; two tiles are in flight
-    auto issue = [&](uint32_t tb, uint32_t b) {
-        const uint32_t te = min(tb + kAttnTile, t1), ce = max(tb, min(te, pos));
-        const uint32_t bytes = (ce - tb) * rowb;
-        mbar_arrive_expect_tx(&sm.bar[b], 2u * bytes);
-        if (bytes) {
-            bulk_g2s(sm.u.tl.k[b], reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes,
-                     &sm.bar[b]);
-            bulk_g2s(sm.u.tl.v[b], reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes,
-                     &sm.bar[b]);
-        }
-    };
-    if (threadIdx.x == 0) {
-        mbar_init(&sm.bar[0], 1u);
-        mbar_init(&sm.bar[1], 1u);
-        fence_mbar_init();
-        if (t0 < t1) issue(t0, 0u);
-        if (t0 + kAttnTile < t1) issue(t0 + kAttnTile, 1u);
-    }
-    __syncthreads();
-    pdl_wait();
     const bool qkn = a.q_norm != nullptr;
     if (qkn) {
         // qwen3 per-head RMSNorm before RoPE (src/brain_runtime.c:1727-1737,
@@ -930,89 +895,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
             reinterpret_cast<float *>(a.v_cache)[off] = vv;
         }
     }
-    constexpr uint32_t kL = GP == 8 ? 3u : GP == 4 ? 2u : GP == 2 ? 1u : 0u;
-    const uint32_t hm = lane >> (5u - kL);                       // this lane's head after head_sums
-    constexpr uint32_t kHs = 32u >> kL;                          // lanes per head
-    const uint32_t hl = lane & (kHs - 1u);                       // its place among them: float4s hl + kHs i
-    float4 qr[GP];
-#pragma unroll
-    for (int i = 0; i < GP; ++i) {
-        const uint32_t hh = (uint32_t)i ^ hm;
-        qr[i] = hh < group ? sm.q[hh][lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float m = -FLT_MAX, l = 0.f;
-    float4 acc[GP];
-#pragma unroll
-    for (int i = 0; i < GP; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    uint32_t it = 0;
-    for (uint32_t tb = t0; tb < t1; tb += kAttnTile, ++it) {
-        const uint32_t te = min(tb + kAttnTile, t1), b = it & 1u;
-        const uint8_t *kt = sm.u.tl.k[b], *vt = sm.u.tl.v[b];
-        mbar_wait(&sm.bar[b], (it >> 1) & 1u, err);
-        const uint32_t p0 = tb + kAttnPer * warp;   // this warp's positions p0 .. p0 + kAttnPer - 1
-        float sc[kAttnPer];
-#pragma unroll
-        for (uint32_t j = 0; j < kAttnPer; ++j) {
-            const uint32_t p = p0 + j;
-            sc[j] = -FLT_MAX;
-            if (p < te) {
-                const float4 kv = p == pos ? sm.knew[lane] : kv_row4(kt + (size_t)(p - tb) * rowb, lane, f16);
-                float d[GP];
-#pragma unroll
-                for (int i = 0; i < GP; ++i)
-                    d[i] = fmaf(qr[i].x, kv.x, qr[i].y * kv.y) + fmaf(qr[i].z, kv.z, qr[i].w * kv.w);
-                sc[j] = head_sums<GP>(d) * scale;
-            }
-        }
-        float mc = sc[0];
-#pragma unroll
-        for (uint32_t j = 1; j < kAttnPer; ++j) mc = fmaxf(mc, sc[j]);
-        const float mn = fmaxf(m, mc);
-        const float corr = expf(m - mn);
-        float w[kAttnPer], ws = 0.f;
-#pragma unroll
-        for (uint32_t j = 0; j < kAttnPer; ++j) {
-            w[j] = p0 + j < te ? expf(sc[j] - mn) : 0.f;
-            ws += w[j];
-        }
-        l = l * corr + ws;
-#pragma unroll
-        for (int i = 0; i < GP; ++i) {
-            acc[i].x *= corr;
-            acc[i].y *= corr;
-            acc[i].z *= corr;
-            acc[i].w *= corr;
-        }
-#pragma unroll
-        for (uint32_t j = 0; j < kAttnPer; ++j) {
-            const uint32_t p = p0 + j;
-            if (p < te) {
-                const uint8_t *vr = vt + (size_t)(p - tb) * rowb;
-#pragma unroll
-                for (int i = 0; i < GP; ++i) {
-                    const uint32_t d4 = hl + kHs * (uint32_t)i;   // the head's lanes read adjacent float4s
-                    const float4 vv = p == pos ? sm.vnew[d4] : kv_row4(vr, d4, f16);
-                    acc[i].x = fmaf(w[j], vv.x, acc[i].x);
-                    acc[i].y = fmaf(w[j], vv.y, acc[i].y);
-                    acc[i].z = fmaf(w[j], vv.z, acc[i].z);
-                    acc[i].w = fmaf(w[j], vv.w, acc[i].w);
-                }
-            }
-        }
-        m = mn;
-        __syncthreads();   // tile consumed: its buffer takes the tile after next
-        if (threadIdx.x == 0 && tb + 2u * kAttnTile < t1) issue(tb + 2u * kAttnTile, b);
-    }
-    // every copy was consumed: the tile buffers hold the warps' states now
-    if (hm < group) {
-        float *dst = sm.u.wrec[warp][hm];
-#pragma unroll
-        for (int i = 0; i < GP; ++i) reinterpret_cast<float4 *>(dst)[hl + kHs * (uint32_t)i] = acc[i];
-        if (hl == 0u) {
-            dst[128] = m;
-            dst[129] = l;
-        }
-    }
+}
+
+// The warps' (acc, max, sum) records of every head are in sm.u.wrec: merge
+// them into the split's record, then over the cluster (CTA r takes head r)
+// and, with several clusters, over the clusters of the KV head (the last
+// cluster to finish a head). All threads of every CTA of the cluster.
+__device__ __forceinline__ void attn_merge(const AttnArgs &a, AttnSmem &sm, uint32_t kvh, uint32_t group,
+                                           uint32_t cl, uint32_t ncl)
+{
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     __syncthreads();
     {
         const uint32_t hh = threadIdx.x >> 5, d4 = lane;   // 8 heads x 32 float4
@@ -1100,6 +992,341 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
         const float den = sm.cden;
         out[threadIdx.x] = num * (den > 0.f ? 1.0f / den : 0.f);
     }
+}
+
+template <int GP>
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem_a[];
+    AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
+    pdl_launch();
+    const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
+    if (pos >= a.max_context) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&a.st->status, kStatusOk, kStatusBadArgument);
+        return;
+    }
+    const uint32_t n = pos + 1u;
+    const uint32_t ms = a.min_span ? a.min_span : kAttnMinSpan;
+    // splits in use: whole clusters (a.splits is a multiple of the cluster size)
+    const uint32_t ns = min(a.splits, ((n + ms - 1u) / ms + kAttnCluster - 1u) / kAttnCluster * kAttnCluster);
+    const uint32_t span = (n + ns - 1u) / ns;
+    const uint32_t kvh = blockIdx.x / a.splits, s = blockIdx.x % a.splits;
+    if (s >= ns) return;   // the whole cluster leaves
+    const uint32_t ncl = ns / kAttnCluster, cl = s / kAttnCluster;
+    const uint32_t group = a.q_heads / a.kv_heads;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t t0 = min(s * span, n), t1 = min(n, t0 + span);
+    const bool has_pos = t0 <= pos && pos < t1;
+    const bool f16 = a.kv_fp16 != 0u;
+    const uint32_t rowb = f16 ? 256u : 512u;
+    const float scale = 1.0f / sqrtf(128.0f);
+    volatile uint32_t *err = &a.st->status;
+    const size_t head_row0 = (size_t)kvh * a.max_context;
+    // tile [tb, tb + kAttnTile) of the split into buffer b: cached rows
+    // [tb, min(te, pos)) by bulk copies; two tiles are in flight
+    auto issue = [&](uint32_t tb, uint32_t b) {
+        const uint32_t te = min(tb + kAttnTile, t1), ce = max(tb, min(te, pos));
+        const uint32_t bytes = (ce - tb) * rowb;
+        mbar_arrive_expect_tx(&sm.bar[b], 2u * bytes);
+        if (bytes) {
+            bulk_g2s(sm.u.tl.k[b], reinterpret_cast<const uint8_t *>(a.k_cache) + (head_row0 + tb) * rowb, bytes,
+                     &sm.bar[b]);
+            bulk_g2s(sm.u.tl.v[b], reinterpret_cast<const uint8_t *>(a.v_cache) + (head_row0 + tb) * rowb, bytes,
+                     &sm.bar[b]);
+        }
+    };
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.bar[0], 1u);
+        mbar_init(&sm.bar[1], 1u);
+        fence_mbar_init();
+        if (t0 < t1) issue(t0, 0u);
+        if (t0 + kAttnTile < t1) issue(t0 + kAttnTile, 1u);
+    }
+    __syncthreads();
+    pdl_wait();
+    attn_stage_qkv(a, sm, kvh, group, pos, has_pos, f16, head_row0);
+    constexpr uint32_t kL = GP == 8 ? 3u : GP == 4 ? 2u : GP == 2 ? 1u : 0u;
+    const uint32_t hm = lane >> (5u - kL);                       // this lane's head after head_sums
+    constexpr uint32_t kHs = 32u >> kL;                          // lanes per head
+    const uint32_t hl = lane & (kHs - 1u);                       // its place among them: float4s hl + kHs i
+    float4 qr[GP];
+#pragma unroll
+    for (int i = 0; i < GP; ++i) {
+        const uint32_t hh = (uint32_t)i ^ hm;
+        qr[i] = hh < group ? sm.q[hh][lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float m = -FLT_MAX, l = 0.f;
+    float4 acc[GP];
+#pragma unroll
+    for (int i = 0; i < GP; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t it = 0;
+    for (uint32_t tb = t0; tb < t1; tb += kAttnTile, ++it) {
+        const uint32_t te = min(tb + kAttnTile, t1), b = it & 1u;
+        const uint8_t *kt = sm.u.tl.k[b], *vt = sm.u.tl.v[b];
+        mbar_wait(&sm.bar[b], (it >> 1) & 1u, err);
+        const uint32_t p0 = tb + kAttnPer * warp;   // this warp's positions p0 .. p0 + kAttnPer - 1
+        float sc[kAttnPer];
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnPer; ++j) {
+            const uint32_t p = p0 + j;
+            sc[j] = -FLT_MAX;
+            if (p < te) {
+                const float4 kv = p == pos ? sm.knew[lane] : kv_row4(kt + (size_t)(p - tb) * rowb, lane, f16);
+                float d[GP];
+#pragma unroll
+                for (int i = 0; i < GP; ++i)
+                    d[i] = fmaf(qr[i].x, kv.x, qr[i].y * kv.y) + fmaf(qr[i].z, kv.z, qr[i].w * kv.w);
+                sc[j] = head_sums<GP>(d) * scale;
+            }
+        }
+        float mc = sc[0];
+#pragma unroll
+        for (uint32_t j = 1; j < kAttnPer; ++j) mc = fmaxf(mc, sc[j]);
+        const float mn = fmaxf(m, mc);
+        const float corr = expf(m - mn);
+        float w[kAttnPer], ws = 0.f;
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnPer; ++j) {
+            w[j] = p0 + j < te ? expf(sc[j] - mn) : 0.f;
+            ws += w[j];
+        }
+        l = l * corr + ws;
+#pragma unroll
+        for (int i = 0; i < GP; ++i) {
+            acc[i].x *= corr;
+            acc[i].y *= corr;
+            acc[i].z *= corr;
+            acc[i].w *= corr;
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnPer; ++j) {
+            const uint32_t p = p0 + j;
+            if (p < te) {
+                const uint8_t *vr = vt + (size_t)(p - tb) * rowb;
+#pragma unroll
+                for (int i = 0; i < GP; ++i) {
+                    const uint32_t d4 = hl + kHs * (uint32_t)i;   // the head's lanes read adjacent float4s
+                    const float4 vv = p == pos ? sm.vnew[d4] : kv_row4(vr, d4, f16);
+                    acc[i].x = fmaf(w[j], vv.x, acc[i].x);
+                    acc[i].y = fmaf(w[j], vv.y, acc[i].y);
+                    acc[i].z = fmaf(w[j], vv.z, acc[i].z);
+                    acc[i].w = fmaf(w[j], vv.w, acc[i].w);
+                }
+            }
+        }
+        m = mn;
+        __syncthreads();   // tile consumed: its buffer takes the tile after next
+        if (threadIdx.x == 0 && tb + 2u * kAttnTile < t1) issue(tb + 2u * kAttnTile, b);
+    }
+    // every copy was consumed: the tile buffers hold the warps' states now
+    if (hm < group) {
+        float *dst = sm.u.wrec[warp][hm];
+#pragma unroll
+        for (int i = 0; i < GP; ++i) reinterpret_cast<float4 *>(dst)[hl + kHs * (uint32_t)i] = acc[i];
+        if (hl == 0u) {
+            dst[128] = m;
+            dst[129] = l;
+        }
+    }
+    attn_merge(a, sm, kvh, group, cl, ncl);
+}
+
+// ------------------------------------------- attention, fp16 cache, MMA ----
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void ldmatrix_x4_t(const void *p, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_addr(p)));
+}
+
+// d += A (16 x 16) B (16 x 8), binary16 in, fp32 accumulate
+__device__ __forceinline__ void mma_k16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d += A (16 x 8) B (8 x 8)
+__device__ __forceinline__ void mma_k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0)
+{
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// (x, y) -> binary16 pair hi and the rounded remainder lo (x = hi + lo to ~22 bits)
+__device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo)
+{
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// Decode attention over an fp16 KV cache on tensor cores: the same splits,
+// clusters, staging of q / k / v and merges as attn_kernel, with the tile
+// loop as two MMAs. The cached K and V rows are binary16 already (exact MMA
+// operands); q and the softmax weights P are split into binary16 pairs
+// hi + lo, stacked as MMA rows 0-7 (hi) and 8-15 (lo) of one A operand, so
+// each product term is one MMA and row h plus row h + 8 is the head's sum:
+//   S = [q_hi; q_lo] K^T   m16n8k16, K by ldmatrix (8 positions per warp)
+//   O += [P_hi; P_lo] V    m16n8k8,  V by ldmatrix.trans (16 tiles of 8 dims)
+// Tiles of 64 positions arrive by per-thread 16-byte cp.async into rows of
+// 272 bytes (the 8 rows an ldmatrix reads fall in distinct banks), two tiles
+// in flight, the first two issued before the predecessor wait. Warp w takes
+// positions 8w .. 8w + 7 of a tile; lane (g, t) holds head g's scores of
+// positions 2t, 2t + 1 and its outputs of dimensions 8j + 2t, 8j + 2t + 1.
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid_constant__ AttnArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem_a[];
+    AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
+    pdl_launch();
+    const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
+    if (pos >= a.max_context) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&a.st->status, kStatusOk, kStatusBadArgument);
+        return;
+    }
+    const uint32_t n = pos + 1u;
+    const uint32_t ms = a.min_span ? a.min_span : kAttnMinSpan;
+    const uint32_t ns = min(a.splits, ((n + ms - 1u) / ms + kAttnCluster - 1u) / kAttnCluster * kAttnCluster);
+    const uint32_t span = (n + ns - 1u) / ns;
+    const uint32_t kvh = blockIdx.x / a.splits, s = blockIdx.x % a.splits;
+    if (s >= ns) return;   // the whole cluster leaves
+    const uint32_t ncl = ns / kAttnCluster, cl = s / kAttnCluster;
+    const uint32_t group = a.q_heads / a.kv_heads;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, g = lane >> 2, t = lane & 3u;
+    const uint32_t t0 = min(s * span, n), t1 = min(n, t0 + span);
+    const bool has_pos = t0 <= pos && pos < t1;
+    const float scale = 1.0f / sqrtf(128.0f);
+    const size_t head_row0 = (size_t)kvh * a.max_context;
+    const uint8_t *kc = reinterpret_cast<const uint8_t *>(a.k_cache) + head_row0 * 256u;
+    const uint8_t *vc = reinterpret_cast<const uint8_t *>(a.v_cache) + head_row0 * 256u;
+    // cached rows [tb, min(te, pos)) of tile tb into buffer b, one group per
+    // call (an empty one past the split's end)
+    auto issue = [&](uint32_t tb, uint32_t b) {
+        if (tb < t1) {
+            const uint32_t te = min(tb + kTcTile, t1), ce = max(tb, min(te, pos));
+            const uint32_t chunks = (ce - tb) * 16u;   // 16-byte pieces of 256-byte rows
+            for (uint32_t i = threadIdx.x; i < chunks; i += kAttnThreads) {
+                const uint32_t r = i >> 4, c = i & 15u;
+                cp_async16(&sm.u.tc.k[b][r][8u * c], kc + (size_t)(tb + r) * 256u + 16u * c);
+                cp_async16(&sm.u.tc.v[b][r][8u * c], vc + (size_t)(tb + r) * 256u + 16u * c);
+            }
+        }
+        cp_async_commit();
+    };
+    issue(t0, 0u);
+    issue(t0 + kTcTile, 1u);
+    pdl_wait();
+    attn_stage_qkv(a, sm, kvh, group, pos, has_pos, true, head_row0);
+    // A operands of q: rows g (hi) and g + 8 (lo) of head g, 8 steps of 16 dimensions
+    uint32_t qa[8][4];
+    {
+        const float *qg = reinterpret_cast<const float *>(sm.q[g < group ? g : 0u]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (g < group) {
+                split_h2(qg[16 * k + 2 * (int)t], qg[16 * k + 2 * (int)t + 1], qa[k][0], qa[k][1]);
+                split_h2(qg[16 * k + 2 * (int)t + 8], qg[16 * k + 2 * (int)t + 9], qa[k][2], qa[k][3]);
+            } else {
+                qa[k][0] = qa[k][1] = qa[k][2] = qa[k][3] = 0u;
+            }
+        }
+    }
+    float m = -FLT_MAX, l = 0.f;
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    const float *knew = reinterpret_cast<const float *>(sm.knew), *vnew = reinterpret_cast<const float *>(sm.vnew);
+    uint32_t it = 0;
+    for (uint32_t tb = t0; tb < t1; tb += kTcTile, ++it) {
+        const uint32_t te = min(tb + kTcTile, t1), b = it & 1u;
+        const uint32_t nrow = max(tb, min(te, pos)) - tb;   // rows the copies filled
+        cp_async_wait1();   // this tile's group; the next tile's may still be in flight
+        __syncthreads();
+        // the other rows: the current position (the new k and v, rounded as the
+        // cache keeps them) and zeros past the split's end (a weight of 0 times
+        // stale shared memory could be NaN)
+        for (uint32_t i = threadIdx.x; i < (kTcTile - nrow) * 128u; i += kAttnThreads) {
+            const uint32_t r = nrow + (i >> 7), d = i & 127u;
+            const bool cur = has_pos && tb + r == pos;   // only the owning split has the new k, v
+            sm.u.tc.k[b][r][d] = __float2half_rn(cur ? knew[d] : 0.f);
+            sm.u.tc.v[b][r][d] = __float2half_rn(cur ? vnew[d] : 0.f);
+        }
+        __syncthreads();
+        const uint32_t pw = tb + 8u * warp;   // this warp's positions pw .. pw + 7
+        if (pw < te) {
+            const __half *krow = &sm.u.tc.k[b][8u * warp + (lane & 7u)][0];
+            const __half *vrow = &sm.u.tc.v[b][8u * warp + (lane & 7u)][0];
+            float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                // matrices: dims 16k + 8 (lane >> 3) .. + 7 of the warp's 8 rows
+                uint32_t b4[4];
+                ldmatrix_x4(krow + 16u * (uint32_t)k + 8u * (lane >> 3), b4[0], b4[1], b4[2], b4[3]);
+                mma_k16(sacc, qa[k], b4[0], b4[1]);
+                mma_k16(sacc, qa[k + 1], b4[2], b4[3]);
+            }
+            const uint32_t p0 = pw + 2u * t;
+            const float s0 = p0 < te ? (sacc[0] + sacc[2]) * scale : -FLT_MAX;
+            const float s1 = p0 + 1u < te ? (sacc[1] + sacc[3]) * scale : -FLT_MAX;
+            float mx = fmaxf(s0, s1);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(m, mx);
+            const float corr = expf(m - mn);
+            const float w0 = p0 < te ? expf(s0 - mn) : 0.f;
+            const float w1 = p0 + 1u < te ? expf(s1 - mn) : 0.f;
+            float ws = w0 + w1;
+            ws += __shfl_xor_sync(0xffffffffu, ws, 1);
+            ws += __shfl_xor_sync(0xffffffffu, ws, 2);
+            l = l * corr + ws;
+            m = mn;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                o[j][0] *= corr;
+                o[j][1] *= corr;
+                o[j][2] *= corr;
+                o[j][3] *= corr;
+            }
+            uint32_t ph, pl;
+            split_h2(w0, w1, ph, pl);
+#pragma unroll
+            for (int jd = 0; jd < 16; jd += 4) {
+                // matrices: dims 8 (jd + (lane >> 3)) .. + 7 of the warp's 8 rows, transposed
+                uint32_t v4[4];
+                ldmatrix_x4_t(vrow + 8u * ((uint32_t)jd + (lane >> 3)), v4[0], v4[1], v4[2], v4[3]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) mma_k8(o[jd + e], ph, pl, v4[e]);
+            }
+        }
+        __syncthreads();   // tile consumed: its buffer takes the tile after next
+        issue(tb + 2u * kTcTile, b);
+    }
+    cp_async_wait0();
+    if (g < group) {
+        float *dst = sm.u.wrec[warp][g];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            *reinterpret_cast<float2 *>(dst + 8 * j + 2 * (int)t) = make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
+        if (t == 0u) {
+            dst[128] = m;
+            dst[129] = l;
+        }
+    }
+    attn_merge(a, sm, kvh, group, cl, ncl);
 }
 
 // --------------------------------------------------------- embed, argmax --
@@ -1243,9 +1470,11 @@ cudaError_t launch_ex(const void *fn, void **args, dim3 grid, dim3 block, size_t
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-// attention instance for `group` query heads per KV head (rounded up to a power of two)
-const void *attn_fn(uint32_t group)
+// attention instance for `group` query heads per KV head (rounded up to a
+// power of two); tc: the tensor-core kernel of fp16 caches
+const void *attn_fn(uint32_t group, bool tc = false)
 {
+    if (tc) return (const void *)attn_tc16_kernel;
     if (group <= 1u) return (const void *)attn_kernel<1>;
     if (group <= 2u) return (const void *)attn_kernel<2>;
     if (group <= 4u) return (const void *)attn_kernel<4>;
@@ -1262,7 +1491,7 @@ extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_
 
 // Clusters of the attention launch (kAttnCluster CTAs each) that fit on the
 // device at once, for `group` query heads per KV head; 0 on error.
-extern "C" int atlas_d2_attn_max_clusters(uint32_t group)
+extern "C" int atlas_d2_attn_max_clusters(uint32_t group, uint32_t tc)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kAttnCluster * 64u);
@@ -1276,9 +1505,9 @@ extern "C" int atlas_d2_attn_max_clusters(uint32_t group)
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaFuncSetAttribute(attn_fn(group), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem)) !=
-            cudaSuccess ||
-        cudaOccupancyMaxActiveClusters(&n, attn_fn(group), &cfg) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_fn(group, tc != 0u), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(AttnSmem)) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, attn_fn(group, tc != 0u), &cfg) != cudaSuccess)
         return 0;
     return n;
 }
@@ -1298,7 +1527,7 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
         if ((e = cudaFuncSetAttribute(attn_fn(g), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem)) !=
             cudaSuccess)
             return e;
-    return cudaSuccess;
+    return cudaFuncSetAttribute(attn_fn(1, true), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem);
 }
 
 extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaStream_t stream)
@@ -1316,8 +1545,9 @@ extern "C" cudaError_t atlas_d2_launch_attn(const AttnArgs *a, uint32_t grid, cu
     if (group == 0u || group > kAttnMaxGroup || a->splits % kAttnCluster != 0u || a->splits / kAttnCluster > 32u ||
         grid != a->kv_heads * a->splits)
         return cudaErrorInvalidValue;
-    return launch_ex(attn_fn(group), args, dim3(grid), dim3(kAttnThreads), atlas_d2_attn_smem(a->splits), stream, true,
-                     kAttnCluster);
+    if (a->tc && !a->kv_fp16) return cudaErrorInvalidValue;
+    return launch_ex(attn_fn(group, a->tc != 0u), args, dim3(grid), dim3(kAttnThreads), atlas_d2_attn_smem(a->splits),
+                     stream, true, kAttnCluster);
 }
 
 extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,

@@ -168,6 +168,7 @@ struct AttnArgs {
     uint32_t min_span;          // cached positions per split, at least (0: kAttnMinSpan)
     const float *q_norm, *k_norm;   // qwen3: per-head RMSNorm weights [128] of q and k, or null
     float eps;
+    uint32_t tc;                // fp16 cache: tensor-core kernel (attn_tc16_kernel)
 };
 
 }  // namespace d2

@@ -40,7 +40,7 @@ extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t 
 extern "C" cudaError_t atlas_launch_prefill_attn_tc(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots);
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits);
-extern "C" int atlas_d2_attn_max_clusters(uint32_t group);
+extern "C" int atlas_d2_attn_max_clusters(uint32_t group, uint32_t tc);
 extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
 extern "C" cudaError_t atlas_d2_launch_mv(const atlas::d2::MvArgs *a, uint32_t grid, cudaStream_t stream);
 extern "C" cudaError_t atlas_d2_launch_attn(const atlas::d2::AttnArgs *a, uint32_t grid, cudaStream_t stream);
@@ -127,6 +127,7 @@ struct AtlasCuda {
         float *apart = nullptr;
         uint32_t *actr = nullptr, *status = nullptr;
         uint32_t splits = 0, kernels = 0;
+        bool attn_tc = false;   // fp16 cache: the tensor-core decode attention
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
     } g2;
@@ -722,7 +723,10 @@ int build_graph2(AtlasCuda *h)
     // wave waits for the last free SMs of a GPC as the preceding kernel drains)
     const uint32_t C = d2::kAttnCluster;
     g.splits = std::max(C, std::min(2u * G / sl.kv_heads, 160u) / C * C);
-    const int max_cl = atlas_d2_attn_max_clusters(group);
+    // fp16 cache: the tensor-core kernel unless ATLAS_ATTN_TC=0
+    const char *tce = getenv("ATLAS_ATTN_TC");
+    g.attn_tc = d.kv_fp16 && !(tce && atoi(tce) == 0);
+    const int max_cl = atlas_d2_attn_max_clusters(group, g.attn_tc ? 1u : 0u);
     if (max_cl > 0) g.splits = std::max(C, std::min(g.splits, (uint32_t)max_cl * 3u / 4u / sl.kv_heads * C));
     if (const char *e = getenv("ATLAS_ATTN_SPLITS")) g.splits = std::max(C, std::min(160u, (uint32_t)atoi(e)) / C * C);
     if ((rc = dalloc(h, &g.apart, (size_t)sl.kv_heads * (g.splits / C) * group * d2::kRec * sizeof(float)))) return rc;
@@ -814,6 +818,7 @@ int build_graph2(AtlasCuda *h)
     at.kv_heads = sl.kv_heads;
     at.max_context = d.max_context;
     at.splits = g.splits;
+    at.tc = g.attn_tc ? 1u : 0u;
     at.kv_fp16 = d.kv_fp16 ? 1u : 0u;
     at.eps = d.rms_eps;
     if (const char *e = getenv("ATLAS_ATTN_MIN_SPAN")) at.min_span = (uint32_t)std::max(1, atoi(e));

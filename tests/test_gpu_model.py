@@ -203,3 +203,28 @@ def test_qwen3_qk_norm_matches_oracle(torch_cuda, oracle, tiny_qwen3_model):
         assert am == want_picks[0]
         picks = rt.generate(am, len(prompt), 31)
         np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("min_span", ["96", "8"])
+def test_fp16_cache_tensor_core_attention_matches_cuda_cores(torch_cuda, small_model, monkeypatch, min_span):
+    """fp16 KV cache: the tensor-core decode attention (binary16 pairs of q and
+    of the softmax weights against the cache's binary16 K and V) against the
+    CUDA-core kernel over the same cache, 600 cached positions, with one
+    cluster of splits and with 10 clusters (their records merged in global
+    memory): logits of a decode step within 1e-4 of the largest, and 16 greedy
+    picks identical."""
+    monkeypatch.setenv("ATLAS_ATTN_MIN_SPAN", min_span)
+    prompt = np.random.default_rng(17).integers(0, 4096, 600).astype(np.uint32)
+    runs = []
+    for tc in ("1", "0"):
+        monkeypatch.setenv("ATLAS_ATTN_TC", tc)
+        with atlas_cuda.Runtime(small_model, max_context=700, max_prefill=128, kv_fp16=True) as rt:
+            _, am = rt.prefill(prompt)
+            lg, am1 = rt.forward(am, len(prompt))
+            picks = rt.generate(am1, len(prompt) + 1, 16)
+        runs.append((lg, am, am1, picks))
+    (lg_tc, am_tc, am1_tc, picks_tc), (lg_cc, am_cc, am1_cc, picks_cc) = runs
+    _close(lg_tc, lg_cc.astype(np.float64), 1e-4)
+    assert (am_tc, am1_tc) == (am_cc, am1_cc)
+    np.testing.assert_array_equal(picks_tc, picks_cc)
