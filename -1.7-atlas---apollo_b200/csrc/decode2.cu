@@ -7,12 +7,13 @@
 // Every kernel first lets its successor launch (griddepcontrol.launch_dependents)
 // and only then waits for its predecessor (griddepcontrol.wait). A successor
 // CTA becomes resident on an SM as soon as resources there allow - for two
-// mv kernels, when the predecessor's CTA on that SM exits (at 112 registers
+// mv kernels, when the predecessor's CTA on that SM exits (at 128 registers
 // per thread the register banks hold one 9-warp mv CTA per SM) - and its
 // producer warp starts streaming weights at once: weights never depend on
 // the activations, so HBM keeps streaming while other SMs finish the
 // predecessor. (A 96-register build that fits two mv CTAs per SM ran the 3B
-// step 16 % slower: co-resident CTAs compete for issue slots.)
+// step 16 % slower: co-resident CTAs compete for issue slots; caps of 128
+// and 168 registers ran it 1.3 % and 1.0 % faster than 112.)
 //
 // mv kernel (dequant-GEMV, one CTA per SM): a producer warp copies the raw
 // Q4_K / Q6_K rows of the CTA's task range into a shared-memory ring with
@@ -635,7 +636,7 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
     return true;
 }
 
-__global__ void __maxnreg__(112) mv_kernel(const __grid_constant__ MvArgs a)
+__global__ void __maxnreg__(128) mv_kernel(const __grid_constant__ MvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     MvHdr *h = reinterpret_cast<MvHdr *>(smem);
