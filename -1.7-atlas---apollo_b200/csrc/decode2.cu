@@ -1260,13 +1260,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid
         // the other rows: the current position (the new k and v, rounded as the
         // cache keeps them) and zeros past the split's end (a weight of 0 times
         // stale shared memory could be NaN)
-        for (uint32_t i = threadIdx.x; i < (kTcTile - nrow) * 128u; i += kAttnThreads) {
-            const uint32_t r = nrow + (i >> 7), d = i & 127u;
-            const bool cur = has_pos && tb + r == pos;   // only the owning split has the new k, v
-            sm.u.tc.k[b][r][d] = __float2half_rn(cur ? knew[d] : 0.f);
-            sm.u.tc.v[b][r][d] = __float2half_rn(cur ? vnew[d] : 0.f);
+        if (nrow < kTcTile) {   // CTA-uniform: full tiles of cached rows skip the fill and its barrier
+            for (uint32_t i = threadIdx.x; i < (kTcTile - nrow) * 128u; i += kAttnThreads) {
+                const uint32_t r = nrow + (i >> 7), d = i & 127u;
+                const bool cur = has_pos && tb + r == pos;   // only the owning split has the new k, v
+                sm.u.tc.k[b][r][d] = __float2half_rn(cur ? knew[d] : 0.f);
+                sm.u.tc.v[b][r][d] = __float2half_rn(cur ? vnew[d] : 0.f);
+            }
+            __syncthreads();
         }
-        __syncthreads();
         const uint32_t pw = tb + 8u * warp;   // this warp's positions pw .. pw + 7
         if (pw < te) {
             const __half *krow = &sm.u.tc.k[b][8u * warp + (lane & 7u)][0];
