@@ -915,39 +915,40 @@ __global__ void __launch_bounds__(256) split_kernel(const float *x, uint32_t ldx
     const float *xr = x + (size_t)t * ldx;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const bool vec = ((reinterpret_cast<uintptr_t>(xr) & 15u) == 0);
+    // pass 1: the row into shared memory, with the sum of squares (RMSNorm)
+    // or, without a norm, the largest magnitude
     double ss = 0.0;
+    float amax = 0.f;
+    const bool norm = norm_w != nullptr;
     if (vec) {
         for (uint32_t i = threadIdx.x; i < cols / 4; i += blockDim.x) {
             const float4 v = __ldcg(reinterpret_cast<const float4 *>(xr) + i);
             reinterpret_cast<float4 *>(rowbuf)[i] = v;
-            ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+            if (norm) ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+            else amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
     } else {
         for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
             const float v = __ldcg(xr + i);
             rowbuf[i] = v;
-            ss += (double)v * v;
+            if (norm) ss += (double)v * v;
+            else amax = fmaxf(amax, fabsf(v));
         }
     }
-    float inv = 1.f;
-    if (norm_w) {
+    if (norm) {
+        // pass 2: normalise in place, then the largest magnitude
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) dred[warp] = ss;
         __syncthreads();
         double tot = 0.0;
         for (int i = 0; i < 8; ++i) tot += dred[i];
-        inv = 1.0f / sqrtf((float)(tot / (double)cols) + eps);
-    }
-    __syncthreads();
-    float amax = 0.f;
-    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
-        float v = rowbuf[i];
-        if (norm_w) {
-            v = __fmul_rn(__fmul_rn(v, inv), __ldg(norm_w + i));
+        const float inv = 1.0f / sqrtf((float)(tot / (double)cols) + eps);
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+            const float v = __fmul_rn(__fmul_rn(rowbuf[i], inv), __ldg(norm_w + i));
             rowbuf[i] = v;
+            amax = fmaxf(amax, fabsf(v));
         }
-        amax = fmaxf(amax, fabsf(v));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
