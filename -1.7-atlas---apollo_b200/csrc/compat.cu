@@ -121,7 +121,10 @@ int brain_gpu_matvec_batch(const BrainGpuMatvec *ops, size_t count)
     for (size_t i = 0; i < count; ++i) {
         const BrainGpuMatvec &op = ops[i];
         const uint32_t be = atlas::block_elems(op.type), bb = atlas::block_bytes(op.type);
+        // rows, cols and offset above 2^32 are rejected first (as src/gpu_matvec.c:220-223
+        // does), so the byte count below cannot overflow 64 bits
         if (!op.input || !op.output || !op.rows || !op.cols || !be || op.type == 1u || op.cols % be ||
+            op.rows > 0xffffffffull || op.cols > 0xffffffffull || op.offset > 0xffffffffull ||
             op.offset > g_compat.size || op.rows * (op.cols / be) * bb > g_compat.size - op.offset) {
             report("arguments", "invalid operation", count);
             return 0;

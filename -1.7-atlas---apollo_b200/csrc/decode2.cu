@@ -223,14 +223,17 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
 // q4_order: the CTA's tasks are Q4_K - each 4-element group is stored as
 // (x0, x2, x1, x3), the order in which q4k_task pairs the nibbles of a quant
 // word (bytes 0 and 2, bytes 1 and 3) without byte permutes.
-__device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea, bool q4_order)
+// W: the staging warps (threads 0 .. 32 W - 1, synchronised on named barrier 1);
+// dred / fred: W slots each for the block reductions.
+template <int W>
+__device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t *xarea, bool q4_order)
 {
     const uint32_t n4 = a.cols / 4u;
     const bool norm = a.norm_w != nullptr;
     float4 *xf = reinterpret_cast<float4 *>(xarea);
     float mx = 0.f;
     double ss = 0.0;
-    constexpr uint32_t kStride = kMvWarps * 32;
+    constexpr uint32_t kStride = W * 32;
     constexpr int kDepth = 8;
     // the norm weights of the first round do not depend on the preceding
     // kernel: load them before waiting for it
@@ -254,7 +257,7 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea, bool q4_o
             wait_counter_sys(reinterpret_cast<const uint32_t *>(a.peer[a.rank] + a.in_cnt), k * a.in_arrivals,
                              a.status);
         }
-        mv_sync();
+        asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
         red = reinterpret_cast<const float4 *>(a.peer[a.rank] + a.in_red);
         own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
         own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
@@ -319,12 +322,12 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea, bool q4_o
         if (norm) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    if (lane == 0) { h->fred[warp] = mx; h->dred[warp] = ss; }
-    mv_sync();
+    if (lane == 0) { fred[warp] = mx; dred[warp] = ss; }
+    asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
     float m = 0.f;
     double t = 0.0;
 #pragma unroll
-    for (int w = 0; w < kMvWarps; ++w) { m = fmaxf(m, h->fred[w]); t += h->dred[w]; }
+    for (int w = 0; w < W; ++w) { m = fmaxf(m, fred[w]); t += dred[w]; }
     // exponent capped at 126: rows of tiny values (a SwiGLU output of
     // all-negative gates) keep a finite scale and contribute ~0, as in fp32
     const float s = (m > 0.f && isfinite(m)) ? exp2f((float)min(13 - ilogbf(m), 126)) : 1.0f;
@@ -354,7 +357,7 @@ __device__ float mv_stage_x(const MvArgs &a, MvHdr *h, uint8_t *xarea, bool q4_o
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         if ((lane & 3u) == 0u) xs16[i / 4u] = sum;
     }
-    mv_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
     return inv_rms / s;
 }
 
@@ -557,7 +560,7 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const int g = (int)(lane >> 2), t4 = (int)(lane & 3u);
     // waits for the preceding kernel; a CTA's tasks are all of its segment's type
-    const float out_scale = mv_stage_x(a, h, xarea, a.seg[c.seg].type == 12u);
+    const float out_scale = mv_stage_x<kMvWarps>(a, h->dred, h->fred, xarea, a.seg[c.seg].type == 12u);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
     const uint32_t per = a.st > (uint32_t)kMvWarps ? a.st / kMvWarps : 1u;    // tasks per slot visit
     const uint32_t step = a.st > (uint32_t)kMvWarps ? 1u : kMvWarps / a.st, u = warp % a.st;
@@ -697,6 +700,273 @@ __global__ void __maxnreg__(128) mv_kernel(const __grid_constant__ MvArgs a)
             if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
         if (a.tp > 1u) {
             // (max, global row) into this rank's slot at every rank
+            for (uint32_t p = 0; p < a.tp; ++p) {
+                reinterpret_cast<float *>(a.peer[p] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
+                reinterpret_cast<uint32_t *>(a.peer[p] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
+                                                                                            blockIdx.x] =
+                    a.row_base + best.i;
+            }
+            __threadfence_system();
+            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        } else {
+            a.pmax[blockIdx.x] = best.v;
+            a.pidx[blockIdx.x] = best.i;
+        }
+    }
+}
+
+// ------------------------------------------------------------ mv4 kernel ----
+//
+// Every warp owns the tasks [start(w), start(w + 1)) of the CTA's range,
+// start(w) = j0 + floor(w L / W): consecutive blocks of the same row tile, so
+// a warp sums a tile's blocks in registers and finishes it alone unless its
+// range ends inside the tile. A tile shared by warps wa..wb is finished by the
+// last of them to arrive, which adds the warps' partial rows in warp order
+// (a fixed order, so the result does not depend on timing).
+//
+// Copies: each warp keeps nslot - 1 tasks in flight in its own ring; the
+// first nslot - 1 are issued before the wait for the preceding kernel (the
+// weights never depend on it), so they stream while x is staged.
+
+struct __align__(16) M4Hdr {
+    double dred[kM4Warps];
+    float fred[kM4Warps];
+    float amax[kM4Warps];
+    uint32_t aidx[kM4Warps];
+    uint32_t cnt[kM4Warps];     // arrivals at a shared tile, indexed by its first warp
+};
+// partial rows of shared tiles: [warp][first / last tile][segment][16]
+constexpr uint32_t kM4PartBytes = kM4Warps * 2u * 2u * 16u * 4u;
+
+__host__ __device__ constexpr uint32_t m4_hdr_bytes() { return align128((uint32_t)sizeof(M4Hdr)); }
+__host__ __device__ constexpr uint32_t m4_slot_bytes(uint32_t type) { return 16u * (type == 12u ? kM4Q4Row : kM4Q6Row); }
+__host__ __device__ constexpr uint32_t m4_smem_bytes(uint32_t cols, uint32_t nslot, uint32_t slot_bytes)
+{
+    return m4_hdr_bytes() + kM4PartBytes + mv_x_bytes(cols) + (uint32_t)kM4Warps * nslot * slot_bytes;
+}
+
+__device__ __forceinline__ void m4_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kM4Threads) : "memory"); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint64_t policy)
+{
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void m4_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Task j of the launch: row tile t, segment s, block column b.
+struct M4Task {
+    uint32_t t, s, b;
+};
+__device__ __forceinline__ M4Task m4_task(const MvArgs &a, uint32_t seg, uint32_t j)
+{
+    if (!a.paired) return M4Task{j / a.nb, seg, j % a.nb};
+    const uint32_t tp = 2u * a.nb, r = j % tp;
+    return M4Task{j / tp, r / a.nb, r % a.nb};
+}
+
+// First task of warp w (w = Weff gives the range's end).
+__device__ __forceinline__ uint32_t m4_start(uint32_t j0, uint32_t L, uint32_t weff, uint32_t w)
+{
+    return j0 + (uint32_t)((uint64_t)w * L / weff);
+}
+// The warp whose range holds task j.
+__device__ __forceinline__ uint32_t m4_warp_of(uint32_t j0, uint32_t L, uint32_t weff, uint32_t j)
+{
+    return (uint32_t)(((uint64_t)(j - j0 + 1u) * weff + L - 1u) / L) - 1u;
+}
+
+// Issue the copies of one task (16 rows x one block) into a slot.
+__device__ __forceinline__ void m4_issue(const MvArgs &a, uint32_t seg, uint32_t j, uint32_t slot, uint32_t lane,
+                                         uint64_t policy)
+{
+    const M4Task k = m4_task(a, seg, j);
+    const MvSeg &sg = a.seg[k.s];
+    if (sg.type == 12u) {
+        const uint8_t *base = sg.w + (uint64_t)(16u * k.t) * sg.row_bytes + (uint64_t)k.b * 144u;
+#pragma unroll
+        for (uint32_t i = 0; i < 5u; ++i) {
+            const uint32_t idx = lane + 32u * i;   // 16 rows x 9 chunks of 16 bytes
+            if (idx < 144u) {
+                const uint32_t r = idx / 9u, p = idx - 9u * r;
+                cp_async16(slot + r * kM4Q4Row + 16u * p, base + (uint64_t)r * sg.row_bytes + 16u * p, policy);
+            }
+        }
+    } else {
+        const uint8_t *base = sg.w + (uint64_t)(16u * k.t) * sg.row_bytes + (uint64_t)k.b * 210u;
+        const uint32_t p = lane & 15u;
+#pragma unroll
+        for (uint32_t i = 0; i < 8u; ++i) {
+            const uint32_t r = 2u * i + (lane >> 4);
+            const uint8_t *row = base + (uint64_t)r * sg.row_bytes;
+            const uint8_t *win = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(row) & ~uintptr_t(15));
+            cp_async16(slot + r * kM4Q6Row + 16u * p, win + 16u * p, policy);
+        }
+    }
+}
+
+// Rows lane / 4 and lane / 4 + 8 of a finished tile's partial sums (this
+// lane's share) -> lane i < 16 holds row i, summed over the 4 lanes of a row.
+__device__ __forceinline__ float m4_rows(float v0, float v1, uint32_t lane)
+{
+    v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+    v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+    const uint32_t src = 4u * (lane & 7u);
+    const float a0 = __shfl_sync(0xffffffffu, v0, src), a1 = __shfl_sync(0xffffffffu, v1, src);
+    return (lane & 8u) ? a1 : a0;
+}
+
+// Finish tile t after this warp's last task in it: alone (registers), or as
+// one of the warps wa..wb sharing it (partials in shared memory, the last to
+// arrive adds them in warp order).
+__device__ __forceinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, const MvCta &c, uint32_t L,
+                                         uint32_t weff, uint32_t my0, uint32_t t, const float (&acc)[2][2],
+                                         float out_scale, MvBest &best)
+{
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t P = a.paired ? 2u : 1u, TP = a.nb * P;
+    const uint32_t tj0 = t * TP;
+    const uint32_t wa = m4_warp_of(c.j0, L, weff, tj0), wb = m4_warp_of(c.j0, L, weff, tj0 + TP - 1u);
+    float r[2];
+    r[0] = m4_rows(acc[0][0], acc[0][1], lane);
+    r[1] = P == 2u ? m4_rows(acc[1][0], acc[1][1], lane) : 0.f;
+    if (wa != wb) {
+        // slot 0: the tile where this warp's range starts; slot 1: where it ends
+        const uint32_t which = my0 >= tj0 ? 0u : 1u;
+        float *pp = part + (warp * 2u + which) * 32u;
+        if (lane < 16u) {
+            pp[lane] = r[0];
+            pp[16u + lane] = r[1];
+        }
+        __syncwarp();
+        uint32_t last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = (atomicAdd(&h->cnt[wa], 1u) + 1u == wb - wa + 1u) ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        __threadfence_block();
+        r[0] = r[1] = 0.f;
+        const uint32_t i = lane & 15u;
+        for (uint32_t w = wa; w <= wb; ++w) {
+            const uint32_t ww = (w > wa || m4_start(c.j0, L, weff, wa) >= tj0) ? 0u : 1u;
+            const volatile float *q = part + (w * 2u + ww) * 32u;
+            r[0] += q[i];
+            r[1] += q[16u + i];
+        }
+    }
+    const float pre = mv_pre(a, c.seg, t, lane);
+    if (lane < 16u) mv_finish(a, c.seg, t, r[0] * out_scale, r[1] * out_scale, pre, lane, best);
+}
+
+template <int NS>
+__device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xarea, uint8_t *ring, const MvCta &c,
+                           MvBest &best)
+{
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t g = lane >> 2, t4 = lane & 3u;
+    const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)kM4Warps, L);
+    const bool active = warp < weff;
+    const uint32_t my0 = active ? m4_start(c.j0, L, weff, warp) : 0u;
+    const uint32_t my1 = active ? m4_start(c.j0, L, weff, warp + 1u) : 0u;
+    const uint32_t n = my1 - my0;
+    const uint64_t policy = policy_evict_first();
+    const uint32_t ring_w = smem_addr(ring) + warp * (uint32_t)NS * a.slot_bytes;
+    // prologue: the first NS - 1 tasks, before the wait for the preceding kernel
+#pragma unroll
+    for (uint32_t k = 0; k + 1u < (uint32_t)NS; ++k) {
+        if (k < n) m4_issue(a, c.seg, my0 + k, ring_w + k * a.slot_bytes, lane, policy);
+        m4_commit();
+    }
+    const float out_scale = mv_stage_x<kM4Warps>(a, h->dred, h->fred, xarea, a.seg[c.seg].type == 12u);
+    if (!active) return;
+    const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
+    const uint8_t *ringp = ring + (size_t)warp * NS * a.slot_bytes;
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    uint32_t cur = m4_task(a, c.seg, my0).t;
+    for (uint32_t k = 0; k < n; ++k) {
+        {
+            const uint32_t kn = k + (uint32_t)NS - 1u;
+            if (kn < n) m4_issue(a, c.seg, my0 + kn, ring_w + (kn % (uint32_t)NS) * a.slot_bytes, lane, policy);
+            m4_commit();
+        }
+        const M4Task tk = m4_task(a, c.seg, my0 + k);
+        if (tk.t != cur) {
+            m4_flush(a, h, part, c, L, weff, my0, cur, acc, out_scale, best);
+            acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+            cur = tk.t;
+        }
+        cp_async_wait<NS - 1>();
+        __syncwarp();
+        const uint8_t *slot = ringp + (size_t)(k % (uint32_t)NS) * a.slot_bytes;
+        const uint8_t *xb = xarea + (size_t)tk.b * 1024u;
+        const float *xs = xs16 + (size_t)tk.b * 16u;
+        const MvSeg &sg = a.seg[tk.s];
+        float o0 = 0.f, o1 = 0.f;
+        if (sg.type == 12u) {
+            q4k_task(slot, 0u, 0u, kM4Q4Row, xb, xs, lane, o0, o1);
+        } else {
+            const uintptr_t rb = reinterpret_cast<uintptr_t>(sg.w) + (uint64_t)(16u * tk.t) * sg.row_bytes +
+                                 (uint64_t)tk.b * 210u;
+            const uint8_t *r0[1] = {slot + g * kM4Q6Row + (uint32_t)((rb + (uint64_t)g * sg.row_bytes) & 15u)};
+            const uint8_t *r1[1] = {slot + (g + 8u) * kM4Q6Row +
+                                    (uint32_t)((rb + (uint64_t)(g + 8u) * sg.row_bytes) & 15u)};
+            const uint8_t *xbs[1] = {xb};
+            const float *xss[1] = {xs};
+            float p0[1] = {0.f}, p1[1] = {0.f};
+            q6k_tiles<1, true>(r0, r1, xbs, xss, (int)g, (int)t4, p0, p1);
+            o0 = p0[0];
+            o1 = p1[0];
+        }
+        __syncwarp();   // the slot is re-filled by a later iteration's copies
+        const uint32_t si = (a.paired && tk.s) ? 1u : 0u;
+        acc[si][0] += o0;
+        acc[si][1] += o1;
+    }
+    m4_flush(a, h, part, c, L, weff, my0, cur, acc, out_scale, best);
+}
+
+template <int NS>
+__global__ void __launch_bounds__(kM4Threads, 1) mv4_kernel(const __grid_constant__ MvArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    M4Hdr *h = reinterpret_cast<M4Hdr *>(smem);
+    float *part = reinterpret_cast<float *>(smem + m4_hdr_bytes());
+    uint8_t *xarea = smem + m4_hdr_bytes() + kM4PartBytes;
+    uint8_t *ring = xarea + mv_x_bytes(a.cols);
+    const MvCta c = a.cta[blockIdx.x];
+    if (threadIdx.x < (uint32_t)kM4Warps) h->cnt[threadIdx.x] = 0u;
+    __syncthreads();
+    pdl_launch();
+    MvBest best{-FLT_MAX, 0xffffffffu};
+    m4_consume<NS>(a, h, part, xarea, ring, c, best);
+    cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
+    if (a.epi == MV_PART) {
+        __threadfence_system();
+        m4_sync();
+        if (threadIdx.x == 0)
+            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        return;
+    }
+    if (a.epi != MV_LOGITS) return;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+        if (ov > best.v || (ov == best.v && oi < best.i)) { best.v = ov; best.i = oi; }
+    }
+    if (lane == 0) { h->amax[warp] = best.v; h->aidx[warp] = best.i; }
+    m4_sync();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kM4Warps; ++w)
+            if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
+        if (a.tp > 1u) {
             for (uint32_t p = 0; p < a.tp; ++p) {
                 reinterpret_cast<float *>(a.peer[p] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
                 reinterpret_cast<uint32_t *>(a.peer[p] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
@@ -1486,6 +1756,20 @@ const void *attn_fn(uint32_t group, bool tc = false)
 
 }  // namespace
 
+namespace {
+const void *mv4_fn(uint32_t nslot)
+{
+    switch (nslot) {
+    case 2: return (const void *)mv4_kernel<2>;
+    case 3: return (const void *)mv4_kernel<3>;
+    case 4: return (const void *)mv4_kernel<4>;
+    case 5: return (const void *)mv4_kernel<5>;
+    case 6: return (const void *)mv4_kernel<6>;
+    default: return nullptr;
+    }
+}
+}  // namespace
+
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots)
 {
     return (size_t)mv_hdr_bytes() + mv_tile_bytes(tslots) + mv_desc_bytes(nslot) + mv_x_bytes(cols) +
@@ -1526,6 +1810,10 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
 {
     cudaError_t e = cudaFuncSetAttribute(mv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
     if (e != cudaSuccess) return e;
+    for (uint32_t ns = 2; ns <= kM4MaxSlots; ++ns)
+        if ((e = cudaFuncSetAttribute(mv4_fn(ns), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem)) !=
+            cudaSuccess)
+            return e;
     for (uint32_t g = 1; g <= kAttnMaxGroup; g *= 2u)
         if ((e = cudaFuncSetAttribute(attn_fn(g), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem)) !=
             cudaSuccess)
@@ -1533,10 +1821,20 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
     return cudaFuncSetAttribute(attn_fn(1, true), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem);
 }
 
+extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes)
+{
+    return m4_smem_bytes(cols, nslot, slot_bytes);
+}
+
 extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaStream_t stream)
 {
     MvArgs copy = *a;
     void *args[] = {&copy};
+    if (a->engine == 1u) {
+        const void *fn = mv4_fn(a->nslot);
+        if (!fn) return cudaErrorInvalidValue;
+        return launch_ex(fn, args, dim3(grid), dim3(kM4Threads), a->smem_bytes, stream, a->pdl != 0u);
+    }
     return launch_ex((const void *)mv_kernel, args, dim3(grid), dim3(kMvThreads), a->smem_bytes, stream, a->pdl != 0u);
 }
 

@@ -39,6 +39,7 @@ extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t 
                                                   cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_prefill_attn_tc(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots);
+extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes);
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits);
 extern "C" int atlas_d2_attn_max_clusters(uint32_t group, uint32_t tc);
 extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
@@ -273,7 +274,9 @@ int upload_matrix_part(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, ui
     if (row0 + nrows > rows || b0 + nblk > nb || !nrows || !nblk) return fail(h, ATLAS_EINVAL, "%s: bad slice", t->name);
     const uint64_t bytes = nrows * nblk * bb;
     uint8_t *d = nullptr;
-    int rc = dalloc(h, &d, bytes);
+    // slack past the end: the decode GEMV reads a Q6_K block as a 256-byte
+    // window from the 16-byte boundary below it
+    int rc = dalloc(h, &d, bytes + d2::kM4Q6Overread);
     if (rc) return rc;
     const uint8_t *src = static_cast<const uint8_t *>(t->data) + row0 * rb;
     if (nblk == nb) {
@@ -526,6 +529,10 @@ int run_program(AtlasCuda *h, ProgramBuffers &pb, uint32_t token, uint32_t pos, 
 // successor's) fit on one SM: (228 KB - 2 x 1 KB reserved) / 2.
 constexpr uint32_t kHalfSmBytes = 115712;
 
+// Decode GEMV kernel of the graph step: 1 = mv4_kernel (per-warp rings),
+// 0 = mv_kernel (producer warp and a ring shared by the CTA).
+constexpr uint32_t kMvEngine = 0u;
+
 struct MvPlan {
     d2::MvArgs a{};
     uint32_t grid = 0;
@@ -687,6 +694,23 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     }
     if (!ok) return fail(h, ATLAS_EINVAL, "mv: no shared-memory plan for %u columns", cols);
     a.smem_bytes = (uint32_t)atlas_d2_mv_smem(cols, a.nslot, a.slot_bytes, a.tslots);
+    if (kMvEngine == 1u) {
+        // per-warp rings (mv4_kernel): the deepest ring that fits the SM's
+        // shared memory; inputs too long for two slots per warp stay on mv_kernel
+        uint32_t slot = 0;
+        for (uint32_t s = 0; s < a.n_seg; ++s)
+            slot = std::max(slot, a.seg[s].type == 12u ? 16u * d2::kM4Q4Row : 16u * d2::kM4Q6Row);
+        for (uint32_t ns = d2::kM4MaxSlots; ns >= 2u; --ns) {
+            const size_t need = atlas_d2_mv4_smem(cols, ns, slot);
+            if (need <= 227u * 1024u) {
+                a.engine = 1u;
+                a.nslot = ns;
+                a.slot_bytes = slot;
+                a.smem_bytes = (uint32_t)need;
+                break;
+            }
+        }
+    }
     d2::MvCta *dc = nullptr;
     int rc = dalloc(h, &dc, ctas.size() * sizeof(d2::MvCta));
     if (rc) return rc;
@@ -1799,14 +1823,6 @@ __global__ void dequant_kernel(uint32_t type, const uint8_t *blocks, uint64_t nb
         out[i] = deq_elem(type, blocks + (i / be) * bb, (int)(i % be));
 }
 
-struct GemvCtx {
-    int device = -1;
-    int sms = 0;
-    ProgramBuffers pb;
-};
-
-GemvCtx g_gemv_ctx[16];
-
 }  // namespace
 
 extern "C" int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, float *d_out, void *stream)
@@ -1939,11 +1955,12 @@ extern "C" int atlas_cuda_gemm(uint32_t type, const void *d_weights, uint64_t ro
 // For callers that cannot allocate device memory: a host that reserves all of
 // HBM up front for weights and KV cache and hands plugins no allocator, or a
 // path with a latency budget that cannot absorb cudaMalloc's implicit device
-// synchronisation. atlas_cuda_gemv keeps its launch scratch in buffers it
-// cudaMallocs on first use; this variant keeps the same scratch - the decode
-// kernel's phase descriptor, its phase counters and its step state - in a
-// fixed 4 KB array of this module's static device memory instead, which every
-// GPU that loads the library holds until the process exits.
+// synchronisation. atlas_cuda_gemv needs no scratch at all; this variant runs
+// the persistent decode kernel (decode.cu) on one GEMV phase, and that kernel
+// needs launch scratch - its phase descriptor, its phase counters and its step
+// state. Here that scratch is a fixed 4 KB array of this module's static
+// device memory, which every GPU that loads the library holds until the
+// process exits.
 #include <mutex>
 
 namespace {
@@ -1956,9 +1973,24 @@ constexpr size_t kNoAllocCtrOff = (sizeof(Phase) + 255) & ~size_t(255);
 constexpr size_t kNoAllocStateOff = kNoAllocCtrOff + 256;
 constexpr size_t kNoAllocNeeded = kNoAllocStateOff + sizeof(StepState);
 static_assert(kNoAllocNeeded <= kNoAllocScratchBytes, "no-alloc scratch too small for the launch descriptor");
+static_assert(sizeof(Phase) % 4 == 0 && kNoAllocNeeded % 4 == 0, "no-alloc scratch is written in words");
 
 std::mutex g_noalloc_mu;
 uint8_t *g_noalloc_ptr[64];  // device address of g_noalloc_scratch, per device
+
+// Writes the phase descriptor (passed by value in the launch parameters, so
+// no host memory is involved) into the scratch and zeroes the phase counters
+// and the step state, which keep the previous call's values otherwise.
+__global__ void noalloc_setup_kernel(const __grid_constant__ Phase ph, uint32_t *scratch)
+{
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(&ph);
+    for (uint32_t i = threadIdx.x; i < (uint32_t)(kNoAllocNeeded / 4); i += blockDim.x) {
+        uint32_t v = 0u;
+        if (i < (uint32_t)(sizeof(Phase) / 4)) v = src[i];
+        else if (i < (uint32_t)(kNoAllocCtrOff / 4)) continue;
+        scratch[i] = v;
+    }
+}
 
 }  // namespace
 
@@ -2008,11 +2040,17 @@ extern "C" int atlas_cuda_gemv_noalloc(uint32_t type, const void *d_weights, uin
     pg.stage_bytes = stage_bytes;
     pg.max_cols = (uint32_t)cols;
     cudaStream_t s = (cudaStream_t)stream;
-    // The array keeps the previous call's contents: the phase counters and the
-    // step state (epoch, exit count, status) must start at zero for each call.
-    cudaError_t e = cudaMemsetAsync(scratch + kNoAllocCtrOff, 0, kNoAllocNeeded - kNoAllocCtrOff, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(scratch + kNoAllocPhaseOff, &ph, sizeof(Phase), cudaMemcpyHostToDevice, s);
+    noalloc_setup_kernel<<<1, 256, 0, s>>>(ph, reinterpret_cast<uint32_t *>(scratch));
+    cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = atlas_launch_decode(&pg, sms, s);
     if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "gemv (no-alloc) launch: %s", cudaGetErrorString(e));
-    return ATLAS_OK;
+    // The kernel's bounded waits record a status word in the scratch's step
+    // state instead of hanging; read it back (into host stack memory, nothing
+    // is allocated), so a timed-out wait is reported rather than a partial y.
+    uint32_t st = 0;
+    e = cudaMemcpyAsync(&st, scratch + kNoAllocStateOff + offsetof(StepState, status), sizeof(st),
+                        cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(nullptr, ATLAS_ECUDA, "gemv (no-alloc): %s", cudaGetErrorString(e));
+    return status_to_code(nullptr, st);
 }

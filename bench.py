@@ -1,32 +1,39 @@
 #!/usr/bin/env python3
-"""Benchmark: batch-1 greedy decode (tok/s, % of HBM roofline) and 512-token
-prefill of the Qwen2.5-3B-shaped synthetic Q4_K/Q6_K model on B200.
+"""Benchmark: batch-1 greedy decode (tok/s, fraction of the HBM roofline) and
+512-token batched prefill (tok/s, fraction of the bf16 tensor roofline) of the
+Qwen2.5-7B-shaped synthetic Q4_K/Q6_K model on B200.
 
 Workload (one "step"): prefill a 512-token seeded random prompt, then 256
-greedy decode steps, batch 1 - the 3B configuration of the benchmark contract
-(hidden 2048, 36 layers, 16/2 heads, FFN 11008, vocab 151936, tied Q6_K head).
-Weights are generated from a fixed seed (no checkpoints or datasets exist on
-the machine) and are 2.03 GB, far larger than L2, so every token streams them
-from HBM.
+greedy decode steps at batch 1 (hidden 3584, 28 layers, 28 query / 4 KV
+heads, FFN 18944, vocab 152064, untied Q6_K head, fp32 KV cache). Weights are
+generated from a fixed seed (no checkpoints or datasets exist on the machine):
+4.62 GB, far larger than L2, so every token streams them from HBM.
 
   value      decode tok/s from CUDA events on the library's stream (device time
              of the generate calls), inputs resident on the GPU
-  e2e        the same metric through the public C API with host buffers:
-             host wall time around atlas_rt_prefill / atlas_rt_generate, which
-             copy token ids in and picked ids (or logits) out every call
+  e2e        the same metric through the public C API with host buffers: host
+             wall time around atlas_rt_prefill / atlas_rt_generate, which copy
+             the token ids in and the picked ids out on every call
   roofline   algorithmic bytes of one decode step (all weights + the KV cache
              read at that position) / device time per token, against the
-             measured HBM copy bandwidth in MEASURED_PEAKS.json
-  cpu_baseline  the reference's own CPU runtime (src/brain_runtime.c compiled
-             in place as oracle/_ref) on a bounded sample of the same workload
+             measured HBM copy bandwidth (MEASURED_PEAKS.json)
+  parity     the first 32 greedy picks against the reference's own run of the
+             same prompt (tests/golden/cfg2.npz, made by the reference itself)
+  cpu_baseline  the reference's own CPU runtime (src/brain_runtime.c compiled in
+             place as oracle/_ref) on the box's host cores: decode at the same
+             positions as the GPU arm (512 onwards) and prompt tokens, on a
+             bounded sample
 
---impl reference runs only that CPU reference (all host cores it may use, the
-reference caps its GEMV workers at 16) and prints its own JSON line.
-Multi-GPU (torchrun, --gpus N): this model has 2 KV heads, so ranks run
-independent replicas ("replicas only"): value = N * tokens / max-over-ranks time.
+Multi-GPU (torchrun, --gpus N): the 7B model is tensor-parallel over its 4 KV
+heads. N = 2 and 4 run one tensor-parallel group of N ranks; N = 8 runs two
+groups of 4 (each decodes its own copy of the workload). value = groups x
+tokens / max-over-ranks device time.
+
+--impl reference runs only the CPU reference (rank 0; other ranks exit) and
+prints its own JSON line; it never loads libatlas_cuda.so (its model file
+comes from the writer built into oracle/liboracle.so).
 """
 import argparse
-import ctypes
 import json
 import os
 import statistics
@@ -38,23 +45,39 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "-1.7-atlas---apollo_b200", "python"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
 
-CFG = dict(hidden=2048, layers=36, q_heads=16, kv_heads=2, ffn=11008, vocab=151936, head_dim=128,
-           context_length=32768, seed=1, tied=True)
-PROMPT, GEN = 512, 256
+CFG2 = dict(hidden=3584, layers=28, q_heads=28, kv_heads=4, ffn=18944, vocab=152064, context_length=32768, seed=2,
+            tied=False)
+CFG1 = dict(hidden=2048, layers=36, q_heads=16, kv_heads=2, ffn=11008, vocab=151936, context_length=32768, seed=1,
+            tied=True)
+WORKLOAD = {
+    "cfg2": "Qwen2.5-7B-shaped Q4_K/Q6_K (hidden 3584, 28 layers, 28/4 heads, FFN 18944, vocab 152064, untied Q6_K "
+            "head): 512-token prefill + 256 greedy decode, batch 1",
+    "cfg1": "Qwen2.5-3B-shaped Q4_K/Q6_K (hidden 2048, 36 layers, 16/2 heads, FFN 11008, vocab 151936, tied Q6_K "
+            "head): 512-token prefill + 256 greedy decode, batch 1",
+}
+PROMPT, GEN, PROMPT_SEED = 512, 256, 1234
 METRIC = "decode tok/s (batch 1) & % HBM roofline; prefill tok/s at 512-token prompt"
 Q4K, Q6K = 144.0 / 256.0, 210.0 / 256.0
 
 
-def weight_bytes(c):
-    H, qd, kvd, F, L, V = c["hidden"], c["q_heads"] * 128, c["kv_heads"] * 128, c["ffn"], c["layers"], c["vocab"]
-    per_layer = (qd * H * Q4K + kvd * H * Q4K + kvd * H * Q6K + H * qd * Q4K + 2 * F * H * Q4K + H * F * Q6K
-                 + 4 * (2 * H + qd + 2 * kvd))
-    return L * per_layer + V * H * Q6K + 4 * H
+def weight_bytes(c, sl=None):
+    """Algorithmic weight bytes of one decode step (of one tensor-parallel rank when sl is its slice)."""
+    H, L, V = c["hidden"], c["layers"], c["vocab"]
+    qd, kvd, F = c["q_heads"] * 128, c["kv_heads"] * 128, c["ffn"]
+    if sl is None:
+        per_layer = (qd * H * Q4K + kvd * H * Q4K + kvd * H * Q6K + H * qd * Q4K + 2 * F * H * Q4K + H * F * Q6K
+                     + 4 * (2 * H + qd + 2 * kvd))
+        return L * per_layer + V * H * Q6K + 4 * H
+    lq, lkv = sl["q_heads"] * 128, sl["kv_heads"] * 128
+    per_layer = ((lq + lkv) * H * Q4K + lkv * H * Q6K + H * sl["o_blocks"] * 256 * Q4K + 2 * sl["ffn_rows"] * H * Q4K
+                 + H * sl["ffn_rows"] * Q6K + 4 * (2 * H + lq + 2 * lkv))
+    return L * per_layer + sl["vocab_rows"] * H * Q6K + 4 * H
 
 
-def kv_bytes_per_position(c, kv_elem_bytes=4):
-    return 2 * c["layers"] * c["kv_heads"] * 128 * kv_elem_bytes
+def kv_bytes_per_position(c, kv_heads=None):
+    return 2 * c["layers"] * (kv_heads or c["kv_heads"]) * 128 * 4
 
 
 def prefill_flops(c, T):
@@ -64,27 +87,34 @@ def prefill_flops(c, T):
     return L * (2.0 * T * (2 * qd * H + 2 * kvd * H + 3 * F * H) + 4.0 * c["q_heads"] * 128 * T * T / 2.0)
 
 
-def tensor_peak():
+def measured(key, fallback):
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            p = json.load(f)
-        return float(p["bf16_tflops"]), "measured"
+            return float(json.load(f)[key]), "measured"
     except Exception:
-        return 1590.0, "fallback"
+        return fallback, "fallback"
 
 
-def model_path(rank):
+def model_path(name):
     d = os.environ.get("ATLAS_BENCH_DIR", tempfile.gettempdir())
-    return os.path.join(d, "atlas_bench_qwen25_3b_seed1.gguf")
+    return os.path.join(d, f"atlas_bench_{name}.gguf")
 
 
-def peaks():
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
-    except Exception:
-        return 6650.0, "fallback"
+def prompt_ids(cfg):
+    import numpy as np
+    return np.random.default_rng(PROMPT_SEED).integers(0, cfg["vocab"], PROMPT).astype(np.uint32)
+
+
+def golden_picks(name, cfg):
+    """The reference's 32 greedy picks after this prompt, if the fixture exists and matches the model."""
+    import numpy as np
+    p = os.path.join(ROOT, "tests", "golden", f"{name}.npz")
+    if not os.path.exists(p):
+        return None
+    g = np.load(p)
+    if any(int(g[f"cfg_{k}"]) != int(v) for k, v in cfg.items()) or not np.array_equal(g["prompt"], prompt_ids(cfg)):
+        return None
+    return g["picks"]
 
 
 class Clocks:
@@ -129,34 +159,93 @@ class Clocks:
                 "reasons": reasons, "samples": len(sm)}
 
 
-def cpu_reference_sample(path, n_decode=4, n_prompt=2):
-    """The reference's own forward_token (oracle/_ref) on the host cores: a
-    bounded sample of the workload (n_prompt prompt tokens, then n_decode
-    greedy decode tokens); returns (decode tok/s, cores)."""
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
+# ------------------------------------------------------------------ CPU side --
+
+def ref_threads():
+    """All host threads; the reference itself caps its GEMV workers at 16 (src/brain_runtime.c:1172)."""
+    n = os.cpu_count() or 1
+    return n, min(16, n)
+
+
+def cpu_reference_sample(path, cfg, n_decode, n_prompt):
+    """The reference's own forward_token (oracle/_ref) on the host cores.
+    Prompt rate: n_prompt tokens without logits, as the reference's own prompt
+    loop runs them (src/brain_runtime.c:2025-2028). Decode rate: the cache is
+    filled to PROMPT positions by repeating those rows (the work of a decode
+    step does not depend on the cached values), then n_decode greedy steps at
+    positions PROMPT.. as the GPU arm decodes them. Returns a dict or None."""
     import numpy as np
     import oracle_bind
-    cores = min(16, os.cpu_count() or 1)
-    os.environ["ATLAS_REF_THREADS"] = str(cores)
+    host, used = ref_threads()
+    os.environ["ATLAS_REF_THREADS"] = str(host)
     ref = oracle_bind.Reference.load()
     if ref is None:
-        return None, cores, "oracle/_ref/libbrainref.so not built"
+        return None
     r = ref.open(path)
-    prompt = np.random.default_rng(0).integers(0, CFG["vocab"], n_prompt)
-    lg = None
+    prompt = prompt_ids(cfg)[:n_prompt]
+    t0 = time.perf_counter()
     for i, t in enumerate(prompt):
-        lg = r.forward(int(t), i, i + 1 == n_prompt)
-    nxt = r.greedy(lg)
+        r.forward(int(t), i, False)
+    t_prompt = time.perf_counter() - t0
+    r.fill_cache(n_prompt, PROMPT)
+    nxt = int(prompt[-1])
     t0 = time.perf_counter()
     for s in range(n_decode):
-        lg = r.forward(nxt, n_prompt + s)
+        lg = r.forward(nxt, PROMPT + s, True)
         nxt = r.greedy(lg)
-    dt = time.perf_counter() - t0
+    t_dec = time.perf_counter() - t0
     r.close()
-    return n_decode / dt, cores, f"{n_prompt} prompt tokens then {n_decode} greedy decode tokens of the 3B model"
+    return {"decode_tok_s": n_decode / t_dec, "prefill_tok_s": n_prompt / t_prompt, "host_cores": host,
+            "gemv_threads": used}
 
 
-def dist_setup(n_gpus):
+def ensure_model_oracle_writer(name, cfg):
+    import oracle_bind
+    path = model_path(name)
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        oracle_bind.write_synthetic_gguf(tmp, **cfg)
+        os.replace(tmp, path)
+    return path
+
+
+def run_reference(args):
+    """CPU reference arm: rank 0 only; other ranks exit at once without work."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    path = ensure_model_oracle_writer("cfg2", CFG2)
+    dec, pre = [], []
+    smp = None
+    for i in range(args.warmup + args.steps):
+        smp = cpu_reference_sample(path, CFG2, n_decode=2, n_prompt=2)
+        if smp is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libbrainref.so was not built "
+                                                                  "(the reference sources were absent at build time)"}))
+            return
+        if i >= args.warmup:
+            dec.append(smp["decode_tok_s"])
+            pre.append(smp["prefill_tok_s"])
+    v = statistics.mean(dec)
+    sample = (f"per step: 2 prompt tokens (token at a time, no logits), then 2 greedy decode tokens at positions "
+              f"{PROMPT}-{PROMPT + 1} over a {PROMPT}-position cache, 7B shape; "
+              f"{smp['host_cores']} host threads, {smp['gemv_threads']} GEMV workers (the reference's cap)")
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(2000.0 / v + 2000.0 / statistics.mean(pre), 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
+            "config": {"workload": WORKLOAD["cfg2"] + " (CPU: bounded sample)", "parallelism": "CPU threads",
+                       "kv_cache": "fp32"},
+            "prefill_tok_s": round(statistics.mean(pre), 4),
+            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": smp["gemv_threads"],
+                             "host_cores": smp["host_cores"], "kind": "reference", "sample": sample,
+                             "prefill_tok_s": round(statistics.mean(pre), 4)},
+            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU side --
+
+def dist_setup():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -184,52 +273,19 @@ def allmax(pg, v):
     return float(t.item())
 
 
-def ensure_model(rank, pg):
-    import atlas_cuda
-    path = model_path(rank)
-    if rank == 0 and not os.path.exists(path):
-        tmp = path + ".tmp"
-        atlas_cuda.write_synthetic_gguf(tmp, **CFG)
-        os.replace(tmp, path)
-    barrier(pg)
-    return path
+def tp_layout(ws):
+    """(tensor-parallel size, groups) for N ranks of the 7B model (4 KV heads)."""
+    if ws <= 4:
+        return ws, 1
+    if ws % 4:
+        raise SystemExit(f"--gpus {ws}: the 7B model is tensor-parallel over 1, 2 or 4 ranks; use 1, 2, 4 or 8")
+    return 4, ws // 4
 
 
-def run_reference(args):
-    ws, rank, local, pg = dist_setup(args.gpus)
-    path = ensure_model(rank, pg)
-    if rank != 0:
-        barrier(pg)
-        return
-    steps = []
-    for i in range(args.warmup + args.steps):
-        tps, cores, sample = cpu_reference_sample(path, n_decode=2, n_prompt=1)
-        if tps is None:
-            print(json.dumps({"impl": "reference", "unavailable": sample}))
-            barrier(pg)
-            return
-        if i >= args.warmup:
-            steps.append(tps)
-    v = statistics.mean(steps)
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(2000.0 / v, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded random Q4_K/Q6_K weights)",
-            "config": {"workload": "Qwen2.5-3B-shaped Q4_K/Q6_K, batch-1 greedy decode (CPU sample)"},
-            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "reference",
-                             "sample": "per step: 1 prompt token then 2 greedy decode tokens of the 3B model"},
-            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
-    barrier(pg)
-
-
-def run_ours(args):
+def run_model(name, cfg, rt, steps, warmup, pg, clocks_gpu=None):
+    """Times `steps` workload steps (prefill + GEN decode) after `warmup`; returns per-rank sums."""
     import numpy as np
-    import atlas_cuda
-    ws, rank, local, pg = dist_setup(args.gpus)
-    path = ensure_model(rank, pg)
-    rt = atlas_cuda.Runtime(path, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT)
-    prompt = np.random.default_rng(1234).integers(0, CFG["vocab"], PROMPT).astype(np.uint32)
+    prompt = prompt_ids(cfg)
 
     def step():
         d0 = rt.stats()[2]
@@ -241,85 +297,164 @@ def run_ours(args):
         t2 = time.perf_counter()
         d2 = rt.stats()[2]
         return dict(prefill_dev=(d1 - d0) / 1e3, gen_dev=(d2 - d1) / 1e3, prefill_wall=t1 - t0, gen_wall=t2 - t1,
-                    ids=ids)
+                    ids=np.concatenate([[first], ids]).astype(np.uint32))
 
-    for _ in range(args.warmup):
+    ref_ids = None
+    for _ in range(warmup):
         ref_ids = step()["ids"]
     barrier(pg)
     launches0 = rt.stats()[0]
     res = []
-    with Clocks(local) as clk:
+    clk = Clocks(clocks_gpu) if clocks_gpu is not None else None
+    if clk:
+        clk.__enter__()
+    try:
         barrier(pg)
-        for _ in range(args.steps):
+        for _ in range(steps):
             r = step()
-            assert np.array_equal(r["ids"], ref_ids), "greedy output changed between steps"
+            if ref_ids is not None and not np.array_equal(r["ids"], ref_ids):
+                raise AssertionError(f"{name}: greedy output changed between steps")
+            ref_ids = r["ids"]
             res.append(r)
         barrier(pg)
-    launches = rt.stats()[0] - launches0
-    gen_dev = allmax(pg, sum(r["gen_dev"] for r in res))
-    pre_dev = allmax(pg, sum(r["prefill_dev"] for r in res))
-    gen_wall = allmax(pg, sum(r["gen_wall"] for r in res))
-    pre_wall = allmax(pg, sum(r["prefill_wall"] for r in res))
-    decode_tps = ws * args.steps * GEN / gen_dev
-    prefill_tps = ws * args.steps * PROMPT / pre_dev
-    e2e_decode = ws * args.steps * GEN / gen_wall
-    # roofline of the decode step (a chain of HBM-bound kernels replayed as one graph per token)
-    wb = weight_bytes(CFG)
-    kv_avg = kv_bytes_per_position(CFG) * (PROMPT + GEN / 2.0)
-    bytes_per_token = wb + kv_avg
-    per_token_s = gen_dev / (args.steps * GEN)
-    achieved = bytes_per_token / per_token_s / 1e9
-    peak, peak_kind = peaks()
-    tpeak, tpeak_kind = tensor_peak()
-    pf_flops = prefill_flops(CFG, PROMPT)
-    pf_tflops = pf_flops / (pre_dev / (ws * args.steps)) / 1e12
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tf):
-        try:
-            traffic = json.load(open(tf)).get("dram_bytes_per_token")
-        except Exception:
-            traffic = None
-    cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        tps, cores, sample = cpu_reference_sample(path)
-        if tps is not None:
-            cpu = {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample}
-    if rank == 0:
-        clocks = clk.summary()
-        line = {
-            "metric": METRIC, "value": round(decode_tps, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(1e3 * (gen_dev + pre_dev) / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
-            "config": {"workload": "Qwen2.5-3B-shaped Q4_K/Q6_K (hidden 2048, 36 layers, 16/2 heads, FFN 11008, "
-                                   "vocab 151936, tied Q6_K head): 512-token prefill + 256 greedy decode, batch 1",
-                       "parallelism": f"replicas x{ws}" if ws > 1 else "1 GPU",
-                       "l2": "inputs larger than L2 (2.03 GB of weights streamed per token)",
-                       "kv_cache": "fp32"},
-            "prefill_tok_s": round(prefill_tps, 2),
-            "prefill_roofline": {"bound": "tensor", "achieved": round(pf_tflops, 1), "peak": tpeak, "unit": "TFLOP/s",
-                                 "frac": round(pf_tflops / tpeak, 4), "peak_kind": tpeak_kind,
-                                 "flops_per_prefill": pf_flops,
-                                 "note": "algorithmic flops; the contraction computes hi.hi + lo.hi + hi.lo binary16 "
-                                         "products (3x the tensor work) for fp32-level accuracy"},
-            "decode_ms_per_token": round(1e3 * per_token_s, 4),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "bytes_per_token": int(bytes_per_token),
-                         "kernel": "decode step: CUDA graph of PDL-chained kernels (mv_kernel dequant-GEMVs, "
-                                   "attn_kernel, embed, argmax); achieved = weight + KV bytes per token / device "
-                                   "time per token"},
-            "e2e": {"value": round(e2e_decode, 2), "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4 + 64,
-                    "d2h_bytes_per_step": GEN * 4 + 64,
-                    "prefill_tok_s": round(ws * args.steps * PROMPT / pre_wall, 2)},
-            "gpu_launches": int(launches),
-            "cpu_baseline": cpu,
-            "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
-        }
-        print(json.dumps(line), flush=True)
+    finally:
+        if clk:
+            clk.__exit__(None, None, None)
+    out = {k: sum(r[k] for r in res) for k in ("gen_dev", "prefill_dev", "gen_wall", "prefill_wall")}
+    out["launches"] = rt.stats()[0] - launches0
+    out["ids"] = ref_ids
+    out["clocks"] = clk.summary() if clk else None
+    return out
+
+
+def summarize(name, cfg, r, steps, pg, groups, sl=None, tp=1):
+    """Whole-job rates (max over ranks) and the roofline of the decode step."""
+    gen_dev, pre_dev = allmax(pg, r["gen_dev"]), allmax(pg, r["prefill_dev"])
+    gen_wall, pre_wall = allmax(pg, r["gen_wall"]), allmax(pg, r["prefill_wall"])
+    decode_tps = groups * steps * GEN / gen_dev
+    per_token_s = gen_dev / (steps * GEN)
+    kv_heads = sl["kv_heads"] if sl else cfg["kv_heads"]
+    kv_avg = kv_bytes_per_position(cfg, kv_heads) * (PROMPT + GEN / 2.0)
+    rank_bytes = weight_bytes(cfg, sl) + kv_avg             # one rank's algorithmic bytes per token
+    total_bytes = weight_bytes(cfg) + kv_bytes_per_position(cfg) * (PROMPT + GEN / 2.0)
+    hbm, hbm_kind = measured("hbm_gbs", 6650.0)
+    tpk, tpk_kind = measured("bf16_tflops", 1590.0)
+    rank_gbs = rank_bytes / per_token_s / 1e9
+    pf_tflops = prefill_flops(cfg, PROMPT) / (pre_dev / steps) / 1e12 / tp   # per GPU of a group
+    golden = golden_picks(name, cfg)
+    parity = None
+    if golden is not None and r["ids"] is not None:
+        n = min(len(golden), len(r["ids"]))
+        parity = {"picks_checked": int(n), "picks_match_reference": bool((r["ids"][:n] == golden[:n]).all()),
+                  "fixture": f"tests/golden/{name}.npz"}
+    return {
+        "decode_tok_s": decode_tps, "prefill_tok_s": groups * steps * PROMPT / pre_dev,
+        "decode_ms_per_token": 1e3 * per_token_s, "ms_per_step": 1e3 * (gen_dev + pre_dev) / steps,
+        "e2e_decode_tok_s": groups * steps * GEN / gen_wall, "e2e_prefill_tok_s": groups * steps * PROMPT / pre_wall,
+        "roofline": {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(rank_gbs / hbm, 4), "peak_kind": hbm_kind,
+                     "bytes_per_token": int(rank_bytes), "traffic": None,
+                     "traffic_note": "DRAM bytes of one decode step from an ncu capture are in profiles/ "
+                                     "(decode_step_*); not re-measured inside the timed run",
+                     "kernel": "decode step: CUDA graph of PDL-chained kernels (mv_kernel dequant-GEMVs, attention, "
+                               "embed, argmax); achieved = one GPU's weight + KV bytes per token / device time per "
+                               "token"},
+        "prefill_roofline": {"bound": "tensor", "achieved": round(pf_tflops, 1), "peak": tpk, "unit": "TFLOP/s",
+                             "frac": round(pf_tflops / tpk, 4), "peak_kind": tpk_kind,
+                             "flops_per_prefill": prefill_flops(cfg, PROMPT),
+                             "note": "algorithmic flops per GPU; the contraction computes hi.hi + lo.hi + hi.lo "
+                                     "binary16 products (3x the tensor work) for fp32-level accuracy"},
+        "total_bytes_per_token": int(total_bytes),
+        "parity": parity,
+    }
+
+
+def ensure_model_product_writer(name, cfg, rank, pg):
+    import atlas_cuda
+    path = model_path(name)
+    if rank == 0 and not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        atlas_cuda.write_synthetic_gguf(tmp, **cfg)
+        os.replace(tmp, path)
+    barrier(pg)
+    return path
+
+
+def run_ours(args):
+    import atlas_cuda
+    ws, rank, local, pg = dist_setup()
+    tp, groups = tp_layout(ws)
+    group_id, tp_rank = rank // tp, rank % tp
+    tp_group = None
+    if pg and groups > 1:
+        subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
+        tp_group = subgroups[group_id]
+    path = ensure_model_product_writer("cfg2", CFG2, rank, pg)
+    rt = atlas_cuda.Runtime(path, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT,
+                            tp_rank=tp_rank, tp_size=tp)
+    if tp > 1:
+        atlas_cuda.connect_tp(rt, group=tp_group)
+    barrier(pg)
+    sl = rt.tp_slice().as_dict() if tp > 1 else None
+    r = run_model("cfg2", CFG2, rt, args.steps, args.warmup, pg, clocks_gpu=local if rank == 0 else None)
+    s = summarize("cfg2", CFG2, r, args.steps, pg, groups, sl, tp)
     rt.close()
     barrier(pg)
+    if ws == 1 and s["parity"] is not None and not s["parity"]["picks_match_reference"]:
+        raise SystemExit(f"greedy picks differ from the reference's (tests/golden/cfg2.npz): {list(r['ids'][:32])}")
+    secondary, cpu = None, None
+    if ws == 1 and not args.no_secondary:
+        p1 = ensure_model_product_writer("cfg1", CFG1, rank, pg)
+        with atlas_cuda.Runtime(p1, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT) as rt1:
+            r1 = run_model("cfg1", CFG1, rt1, args.steps, args.warmup, pg)
+            s1 = summarize("cfg1", CFG1, r1, args.steps, pg, 1)
+        if s1["parity"] is not None and not s1["parity"]["picks_match_reference"]:
+            raise SystemExit(f"greedy picks differ from the reference's (tests/golden/cfg1.npz): {list(r1['ids'][:32])}")
+        secondary = {"workload": WORKLOAD["cfg1"], "decode_tok_s": round(s1["decode_tok_s"], 2),
+                     "decode_ms_per_token": round(s1["decode_ms_per_token"], 4),
+                     "prefill_tok_s": round(s1["prefill_tok_s"], 1), "roofline_frac": s1["roofline"]["frac"],
+                     "prefill_roofline_frac": s1["prefill_roofline"]["frac"],
+                     "e2e_decode_tok_s": round(s1["e2e_decode_tok_s"], 2), "parity": s1["parity"],
+                     "gpu_launches": int(r1["launches"])}
+    if ws == 1 and not args.no_cpu_baseline:
+        c = cpu_reference_sample(model_path("cfg2"), CFG2, n_decode=3, n_prompt=3)
+        if c is not None:
+            cpu = {"value": round(c["decode_tok_s"], 4), "unit": "tok/s", "cores": c["gemv_threads"],
+                   "host_cores": c["host_cores"], "kind": "reference",
+                   "prefill_tok_s": round(c["prefill_tok_s"], 4),
+                   "sample": f"3 prompt tokens (token at a time, no logits), then 3 greedy decode tokens at positions "
+                             f"{PROMPT}-{PROMPT + 2} over a {PROMPT}-position cache, 7B shape"}
+    if rank == 0:
+        clocks = r["clocks"] or {}
+        par = f"tp{tp}" if groups == 1 else f"tp{tp} x {groups} groups"
+        line = {
+            "metric": METRIC, "value": round(s["decode_tok_s"], 2), "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(s["ms_per_step"], 3),
+            "higher_is_better": True, "scaling": "strong" if groups == 1 and ws > 1 else "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
+            "config": {"workload": WORKLOAD["cfg2"], "parallelism": par if ws > 1 else "1 GPU",
+                       "l2": "inputs larger than L2 (4.62 GB of weights streamed per token)", "kv_cache": "fp32"},
+            "decode_ms_per_token": round(s["decode_ms_per_token"], 4),
+            "prefill_tok_s": round(s["prefill_tok_s"], 1),
+            "roofline": s["roofline"],
+            "prefill_roofline": s["prefill_roofline"],
+            "e2e": {"value": round(s["e2e_decode_tok_s"], 2), "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4 + 4,
+                    "d2h_bytes_per_step": GEN * 4 + 4, "prefill_tok_s": round(s["e2e_prefill_tok_s"], 1)},
+            "parity": s["parity"],
+            "gpu_launches": int(r["launches"]),
+            "cpu_baseline": cpu,
+            "secondary": secondary,
+            "clocks": {k: clocks.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        }
+        if tp > 1:
+            line["tensor_parallel"] = {"tp": tp, "groups": groups, "rank0_slice": sl,
+                                       "per_gpu_gbs": s["roofline"]["achieved"],
+                                       "aggregate_gbs": round(s["roofline"]["achieved"] * ws, 1)}
+        print(json.dumps(line), flush=True)
+    barrier(pg)
+    if pg:
+        pg.destroy_process_group()
 
 
 def main():
@@ -329,6 +464,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the 3B workload at N=1")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -170,23 +170,29 @@ int atlas_cuda_dequant(uint32_t type, const void *d_blocks, uint64_t nblocks, fl
 
 /* y[rows] = W[rows x cols] x[cols] for a Q4_K / Q6_K tensor in device memory
    (matvec_rows, src/brain_runtime.c:1133) on the streaming GEMV kernel: fp32
-   FMAs over the exactly dequantized quants, one launch, no scratch.
+   FMAs over the exactly dequantized quants, one launch, no scratch memory.
    d_weights: 16-byte aligned for Q4_K, 2-byte for Q6_K; cols a multiple of 256,
    at most 49152; d_x 16-byte aligned, d_y 4-byte aligned. */
 int atlas_cuda_gemv(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                     const float *d_x, float *d_y, void *stream);
 
-/* atlas_cuda_gemv for callers that cannot allocate device memory (a host that
-   owns all of HBM, or a path that cannot absorb cudaMalloc's device
-   synchronisation). No counterpart in the reference. Same arguments, result
-   and limits as atlas_cuda_gemv, but it calls no cudaMalloc / cudaFree: its
-   launch scratch (kernel descriptor, phase counters, step state) is a 4 KB
-   static device array in this library, held by every GPU that loads it until
-   the process exits. The first call on a device looks up that array's device
-   address; make that first call before any stream capture. All calls share the
-   one array: calls that overlap on the GPU (other streams, other host threads)
-   race and give wrong results. Inputs longer than the shared-memory plan
-   supports are rejected with ATLAS_EINVAL. */
+/* A GEMV for callers that cannot allocate device memory: a host that owns all
+   of HBM and hands plugins no allocator, or a path that cannot absorb
+   cudaMalloc's device synchronisation. No counterpart in the reference.
+   Same arguments and result as atlas_cuda_gemv (y = W x, within 1e-4 max|y|
+   of the oracle), computed by the persistent decode kernel, which needs
+   launch scratch (kernel descriptor, phase counters, step state). That
+   scratch is a 4 KB static device array in this library, held by every GPU
+   that loads it until the process exits; the call makes no cudaMalloc or
+   cudaFree. Its first call on a device looks up the array's device address
+   (cudaGetSymbolAddress) and keeps it, so that first call should come before
+   any stream capture, and the kept address does not survive cudaDeviceReset.
+   All calls share the one array: calls that overlap on the GPU (other streams,
+   other host threads) race and give wrong results. The call waits for the
+   stream and reads the kernel's status word back: it returns ATLAS_ETIMEOUT
+   if a bounded device wait ran out, and y is complete when it returns
+   ATLAS_OK. Input lengths beyond what the kernel stages in shared memory
+   (about 49,000 columns on B200) are rejected with ATLAS_EINVAL. */
 int atlas_cuda_gemv_noalloc(uint32_t type, const void *d_weights, uint64_t rows, uint64_t cols,
                             const float *d_x, float *d_y, void *stream);
 

@@ -169,6 +169,22 @@ int ref_kv_row(uint32_t layer, uint64_t pos, float *k_out, float *v_out)
     return 1;
 }
 
+/* Benchmark helper: fills cache positions [filled, upto) of every layer by
+   repeating rows [0, filled), so that forward_token can be timed at position
+   `upto` without running upto prompt tokens first. The work of a decode step
+   at a position does not depend on the cached values. */
+int ref_fill_cache(uint64_t filled, uint64_t upto)
+{
+    if (!g_ref_kc || !filled || upto > (uint64_t)MAX_CONTEXT || filled > upto) return 0;
+    for (size_t l = 0; l < (size_t)LAYERS; ++l)
+        for (uint64_t p = filled; p < upto; ++p) {
+            size_t dst = (l * MAX_CONTEXT + (size_t)p) * KV_DIM, src = (l * MAX_CONTEXT + (size_t)(p % filled)) * KV_DIM;
+            memcpy(g_ref_kc + dst, g_ref_kc + src, (size_t)KV_DIM * sizeof(float));
+            memcpy(g_ref_vc + dst, g_ref_vc + src, (size_t)KV_DIM * sizeof(float));
+        }
+    return 1;
+}
+
 /* Greedy pick exactly as atlas_sample_token(..., allow_stop=1, greedy=1). */
 uint32_t ref_sample_greedy(const float *logits, uint64_t vocab)
 {

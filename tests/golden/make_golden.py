@@ -13,6 +13,17 @@ Fixtures (all produced by the reference's own code, src/brain_runtime.c):
                 12/2 heads, FFN 8960, vocab 151936, tied Q6_K head, seed 0):
                 a 32-token uniform-random prompt, the 32 greedy picks, and the
                 logits (fp16) after the prompt and after the first pick
+  cfg1.npz      the same for the Qwen2.5-3B shape (hidden 2048, 36 layers,
+                16/2 heads, FFN 11008, vocab 151936, tied head, seed 1) with
+                the 512-token prompt the benchmark decodes after
+  cfg2.npz      the same for the Qwen2.5-7B shape (hidden 3584, 28 layers,
+                28/4 heads, FFN 18944, vocab 152064, untied Q6_K head, seed 2),
+                512-token prompt
+
+The reference runs the prompt token by token (src/brain_runtime.c:2025-2028),
+so cfg1/cfg2 take tens of minutes on a few cores. Usage:
+  python tests/golden/make_golden.py            # dequant, tiny, cfg0
+  python tests/golden/make_golden.py cfg1 cfg2  # the large shapes
 """
 import hashlib
 import os
@@ -31,6 +42,13 @@ import oracle_bind  # noqa: E402
 
 TINY = dict(hidden=512, layers=2, q_heads=4, kv_heads=2, ffn=768, vocab=1024, context_length=512, seed=1234)
 CFG0 = dict(hidden=1536, layers=28, q_heads=12, kv_heads=2, ffn=8960, vocab=151936, context_length=32768, seed=0)
+# large shapes: (model, tied, prompt seed, prompt length)
+LARGE = {
+    "cfg1": (dict(hidden=2048, layers=36, q_heads=16, kv_heads=2, ffn=11008, vocab=151936, context_length=32768,
+                  seed=1), True, 1234, 512),
+    "cfg2": (dict(hidden=3584, layers=28, q_heads=28, kv_heads=4, ffn=18944, vocab=152064, context_length=32768,
+                  seed=2), False, 1234, 512),
+}
 
 
 def sha256(path):
@@ -60,7 +78,33 @@ def greedy_run(ref, prompt, steps):
     return np.array(picks, np.uint32), logits
 
 
+def make_large(ref, name, workdir):
+    cfg, tied, pseed, plen = LARGE[name]
+    p = os.path.join(workdir, f"{name}.gguf")
+    atlas_cuda.write_synthetic_gguf(p, tied=tied, **cfg)
+    r = ref.open(p)
+    prompt = np.random.default_rng(pseed).integers(0, cfg["vocab"], plen).astype(np.uint32)
+    picks, logits = greedy_run(r, prompt, 32)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), sha256=sha256(p), prompt=prompt, picks=picks,
+                        tied=np.int32(tied), logits_prompt=logits[0].astype(np.float16),
+                        logits_step1=logits[1].astype(np.float16),
+                        max_abs_prompt=np.float32(np.abs(logits[0]).max()),
+                        max_abs_step1=np.float32(np.abs(logits[1]).max()),
+                        **{f"cfg_{k}": v for k, v in cfg.items()})
+    r.close()
+    os.remove(p)
+
+
 def main():
+    ref = oracle_bind.Reference.load()
+    assert ref is not None, "build oracle/_ref first (make -C oracle ref)"
+    large = [a for a in sys.argv[1:] if a in LARGE]
+    if large:
+        with tempfile.TemporaryDirectory(dir=os.environ.get("ATLAS_GOLDEN_TMP")) as td:
+            for name in large:
+                make_large(ref, name, td)
+                print("golden fixture written:", name, flush=True)
+        return
     ref = oracle_bind.Reference.load()
     assert ref is not None, "build oracle/_ref first (make -C oracle ref)"
     rng = np.random.default_rng(20261201)

@@ -18,6 +18,21 @@ def _p(a):
     return ctypes.c_void_p(0) if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
 
+def write_synthetic_gguf(path, *, hidden, layers, q_heads, kv_heads, ffn, vocab, head_dim=128, context_length=32768,
+                         rope_base=1e6, tied=True, qkv_bias=True, seed=0, threads=0, qk_norm=False):
+    """The seeded synthetic GGUF writer as built into liboracle.so (the same
+    writer source as the product library's atlas_synth_write_gguf; a CPU test
+    checks that both produce identical bytes). Lets the CPU reference arm make
+    its model file without loading libatlas_cuda.so."""
+    from atlas_cuda import SynthConfig
+    L = ctypes.CDLL(Oracle.PATH)
+    L.atlas_synth_write_gguf.argtypes = [P, ctypes.c_char_p]
+    cfg = SynthConfig(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, context_length, rope_base, int(tied),
+                      int(qkv_bias), threads, seed, int(qk_norm))
+    if L.atlas_synth_write_gguf(ctypes.byref(cfg), path.encode()) != 0:
+        raise RuntimeError(f"synthetic GGUF write failed: {path}")
+
+
 class Oracle:
     PATH = os.path.join(ROOT, "oracle", "liboracle.so")
 
@@ -129,6 +144,7 @@ class Reference:
         L.ref_data_base.restype = U64
         L.ref_kv_row.argtypes = [U32, U64, P, P]
         L.ref_last_hidden.argtypes = [P]
+        L.ref_fill_cache.argtypes = [U64, U64]
         self.L = L
         self.vocab = None
 
@@ -159,6 +175,10 @@ class Reference:
 
     def greedy(self, logits):
         return int(self.L.ref_sample_greedy(_p(logits), len(logits)))
+
+    def fill_cache(self, filled, upto):
+        """Cache positions [filled, upto) repeat rows [0, filled) (benchmark helper)."""
+        assert self.L.ref_fill_cache(filled, upto)
 
     def close(self):
         self.L.ref_close()

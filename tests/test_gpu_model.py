@@ -247,3 +247,72 @@ def test_fp16_cache_tensor_core_attention_qwen3(torch_cuda, tiny_qwen3_model, mo
     _close(lg_tc, lg_cc.astype(np.float64), 1e-4)
     assert (am_tc, am1_tc) == (am_cc, am1_cc)
     np.testing.assert_array_equal(picks_tc, picks_cc)
+
+
+def _sha256(path):
+    import hashlib
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 24), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def _large(model_dir, name):
+    p = os.path.join(GOLDEN, f"{name}.npz")
+    if not os.path.exists(p):
+        pytest.skip(f"{name}.npz not generated (tests/golden/make_golden.py {name})")
+    g = np.load(p)
+    cfg = {k[4:]: int(g[k]) for k in g.files if k.startswith("cfg_")}
+    path = os.path.join(str(model_dir), f"{name}.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, tied=bool(int(g["tied"])), **cfg)
+        assert _sha256(path) == str(g["sha256"]), "the model file differs from the one the fixture was made from"
+    return g, path
+
+
+def _run_512(g, path, kv_fp16):
+    """The benchmark's workload shape against the reference's own run: the
+    512-token prompt through the batched prefill, the first pick through one
+    forward, 30 more through the decode graph (src/brain_runtime.c:2025-2048)."""
+    prompt = g["prompt"]
+    with atlas_cuda.Runtime(path, max_context=len(prompt) + 64, max_prefill=len(prompt), kv_fp16=kv_fp16) as rt:
+        lg, am = rt.prefill(prompt)
+        lg1, am1 = rt.forward(am, len(prompt))
+        picks = rt.generate(am1, len(prompt) + 1, 30)
+    got = np.concatenate([[am, am1], picks]).astype(np.uint32)
+    rel = [np.abs(lg.astype(np.float64) - g["logits_prompt"].astype(np.float64)).max() / float(g["max_abs_prompt"]),
+           np.abs(lg1.astype(np.float64) - g["logits_step1"].astype(np.float64)).max() / float(g["max_abs_step1"])]
+    return rel, got
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["cfg1", "cfg2"])
+def test_full_depth_512_token_prompt_matches_reference(torch_cuda, model_dir, name):
+    """Qwen2.5-3B (36 layers) and -7B (28 layers, untied head) shapes at full
+    depth, fp32 KV cache: logits after the 512-token prompt and after the first
+    pick within 2e-2 of the largest reference logit (the fixture stores them
+    as fp16, whose rounding is ~5e-4 of the largest), and the 32 greedy picks
+    identical to the reference's."""
+    g, path = _large(model_dir, name)
+    rel, got = _run_512(g, path, kv_fp16=False)
+    print(f"{name} fp32 cache: max|dlogit|/max|logit| after prompt {rel[0]:.2e}, after pick 1 {rel[1]:.2e}")
+    assert max(rel) <= TOL, rel
+    np.testing.assert_array_equal(got, g["picks"])
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["cfg1", "cfg2"])
+def test_full_depth_fp16_cache_against_reference(torch_cuda, model_dir, name):
+    """The fp16 KV cache (binary16 K and V, read by the tensor-core decode
+    attention and the prefill) against the reference's fp32 run of the same
+    512-token prompt, held to the same contract: logits within 2e-2 of the
+    largest and 32 identical greedy picks."""
+    g, path = _large(model_dir, name)
+    rel, got = _run_512(g, path, kv_fp16=True)
+    agree = int((got == g["picks"]).sum())
+    first_diff = int(np.argmax(got != g["picks"])) if agree < len(got) else -1
+    print(f"{name} fp16 cache: max|dlogit|/max|logit| after prompt {rel[0]:.2e}, after pick 1 {rel[1]:.2e}; "
+          f"greedy picks equal {agree}/32 (first difference at {first_diff})")
+    assert max(rel) <= TOL, rel
+    np.testing.assert_array_equal(got, g["picks"])

@@ -111,3 +111,36 @@ def test_oracle_cfg0_prompt_logits(oracle, model_dir):
         lg = m.forward(int(t), i, i + 1 == len(prompt))
     np.testing.assert_array_equal(lg.astype(np.float16), g["logits_prompt"])
     assert m.argmax(lg) == int(g["picks"][0])
+
+
+@pytest.mark.parametrize("tied", [True, False])
+def test_oracle_writer_bytes_equal_product_writer(model_dir, tied):
+    """The CPU reference arm of the benchmark writes its model file with the
+    writer built into liboracle.so (it never loads libatlas_cuda.so); the file
+    must be byte-identical to the product library's."""
+    import oracle_bind
+    cfg = dict(hidden=768, layers=2, q_heads=6, kv_heads=2, ffn=1280, vocab=2048, context_length=4096,
+               seed=42 + int(tied))
+    a = os.path.join(str(model_dir), f"writer_product_{tied}.gguf")
+    b = os.path.join(str(model_dir), f"writer_oracle_{tied}.gguf")
+    atlas_cuda.write_synthetic_gguf(a, tied=tied, **cfg)
+    oracle_bind.write_synthetic_gguf(b, tied=tied, **cfg)
+    assert os.path.getsize(a) == os.path.getsize(b)
+    assert _sha256(a) == _sha256(b)
+
+
+def test_large_goldens_pin_their_model_files():
+    """cfg1.npz / cfg2.npz (512-token prompts, made by the reference itself) name
+    the sha256 of the model file they were made from and carry the prompt the
+    benchmark decodes after."""
+    for name, vocab in (("cfg1", 151936), ("cfg2", 152064)):
+        p = os.path.join(GOLDEN, f"{name}.npz")
+        if not os.path.exists(p):
+            pytest.skip(f"{name}.npz not generated")
+        g = np.load(p)
+        assert len(str(g["sha256"])) == 64
+        assert g["prompt"].shape == (512,) and int(g["prompt"].max()) < vocab
+        assert g["picks"].shape == (32,) and int(g["picks"].max()) < vocab
+        assert np.isfinite(g["logits_prompt"].astype(np.float32)).all()
+        want = np.random.default_rng(1234).integers(0, vocab, 512).astype(np.uint32)
+        np.testing.assert_array_equal(g["prompt"], want)
