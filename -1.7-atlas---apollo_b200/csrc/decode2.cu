@@ -720,13 +720,15 @@ __global__ void __maxnreg__(128) mv_kernel(const __grid_constant__ MvArgs a)
 // Every warp owns the tasks [start(w), start(w + 1)) of the CTA's range,
 // start(w) = j0 + floor(w L / W): consecutive blocks of the same row tile, so
 // a warp sums a tile's blocks in registers and finishes it alone unless its
-// range ends inside the tile. A tile shared by warps wa..wb is finished by the
-// last of them to arrive, which adds the warps' partial rows in warp order
-// (a fixed order, so the result does not depend on timing).
+// range begins or ends inside the tile. A tile shared by warps wa..wb is
+// finished by the last of them to arrive, which adds the warps' partial rows
+// in warp order (a fixed order: the result does not depend on timing).
 //
 // Copies: each warp keeps nslot - 1 tasks in flight in its own ring; the
 // first nslot - 1 are issued before the wait for the preceding kernel (the
-// weights never depend on it), so they stream while x is staged.
+// weights never depend on it), so they stream while x is staged. Task
+// cursors advance incrementally and every lane's copy offsets come from a
+// table built once per CTA, so the loop has no divisions.
 
 struct __align__(16) M4Hdr {
     double dred[kM4Warps];
@@ -734,12 +736,13 @@ struct __align__(16) M4Hdr {
     float amax[kM4Warps];
     uint32_t aidx[kM4Warps];
     uint32_t cnt[kM4Warps];     // arrivals at a shared tile, indexed by its first warp
+    uint32_t wstart[kM4Warps];  // first task of each warp
+    uint2 cp[8][32];            // per (copy i, lane): source offset in the block's rows, slot offset
 };
 // partial rows of shared tiles: [warp][first / last tile][segment][16]
 constexpr uint32_t kM4PartBytes = kM4Warps * 2u * 2u * 16u * 4u;
 
 __host__ __device__ constexpr uint32_t m4_hdr_bytes() { return align128((uint32_t)sizeof(M4Hdr)); }
-__host__ __device__ constexpr uint32_t m4_slot_bytes(uint32_t type) { return 16u * (type == 12u ? kM4Q4Row : kM4Q6Row); }
 __host__ __device__ constexpr uint32_t m4_smem_bytes(uint32_t cols, uint32_t nslot, uint32_t slot_bytes)
 {
     return m4_hdr_bytes() + kM4PartBytes + mv_x_bytes(cols) + (uint32_t)kM4Warps * nslot * slot_bytes;
@@ -756,59 +759,70 @@ __device__ __forceinline__ void m4_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Task j of the launch: row tile t, segment s, block column b.
-struct M4Task {
-    uint32_t t, s, b;
-};
-__device__ __forceinline__ M4Task m4_task(const MvArgs &a, uint32_t seg, uint32_t j)
-{
-    if (!a.paired) return M4Task{j / a.nb, seg, j % a.nb};
-    const uint32_t tp = 2u * a.nb, r = j % tp;
-    return M4Task{j / tp, r / a.nb, r % a.nb};
-}
-
-// First task of warp w (w = Weff gives the range's end).
+// First task of warp w of weff (w = weff gives the range's end).
+// (32-bit arithmetic: a CTA holds far fewer than 2^27 tasks.)
 __device__ __forceinline__ uint32_t m4_start(uint32_t j0, uint32_t L, uint32_t weff, uint32_t w)
 {
-    return j0 + (uint32_t)((uint64_t)w * L / weff);
+    return j0 + w * L / weff;
 }
 // The warp whose range holds task j.
 __device__ __forceinline__ uint32_t m4_warp_of(uint32_t j0, uint32_t L, uint32_t weff, uint32_t j)
 {
-    return (uint32_t)(((uint64_t)(j - j0 + 1u) * weff + L - 1u) / L) - 1u;
+    return ((j - j0 + 1u) * weff + L - 1u) / L - 1u;
 }
 
-// Issue the copies of one task (16 rows x one block) into a slot.
-__device__ __forceinline__ void m4_issue(const MvArgs &a, uint32_t seg, uint32_t j, uint32_t slot, uint32_t lane,
-                                         uint64_t policy)
+// Task cursor: row tile t, segment s (0 / 1 of a pair), block column b.
+struct M4Cur {
+    uint32_t t, s, b;
+};
+__device__ __forceinline__ void m4_next(M4Cur &c, uint32_t nb, bool paired)
 {
-    const M4Task k = m4_task(a, seg, j);
-    const MvSeg &sg = a.seg[k.s];
-    if (sg.type == 12u) {
-        const uint8_t *base = sg.w + (uint64_t)(16u * k.t) * sg.row_bytes + (uint64_t)k.b * 144u;
-#pragma unroll
-        for (uint32_t i = 0; i < 5u; ++i) {
-            const uint32_t idx = lane + 32u * i;   // 16 rows x 9 chunks of 16 bytes
-            if (idx < 144u) {
-                const uint32_t r = idx / 9u, p = idx - 9u * r;
-                cp_async16(slot + r * kM4Q4Row + 16u * p, base + (uint64_t)r * sg.row_bytes + 16u * p, policy);
-            }
-        }
-    } else {
-        const uint8_t *base = sg.w + (uint64_t)(16u * k.t) * sg.row_bytes + (uint64_t)k.b * 210u;
-        const uint32_t p = lane & 15u;
-#pragma unroll
-        for (uint32_t i = 0; i < 8u; ++i) {
-            const uint32_t r = 2u * i + (lane >> 4);
-            const uint8_t *row = base + (uint64_t)r * sg.row_bytes;
-            const uint8_t *win = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(row) & ~uintptr_t(15));
-            cp_async16(slot + r * kM4Q6Row + 16u * p, win + 16u * p, policy);
+    if (++c.b == nb) {
+        c.b = 0u;
+        if (paired && c.s == 0u) {
+            c.s = 1u;
+        } else {
+            c.s = 0u;
+            ++c.t;
         }
     }
 }
 
-// Rows lane / 4 and lane / 4 + 8 of a finished tile's partial sums (this
-// lane's share) -> lane i < 16 holds row i, summed over the 4 lanes of a row.
+// The CTA's operands of one kind: all its tasks share the type and row length.
+struct M4Seg {
+    const uint8_t *w0, *w1;     // segment (pair: gate, up) row 0
+    uint32_t rb, bb, q4;        // row bytes, block bytes, Q4_K?
+    uint32_t ncp;               // copies per lane per task
+};
+
+__device__ __forceinline__ const uint8_t *m4_block(const M4Seg &g, const M4Cur &c)
+{
+    return (c.s ? g.w1 : g.w0) + (uint64_t)(16u * c.t) * g.rb + c.b * g.bb;
+}
+
+// Issue the copies of one task (16 rows x one block) into a slot: Q4_K 144
+// chunks (5 per lane, the last by lanes 0-15), Q6_K 224 (7 per lane).
+template <bool Q4>
+__device__ __forceinline__ void m4_issue(const M4Seg &g, const M4Hdr *h, const M4Cur &c, uint32_t slot, uint32_t lane,
+                                         uint64_t policy)
+{
+    const uint8_t *base = m4_block(g, c);
+#pragma unroll
+    for (uint32_t i = 0; i < (Q4 ? 5u : 7u); ++i) {
+        const uint2 e = h->cp[i][lane];
+        if (Q4) {
+            if (i < 4u || lane < 16u) cp_async16(slot + e.y, base + e.x, policy);
+        } else {
+            // the 16-byte boundary at or below the row's block, plus chunk e.y % kM4Q6Row
+            const uint8_t *win =
+                reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(base + e.x) & ~uintptr_t(15));
+            cp_async16(slot + e.y, win + e.y % kM4Q6Row, policy);
+        }
+    }
+}
+
+// Rows g and g + 8 of a tile's partial sums (this lane's share, summed over
+// the 4 lanes of a row) -> lane i < 16 holds row i.
 __device__ __forceinline__ float m4_rows(float v0, float v1, uint32_t lane)
 {
     v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
@@ -820,27 +834,23 @@ __device__ __forceinline__ float m4_rows(float v0, float v1, uint32_t lane)
     return (lane & 8u) ? a1 : a0;
 }
 
-// Finish tile t after this warp's last task in it: alone (registers), or as
-// one of the warps wa..wb sharing it (partials in shared memory, the last to
+// Finish tile t after this warp's last task in it: alone (wa == wb), or as
+// one of the warps wa..wb sharing it (partials in shared memory; the last to
 // arrive adds them in warp order).
-__device__ __forceinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, const MvCta &c, uint32_t L,
-                                         uint32_t weff, uint32_t my0, uint32_t t, const float (&acc)[2][2],
-                                         float out_scale, MvBest &best)
+__device__ __noinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, uint32_t seg, uint32_t t, uint32_t tj0,
+                                      uint32_t wa, uint32_t wb, uint32_t my0, float a00, float a01, float a10,
+                                      float a11, float out_scale, MvBest &best)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t P = a.paired ? 2u : 1u, TP = a.nb * P;
-    const uint32_t tj0 = t * TP;
-    const uint32_t wa = m4_warp_of(c.j0, L, weff, tj0), wb = m4_warp_of(c.j0, L, weff, tj0 + TP - 1u);
-    float r[2];
-    r[0] = m4_rows(acc[0][0], acc[0][1], lane);
-    r[1] = P == 2u ? m4_rows(acc[1][0], acc[1][1], lane) : 0.f;
+    float r0 = m4_rows(a00, a01, lane);
+    float r1 = a.paired ? m4_rows(a10, a11, lane) : 0.f;
     if (wa != wb) {
         // slot 0: the tile where this warp's range starts; slot 1: where it ends
         const uint32_t which = my0 >= tj0 ? 0u : 1u;
         float *pp = part + (warp * 2u + which) * 32u;
         if (lane < 16u) {
-            pp[lane] = r[0];
-            pp[16u + lane] = r[1];
+            pp[lane] = r0;
+            pp[16u + lane] = r1;
         }
         __syncwarp();
         uint32_t last = 0;
@@ -851,84 +861,180 @@ __device__ __forceinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part,
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) return;
         __threadfence_block();
-        r[0] = r[1] = 0.f;
+        r0 = r1 = 0.f;
         const uint32_t i = lane & 15u;
         for (uint32_t w = wa; w <= wb; ++w) {
-            const uint32_t ww = (w > wa || m4_start(c.j0, L, weff, wa) >= tj0) ? 0u : 1u;
+            const uint32_t ww = (w > wa || h->wstart[wa] >= tj0) ? 0u : 1u;
             const volatile float *q = part + (w * 2u + ww) * 32u;
-            r[0] += q[i];
-            r[1] += q[16u + i];
+            r0 += q[i];
+            r1 += q[16u + i];
         }
     }
-    const float pre = mv_pre(a, c.seg, t, lane);
-    if (lane < 16u) mv_finish(a, c.seg, t, r[0] * out_scale, r[1] * out_scale, pre, lane, best);
+    const float pre = mv_pre(a, seg, t, lane);
+    if (lane < 16u) mv_finish(a, seg, t, r0 * out_scale, r1 * out_scale, pre, lane, best);
 }
 
-template <int NS>
+// 16 bytes at a 2-byte-aligned shared-memory address, as four words: five
+// aligned loads and a funnel shift by the misalignment (0 or 16 bits).
+__device__ __forceinline__ void ld16_u2(const uint8_t *p, uint32_t (&w)[4])
+{
+    const uintptr_t ad = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(ad & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(ad & 3u) * 8u;
+    uint32_t v[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = q[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
+}
+
+// One Q6_K task (16 rows x 256 elements) for lane (g, t): rows g (r0) and
+// g + 8 (r1), block starts in shared memory (2-byte aligned). Four MMAs
+// cover four 16-element scale groups at once: the four lanes t of a row
+// group supply the k slots of group (h, k = t, l16) - 4 elements each, word m
+// of the group's 16 quant bytes - and B holds x only in the column pair of
+// the group that lane's k slots carry (B lane t' is nonzero in columns
+// 2t', 2t' + 1), so accumulator columns 2t, 2t + 1 of lane t end as the
+// sums (hi, lo) of its own group, ready for that group's scale. A 6-bit quant
+// q, zero-extended into a 16-bit lane, is the fp16 subnormal q 2^-24
+// exactly; the -32 offset is applied through the group's sum of x
+// (dequant_q6_k, src/brain_runtime.c:1049-1083).
+__device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, const uint8_t *xb, const float *xs,
+                                          uint32_t lane, float &o0, float &o1)
+{
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const uint32_t podd = (g & 1u) * 8u;
+    const bool bmine = (g >> 1) == t;
+    const uint32_t ns = 4u * (t >> 1), rot = (4u - 2u * t) & 31u;   // low / high nibbles; qh bits 2t -> 4
+    const float d0 = h2f((uint16_t)ld_u16(r0 + 208)), d1 = h2f((uint16_t)ld_u16(r1 + 208));
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (uint32_t h = 0; h < 2u; ++h) {
+#pragma unroll
+        for (uint32_t l16 = 0; l16 < 2u; ++l16) {
+            const uint32_t oq = 64u * h + 32u * (t & 1u) + 16u * l16, oh = 128u + 32u * h + 16u * l16;
+            uint32_t q0[4], h0[4], q1[4], h1[4];
+            ld16_u2(r0 + oq, q0);
+            ld16_u2(r0 + oh, h0);
+            ld16_u2(r1 + oq, q1);
+            ld16_u2(r1 + oh, h1);
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (uint32_t m = 0; m < 4u; ++m) {
+                const uint32_t v0 = ((q0[m] >> ns) & 0x0f0f0f0fu) | (__funnelshift_l(h0[m], h0[m], rot) & 0x30303030u);
+                const uint32_t v1 = ((q1[m] >> ns) & 0x0f0f0f0fu) | (__funnelshift_l(h1[m], h1[m], rot) & 0x30303030u);
+                uint2 b = make_uint2(0u, 0u);
+                if (bmine) b = *reinterpret_cast<const uint2 *>(xb + (32u * h + 8u * t + 4u * l16 + m) * 16u + podd);
+                if (m == 0u) {
+                    mma16816(c, sub2(v0, 0x4140), sub2(v1, 0x4140), sub2(v0, 0x4342), sub2(v1, 0x4342), b, zero);
+                } else {
+                    const float cc[4] = {c[0], c[1], c[2], c[3]};
+                    mma16816(c, sub2(v0, 0x4140), sub2(v1, 0x4140), sub2(v0, 0x4342), sub2(v1, 0x4342), b, cc);
+                }
+            }
+            const uint32_t G = 8u * h + 2u * t + l16;
+            const float sx = 32.0f * xs[G];
+            const float s0 = d0 * (float)(int8_t)r0[192u + G], s1 = d1 * (float)(int8_t)r1[192u + G];
+            o0 += s0 * ((c[0] + c[1]) * kTwo24 - sx);
+            o1 += s1 * ((c[2] + c[3]) * kTwo24 - sx);
+        }
+    }
+}
+
+template <int NS, bool Q4>
 __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xarea, uint8_t *ring, const MvCta &c,
                            MvBest &best)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t g = lane >> 2, t4 = lane & 3u;
+    const uint32_t g = lane >> 2;
     const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)kM4Warps, L);
     const bool active = warp < weff;
-    const uint32_t my0 = active ? m4_start(c.j0, L, weff, warp) : 0u;
-    const uint32_t my1 = active ? m4_start(c.j0, L, weff, warp + 1u) : 0u;
+    const bool paired = a.paired != 0u;
+    const uint32_t nb = a.nb, TP = nb * (paired ? 2u : 1u);
+    const uint32_t my0 = active ? h->wstart[warp] : 0u;
+    const uint32_t my1 = active ? (warp + 1u < weff ? h->wstart[warp + 1u] : c.j1) : 0u;
     const uint32_t n = my1 - my0;
+    M4Seg sg;
+    {
+        const MvSeg &s0 = a.seg[c.seg];
+        sg.w0 = s0.w;
+        sg.w1 = paired ? a.seg[1].w : s0.w;
+        sg.rb = (uint32_t)s0.row_bytes;
+        sg.q4 = Q4 ? 1u : 0u;
+        sg.bb = Q4 ? 144u : 210u;
+        sg.ncp = Q4 ? 5u : 7u;
+    }
+    M4Cur ci{}, cc{};
+    uint32_t first_tile = 0, last_tile = 0;
+    if (active) {
+        first_tile = my0 / TP;
+        last_tile = (my1 - 1u) / TP;
+        const uint32_t r = my0 - first_tile * TP;
+        ci.t = first_tile;
+        ci.s = paired && r >= nb ? 1u : 0u;
+        ci.b = r - ci.s * nb;
+        cc = ci;
+    }
     const uint64_t policy = policy_evict_first();
     const uint32_t ring_w = smem_addr(ring) + warp * (uint32_t)NS * a.slot_bytes;
     // prologue: the first NS - 1 tasks, before the wait for the preceding kernel
 #pragma unroll
     for (uint32_t k = 0; k + 1u < (uint32_t)NS; ++k) {
-        if (k < n) m4_issue(a, c.seg, my0 + k, ring_w + k * a.slot_bytes, lane, policy);
+        if (k < n) {
+            m4_issue<Q4>(sg, h, ci, ring_w + k * a.slot_bytes, lane, policy);
+            m4_next(ci, nb, paired);
+        }
         m4_commit();
     }
-    const float out_scale = mv_stage_x<kM4Warps>(a, h->dred, h->fred, xarea, a.seg[c.seg].type == 12u);
+    const float out_scale = mv_stage_x<kM4Warps>(a, h->dred, h->fred, xarea, Q4);
     if (!active) return;
+    // sharing of the first and last tiles with neighbouring warps
+    const uint32_t fa = m4_warp_of(c.j0, L, weff, first_tile * TP), fb = m4_warp_of(c.j0, L, weff, first_tile * TP + TP - 1u);
+    const uint32_t la = m4_warp_of(c.j0, L, weff, last_tile * TP), lb = m4_warp_of(c.j0, L, weff, last_tile * TP + TP - 1u);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
     const uint8_t *ringp = ring + (size_t)warp * NS * a.slot_bytes;
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    uint32_t cur = m4_task(a, c.seg, my0).t;
+    const uint32_t wlow = (uint32_t)reinterpret_cast<uintptr_t>(sg.w0), wlow1 = (uint32_t)reinterpret_cast<uintptr_t>(sg.w1);
+    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+    uint32_t si = 0, sn = (uint32_t)NS - 1u;   // slots of the consumed and of the next issued task
     for (uint32_t k = 0; k < n; ++k) {
-        {
-            const uint32_t kn = k + (uint32_t)NS - 1u;
-            if (kn < n) m4_issue(a, c.seg, my0 + kn, ring_w + (kn % (uint32_t)NS) * a.slot_bytes, lane, policy);
-            m4_commit();
+        if (k + (uint32_t)NS - 1u < n) {
+            m4_issue<Q4>(sg, h, ci, ring_w + sn * a.slot_bytes, lane, policy);
+            m4_next(ci, nb, paired);
         }
-        const M4Task tk = m4_task(a, c.seg, my0 + k);
-        if (tk.t != cur) {
-            m4_flush(a, h, part, c, L, weff, my0, cur, acc, out_scale, best);
-            acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
-            cur = tk.t;
-        }
+        m4_commit();
+        if (++sn == (uint32_t)NS) sn = 0u;
         cp_async_wait<NS - 1>();
         __syncwarp();
-        const uint8_t *slot = ringp + (size_t)(k % (uint32_t)NS) * a.slot_bytes;
-        const uint8_t *xb = xarea + (size_t)tk.b * 1024u;
-        const float *xs = xs16 + (size_t)tk.b * 16u;
-        const MvSeg &sg = a.seg[tk.s];
+        const uint8_t *slot = ringp + si * a.slot_bytes;
+        if (++si == (uint32_t)NS) si = 0u;
+        const uint8_t *xb = xarea + cc.b * 1024u;
+        const float *xs = xs16 + cc.b * 16u;
         float o0 = 0.f, o1 = 0.f;
-        if (sg.type == 12u) {
+        if (Q4) {
             q4k_task(slot, 0u, 0u, kM4Q4Row, xb, xs, lane, o0, o1);
         } else {
-            const uintptr_t rb = reinterpret_cast<uintptr_t>(sg.w) + (uint64_t)(16u * tk.t) * sg.row_bytes +
-                                 (uint64_t)tk.b * 210u;
-            const uint8_t *r0[1] = {slot + g * kM4Q6Row + (uint32_t)((rb + (uint64_t)g * sg.row_bytes) & 15u)};
-            const uint8_t *r1[1] = {slot + (g + 8u) * kM4Q6Row +
-                                    (uint32_t)((rb + (uint64_t)(g + 8u) * sg.row_bytes) & 15u)};
-            const uint8_t *xbs[1] = {xb};
-            const float *xss[1] = {xs};
-            float p0[1] = {0.f}, p1[1] = {0.f};
-            q6k_tiles<1, true>(r0, r1, xbs, xss, (int)g, (int)t4, p0, p1);
-            o0 = p0[0];
-            o1 = p1[0];
+            // the block's offset inside its 16-byte-aligned window, per row
+            const uint32_t lb0 = (cc.s ? wlow1 : wlow) + 16u * cc.t * sg.rb + cc.b * 210u;
+            q6k_task4(slot + g * kM4Q6Row + ((lb0 + g * sg.rb) & 15u),
+                      slot + (g + 8u) * kM4Q6Row + ((lb0 + (g + 8u) * sg.rb) & 15u), xb, xs, lane, o0, o1);
         }
         __syncwarp();   // the slot is re-filled by a later iteration's copies
-        const uint32_t si = (a.paired && tk.s) ? 1u : 0u;
-        acc[si][0] += o0;
-        acc[si][1] += o1;
+        if (cc.s) {
+            a10 += o0;
+            a11 += o1;
+        } else {
+            a00 += o0;
+            a01 += o1;
+        }
+        const uint32_t t = cc.t;
+        m4_next(cc, nb, paired);
+        if (cc.t != t || k + 1u == n) {
+            const uint32_t wa = t == first_tile ? fa : (t == last_tile ? la : warp);
+            const uint32_t wb = t == first_tile ? fb : (t == last_tile ? lb : warp);
+            m4_flush(a, h, part, c.seg, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
+            a00 = a01 = a10 = a11 = 0.f;
+        }
     }
-    m4_flush(a, h, part, c, L, weff, my0, cur, acc, out_scale, best);
 }
 
 template <int NS>
@@ -940,11 +1046,35 @@ __global__ void __launch_bounds__(kM4Threads, 1) mv4_kernel(const __grid_constan
     uint8_t *xarea = smem + m4_hdr_bytes() + kM4PartBytes;
     uint8_t *ring = xarea + mv_x_bytes(a.cols);
     const MvCta c = a.cta[blockIdx.x];
-    if (threadIdx.x < (uint32_t)kM4Warps) h->cnt[threadIdx.x] = 0u;
+    {
+        const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)kM4Warps, L);
+        if (threadIdx.x < (uint32_t)kM4Warps) {
+            h->cnt[threadIdx.x] = 0u;
+            h->wstart[threadIdx.x] = threadIdx.x < weff ? m4_start(c.j0, L, weff, threadIdx.x) : 0xffffffffu;
+        }
+        // copy table: Q4_K 16 rows x 9 chunks of 16 bytes (5 per lane); Q6_K
+        // 16 rows x 14 chunks (a 224-byte window holds the 210-byte block at
+        // any 2-byte offset), 7 per lane
+        const bool q4 = a.seg[c.seg].type == 12u;
+        const uint32_t rb = (uint32_t)a.seg[c.seg].row_bytes;
+        for (uint32_t e = threadIdx.x; e < 8u * 32u; e += blockDim.x) {
+            const uint32_t i = e >> 5, l = e & 31u, idx = l + 32u * i;
+            uint2 v = make_uint2(0u, 0xffffffffu);
+            if (q4 && idx < 144u) {
+                const uint32_t r = idx / 9u, p = idx - 9u * r;
+                v = make_uint2(r * rb + 16u * p, r * kM4Q4Row + 16u * p);
+            } else if (!q4 && idx < 224u) {
+                const uint32_t r = idx / 14u, p = idx - 14u * r;
+                v = make_uint2(r * rb, r * kM4Q6Row + 16u * p);
+            }
+            h->cp[i][l] = v;
+        }
+    }
     __syncthreads();
     pdl_launch();
     MvBest best{-FLT_MAX, 0xffffffffu};
-    m4_consume<NS>(a, h, part, xarea, ring, c, best);
+    if (a.seg[c.seg].type == 12u) m4_consume<NS, true>(a, h, part, xarea, ring, c, best);
+    else m4_consume<NS, false>(a, h, part, xarea, ring, c, best);
     cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
     if (a.epi == MV_PART) {
         __threadfence_system();

@@ -154,14 +154,14 @@ struct MvArgs {
 // producer warp: 16 warps, each with a contiguous range of the CTA's tasks
 // and its own ring of nslot task slots filled by cp.async (16-byte copies
 // issued by its own lanes). A slot holds the 16 rows of one task: Q4_K rows
-// 144 bytes apart (the block itself), Q6_K rows as 256-byte windows from the
-// 16-byte boundary below the block, kM4Q6Row apart (the window rounds the
-// 2-byte-aligned block down; rows of a window land in distinct banks).
+// 144 bytes apart (the block itself), Q6_K rows as 224-byte windows from the
+// 16-byte boundary at or below the block (the 2-byte-aligned 210-byte block
+// lies inside at any offset), kM4Q6Row apart (rows in distinct banks).
 constexpr int kM4Warps = 16;
 constexpr int kM4Threads = kM4Warps * 32;
-constexpr uint32_t kM4Q4Row = 144u, kM4Q6Row = 272u;
+constexpr uint32_t kM4Q4Row = 144u, kM4Q6Row = 240u;
 constexpr uint32_t kM4MaxSlots = 6u;
-// bytes past the end of a Q6_K tensor that a 256-byte window may read
+// bytes past the end of a Q6_K tensor that a 224-byte window may read (14), rounded up
 constexpr uint32_t kM4Q6Overread = 48u;
 
 // ------------------------------------------------------ attention kernel ----

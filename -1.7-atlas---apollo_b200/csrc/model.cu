@@ -531,7 +531,7 @@ constexpr uint32_t kHalfSmBytes = 115712;
 
 // Decode GEMV kernel of the graph step: 1 = mv4_kernel (per-warp rings),
 // 0 = mv_kernel (producer warp and a ring shared by the CTA).
-constexpr uint32_t kMvEngine = 0u;
+constexpr uint32_t kMvEngine = 1u;
 
 struct MvPlan {
     d2::MvArgs a{};
