@@ -227,6 +227,15 @@ __device__ __forceinline__ float h2f(uint16_t bits)
     return __half2float(__ushort_as_half(bits));
 }
 
+// Small integers to float without the conversion unit: 2^23 + v read as a
+// float is exact for v < 2^23, and subtracting 2^23 leaves v exactly.
+__device__ __forceinline__ float u2f_small(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+// The int8 in the low byte of `byte`: offset to 0..255 by flipping the sign bit.
+__device__ __forceinline__ float s8f(uint32_t byte)
+{
+    return __uint_as_float(0x4B000000u | ((byte ^ 0x80u) & 0xffu)) - 8388736.0f;
+}
+
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll

@@ -324,34 +324,43 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     if (lane == 0) { fred[warp] = mx; dred[warp] = ss; }
     asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
-    float m = 0.f;
-    double t = 0.0;
+    // warp 0 reduces the warps' partials and derives the two scalars once
+    if (warp == 0) {
+        float m = lane < (uint32_t)W ? fred[lane] : 0.f;
+        double t = lane < (uint32_t)W ? dred[lane] : 0.0;
 #pragma unroll
-    for (int w = 0; w < W; ++w) { m = fmaxf(m, fred[w]); t += dred[w]; }
-    // exponent capped at 126: rows of tiny values (a SwiGLU output of
-    // all-negative gates) keep a finite scale and contribute ~0, as in fp32
-    const float s = (m > 0.f && isfinite(m)) ? exp2f((float)min(13 - ilogbf(m), 126)) : 1.0f;
-    const float inv_rms = norm ? 1.0f / sqrtf((float)(t / (double)a.cols) + a.eps) : 1.0f;
+        for (int o = 16; o > 0; o >>= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (norm) t += __shfl_xor_sync(0xffffffffu, t, o);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            // exponent capped at 126: rows of tiny values (a SwiGLU output of
+            // all-negative gates) keep a finite scale and contribute ~0, as in fp32
+            fred[0] = (m > 0.f && isfinite(m)) ? exp2f((float)min(13 - ilogbf(m), 126)) : 1.0f;
+            fred[1] = norm ? 1.0f / sqrtf((float)(t / (double)a.cols) + a.eps) : 1.0f;
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
+    const float s = fred[0], inv_rms = fred[1];
     float *xs16 = reinterpret_cast<float *>(xarea + (size_t)a.cols * 4u);
     // n4 is a multiple of 4 (cols % 256 == 0) and the stride of 256 keeps the
     // four groups of a 16-element sum in lanes 4k..4k+3 of one warp
     for (uint32_t i = threadIdx.x; i < n4; i += kStride) {
         const float4 v = xf[i];
-        const float e[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
-        __half hi[4], lo[4];
-        float sum = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            hi[q] = __float2half_rn(e[q]);
-            lo[q] = __float2half_rn(e[q] - __half2float(hi[q]));
-            sum += e[q];
-        }
+        const float e0 = v.x * s, e1 = v.y * s, e2 = v.z * s, e3 = v.w * s;
+        float sum = e0 + e1 + e2 + e3;
+        // hi = fp16(e), lo = fp16(e - hi), two per conversion; Q4_K CTAs keep
+        // the order (x0, x2, x1, x3) of the quant words' nibble pairs
+        const float a0 = e0, a1 = q4_order ? e2 : e1, a2 = q4_order ? e1 : e2, a3 = e3;
+        const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        const __half2 l01 = __floats2half2_rn(a0 - f01.x, a1 - f01.y), l23 = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
         uint4 pk;
-        const int e1 = q4_order ? 2 : 1, e2 = q4_order ? 1 : 2;
-        pk.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[e1]) << 16);
-        pk.y = (uint32_t)__half_as_ushort(hi[e2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
-        pk.z = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[e1]) << 16);
-        pk.w = (uint32_t)__half_as_ushort(lo[e2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+        pk.x = *reinterpret_cast<const uint32_t *>(&h01);
+        pk.y = *reinterpret_cast<const uint32_t *>(&h23);
+        pk.z = *reinterpret_cast<const uint32_t *>(&l01);
+        pk.w = *reinterpret_cast<const uint32_t *>(&l23);
         reinterpret_cast<uint4 *>(xarea)[i] = pk;   // in place: group i is only touched by this thread
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
@@ -506,10 +515,10 @@ __device__ __forceinline__ void q4k_task(const uint8_t *blk, uint32_t lc, uint32
         const float d = h2f((uint16_t)(hd.x & 0xffffu)), dm = h2f((uint16_t)(hd.x >> 16));
         const uint32_t sh = 8u * t;
         const uint32_t y = (hd.y >> sh) & 255u, z = (hd.z >> sh) & 255u, w = (hd.w >> sh) & 255u;
-        dsc[r][0] = d * (float)(y & 63u);                        // sub-block j = t
-        dmn[r][0] = dm * (float)(z & 63u);
-        dsc[r][1] = d * (float)((w & 15u) | ((y >> 6) << 4));    // j = t + 4
-        dmn[r][1] = dm * (float)((w >> 4) | ((z >> 6) << 4));
+        dsc[r][0] = d * u2f_small(y & 63u);                        // sub-block j = t
+        dmn[r][0] = dm * u2f_small(z & 63u);
+        dsc[r][1] = d * u2f_small((w & 15u) | ((y >> 6) << 4));    // j = t + 4
+        dmn[r][1] = dm * u2f_small((w >> 4) | ((z >> 6) << 4));
     }
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t podd = (g & 1u) * 8u;
@@ -934,7 +943,7 @@ __device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, 
             }
             const uint32_t G = 8u * h + 2u * t + l16;
             const float sx = 32.0f * xs[G];
-            const float s0 = d0 * (float)(int8_t)r0[192u + G], s1 = d1 * (float)(int8_t)r1[192u + G];
+            const float s0 = d0 * s8f(r0[192u + G]), s1 = d1 * s8f(r1[192u + G]);
             o0 += s0 * ((c[0] + c[1]) * kTwo24 - sx);
             o1 += s1 * ((c[2] + c[3]) * kTwo24 - sx);
         }

@@ -66,10 +66,10 @@ __device__ __forceinline__ void q4k_tiles(const uint8_t *const (&r0)[NT], const 
             const float d = h2f((uint16_t)(hd.x & 0xffffu)), dm = h2f((uint16_t)(hd.x >> 16));
             const uint32_t sh = 8u * (uint32_t)t;
             const uint32_t y = (hd.y >> sh) & 255u, z = (hd.z >> sh) & 255u, w = (hd.w >> sh) & 255u;
-            dsc[n][r][0] = d * (float)(y & 63u);                        // j = t
-            dmn[n][r][0] = dm * (float)(z & 63u);
-            dsc[n][r][1] = d * (float)((w & 15u) | ((y >> 6) << 4));    // j = t + 4
-            dmn[n][r][1] = dm * (float)((w >> 4) | ((z >> 6) << 4));
+            dsc[n][r][0] = d * u2f_small(y & 63u);                        // j = t
+            dmn[n][r][0] = dm * u2f_small(z & 63u);
+            dsc[n][r][1] = d * u2f_small((w & 15u) | ((y >> 6) << 4));    // j = t + 4
+            dmn[n][r][1] = dm * u2f_small((w >> 4) | ((z >> 6) << 4));
         }
     }
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
@@ -146,8 +146,8 @@ __device__ __forceinline__ void q6k_tiles(const uint8_t *const (&r0)[NT], const 
                 Q0[n] = h0 ? ld32u(r0[n] + oq) : 0u;
                 A1[n] = h1 ? ld32u(r1[n] + oa) : 0u; B1[n] = h1 ? ld32u(r1[n] + ob) : 0u;
                 Q1[n] = h1 ? ld32u(r1[n] + oq) : 0u;
-                s0[n] = h0 ? d0[n] * (float)(int8_t)r0[n][si] : 0.f;
-                s1[n] = h1 ? d1[n] * (float)(int8_t)r1[n][si] : 0.f;
+                s0[n] = h0 ? d0[n] * s8f(r0[n][si]) : 0.f;
+                s1[n] = h1 ? d1[n] * s8f(r1[n][si]) : 0.f;
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
