@@ -39,6 +39,26 @@ namespace d2 {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Loads the step's trace pointer (lane 0 of each warp, early, so that the
+// load is long done when the warp records its stamps at the end).
+__device__ __forceinline__ uint64_t *trace_ptr(const DecState *st)
+{
+    if (!st || (threadIdx.x & 31u)) return nullptr;
+    return *reinterpret_cast<uint64_t *const volatile *>(&st->trace);
+}
+// Warp w's stamps into launch `slot`'s record of this CTA (lane 0 only).
+__device__ __forceinline__ void trace_done(uint64_t *tr, uint32_t slot, uint64_t t_start, uint64_t t_ready)
+{
+    if (!tr || blockIdx.x >= kTraceCtas) return;
+    const uint32_t warp = threadIdx.x >> 5;
+    uint64_t *rec = tr + ((size_t)slot * kTraceCtas + blockIdx.x) * kTraceWords;
+    if (warp == 0) {
+        rec[0] = t_start;
+        rec[1] = t_ready;
+    }
+    if (warp + 2u < kTraceWords) rec[2 + warp] = global_ns();
+}
+
 // consumer warps only (the producer warp never joins)
 __device__ __forceinline__ void mv_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kMvWarps * 32) : "memory"); }
 
@@ -752,12 +772,13 @@ struct __align__(16) M4Hdr {
 constexpr uint32_t kM4PartBytes = kM4Warps * 2u * 2u * 16u * 4u;
 
 __host__ __device__ constexpr uint32_t m4_hdr_bytes() { return align128((uint32_t)sizeof(M4Hdr)); }
-__host__ __device__ constexpr uint32_t m4_smem_bytes(uint32_t cols, uint32_t nslot, uint32_t slot_bytes)
+__host__ __device__ constexpr uint32_t m4_smem_bytes(uint32_t cols, uint32_t warps, uint32_t nslot, uint32_t slot_bytes)
 {
-    return m4_hdr_bytes() + kM4PartBytes + mv_x_bytes(cols) + (uint32_t)kM4Warps * nslot * slot_bytes;
+    return m4_hdr_bytes() + kM4PartBytes + mv_x_bytes(cols) + warps * nslot * slot_bytes;
 }
 
-__device__ __forceinline__ void m4_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kM4Threads) : "memory"); }
+template <int W>
+__device__ __forceinline__ void m4_sync() { asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory"); }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint64_t policy)
 {
@@ -950,13 +971,13 @@ __device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, 
     }
 }
 
-template <int NS, bool Q4>
+template <int NS, bool Q4, int W>
 __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xarea, uint8_t *ring, const MvCta &c,
-                           MvBest &best)
+                           MvBest &best, uint64_t &t_ready)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 2;
-    const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)kM4Warps, L);
+    const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)W, L);
     const bool active = warp < weff;
     const bool paired = a.paired != 0u;
     const uint32_t nb = a.nb, TP = nb * (paired ? 2u : 1u);
@@ -995,7 +1016,8 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         }
         m4_commit();
     }
-    const float out_scale = mv_stage_x<kM4Warps>(a, h->dred, h->fred, xarea, Q4);
+    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4);
+    t_ready = global_ns();
     if (!active) return;
     // sharing of the first and last tiles with neighbouring warps
     const uint32_t fa = m4_warp_of(c.j0, L, weff, first_tile * TP), fb = m4_warp_of(c.j0, L, weff, first_tile * TP + TP - 1u);
@@ -1046,18 +1068,24 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
     }
 }
 
-template <int NS>
-__global__ void __launch_bounds__(kM4Threads, 1) mv4_kernel(const __grid_constant__ MvArgs a)
+// W = 16: one CTA per SM; W = 8: two CTAs fit on an SM (registers), so that
+// the next launch's CTAs become resident, and stream their first weights,
+// while this launch still runs.
+template <int NS, int W>
+__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __grid_constant__ MvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     M4Hdr *h = reinterpret_cast<M4Hdr *>(smem);
     float *part = reinterpret_cast<float *>(smem + m4_hdr_bytes());
     uint8_t *xarea = smem + m4_hdr_bytes() + kM4PartBytes;
     uint8_t *ring = xarea + mv_x_bytes(a.cols);
+    const uint64_t t_start = global_ns();
+    uint64_t *const tr = trace_ptr(a.dstate);
+    uint64_t t_ready = 0;
     const MvCta c = a.cta[blockIdx.x];
     {
-        const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)kM4Warps, L);
-        if (threadIdx.x < (uint32_t)kM4Warps) {
+        const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)W, L);
+        if (threadIdx.x < (uint32_t)W) {
             h->cnt[threadIdx.x] = 0u;
             h->wstart[threadIdx.x] = threadIdx.x < weff ? m4_start(c.j0, L, weff, threadIdx.x) : 0xffffffffu;
         }
@@ -1082,12 +1110,13 @@ __global__ void __launch_bounds__(kM4Threads, 1) mv4_kernel(const __grid_constan
     __syncthreads();
     pdl_launch();
     MvBest best{-FLT_MAX, 0xffffffffu};
-    if (a.seg[c.seg].type == 12u) m4_consume<NS, true>(a, h, part, xarea, ring, c, best);
-    else m4_consume<NS, false>(a, h, part, xarea, ring, c, best);
+    if (a.seg[c.seg].type == 12u) m4_consume<NS, true, W>(a, h, part, xarea, ring, c, best, t_ready);
+    else m4_consume<NS, false, W>(a, h, part, xarea, ring, c, best, t_ready);
     cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
+    trace_done(tr, a.trace_slot, t_start, t_ready);
     if (a.epi == MV_PART) {
         __threadfence_system();
-        m4_sync();
+        m4_sync<W>();
         if (threadIdx.x == 0)
             for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
         return;
@@ -1101,9 +1130,9 @@ __global__ void __launch_bounds__(kM4Threads, 1) mv4_kernel(const __grid_constan
         if (ov > best.v || (ov == best.v && oi < best.i)) { best.v = ov; best.i = oi; }
     }
     if (lane == 0) { h->amax[warp] = best.v; h->aidx[warp] = best.i; }
-    m4_sync();
+    m4_sync<W>();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < kM4Warps; ++w)
+        for (int w = 1; w < W; ++w)
             if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
         if (a.tp > 1u) {
             for (uint32_t p = 0; p < a.tp; ++p) {
@@ -1409,6 +1438,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
 {
     extern __shared__ __align__(16) uint8_t smem_a[];
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
+    const uint64_t t_start = global_ns();
+    uint64_t *const tr = trace_ptr(a.st);
     pdl_launch();
     const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
     if (pos >= a.max_context) {
@@ -1454,6 +1485,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
     }
     __syncthreads();
     pdl_wait();
+    const uint64_t t_ready = global_ns();
     attn_stage_qkv(a, sm, kvh, group, pos, has_pos, f16, head_row0);
     constexpr uint32_t kL = GP == 8 ? 3u : GP == 4 ? 2u : GP == 2 ? 1u : 0u;
     const uint32_t hm = lane >> (5u - kL);                       // this lane's head after head_sums
@@ -1539,6 +1571,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
         }
     }
     attn_merge(a, sm, kvh, group, cl, ncl);
+    trace_done(tr, a.trace_slot, t_start, t_ready);
 }
 
 // ------------------------------------------- attention, fp16 cache, MMA ----
@@ -1602,6 +1635,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid
 {
     extern __shared__ __align__(16) uint8_t smem_a[];
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
+    const uint64_t t_start = global_ns();
+    uint64_t *const tr = trace_ptr(a.st);
     pdl_launch();
     const uint32_t pos = *reinterpret_cast<volatile const uint32_t *>(&a.st->pos);
     if (pos >= a.max_context) {
@@ -1640,6 +1675,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid
     issue(t0, 0u);
     issue(t0 + kTcTile, 1u);
     pdl_wait();
+    const uint64_t t_ready = global_ns();
     attn_stage_qkv(a, sm, kvh, group, pos, has_pos, true, head_row0);
     // A operands of q: rows g (hi) and g + 8 (lo) of head g, 8 steps of 16 dimensions
     uint32_t qa[8][4];
@@ -1739,6 +1775,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid
         }
     }
     attn_merge(a, sm, kvh, group, cl, ncl);
+    trace_done(tr, a.trace_slot, t_start, t_ready);
 }
 
 // --------------------------------------------------------- embed, argmax --
@@ -1896,16 +1933,29 @@ const void *attn_fn(uint32_t group, bool tc = false)
 }  // namespace
 
 namespace {
-const void *mv4_fn(uint32_t nslot)
+const void *mv4_fn(uint32_t nslot, uint32_t warps)
 {
-    switch (nslot) {
-    case 2: return (const void *)mv4_kernel<2>;
-    case 3: return (const void *)mv4_kernel<3>;
-    case 4: return (const void *)mv4_kernel<4>;
-    case 5: return (const void *)mv4_kernel<5>;
-    case 6: return (const void *)mv4_kernel<6>;
-    default: return nullptr;
+    if (warps == 16u) {
+        switch (nslot) {
+        case 2: return (const void *)mv4_kernel<2, 16>;
+        case 3: return (const void *)mv4_kernel<3, 16>;
+        case 4: return (const void *)mv4_kernel<4, 16>;
+        case 5: return (const void *)mv4_kernel<5, 16>;
+        case 6: return (const void *)mv4_kernel<6, 16>;
+        default: return nullptr;
+        }
     }
+    if (warps == 8u) {
+        switch (nslot) {
+        case 2: return (const void *)mv4_kernel<2, 8>;
+        case 3: return (const void *)mv4_kernel<3, 8>;
+        case 4: return (const void *)mv4_kernel<4, 8>;
+        case 5: return (const void *)mv4_kernel<5, 8>;
+        case 6: return (const void *)mv4_kernel<6, 8>;
+        default: return nullptr;
+        }
+    }
+    return nullptr;
 }
 }  // namespace
 
@@ -1949,10 +1999,11 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
 {
     cudaError_t e = cudaFuncSetAttribute(mv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
     if (e != cudaSuccess) return e;
-    for (uint32_t ns = 2; ns <= kM4MaxSlots; ++ns)
-        if ((e = cudaFuncSetAttribute(mv4_fn(ns), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem)) !=
-            cudaSuccess)
-            return e;
+    for (uint32_t w : {8u, 16u})
+        for (uint32_t ns = 2; ns <= kM4MaxSlots; ++ns)
+            if ((e = cudaFuncSetAttribute(mv4_fn(ns, w), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem)) !=
+                cudaSuccess)
+                return e;
     for (uint32_t g = 1; g <= kAttnMaxGroup; g *= 2u)
         if ((e = cudaFuncSetAttribute(attn_fn(g), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem)) !=
             cudaSuccess)
@@ -1960,9 +2011,9 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
     return cudaFuncSetAttribute(attn_fn(1, true), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem);
 }
 
-extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes)
+extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t warps, uint32_t nslot, uint32_t slot_bytes)
 {
-    return m4_smem_bytes(cols, nslot, slot_bytes);
+    return m4_smem_bytes(cols, warps, nslot, slot_bytes);
 }
 
 extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaStream_t stream)
@@ -1970,9 +2021,9 @@ extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaSt
     MvArgs copy = *a;
     void *args[] = {&copy};
     if (a->engine == 1u) {
-        const void *fn = mv4_fn(a->nslot);
+        const void *fn = mv4_fn(a->nslot, a->warps);
         if (!fn) return cudaErrorInvalidValue;
-        return launch_ex(fn, args, dim3(grid), dim3(kM4Threads), a->smem_bytes, stream, a->pdl != 0u);
+        return launch_ex(fn, args, dim3(grid), dim3(32u * a->warps), a->smem_bytes, stream, a->pdl != 0u);
     }
     return launch_ex((const void *)mv_kernel, args, dim3(grid), dim3(kMvThreads), a->smem_bytes, stream, a->pdl != 0u);
 }

@@ -29,7 +29,14 @@ struct DecState {
     const uint32_t *in_ids;  // prompt mode: the token after step s is in_ids[s + 1] while s + 1 < n_in
     uint32_t n_in;
     uint32_t epoch;        // steps completed since creation (tensor-parallel exchange sequence)
+    uint64_t *trace;       // null, or the trace records of the next step (kernels record globaltimer stamps)
 };
+
+// Trace record of launch `slot` of the step, CTA c: kTraceWords stamps at
+// trace + (slot * kTraceCtas + c) * kTraceWords - [0] the CTA started, [1] its
+// inputs were ready (after the wait for the preceding kernel, the input
+// staging and any tensor-parallel exchange), [2 + w] warp w finished.
+constexpr uint32_t kTraceCtas = 512, kTraceWords = 20;
 
 // ------------------------------------------------ tensor-parallel exchange --
 //
@@ -146,12 +153,14 @@ struct MvArgs {
     uint32_t out_red, out_cnt;
     uint32_t row_base;       // MV_LOGITS: global index of row 0
     uint32_t engine;         // 0: mv_kernel (producer warp + shared ring); 1: mv4_kernel (per-warp rings)
+    uint32_t trace_slot;     // this launch's index in the step (trace records)
+    uint32_t warps;          // mv4_kernel: 8 (two CTAs per SM) or 16 warps per CTA
 };
 
 // ------------------------------------------------------------ mv4 kernel ----
 //
 // The same launches (MvArgs, task ranges, epilogues) on a kernel without a
-// producer warp: 16 warps, each with a contiguous range of the CTA's tasks
+// producer warp: 8 or 16 warps, each with a contiguous range of the CTA's tasks
 // and its own ring of nslot task slots filled by cp.async (16-byte copies
 // issued by its own lanes). A slot holds the 16 rows of one task: Q4_K rows
 // 144 bytes apart (the block itself), Q6_K rows as 224-byte windows from the
@@ -186,6 +195,7 @@ struct AttnArgs {
     const float *q_norm, *k_norm;   // qwen3: per-head RMSNorm weights [128] of q and k, or null
     float eps;
     uint32_t tc;                // fp16 cache: tensor-core kernel (attn_tc16_kernel)
+    uint32_t trace_slot;        // this launch's index in the step (trace records)
 };
 
 }  // namespace d2

@@ -39,7 +39,7 @@ extern "C" cudaError_t atlas_launch_prefill_embed(const uint32_t *ids, uint32_t 
                                                   cudaStream_t stream);
 extern "C" cudaError_t atlas_launch_prefill_attn_tc(const atlas::pf::AttnArgs *a, int grid, cudaStream_t stream);
 extern "C" size_t atlas_d2_mv_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes, uint32_t tslots);
-extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t nslot, uint32_t slot_bytes);
+extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t warps, uint32_t nslot, uint32_t slot_bytes);
 extern "C" size_t atlas_d2_attn_smem(uint32_t splits);
 extern "C" int atlas_d2_attn_max_clusters(uint32_t group, uint32_t tc);
 extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
@@ -129,6 +129,7 @@ struct AtlasCuda {
         uint32_t *actr = nullptr, *status = nullptr;
         uint32_t splits = 0, kernels = 0;
         bool attn_tc = false;   // fp16 cache: the tensor-core decode attention
+        uint64_t *trace = nullptr;   // trace records of atlas_cuda_trace_graph (allocated on first use)
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
     } g2;
@@ -695,18 +696,29 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     if (!ok) return fail(h, ATLAS_EINVAL, "mv: no shared-memory plan for %u columns", cols);
     a.smem_bytes = (uint32_t)atlas_d2_mv_smem(cols, a.nslot, a.slot_bytes, a.tslots);
     if (kMvEngine == 1u) {
-        // per-warp rings (mv4_kernel): the deepest ring that fits the SM's
-        // shared memory; inputs too long for two slots per warp stay on mv_kernel
+        // per-warp rings (mv4_kernel): 16 warps with the deepest ring the SM
+        // holds (at least 2 slots). The kernel is bound by instruction issue,
+        // so all 16 warps stay busy: 8-warp CTAs that let the next launch's
+        // CTAs start early measured 32 % slower on the 7B step (3.41 against
+        // 2.59 ms), and 8 warps with deeper rings slower on the down
+        // projection too. Inputs too long for two slots stay on mv_kernel.
         uint32_t slot = 0;
         for (uint32_t s = 0; s < a.n_seg; ++s)
             slot = std::max(slot, a.seg[s].type == 12u ? 16u * d2::kM4Q4Row : 16u * d2::kM4Q6Row);
-        for (uint32_t ns = d2::kM4MaxSlots; ns >= 2u; --ns) {
-            const size_t need = atlas_d2_mv4_smem(cols, ns, slot);
-            if (need <= 227u * 1024u) {
+        auto deepest = [&](uint32_t warps, uint32_t budget) {
+            for (uint32_t ns = d2::kM4MaxSlots; ns >= 2u; --ns)
+                if (atlas_d2_mv4_smem(cols, warps, ns, slot) <= budget) return ns;
+            return 0u;
+        };
+        const struct { uint32_t warps, budget, min_ns; } choices[] = {{16u, 227u * 1024u, 2u}};
+        for (const auto &ch : choices) {
+            const uint32_t ns = deepest(ch.warps, ch.budget);
+            if (ns >= ch.min_ns) {
                 a.engine = 1u;
+                a.warps = ch.warps;
                 a.nslot = ns;
                 a.slot_bytes = slot;
-                a.smem_bytes = (uint32_t)need;
+                a.smem_bytes = (uint32_t)atlas_d2_mv4_smem(cols, ch.warps, ns, slot);
                 break;
             }
         }
@@ -826,7 +838,10 @@ int build_graph2(AtlasCuda *h)
         hd.a.row_base = sl.vocab_row0;
     }
     size_t mv_smem = 0;
-    for (const MvPlan *p : {&qkv, &o, &gu, &dn, &hd}) mv_smem = std::max<size_t>(mv_smem, p->a.smem_bytes);
+    for (MvPlan *p : {&qkv, &o, &gu, &dn, &hd}) {
+        mv_smem = std::max<size_t>(mv_smem, p->a.smem_bytes);
+        p->a.dstate = g.st;   // the step's state (tensor-parallel epoch, trace pointer)
+    }
     CU(h, atlas_d2_setup(mv_smem, atlas_d2_attn_smem(g.splits)));
 
     d2::AttnArgs at{};
@@ -869,27 +884,36 @@ int build_graph2(AtlasCuda *h)
             a.seq_add = l;
             a.xout = h->x;
         }
+        a.trace_slot = kernels;
         if ((e = atlas_d2_launch_mv(&a, qkv.grid, h->stream)) != cudaSuccess) break;
         at.k_cache = w.kc;
         at.v_cache = w.vc;
         at.q_norm = w.qn;
         at.k_norm = w.kn;
+        at.trace_slot = kernels + 1u;
         if ((e = atlas_d2_launch_attn(&at, sl.kv_heads * g.splits, h->stream)) != cudaSuccess) break;
         a = o.a;
         a.seg[0].w = w.o;
+        a.trace_slot = kernels + 2u;
         if ((e = atlas_d2_launch_mv(&a, o.grid, h->stream)) != cudaSuccess) break;
         a = gu.a;
         a.seg[0].w = w.gate;
         a.seg[1].w = w.up;
         a.norm_w = w.ffn_norm;
         a.seq_add = l + 1u;
+        a.trace_slot = kernels + 3u;
         if ((e = atlas_d2_launch_mv(&a, gu.grid, h->stream)) != cudaSuccess) break;
         a = dn.a;
         a.seg[0].w = w.down;
+        a.trace_slot = kernels + 4u;
         if ((e = atlas_d2_launch_mv(&a, dn.grid, h->stream)) != cudaSuccess) break;
         kernels += 5;
     }
-    if (e == cudaSuccess) { e = atlas_d2_launch_mv(&hd.a, hd.grid, h->stream); ++kernels; }
+    if (e == cudaSuccess) {
+        hd.a.trace_slot = kernels;
+        e = atlas_d2_launch_mv(&hd.a, hd.grid, h->stream);
+        ++kernels;
+    }
     if (e == cudaSuccess) {
         if (tp > 1) {
             const d2::TpLayout xl = d2::tp_layout(tp, d.hidden);
@@ -1790,6 +1814,35 @@ int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out
     }
     cudaFree(d);
     return rc;
+}
+
+int atlas_cuda_trace_graph(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out, size_t cap, uint32_t *n_launches,
+                           uint32_t *n_ctas, uint32_t *n_words)
+{
+    if (!h) return fail(h, ATLAS_EINVAL, "null handle");
+    AtlasCuda::Graph2 &g = h->g2;
+    if (!g.on) return fail(h, ATLAS_EINVAL, "the decode step is not built (tensor parallel: call atlas_cuda_tp_connect)");
+    const size_t need = (size_t)g.kernels * d2::kTraceCtas * d2::kTraceWords;
+    if (n_launches) *n_launches = g.kernels;
+    if (n_ctas) *n_ctas = d2::kTraceCtas;
+    if (n_words) *n_words = d2::kTraceWords;
+    if (!out) return ATLAS_OK;
+    if (cap < need) return fail(h, ATLAS_EINVAL, "trace buffer needs %zu slots", need);
+    if (id >= h->desc.vocab || pos >= h->desc.max_context) return fail(h, ATLAS_ERANGE, "token or position out of range");
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    if (!g.trace) {
+        int rc = dalloc(h, &g.trace, need * sizeof(uint64_t));
+        if (rc) return rc;
+    }
+    CU(h, cudaMemsetAsync(g.trace, 0, need * sizeof(uint64_t), h->stream));
+    uint64_t *const on = g.trace, *const off = nullptr;
+    CU(h, cudaMemcpyAsync(&g.st->trace, &on, sizeof(on), cudaMemcpyHostToDevice, h->stream));
+    const int rc = run_graph2(h, id, pos, 1, nullptr, nullptr, nullptr);
+    CU(h, cudaMemcpyAsync(&g.st->trace, &off, sizeof(off), cudaMemcpyHostToDevice, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    if (rc) return rc;
+    CU(h, cudaMemcpy(out, g.trace, need * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    return ATLAS_OK;
 }
 
 int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last_ms)

@@ -27,7 +27,7 @@ EXPORTS = [
     "atlas_cuda_create", "atlas_cuda_destroy", "atlas_cuda_last_error", "atlas_cuda_prefill",
     "atlas_cuda_decode", "atlas_cuda_generate", "atlas_cuda_stats", "atlas_cuda_dequant",
     "atlas_cuda_gemv", "atlas_cuda_gemm", "atlas_cuda_device_info", "atlas_cuda_trace_step",
-    "atlas_cuda_device_ms", "atlas_cuda_gemv_noalloc", "atlas_cuda_tp_slice", "atlas_cuda_tp_handle",
+    "atlas_cuda_device_ms", "atlas_cuda_trace_graph", "atlas_cuda_gemv_noalloc", "atlas_cuda_tp_slice", "atlas_cuda_tp_handle",
     "atlas_cuda_tp_connect",
     "brain_gpu_init", "brain_gpu_matvec_batch", "brain_gpu_matvec", "brain_gpu_shutdown",
     "atlas_rt_open", "atlas_rt_close", "atlas_rt_error", "atlas_rt_shape", "atlas_rt_data_base",
@@ -119,6 +119,7 @@ def lib() -> ctypes.CDLL:
         L.atlas_cuda_stats.argtypes = [P, P, P]
         L.atlas_cuda_device_ms.argtypes = [P, P]
         L.atlas_cuda_trace_step.argtypes = [P, U32, U32, P, ctypes.c_size_t, P, P, P]
+        L.atlas_cuda_trace_graph.argtypes = [P, U32, U32, P, ctypes.c_size_t, P, P, P]
         L.atlas_cuda_tp_slice.argtypes = [P, I32, I32, P]
         L.atlas_cuda_tp_handle.argtypes = [P, P]
         L.atlas_cuda_tp_connect.argtypes = [P, P]
@@ -250,6 +251,19 @@ class Runtime:
         check(lib().atlas_cuda_trace_step(dev, token, pos, _ptr(buf), buf.size, ctypes.byref(nc), ctypes.byref(nph),
                                           _ptr(kinds)), "trace_step", dev)
         return buf[:per * 4].reshape(nc.value, nph.value, 4), buf[per * 4:].reshape(nc.value, nph.value, 8), kinds
+
+    def trace_graph(self, token: int, pos: int):
+        """One decode step of the graph engine with device timestamps:
+        array [launch, cta, word] of globaltimer ns (0 = not recorded); word 0
+        start, 1 inputs ready, 2 + w warp w done (atlas_cuda_trace_graph)."""
+        import numpy as np
+        dev = lib().atlas_rt_device(self._h)
+        nl, nc, nw = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+        check(lib().atlas_cuda_trace_graph(dev, token, pos, None, 0, ctypes.byref(nl), ctypes.byref(nc),
+                                           ctypes.byref(nw)), "trace_graph", dev)
+        buf = np.zeros(nl.value * nc.value * nw.value, np.uint64)
+        check(lib().atlas_cuda_trace_graph(dev, token, pos, _ptr(buf), buf.size, None, None, None), "trace_graph", dev)
+        return buf.reshape(nl.value, nc.value, nw.value)
 
     def tp_slice(self) -> TpSlice:
         """This rank's share of the model (the whole model without tensor parallelism)."""

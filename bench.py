@@ -112,7 +112,8 @@ def golden_picks(name, cfg):
     if not os.path.exists(p):
         return None
     g = np.load(p)
-    if any(int(g[f"cfg_{k}"]) != int(v) for k, v in cfg.items()) or not np.array_equal(g["prompt"], prompt_ids(cfg)):
+    same = all(int(g[f"cfg_{k}"]) == int(v) for k, v in cfg.items() if f"cfg_{k}" in g.files)
+    if not same or int(g["tied"]) != int(cfg["tied"]) or not np.array_equal(g["prompt"], prompt_ids(cfg)):
         return None
     return g["picks"]
 

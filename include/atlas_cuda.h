@@ -121,6 +121,19 @@ int atlas_cuda_device_ms(const AtlasCuda *h, double *total_ms);
 int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out_ns, size_t cap,
                           uint32_t *n_ctas, uint32_t *n_phases, uint32_t *phase_kinds);
 
+/* One decode step of the graph engine (forward_token + greedy pick at `pos`)
+   with device timestamps: every mv / attention launch records, per CTA, the
+   globaltimer (ns) when it started, when its inputs were ready (after the
+   wait for the preceding kernel, the input staging and, under tensor
+   parallelism, the wait for the peers' partial rows), and when each warp
+   finished. out receives n_launches x n_ctas x n_words stamps (0 = not
+   recorded; launch 0 is the embedding, then 5 per layer - q/k/v, attention,
+   o, gate/up, down - then the head and the argmax). With out == NULL only
+   the three sizes are returned. Diagnostics; no counterpart in the
+   reference. */
+int atlas_cuda_trace_graph(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out, size_t cap,
+                           uint32_t *n_launches, uint32_t *n_ctas, uint32_t *n_words);
+
 /* ---- tensor parallelism (one process per GPU, tp_size ranks) ----
 
    The layout of the reference's forward_token across ranks: query heads with

@@ -202,5 +202,24 @@ uint32_t ref_sample_greedy(const float *logits, uint64_t vocab)
     return id;
 }
 
+/* The reference's device plugin for forward_token's GEMVs, as run_main_utf8
+   brings it up (src/brain_runtime.c:1941-1946): brain_gpu_init over the
+   loaded file, hybrid row split when `hybrid`. Returns whether the plugin
+   came up (the CPU build links a stub that never does). */
+int ref_gpu_init(int hybrid)
+{
+    if (!g_ram_model.data) return 0;
+    g_gpu_enabled = brain_gpu_init(g_ram_model.data, g_ram_model.size);
+    g_hybrid_enabled = hybrid ? 1 : 0;
+    return g_gpu_enabled;
+}
+
+void ref_gpu_shutdown(void)
+{
+    if (g_gpu_enabled) brain_gpu_shutdown();
+    g_gpu_enabled = 0;
+    g_hybrid_enabled = 0;
+}
+
 /* The reference CLI (argv contract of atlas_dynamic_infer). */
 int ref_main(int argc, char **argv) { return run_main_utf8(argc, argv); }

@@ -1,0 +1,76 @@
+"""GPU: the reference's own runtime (src/brain_runtime.c, compiled in place as
+oracle/_ref/libbrainref_gpu.so) with its device plugin (src/gpu_matvec.h)
+taken from libatlas_cuda.so instead of the Direct3D 12 file - the drop-in the
+plugin ABI exists for:
+  * its `model.gguf --gpu-check` self-test (src/brain_runtime.c:1958-1984)
+    passes by the reference's own criterion;
+  * forward_token with the plugin on (every GEMV on the GPU) and with
+    BRAIN_HYBRID=1 (rows split between the GPU and CPU threads,
+    src/brain_runtime.c:1202-1244) gives the CPU runtime's logits and picks."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import atlas_cuda
+import oracle_bind
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "oracle", "_ref", "libbrainref_gpu.so")
+# vocab >= 8192 rows: the hybrid path splits the output head between GPU and CPU
+BOUNDARY = dict(hidden=512, layers=2, q_heads=4, kv_heads=2, ffn=768, vocab=16384, context_length=512, seed=4242)
+
+
+class RefGpu(oracle_bind.Reference):
+    PATH = LIB
+
+    def __init__(self):
+        super().__init__()
+        self.L.ref_gpu_init.argtypes = [ctypes.c_int]
+        self.L.ref_main.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p)]
+
+
+@pytest.fixture(scope="module")
+def refgpu(torch_cuda):
+    if not os.path.exists(LIB):
+        pytest.skip("oracle/_ref/libbrainref_gpu.so is not built (make -C oracle ref-gpu)")
+    return RefGpu()
+
+
+@pytest.fixture(scope="module")
+def boundary_model(model_dir):
+    path = os.path.join(str(model_dir), "boundary.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, tied=False, **BOUNDARY)
+    return path
+
+
+def test_reference_gpu_check_passes_on_b200(refgpu, small_model, capfd):
+    argv = (ctypes.c_char_p * 3)(b"atlas_dynamic_infer", small_model.encode(), b"--gpu-check")
+    rc = refgpu.L.ref_main(3, argv)
+    ctypes.CDLL(None).fflush(None)
+    out = capfd.readouterr().out
+    assert rc == 0, out
+    assert out.count("GPU/CPU PASS") == 2, out
+
+
+@pytest.mark.parametrize("hybrid", [0, 1])
+def test_reference_forward_with_b200_plugin(refgpu, ref, boundary_model, hybrid):
+    tokens = [5, 900, 77, 3000, 12000, 16383, 1]
+    ref.open(boundary_model)
+    want = [ref.forward(t, p) for p, t in enumerate(tokens)]
+    ref.close()
+    refgpu.open(boundary_model)
+    try:
+        assert refgpu.L.ref_gpu_init(hybrid) == 1, "brain_gpu_init failed"
+        assert refgpu.L.ref_session_begin()
+        got = [refgpu.forward(t, p) for p, t in enumerate(tokens)]
+    finally:
+        refgpu.L.ref_gpu_shutdown()
+        refgpu.close()
+    for p, (g, w) in enumerate(zip(got, want)):
+        err = np.abs(g.astype(np.float64) - w).max()
+        assert err <= 1e-3 * np.abs(w).max(), (p, err)
+        assert int(np.argmax(g)) == int(np.argmax(w)), p
