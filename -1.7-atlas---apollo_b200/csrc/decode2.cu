@@ -47,7 +47,8 @@ __device__ __forceinline__ uint64_t *trace_ptr(const DecState *st)
     return *reinterpret_cast<uint64_t *const volatile *>(&st->trace);
 }
 // Warp w's stamps into launch `slot`'s record of this CTA (lane 0 only).
-__device__ __forceinline__ void trace_done(uint64_t *tr, uint32_t slot, uint64_t t_start, uint64_t t_ready)
+__device__ __forceinline__ void trace_done(uint64_t *tr, uint32_t slot, uint64_t t_start, uint64_t t_ready,
+                                           uint64_t t_wait = 0)
 {
     if (!tr || blockIdx.x >= kTraceCtas) return;
     const uint32_t warp = threadIdx.x >> 5;
@@ -55,8 +56,9 @@ __device__ __forceinline__ void trace_done(uint64_t *tr, uint32_t slot, uint64_t
     if (warp == 0) {
         rec[0] = t_start;
         rec[1] = t_ready;
+        rec[kTraceWords - 1] = t_wait;
     }
-    if (warp + 2u < kTraceWords) rec[2 + warp] = global_ns();
+    if (warp + 3u < kTraceWords) rec[2 + warp] = global_ns();
 }
 
 // consumer warps only (the producer warp never joins)
@@ -246,7 +248,8 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
 // W: the staging warps (threads 0 .. 32 W - 1, synchronised on named barrier 1);
 // dred / fred: W slots each for the block reductions.
 template <int W>
-__device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t *xarea, bool q4_order)
+__device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t *xarea, bool q4_order,
+                           uint64_t *t_wait = nullptr)
 {
     const uint32_t n4 = a.cols / 4u;
     const bool norm = a.norm_w != nullptr;
@@ -266,6 +269,7 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
         }
     }
     if (a.pdl) pdl_wait();
+    if (t_wait) *t_wait = global_ns();
     // tensor parallel: the partial rows of the preceding row-split projection
     // from every rank, then x = a.x + slot 0 + slot 1 + ... in rank order
     const float4 *red = nullptr;
@@ -973,7 +977,7 @@ __device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, 
 
 template <int NS, bool Q4, int W>
 __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xarea, uint8_t *ring, const MvCta &c,
-                           MvBest &best, uint64_t &t_ready)
+                           MvBest &best, uint64_t &t_ready, uint64_t &t_wait)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 2;
@@ -1016,7 +1020,7 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         }
         m4_commit();
     }
-    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4);
+    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4, &t_wait);
     t_ready = global_ns();
     if (!active) return;
     // sharing of the first and last tiles with neighbouring warps
@@ -1081,7 +1085,7 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     uint8_t *ring = xarea + mv_x_bytes(a.cols);
     const uint64_t t_start = global_ns();
     uint64_t *const tr = trace_ptr(a.dstate);
-    uint64_t t_ready = 0;
+    uint64_t t_ready = 0, t_wait = 0;
     const MvCta c = a.cta[blockIdx.x];
     {
         const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)W, L);
@@ -1110,10 +1114,10 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     __syncthreads();
     pdl_launch();
     MvBest best{-FLT_MAX, 0xffffffffu};
-    if (a.seg[c.seg].type == 12u) m4_consume<NS, true, W>(a, h, part, xarea, ring, c, best, t_ready);
-    else m4_consume<NS, false, W>(a, h, part, xarea, ring, c, best, t_ready);
+    if (a.seg[c.seg].type == 12u) m4_consume<NS, true, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
+    else m4_consume<NS, false, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
     cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
-    trace_done(tr, a.trace_slot, t_start, t_ready);
+    trace_done(tr, a.trace_slot, t_start, t_ready, t_wait);
     if (a.epi == MV_PART) {
         __threadfence_system();
         m4_sync<W>();

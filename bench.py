@@ -357,7 +357,7 @@ def summarize(name, cfg, r, steps, pg, groups, sl=None, tp=1):
                      "bytes_per_token": int(rank_bytes), "traffic": None,
                      "traffic_note": "DRAM bytes of one decode step from an ncu capture are in profiles/ "
                                      "(decode_step_*); not re-measured inside the timed run",
-                     "kernel": "decode step: CUDA graph of PDL-chained kernels (mv_kernel dequant-GEMVs, attention, "
+                     "kernel": "decode step: CUDA graph of PDL-chained kernels (mv4_kernel dequant-GEMVs, attention, "
                                "embed, argmax); achieved = one GPU's weight + KV bytes per token / device time per "
                                "token"},
         "prefill_roofline": {"bound": "tensor", "achieved": round(pf_tflops, 1), "peak": tpk, "unit": "TFLOP/s",
@@ -390,21 +390,22 @@ def run_ours(args):
     if pg and groups > 1:
         subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
         tp_group = subgroups[group_id]
-    path = ensure_model_product_writer("cfg2", CFG2, rank, pg)
+    name, cfg = ("cfg1", CFG1) if args.shape == "3b" else ("cfg2", CFG2)
+    path = ensure_model_product_writer(name, cfg, rank, pg)
     rt = atlas_cuda.Runtime(path, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT,
                             tp_rank=tp_rank, tp_size=tp)
     if tp > 1:
         atlas_cuda.connect_tp(rt, group=tp_group)
     barrier(pg)
     sl = rt.tp_slice().as_dict() if tp > 1 else None
-    r = run_model("cfg2", CFG2, rt, args.steps, args.warmup, pg, clocks_gpu=local if rank == 0 else None)
-    s = summarize("cfg2", CFG2, r, args.steps, pg, groups, sl, tp)
+    r = run_model(name, cfg, rt, args.steps, args.warmup, pg, clocks_gpu=local if rank == 0 else None)
+    s = summarize(name, cfg, r, args.steps, pg, groups, sl, tp)
     rt.close()
     barrier(pg)
     if ws == 1 and s["parity"] is not None and not s["parity"]["picks_match_reference"]:
-        raise SystemExit(f"greedy picks differ from the reference's (tests/golden/cfg2.npz): {list(r['ids'][:32])}")
+        raise SystemExit(f"greedy picks differ from the reference's (tests/golden/{name}.npz): {list(r['ids'][:32])}")
     secondary, cpu = None, None
-    if ws == 1 and not args.no_secondary:
+    if ws == 1 and not args.no_secondary and name == "cfg2":
         p1 = ensure_model_product_writer("cfg1", CFG1, rank, pg)
         with atlas_cuda.Runtime(p1, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT) as rt1:
             r1 = run_model("cfg1", CFG1, rt1, args.steps, args.warmup, pg)
@@ -418,13 +419,13 @@ def run_ours(args):
                      "e2e_decode_tok_s": round(s1["e2e_decode_tok_s"], 2), "parity": s1["parity"],
                      "gpu_launches": int(r1["launches"])}
     if ws == 1 and not args.no_cpu_baseline:
-        c = cpu_reference_sample(model_path("cfg2"), CFG2, n_decode=3, n_prompt=3)
+        c = cpu_reference_sample(model_path(name), cfg, n_decode=3, n_prompt=3)
         if c is not None:
             cpu = {"value": round(c["decode_tok_s"], 4), "unit": "tok/s", "cores": c["gemv_threads"],
                    "host_cores": c["host_cores"], "kind": "reference",
                    "prefill_tok_s": round(c["prefill_tok_s"], 4),
                    "sample": f"3 prompt tokens (token at a time, no logits), then 3 greedy decode tokens at positions "
-                             f"{PROMPT}-{PROMPT + 2} over a {PROMPT}-position cache, 7B shape"}
+                             f"{PROMPT}-{PROMPT + 2} over a {PROMPT}-position cache, {args.shape.upper()} shape"}
     if rank == 0:
         clocks = r["clocks"] or {}
         par = f"tp{tp}" if groups == 1 else f"tp{tp} x {groups} groups"
@@ -434,8 +435,9 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong" if groups == 1 and ws > 1 else "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
-            "config": {"workload": WORKLOAD["cfg2"], "parallelism": par if ws > 1 else "1 GPU",
-                       "l2": "inputs larger than L2 (4.62 GB of weights streamed per token)", "kv_cache": "fp32"},
+            "config": {"workload": WORKLOAD[name], "parallelism": par if ws > 1 else "1 GPU",
+                       "l2": f"inputs larger than L2 ({weight_bytes(cfg) / 1e9:.2f} GB of weights streamed per token)",
+                       "kv_cache": "fp32"},
             "decode_ms_per_token": round(s["decode_ms_per_token"], 4),
             "prefill_tok_s": round(s["prefill_tok_s"], 1),
             "roofline": s["roofline"],
@@ -459,6 +461,7 @@ def run_ours(args):
 
 
 def main():
+    global GEN
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -466,7 +469,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the 3B workload at N=1")
+    ap.add_argument("--shape", default="7b", choices=["7b", "3b"],
+                    help="the headline workload's model shape (3b: the secondary workload alone, e.g. for profiles)")
+    ap.add_argument("--gen", type=int, default=GEN, help="greedy decode steps per workload step (profiles: fewer)")
     args = ap.parse_args()
+    GEN = args.gen
     if args.impl == "reference":
         run_reference(args)
     else:
