@@ -48,7 +48,7 @@ __device__ __forceinline__ uint64_t *trace_ptr(const DecState *st)
 }
 // Warp w's stamps into launch `slot`'s record of this CTA (lane 0 only).
 __device__ __forceinline__ void trace_done(uint64_t *tr, uint32_t slot, uint64_t t_start, uint64_t t_ready,
-                                           uint64_t t_wait = 0)
+                                           uint64_t t_wait = 0, uint64_t t_peers = 0)
 {
     if (!tr || blockIdx.x >= kTraceCtas) return;
     const uint32_t warp = threadIdx.x >> 5;
@@ -56,9 +56,10 @@ __device__ __forceinline__ void trace_done(uint64_t *tr, uint32_t slot, uint64_t
     if (warp == 0) {
         rec[0] = t_start;
         rec[1] = t_ready;
+        rec[kTraceWords - 2] = t_peers;
         rec[kTraceWords - 1] = t_wait;
     }
-    if (warp + 3u < kTraceWords) rec[2 + warp] = global_ns();
+    if (warp + 4u < kTraceWords) rec[2 + warp] = global_ns();
 }
 
 // consumer warps only (the producer warp never joins)
@@ -269,7 +270,7 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
         }
     }
     if (a.pdl) pdl_wait();
-    if (t_wait) *t_wait = global_ns();
+    if (t_wait) t_wait[0] = global_ns();
     // tensor parallel: the partial rows of the preceding row-split projection
     // from every rank, then x = a.x + slot 0 + slot 1 + ... in rank order
     const float4 *red = nullptr;
@@ -280,6 +281,7 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
             const uint32_t k = epoch * a.seq_mul + a.seq_add;
             wait_counter_sys(reinterpret_cast<const uint32_t *>(a.peer[a.rank] + a.in_cnt), k * a.in_arrivals,
                              a.status);
+            if (t_wait) t_wait[1] = global_ns();   // the peers' partial rows have all arrived
         }
         asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
         red = reinterpret_cast<const float4 *>(a.peer[a.rank] + a.in_red);
@@ -977,7 +979,7 @@ __device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, 
 
 template <int NS, bool Q4, int W>
 __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xarea, uint8_t *ring, const MvCta &c,
-                           MvBest &best, uint64_t &t_ready, uint64_t &t_wait)
+                           MvBest &best, uint64_t &t_ready, uint64_t *t_wait)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 2;
@@ -1020,7 +1022,7 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         }
         m4_commit();
     }
-    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4, &t_wait);
+    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4, t_wait);
     t_ready = global_ns();
     if (!active) return;
     // sharing of the first and last tiles with neighbouring warps
@@ -1085,7 +1087,7 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     uint8_t *ring = xarea + mv_x_bytes(a.cols);
     const uint64_t t_start = global_ns();
     uint64_t *const tr = trace_ptr(a.dstate);
-    uint64_t t_ready = 0, t_wait = 0;
+    uint64_t t_ready = 0, t_wait[2] = {0, 0};
     const MvCta c = a.cta[blockIdx.x];
     {
         const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)W, L);
@@ -1117,14 +1119,17 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     if (a.seg[c.seg].type == 12u) m4_consume<NS, true, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
     else m4_consume<NS, false, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
     cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
-    trace_done(tr, a.trace_slot, t_start, t_ready, t_wait);
     if (a.epi == MV_PART) {
-        __threadfence_system();
+        // The barrier orders every thread's partial-row stores to the peers
+        // before thread 0's system-scope release, which is cumulative: a rank
+        // that acquires the counter sees all of them.
         m4_sync<W>();
         if (threadIdx.x == 0)
             for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        trace_done(tr, a.trace_slot, t_start, t_ready, t_wait[0], t_wait[1]);
         return;
     }
+    trace_done(tr, a.trace_slot, t_start, t_ready, t_wait[0], t_wait[1]);
     if (a.epi != MV_LOGITS) return;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 #pragma unroll

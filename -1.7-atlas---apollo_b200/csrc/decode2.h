@@ -36,7 +36,9 @@ struct DecState {
 // trace + (slot * kTraceCtas + c) * kTraceWords - [0] the CTA started, [1] its
 // inputs were ready (after the wait for the preceding kernel, the input
 // staging and any tensor-parallel exchange), [2 + w] warp w finished (w < 16),
-// [kTraceWords - 1] the wait for the preceding kernel returned (GEMV launches).
+// [kTraceWords - 2] the peers' partial rows had all arrived (tensor-parallel
+// GEMV launches), [kTraceWords - 1] the wait for the preceding kernel returned
+// (GEMV launches).
 constexpr uint32_t kTraceCtas = 512, kTraceWords = 20;
 
 // ------------------------------------------------ tensor-parallel exchange --
