@@ -74,3 +74,32 @@ def test_reference_forward_with_b200_plugin(refgpu, ref, boundary_model, hybrid)
         err = np.abs(g.astype(np.float64) - w).max()
         assert err <= 1e-3 * np.abs(w).max(), (p, err)
         assert int(np.argmax(g)) == int(np.argmax(w)), p
+
+
+CLI_GPU = os.path.join(ROOT, "oracle", "_ref", "atlas_dynamic_infer")
+CLI_CPU = os.path.join(ROOT, "oracle", "_ref", "atlas_dynamic_infer_cpu")
+
+
+def _cli(exe, *args):
+    import subprocess
+    env = dict(os.environ, ATLAS_REF_THREADS="8")
+    return subprocess.run(["timeout", "300", exe, *args], capture_output=True, env=env)
+
+
+def test_reference_cli_drop_in_matches_cpu(torch_cuda, small_model):
+    """The reference's own atlas_dynamic_infer (argv, chat template,
+    tokenizer, greedy sampling, stop tokens, stdout text), linked against
+    libatlas_cuda.so as its device plugin, prints exactly what its CPU build
+    prints for the same prompt, and keeps the exit codes."""
+    if not (os.path.exists(CLI_GPU) and os.path.exists(CLI_CPU)):
+        pytest.skip("oracle/_ref/atlas_dynamic_infer is not built (make -C oracle ref-gpu)")
+    prompt = "Hello there, how are you?"
+    gpu = _cli(CLI_GPU, small_model, prompt, "16")
+    cpu = _cli(CLI_CPU, small_model, prompt, "16")
+    assert gpu.returncode == 0 and cpu.returncode == 0, (gpu.stderr[-2000:], cpu.stderr[-2000:])
+    assert b"Direct3D 12 GPU" in gpu.stderr          # the plugin came up (the reference's own device message)
+    assert b"CPU fallback" in cpu.stderr
+    assert gpu.stdout == cpu.stdout and len(gpu.stdout) > 1
+    check = _cli(CLI_GPU, small_model, "--gpu-check")
+    assert check.returncode == 0 and check.stdout.count(b"GPU/CPU PASS") == 2, check.stdout
+    assert _cli(CLI_GPU, small_model, prompt, "0").returncode == 2      # max_new_tokens out of range
