@@ -791,6 +791,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint64
     asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(policy)
                  : "memory");
 }
+__device__ __forceinline__ void cp_async16_plain(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void m4_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -873,9 +877,9 @@ __device__ __forceinline__ float m4_rows(float v0, float v1, uint32_t lane)
 // Finish tile t after this warp's last task in it: alone (wa == wb), or as
 // one of the warps wa..wb sharing it (partials in shared memory; the last to
 // arrive adds them in warp order).
-__device__ __noinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, uint32_t seg, uint32_t t, uint32_t tj0,
-                                      uint32_t wa, uint32_t wb, uint32_t my0, float a00, float a01, float a10,
-                                      float a11, float out_scale, MvBest &best)
+__device__ __forceinline__ void m4_flush_body(const MvArgs &a, M4Hdr *h, float *part, uint32_t seg, uint32_t t,
+                                              uint32_t tj0, uint32_t wa, uint32_t wb, uint32_t my0, float a00,
+                                              float a01, float a10, float a11, float out_scale, MvBest &best)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     float r0 = m4_rows(a00, a01, lane);
@@ -908,6 +912,15 @@ __device__ __noinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, ui
     }
     const float pre = mv_pre(a, seg, t, lane);
     if (lane < 16u) mv_finish(a, seg, t, r0 * out_scale, r1 * out_scale, pre, lane, best);
+}
+
+// Out of line for the Q4_K / Q6_K kernels (code size); the other types'
+// kernels inline the body.
+__device__ __noinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, uint32_t seg, uint32_t t, uint32_t tj0,
+                                      uint32_t wa, uint32_t wb, uint32_t my0, float a00, float a01, float a10,
+                                      float a11, float out_scale, MvBest &best)
+{
+    m4_flush_body(a, h, part, seg, t, tj0, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
 }
 
 // 16 bytes at a 2-byte-aligned shared-memory address, as four words: five
@@ -977,10 +990,154 @@ __device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, 
     }
 }
 
-template <int NS, bool Q4, int W>
+// ------------------------------------------------ other block types ----
+//
+// A task of type TY (F16, Q5_0, Q5_1, Q8_0, Q5_K) reads every weight of a
+// 16-element group G as  w = S q + M,  with q a small unsigned integer and
+// S, M per row and group (dequant_block, src/brain_runtime.c:1017-1121):
+//   Q5_0  q = nibble | high bit << 4   S = d        M = -16 d
+//   Q5_1  q = nibble | high bit << 4   S = d        M = m
+//   Q8_0  q = int8 + 128               S = d        M = -128 d
+//   Q5_K  q = nibble | high bit << 4   S = d sc_j   M = -dmin m_j   (j = G / 2)
+//   F16   the binary16 weight itself   S = 1        M = 0
+// so a row's dot over G is  S sum(q x) + M sum(x).  q enters the MMA as a
+// zero-extended 16-bit lane (the fp16 subnormal q 2^-24 exactly). The lanes
+// share the MMAs as in q6k_task4: in round `it`, the four lanes t of a row
+// group supply the k slots of group G = 4 it + t, four elements per MMA, and
+// B holds x only in the column pair (hi, lo) of the group its lane carries,
+// so accumulator columns 2t, 2t + 1 end as group G's sums for rows g, g + 8.
+
+// The group's 4-byte words of quant values (bytes zero-extended later), and
+// the group's (S, M) for one row of a task chunk at `r` (shared memory).
+template <uint32_t TY>
+__device__ __forceinline__ void gen_group(const uint8_t *r, uint32_t it, uint32_t t, uint32_t (&q)[4], float &s,
+                                          float &m)
+{
+    if (TY == 8u) {   // Q8_0: 34-byte blocks of 32 (d, int8[32])
+        const uint8_t *b = r + 34u * (2u * it + (t >> 1));
+        ld16_u2(b + 2u + 16u * (t & 1u), q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] ^= 0x80808080u;
+        s = h2f(*reinterpret_cast<const uint16_t *>(b));
+        m = -128.0f * s;
+    } else if (TY == 6u) {   // Q5_0: 22-byte blocks (d, qh u32, qs[16])
+        const uint8_t *b = r + 22u * (2u * it + (t >> 1));
+        const uint32_t half = t & 1u;
+        ld16_u2(b + 6u, q);
+        const uint32_t qh = *reinterpret_cast<const uint16_t *>(b + 2u + 2u * half);
+#pragma unroll
+        for (uint32_t i = 0; i < 4u; ++i) {
+            // bits 4i..4i+3 of the group's 16 high bits -> bit 4 of bytes 0..3
+            const uint32_t h4 = (qh >> (4u * i)) & 15u;
+            q[i] = ((q[i] >> (4u * half)) & 0x0f0f0f0fu) | (((h4 * 0x00204081u) & 0x01010101u) << 4);
+        }
+        s = h2f(*reinterpret_cast<const uint16_t *>(b));
+        m = -16.0f * s;
+    } else if (TY == 7u) {   // Q5_1: 24-byte blocks (d, m, qh u32, qs[16])
+        const uint8_t *b = r + 24u * (2u * it + (t >> 1));
+        const uint32_t half = t & 1u;
+        const uint2 w0 = *reinterpret_cast<const uint2 *>(b + 8u), w1 = *reinterpret_cast<const uint2 *>(b + 16u);
+        const uint32_t hd = *reinterpret_cast<const uint32_t *>(b);
+        const uint32_t qh = *reinterpret_cast<const uint32_t *>(b + 4u) >> (16u * half);
+        const uint32_t raw[4] = {w0.x, w0.y, w1.x, w1.y};
+#pragma unroll
+        for (uint32_t i = 0; i < 4u; ++i) {
+            const uint32_t h4 = (qh >> (4u * i)) & 15u;
+            q[i] = ((raw[i] >> (4u * half)) & 0x0f0f0f0fu) | (((h4 * 0x00204081u) & 0x01010101u) << 4);
+        }
+        s = h2f((uint16_t)(hd & 0xffffu));
+        m = h2f((uint16_t)(hd >> 16));
+    } else {   // Q5_K: the 176-byte super-block (d, dmin, scales[12], qh[32], ql[128])
+        const uint32_t hi = t >> 1, half = t & 1u, sh = 2u * it + hi;
+        const uint4 ql = *reinterpret_cast<const uint4 *>(r + 48u + 32u * it + 16u * half);
+        // the reference's qh bytes 16 + 8 c + l for chunk c = it (its pointer
+        // advances 8 bytes per 64 values), bit 2 c + hi
+        const uint2 h0 = *reinterpret_cast<const uint2 *>(r + 16u + 8u * it + 16u * half);
+        const uint2 h1 = *reinterpret_cast<const uint2 *>(r + 24u + 8u * it + 16u * half);
+        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {h0.x, h0.y, h1.x, h1.y};
+        const uint32_t rot = (4u - sh) & 31u;   // bit sh of every byte -> bit 4
+#pragma unroll
+        for (uint32_t i = 0; i < 4u; ++i)
+            q[i] = ((lw[i] >> (4u * hi)) & 0x0f0f0f0fu) | (__funnelshift_l(hw[i], hw[i], rot) & 0x10101010u);
+        const uint32_t hd = *reinterpret_cast<const uint32_t *>(r);
+        uint32_t sc, mn;
+        k4_scale_min((int)sh, r + 4, sc, mn);
+        s = h2f((uint16_t)(hd & 0xffffu)) * u2f_small(sc);
+        m = -(h2f((uint16_t)(hd >> 16)) * u2f_small(mn));
+    }
+}
+
+// One task (16 rows x 256 elements) of type TY for lane (g, t): rows g (r0)
+// and g + 8 (r1) of the slot; xb / xs: the block column's staged x groups
+// (natural element order) and 16-element sums.
+template <uint32_t TY>
+__device__ __forceinline__ void gen_task(const uint8_t *r0, const uint8_t *r1, const uint8_t *xb, const float *xs,
+                                         uint32_t lane, float &o0, float &o1)
+{
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const uint32_t podd = (g & 1u) * 8u;
+    const bool bmine = (g >> 1) == t;
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (uint32_t it = 0; it < 4u; ++it) {
+        const uint32_t G = 4u * it + t;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        if (TY == 1u) {
+            // F16: the group's 32 bytes; elements 4i, 4i + 1 in word 2i, 4i + 2, 4i + 3 in word 2i + 1
+            const uint4 u0 = *reinterpret_cast<const uint4 *>(r0 + 32u * G),
+                        u1 = *reinterpret_cast<const uint4 *>(r0 + 32u * G + 16u);
+            const uint4 v0 = *reinterpret_cast<const uint4 *>(r1 + 32u * G),
+                        v1 = *reinterpret_cast<const uint4 *>(r1 + 32u * G + 16u);
+            const uint32_t w0[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};   // row g
+            const uint32_t w1[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};   // row g + 8
+#pragma unroll
+            for (uint32_t i = 0; i < 4u; ++i) {
+                uint2 b = make_uint2(0u, 0u);
+                if (bmine) b = *reinterpret_cast<const uint2 *>(xb + (4u * G + i) * 16u + podd);
+                const float cc[4] = {c[0], c[1], c[2], c[3]};
+                mma16816(c, w0[2 * i], w1[2 * i], w0[2 * i + 1], w1[2 * i + 1], b, i == 0u ? zero : cc);
+            }
+            o0 += c[0] + c[1];
+            o1 += c[2] + c[3];
+        } else {
+            uint32_t q0[4], q1[4];
+            float s0, m0, s1, m1;
+            gen_group<TY>(r0, it, t, q0, s0, m0);
+            gen_group<TY>(r1, it, t, q1, s1, m1);
+#pragma unroll
+            for (uint32_t i = 0; i < 4u; ++i) {
+                uint2 b = make_uint2(0u, 0u);
+                if (bmine) b = *reinterpret_cast<const uint2 *>(xb + (4u * G + i) * 16u + podd);
+                const float cc[4] = {c[0], c[1], c[2], c[3]};
+                mma16816(c, sub2(q0[i], 0x4140), sub2(q1[i], 0x4140), sub2(q0[i], 0x4342), sub2(q1[i], 0x4342), b,
+                         i == 0u ? zero : cc);
+            }
+            const float sx = xs[G];
+            o0 += fmaf(s0, (c[0] + c[1]) * kTwo24, m0 * sx);
+            o1 += fmaf(s1, (c[2] + c[3]) * kTwo24, m1 * sx);
+        }
+    }
+}
+
+// Copies of one task of type TY: lane L copies row L % 16's 16-byte chunks
+// L / 16, L / 16 + 2, ...
+template <uint32_t TY>
+__device__ __forceinline__ void m4_issue_gen(const uint8_t *base, uint32_t rb, uint32_t slot, uint32_t lane)
+{
+    constexpr uint32_t NP = m4_chunk_bytes(TY) / 16u, RS = m4_gen_row(TY);
+    const uint32_t r = lane & 15u, p0 = lane >> 4;
+    const uint8_t *src = base + r * rb + 16u * p0;
+    const uint32_t dst = slot + r * RS + 16u * p0;
+#pragma unroll
+    for (uint32_t i = 0; i < (NP + 1u) / 2u; ++i)
+        if (p0 + 2u * i < NP) cp_async16_plain(dst + 32u * i, src + 32u * i);
+}
+
+template <int NS, uint32_t TY, int W>
 __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xarea, uint8_t *ring, const MvCta &c,
                            MvBest &best, uint64_t &t_ready, uint64_t *t_wait)
 {
+    constexpr bool Q4 = TY == 12u, Q6 = TY == 14u;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 2;
     const uint32_t L = c.j1 - c.j0, weff = min((uint32_t)W, L);
@@ -997,7 +1154,7 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         sg.w1 = paired ? a.seg[1].w : s0.w;
         sg.rb = (uint32_t)s0.row_bytes;
         sg.q4 = Q4 ? 1u : 0u;
-        sg.bb = Q4 ? 144u : 210u;
+        sg.bb = m4_chunk_bytes(TY);
         sg.ncp = Q4 ? 5u : 7u;
     }
     M4Cur ci{}, cc{};
@@ -1017,7 +1174,8 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
 #pragma unroll
     for (uint32_t k = 0; k + 1u < (uint32_t)NS; ++k) {
         if (k < n) {
-            m4_issue<Q4>(sg, h, ci, ring_w + k * a.slot_bytes, lane, policy);
+            if constexpr (Q4 || Q6) m4_issue<Q4>(sg, h, ci, ring_w + k * a.slot_bytes, lane, policy);
+            else m4_issue_gen<TY>(m4_block(sg, ci), sg.rb, ring_w + k * a.slot_bytes, lane);
             m4_next(ci, nb, paired);
         }
         m4_commit();
@@ -1035,7 +1193,8 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
     uint32_t si = 0, sn = (uint32_t)NS - 1u;   // slots of the consumed and of the next issued task
     for (uint32_t k = 0; k < n; ++k) {
         if (k + (uint32_t)NS - 1u < n) {
-            m4_issue<Q4>(sg, h, ci, ring_w + sn * a.slot_bytes, lane, policy);
+            if constexpr (Q4 || Q6) m4_issue<Q4>(sg, h, ci, ring_w + sn * a.slot_bytes, lane, policy);
+            else m4_issue_gen<TY>(m4_block(sg, ci), sg.rb, ring_w + sn * a.slot_bytes, lane);
             m4_next(ci, nb, paired);
         }
         m4_commit();
@@ -1047,13 +1206,15 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         const uint8_t *xb = xarea + cc.b * 1024u;
         const float *xs = xs16 + cc.b * 16u;
         float o0 = 0.f, o1 = 0.f;
-        if (Q4) {
+        if constexpr (Q4) {
             q4k_task(slot, 0u, 0u, kM4Q4Row, xb, xs, lane, o0, o1);
-        } else {
+        } else if constexpr (Q6) {
             // the block's offset inside its 16-byte-aligned window, per row
             const uint32_t lb0 = (cc.s ? wlow1 : wlow) + 16u * cc.t * sg.rb + cc.b * 210u;
             q6k_task4(slot + g * kM4Q6Row + ((lb0 + g * sg.rb) & 15u),
                       slot + (g + 8u) * kM4Q6Row + ((lb0 + (g + 8u) * sg.rb) & 15u), xb, xs, lane, o0, o1);
+        } else {
+            gen_task<TY>(slot + g * m4_gen_row(TY), slot + (g + 8u) * m4_gen_row(TY), xb, xs, lane, o0, o1);
         }
         __syncwarp();   // the slot is re-filled by a later iteration's copies
         if (cc.s) {
@@ -1068,7 +1229,8 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         if (cc.t != t || k + 1u == n) {
             const uint32_t wa = t == first_tile ? fa : (t == last_tile ? la : warp);
             const uint32_t wb = t == first_tile ? fb : (t == last_tile ? lb : warp);
-            m4_flush(a, h, part, c.seg, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
+            if constexpr (Q4 || Q6) m4_flush(a, h, part, c.seg, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
+            else m4_flush_body(a, h, part, c.seg, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
             a00 = a01 = a10 = a11 = 0.f;
         }
     }
@@ -1077,7 +1239,9 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
 // W = 16: one CTA per SM; W = 8: two CTAs fit on an SM (registers), so that
 // the next launch's CTAs become resident, and stream their first weights,
 // while this launch still runs.
-template <int NS, int W>
+// GT = 0: Q4_K and Q6_K segments (each CTA takes its segment's type); GT = one
+// of the other block types (F16, Q5_0, Q5_1, Q8_0, Q5_K): every segment has it.
+template <int NS, int W, uint32_t GT>
 __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __grid_constant__ MvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1116,8 +1280,12 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     __syncthreads();
     pdl_launch();
     MvBest best{-FLT_MAX, 0xffffffffu};
-    if (a.seg[c.seg].type == 12u) m4_consume<NS, true, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
-    else m4_consume<NS, false, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
+    if constexpr (GT != 0u) {
+        m4_consume<NS, GT, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
+    } else {
+        if (a.seg[c.seg].type == 12u) m4_consume<NS, 12u, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
+        else m4_consume<NS, 14u, W>(a, h, part, xarea, ring, c, best, t_ready, t_wait);
+    }
     cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
     if (a.epi == MV_PART) {
         // The barrier orders every thread's partial-row stores to the peers
@@ -1942,25 +2110,55 @@ const void *attn_fn(uint32_t group, bool tc = false)
 }  // namespace
 
 namespace {
-const void *mv4_fn(uint32_t nslot, uint32_t warps)
+template <uint32_t GT>
+const void *mv4_gen_fn(uint32_t nslot, uint32_t warps)
 {
     if (warps == 16u) {
         switch (nslot) {
-        case 2: return (const void *)mv4_kernel<2, 16>;
-        case 3: return (const void *)mv4_kernel<3, 16>;
-        case 4: return (const void *)mv4_kernel<4, 16>;
-        case 5: return (const void *)mv4_kernel<5, 16>;
-        case 6: return (const void *)mv4_kernel<6, 16>;
+        case 2: return (const void *)mv4_kernel<2, 16, GT>;
+        case 3: return (const void *)mv4_kernel<3, 16, GT>;
+        case 4: return (const void *)mv4_kernel<4, 16, GT>;
         default: return nullptr;
         }
     }
     if (warps == 8u) {
         switch (nslot) {
-        case 2: return (const void *)mv4_kernel<2, 8>;
-        case 3: return (const void *)mv4_kernel<3, 8>;
-        case 4: return (const void *)mv4_kernel<4, 8>;
-        case 5: return (const void *)mv4_kernel<5, 8>;
-        case 6: return (const void *)mv4_kernel<6, 8>;
+        case 2: return (const void *)mv4_kernel<2, 8, GT>;
+        case 3: return (const void *)mv4_kernel<3, 8, GT>;
+        default: return nullptr;
+        }
+    }
+    return nullptr;
+}
+
+const void *mv4_fn(uint32_t nslot, uint32_t warps, uint32_t gen_type = 0u)
+{
+    switch (gen_type) {
+    case 0u: break;
+    case 1u: return mv4_gen_fn<1u>(nslot, warps);
+    case 6u: return mv4_gen_fn<6u>(nslot, warps);
+    case 7u: return mv4_gen_fn<7u>(nslot, warps);
+    case 8u: return mv4_gen_fn<8u>(nslot, warps);
+    case 13u: return mv4_gen_fn<13u>(nslot, warps);
+    default: return nullptr;
+    }
+    if (warps == 16u) {
+        switch (nslot) {
+        case 2: return (const void *)mv4_kernel<2, 16, 0u>;
+        case 3: return (const void *)mv4_kernel<3, 16, 0u>;
+        case 4: return (const void *)mv4_kernel<4, 16, 0u>;
+        case 5: return (const void *)mv4_kernel<5, 16, 0u>;
+        case 6: return (const void *)mv4_kernel<6, 16, 0u>;
+        default: return nullptr;
+        }
+    }
+    if (warps == 8u) {
+        switch (nslot) {
+        case 2: return (const void *)mv4_kernel<2, 8, 0u>;
+        case 3: return (const void *)mv4_kernel<3, 8, 0u>;
+        case 4: return (const void *)mv4_kernel<4, 8, 0u>;
+        case 5: return (const void *)mv4_kernel<5, 8, 0u>;
+        case 6: return (const void *)mv4_kernel<6, 8, 0u>;
         default: return nullptr;
         }
     }
@@ -2010,9 +2208,12 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
     if (e != cudaSuccess) return e;
     for (uint32_t w : {8u, 16u})
         for (uint32_t ns = 2; ns <= kM4MaxSlots; ++ns)
-            if ((e = cudaFuncSetAttribute(mv4_fn(ns, w), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem)) !=
-                cudaSuccess)
-                return e;
+            for (uint32_t gt : {0u, 1u, 6u, 7u, 8u, 13u}) {
+                const void *fn = mv4_fn(ns, w, gt);
+                if (fn && (e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem)) !=
+                              cudaSuccess)
+                    return e;
+            }
     for (uint32_t g = 1; g <= kAttnMaxGroup; g *= 2u)
         if ((e = cudaFuncSetAttribute(attn_fn(g), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem)) !=
             cudaSuccess)
@@ -2030,7 +2231,7 @@ extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaSt
     MvArgs copy = *a;
     void *args[] = {&copy};
     if (a->engine == 1u) {
-        const void *fn = mv4_fn(a->nslot, a->warps);
+        const void *fn = mv4_fn(a->nslot, a->warps, a->gen_type);
         if (!fn) return cudaErrorInvalidValue;
         return launch_ex(fn, args, dim3(grid), dim3(32u * a->warps), a->smem_bytes, stream, a->pdl != 0u);
     }

@@ -111,7 +111,7 @@ enum MvEpi : uint32_t { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_LOGITS = 3
 struct MvSeg {
     const uint8_t *w;      // row 0 of the raw GGUF tensor
     uint64_t row_bytes;
-    uint32_t type;         // 12 = Q4_K, 14 = Q6_K
+    uint32_t type;         // 12 = Q4_K, 14 = Q6_K; mv4_kernel: also 1, 6, 7, 8, 13
     uint32_t rows;         // multiple of kMvRows
     const float *bias;     // optional (MV_STORE)
     float *out;
@@ -158,6 +158,7 @@ struct MvArgs {
     uint32_t engine;         // 0: mv_kernel (producer warp + shared ring); 1: mv4_kernel (per-warp rings)
     uint32_t trace_slot;     // this launch's index in the step (trace records)
     uint32_t warps;          // mv4_kernel: 8 (two CTAs per SM) or 16 warps per CTA
+    uint32_t gen_type;       // mv4_kernel: 0 (Q4_K / Q6_K segments), or the other block type of every segment
 };
 
 // ------------------------------------------------------------ mv4 kernel ----
@@ -175,6 +176,31 @@ constexpr uint32_t kM4Q4Row = 144u, kM4Q6Row = 240u;
 constexpr uint32_t kM4MaxSlots = 6u;
 // bytes past the end of a Q6_K tensor that a 224-byte window may read (14), rounded up
 constexpr uint32_t kM4Q6Overread = 48u;
+
+// The reference's other block types (F16 = 1, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8,
+// Q5_K = 13) run on the same kernel: a task copies the row's whole chunk of
+// 256 elements - 512, 176, 192, 272, 176 bytes, multiples of 16 - rows
+// m4_gen_row bytes apart (an odd multiple of 16), with 16 bytes of slack
+// after the last row for the 20-byte reads of 2-byte-aligned fields.
+__host__ __device__ constexpr uint32_t m4_chunk_bytes(uint32_t type)
+{
+    return type == 12u ? 144u : type == 14u ? 210u : type == 6u ? 176u : type == 7u ? 192u : type == 8u ? 272u :
+           type == 13u ? 176u : type == 1u ? 512u : 0u;
+}
+__host__ __device__ constexpr bool m4_other_type(uint32_t type)
+{
+    return type == 1u || type == 6u || type == 7u || type == 8u || type == 13u;
+}
+__host__ __device__ constexpr uint32_t m4_gen_row(uint32_t type)
+{
+    return (m4_chunk_bytes(type) / 16u) & 1u ? m4_chunk_bytes(type) : m4_chunk_bytes(type) + 16u;
+}
+__host__ __device__ constexpr uint32_t m4_slot_bytes(uint32_t type)
+{
+    return type == 12u ? 16u * kM4Q4Row : type == 14u ? 16u * kM4Q6Row : 16u * m4_gen_row(type) + 16u;
+}
+// ring depths of the kernels of the other types (16 warps: 2..4, 8 warps: 2..3)
+constexpr uint32_t kM4GenSlots16 = 4u, kM4GenSlots8 = 3u;
 
 // ------------------------------------------------------ attention kernel ----
 

@@ -16,6 +16,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
+#include <array>
 #include <vector>
 #include "../../include/atlas_cuda.h"
 #include "engine.h"
@@ -87,6 +89,14 @@ struct AtlasCuda {
     cudaStream_t stream = nullptr;
     std::string err;
     std::vector<void *> allocs;
+    // Pinned staging of the weight upload (creation only): host threads fill
+    // one buffer while the copy engine drains the other.
+    struct Staging {
+        uint8_t *buf[2] = {nullptr, nullptr};
+        cudaEvent_t done[2] = {nullptr, nullptr};
+        size_t cap = 0;
+        int next = 0;
+    } stg;
     // weights
     struct W {
         const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
@@ -148,6 +158,11 @@ struct AtlasCuda {
     float *x2 = nullptr;
     uint32_t *d_in_ids = nullptr;
     uint32_t in_cap = 0;
+    // Matrices of the reference's other block types (F16, Q5_0, Q5_1, Q8_0,
+    // Q5_K): the graph decode step only, prompts replayed through it token by
+    // token (prompt mode); the batched prefill's tensor-core contractions take
+    // Q4_K / Q6_K.
+    bool other_types = false;
     uint32_t pf_seq = 0;   // prefill all-reduces run so far (their exchange occurrence numbers)
     bool broken = false;   // a failed tensor-parallel step left the ranks out of step
 };
@@ -207,6 +222,64 @@ int dalloc(AtlasCuda *h, T **out, size_t bytes)
     return ATLAS_OK;
 }
 
+// Host bytes -> device. Large copies go through the pinned staging buffers in
+// chunks: host threads copy chunk i into one buffer while chunk i - 1's
+// transfer runs from the other (a pageable cudaMemcpy stages through the
+// driver's own small buffers one at a time).
+int upload(AtlasCuda *h, void *dst, const void *src, size_t bytes)
+{
+    AtlasCuda::Staging &st = h->stg;
+    if (!st.cap || bytes < (size_t(4) << 20)) {
+        CU(h, cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+        return ATLAS_OK;
+    }
+    const unsigned nt = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    for (size_t off = 0; off < bytes; off += st.cap) {
+        const size_t n = std::min(st.cap, bytes - off);
+        const int i = st.next;
+        st.next ^= 1;
+        CU(h, cudaEventSynchronize(st.done[i]));   // the buffer's previous transfer has finished
+        const uint8_t *s0 = static_cast<const uint8_t *>(src) + off;
+        std::vector<std::thread> pool;
+        const size_t per = (n / nt + 4095) & ~size_t(4095);
+        for (unsigned t = 0; t < nt; ++t) {
+            const size_t a = std::min(n, t * per), b = std::min(n, a + per);
+            if (a < b) pool.emplace_back([&st, i, s0, a, b] { memcpy(st.buf[i] + a, s0 + a, b - a); });
+        }
+        for (std::thread &th : pool) th.join();
+        CU(h, cudaMemcpyAsync(static_cast<uint8_t *>(dst) + off, st.buf[i], n, cudaMemcpyHostToDevice, h->stream));
+        CU(h, cudaEventRecord(st.done[i], h->stream));
+    }
+    return ATLAS_OK;
+}
+
+void staging_open(AtlasCuda *h)
+{
+    AtlasCuda::Staging &st = h->stg;
+    const size_t cap = size_t(64) << 20;
+    for (int i = 0; i < 2; ++i) {
+        if (cudaHostAlloc(reinterpret_cast<void **>(&st.buf[i]), cap, cudaHostAllocDefault) != cudaSuccess ||
+            cudaEventCreateWithFlags(&st.done[i], cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return;   // plain pageable copies (cap stays 0)
+        }
+    }
+    st.cap = cap;
+}
+
+void staging_close(AtlasCuda *h)
+{
+    AtlasCuda::Staging &st = h->stg;
+    if (st.cap) cudaStreamSynchronize(h->stream);
+    for (int i = 0; i < 2; ++i) {
+        if (st.buf[i]) cudaFreeHost(st.buf[i]);
+        if (st.done[i]) cudaEventDestroy(st.done[i]);
+        st.buf[i] = nullptr;
+        st.done[i] = nullptr;
+    }
+    st.cap = 0;
+}
+
 const AtlasTensorDesc *find(const AtlasTensorDesc *t, uint32_t n, const char *name)
 {
     for (uint32_t i = 0; i < n; ++i)
@@ -256,22 +329,26 @@ const char *tp_slice_of(const AtlasModelDesc &d, int rank, int size, AtlasTpSlic
     return nullptr;
 }
 
-// Rows [row0, row0 + nrows) and 256-column blocks [b0, b0 + nblk) of a matrix
-// tensor [rows x cols] of a supported GEMV type. The blocks are uploaded
-// unchanged; a block-column slice (a tensor-parallel rank's share of a
-// row-split projection) is packed row after row.
+// Rows [row0, row0 + nrows) and 256-column chunks [b0, b0 + nblk) of a matrix
+// tensor [rows x cols] of a GEMV type (Q4_K, Q6_K; F16, Q5_0, Q5_1, Q8_0,
+// Q5_K). The blocks are uploaded unchanged; a chunk-column slice (a
+// tensor-parallel rank's share of a row-split projection) is packed row after
+// row.
 int upload_matrix_part(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, uint64_t rows, uint64_t row0,
                        uint64_t nrows, uint64_t b0, uint64_t nblk, const uint8_t **dev, uint32_t *type)
 {
     if (!t) return fail(h, ATLAS_EINVAL, "missing matrix tensor");
-    if (t->type != ATLAS_TYPE_Q4_K && t->type != ATLAS_TYPE_Q6_K)
-        return fail(h, ATLAS_EINVAL, "%s: tensor type %u is not supported by the decode engine (Q4_K, Q6_K)",
+    if (t->type != ATLAS_TYPE_Q4_K && t->type != ATLAS_TYPE_Q6_K && !d2::m4_other_type(t->type))
+        return fail(h, ATLAS_EINVAL,
+                    "%s: tensor type %u is not supported by the decode engine (F16, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, "
+                    "Q6_K)",
                     t->name, t->type);
     if (t->n_dims != 2 || t->dims[0] != cols || t->dims[1] != rows || cols % 256)
         return fail(h, ATLAS_EINVAL, "%s: dims %llu x %llu, expected %llu x %llu", t->name,
                     (unsigned long long)t->dims[0], (unsigned long long)t->dims[1], (unsigned long long)cols,
                     (unsigned long long)rows);
-    const uint64_t nb = cols / 256, bb = block_bytes(t->type), rb = nb * bb;
+    // bb: bytes of one row's 256 elements
+    const uint64_t nb = cols / 256, bb = 256u / block_elems(t->type) * block_bytes(t->type), rb = nb * bb;
     if (row0 + nrows > rows || b0 + nblk > nb || !nrows || !nblk) return fail(h, ATLAS_EINVAL, "%s: bad slice", t->name);
     const uint64_t bytes = nrows * nblk * bb;
     uint8_t *d = nullptr;
@@ -281,11 +358,11 @@ int upload_matrix_part(AtlasCuda *h, const AtlasTensorDesc *t, uint64_t cols, ui
     if (rc) return rc;
     const uint8_t *src = static_cast<const uint8_t *>(t->data) + row0 * rb;
     if (nblk == nb) {
-        CU(h, cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice));
+        if ((rc = upload(h, d, src, bytes))) return rc;
     } else {
         std::vector<uint8_t> tmp(bytes);
         for (uint64_t r = 0; r < nrows; ++r) memcpy(&tmp[r * nblk * bb], src + r * rb + b0 * bb, nblk * bb);
-        CU(h, cudaMemcpy(d, tmp.data(), bytes, cudaMemcpyHostToDevice));
+        if ((rc = upload(h, d, tmp.data(), bytes))) return rc;
     }
     *dev = d;
     *type = t->type;
@@ -545,7 +622,7 @@ d2::MvSeg mvseg(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, c
     s.w = w;
     s.type = type;
     s.rows = rows;
-    s.row_bytes = (uint64_t)(cols / 256u) * block_bytes(type);
+    s.row_bytes = (uint64_t)(cols / block_elems(type)) * block_bytes(type);
     s.bias = bias;
     s.out = out;
     return s;
@@ -587,18 +664,24 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     a.nb = cols / 256u;
     a.paired = paired ? 1u : 0u;
     a.epi = epi;
+    bool other = false;   // a segment of another block type: mv4_kernel's all-types variant
     for (const d2::MvSeg &sg : segs) {
         if (a.n_seg == 3) return fail(h, ATLAS_EINVAL, "mv: too many segments");
-        if ((sg.type != 12u && sg.type != 14u) || sg.rows % (uint32_t)d2::kMvRows || !sg.rows)
+        const bool ok_type = sg.type == 12u || sg.type == 14u || d2::m4_other_type(sg.type);
+        if (!ok_type || sg.rows % (uint32_t)d2::kMvRows || !sg.rows)
             return fail(h, ATLAS_EINVAL, "mv: segment type %u rows %u unsupported", sg.type, sg.rows);
-        if (sg.type == 12u && (reinterpret_cast<uintptr_t>(sg.w) & 15u))
-            return fail(h, ATLAS_EINVAL, "mv: Q4_K tensor not 16-byte aligned");
+        if (sg.type != 14u && (reinterpret_cast<uintptr_t>(sg.w) & 15u))
+            return fail(h, ATLAS_EINVAL, "mv: type %u tensor not 16-byte aligned", sg.type);
+        other = other || d2::m4_other_type(sg.type);
         a.seg[a.n_seg] = sg;
         a.seg[a.n_seg].copies = mv_copies(sg.row_bytes);
         ++a.n_seg;
     }
     if (!cols || cols % 256u || (paired && (a.n_seg != 2 || a.seg[0].rows != a.seg[1].rows)))
         return fail(h, ATLAS_EINVAL, "mv: bad shape");
+    if (paired && a.seg[0].type != a.seg[1].type)
+        return fail(h, ATLAS_EINVAL, "mv: gate and up of types %u and %u (one type per pair)", a.seg[0].type,
+                    a.seg[1].type);
     const uint32_t G = (uint32_t)h->sm_count;
     const uint32_t P = paired ? 2u : 1u, TP = a.nb * P;
     std::vector<uint32_t> cta_n, tiles;
@@ -656,7 +739,7 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     // blocks long (a bulk copy costs the copy engine tens of nanoseconds
     // whatever its size), giving up co-residency with their neighbours.
     const uint32_t budgets[2] = {a.nb > 8u ? 227u * 1024u : kHalfSmBytes, 227u * 1024u};
-    bool ok = false;
+    bool ok = other;   // mv_kernel takes Q4_K and Q6_K only: no plan of its own then
     // The largest slot wins (per-slot costs - descriptors, copy issue,
     // barrier round trips - dominate small slots), on the whole SM if it
     // must: mv CTAs do not share an SM anyway (registers)
@@ -694,8 +777,31 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
         if (ok) break;
     }
     if (!ok) return fail(h, ATLAS_EINVAL, "mv: no shared-memory plan for %u columns", cols);
-    a.smem_bytes = (uint32_t)atlas_d2_mv_smem(cols, a.nslot, a.slot_bytes, a.tslots);
-    if (kMvEngine == 1u) {
+    if (!other) a.smem_bytes = (uint32_t)atlas_d2_mv_smem(cols, a.nslot, a.slot_bytes, a.tslots);
+    if (other) {
+        // the kernel of that one type: 16 warps with up to 4 slots, else 8
+        // warps with up to 3 (F16 tasks take 8 KB a slot)
+        for (uint32_t s = 1; s < a.n_seg; ++s)
+            if (a.seg[s].type != a.seg[0].type)
+                return fail(h, ATLAS_EINVAL, "mv: a launch of type %u with a segment of type %u", a.seg[0].type,
+                            a.seg[s].type);
+        const uint32_t slot = d2::m4_slot_bytes(a.seg[0].type);
+        a.engine = 0u;
+        for (const uint32_t warps : {16u, 8u}) {
+            const uint32_t top = warps == 16u ? d2::kM4GenSlots16 : d2::kM4GenSlots8;
+            for (uint32_t ns = top; ns >= 2u && !a.engine; --ns)
+                if (atlas_d2_mv4_smem(cols, warps, ns, slot) <= 227u * 1024u) {
+                    a.engine = 1u;
+                    a.gen_type = a.seg[0].type;
+                    a.warps = warps;
+                    a.nslot = ns;
+                    a.slot_bytes = slot;
+                    a.smem_bytes = (uint32_t)atlas_d2_mv4_smem(cols, warps, ns, slot);
+                }
+            if (a.engine) break;
+        }
+        if (!a.engine) return fail(h, ATLAS_EINVAL, "mv: no shared-memory plan for %u columns", cols);
+    } else if (kMvEngine == 1u) {
         // per-warp rings (mv4_kernel): 16 warps with the deepest ring the SM
         // holds (at least 2 slots). The kernel is bound by instruction issue,
         // so all 16 warps stay busy: 8-warp CTAs that let the next launch's
@@ -736,6 +842,106 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
     return ATLAS_OK;
 }
 
+// Layer l's launch of a planned shape: the layer-0 plan with the layer's
+// weight pointers when its matrices have layer 0's types, else the plan of
+// the layer's own types (a Q4_K_M file mixes Q4_K and Q6_K across layers)
+// with the launch's other fields kept. Plans of a type combination are made
+// once (cache).
+int layer_plan(AtlasCuda *h, const MvPlan &p0, bool paired, std::initializer_list<d2::MvSeg> segs, MvPlan &out,
+               std::vector<std::pair<std::vector<uint32_t>, MvPlan>> &cache)
+{
+    out = p0;
+    std::vector<uint32_t> key{p0.a.cols, p0.a.epi, paired ? 1u : 0u};
+    bool same = true;
+    uint32_t i = 0;
+    for (const d2::MvSeg &sg : segs) {
+        out.a.seg[i].w = sg.w;
+        out.a.seg[i].bias = sg.bias;
+        same = same && sg.type == p0.a.seg[i].type;
+        key.push_back(sg.type);
+        key.push_back(sg.rows);
+        ++i;
+    }
+    if (same) return ATLAS_OK;
+    const MvPlan *fresh = nullptr;
+    for (const auto &e : cache)
+        if (e.first == key) fresh = &e.second;
+    if (!fresh) {
+        MvPlan p;
+        const int rc = plan_mv(h, p, p0.a.cols, paired, segs, p0.a.epi);
+        if (rc) return rc;
+        cache.emplace_back(key, p);
+        fresh = &cache.back().second;
+    }
+    if (p0.a.epi == d2::MV_PART && fresh->grid != p0.grid)
+        return fail(h, ATLAS_EINVAL, "tensor parallel: layer types change the grid of a row-split launch");
+    for (uint32_t s = 0; s < p0.a.n_seg; ++s) {
+        out.a.seg[s].type = fresh->a.seg[s].type;
+        out.a.seg[s].row_bytes = fresh->a.seg[s].row_bytes;
+        out.a.seg[s].copies = fresh->a.seg[s].copies;
+    }
+    out.a.st = fresh->a.st;
+    out.a.nslot = fresh->a.nslot;
+    out.a.slot_bytes = fresh->a.slot_bytes;
+    out.a.tslots = fresh->a.tslots;
+    out.a.smem_bytes = fresh->a.smem_bytes;
+    out.a.cta = fresh->a.cta;
+    out.a.engine = fresh->a.engine;
+    out.a.warps = fresh->a.warps;
+    out.a.gen_type = fresh->a.gen_type;
+    out.grid = fresh->grid;
+    return ATLAS_OK;
+}
+
+// Kernel family of a block type: Q4_K and Q6_K share mv4_kernel's dispatch,
+// every other type has a kernel of its own.
+uint32_t mv_family(uint32_t type) { return d2::m4_other_type(type) ? type : 0u; }
+
+// Layer l's q/k/v projections as one launch per kernel family among the
+// three matrices (a file may keep attn_q in Q8_0 and attn_k / attn_v in
+// Q4_K / Q6_K); x and the step state are the decode step's.
+int split_qkv(AtlasCuda *h, const d2::MvSeg (&sg)[3], std::vector<MvPlan> &out,
+              std::vector<std::pair<std::vector<uint32_t>, MvPlan>> &cache)
+{
+    out.clear();
+    bool done[3] = {false, false, false};
+    for (uint32_t i = 0; i < 3; ++i) {
+        if (done[i]) continue;
+        std::vector<d2::MvSeg> grp;
+        std::vector<uint32_t> key{h->desc.hidden, (uint32_t)d2::MV_STORE, 0u};
+        for (uint32_t j = i; j < 3; ++j)
+            if (!done[j] && mv_family(sg[j].type) == mv_family(sg[i].type)) {
+                grp.push_back(sg[j]);
+                key.push_back(sg[j].type);
+                key.push_back(sg[j].rows);
+                done[j] = true;
+            }
+        const MvPlan *fresh = nullptr;
+        for (const auto &e : cache)
+            if (e.first == key) fresh = &e.second;
+        if (!fresh) {
+            MvPlan p;
+            int rc = ATLAS_OK;
+            if (grp.size() == 1) rc = plan_mv(h, p, h->desc.hidden, false, {grp[0]}, d2::MV_STORE);
+            else if (grp.size() == 2) rc = plan_mv(h, p, h->desc.hidden, false, {grp[0], grp[1]}, d2::MV_STORE);
+            else rc = plan_mv(h, p, h->desc.hidden, false, {grp[0], grp[1], grp[2]}, d2::MV_STORE);
+            if (rc) return rc;
+            cache.emplace_back(key, p);
+            fresh = &cache.back().second;
+        }
+        MvPlan p = *fresh;
+        for (size_t k = 0; k < grp.size(); ++k) {
+            p.a.seg[k].w = grp[k].w;
+            p.a.seg[k].bias = grp[k].bias;
+            p.a.seg[k].out = grp[k].out;
+        }
+        p.a.x = h->x;
+        p.a.dstate = h->g2.st;
+        out.push_back(p);
+    }
+    return ATLAS_OK;
+}
+
 // Capture one decode step as a CUDA graph of PDL-chained kernels. With
 // tensor parallelism the shapes are the rank's slice; o and down push partial
 // rows (MV_PART) that the next kernel's staging sums in rank order, with the
@@ -764,7 +970,6 @@ int build_graph2(AtlasCuda *h)
     g.attn_tc = d.kv_fp16 && !(tce && atoi(tce) == 0);
     const int max_cl = atlas_d2_attn_max_clusters(group, g.attn_tc ? 1u : 0u);
     if (max_cl > 0) g.splits = std::max(C, std::min(g.splits, (uint32_t)max_cl * 3u / 4u / sl.kv_heads * C));
-    if (const char *e = getenv("ATLAS_ATTN_SPLITS")) g.splits = std::max(C, std::min(160u, (uint32_t)atoi(e)) / C * C);
     if ((rc = dalloc(h, &g.apart, (size_t)sl.kv_heads * (g.splits / C) * group * d2::kRec * sizeof(float)))) return rc;
     if ((rc = dalloc(h, &g.actr, (size_t)sl.q_heads * 4u))) return rc;
     CU(h, cudaMemset(g.actr, 0, (size_t)sl.q_heads * 4u));
@@ -773,7 +978,11 @@ int build_graph2(AtlasCuda *h)
     const uint32_t o_cols = sl.o_blocks * 256u;
     const uint32_t part = tp > 1 ? (uint32_t)d2::MV_PART : (uint32_t)d2::MV_RESID;
     MvPlan qkv, o, gu, dn, hd;
-    if ((rc = plan_mv(h, qkv, d.hidden, false,
+    // q, k and v in one launch when one kernel takes all three (always under
+    // tensor parallelism: Q4_K / Q6_K files only)
+    const bool qkv_one0 = mv_family(w0.tq) == mv_family(w0.tk) && mv_family(w0.tk) == mv_family(w0.tv);
+    if (qkv_one0 &&
+        (rc = plan_mv(h, qkv, d.hidden, false,
                       {mvseg(w0.q, w0.tq, lq, d.hidden, w0.bq, h->q), mvseg(w0.k, w0.tk, lkv, d.hidden, w0.bk, h->k),
                        mvseg(w0.v, w0.tv, lkv, d.hidden, w0.bv, h->v)},
                       d2::MV_STORE)))
@@ -842,6 +1051,36 @@ int build_graph2(AtlasCuda *h)
         mv_smem = std::max<size_t>(mv_smem, p->a.smem_bytes);
         p->a.dstate = g.st;   // the step's state (tensor-parallel epoch, trace pointer)
     }
+    // every layer's launches: q/k/v (one per kernel family), o, gate/up, down
+    std::vector<std::array<MvPlan, 4>> lp(d.layers);
+    std::vector<std::vector<MvPlan>> lqkv(d.layers);
+    {
+        std::vector<std::pair<std::vector<uint32_t>, MvPlan>> cache;
+        for (uint32_t l = 0; l < d.layers; ++l) {
+            const AtlasCuda::W &w = h->layers[l];
+            const d2::MvSeg qs[3] = {mvseg(w.q, w.tq, lq, d.hidden, w.bq, h->q), mvseg(w.k, w.tk, lkv, d.hidden, w.bk, h->k),
+                                     mvseg(w.v, w.tv, lkv, d.hidden, w.bv, h->v)};
+            const bool one = mv_family(w.tq) == mv_family(w.tk) && mv_family(w.tk) == mv_family(w.tv);
+            if (one && qkv_one0) {
+                MvPlan p;
+                if ((rc = layer_plan(h, qkv, false, {qs[0], qs[1], qs[2]}, p, cache))) return rc;
+                lqkv[l].push_back(p);
+            } else {
+                if (tp > 1) return fail(h, ATLAS_EINVAL, "tensor parallel: q, k, v of one kernel family only");
+                if ((rc = split_qkv(h, qs, lqkv[l], cache))) return rc;
+            }
+            for (const MvPlan &p : lqkv[l]) mv_smem = std::max<size_t>(mv_smem, p.a.smem_bytes);
+            if ((rc = layer_plan(h, o, false, {mvseg(w.o, w.to, d.hidden, o_cols, nullptr, h->x)}, lp[l][1], cache)) ||
+                (rc = layer_plan(h, gu, true,
+                                 {mvseg(w.gate, w.tg, sl.ffn_rows, d.hidden, nullptr, h->ffn),
+                                  mvseg(w.up, w.tu, sl.ffn_rows, d.hidden, nullptr, nullptr)},
+                                 lp[l][2], cache)) ||
+                (rc = layer_plan(h, dn, false, {mvseg(w.down, w.td, d.hidden, sl.ffn_rows, nullptr, h->x)}, lp[l][3],
+                                 cache)))
+                return rc;
+            for (const MvPlan &p : lp[l]) mv_smem = std::max<size_t>(mv_smem, p.a.smem_bytes);
+        }
+    }
     CU(h, atlas_d2_setup(mv_smem, atlas_d2_attn_smem(g.splits)));
 
     d2::AttnArgs at{};
@@ -869,45 +1108,41 @@ int build_graph2(AtlasCuda *h)
     ++kernels;
     for (uint32_t l = 0; l < d.layers && e == cudaSuccess; ++l) {
         const AtlasCuda::W &w = h->layers[l];
-        d2::MvArgs a = qkv.a;
-        a.seg[0].w = w.q; a.seg[0].bias = w.bq;
-        a.seg[1].w = w.k; a.seg[1].bias = w.bk;
-        a.seg[2].w = w.v; a.seg[2].bias = w.bv;
-        a.norm_w = w.attn_norm;
-        if (tp > 1 && l > 0) {
-            // x = x2 + the down partials of layer l - 1 (occurrence epoch * L + l)
-            const d2::TpLayout xl = d2::tp_layout(tp, d.hidden);
-            a.x = h->x2;
-            a.in_red = xl.red_dn;
-            a.in_cnt = d2::kTpCntDn;
-            a.in_arrivals = arr_dn;
-            a.seq_add = l;
-            a.xout = h->x;
+        d2::MvArgs a{};
+        for (const MvPlan &p : lqkv[l]) {
+            a = p.a;
+            a.norm_w = w.attn_norm;
+            if (tp > 1 && l > 0) {
+                // x = x2 + the down partials of layer l - 1 (occurrence epoch * L + l)
+                const d2::TpLayout xl = d2::tp_layout(tp, d.hidden);
+                a.x = h->x2;
+                a.in_red = xl.red_dn;
+                a.in_cnt = d2::kTpCntDn;
+                a.in_arrivals = arr_dn;
+                a.seq_add = l;
+                a.xout = h->x;
+            }
+            a.trace_slot = kernels++;
+            if ((e = atlas_d2_launch_mv(&a, p.grid, h->stream)) != cudaSuccess) break;
         }
-        a.trace_slot = kernels;
-        if ((e = atlas_d2_launch_mv(&a, qkv.grid, h->stream)) != cudaSuccess) break;
+        if (e != cudaSuccess) break;
         at.k_cache = w.kc;
         at.v_cache = w.vc;
         at.q_norm = w.qn;
         at.k_norm = w.kn;
-        at.trace_slot = kernels + 1u;
+        at.trace_slot = kernels++;
         if ((e = atlas_d2_launch_attn(&at, sl.kv_heads * g.splits, h->stream)) != cudaSuccess) break;
-        a = o.a;
-        a.seg[0].w = w.o;
-        a.trace_slot = kernels + 2u;
-        if ((e = atlas_d2_launch_mv(&a, o.grid, h->stream)) != cudaSuccess) break;
-        a = gu.a;
-        a.seg[0].w = w.gate;
-        a.seg[1].w = w.up;
+        a = lp[l][1].a;
+        a.trace_slot = kernels++;
+        if ((e = atlas_d2_launch_mv(&a, lp[l][1].grid, h->stream)) != cudaSuccess) break;
+        a = lp[l][2].a;
         a.norm_w = w.ffn_norm;
         a.seq_add = l + 1u;
-        a.trace_slot = kernels + 3u;
-        if ((e = atlas_d2_launch_mv(&a, gu.grid, h->stream)) != cudaSuccess) break;
-        a = dn.a;
-        a.seg[0].w = w.down;
-        a.trace_slot = kernels + 4u;
-        if ((e = atlas_d2_launch_mv(&a, dn.grid, h->stream)) != cudaSuccess) break;
-        kernels += 5;
+        a.trace_slot = kernels++;
+        if ((e = atlas_d2_launch_mv(&a, lp[l][2].grid, h->stream)) != cudaSuccess) break;
+        a = lp[l][3].a;
+        a.trace_slot = kernels++;
+        if ((e = atlas_d2_launch_mv(&a, lp[l][3].grid, h->stream)) != cudaSuccess) break;
     }
     if (e == cudaSuccess) {
         hd.a.trace_slot = kernels;
@@ -1047,10 +1282,8 @@ int build_decode_program(AtlasCuda *h)
     }
     Phase hd = gemv_phase(d.hidden, G, SB, false, {seg_of(h->head, h->t_head, d.vocab, d.hidden, nullptr, h->logits)}, h->x,
                           IN_RMSNORM, h->out_norm, EPI_LOGITS);
-    // one (max, argmax) partial per CTA that holds head items
-    int rc = dalloc(h, &h->pmax, (size_t)G * sizeof(float));
-    if (rc) return rc;
-    if ((rc = dalloc(h, &h->pidx, (size_t)G * sizeof(uint32_t)))) return rc;
+    // one (max, argmax) partial per CTA that holds head items (allocated at creation)
+    int rc = ATLAS_OK;
     hd.partial_max = h->pmax;
     hd.partial_idx = h->pidx;
     const uint32_t head_index = (uint32_t)P.size();
@@ -1296,7 +1529,6 @@ int plan_attention(AtlasCuda *h, uint32_t n, uint32_t pos0, pf::AttnArgs &a)
         span_chunks = 1;
         while (span_chunks < max_chunks && units(span_chunks) > G) ++span_chunks;
     }
-    if (const char *e = getenv("ATLAS_PF_ATTN_SPAN_CHUNKS")) span_chunks = (uint32_t)std::max(1, atoi(e));
     std::vector<uint32_t> tab;
     for (;;) {
         tab.clear();
@@ -1453,6 +1685,7 @@ void atlas_cuda_destroy(AtlasCuda *h)
 {
     if (!h) return;
     if (h->stream) cudaStreamSynchronize(h->stream);
+    staging_close(h);
     if (h->g2.exec) cudaGraphExecDestroy(h->g2.exec);
     if (h->g2.graph) cudaGraphDestroy(h->g2.graph);
     for (int r = 0; r < (int)d2::kTpMax; ++r)
@@ -1501,13 +1734,14 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     cudaEventCreate(&h->ev0);
     cudaEventCreate(&h->ev1);
     char name[96];
+    staging_open(h);
     const AtlasTensorDesc *emb = find(tensors, n_tensors, "token_embd.weight");
     if (!emb) TRY(fail(h, ATLAS_EINVAL, "missing token_embd.weight"));
     TRY(upload_matrix(h, emb, d.hidden, d.vocab, &h->embd, &h->t_embd));
     const AtlasTensorDesc *outw = find(tensors, n_tensors, "output.weight");
     if (!outw || (outw->data == emb->data && outw->type == emb->type)) {
         // tied embeddings: one device copy (a rank's head rows are a row range of it)
-        h->head = h->embd + (uint64_t)sl.vocab_row0 * (d.hidden / 256u) * block_bytes(h->t_embd);
+        h->head = h->embd + (uint64_t)sl.vocab_row0 * (d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
         h->t_head = h->t_embd;
     } else {
         TRY(upload_matrix_part(h, outw, d.hidden, d.vocab, sl.vocab_row0, sl.vocab_rows, 0, d.hidden / 256u,
@@ -1546,9 +1780,22 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
 #undef TN
         TRY(dalloc(h, &w.kc, kv_layer));
         TRY(dalloc(h, &w.vc, kv_layer));
+        for (uint32_t ty : {w.tq, w.tk, w.tv, w.to, w.tg, w.tu, w.td})
+            if (d2::m4_other_type(ty)) h->other_types = true;
+    }
+    staging_close(h);   // every matrix is on the device (the stream is drained)
+    if (d2::m4_other_type(h->t_head)) h->other_types = true;
+    if (h->other_types && tp > 1)
+        TRY(fail(h, ATLAS_EINVAL, "tensor parallel: Q4_K / Q6_K matrices only (the batched prefill is sliced)"));
+    if (h->other_types) {
+        TRY(dalloc(h, &h->d_in_ids, (size_t)d.max_context * 4));
+        h->in_cap = d.max_context;
     }
     uint32_t big = d.ffn > d.q_dim ? d.ffn : d.q_dim;
     if (d.hidden > big) big = d.hidden;
+    // the head's per-CTA (max, row) partials: one per SM, for every engine
+    TRY(dalloc(h, &h->pmax, (size_t)sms * sizeof(float)));
+    TRY(dalloc(h, &h->pidx, (size_t)sms * sizeof(uint32_t)));
     TRY(dalloc(h, &h->x, d.hidden * 4));
     TRY(dalloc(h, &h->q, lq * 4));
     TRY(dalloc(h, &h->k, lkv * 4));
@@ -1595,14 +1842,16 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
         if (cudaMemcpy(h->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
             TRY(fail(h, ATLAS_ECUDA, "rope upload failed"));
     }
-    if (tp == 1) {
+    if (tp == 1 && h->other_types) {
+        TRY(build_graph2(h));
+    } else if (tp == 1) {
         TRY(build_decode_program(h));
         // graph decode step unless the persistent decode kernel is asked for
         // (qwen3's q/k norm exists in the graph step only)
         const char *eng = getenv("ATLAS_DECODE_ENGINE");
         if (!eng || strcmp(eng, "persistent") != 0 || d.has_qk_norm) TRY(build_graph2(h));
     }
-    TRY(alloc_prefill(h));
+    if (!h->other_types) TRY(alloc_prefill(h));
     // tensor parallel: the decode step is built by atlas_cuda_tp_connect
     if (cudaDeviceSynchronize() != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "device sync failed"));
 #undef TRY
@@ -1663,6 +1912,21 @@ int atlas_cuda_prefill(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t p
     for (uint32_t i = 0; i < n; ++i)
         if (ids[i] >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab %u", ids[i], h->desc.vocab);
     if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    if (h->other_types) {
+        // the decode step replayed over the prompt (prompt mode: each step's
+        // token is the next prompt token), as the reference's prompt loop
+        // runs forward_token per token (src/brain_runtime.c:2025-2028)
+        CU(h, cudaMemcpyAsync(h->d_in_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, h->stream));
+        uint32_t next = 0;
+        const int rc = run_graph2(h, ids[0], pos0, n, nullptr, &next, nullptr, h->d_in_ids, n);
+        if (rc) return rc;
+        if (last_logits) {
+            CU(h, cudaMemcpyAsync(last_logits, h->logits, (size_t)h->desc.vocab * 4, cudaMemcpyDeviceToHost, h->stream));
+            CU(h, cudaStreamSynchronize(h->stream));
+        }
+        if (argmax) *argmax = next;
+        return ATLAS_OK;
+    }
     if (h->tp > 1) {
         // tensor parallel: all but the last token through the batched
         // contractions (partial rows all-reduced over peer memory), then the
@@ -1789,8 +2053,8 @@ int atlas_cuda_trace_step(AtlasCuda *h, uint32_t id, uint32_t pos, uint64_t *out
                           uint32_t *n_phases, uint32_t *phase_kinds)
 {
     if (!h) return fail(h, ATLAS_EINVAL, "null handle");
-    if (h->tp > 1 || h->desc.has_qk_norm)
-        return fail(h, ATLAS_EINVAL, "tracing covers the single-GPU persistent engine (qwen2) only");
+    if (h->tp > 1 || h->desc.has_qk_norm || h->other_types)
+        return fail(h, ATLAS_EINVAL, "tracing covers the single-GPU persistent engine (qwen2, Q4_K / Q6_K) only");
     const size_t np = h->decode.phases.size(), per = (size_t)h->sm_count * np, need = per * 12;
     if (n_ctas) *n_ctas = (uint32_t)h->sm_count;
     if (n_phases) *n_phases = (uint32_t)np;

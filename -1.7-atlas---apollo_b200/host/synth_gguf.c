@@ -17,8 +17,27 @@
 #include <stdlib.h>
 #include <string.h>
 
-enum { T_F32 = 0, T_Q4K = 12, T_Q6K = 14 };
+enum { T_F32 = 0, T_F16 = 1, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q4K = 12, T_Q5K = 13, T_Q6K = 14 };
 enum { Q4K_BYTES = 144, Q6K_BYTES = 210, QK = 256, ALIGN = 32 };
+
+/* ggml block geometry of the types the writer emits (src/brain_runtime.c:117-136) */
+static uint32_t blk_elems(uint32_t t)
+{
+    return t == T_F16 ? 1u : (t == T_Q5_0 || t == T_Q5_1 || t == T_Q8_0) ? 32u : (t == T_F32 ? 1u : 256u);
+}
+static uint32_t blk_bytes(uint32_t t)
+{
+    switch (t) {
+    case T_F16: return 2u;
+    case T_Q5_0: return 22u;
+    case T_Q5_1: return 24u;
+    case T_Q8_0: return 34u;
+    case T_Q4K: return Q4K_BYTES;
+    case T_Q5K: return 176u;
+    case T_Q6K: return Q6K_BYTES;
+    default: return 0u;
+    }
+}
 
 /* ---------------- counter-based random numbers ---------------- */
 
@@ -114,6 +133,25 @@ static void gen_q6k_block(Rng *r, uint8_t *b)
     }
     uint16_t d = scale_f16(r);
     memcpy(b + 208, &d, 2);
+}
+
+/* Blocks of the other types: scale fields as Q4_K's d, every other byte uniform. */
+static void gen_other_block(Rng *r, uint32_t type, uint8_t *b)
+{
+    if (type == T_F16) {
+        uint16_t h = f32_to_f16((float)(-0.05 + 0.1 * rng_uniform(r)));
+        memcpy(b, &h, 2);
+        return;
+    }
+    uint16_t d = scale_f16(r);
+    memcpy(b, &d, 2);
+    uint32_t head = 2;
+    if (type == T_Q5_1 || type == T_Q5K) {   /* m / dmin */
+        uint16_t m = scale_f16(r);
+        memcpy(b + 2, &m, 2);
+        head = 4;
+    }
+    fill_bytes(r, b + head, blk_bytes(type) - head);
 }
 
 void atlas_synth_q4k_blocks(uint64_t seed, uint64_t stream, uint8_t *dst, uint64_t n)
@@ -240,8 +278,7 @@ typedef struct {
 static uint64_t tensor_bytes(uint32_t type, uint64_t cols, uint64_t rows)
 {
     if (type == T_F32) return cols * rows * 4u;
-    uint64_t blocks = cols / QK * rows;
-    return blocks * (type == T_Q4K ? Q4K_BYTES : Q6K_BYTES);
+    return cols / blk_elems(type) * rows * blk_bytes(type);
 }
 
 static int build_plan(const AtlasSynthConfig *c, Plan **out, int *count)
@@ -257,9 +294,10 @@ static int build_plan(const AtlasSynthConfig *c, Plan **out, int *count)
         p[k].n_dims = (ROWS) == 1 ? 1u : 2u; p[k].alias_of = -1;            \
         p[k].init = INIT; ++k;                                              \
     } while (0)
-    ADD("token_embd.weight", T_Q6K, H, c->vocab, 0);
+    const uint32_t alt = (uint32_t)c->alt_type;
+    ADD("token_embd.weight", (alt && c->tied) ? alt : T_Q6K, H, c->vocab, 0);
     ADD("output_norm.weight", T_F32, H, 1, 1);
-    ADD("output.weight", T_Q6K, H, c->vocab, 0);
+    ADD("output.weight", alt ? alt : T_Q6K, H, c->vocab, 0);   /* tied: an alias of token_embd, same type */
     if (c->tied) p[k - 1].alias_of = 0;
     char nm[96];
     for (uint32_t l = 0; l < c->layers; ++l) {
@@ -268,9 +306,10 @@ static int build_plan(const AtlasSynthConfig *c, Plan **out, int *count)
         ADD(nm, TYPE, COLS, ROWS, INIT);                                    \
     } while (0)
         LADD("attn_norm.weight", T_F32, H, 1, 1);
-        LADD("attn_q.weight", T_Q4K, H, qd, 0);
+        LADD("attn_q.weight", alt ? alt : T_Q4K, H, qd, 0);
         LADD("attn_k.weight", T_Q4K, H, kvd, 0);
-        LADD("attn_v.weight", T_Q6K, H, kvd, 0);
+        const int odd = c->layer_mix && (l & 1u);   /* types that change across layers */
+        LADD("attn_v.weight", odd ? T_Q4K : T_Q6K, H, kvd, 0);
         if (c->qkv_bias) {
             LADD("attn_q.bias", T_F32, qd, 1, 2);
             LADD("attn_k.bias", T_F32, kvd, 1, 2);
@@ -282,9 +321,9 @@ static int build_plan(const AtlasSynthConfig *c, Plan **out, int *count)
         }
         LADD("attn_output.weight", T_Q4K, qd, H, 0);
         LADD("ffn_norm.weight", T_F32, H, 1, 1);
-        LADD("ffn_gate.weight", T_Q4K, H, c->ffn, 0);
-        LADD("ffn_up.weight", T_Q4K, H, c->ffn, 0);
-        LADD("ffn_down.weight", T_Q6K, c->ffn, H, 0);
+        LADD("ffn_gate.weight", alt ? alt : T_Q4K, H, c->ffn, 0);
+        LADD("ffn_up.weight", alt ? alt : T_Q4K, H, c->ffn, 0);
+        LADD("ffn_down.weight", odd ? T_Q4K : alt ? alt : T_Q6K, c->ffn, H, 0);
 #undef LADD
     }
 #undef ADD
@@ -308,6 +347,7 @@ static int validate(const AtlasSynthConfig *c)
         return -1;
     uint32_t qd = c->q_heads * c->head_dim;
     if (c->hidden % QK || c->ffn % QK || qd % QK || c->q_heads % c->kv_heads) return -1;
+    if (c->alt_type && (c->alt_type == T_Q4K || c->alt_type == T_Q6K || !blk_bytes((uint32_t)c->alt_type))) return -1;
     return 0;
 }
 
@@ -399,15 +439,17 @@ int atlas_synth_write_gguf(const AtlasSynthConfig *c, const char *path)
             written += cnt * 4u;
             continue;
         }
-        size_t bb = p[t].type == T_Q4K ? Q4K_BYTES : Q6K_BYTES;
+        const uint32_t ty = p[t].type;
+        size_t bb = blk_bytes(ty);
         uint64_t blocks = p[t].bytes / bb, per = chunk / bb;
         for (uint64_t b0 = 0; rc == 0 && b0 < blocks; b0 += per) {
             uint64_t m = blocks - b0 < per ? blocks - b0 : per;
 #pragma omp parallel for schedule(static)
             for (int64_t i = 0; i < (int64_t)m; ++i) {
                 Rng r = rng_for(c->seed, (uint64_t)t, b0 + (uint64_t)i);
-                if (bb == Q4K_BYTES) gen_q4k_block(&r, buf + (uint64_t)i * bb);
-                else gen_q6k_block(&r, buf + (uint64_t)i * bb);
+                if (ty == T_Q4K) gen_q4k_block(&r, buf + (uint64_t)i * bb);
+                else if (ty == T_Q6K) gen_q6k_block(&r, buf + (uint64_t)i * bb);
+                else gen_other_block(&r, ty, buf + (uint64_t)i * bb);
             }
             if (fwrite(buf, 1, (size_t)(m * bb), f) != m * bb) rc = -1;
             written += m * bb;

@@ -47,7 +47,8 @@ class SynthConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in
                 ("hidden", "layers", "q_heads", "kv_heads", "head_dim", "ffn", "vocab", "context_length")] + [
         ("rope_base", ctypes.c_float), ("tied", ctypes.c_int32), ("qkv_bias", ctypes.c_int32),
-        ("threads", ctypes.c_int32), ("seed", ctypes.c_uint64), ("qk_norm", ctypes.c_int32)]
+        ("threads", ctypes.c_int32), ("seed", ctypes.c_uint64), ("qk_norm", ctypes.c_int32),
+        ("alt_type", ctypes.c_int32), ("layer_mix", ctypes.c_int32)]
 
 
 class Shape(ctypes.Structure):
@@ -168,10 +169,12 @@ def _ptr(a) -> ctypes.c_void_p:
 def write_synthetic_gguf(path: str, *, hidden: int, layers: int, q_heads: int, kv_heads: int, ffn: int, vocab: int,
                          head_dim: int = 128, context_length: int = 32768, rope_base: float = 1e6,
                          tied: bool = True, qkv_bias: bool = True, seed: int = 0, threads: int = 0,
-                         qk_norm: bool = False) -> int:
-    """qk_norm: a qwen3 file (per-head q/k RMSNorm weights)."""
+                         qk_norm: bool = False, alt_type: int = 0, layer_mix: bool = False) -> int:
+    """qk_norm: a qwen3 file (per-head q/k RMSNorm weights). alt_type: another
+    block type (F16, Q5_0, Q5_1, Q8_0, Q5_K) for attn_q, ffn_gate, ffn_up,
+    ffn_down and the head. layer_mix: odd layers' attn_v and ffn_down are Q4_K."""
     cfg = SynthConfig(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, context_length, rope_base,
-                      int(tied), int(qkv_bias), threads, seed, int(qk_norm))
+                      int(tied), int(qkv_bias), threads, seed, int(qk_norm), int(alt_type), int(layer_mix))
     rc = lib().atlas_synth_write_gguf(ctypes.byref(cfg), path.encode())
     if rc != 0:
         raise RuntimeError(f"synthetic GGUF write failed: {path}")

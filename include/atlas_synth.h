@@ -47,6 +47,14 @@ typedef struct {
     uint64_t seed;
     int32_t qk_norm;          /* 1: a qwen3 file (architecture "qwen3", per-head
                                  blk.N.attn_q_norm / attn_k_norm.weight, head_dim floats) */
+    int32_t alt_type;         /* 0, or another ggml block type the reference reads (1 F16,
+                                 6 Q5_0, 7 Q5_1, 8 Q8_0, 13 Q5_K) for attn_q, ffn_gate,
+                                 ffn_up, ffn_down and the head (token_embd.weight when
+                                 tied, else output.weight): d (and dmin / m)
+                                 fp16(U[1e-4, 2e-3]), every other byte uniform; F16
+                                 elements fp16(U[-0.05, 0.05]) */
+    int32_t layer_mix;        /* 1: odd layers' attn_v and ffn_down are Q4_K (types that
+                                 change across layers, as in a Q4_K_M file) */
 } AtlasSynthConfig;
 
 /* Writes the model to `path`. Returns 0 on success, -1 on failure (errno-style

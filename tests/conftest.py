@@ -60,6 +60,22 @@ def _model(model_dir, name, cfg, tied=True):
     return path
 
 
+# Models with the reference's other block types (F16, Q5_0, Q5_1, Q8_0, Q5_K)
+# in attn_q, ffn_gate/up/down and the head; odd layers' attn_v / ffn_down Q4_K
+# where layer_mix is set. (name, alt_type, tied, layer_mix)
+OTHER_TYPES = [("f16", 1, True, False), ("q5_0", 6, False, True), ("q5_1", 7, True, True),
+               ("q8_0", 8, False, False), ("q5_k", 13, False, True), ("q4q6_mix", 0, True, True)]
+OTHER = dict(hidden=512, layers=3, q_heads=4, kv_heads=2, ffn=768, vocab=2048, context_length=512, seed=777)
+
+
+def other_type_model(model_dir, case):
+    name, alt, tied, mix = case
+    path = os.path.join(str(model_dir), f"types_{name}.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, tied=tied, alt_type=alt, layer_mix=mix, **OTHER)
+    return path
+
+
 @pytest.fixture(scope="session")
 def tiny_model(model_dir):
     return _model(model_dir, "tiny", TINY)

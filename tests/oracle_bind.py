@@ -19,7 +19,8 @@ def _p(a):
 
 
 def write_synthetic_gguf(path, *, hidden, layers, q_heads, kv_heads, ffn, vocab, head_dim=128, context_length=32768,
-                         rope_base=1e6, tied=True, qkv_bias=True, seed=0, threads=0, qk_norm=False):
+                         rope_base=1e6, tied=True, qkv_bias=True, seed=0, threads=0, qk_norm=False, alt_type=0,
+                         layer_mix=False):
     """The seeded synthetic GGUF writer as built into liboracle.so (the same
     writer source as the product library's atlas_synth_write_gguf; a CPU test
     checks that both produce identical bytes). Lets the CPU reference arm make
@@ -28,7 +29,7 @@ def write_synthetic_gguf(path, *, hidden, layers, q_heads, kv_heads, ffn, vocab,
     L = ctypes.CDLL(Oracle.PATH)
     L.atlas_synth_write_gguf.argtypes = [P, ctypes.c_char_p]
     cfg = SynthConfig(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, context_length, rope_base, int(tied),
-                      int(qkv_bias), threads, seed, int(qk_norm))
+                      int(qkv_bias), threads, seed, int(qk_norm), int(alt_type), int(layer_mix))
     if L.atlas_synth_write_gguf(ctypes.byref(cfg), path.encode()) != 0:
         raise RuntimeError(f"synthetic GGUF write failed: {path}")
 

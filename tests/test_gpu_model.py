@@ -68,6 +68,78 @@ def test_small_prefill_generate_matches_oracle(torch_cuda, oracle, small_model):
         np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
 
 
+@pytest.mark.parametrize("case", __import__("conftest").OTHER_TYPES, ids=lambda c: c[0])
+def test_other_block_types_match_oracle(torch_cuda, oracle, model_dir, case):
+    """Files with the reference's other block types in the projections and the
+    head, and with types that change across layers: the prompt (replayed
+    through the decode step for the other types, batched for Q4_K / Q6_K) and
+    24 greedy steps against the oracle."""
+    from conftest import other_type_model
+    path = other_type_model(model_dir, case)
+    m = oracle.open(path)
+    m.begin(128)
+    prompt = np.random.default_rng(5).integers(0, 2048, 20).astype(np.uint32)
+    for i, t in enumerate(prompt):
+        want = m.forward(int(t), i, i + 1 == len(prompt))
+    want_picks, lg = [], want
+    for s in range(24):
+        want_picks.append(m.argmax(lg))
+        lg = m.forward(want_picks[-1], len(prompt) + s)
+    with atlas_cuda.Runtime(path, max_context=128) as rt:
+        got, am = rt.prefill(prompt)
+        _close(got, want, 1e-3)
+        assert am == want_picks[0]
+        picks = rt.generate(am, len(prompt), 23)
+        np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
+        got2, _ = rt.forward(int(want_picks[0]), len(prompt))
+        w2 = m.forward(int(want_picks[0]), len(prompt))   # the oracle's cache is rewritten at this position too
+        _close(got2, w2, 1e-3)
+
+
+LONG = dict(hidden=256, layers=2, q_heads=2, kv_heads=1, ffn=512, vocab=1024, context_length=8448, seed=8191)
+LONG_PROMPT = 8176   # positions up to 8,191 after the 16 greedy steps (the 14B shape's 8,192-token prompt length)
+_long_want = {}
+
+
+def _long_oracle(oracle, path):
+    """The oracle over the long prompt and 16 greedy steps (computed once)."""
+    if path not in _long_want:
+        m = oracle.open(path)
+        m.begin(LONG_PROMPT + 32)
+        prompt = np.random.default_rng(81).integers(0, LONG["vocab"], LONG_PROMPT).astype(np.uint32)
+        for i, t in enumerate(prompt):
+            lg = m.forward(int(t), i, i + 1 == len(prompt))
+        first = lg
+        picks = []
+        for s in range(16):
+            picks.append(m.argmax(lg))
+            lg = m.forward(picks[-1], LONG_PROMPT + s)
+        _long_want[path] = (prompt, first, picks, lg)
+    return _long_want[path]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("kv_fp16", [False, True])
+def test_long_context_matches_oracle(torch_cuda, oracle, model_dir, kv_fp16):
+    """An 8,176-token batched prefill and 16 greedy steps (positions up to
+    8,191) against the oracle. fp32 cache: logits within 1e-3 max|logit| and
+    every pick; fp16 cache (the 14B shape's cache): within the 2e-2 bound."""
+    path = os.path.join(str(model_dir), "long.gguf")
+    if not os.path.exists(path):
+        atlas_cuda.write_synthetic_gguf(path, tied=True, **LONG)
+    prompt, first, picks, last = _long_oracle(oracle, path)
+    with atlas_cuda.Runtime(path, max_context=LONG_PROMPT + 32, max_prefill=512, kv_fp16=kv_fp16) as rt:
+        got, am = rt.prefill(prompt)
+        rel = _close(got, first, 2e-2 if kv_fp16 else 1e-3)
+        if not kv_fp16:
+            assert am == picks[0]
+            got_picks = rt.generate(am, LONG_PROMPT, 15)
+            np.testing.assert_array_equal(got_picks, np.array(picks[1:], np.uint32))
+            lg, _ = rt.forward(int(picks[-1]), LONG_PROMPT + 15)
+            _close(lg, last, 1e-3)
+        print(f"long context, fp16 cache {kv_fp16}: max|dlogit|/max|logit| {rel:.3g}")
+
+
 def test_generate_equals_forward_loop(torch_cuda, small_model):
     with atlas_cuda.Runtime(small_model, max_context=64) as rt:
         _, am = rt.prefill(np.arange(10, 30, dtype=np.uint32))

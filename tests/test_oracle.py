@@ -144,3 +144,18 @@ def test_large_goldens_pin_their_model_files():
         assert np.isfinite(g["logits_prompt"].astype(np.float32)).all()
         want = np.random.default_rng(1234).integers(0, vocab, 512).astype(np.uint32)
         np.testing.assert_array_equal(g["prompt"], want)
+
+
+@pytest.mark.parametrize("case", __import__("conftest").OTHER_TYPES, ids=lambda c: c[0])
+def test_oracle_forward_matches_reference_other_types(oracle, ref, model_dir, case):
+    """Files whose projections and head use F16 / Q5_0 / Q5_1 / Q8_0 / Q5_K
+    (dequant_block, src/brain_runtime.c:1017-1121), and types that change
+    across layers: the oracle's logits equal the reference's bit for bit."""
+    from conftest import other_type_model
+    path = other_type_model(model_dir, case)
+    m = oracle.open(path)
+    m.begin(64)
+    r = ref.open(path)
+    for pos, tok in enumerate([1, 900, 44, 2000, 2, 17]):
+        np.testing.assert_array_equal(m.forward(tok, pos), r.forward(tok, pos))
+    r.close()
