@@ -1611,7 +1611,7 @@ __device__ __forceinline__ void attn_merge(const AttnArgs &a, AttnSmem &sm, uint
 }
 
 template <int GP>
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a)
+__device__ __forceinline__ void attn_body(const AttnArgs &a)
 {
     extern __shared__ __align__(16) uint8_t smem_a[];
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
@@ -1751,6 +1751,35 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_cons
     trace_done(tr, a.trace_slot, t_start, t_ready);
 }
 
+// Sequence s's view of a batched step's arguments.
+__device__ __forceinline__ AttnArgs seq_view(const AttnArgs &a, uint32_t s)
+{
+    AttnArgs v = a;
+    v.q = a.q + (size_t)s * a.qkv_stride;
+    v.k = a.k + (size_t)s * a.qkv_stride;
+    v.v = a.v + (size_t)s * a.qkv_stride;
+    v.k_cache = static_cast<uint8_t *>(a.k_cache) + s * a.cache_seq_bytes;
+    v.v_cache = static_cast<uint8_t *>(a.v_cache) + s * a.cache_seq_bytes;
+    v.att = a.att + (size_t)s * a.att_stride;
+    v.part = a.part + (size_t)s * a.part_seq;
+    v.ctr = a.ctr + (size_t)s * a.ctr_seq;
+    v.st = a.st + s;
+    return v;
+}
+
+template <int GP>
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a)
+{
+    attn_body<GP>(a);
+}
+
+template <int GP>
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel_b(const __grid_constant__ AttnArgs a)
+{
+    const AttnArgs v = seq_view(a, blockIdx.y);
+    attn_body<GP>(v);
+}
+
 // ------------------------------------------- attention, fp16 cache, MMA ----
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src)
@@ -1808,7 +1837,7 @@ __device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_
 // in flight, the first two issued before the predecessor wait. Warp w takes
 // positions 8w .. 8w + 7 of a tile; lane (g, t) holds head g's scores of
 // positions 2t, 2t + 1 and its outputs of dimensions 8j + 2t, 8j + 2t + 1.
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid_constant__ AttnArgs a)
+__device__ __forceinline__ void attn_tc16_body(const AttnArgs &a)
 {
     extern __shared__ __align__(16) uint8_t smem_a[];
     AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_a);
@@ -1955,6 +1984,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid
     trace_done(tr, a.trace_slot, t_start, t_ready);
 }
 
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel(const __grid_constant__ AttnArgs a)
+{
+    attn_tc16_body(a);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_tc16_kernel_b(const __grid_constant__ AttnArgs a)
+{
+    const AttnArgs v = seq_view(a, blockIdx.y);
+    attn_tc16_body(v);
+}
+
 // --------------------------------------------------------- embed, argmax --
 
 // token_embd row of the current token -> x, bit-exact (load_embedding_row,
@@ -2098,8 +2138,15 @@ cudaError_t launch_ex(const void *fn, void **args, dim3 grid, dim3 block, size_t
 
 // attention instance for `group` query heads per KV head (rounded up to a
 // power of two); tc: the tensor-core kernel of fp16 caches
-const void *attn_fn(uint32_t group, bool tc = false)
+const void *attn_fn(uint32_t group, bool tc = false, bool batch = false)
 {
+    if (batch) {
+        if (tc) return (const void *)attn_tc16_kernel_b;
+        if (group <= 1u) return (const void *)attn_kernel_b<1>;
+        if (group <= 2u) return (const void *)attn_kernel_b<2>;
+        if (group <= 4u) return (const void *)attn_kernel_b<4>;
+        return (const void *)attn_kernel_b<8>;
+    }
     if (tc) return (const void *)attn_tc16_kernel;
     if (group <= 1u) return (const void *)attn_kernel<1>;
     if (group <= 2u) return (const void *)attn_kernel<2>;
@@ -2214,11 +2261,16 @@ extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem)
                               cudaSuccess)
                     return e;
             }
-    for (uint32_t g = 1; g <= kAttnMaxGroup; g *= 2u)
-        if ((e = cudaFuncSetAttribute(attn_fn(g), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem)) !=
-            cudaSuccess)
+    for (bool b : {false, true}) {
+        for (uint32_t g = 1; g <= kAttnMaxGroup; g *= 2u)
+            if ((e = cudaFuncSetAttribute(attn_fn(g, false, b), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)attn_smem)) != cudaSuccess)
+                return e;
+        if ((e = cudaFuncSetAttribute(attn_fn(1, true, b), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_smem)) != cudaSuccess)
             return e;
-    return cudaFuncSetAttribute(attn_fn(1, true), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem);
+    }
+    return cudaSuccess;
 }
 
 extern "C" size_t atlas_d2_mv4_smem(uint32_t cols, uint32_t warps, uint32_t nslot, uint32_t slot_bytes)
@@ -2236,6 +2288,20 @@ extern "C" cudaError_t atlas_d2_launch_mv(const MvArgs *a, uint32_t grid, cudaSt
         return launch_ex(fn, args, dim3(grid), dim3(32u * a->warps), a->smem_bytes, stream, a->pdl != 0u);
     }
     return launch_ex((const void *)mv_kernel, args, dim3(grid), dim3(kMvThreads), a->smem_bytes, stream, a->pdl != 0u);
+}
+
+// A batched step's attention: grid.y = nseq sequences.
+extern "C" cudaError_t atlas_d2_launch_attn_b(const AttnArgs *a, uint32_t grid, uint32_t nseq, cudaStream_t stream)
+{
+    AttnArgs copy = *a;
+    void *args[] = {&copy};
+    const uint32_t group = a->q_heads / a->kv_heads;
+    if (group == 0u || group > kAttnMaxGroup || a->splits % kAttnCluster != 0u || a->splits / kAttnCluster > 32u ||
+        grid != a->kv_heads * a->splits || nseq == 0u)
+        return cudaErrorInvalidValue;
+    if (a->tc && !a->kv_fp16) return cudaErrorInvalidValue;
+    return launch_ex(attn_fn(group, a->tc != 0u, true), args, dim3(grid, nseq), dim3(kAttnThreads),
+                     atlas_d2_attn_smem(a->splits), stream, true, kAttnCluster);
 }
 
 extern "C" cudaError_t atlas_d2_launch_attn(const AttnArgs *a, uint32_t grid, cudaStream_t stream)

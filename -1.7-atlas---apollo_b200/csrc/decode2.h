@@ -225,6 +225,11 @@ struct AttnArgs {
     float eps;
     uint32_t tc;                // fp16 cache: tensor-core kernel (attn_tc16_kernel)
     uint32_t trace_slot;        // this launch's index in the step (trace records)
+    // batched step (attn_kernel_b: blockIdx.y = sequence s): q, k, v at + s *
+    // qkv_stride, the caches at + s * cache_seq_bytes, att at + s * att_stride,
+    // part at + s * part_seq, ctr at + s * ctr_seq, st at + s
+    uint32_t qkv_stride, att_stride, part_seq, ctr_seq;
+    uint64_t cache_seq_bytes;
 };
 
 }  // namespace d2

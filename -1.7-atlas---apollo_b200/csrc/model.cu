@@ -26,6 +26,7 @@
 #include "prefill.h"
 #include "gemv.h"
 #include "decode2.h"
+#include "batch.h"
 
 extern "C" cudaError_t atlas_launch_decode(const atlas::Program *pg, int grid, cudaStream_t stream);
 extern "C" size_t atlas_decode_hdr_bytes();
@@ -47,6 +48,8 @@ extern "C" int atlas_d2_attn_max_clusters(uint32_t group, uint32_t tc);
 extern "C" cudaError_t atlas_d2_setup(size_t mv_smem, size_t attn_smem);
 extern "C" cudaError_t atlas_d2_launch_mv(const atlas::d2::MvArgs *a, uint32_t grid, cudaStream_t stream);
 extern "C" cudaError_t atlas_d2_launch_attn(const atlas::d2::AttnArgs *a, uint32_t grid, cudaStream_t stream);
+extern "C" cudaError_t atlas_d2_launch_attn_b(const atlas::d2::AttnArgs *a, uint32_t grid, uint32_t nseq,
+                                              cudaStream_t stream);
 extern "C" cudaError_t atlas_d2_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,
                                              uint32_t vocab, float *x, atlas::d2::DecState *st, cudaStream_t stream);
 extern "C" cudaError_t atlas_d2_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n,
@@ -158,6 +161,23 @@ struct AtlasCuda {
     float *x2 = nullptr;
     uint32_t *d_in_ids = nullptr;
     uint32_t in_cap = 0;
+    // Several sequences (batch.cu): each has a KV-cache region of kv_seq_bytes
+    // in every layer's cache; kv_off selects the region the batched prefill
+    // writes. gb: the batched step of nseq sequences as one CUDA graph.
+    uint32_t max_batch = 1;
+    uint64_t kv_seq_bytes = 0, kv_off = 0;
+    struct GraphB {
+        bool on = false;
+        uint32_t nseq = 0, kernels = 0, out_cap = 0, red_logits = 0;
+        size_t part_cap = 0;   // floats
+        d2::DecState *st = nullptr;
+        float *x = nullptr, *qkv = nullptr, *att = nullptr, *ffn = nullptr, *logits = nullptr, *inv = nullptr;
+        float *part = nullptr, *apart = nullptr, *pmax = nullptr;
+        uint32_t *actr = nullptr, *pidx = nullptr, *out_ids = nullptr;
+        std::vector<float *> qkv_bias;   // per layer: q, k, v biases back to back (null: none)
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+    } gb;
     // Matrices of the reference's other block types (F16, Q5_0, Q5_1, Q8_0,
     // Q5_K): the graph decode step only, prompts replayed through it token by
     // token (prompt mode); the batched prefill's tensor-core contractions take
@@ -1608,7 +1628,9 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
     const uint64_t cache_head = (uint64_t)d.max_context * d.head_dim;
     for (uint32_t l = 0; l < d.layers; ++l) {
         const AtlasCuda::W &w = h->layers[l];
-        float *kc = static_cast<float *>(w.kc), *vc = static_cast<float *>(w.vc);
+        // the sequence region the prompt belongs to (kv_off: 0 for sequence 0)
+        float *kc = reinterpret_cast<float *>(static_cast<uint8_t *>(w.kc) + h->kv_off);
+        float *vc = reinterpret_cast<float *>(static_cast<uint8_t *>(w.vc) + h->kv_off);
         // attention block: rms_norm -> Q, K, V (+bias, RoPE, KV-cache store) -> attention -> O (+residual)
         if ((rc = launch_split(h, p.x, d.hidden, n, w.attn_norm))) return rc;
         pf::GemmArgs g{};
@@ -1624,7 +1646,7 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
         if ((rc = launch_gemm(h, g, d.hidden, n, pos0))) return rc;
         if (qkn) {
             // qwen3: per-head RMSNorm, then RoPE; keys into the cache
-            CU(h, atlas_launch_prefill_qknorm(p.q, sl.q_heads, p.kq, w.kc, sl.kv_heads, d.max_context, pos0, n, w.qn,
+            CU(h, atlas_launch_prefill_qknorm(p.q, sl.q_heads, p.kq, kc, sl.kv_heads, d.max_context, pos0, n, w.qn,
                                               w.kn, h->rope, d.rms_eps, d.kv_fp16 ? 1u : 0u, h->stream));
             ++h->launches;
         }
@@ -1663,6 +1685,344 @@ int prefill_chunk(AtlasCuda *h, const uint32_t *ids, uint32_t n, uint32_t pos0)
     return ATLAS_OK;
 }
 
+// ----------------------------------------------------- batched step (bt) --
+
+struct BPlan {
+    bt::BArgs a{};
+    uint32_t grid = 0;
+};
+
+bt::BSeg bseg(const uint8_t *w, uint32_t type, uint32_t rows, uint32_t cols, uint32_t prow0)
+{
+    bt::BSeg s{};
+    s.w = w;
+    s.type = type;
+    s.rows = rows;
+    s.row_bytes = (uint64_t)(cols / 256u) * block_bytes(type);
+    s.prow0 = prow0;
+    return s;
+}
+
+// CTAs of one batched GEMV launch: K is cut into slices of at most
+// kSplitMax blocks (the 8 inputs of a slice fit in shared memory); every
+// (segment, slice) pair gets CTAs in proportion to its bytes, each a
+// contiguous range of whole tiles; the ring is the deepest that fits.
+int plan_mvb(AtlasCuda *h, BPlan &p, uint32_t cols, std::initializer_list<bt::BSeg> segs, uint32_t nseq)
+{
+    bt::BArgs &a = p.a;
+    a = bt::BArgs{};
+    a.cols = cols;
+    a.nb = cols / 256u;
+    a.nseq = nseq;
+    if (!cols || cols % 256u || !nseq || nseq > bt::kMaxSeq) return fail(h, ATLAS_EINVAL, "mvb: bad shape");
+    for (const bt::BSeg &sg : segs) {
+        if (a.n_seg == 3) return fail(h, ATLAS_EINVAL, "mvb: too many segments");
+        if ((sg.type != 12u && sg.type != 14u) || sg.rows % 16u || !sg.rows)
+            return fail(h, ATLAS_EINVAL, "several sequences: matrices of type %u are not supported (Q4_K, Q6_K)",
+                        sg.type);
+        a.seg[a.n_seg++] = sg;
+        a.prows = std::max(a.prows, sg.prow0 + sg.rows);
+    }
+    a.nsplit = (a.nb + bt::kSplitMax - 1u) / bt::kSplitMax;
+    a.split_blocks = (a.nb + a.nsplit - 1u) / a.nsplit;
+    a.nsplit = (a.nb + a.split_blocks - 1u) / a.split_blocks;
+    const uint32_t G = (uint32_t)h->sm_count;
+    struct Pair { uint32_t seg, split, tiles, n; double bytes; };
+    std::vector<Pair> pr;
+    double total = 0;
+    for (uint32_t s = 0; s < a.n_seg; ++s)
+        for (uint32_t k = 0; k < a.nsplit; ++k) {
+            const uint32_t nbs = std::min(a.split_blocks, a.nb - k * a.split_blocks);
+            const double by = (double)a.seg[s].rows * nbs * block_bytes(a.seg[s].type);
+            pr.push_back(Pair{s, k, a.seg[s].rows / 16u, 1u, by});
+            total += by;
+        }
+    uint32_t used = 0;
+    for (Pair &q : pr) {
+        q.n = std::min(q.tiles, (uint32_t)std::max(1.0, std::floor((double)G * q.bytes / total + 0.5)));
+        used += q.n;
+    }
+    while (used > G) {
+        size_t big = 0;
+        for (size_t i = 1; i < pr.size(); ++i)
+            if (pr[i].n > pr[big].n) big = i;
+        if (pr[big].n <= 1) break;
+        --pr[big].n;
+        --used;
+    }
+    std::vector<bt::BCta> ctas;
+    for (const Pair &q : pr)
+        for (uint32_t c = 0; c < q.n; ++c)
+            ctas.push_back(bt::BCta{q.seg, q.tiles * c / q.n, q.tiles * (c + 1) / q.n, q.split});
+    p.grid = (uint32_t)ctas.size();
+    uint32_t slot = 0;
+    for (uint32_t s = 0; s < a.n_seg; ++s) slot = std::max(slot, a.seg[s].type == 12u ? 16u * 144u : 16u * 240u);
+    a.nslot = 0;
+    for (uint32_t ns = bt::kBMaxSlots; ns >= 2u && !a.nslot; --ns)
+        if (bt::mvb_smem(a.split_blocks, ns, slot) <= 227u * 1024u) a.nslot = ns;
+    if (!a.nslot) return fail(h, ATLAS_EINVAL, "mvb: no shared-memory plan");
+    a.slot_bytes = slot;
+    a.smem_bytes = (uint32_t)bt::mvb_smem(a.split_blocks, a.nslot, slot);
+    bt::BCta *dc = nullptr;
+    int rc = dalloc(h, &dc, ctas.size() * sizeof(bt::BCta));
+    if (rc) return rc;
+    CU(h, cudaMemcpy(dc, ctas.data(), ctas.size() * sizeof(bt::BCta), cudaMemcpyHostToDevice));
+    a.cta = dc;
+    a.pdl = 1u;
+    return ATLAS_OK;
+}
+
+// A plan of a launch shape, made once per combination of block types
+// (a Q4_K_M file's attn_v and ffn_down change type across layers).
+int cached_mvb(AtlasCuda *h, std::vector<std::pair<std::vector<uint32_t>, BPlan>> &cache, BPlan &out, uint32_t cols,
+               std::initializer_list<bt::BSeg> segs, uint32_t nseq)
+{
+    std::vector<uint32_t> key{cols, nseq};
+    for (const bt::BSeg &sg : segs) {
+        key.push_back(sg.type);
+        key.push_back(sg.rows);
+        key.push_back(sg.prow0);
+    }
+    const BPlan *f = nullptr;
+    for (const auto &e : cache)
+        if (e.first == key) f = &e.second;
+    if (!f) {
+        BPlan p;
+        const int rc = plan_mvb(h, p, cols, segs, nseq);
+        if (rc) return rc;
+        cache.emplace_back(key, p);
+        f = &cache.back().second;
+    }
+    out = *f;
+    uint32_t i = 0;
+    for (const bt::BSeg &sg : segs) out.a.seg[i++].w = sg.w;
+    return ATLAS_OK;
+}
+
+// The batched step of nseq sequences as one CUDA graph (built on first use,
+// rebuilt when nseq changes).
+int build_graphb(AtlasCuda *h, uint32_t nseq)
+{
+    const AtlasModelDesc &d = h->desc;
+    AtlasCuda::GraphB &b = h->gb;
+    if (b.on && b.nseq == nseq) return ATLAS_OK;
+    if (!h->g2.on) return fail(h, ATLAS_EINVAL, "several sequences: the decode step is not built");
+    if (h->tp > 1 || h->other_types)
+        return fail(h, ATLAS_EINVAL, "several sequences: one GPU and Q4_K / Q6_K matrices only");
+    if (!nseq || nseq > h->max_batch)
+        return fail(h, ATLAS_EINVAL, "%u sequences: the handle was created for at most %u (desc.max_batch)", nseq,
+                    h->max_batch);
+    if (b.exec) cudaGraphExecDestroy(b.exec);
+    if (b.graph) cudaGraphDestroy(b.graph);
+    b.exec = nullptr;
+    b.graph = nullptr;
+    b.on = false;
+    const uint32_t G = (uint32_t)h->sm_count, B = h->max_batch, group = d.q_heads / d.kv_heads;
+    const uint32_t qkvw = d.q_dim + 2u * d.kv_dim;
+    const uint32_t C = d2::kAttnCluster;
+    const uint32_t splits = std::max(C, (h->g2.splits / nseq) / C * C);
+    int rc = ATLAS_OK;
+    if (!b.st) {
+        if ((rc = dalloc(h, &b.st, B * sizeof(d2::DecState))) || (rc = dalloc(h, &b.x, (size_t)B * d.hidden * 4)) ||
+            (rc = dalloc(h, &b.qkv, (size_t)B * qkvw * 4)) || (rc = dalloc(h, &b.att, (size_t)B * d.q_dim * 4)) ||
+            (rc = dalloc(h, &b.ffn, (size_t)B * d.ffn * 4)) || (rc = dalloc(h, &b.logits, (size_t)B * d.vocab * 4)) ||
+            (rc = dalloc(h, &b.inv, B * 4)) ||
+            (rc = dalloc(h, &b.apart, (size_t)B * d.kv_heads * (h->g2.splits / C) * group * d2::kRec * 4)) ||
+            (rc = dalloc(h, &b.actr, (size_t)B * d.q_heads * 4)))
+            return rc;
+        CU(h, cudaMemset(b.st, 0, B * sizeof(d2::DecState)));
+        CU(h, cudaMemset(b.actr, 0, (size_t)B * d.q_heads * 4));
+        b.qkv_bias.assign(d.layers, nullptr);
+        for (uint32_t l = 0; l < d.layers; ++l) {
+            const AtlasCuda::W &w = h->layers[l];
+            if (!w.bq && !w.bk && !w.bv) continue;
+            float *bb = nullptr;
+            if ((rc = dalloc(h, &bb, (size_t)qkvw * 4))) return rc;
+            CU(h, cudaMemset(bb, 0, (size_t)qkvw * 4));
+            if (w.bq) CU(h, cudaMemcpy(bb, w.bq, (size_t)d.q_dim * 4, cudaMemcpyDeviceToDevice));
+            if (w.bk) CU(h, cudaMemcpy(bb + d.q_dim, w.bk, (size_t)d.kv_dim * 4, cudaMemcpyDeviceToDevice));
+            if (w.bv) CU(h, cudaMemcpy(bb + d.q_dim + d.kv_dim, w.bv, (size_t)d.kv_dim * 4, cudaMemcpyDeviceToDevice));
+            b.qkv_bias[l] = bb;
+        }
+        b.red_logits = std::min(2u * G, (d.vocab + 1023u) / 1024u);
+        if ((rc = dalloc(h, &b.pmax, (size_t)B * b.red_logits * 4)) || (rc = dalloc(h, &b.pidx, (size_t)B * b.red_logits * 4)))
+            return rc;
+    }
+    // the launches' plans (per layer: q/k/v, o, gate/up, down; then the head)
+    std::vector<std::pair<std::vector<uint32_t>, BPlan>> cache;
+    std::vector<std::array<BPlan, 4>> lp(d.layers);
+    BPlan hd;
+    size_t part_floats = 0, smem = 0;
+    for (uint32_t l = 0; l < d.layers; ++l) {
+        const AtlasCuda::W &w = h->layers[l];
+        if ((rc = cached_mvb(h, cache, lp[l][0], d.hidden,
+                             {bseg(w.q, w.tq, d.q_dim, d.hidden, 0u), bseg(w.k, w.tk, d.kv_dim, d.hidden, d.q_dim),
+                              bseg(w.v, w.tv, d.kv_dim, d.hidden, d.q_dim + d.kv_dim)},
+                             nseq)) ||
+            (rc = cached_mvb(h, cache, lp[l][1], d.q_dim, {bseg(w.o, w.to, d.hidden, d.q_dim, 0u)}, nseq)) ||
+            (rc = cached_mvb(h, cache, lp[l][2], d.hidden,
+                             {bseg(w.gate, w.tg, d.ffn, d.hidden, 0u), bseg(w.up, w.tu, d.ffn, d.hidden, d.ffn)}, nseq)) ||
+            (rc = cached_mvb(h, cache, lp[l][3], d.ffn, {bseg(w.down, w.td, d.hidden, d.ffn, 0u)}, nseq)))
+            return rc;
+        for (const BPlan &p : lp[l]) {
+            part_floats = std::max(part_floats, (size_t)p.a.nsplit * nseq * p.a.prows);
+            smem = std::max<size_t>(smem, p.a.smem_bytes);
+        }
+    }
+    if ((rc = cached_mvb(h, cache, hd, d.hidden, {bseg(h->head, h->t_head, d.vocab, d.hidden, 0u)}, nseq))) return rc;
+    part_floats = std::max(part_floats, (size_t)hd.a.nsplit * nseq * hd.a.prows);
+    smem = std::max<size_t>(smem, hd.a.smem_bytes);
+    if (part_floats > b.part_cap) {
+        if ((rc = dalloc(h, &b.part, part_floats * 4))) return rc;
+        b.part_cap = part_floats;
+    }
+    CU(h, atlas_bt_setup(smem));
+
+    d2::AttnArgs at{};
+    at.q = b.qkv;
+    at.k = b.qkv + d.q_dim;
+    at.v = b.qkv + d.q_dim + d.kv_dim;
+    at.att = b.att;
+    at.part = b.apart;
+    at.ctr = b.actr;
+    at.rope = h->rope;
+    at.st = b.st;
+    at.q_heads = d.q_heads;
+    at.kv_heads = d.kv_heads;
+    at.max_context = d.max_context;
+    at.splits = splits;
+    at.kv_fp16 = d.kv_fp16 ? 1u : 0u;
+    at.tc = h->g2.attn_tc ? 1u : 0u;
+    at.eps = d.rms_eps;
+    at.qkv_stride = qkvw;
+    at.att_stride = d.q_dim;
+    at.part_seq = d.kv_heads * (splits / C) * group * d2::kRec;
+    at.ctr_seq = d.q_heads;
+    at.cache_seq_bytes = h->kv_seq_bytes;
+    const uint64_t embd_row = (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
+    auto reduce = [&](const BPlan &p, uint32_t mode, uint32_t rows, const float *bias, float *out, uint32_t grid) {
+        bt::BReduce r{};
+        r.part = b.part;
+        r.nsplit = p.a.nsplit;
+        r.nseq = nseq;
+        r.prows = p.a.prows;
+        r.mode = mode;
+        r.rows = rows;
+        r.bias = bias;
+        r.inv = b.inv;
+        r.out = out;
+        r.ostride = rows;
+        r.pmax = b.pmax;
+        r.pidx = b.pidx;
+        r.pdl = 1u;
+        return atlas_bt_launch_reduce(&r, grid, h->stream);
+    };
+    auto resid = [&](const BPlan &p) {
+        bt::BResid r{};
+        r.part = b.part;
+        r.nsplit = p.a.nsplit;
+        r.nseq = nseq;
+        r.prows = p.a.prows;
+        r.x = b.x;
+        r.hidden = d.hidden;
+        r.inv = b.inv;
+        r.eps = d.rms_eps;
+        r.pdl = 1u;
+        return atlas_bt_launch_resid(&r, h->stream);
+    };
+    auto mv = [&](BPlan p, const float *x, uint32_t xstride, const float *norm) {
+        p.a.x = x;
+        p.a.xstride = xstride;
+        p.a.norm_w = norm;
+        p.a.part = b.part;
+        p.a.status = &b.st->status;
+        return atlas_bt_launch_mv(&p.a, p.grid, h->stream);
+    };
+    CU(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    uint32_t k = 0;
+    cudaError_t e = atlas_bt_launch_embed(h->embd, embd_row, h->t_embd, d.hidden, d.vocab, b.x, b.inv, d.rms_eps, b.st,
+                                          nseq, h->stream);
+    ++k;
+    for (uint32_t l = 0; l < d.layers && e == cudaSuccess; ++l) {
+        const AtlasCuda::W &w = h->layers[l];
+        if ((e = mv(lp[l][0], b.x, d.hidden, w.attn_norm)) != cudaSuccess) break;
+        if ((e = reduce(lp[l][0], bt::BRED_STORE, qkvw, b.qkv_bias[l], b.qkv, (qkvw + 1023u) / 1024u)) != cudaSuccess) break;
+        at.k_cache = w.kc;
+        at.v_cache = w.vc;
+        at.q_norm = w.qn;
+        at.k_norm = w.kn;
+        if ((e = atlas_d2_launch_attn_b(&at, d.kv_heads * splits, nseq, h->stream)) != cudaSuccess) break;
+        if ((e = mv(lp[l][1], b.att, d.q_dim, nullptr)) != cudaSuccess) break;
+        if ((e = resid(lp[l][1])) != cudaSuccess) break;
+        if ((e = mv(lp[l][2], b.x, d.hidden, w.ffn_norm)) != cudaSuccess) break;
+        if ((e = reduce(lp[l][2], bt::BRED_SWIGLU, d.ffn, nullptr, b.ffn, (d.ffn + 1023u) / 1024u)) != cudaSuccess) break;
+        if ((e = mv(lp[l][3], b.ffn, d.ffn, nullptr)) != cudaSuccess) break;
+        if ((e = resid(lp[l][3])) != cudaSuccess) break;
+        k += 9;
+    }
+    if (e == cudaSuccess && (e = mv(hd, b.x, d.hidden, h->out_norm)) == cudaSuccess &&
+        (e = reduce(hd, bt::BRED_LOGITS, d.vocab, nullptr, b.logits, b.red_logits)) == cudaSuccess)
+        e = atlas_bt_launch_argmax(b.pmax, b.pidx, b.red_logits, b.st, nseq, h->stream);
+    k += 3;
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return fail(h, ATLAS_ECUDA, "batched graph capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    b.graph = graph;
+    CU(h, cudaGraphInstantiate(&b.exec, graph, 0));
+    b.kernels = k;
+    b.nseq = nseq;
+    b.on = true;
+    return ATLAS_OK;
+}
+
+// `steps` replays of the batched step from each sequence's (token, position);
+// out_dev[s * steps + i]: sequence s's pick after step i (advance mode).
+int run_graphb(AtlasCuda *h, uint32_t nseq, const uint32_t *tok, const uint32_t *pos, uint32_t steps, bool advance)
+{
+    AtlasCuda::GraphB &b = h->gb;
+    int rc = build_graphb(h, nseq);
+    if (rc) return rc;
+    const size_t need = (size_t)nseq * std::max(steps, 1u);
+    if (need > b.out_cap) {
+        uint32_t *p = nullptr;
+        if ((rc = dalloc(h, &p, need * 4))) return rc;
+        b.out_ids = p;
+        b.out_cap = (uint32_t)need;
+    }
+    std::vector<d2::DecState> init(nseq);
+    for (uint32_t s = 0; s < nseq; ++s) {
+        init[s].pos = pos[s];
+        init[s].token = tok[s];
+        init[s].advance = advance ? 1u : 0u;
+        init[s].max_steps = steps;
+        init[s].out_ids = b.out_ids + (size_t)s * steps;
+    }
+    CU(h, cudaMemcpyAsync(b.st, init.data(), nseq * sizeof(d2::DecState), cudaMemcpyHostToDevice, h->stream));
+    CU(h, cudaEventRecord(h->ev0, h->stream));
+    for (uint32_t i = 0; i < std::max(steps, 1u); ++i) CU(h, cudaGraphLaunch(b.exec, h->stream));
+    CU(h, cudaEventRecord(h->ev1, h->stream));
+    h->launches += (uint64_t)std::max(steps, 1u) * b.kernels;
+    std::vector<d2::DecState> out(nseq);
+    CU(h, cudaMemcpyAsync(out.data(), b.st, nseq * sizeof(d2::DecState), cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->last_ms = ms;
+    h->total_ms += ms;
+    for (uint32_t s = 0; s < nseq; ++s)
+        if (out[s].status != kStatusOk) {
+            const int code = status_to_code(h, out[s].status);
+            cudaMemsetAsync(b.actr, 0, (size_t)h->max_batch * h->desc.q_heads * 4, h->stream);
+            cudaMemsetAsync(b.st, 0, h->max_batch * sizeof(d2::DecState), h->stream);
+            cudaStreamSynchronize(h->stream);
+            return code;
+        }
+    return ATLAS_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1687,6 +2047,8 @@ void atlas_cuda_destroy(AtlasCuda *h)
     if (h->stream) cudaStreamSynchronize(h->stream);
     staging_close(h);
     if (h->g2.exec) cudaGraphExecDestroy(h->g2.exec);
+    if (h->gb.exec) cudaGraphExecDestroy(h->gb.exec);
+    if (h->gb.graph) cudaGraphDestroy(h->gb.graph);
     if (h->g2.graph) cudaGraphDestroy(h->g2.graph);
     for (int r = 0; r < (int)d2::kTpMax; ++r)
         if (h->peer_mapped[r]) cudaIpcCloseMemHandle(h->peer[r]);
@@ -1751,6 +2113,9 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     h->layers.resize(d.layers);
     const size_t esz = d.kv_fp16 ? 2 : 4;
     const size_t kv_layer = (size_t)sl.kv_heads * d.max_context * d.head_dim * esz;
+    h->max_batch = std::max(1u, std::min(d.max_batch, bt::kMaxSeq));
+    if (h->max_batch > 1 && tp > 1) TRY(fail(h, ATLAS_EINVAL, "several sequences: one GPU (tp_size 1) only"));
+    h->kv_seq_bytes = kv_layer;
     const uint32_t hb = d.hidden / 256u, lq = sl.q_heads * 128u, lkv = sl.kv_heads * 128u;
     for (uint32_t l = 0; l < d.layers; ++l) {
         AtlasCuda::W &w = h->layers[l];
@@ -1778,8 +2143,8 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
             TRY(upload_vector(h, TN("attn_k_norm.weight"), d.head_dim, &w.kn));
         }
 #undef TN
-        TRY(dalloc(h, &w.kc, kv_layer));
-        TRY(dalloc(h, &w.vc, kv_layer));
+        TRY(dalloc(h, &w.kc, kv_layer * h->max_batch));
+        TRY(dalloc(h, &w.vc, kv_layer * h->max_batch));
         for (uint32_t ty : {w.tq, w.tk, w.tv, w.to, w.tg, w.tu, w.td})
             if (d2::m4_other_type(ty)) h->other_types = true;
     }
@@ -1895,6 +2260,59 @@ int atlas_cuda_generate(AtlasCuda *h, uint32_t first, uint32_t pos0, uint32_t st
     int rc = run_decode(h, first, pos0, steps, h->d_out_ids, nullptr, nullptr);
     if (rc) return rc;
     CU(h, cudaMemcpyAsync(out_ids, h->d_out_ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    return ATLAS_OK;
+}
+
+int atlas_cuda_prefill_seq(AtlasCuda *h, uint32_t seq, const uint32_t *ids, uint32_t n, uint32_t pos0,
+                           float *last_logits, uint32_t *argmax)
+{
+    if (!h) return fail(nullptr, ATLAS_EINVAL, "null handle");
+    if (seq >= h->max_batch)
+        return fail(h, ATLAS_ERANGE, "sequence %u >= desc.max_batch %u", seq, h->max_batch);
+    if (seq && (h->tp > 1 || h->other_types))
+        return fail(h, ATLAS_EINVAL, "several sequences: one GPU and Q4_K / Q6_K matrices only");
+    h->kv_off = (uint64_t)seq * h->kv_seq_bytes;
+    const int rc = atlas_cuda_prefill(h, ids, n, pos0, last_logits, argmax);
+    h->kv_off = 0;
+    return rc;
+}
+
+int atlas_cuda_generate_batch(AtlasCuda *h, uint32_t nseq, const uint32_t *first, const uint32_t *pos0,
+                              uint32_t steps, uint32_t *out_ids)
+{
+    if (!h || !first || !pos0 || !out_ids) return fail(h, ATLAS_EINVAL, "null argument");
+    if (!steps) return ATLAS_OK;
+    if (!nseq || nseq > h->max_batch) return fail(h, ATLAS_ERANGE, "nseq %u: 1 .. %u", nseq, h->max_batch);
+    for (uint32_t s = 0; s < nseq; ++s) {
+        if (first[s] >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab", first[s]);
+        if ((uint64_t)pos0[s] + steps > h->desc.max_context)
+            return fail(h, ATLAS_ERANGE, "sequence %u: positions exceed max_context", s);
+    }
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    int rc = run_graphb(h, nseq, first, pos0, steps, true);
+    if (rc) return rc;
+    CU(h, cudaMemcpyAsync(out_ids, h->gb.out_ids, (size_t)nseq * steps * 4, cudaMemcpyDeviceToHost, h->stream));
+    CU(h, cudaStreamSynchronize(h->stream));
+    return ATLAS_OK;
+}
+
+int atlas_cuda_decode_batch(AtlasCuda *h, uint32_t nseq, const uint32_t *ids, const uint32_t *pos, float *logits,
+                            uint32_t *argmax)
+{
+    if (!h || !ids || !pos) return fail(h, ATLAS_EINVAL, "null argument");
+    if (!nseq || nseq > h->max_batch) return fail(h, ATLAS_ERANGE, "nseq %u: 1 .. %u", nseq, h->max_batch);
+    for (uint32_t s = 0; s < nseq; ++s) {
+        if (ids[s] >= h->desc.vocab) return fail(h, ATLAS_ERANGE, "token %u >= vocab", ids[s]);
+        if (pos[s] >= h->desc.max_context) return fail(h, ATLAS_ERANGE, "position %u >= max_context", pos[s]);
+    }
+    if (cudaSetDevice(h->desc.device) != cudaSuccess) return fail(h, ATLAS_ECUDA, "cudaSetDevice failed");
+    int rc = run_graphb(h, nseq, ids, pos, 1, true);
+    if (rc) return rc;
+    if (logits)
+        CU(h, cudaMemcpyAsync(logits, h->gb.logits, (size_t)nseq * h->desc.vocab * 4, cudaMemcpyDeviceToHost,
+                              h->stream));
+    if (argmax) CU(h, cudaMemcpyAsync(argmax, h->gb.out_ids, (size_t)nseq * 4, cudaMemcpyDeviceToHost, h->stream));
     CU(h, cudaStreamSynchronize(h->stream));
     return ATLAS_OK;
 }

@@ -286,6 +286,7 @@ int atlas_rt_open(const char *path, const AtlasRtOptions *opt, AtlasRuntime **ou
     d.rope_base = s->rope_base; d.rms_eps = 1.0e-6f; d.has_qk_norm = s->has_qk_norm;
     d.kv_fp16 = o.kv_fp16; d.device = o.device;
     d.tp_rank = o.tp_size > 1 ? o.tp_rank : 0; d.tp_size = o.tp_size > 1 ? o.tp_size : 1;
+    d.max_batch = o.max_batch > 1 ? o.max_batch : 1;
     rc = atlas_cuda_create(&d, td, n, &rt->dev);
     free(td);
     if (rc) rt_fail(rt, rc, "%s", atlas_cuda_last_error(NULL));

@@ -28,7 +28,7 @@ EXPORTS = [
     "atlas_cuda_decode", "atlas_cuda_generate", "atlas_cuda_stats", "atlas_cuda_dequant",
     "atlas_cuda_gemv", "atlas_cuda_gemm", "atlas_cuda_device_info", "atlas_cuda_trace_step",
     "atlas_cuda_device_ms", "atlas_cuda_trace_graph", "atlas_cuda_gemv_noalloc", "atlas_cuda_tp_slice", "atlas_cuda_tp_handle",
-    "atlas_cuda_tp_connect",
+    "atlas_cuda_tp_connect", "atlas_cuda_prefill_seq", "atlas_cuda_generate_batch", "atlas_cuda_decode_batch",
     "brain_gpu_init", "brain_gpu_matvec_batch", "brain_gpu_matvec", "brain_gpu_shutdown",
     "atlas_rt_open", "atlas_rt_close", "atlas_rt_error", "atlas_rt_shape", "atlas_rt_data_base",
     "atlas_rt_find_tensor", "atlas_rt_file_bytes", "atlas_rt_device", "atlas_rt_forward_token",
@@ -66,7 +66,7 @@ class TensorInfo(ctypes.Structure):
 class RtOptions(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("max_context", ctypes.c_uint32), ("max_prefill", ctypes.c_uint32),
                 ("kv_fp16", ctypes.c_int32), ("no_device", ctypes.c_int32), ("tp_rank", ctypes.c_int32),
-                ("tp_size", ctypes.c_int32)]
+                ("tp_size", ctypes.c_int32), ("max_batch", ctypes.c_uint32)]
 
 
 class ModelDesc(ctypes.Structure):
@@ -75,7 +75,8 @@ class ModelDesc(ctypes.Structure):
                 ("hidden", "q_dim", "kv_dim", "q_heads", "kv_heads", "head_dim", "ffn", "layers", "vocab",
                  "max_context", "max_prefill")] + [
         ("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)] + [
-        (n, ctypes.c_int32) for n in ("has_qk_norm", "kv_fp16", "device", "tp_rank", "tp_size")]
+        (n, ctypes.c_int32) for n in ("has_qk_norm", "kv_fp16", "device", "tp_rank", "tp_size")] + [
+        ("max_batch", ctypes.c_uint32)]
 
 
 class TpSlice(ctypes.Structure):
@@ -139,6 +140,9 @@ def lib() -> ctypes.CDLL:
         L.atlas_rt_forward_token.argtypes = [P, U32, U32, P, P]
         L.atlas_rt_prefill.argtypes = [P, P, U32, U32, P, P]
         L.atlas_rt_generate.argtypes = [P, U32, U32, U32, P]
+        L.atlas_cuda_prefill_seq.argtypes = [P, U32, P, U32, U32, P, P]
+        L.atlas_cuda_generate_batch.argtypes = [P, U32, P, P, U32, P]
+        L.atlas_cuda_decode_batch.argtypes = [P, U32, P, P, P, P]
         L.atlas_synth_write_gguf.argtypes = [P, ctypes.c_char_p]
         L.atlas_synth_q4k_blocks.argtypes = [U64, U64, P, U64]
         L.atlas_synth_q6k_blocks.argtypes = [U64, U64, P, U64]
@@ -193,9 +197,10 @@ class Runtime:
     """Reference-shaped model API: open a GGUF, forward tokens, prefill, generate."""
 
     def __init__(self, path: str, *, device: int = 0, max_context: int = 0, max_prefill: int = 0,
-                 kv_fp16: bool = False, no_device: bool = False, tp_rank: int = 0, tp_size: int = 1):
+                 kv_fp16: bool = False, no_device: bool = False, tp_rank: int = 0, tp_size: int = 1,
+                 max_batch: int = 1):
         self._h = ctypes.c_void_p()
-        opt = RtOptions(device, max_context, max_prefill, int(kv_fp16), int(no_device), tp_rank, tp_size)
+        opt = RtOptions(device, max_context, max_prefill, int(kv_fp16), int(no_device), tp_rank, tp_size, max_batch)
         self.tp_rank, self.tp_size = tp_rank, tp_size
         rc = lib().atlas_rt_open(path.encode(), ctypes.byref(opt), ctypes.byref(self._h))
         if rc != ATLAS_OK:
@@ -241,6 +246,40 @@ class Runtime:
         out = np.zeros(steps, np.uint32)
         self._check(lib().atlas_rt_generate(self._h, first, pos0, steps, _ptr(out)), "generate")
         return out
+
+    def prefill_seq(self, seq: int, ids, pos0: int = 0, want_logits: bool = True):
+        """atlas_cuda_prefill into sequence seq's KV cache (open with max_batch > seq)."""
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        am = ctypes.c_uint32()
+        dev = lib().atlas_rt_device(self._h)
+        check(lib().atlas_cuda_prefill_seq(dev, seq, _ptr(ids), len(ids), pos0, _ptr(logits), ctypes.byref(am)),
+              "prefill_seq", dev)
+        return logits, am.value
+
+    def generate_batch(self, first, pos0, steps: int):
+        """Greedy steps of len(first) sequences at once: array [nseq, steps] of picks."""
+        import numpy as np
+        first = np.ascontiguousarray(first, dtype=np.uint32)
+        pos0 = np.ascontiguousarray(pos0, dtype=np.uint32)
+        out = np.zeros((len(first), steps), np.uint32)
+        dev = lib().atlas_rt_device(self._h)
+        check(lib().atlas_cuda_generate_batch(dev, len(first), _ptr(first), _ptr(pos0), steps, _ptr(out)),
+              "generate_batch", dev)
+        return out
+
+    def decode_batch(self, ids, pos, want_logits: bool = True):
+        """One step of len(ids) sequences: (logits [nseq, vocab] or None, picks [nseq])."""
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        pos = np.ascontiguousarray(pos, dtype=np.uint32)
+        logits = np.zeros((len(ids), self.vocab), np.float32) if want_logits else None
+        am = np.zeros(len(ids), np.uint32)
+        dev = lib().atlas_rt_device(self._h)
+        check(lib().atlas_cuda_decode_batch(dev, len(ids), _ptr(ids), _ptr(pos), _ptr(logits), _ptr(am)),
+              "decode_batch", dev)
+        return logits, am
 
     def trace_step(self, token: int, pos: int):
         """One traced decode step: (stamps[cta, phase, 4], inner stamps[cta, phase, 8], phase kind codes)."""

@@ -74,6 +74,7 @@ typedef struct {
     int32_t device;        /* CUDA device ordinal */
     int32_t tp_rank;       /* tensor-parallel rank, 0..tp_size-1 (one process per GPU) */
     int32_t tp_size;       /* 1, or 2 / 4 / 8 when kv_heads % tp_size == 0 (see atlas_cuda_tp_*) */
+    uint32_t max_batch;    /* sequences with a KV cache of their own (0 or 1: one); see atlas_cuda_generate_batch */
 } AtlasModelDesc;
 
 /* KV-cache precision: the reference keeps K and V in fp32 (src/brain_runtime.c:2019-2020).
@@ -107,6 +108,24 @@ int atlas_cuda_generate(AtlasCuda *h, uint32_t first, uint32_t pos0, uint32_t st
 
 /* Per-phase device time of the last decode/generate call and kernel launch
    counts since creation (diagnostics for the benchmark). */
+/* Several independent sequences (no counterpart in the reference, which runs one
+   sequence per process, src/brain_runtime.c:1698 and :2036-2048; the per-sequence
+   arithmetic is forward_token's). Sequence s (s < desc.max_batch) has its own KV
+   cache; sequence 0's is the one atlas_cuda_prefill / decode / generate use.
+   Q4_K / Q6_K files, one GPU.
+   atlas_cuda_prefill_seq: atlas_cuda_prefill into sequence seq's cache.
+   atlas_cuda_generate_batch: `steps` greedy steps of nseq <= 8 sequences at once,
+     sequence s starting from token first[s] at position pos0[s]; out_ids[s * steps + i]
+     is the pick after step i (every weight is read once per step for all sequences).
+   atlas_cuda_decode_batch: one step: token ids[s] at position pos[s] for each
+     sequence; logits [nseq][vocab] (or NULL) and the greedy picks argmax[nseq]. */
+int atlas_cuda_prefill_seq(AtlasCuda *h, uint32_t seq, const uint32_t *ids, uint32_t n, uint32_t pos0,
+                           float *last_logits, uint32_t *argmax);
+int atlas_cuda_generate_batch(AtlasCuda *h, uint32_t nseq, const uint32_t *first, const uint32_t *pos0,
+                              uint32_t steps, uint32_t *out_ids);
+int atlas_cuda_decode_batch(AtlasCuda *h, uint32_t nseq, const uint32_t *ids, const uint32_t *pos, float *logits,
+                            uint32_t *argmax);
+
 int atlas_cuda_stats(const AtlasCuda *h, uint64_t *kernel_launches, double *last_ms);
 
 /* Device time (CUDA events on the handle's stream) summed over every decode /

@@ -54,6 +54,7 @@ typedef struct {
     int32_t no_device;     /* 1: parse only (no GPU work) */
     int32_t tp_rank;       /* tensor parallel: this process's rank ... */
     int32_t tp_size;       /* ... of tp_size (0 or 1: one GPU); see atlas_cuda_tp_* */
+    uint32_t max_batch;    /* sequences with a KV cache of their own (0 or 1: one); atlas_cuda_generate_batch */
 } AtlasRtOptions;
 
 int atlas_rt_open(const char *path, const AtlasRtOptions *opt, AtlasRuntime **out);
