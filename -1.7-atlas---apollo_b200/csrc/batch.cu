@@ -69,13 +69,24 @@ __host__ __device__ constexpr uint32_t smem_total(uint32_t sb, uint32_t nslot, u
 }
 
 // ------------------------------------------------------------- staging ----
+//
+// Quad e4 of sequence s sits at x unit e4 * 8 + col(e4, s): a 16-byte load is
+// served 8 lanes at a time, and the 8 lanes of a phase - rows g = 2p, 2p + 1,
+// k positions t = 0..3 - must fall in 8 distinct 16-byte bank groups. Their
+// quads are e4 = base + 2t (Q4_K words) or base + t (Q6_K words), so the
+// column is the sequence XOR twice a 2-bit function of e4 that runs over all 4
+// values as t does.
+__device__ __forceinline__ uint32_t xcol(uint32_t e4, uint32_t s, bool q4)
+{
+    return s ^ ((q4 ? ((e4 >> 1) & 3u) : (e4 & 3u)) << 1);
+}
 
 // The CTA's K slice (blocks b0 .. b0 + nbs - 1) of every sequence's input:
 // pass 1 stores x (times the norm weight) as floats in the quad slots and
 // takes each sequence's max |x|; pass 2 scales by a power of two putting the
 // max in [2^13, 2^14), splits into binary16 hi + lo in place and writes the
 // 16-element sums. Sequences >= nseq are zeros.
-__device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t b0, uint32_t nbs)
+__device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t b0, uint32_t nbs, bool q4)
 {
     const uint32_t nq = nbs * 64u, total = nq * kMaxSeq;
     const uint32_t lane = threadIdx.x & 31u;
@@ -91,7 +102,7 @@ __device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t 
                 v.x *= w.x; v.y *= w.y; v.z *= w.z; v.w *= w.w;
             }
         }
-        xf[e4 * kMaxSeq + s] = v;
+        xf[e4 * kMaxSeq + xcol(e4, s, q4)] = v;
         float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -111,7 +122,7 @@ __device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t 
     for (uint32_t i = threadIdx.x; i < total; i += kBThreads) {
         const uint32_t s = (i >> 2) & 7u, e4 = (i >> 5) * 4u + (i & 3u);
         const float sc = __uint_as_float(h->smax[s]);
-        const float4 v = xf[e4 * kMaxSeq + s];
+        const float4 v = xf[e4 * kMaxSeq + xcol(e4, s, q4)];
         const float e0 = v.x * sc, e1 = v.y * sc, e2 = v.z * sc, e3 = v.w * sc;
         const __half2 h01 = __floats2half2_rn(e0, e1), h23 = __floats2half2_rn(e2, e3);
         const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
@@ -121,7 +132,7 @@ __device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t 
         pk.y = *reinterpret_cast<const uint32_t *>(&h23);
         pk.z = *reinterpret_cast<const uint32_t *>(&l01);
         pk.w = *reinterpret_cast<const uint32_t *>(&l23);
-        xq[e4 * kMaxSeq + s] = pk;   // in place: the slot is this item's only
+        xq[e4 * kMaxSeq + xcol(e4, s, q4)] = pk;   // in place: the slot is this item's only
         float sum = (e0 + e1) + (e2 + e3);
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
@@ -168,7 +179,8 @@ __device__ __forceinline__ void q4k_task8(const uint8_t *r0, const uint8_t *r1, 
             for (uint32_t s = 0; s < 2u; ++s) {
                 const uint32_t m = hn ? 0xf0f0f0f0u : 0x0f0f0f0fu;
                 const uint32_t v0 = (s ? w0.y : w0.x) & m, v1 = (s ? w1.y : w1.x) & m;
-                const uint4 xv = xq[(16u * c + 8u * hn + 2u * t + s) * kMaxSeq + g];
+                const uint32_t e4 = 16u * c + 8u * hn + 2u * t + s;
+                const uint4 xv = xq[e4 * kMaxSeq + xcol(e4, g, true)];
                 const uint32_t a0 = sub2(v0, 0x4140), a1 = sub2(v1, 0x4140), a2 = sub2(v0, 0x4342), a3 = sub2(v1, 0x4342);
                 const float ch[4] = {chi[0], chi[1], chi[2], chi[3]}, cl[4] = {clo[0], clo[1], clo[2], clo[3]};
                 mma16816(chi, a0, a1, a2, a3, make_uint2(xv.x, xv.y), ch);
@@ -216,7 +228,8 @@ __device__ __forceinline__ void q6k_task8(const uint8_t *r0, const uint8_t *r1, 
                 const uint32_t ns = 4u * (k >> 1);
                 const uint32_t v0 = ((lo0 >> ns) & 0x0f0f0f0fu) | (((qh0 >> (2u * k)) & 0x03030303u) << 4);
                 const uint32_t v1 = ((lo1 >> ns) & 0x0f0f0f0fu) | (((qh1 >> (2u * k)) & 0x03030303u) << 4);
-                const uint4 xv = xq[(32u * h + 8u * k + 4u * l16 + t) * kMaxSeq + g];
+                const uint32_t e4 = 32u * h + 8u * k + 4u * l16 + t;
+                const uint4 xv = xq[e4 * kMaxSeq + xcol(e4, g, false)];
                 const uint32_t a0 = sub2(v0, 0x4140), a1 = sub2(v1, 0x4140), a2 = sub2(v0, 0x4342), a3 = sub2(v1, 0x4342);
                 const float zero[4] = {0.f, 0.f, 0.f, 0.f};
                 float chi[4], clo[4];
@@ -324,7 +337,7 @@ __device__ void consume(const BArgs &a, const BCta &c, BHdr *h, float *pslot, ui
         cpa_commit();
     }
     if (a.pdl) pdl_wait();
-    stage_x(a, h, xq, xs, b0, nbs);
+    stage_x(a, h, xq, xs, b0, nbs, Q4);
     if (!active) return;
     auto warp_of = [&](uint32_t j) { return ((j + 1u) * weff + L - 1u) / L - 1u; };
     const uint32_t first = my0 / nbs, lastt = (my1 - 1u) / nbs;
@@ -413,115 +426,118 @@ __global__ void __launch_bounds__(kBThreads, 1) mvb_kernel(const __grid_constant
 
 // ------------------------------------------------------ reduce kernels ----
 
-// Partial rows -> outputs for every sequence. CTA b takes rows
-// [b R, (b + 1) R) of every sequence; slices are added in slice order.
+// Sum of squares of the 256 values v of a CTA (one per thread), in double, by
+// a fixed tree.
+__device__ __forceinline__ double block_ssq(float v, double *red)
+{
+    double ss = (double)v * (double)v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < 8; ++w) t += red[w];
+    return t;
+}
+
+__device__ __forceinline__ float rms_factor(const double *ssq, uint32_t n, uint32_t s, uint32_t hidden, float eps)
+{
+    if (!ssq) return 1.0f;
+    double t = 0.0;
+    for (uint32_t i = 0; i < n; ++i) t += ssq[s * n + i];
+    return 1.0f / sqrtf((float)(t / (double)hidden) + eps);
+}
+
+// Partial rows -> outputs: thread = (row, sequence blockIdx.y); slices are
+// added in slice order.
 __global__ void __launch_bounds__(256) reduce_kernel(const __grid_constant__ BReduce a)
 {
     __shared__ float bv[8];
     __shared__ uint32_t bi[8];
     pdl_launch();
     if (a.pdl) pdl_wait();
-    const uint32_t per = (a.rows + gridDim.x - 1u) / gridDim.x;
-    const uint32_t r0 = blockIdx.x * per, r1 = min(a.rows, r0 + per);
-    for (uint32_t s = 0; s < a.nseq; ++s) {
-        const float inv = a.inv ? a.inv[s] : 1.0f;
-        float best = -FLT_MAX;
-        uint32_t idx = 0xffffffffu;
-        for (uint32_t r = r0 + threadIdx.x; r < r1; r += 256u) {
-            float v = 0.f, u = 0.f;
-            for (uint32_t k = 0; k < a.nsplit; ++k) {
-                const float *p = a.part + ((size_t)k * a.nseq + s) * a.prows;
-                v += __ldcg(p + r);
-                if (a.mode == BRED_SWIGLU) u += __ldcg(p + a.rows + r);
-            }
-            v *= inv;
-            if (a.mode == BRED_SWIGLU) {
-                u *= inv;
-                v = (v / (1.0f + expf(-v))) * u;   // src/brain_runtime.c:1755-1758
-            } else if (a.bias) {
-                v += a.bias[r];
-            }
-            a.out[(size_t)s * a.ostride + r] = v;
-            if (v > best || (v == best && r < idx)) { best = v; idx = r; }
+    const uint32_t s = blockIdx.y, r = blockIdx.x * kRowChunk + threadIdx.x;
+    const float inv = rms_factor(a.ssq, a.nssq, s, a.hidden, a.eps);
+    float v = -FLT_MAX;
+    if (r < a.rows) {
+        float x = 0.f, u = 0.f;
+        for (uint32_t k = 0; k < a.nsplit; ++k) {
+            const float *p = a.part + ((size_t)k * a.nseq + s) * a.prows;
+            x += __ldcg(p + r);
+            if (a.mode == BRED_SWIGLU) u += __ldcg(p + a.rows + r);
         }
-        if (a.mode != BRED_LOGITS) continue;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+        x *= inv;
+        if (a.mode == BRED_SWIGLU) {
+            u *= inv;
+            x = (x / (1.0f + expf(-x))) * u;   // src/brain_runtime.c:1755-1758
+        } else if (a.bias) {
+            x += a.bias[r];
         }
-        const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-        if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int w = 1; w < 8; ++w)
-                if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
-            a.pmax[s * gridDim.x + blockIdx.x] = best;
-            a.pidx[s * gridDim.x + blockIdx.x] = idx;
-        }
-        __syncthreads();
+        a.out[(size_t)s * a.ostride + r] = x;
+        v = x;
     }
-}
-
-// Residual add for sequence blockIdx.x, then its rms factor: the sum of
-// squares in double over a fixed thread layout and tree (the same result for
-// the same x on every run).
-__global__ void __launch_bounds__(512) resid_kernel(const __grid_constant__ BResid a)
-{
-    __shared__ double red[16];
-    pdl_launch();
-    if (a.pdl) pdl_wait();
-    const uint32_t s = blockIdx.x;
-    float *x = a.x + (size_t)s * a.hidden;
-    double ss = 0.0;
-    for (uint32_t r = threadIdx.x; r < a.hidden; r += 512u) {
-        float v = x[r];
-        for (uint32_t k = 0; k < a.nsplit; ++k) v += __ldcg(a.part + ((size_t)k * a.nseq + s) * a.prows + r);
-        x[r] = v;   // src/brain_runtime.c:1745, :1762
-        ss += (double)v * (double)v;
-    }
+    if (a.mode != BRED_LOGITS) return;
+    float best = v;
+    uint32_t idx = r < a.rows ? r : 0xffffffffu;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = ss;
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
     __syncthreads();
     if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int w = 0; w < 16; ++w) t += red[w];
-        a.inv[s] = 1.0f / sqrtf((float)(t / (double)a.hidden) + a.eps);
+        for (int w = 1; w < 8; ++w)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
+        a.pmax[s * gridDim.x + blockIdx.x] = best;
+        a.pidx[s * gridDim.x + blockIdx.x] = idx;
     }
 }
 
-// Token rows of every sequence (bit-exact dequantization) and their rms factors.
-__global__ void __launch_bounds__(512) embedb_kernel(const uint8_t *embd, uint64_t row_bytes, uint32_t type,
-                                                     uint32_t hidden, uint32_t vocab, float *x, float *inv, float eps,
+// Residual add (src/brain_runtime.c:1745, :1762): thread = (row, sequence
+// blockIdx.y); the chunk's sum of squares for the next rms_norm.
+__global__ void __launch_bounds__(256) resid_kernel(const __grid_constant__ BResid a)
+{
+    __shared__ double red[8];
+    pdl_launch();
+    if (a.pdl) pdl_wait();
+    const uint32_t s = blockIdx.y, r = blockIdx.x * kRowChunk + threadIdx.x;
+    float v = 0.f;
+    if (r < a.hidden) {
+        float *x = a.x + (size_t)s * a.hidden;
+        v = x[r];
+        for (uint32_t k = 0; k < a.nsplit; ++k) v += __ldcg(a.part + ((size_t)k * a.nseq + s) * a.prows + r);
+        x[r] = v;
+    }
+    const double t = block_ssq(v, red);
+    if (threadIdx.x == 0) a.ssq[s * gridDim.x + blockIdx.x] = t;
+}
+
+// Token rows of every sequence (bit-exact dequantization): thread = (element,
+// sequence blockIdx.y), and the chunk's sum of squares.
+__global__ void __launch_bounds__(256) embedb_kernel(const uint8_t *embd, uint64_t row_bytes, uint32_t type,
+                                                     uint32_t hidden, uint32_t vocab, float *x, double *ssq,
                                                      d2::DecState *st)
 {
-    __shared__ double red[16];
+    __shared__ double red[8];
     pdl_launch();
-    const uint32_t s = blockIdx.x;
+    const uint32_t s = blockIdx.y, i = blockIdx.x * kRowChunk + threadIdx.x;
     const uint32_t token = *reinterpret_cast<volatile const uint32_t *>(&st[s].token);
     if (token >= vocab) {
-        if (threadIdx.x == 0) atomicCAS(&st[s].status, kStatusOk, kStatusBadArgument);
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&st[s].status, kStatusOk, kStatusBadArgument);
         return;
     }
     const uint32_t be = block_elems(type), bbytes = block_bytes(type);
-    const uint8_t *row = embd + (uint64_t)token * row_bytes;
-    double ss = 0.0;
-    for (uint32_t i = threadIdx.x; i < hidden; i += 512u) {
-        const float v = deq_elem(type, row + (i / be) * bbytes, (int)(i % be));
+    float v = 0.f;
+    if (i < hidden) {
+        v = deq_elem(type, embd + (uint64_t)token * row_bytes + (i / be) * bbytes, (int)(i % be));
         x[(size_t)s * hidden + i] = v;
-        ss += (double)v * (double)v;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int w = 0; w < 16; ++w) t += red[w];
-        inv[s] = 1.0f / sqrtf((float)(t / (double)hidden) + eps);
-    }
+    const double t = block_ssq(v, red);
+    if (threadIdx.x == 0) ssq[s * gridDim.x + blockIdx.x] = t;
 }
 
 // Greedy pick of sequence blockIdx.x over the reduce's per-CTA (max, row)
@@ -622,26 +638,31 @@ extern "C" cudaError_t atlas_bt_launch_mv(const BArgs *a, uint32_t grid, cudaStr
     return launch_ex(fn, args, dim3(grid), dim3(kBThreads), a->smem_bytes, stream, a->pdl != 0u);
 }
 
+// grid: row chunks of kRowChunk (BRED_LOGITS: the pmax / pidx columns per sequence)
 extern "C" cudaError_t atlas_bt_launch_reduce(const BReduce *a, uint32_t grid, cudaStream_t stream)
 {
+    if (grid * kRowChunk < a->rows) return cudaErrorInvalidValue;
     BReduce copy = *a;
     void *args[] = {&copy};
-    return launch_ex((const void *)reduce_kernel, args, dim3(grid), dim3(256), 0, stream, a->pdl != 0u);
+    return launch_ex((const void *)reduce_kernel, args, dim3(grid, a->nseq), dim3(kRowChunk), 0, stream,
+                     a->pdl != 0u);
 }
 
 extern "C" cudaError_t atlas_bt_launch_resid(const BResid *a, cudaStream_t stream)
 {
     BResid copy = *a;
     void *args[] = {&copy};
-    return launch_ex((const void *)resid_kernel, args, dim3(a->nseq), dim3(512), 0, stream, a->pdl != 0u);
+    return launch_ex((const void *)resid_kernel, args, dim3((a->hidden + kRowChunk - 1u) / kRowChunk, a->nseq),
+                     dim3(kRowChunk), 0, stream, a->pdl != 0u);
 }
 
 extern "C" cudaError_t atlas_bt_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,
-                                             uint32_t vocab, float *x, float *inv, float eps, d2::DecState *st,
-                                             uint32_t nseq, cudaStream_t stream)
+                                             uint32_t vocab, float *x, double *ssq, d2::DecState *st, uint32_t nseq,
+                                             cudaStream_t stream)
 {
-    void *args[] = {&embd, &row_bytes, &type, &hidden, &vocab, &x, &inv, &eps, &st};
-    return launch_ex((const void *)embedb_kernel, args, dim3(nseq), dim3(512), 0, stream, false);
+    void *args[] = {&embd, &row_bytes, &type, &hidden, &vocab, &x, &ssq, &st};
+    return launch_ex((const void *)embedb_kernel, args, dim3((hidden + kRowChunk - 1u) / kRowChunk, nseq),
+                     dim3(kRowChunk), 0, stream, false);
 }
 
 extern "C" cudaError_t atlas_bt_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n, d2::DecState *st,

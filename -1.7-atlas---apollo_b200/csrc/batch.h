@@ -62,12 +62,17 @@ enum BRedMode : uint32_t {
     BRED_LOGITS = 2,   // out = inv * sum, and per-CTA per-sequence (max, row)
 };
 
+// Grid (row chunks of 256, nseq). The rms factor of sequence s is
+// 1 / sqrt(sum(ssq[s][0..nssq)) / hidden + eps) (src/brain_runtime.c:1345-1360,
+// the sum of squares in double), or 1 without ssq.
 struct BReduce {
     const float *part;
     uint32_t nsplit, nseq, prows;
     uint32_t mode, rows;
     const float *bias;     // [rows] or null
-    const float *inv;      // [nseq] rms factors, or null (1)
+    const double *ssq;     // [nseq][nssq] partial sums of squares of the normed input, or null
+    uint32_t nssq, hidden;
+    float eps;
     float *out;            // out[s * ostride + r]
     uint32_t ostride;
     float *pmax;           // BRED_LOGITS: [nseq][gridDim.x]
@@ -75,17 +80,17 @@ struct BReduce {
     uint32_t pdl;
 };
 
-// x[s] += sum of the partial rows; inv[s] = 1 / sqrt(mean(x[s]^2) + eps)
-// (src/brain_runtime.c:1345-1360, the sum of squares in double).
+// Grid (row chunks of 256, nseq): x[s] += the sum of the partial rows, and
+// chunk c's sum of squares of the new x[s] into ssq[s * gridDim.x + c].
 struct BResid {
     const float *part;
     uint32_t nsplit, nseq, prows;
     float *x;
     uint32_t hidden;
-    float *inv;
-    float eps;
+    double *ssq;
     uint32_t pdl;
 };
+constexpr uint32_t kRowChunk = 256;
 
 // Dynamic shared memory of an mvb CTA.
 size_t mvb_smem(uint32_t split_blocks, uint32_t nslot, uint32_t slot_bytes);
@@ -99,8 +104,8 @@ cudaError_t atlas_bt_launch_mv(const atlas::bt::BArgs *a, uint32_t grid, cudaStr
 cudaError_t atlas_bt_launch_reduce(const atlas::bt::BReduce *a, uint32_t grid, cudaStream_t stream);
 cudaError_t atlas_bt_launch_resid(const atlas::bt::BResid *a, cudaStream_t stream);
 cudaError_t atlas_bt_launch_embed(const uint8_t *embd, uint64_t row_bytes, uint32_t type, uint32_t hidden,
-                                  uint32_t vocab, float *x, float *inv, float eps, atlas::d2::DecState *st,
-                                  uint32_t nseq, cudaStream_t stream);
+                                  uint32_t vocab, float *x, double *ssq, atlas::d2::DecState *st, uint32_t nseq,
+                                  cudaStream_t stream);
 cudaError_t atlas_bt_launch_argmax(const float *pmax, const uint32_t *pidx, uint32_t n, atlas::d2::DecState *st,
                                    uint32_t nseq, cudaStream_t stream);
 }

@@ -171,7 +171,8 @@ struct AtlasCuda {
         uint32_t nseq = 0, kernels = 0, out_cap = 0, red_logits = 0;
         size_t part_cap = 0;   // floats
         d2::DecState *st = nullptr;
-        float *x = nullptr, *qkv = nullptr, *att = nullptr, *ffn = nullptr, *logits = nullptr, *inv = nullptr;
+        float *x = nullptr, *qkv = nullptr, *att = nullptr, *ffn = nullptr, *logits = nullptr;
+        double *ssq = nullptr;   // [sequence][row chunk] sums of squares of the residual stream
         float *part = nullptr, *apart = nullptr, *pmax = nullptr;
         uint32_t *actr = nullptr, *pidx = nullptr, *out_ids = nullptr;
         std::vector<float *> qkv_bias;   // per layer: q, k, v biases back to back (null: none)
@@ -1826,7 +1827,7 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
         if ((rc = dalloc(h, &b.st, B * sizeof(d2::DecState))) || (rc = dalloc(h, &b.x, (size_t)B * d.hidden * 4)) ||
             (rc = dalloc(h, &b.qkv, (size_t)B * qkvw * 4)) || (rc = dalloc(h, &b.att, (size_t)B * d.q_dim * 4)) ||
             (rc = dalloc(h, &b.ffn, (size_t)B * d.ffn * 4)) || (rc = dalloc(h, &b.logits, (size_t)B * d.vocab * 4)) ||
-            (rc = dalloc(h, &b.inv, B * 4)) ||
+            (rc = dalloc(h, &b.ssq, (size_t)B * ((d.hidden + bt::kRowChunk - 1u) / bt::kRowChunk) * 8)) ||
             (rc = dalloc(h, &b.apart, (size_t)B * d.kv_heads * (h->g2.splits / C) * group * d2::kRec * 4)) ||
             (rc = dalloc(h, &b.actr, (size_t)B * d.q_heads * 4)))
             return rc;
@@ -1844,7 +1845,7 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
             if (w.bv) CU(h, cudaMemcpy(bb + d.q_dim + d.kv_dim, w.bv, (size_t)d.kv_dim * 4, cudaMemcpyDeviceToDevice));
             b.qkv_bias[l] = bb;
         }
-        b.red_logits = std::min(2u * G, (d.vocab + 1023u) / 1024u);
+        b.red_logits = (d.vocab + bt::kRowChunk - 1u) / bt::kRowChunk;
         if ((rc = dalloc(h, &b.pmax, (size_t)B * b.red_logits * 4)) || (rc = dalloc(h, &b.pidx, (size_t)B * b.red_logits * 4)))
             return rc;
     }
@@ -1900,6 +1901,8 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
     at.ctr_seq = d.q_heads;
     at.cache_seq_bytes = h->kv_seq_bytes;
     const uint64_t embd_row = (uint64_t)(d.hidden / block_elems(h->t_embd)) * block_bytes(h->t_embd);
+    const uint32_t nchunk = (d.hidden + bt::kRowChunk - 1u) / bt::kRowChunk;
+    auto chunks = [](uint32_t rows) { return (rows + bt::kRowChunk - 1u) / bt::kRowChunk; };
     auto reduce = [&](const BPlan &p, uint32_t mode, uint32_t rows, const float *bias, float *out, uint32_t grid) {
         bt::BReduce r{};
         r.part = b.part;
@@ -1909,7 +1912,10 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
         r.mode = mode;
         r.rows = rows;
         r.bias = bias;
-        r.inv = b.inv;
+        r.ssq = b.ssq;
+        r.nssq = nchunk;
+        r.hidden = d.hidden;
+        r.eps = d.rms_eps;
         r.out = out;
         r.ostride = rows;
         r.pmax = b.pmax;
@@ -1925,8 +1931,7 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
         r.prows = p.a.prows;
         r.x = b.x;
         r.hidden = d.hidden;
-        r.inv = b.inv;
-        r.eps = d.rms_eps;
+        r.ssq = b.ssq;
         r.pdl = 1u;
         return atlas_bt_launch_resid(&r, h->stream);
     };
@@ -1940,13 +1945,13 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
     };
     CU(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
     uint32_t k = 0;
-    cudaError_t e = atlas_bt_launch_embed(h->embd, embd_row, h->t_embd, d.hidden, d.vocab, b.x, b.inv, d.rms_eps, b.st,
-                                          nseq, h->stream);
+    cudaError_t e = atlas_bt_launch_embed(h->embd, embd_row, h->t_embd, d.hidden, d.vocab, b.x, b.ssq, b.st, nseq,
+                                          h->stream);
     ++k;
     for (uint32_t l = 0; l < d.layers && e == cudaSuccess; ++l) {
         const AtlasCuda::W &w = h->layers[l];
         if ((e = mv(lp[l][0], b.x, d.hidden, w.attn_norm)) != cudaSuccess) break;
-        if ((e = reduce(lp[l][0], bt::BRED_STORE, qkvw, b.qkv_bias[l], b.qkv, (qkvw + 1023u) / 1024u)) != cudaSuccess) break;
+        if ((e = reduce(lp[l][0], bt::BRED_STORE, qkvw, b.qkv_bias[l], b.qkv, chunks(qkvw))) != cudaSuccess) break;
         at.k_cache = w.kc;
         at.v_cache = w.vc;
         at.q_norm = w.qn;
@@ -1955,7 +1960,7 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
         if ((e = mv(lp[l][1], b.att, d.q_dim, nullptr)) != cudaSuccess) break;
         if ((e = resid(lp[l][1])) != cudaSuccess) break;
         if ((e = mv(lp[l][2], b.x, d.hidden, w.ffn_norm)) != cudaSuccess) break;
-        if ((e = reduce(lp[l][2], bt::BRED_SWIGLU, d.ffn, nullptr, b.ffn, (d.ffn + 1023u) / 1024u)) != cudaSuccess) break;
+        if ((e = reduce(lp[l][2], bt::BRED_SWIGLU, d.ffn, nullptr, b.ffn, chunks(d.ffn))) != cudaSuccess) break;
         if ((e = mv(lp[l][3], b.ffn, d.ffn, nullptr)) != cudaSuccess) break;
         if ((e = resid(lp[l][3])) != cudaSuccess) break;
         k += 9;

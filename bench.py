@@ -57,6 +57,13 @@ WORKLOAD = {
     "cfg1": "Qwen2.5-3B-shaped Q4_K/Q6_K (hidden 2048, 36 layers, 16/2 heads, FFN 11008, vocab 151936, tied Q6_K "
             "head): 512-token prefill + 256 greedy decode, batch 1",
 }
+# The 8-sequence workload (--workload 32b-batch8): Qwen2.5-32B shape, 8 independent sequences, each a
+# 2048-token prompt prefilled batched, then 256 decode steps at batch 8 (all sequences in one step).
+CFG4 = dict(hidden=5120, layers=64, q_heads=40, kv_heads=8, ffn=27648, vocab=152064, context_length=32768, seed=4,
+            tied=False)
+WORKLOAD["cfg4"] = ("Qwen2.5-32B-shaped Q4_K/Q6_K (hidden 5120, 64 layers, 40/8 heads, FFN 27648, vocab 152064, untied "
+                    "Q6_K head): 8 independent sequences, each a 2048-token prefill, then 256 decode steps at batch 8")
+B8_SEQ, B8_PROMPT, B8_GEN = 8, 2048, 256
 PROMPT, GEN, PROMPT_SEED = 512, 256, 1234
 METRIC = "decode tok/s (batch 1) & % HBM roofline; prefill tok/s at 512-token prompt"
 Q4K, Q6K = 144.0 / 256.0, 210.0 / 256.0
@@ -461,6 +468,90 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+def run_batch8(args):
+    """The 32B-shaped 8-sequence workload on one GPU: every sequence's prompt through the batched prefill
+    (atlas_cuda_prefill_seq), then B8_GEN steps of all 8 sequences at once (atlas_cuda_generate_batch). value =
+    aggregate decode tok/s (8 tokens per step). Consistency: sequence 0's batch-8 picks equal its batch-1 picks
+    from the same prefill."""
+    import numpy as np
+    import atlas_cuda
+    cfg4 = dict(CFG4, layers=args.layers) if args.layers else CFG4
+    name4 = "cfg4" if not args.layers else f"cfg4_l{args.layers}"
+    path = ensure_model_product_writer(name4, cfg4, 0, None)
+    V = cfg4["vocab"]
+    prompts = [np.random.default_rng(PROMPT_SEED + s).integers(0, V, B8_PROMPT).astype(np.uint32)
+               for s in range(B8_SEQ)]
+    with atlas_cuda.Runtime(path, max_context=B8_PROMPT + B8_GEN + 16, max_prefill=B8_PROMPT,
+                            max_batch=B8_SEQ) as rt:
+        def step():
+            d0, t0 = rt.stats()[2], time.perf_counter()
+            first = [rt.prefill_seq(s, prompts[s], 0, want_logits=False)[1] for s in range(B8_SEQ)]
+            d1, t1 = rt.stats()[2], time.perf_counter()
+            ids = rt.generate_batch(first, [B8_PROMPT] * B8_SEQ, B8_GEN)
+            d2, t2 = rt.stats()[2], time.perf_counter()
+            return dict(pre_dev=(d1 - d0) / 1e3, gen_dev=(d2 - d1) / 1e3, pre_wall=t1 - t0, gen_wall=t2 - t1,
+                        first=first, ids=ids)
+        ref = None
+        for _ in range(args.warmup):
+            ref = step()
+        launches0 = rt.stats()[0]
+        res = []
+        with Clocks(0) as clk:
+            for _ in range(args.steps):
+                r = step()
+                if ref is not None and not np.array_equal(r["ids"], ref["ids"]):
+                    raise AssertionError("32b-batch8: greedy output changed between steps")
+                ref = r
+                res.append(r)
+        launches = rt.stats()[0] - launches0
+        # sequence 0 alone at batch 1 from the same prompt
+        _, f0 = rt.prefill_seq(0, prompts[0], 0, want_logits=False)
+        nchk = min(32, B8_GEN)
+        single = rt.generate(f0, B8_PROMPT, nchk)
+        consistent = bool(f0 == ref["first"][0] and np.array_equal(single, ref["ids"][0][:nchk]))
+    gen_dev = sum(r["gen_dev"] for r in res)
+    pre_dev = sum(r["pre_dev"] for r in res)
+    gen_wall = sum(r["gen_wall"] for r in res)
+    pre_wall = sum(r["pre_wall"] for r in res)
+    steps_s = gen_dev / (args.steps * B8_GEN)
+    kv_step = kv_bytes_per_position(cfg4) * (B8_PROMPT + B8_GEN / 2.0) * B8_SEQ
+    step_bytes = weight_bytes(cfg4) + kv_step
+    hbm, hbm_kind = measured("hbm_gbs", 6650.0)
+    tpk, tpk_kind = measured("bf16_tflops", 1590.0)
+    gbs = step_bytes / steps_s / 1e9
+    pf_tflops = prefill_flops(cfg4, B8_PROMPT) * B8_SEQ * args.steps / pre_dev / 1e12
+    c = clk.summary()
+    line = {
+        "metric": "aggregate decode tok/s at batch 8 (8 sequences per step) & % HBM roofline; prefill tok/s",
+        "value": round(args.steps * B8_GEN * B8_SEQ / gen_dev, 2), "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * (gen_dev + pre_dev) / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
+        "config": {"workload": WORKLOAD["cfg4"] + (f" ({args.layers} layers)" if args.layers else ""),
+                   "parallelism": "1 GPU",
+                   "l2": f"inputs larger than L2 ({weight_bytes(cfg4) / 1e9:.2f} GB of weights per step)",
+                   "kv_cache": "fp32"},
+        "decode_ms_per_step": round(1e3 * steps_s, 4),
+        "prefill_tok_s": round(args.steps * B8_SEQ * B8_PROMPT / pre_dev, 1),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                     "peak_kind": hbm_kind, "bytes_per_step": int(step_bytes), "traffic": None,
+                     "kernel": "batched decode step: CUDA graph of mvb_kernel GEMVs (8 sequence columns), reduce, "
+                               "residual and attention kernels; achieved = weights + 8 sequences' KV bytes per step / "
+                               "device time per step"},
+        "prefill_roofline": {"bound": "tensor", "achieved": round(pf_tflops, 1), "peak": tpk, "unit": "TFLOP/s",
+                             "frac": round(pf_tflops / tpk, 4), "peak_kind": tpk_kind},
+        "e2e": {"value": round(args.steps * B8_GEN * B8_SEQ / gen_wall, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": B8_SEQ * (B8_PROMPT * 4 + 8), "d2h_bytes_per_step": B8_SEQ * (B8_GEN * 4 + 4),
+                "prefill_tok_s": round(args.steps * B8_SEQ * B8_PROMPT / pre_wall, 1)},
+        "consistency": {"sequence0_batch8_equals_batch1_picks": consistent, "picks_checked": nchk},
+        "gpu_launches": int(launches),
+        "clocks": {k: c.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+    }
+    print(json.dumps(line), flush=True)
+    if not consistent:
+        raise SystemExit("32b-batch8: sequence 0's batch-8 picks differ from its batch-1 picks")
+
+
 def main():
     global GEN
     ap = argparse.ArgumentParser()
@@ -473,8 +564,20 @@ def main():
     ap.add_argument("--shape", default="7b", choices=["7b", "3b"],
                     help="the headline workload's model shape (3b: the secondary workload alone, e.g. for profiles)")
     ap.add_argument("--gen", type=int, default=GEN, help="greedy decode steps per workload step (profiles: fewer)")
+    ap.add_argument("--workload", default="default", choices=["default", "32b-batch8"],
+                    help="32b-batch8: the 8-sequence 32B-shaped workload (one GPU)")
+    ap.add_argument("--layers", type=int, default=0, help="32b-batch8: fewer layers (profiles on a small case)")
     args = ap.parse_args()
     GEN = args.gen
+    if args.workload == "32b-batch8":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "32b-batch8: the reference decodes one sequence "
+                              "per process; its 32B CPU run takes hours (time the default workload instead)"}))
+            return
+        global B8_GEN
+        B8_GEN = args.gen if args.gen != 256 else B8_GEN
+        run_batch8(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
