@@ -63,9 +63,11 @@ constexpr uint32_t kPartBytes = kBWarps * 2u * 128u * 4u;
 // 16-element sums [split_blocks * 16][8]
 __host__ __device__ constexpr uint32_t xq_bytes(uint32_t sb) { return sb * 64u * kMaxSeq * 16u; }
 __host__ __device__ constexpr uint32_t xs_bytes(uint32_t sb) { return a128(sb * 16u * kMaxSeq * 4u); }
+// 32-element sums for the Q4_K min term: [split_blocks][8 sequences][4] of (hi pair, lo pair)
+__host__ __device__ constexpr uint32_t xm_bytes(uint32_t sb) { return a128(sb * 32u * 8u); }
 __host__ __device__ constexpr uint32_t smem_total(uint32_t sb, uint32_t nslot, uint32_t slot)
 {
-    return hdr_bytes() + kPartBytes + xq_bytes(sb) + xs_bytes(sb) + kBWarps * nslot * slot;
+    return hdr_bytes() + kPartBytes + xq_bytes(sb) + xs_bytes(sb) + xm_bytes(sb) + kBWarps * nslot * slot;
 }
 
 // ------------------------------------------------------------- staging ----
@@ -86,7 +88,7 @@ __device__ __forceinline__ uint32_t xcol(uint32_t e4, uint32_t s, bool q4)
 // takes each sequence's max |x|; pass 2 scales by a power of two putting the
 // max in [2^13, 2^14), splits into binary16 hi + lo in place and writes the
 // 16-element sums. Sequences >= nseq are zeros.
-__device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t b0, uint32_t nbs, bool q4)
+__device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint2 *xm, uint32_t b0, uint32_t nbs, bool q4)
 {
     const uint32_t nq = nbs * 64u, total = nq * kMaxSeq;
     const uint32_t lane = threadIdx.x & 31u;
@@ -139,6 +141,21 @@ __device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t 
         if ((i & 3u) == 0u) xs[(e4 >> 2) * kMaxSeq + s] = sum;
     }
     bsync();
+    if (q4) {
+        // the 32-element sums of sub-blocks 2t, 2t + 1 of sequence g (entry g * 4 + t of
+        // each block) as binary16 hi / lo pairs, scaled by 2^-6 (|sum| < 2^19 -> < 2^13)
+        for (uint32_t i = threadIdx.x; i < nbs * 32u; i += kBThreads) {
+            const uint32_t b = i >> 5, g = (i >> 2) & 7u, t = i & 3u;
+            const float *x16 = xs + (b * 16u + 4u * t) * kMaxSeq + g;
+            const float v0 = (x16[0] + x16[kMaxSeq]) * 0.015625f;
+            const float v1 = (x16[2u * kMaxSeq] + x16[3u * kMaxSeq]) * 0.015625f;
+            const __half2 hi = __floats2half2_rn(v0, v1);
+            const float2 fh = __half22float2(hi);
+            const __half2 lo = __floats2half2_rn(v0 - fh.x, v1 - fh.y);
+            xm[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&hi), *reinterpret_cast<const uint32_t *>(&lo));
+        }
+        bsync();
+    }
 }
 
 // ----------------------------------------------------------- tile math ----
@@ -150,11 +167,42 @@ __device__ void stage_x(const BArgs &a, BHdr *h, uint4 *xq, float *xs, uint32_t 
 // and lo part for the other. Accumulator lane (g, t) ends with rows g, g + 8
 // x sequences 2t, 2t + 1.
 
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c)
+{
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b, const float (&c)[4])
+{
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
 // Q4_K (dequant_q4_k, src/brain_runtime.c:960-1015): chunk c of 64 elements is
 // 32 quant bytes; lane t reads bytes 8t .. 8t + 7 (word s: elements
-// 64c + 32 hn + 8t + 4s + 0..3, hn = low / high nibble). Low nibbles enter as
-// the binary16 subnormals q 2^-24, high nibbles in place as 16 q 2^-24.
-__device__ __forceinline__ void q4k_task8(const uint8_t *r0, const uint8_t *r1, const uint4 *xq, const float *xs,
+// 64c + 32 hn + 8t + 4s + 0..3, hn = low / high nibble). A holds sc_j q: the
+// quant byte under an exponent byte is the binary16 1024 + q (low nibble) or
+// 1024 + 16 q (high nibble in place), and one fused multiply-add per pair,
+// (1024 + q) sc - 1024 sc or (1024 + 16 q) sc / 16 - 64 sc, gives q sc exactly
+// (q sc <= 945). So the 16 k steps of the task sum into one accumulator
+// (hi and lo parts of x: two), scaled once by d; the min term
+// dmin sum_j m_j sum(x over sub-block j) is one m16n8k8 MMA pair of the m_j
+// (binary16 subnormals) against the staged 32-element sums.
+__device__ __forceinline__ void q4k_task8(const uint8_t *r0, const uint8_t *r1, const uint4 *xq, const uint2 *xm,
                                           uint32_t lane, float (&acc)[4])
 {
     const uint32_t g = lane >> 2, t = lane & 3u;
@@ -166,41 +214,51 @@ __device__ __forceinline__ void q4k_task8(const uint8_t *r0, const uint8_t *r1, 
     const uint32_t sl1 = h1.y & 0x3f3f3f3fu, ml1 = h1.z & 0x3f3f3f3fu;
     const uint32_t sh1 = (h1.w & 0x0f0f0f0fu) | ((h1.y >> 2) & 0x30303030u);
     const uint32_t mh1 = ((h1.w >> 4) & 0x0f0f0f0fu) | ((h1.z >> 2) & 0x30303030u);
-    const float d0 = h2f((uint16_t)(h0.x & 0xffffu)) * kTwo24, dm0 = h2f((uint16_t)(h0.x >> 16));
-    const float d1 = h2f((uint16_t)(h1.x & 0xffffu)) * kTwo24, dm1 = h2f((uint16_t)(h1.x >> 16));
+    float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (uint32_t c = 0; c < 4u; ++c) {
         const uint2 w0 = *reinterpret_cast<const uint2 *>(r0 + 16u + 32u * c + 8u * t);
         const uint2 w1 = *reinterpret_cast<const uint2 *>(r1 + 16u + 32u * c + 8u * t);
 #pragma unroll
         for (uint32_t hn = 0; hn < 2u; ++hn) {
-            float chi[4] = {0.f, 0.f, 0.f, 0.f}, clo[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t j = 2u * c + hn, jb = j & 3u;
+            const uint32_t sel = jb | 0x40u | (jb << 8) | 0x4000u;   // (byte jb, 0x64) twice
+            // (sc, sc) in binary16: (1024 + sc) - 1024
+            const uint32_t s0 = hsub2u(__byte_perm(j < 4u ? sl0 : sh0, 0x64u, sel), 0x64006400u);
+            const uint32_t s1 = hsub2u(__byte_perm(j < 4u ? sl1 : sh1, 0x64u, sel), 0x64006400u);
+            const uint32_t mul0 = hn ? hmul2u(s0, 0x2c002c00u) : s0, mul1 = hn ? hmul2u(s1, 0x2c002c00u) : s1;
+            const uint32_t add0 = hmul2u(s0, hn ? 0xd400d400u : 0xe400e400u);   // -64 sc or -1024 sc
+            const uint32_t add1 = hmul2u(s1, hn ? 0xd400d400u : 0xe400e400u);
 #pragma unroll
             for (uint32_t s = 0; s < 2u; ++s) {
                 const uint32_t m = hn ? 0xf0f0f0f0u : 0x0f0f0f0fu;
                 const uint32_t v0 = (s ? w0.y : w0.x) & m, v1 = (s ? w1.y : w1.x) & m;
                 const uint32_t e4 = 16u * c + 8u * hn + 2u * t + s;
                 const uint4 xv = xq[e4 * kMaxSeq + xcol(e4, g, true)];
-                const uint32_t a0 = sub2(v0, 0x4140), a1 = sub2(v1, 0x4140), a2 = sub2(v0, 0x4342), a3 = sub2(v1, 0x4342);
-                const float ch[4] = {chi[0], chi[1], chi[2], chi[3]}, cl[4] = {clo[0], clo[1], clo[2], clo[3]};
-                mma16816(chi, a0, a1, a2, a3, make_uint2(xv.x, xv.y), ch);
-                mma16816(clo, a0, a1, a2, a3, make_uint2(xv.z, xv.w), cl);
+                const uint32_t a0 = hfma2u(__byte_perm(v0, 0x64u, 0x4140), mul0, add0);
+                const uint32_t a1 = hfma2u(__byte_perm(v1, 0x64u, 0x4140), mul1, add1);
+                const uint32_t a2 = hfma2u(__byte_perm(v0, 0x64u, 0x4342), mul0, add0);
+                const uint32_t a3 = hfma2u(__byte_perm(v1, 0x64u, 0x4342), mul1, add1);
+                const float pa[4] = {ca[0], ca[1], ca[2], ca[3]}, pb[4] = {cb[0], cb[1], cb[2], cb[3]};
+                mma16816(ca, a0, a1, a2, a3, make_uint2(xv.x, xv.y), pa);
+                mma16816(cb, a0, a1, a2, a3, make_uint2(xv.z, xv.w), pb);
             }
-            const uint32_t j = 2u * c + hn, jb = 8u * (j & 3u);
-            const uint32_t s0w = j < 4u ? sl0 : sh0, m0w = j < 4u ? ml0 : mh0;
-            const uint32_t s1w = j < 4u ? sl1 : sh1, m1w = j < 4u ? ml1 : mh1;
-            const float f = hn ? 0.0625f : 1.0f;
-            const float S0 = d0 * f * u2f_small((s0w >> jb) & 0xffu), M0 = dm0 * u2f_small((m0w >> jb) & 0xffu);
-            const float S1 = d1 * f * u2f_small((s1w >> jb) & 0xffu), M1 = dm1 * u2f_small((m1w >> jb) & 0xffu);
-            const float2 xa = *reinterpret_cast<const float2 *>(xs + (2u * j) * kMaxSeq + 2u * t);
-            const float2 xb = *reinterpret_cast<const float2 *>(xs + (2u * j + 1u) * kMaxSeq + 2u * t);
-            const float sx0 = xa.x + xb.x, sx1 = xa.y + xb.y;
-            acc[0] = fmaf(-M0, sx0, fmaf(S0, chi[0] + clo[0], acc[0]));
-            acc[1] = fmaf(-M0, sx1, fmaf(S0, chi[1] + clo[1], acc[1]));
-            acc[2] = fmaf(-M1, sx0, fmaf(S1, chi[2] + clo[2], acc[2]));
-            acc[3] = fmaf(-M1, sx1, fmaf(S1, chi[3] + clo[3], acc[3]));
         }
     }
+    // min term: A = m_{2t}, m_{2t+1} of rows g, g + 8 as binary16 subnormals m 2^-24
+    const uint32_t msel = (t & 1u) ? 0x4342u : 0x4140u;
+    const uint32_t am0 = __byte_perm(t < 2u ? ml0 : mh0, 0u, msel), am1 = __byte_perm(t < 2u ? ml1 : mh1, 0u, msel);
+    const uint2 xb = xm[g * 4u + t];
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    float cm[4], cm2[4];
+    mma1688(cm, am0, am1, xb.x, zero);
+    mma1688(cm2, am0, am1, xb.y, cm);
+    const float d0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16)) * 1073741824.0f;
+    const float d1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16)) * 1073741824.0f;
+    acc[0] = fmaf(-dm0, cm2[0], fmaf(d0, ca[0] + cb[0], acc[0]));
+    acc[1] = fmaf(-dm0, cm2[1], fmaf(d0, ca[1] + cb[1], acc[1]));
+    acc[2] = fmaf(-dm1, cm2[2], fmaf(d1, ca[2] + cb[2], acc[2]));
+    acc[3] = fmaf(-dm1, cm2[3], fmaf(d1, ca[3] + cb[3], acc[3]));
 }
 
 // Q6_K (dequant_q6_k, src/brain_runtime.c:1049-1083), the block at a 2-byte
@@ -232,17 +290,17 @@ __device__ __forceinline__ void q6k_task8(const uint8_t *r0, const uint8_t *r1, 
                 const uint4 xv = xq[e4 * kMaxSeq + xcol(e4, g, false)];
                 const uint32_t a0 = sub2(v0, 0x4140), a1 = sub2(v1, 0x4140), a2 = sub2(v0, 0x4342), a3 = sub2(v1, 0x4342);
                 const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-                float chi[4], clo[4];
-                mma16816(chi, a0, a1, a2, a3, make_uint2(xv.x, xv.y), zero);
-                mma16816(clo, a0, a1, a2, a3, make_uint2(xv.z, xv.w), zero);
+                float cp[4], cs[4];   // x hi, then + x lo in the same accumulator
+                mma16816(cp, a0, a1, a2, a3, make_uint2(xv.x, xv.y), zero);
+                mma16816(cs, a0, a1, a2, a3, make_uint2(xv.z, xv.w), cp);
                 const uint32_t G = 8u * h + 2u * k + l16;
                 const float S0 = d0 * s8f(r0[192u + G]), S1 = d1 * s8f(r1[192u + G]);
                 const float2 x2 = *reinterpret_cast<const float2 *>(xs + G * kMaxSeq + 2u * t);
                 const float o0 = 32.0f * x2.x * (1.0f / kTwo24), o1 = 32.0f * x2.y * (1.0f / kTwo24);
-                acc[0] = fmaf(S0, (chi[0] + clo[0]) - o0, acc[0]);
-                acc[1] = fmaf(S0, (chi[1] + clo[1]) - o1, acc[1]);
-                acc[2] = fmaf(S1, (chi[2] + clo[2]) - o0, acc[2]);
-                acc[3] = fmaf(S1, (chi[3] + clo[3]) - o1, acc[3]);
+                acc[0] = fmaf(S0, cs[0] - o0, acc[0]);
+                acc[1] = fmaf(S0, cs[1] - o1, acc[1]);
+                acc[2] = fmaf(S1, cs[2] - o0, acc[2]);
+                acc[3] = fmaf(S1, cs[3] - o1, acc[3]);
             }
         }
     }
@@ -309,7 +367,8 @@ __device__ __forceinline__ void flush(const BArgs &a, const BCta &c, BHdr *h, fl
 }
 
 template <int NS, bool Q4>
-__device__ void consume(const BArgs &a, const BCta &c, BHdr *h, float *pslot, uint4 *xq, float *xs, uint8_t *ring)
+__device__ void consume(const BArgs &a, const BCta &c, BHdr *h, float *pslot, uint4 *xq, float *xs, uint2 *xm,
+                        uint8_t *ring)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, g = lane >> 2, q = lane & 3u;
     const BSeg &sg = a.seg[c.seg];
@@ -337,7 +396,7 @@ __device__ void consume(const BArgs &a, const BCta &c, BHdr *h, float *pslot, ui
         cpa_commit();
     }
     if (a.pdl) pdl_wait();
-    stage_x(a, h, xq, xs, b0, nbs, Q4);
+    stage_x(a, h, xq, xs, xm, b0, nbs, Q4);
     if (!active) return;
     auto warp_of = [&](uint32_t j) { return ((j + 1u) * weff + L - 1u) / L - 1u; };
     const uint32_t first = my0 / nbs, lastt = (my1 - 1u) / nbs;
@@ -360,7 +419,7 @@ __device__ void consume(const BArgs &a, const BCta &c, BHdr *h, float *pslot, ui
         const uint4 *xqb = xq + (size_t)cb * 64u * kMaxSeq;
         const float *xsb = xs + cb * 16u * kMaxSeq;
         if (Q4) {
-            q4k_task8(slot + g * kQ4Row, slot + (g + 8u) * kQ4Row, xqb, xsb, lane, acc);
+            q4k_task8(slot + g * kQ4Row, slot + (g + 8u) * kQ4Row, xqb, xm + cb * 32u, lane, acc);
         } else {
             // the block's offset inside its 16-byte-aligned window, per row
             const uintptr_t blk0 = reinterpret_cast<uintptr_t>(blk(ct, cb));
@@ -391,7 +450,8 @@ __global__ void __launch_bounds__(kBThreads, 1) mvb_kernel(const __grid_constant
     const uint32_t sb = a.split_blocks;
     uint4 *xq = reinterpret_cast<uint4 *>(smem + hdr_bytes() + kPartBytes);
     float *xs = reinterpret_cast<float *>(smem + hdr_bytes() + kPartBytes + xq_bytes(sb));
-    uint8_t *ring = smem + hdr_bytes() + kPartBytes + xq_bytes(sb) + xs_bytes(sb);
+    uint2 *xm = reinterpret_cast<uint2 *>(smem + hdr_bytes() + kPartBytes + xq_bytes(sb) + xs_bytes(sb));
+    uint8_t *ring = smem + hdr_bytes() + kPartBytes + xq_bytes(sb) + xs_bytes(sb) + xm_bytes(sb);
     const BCta c = a.cta[blockIdx.x];
     const BSeg &sg = a.seg[c.seg];
     const bool q4 = sg.type == 12u;
@@ -419,8 +479,8 @@ __global__ void __launch_bounds__(kBThreads, 1) mvb_kernel(const __grid_constant
     }
     __syncthreads();
     pdl_launch();
-    if (q4) consume<NS, true>(a, c, h, pslot, xq, xs, ring);
-    else consume<NS, false>(a, c, h, pslot, xq, xs, ring);
+    if (q4) consume<NS, true>(a, c, h, pslot, xq, xs, xm, ring);
+    else consume<NS, false>(a, c, h, pslot, xq, xs, xm, ring);
     cpa_wait<0>();   // no copy may still target this CTA's shared memory when it exits
 }
 
