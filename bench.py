@@ -175,7 +175,7 @@ def ref_threads():
     return n, min(16, n)
 
 
-def cpu_reference_sample(path, cfg, n_decode, n_prompt):
+def cpu_reference_sample(path, cfg, n_decode, n_prompt, pos=None):
     """The reference's own forward_token (oracle/_ref) on the host cores.
     Prompt rate: n_prompt tokens without logits, as the reference's own prompt
     loop runs them (src/brain_runtime.c:2025-2028). Decode rate: the cache is
@@ -189,17 +189,18 @@ def cpu_reference_sample(path, cfg, n_decode, n_prompt):
     ref = oracle_bind.Reference.load()
     if ref is None:
         return None
+    pos = PROMPT if pos is None else pos
     r = ref.open(path)
     prompt = prompt_ids(cfg)[:n_prompt]
     t0 = time.perf_counter()
     for i, t in enumerate(prompt):
         r.forward(int(t), i, False)
     t_prompt = time.perf_counter() - t0
-    r.fill_cache(n_prompt, PROMPT)
+    r.fill_cache(n_prompt, pos)
     nxt = int(prompt[-1])
     t0 = time.perf_counter()
     for s in range(n_decode):
-        lg = r.forward(nxt, PROMPT + s, True)
+        lg = r.forward(nxt, pos + s, True)
         nxt = r.greedy(lg)
     t_dec = time.perf_counter() - t0
     r.close()
@@ -521,6 +522,15 @@ def run_batch8(args):
     gbs = step_bytes / steps_s / 1e9
     pf_tflops = prefill_flops(cfg4, B8_PROMPT) * B8_SEQ * args.steps / pre_dev / 1e12
     c = clk.summary()
+    cpu = None
+    if not args.no_cpu_baseline:
+        smp = cpu_reference_sample(path, cfg4, n_decode=2, n_prompt=1, pos=B8_PROMPT)
+        if smp is not None:
+            cpu = {"value": round(smp["decode_tok_s"], 4), "unit": "tok/s", "cores": smp["gemv_threads"],
+                   "host_cores": smp["host_cores"], "kind": "reference",
+                   "sample": f"one sequence (the reference decodes one per process): 1 prompt token, then 2 greedy "
+                             f"decode tokens at positions {B8_PROMPT}-{B8_PROMPT + 1} over a {B8_PROMPT}-position "
+                             f"cache, 32B shape"}
     line = {
         "metric": "aggregate decode tok/s at batch 8 (8 sequences per step) & % HBM roofline; prefill tok/s",
         "value": round(args.steps * B8_GEN * B8_SEQ / gen_dev, 2), "unit": "tok/s", "n_gpus": 1,
@@ -545,6 +555,7 @@ def run_batch8(args):
                 "prefill_tok_s": round(args.steps * B8_SEQ * B8_PROMPT / pre_wall, 1)},
         "consistency": {"sequence0_batch8_equals_batch1_picks": consistent, "picks_checked": nchk},
         "gpu_launches": int(launches),
+        "cpu_baseline": cpu,
         "clocks": {k: c.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
     }
     print(json.dumps(line), flush=True)
