@@ -223,3 +223,15 @@ void ref_gpu_shutdown(void)
 
 /* The reference CLI (argv contract of atlas_dynamic_infer). */
 int ref_main(int argc, char **argv) { return run_main_utf8(argc, argv); }
+
+/* tokenize_prompt (src/brain_runtime.c:808-840) with the opened file's
+   tokenizer: the number of ids, or -1. */
+int ref_tokenize(const char *text, uint32_t *out, uint64_t cap)
+{
+    Tokenizer tok;
+    memset(&tok, 0, sizeof(tok));
+    if (!load_tokenizer(&g_ref_file, &tok) || !tokenizer_index(&tok)) { tokenizer_free(&tok); return -1; }
+    const size_t n = tokenize_prompt(&tok, text, out, (size_t)cap);
+    tokenizer_free(&tok);
+    return (int)n;
+}

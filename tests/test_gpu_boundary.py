@@ -103,3 +103,32 @@ def test_reference_cli_drop_in_matches_cpu(torch_cuda, small_model):
     check = _cli(CLI_GPU, small_model, "--gpu-check")
     assert check.returncode == 0 and check.stdout.count(b"GPU/CPU PASS") == 2, check.stdout
     assert _cli(CLI_GPU, small_model, prompt, "0").returncode == 2      # max_new_tokens out of range
+
+
+NATIVE = os.path.join(ROOT, "-1.7-atlas---apollo_b200", "atlas_dynamic_infer")
+
+
+def test_native_cli_matches_reference_cli(torch_cuda, small_model):
+    """The native atlas_dynamic_infer (host/cli.c over the library's batched
+    prefill and graph decode) prints what the reference's CPU build prints for
+    greedy prompts, with the same exit codes, self-test and confidence line."""
+    if not (os.path.exists(NATIVE) and os.path.exists(CLI_CPU)):
+        pytest.skip("atlas_dynamic_infer (make -C -1.7-atlas---apollo_b200) or the reference CLI is not built")
+    for prompt, n in (("Hello there, how are you?", "24"), ("Don't stop: 1234 + 5678 = ?", "40"),
+                      ("<|im_start|>user\nplain template<|im_end|>\n<|im_start|>assistant\n", "16")):
+        got = _cli(NATIVE, small_model, prompt, n)
+        want = _cli(CLI_CPU, small_model, prompt, n)
+        assert got.returncode == 0 and want.returncode == 0, (got.stderr[-2000:], want.stderr[-2000:])
+        assert got.stdout == want.stdout and len(got.stdout) > 1, (prompt, got.stdout, want.stdout)
+    conf = _cli(NATIVE, small_model, "Explain why", "8", "0", "--confidence")
+    assert conf.returncode == 0
+    line = conf.stdout.split(b"\n")[-2]
+    assert line.startswith(b"\x1eATLAS_CONFIDENCE=") and line.endswith(b"\x1e"), conf.stdout
+    check = _cli(NATIVE, small_model, "--gpu-check")
+    assert check.returncode == 0 and check.stdout.count(b"GPU/CPU PASS") == 2, check.stdout
+    assert _cli(NATIVE, small_model, "x", "0").returncode == 2       # max_new_tokens out of range
+    assert _cli(NATIVE, small_model, "x", "769").returncode == 2
+    assert _cli(NATIVE, small_model, "x", "4", "5").returncode == 2  # min_new > max_new
+    assert _cli(NATIVE, small_model).returncode == 2                 # usage
+    sampled = _cli(NATIVE, small_model, "Hello", "12", "3")          # top-k sampling, at least 3 tokens
+    assert sampled.returncode == 0 and len(sampled.stdout) > 1
