@@ -595,7 +595,7 @@ static int gpu_check(AtlasRuntime *rt, const uint8_t *file, uint64_t size)
     int passed = 1;
     for (int which = 0; which < 2; ++which) {
         AtlasTensorInfo t;
-        if (atlas_rt_find_tensor(rt, names[which], &t) || t.n_dims != 2 || !blk_bytes(t.type)) { passed = 0; break; }
+        if (!atlas_rt_find_tensor(rt, names[which], &t) || t.n_dims != 2 || !blk_bytes(t.type)) { passed = 0; break; }
         const uint64_t cols = t.dims[0], rows = t.dims[1], n = rows * cols, nb = n / blk_elems(t.type);
         float *x = malloc(cols * 4), *gpu = malloc(rows * 4), *w = malloc(n * 4);
         void *d_blk = NULL, *d_w = NULL;
@@ -720,7 +720,10 @@ int main(int argc, char **argv)
             pc = keep;
         }
         AtlasTensorInfo out_t;
-        if (atlas_rt_find_tensor(rt, "output.weight", &out_t)) goto out;
+        if (!atlas_rt_find_tensor(rt, "output.weight", &out_t)) {   /* 1: found */
+            fprintf(stderr, "output.weight missing\n");
+            goto out;
+        }
         const uint32_t vocab = (uint32_t)out_t.dims[1];
         /* greedy without a confidence line: the picks are made on the device */
         const int device_picks = min_n == 0 && !emit_confidence;

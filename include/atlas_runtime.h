@@ -62,6 +62,7 @@ void atlas_rt_close(AtlasRuntime *rt);
 const char *atlas_rt_error(const AtlasRuntime *rt);
 int atlas_rt_shape(const AtlasRuntime *rt, AtlasShape *out);
 uint64_t atlas_rt_data_base(const AtlasRuntime *rt);
+/* 1 when the tensor exists (out filled), 0 otherwise - find_tensor's convention, not ATLAS_OK's. */
 int atlas_rt_find_tensor(const AtlasRuntime *rt, const char *name, AtlasTensorInfo *out);
 /* Raw bytes of the mapped file (for callers that address tensors by absolute offset). */
 const uint8_t *atlas_rt_file_bytes(const AtlasRuntime *rt, uint64_t *size);
