@@ -250,10 +250,12 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
 // dred / fred: W slots each for the block reductions.
 template <int W>
 __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t *xarea, bool q4_order,
-                           uint64_t *t_wait = nullptr)
+                           uint64_t *t_wait = nullptr, uint32_t x_off = 0u)
 {
     const uint32_t n4 = a.cols / 4u;
     const bool norm = a.norm_w != nullptr;
+    const float4 *xin = reinterpret_cast<const float4 *>(a.x + x_off);
+    const float4 *nw = norm ? reinterpret_cast<const float4 *>(a.norm_w + x_off) : nullptr;
     float4 *xf = reinterpret_cast<float4 *>(xarea);
     float mx = 0.f;
     double ss = 0.0;
@@ -266,7 +268,7 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
 #pragma unroll
         for (int j = 0; j < kDepth; ++j) {
             const uint32_t i = threadIdx.x + (uint32_t)j * kStride;
-            if (i < n4) w[j] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
+            if (i < n4) w[j] = __ldg(nw + i);
         }
     }
     if (a.pdl) pdl_wait();
@@ -274,8 +276,14 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
     // tensor parallel: the partial rows of the preceding row-split projection
     // from every rank, then x = a.x + slot 0 + slot 1 + ... in rank order
     const float4 *red = nullptr;
-    uint32_t own0 = 0, own1 = 0;
-    if (a.in_red) {
+    uint32_t nred = 0, own0 = 0, own1 = 0;
+    if (a.in_part) {
+        // K parts of the preceding launch on this GPU (complete after the wait)
+        red = reinterpret_cast<const float4 *>(a.in_part);
+        nred = a.in_nparts;
+        own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
+        own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
+    } else if (a.in_red) {
         if (threadIdx.x == 0) {
             const uint32_t epoch = *reinterpret_cast<volatile const uint32_t *>(&a.dstate->epoch);
             const uint32_t k = epoch * a.seq_mul + a.seq_add;
@@ -285,6 +293,7 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
         }
         asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
         red = reinterpret_cast<const float4 *>(a.peer[a.rank] + a.in_red);
+        nred = a.tp;
         own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
         own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
     }
@@ -294,12 +303,12 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
         for (int j = 0; j < kDepth; ++j) {
             const uint32_t i = i0 + (uint32_t)j * kStride;
             if (i < n4) {
-                v[j] = __ldcg(reinterpret_cast<const float4 *>(a.x) + i);
-                if (norm && i0 != threadIdx.x) w[j] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
+                v[j] = __ldcg(xin + i);
+                if (norm && i0 != threadIdx.x) w[j] = __ldg(nw + i);
             }
         }
         if (red) {
-            for (uint32_t r = 0; r < a.tp; ++r) {
+            for (uint32_t r = 0; r < nred; ++r) {
 #pragma unroll
                 for (int j = 0; j < kDepth; ++j) {
                     const uint32_t i = i0 + (uint32_t)j * kStride;
@@ -595,7 +604,7 @@ __device__ bool mv_consumer(const MvArgs &a, MvHdr *h, uint8_t *xarea, const uin
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const int g = (int)(lane >> 2), t4 = (int)(lane & 3u);
     // waits for the preceding kernel; a CTA's tasks are all of its segment's type
-    const float out_scale = mv_stage_x<kMvWarps>(a, h->dred, h->fred, xarea, a.seg[c.seg].type == 12u);
+    const float out_scale = mv_stage_x<kMvWarps>(a, h->dred, h->fred, xarea, a.seg[c.seg].type == 12u, nullptr, a.seg[c.seg].x_off);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
     const uint32_t per = a.st > (uint32_t)kMvWarps ? a.st / kMvWarps : 1u;    // tasks per slot visit
     const uint32_t step = a.st > (uint32_t)kMvWarps ? 1u : kMvWarps / a.st, u = warp % a.st;
@@ -712,11 +721,10 @@ __global__ void __maxnreg__(128) mv_kernel(const __grid_constant__ MvArgs a)
     mv_consumer(a, h, xarea, ring, c, err, best);
     if (a.epi == MV_PART) {
         // every pushing thread orders its own remote stores, then one arrival
-        // per CTA at every rank
+        // per CTA at every rank (lane p of warp 0 at rank p)
         __threadfence_system();
         mv_sync();
-        if (threadIdx.x == 0)
-            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        if (threadIdx.x < a.tp) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + a.out_cnt), 1u);
         return;
     }
     if (a.epi != MV_LOGITS) return;
@@ -730,23 +738,22 @@ __global__ void __maxnreg__(128) mv_kernel(const __grid_constant__ MvArgs a)
     }
     if (lane == 0) { h->amax[warp] = best.v; h->aidx[warp] = best.i; }
     mv_sync();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < kMvWarps; ++w)
-            if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
-        if (a.tp > 1u) {
-            // (max, global row) into this rank's slot at every rank
-            for (uint32_t p = 0; p < a.tp; ++p) {
-                reinterpret_cast<float *>(a.peer[p] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
-                reinterpret_cast<uint32_t *>(a.peer[p] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
-                                                                                            blockIdx.x] =
-                    a.row_base + best.i;
-            }
-            __threadfence_system();
-            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
-        } else {
-            a.pmax[blockIdx.x] = best.v;
-            a.pidx[blockIdx.x] = best.i;
+    if (warp != 0u) return;
+    for (int w = 1; w < kMvWarps; ++w)
+        if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
+    if (a.tp > 1u) {
+        // (max, global row) into this rank's slot at every rank: lane p
+        // stores at rank p and releases there
+        if (lane < a.tp) {
+            reinterpret_cast<float *>(a.peer[lane] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
+            reinterpret_cast<uint32_t *>(a.peer[lane] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
+                                                                                           blockIdx.x] =
+                a.row_base + best.i;
+            red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[lane] + a.out_cnt), 1u);
         }
+    } else if (lane == 0) {
+        a.pmax[blockIdx.x] = best.v;
+        a.pidx[blockIdx.x] = best.i;
     }
 }
 
@@ -876,11 +883,14 @@ __device__ __forceinline__ float m4_rows(float v0, float v1, uint32_t lane)
 
 // Finish tile t after this warp's last task in it: alone (wa == wb), or as
 // one of the warps wa..wb sharing it (partials in shared memory; the last to
-// arrive adds them in warp order).
-__device__ __forceinline__ void m4_flush_body(const MvArgs &a, M4Hdr *h, float *part, uint32_t seg, uint32_t t,
+// arrive adds them in warp order). A tile that other CTAs hold tasks of too
+// (the CTA's range starts or ends inside it) is then finished by the last of
+// those CTAs to arrive, which adds their partial rows in CTA order.
+__device__ __forceinline__ void m4_flush_body(const MvArgs &a, M4Hdr *h, float *part, const MvCta &c, uint32_t t,
                                               uint32_t tj0, uint32_t wa, uint32_t wb, uint32_t my0, float a00,
                                               float a01, float a10, float a11, float out_scale, MvBest &best)
 {
+    const uint32_t seg = c.seg;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     float r0 = m4_rows(a00, a01, lane);
     float r1 = a.paired ? m4_rows(a10, a11, lane) : 0.f;
@@ -910,17 +920,48 @@ __device__ __forceinline__ void m4_flush_body(const MvArgs &a, M4Hdr *h, float *
             r1 += q[16u + i];
         }
     }
+    r0 *= out_scale;
+    r1 *= out_scale;
+    const uint32_t TPn = a.nb * (a.paired ? 2u : 1u);
+    if (tj0 < c.j0 || tj0 + TPn > c.j1) {
+        // t is this CTA's first tile when its range starts inside t (then
+        // slot 0; also when the range lies inside t), else its last (slot 1)
+        const bool first = tj0 <= c.j0, last = tj0 + TPn >= c.j1;
+        const uint32_t ca = first ? c.ca : blockIdx.x, cb = last ? c.cb : blockIdx.x;
+        float *gp = a.xpart + ((size_t)blockIdx.x * 2u + (first ? 0u : 1u)) * 32u;
+        if (lane < 16u) {
+            __stcg(gp + lane, r0);
+            __stcg(gp + 16u + lane, r1);
+            __threadfence();
+        }
+        __syncwarp();
+        uint32_t fin = 0;
+        if (lane == 0) fin = atomicAdd(a.xcnt + ca, 1u) + 1u == cb - ca + 1u ? 1u : 0u;
+        fin = __shfl_sync(0xffffffffu, fin, 0);
+        if (!fin) return;
+        __threadfence();
+        r0 = r1 = 0.f;
+        const uint32_t i = lane & 15u;
+        for (uint32_t k = ca; k <= cb; ++k) {
+            // t is CTA k's first tile exactly when k's range starts inside it
+            const float *q = a.xpart + ((size_t)k * 2u + (a.cta[k].j0 >= tj0 ? 0u : 1u)) * 32u;
+            r0 += __ldcg(q + i);
+            r1 += __ldcg(q + 16u + i);
+        }
+        // back to zero for the next launch, whose CTAs arrive only after this grid is complete
+        if (lane == 0) a.xcnt[ca] = 0u;
+    }
     const float pre = mv_pre(a, seg, t, lane);
-    if (lane < 16u) mv_finish(a, seg, t, r0 * out_scale, r1 * out_scale, pre, lane, best);
+    if (lane < 16u) mv_finish(a, seg, t, r0, r1, pre, lane, best);
 }
 
 // Out of line for the Q4_K / Q6_K kernels (code size); the other types'
 // kernels inline the body.
-__device__ __noinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, uint32_t seg, uint32_t t, uint32_t tj0,
+__device__ __noinline__ void m4_flush(const MvArgs &a, M4Hdr *h, float *part, const MvCta &c, uint32_t t, uint32_t tj0,
                                       uint32_t wa, uint32_t wb, uint32_t my0, float a00, float a01, float a10,
                                       float a11, float out_scale, MvBest &best)
 {
-    m4_flush_body(a, h, part, seg, t, tj0, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
+    m4_flush_body(a, h, part, c, t, tj0, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
 }
 
 // 16 bytes at a 2-byte-aligned shared-memory address, as four words: five
@@ -1180,12 +1221,15 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         }
         m4_commit();
     }
-    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4, t_wait);
+    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4, t_wait, a.seg[c.seg].x_off);
     t_ready = global_ns();
     if (!active) return;
     // sharing of the first and last tiles with neighbouring warps
-    const uint32_t fa = m4_warp_of(c.j0, L, weff, first_tile * TP), fb = m4_warp_of(c.j0, L, weff, first_tile * TP + TP - 1u);
-    const uint32_t la = m4_warp_of(c.j0, L, weff, last_tile * TP), lb = m4_warp_of(c.j0, L, weff, last_tile * TP + TP - 1u);
+    // (the CTA's range may start and end inside a tile: clamp to it)
+    const uint32_t fa = m4_warp_of(c.j0, L, weff, max(first_tile * TP, c.j0)),
+                   fb = m4_warp_of(c.j0, L, weff, min(first_tile * TP + TP, c.j1) - 1u);
+    const uint32_t la = m4_warp_of(c.j0, L, weff, max(last_tile * TP, c.j0)),
+                   lb = m4_warp_of(c.j0, L, weff, min(last_tile * TP + TP, c.j1) - 1u);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
     const uint8_t *ringp = ring + (size_t)warp * NS * a.slot_bytes;
     const uint32_t wlow = (uint32_t)reinterpret_cast<uintptr_t>(sg.w0), wlow1 = (uint32_t)reinterpret_cast<uintptr_t>(sg.w1);
@@ -1229,8 +1273,8 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         if (cc.t != t || k + 1u == n) {
             const uint32_t wa = t == first_tile ? fa : (t == last_tile ? la : warp);
             const uint32_t wb = t == first_tile ? fb : (t == last_tile ? lb : warp);
-            if constexpr (Q4 || Q6) m4_flush(a, h, part, c.seg, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
-            else m4_flush_body(a, h, part, c.seg, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
+            if constexpr (Q4 || Q6) m4_flush(a, h, part, c, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
+            else m4_flush_body(a, h, part, c, t, t * TP, wa, wb, my0, a00, a01, a10, a11, out_scale, best);
             a00 = a01 = a10 = a11 = 0.f;
         }
     }
@@ -1289,11 +1333,11 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     cp_async_wait<0>();   // no copy may still target this CTA's shared memory when it exits
     if (a.epi == MV_PART) {
         // The barrier orders every thread's partial-row stores to the peers
-        // before thread 0's system-scope release, which is cumulative: a rank
-        // that acquires the counter sees all of them.
+        // before the system-scope releases, which are cumulative: a rank that
+        // acquires the counter sees all of them. Lane p of warp 0 signals rank
+        // p, so the ranks' releases are one warp instruction, not tp in turn.
         m4_sync<W>();
-        if (threadIdx.x == 0)
-            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
+        if (threadIdx.x < a.tp) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + a.out_cnt), 1u);
         trace_done(tr, a.trace_slot, t_start, t_ready, t_wait[0], t_wait[1]);
         return;
     }
@@ -1308,22 +1352,24 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
     }
     if (lane == 0) { h->amax[warp] = best.v; h->aidx[warp] = best.i; }
     m4_sync<W>();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < W; ++w)
-            if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
-        if (a.tp > 1u) {
-            for (uint32_t p = 0; p < a.tp; ++p) {
-                reinterpret_cast<float *>(a.peer[p] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
-                reinterpret_cast<uint32_t *>(a.peer[p] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
-                                                                                            blockIdx.x] =
-                    a.row_base + best.i;
-            }
-            __threadfence_system();
-            for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + a.out_cnt), 1u);
-        } else {
-            a.pmax[blockIdx.x] = best.v;
-            a.pidx[blockIdx.x] = best.i;
+    if (warp != 0u) return;
+    // every lane of warp 0 reduces the warps' pairs (the same order, so the
+    // same result in every lane)
+    for (int w = 1; w < W; ++w)
+        if (h->amax[w] > best.v || (h->amax[w] == best.v && h->aidx[w] < best.i)) { best.v = h->amax[w]; best.i = h->aidx[w]; }
+    if (a.tp > 1u) {
+        // lane p stores (max, global row) into this rank's slot at rank p,
+        // then releases it there (its own stores, in program order)
+        if (lane < a.tp) {
+            reinterpret_cast<float *>(a.peer[lane] + a.out_red)[a.rank * kTpPStride + blockIdx.x] = best.v;
+            reinterpret_cast<uint32_t *>(a.peer[lane] + a.out_red + a.tp * kTpPStride * 4u)[a.rank * kTpPStride +
+                                                                                           blockIdx.x] =
+                a.row_base + best.i;
+            red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[lane] + a.out_cnt), 1u);
         }
+    } else if (lane == 0) {
+        a.pmax[blockIdx.x] = best.v;
+        a.pidx[blockIdx.x] = best.i;
     }
 }
 
@@ -2076,9 +2122,9 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *pmax, const ui
 __global__ void __launch_bounds__(256) tp_allreduce_kernel(const __grid_constant__ TpReduceArgs a)
 {
     uint8_t *own = a.peer[a.rank];
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (blockIdx.x == 0 && threadIdx.x < a.tp) {
         __threadfence_system();
-        for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + kTpCntReady), 1u);
+        red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + kTpCntReady), 1u);
     }
     if (threadIdx.x == 0)
         wait_counter_sys(reinterpret_cast<const uint32_t *>(own + kTpCntReady), a.seq * a.tp, a.status);
@@ -2096,10 +2142,9 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(const __grid_constant
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (uint32_t p = 0; p < a.tp; ++p) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[p] + kTpCntDone), 1u);
+    if (threadIdx.x < a.tp) red_release_sys_add(reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + kTpCntDone), 1u);
+    if (threadIdx.x == 0)
         wait_counter_sys(reinterpret_cast<const uint32_t *>(own + kTpCntDone), a.seq * a.tp * gridDim.x, a.status);
-    }
     __syncthreads();
 }
 

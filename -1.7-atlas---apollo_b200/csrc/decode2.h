@@ -108,6 +108,9 @@ constexpr uint32_t kMvMaxSt = 16;                 // tasks per ring slot, at mos
 // MV_PART: partial rows of a row-split projection, pushed to every rank
 enum MvEpi : uint32_t { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_LOGITS = 3, MV_PART = 4 };
 
+// K parts of one launch (segments of one matrix, each over a slice of the columns)
+constexpr uint32_t kMvMaxKParts = 3u;
+
 struct MvSeg {
     const uint8_t *w;      // row 0 of the raw GGUF tensor
     uint64_t row_bytes;
@@ -116,13 +119,18 @@ struct MvSeg {
     const float *bias;     // optional (MV_STORE)
     float *out;
     uint32_t copies;       // bulk copies per whole-row run of 16 rows: 1, 2, 4 or 8
-    uint32_t pad_;
+    uint32_t x_off;        // mv4_kernel: the segment's input starts at x + x_off (a K part of a longer row)
 };
 
 struct MvCta {
     uint32_t seg;          // segment (0 when paired)
-    uint32_t j0, j1;       // task range (whole tiles)
+    uint32_t j0, j1;       // task range (mv_kernel: whole tiles; mv4_kernel: any tasks of the segment)
     uint32_t pad_;
+    // mv4_kernel, a range that starts or ends inside a row tile: the first
+    // CTA whose range holds part of this CTA's first tile, and the last CTA
+    // whose range holds part of its last tile
+    uint32_t ca, cb;
+    uint32_t pad2_[2];
 };
 
 struct MvArgs {
@@ -151,6 +159,15 @@ struct MvArgs {
     // written back to xout (each CTA its share). in_red == 0: no exchange.
     uint32_t in_red, in_cnt, in_arrivals, seq_mul, seq_add;
     float *xout;
+    // one GPU: x = a.x + the in_nparts K-part partial rows at in_part (rows
+    // [r * cols, (r + 1) * cols) for part r, added in part order), written back
+    // to xout (each CTA its share); the preceding launch (PDL) wrote them
+    const float *in_part;
+    uint32_t in_nparts;
+    // mv4_kernel, row tiles shared by CTAs: partial rows [cta][first / last
+    // tile][32] and arrival counters [first CTA of the tile], zero between launches
+    float *xpart;
+    uint32_t *xcnt;
     uint32_t x_lo, x_hi;     // x_hi > 0: staged elements outside [x_lo, x_hi) are zero
     // MV_PART / MV_LOGITS pushes: receive offset and counter at every rank
     uint32_t out_red, out_cnt;

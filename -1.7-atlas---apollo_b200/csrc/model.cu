@@ -159,6 +159,13 @@ struct AtlasCuda {
     uint8_t *peer[d2::kTpMax] = {};
     bool peer_mapped[d2::kTpMax] = {};
     float *x2 = nullptr;
+    // one GPU: the down projection in K parts (partial rows [part][hidden]),
+    // added to the residual by the next launch's input staging
+    float *kpart = nullptr;
+    uint32_t kparts = 1;
+    // mv4_kernel: partial rows and counters of row tiles cut between CTAs
+    float *xpart = nullptr;
+    uint32_t *xcnt = nullptr;
     uint32_t *d_in_ids = nullptr;
     uint32_t in_cap = 0;
     // Several sequences (batch.cu): each has a KV-cache region of kv_seq_bytes
@@ -677,7 +684,7 @@ uint32_t mv_copies(uint64_t row_bytes)
 // The ring slot holds `st` tasks; `st` and the ring depth are the largest
 // that keep the launch within half an SM's shared memory with at least 3
 // slots.
-int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initializer_list<d2::MvSeg> segs, uint32_t epi)
+int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, const std::vector<d2::MvSeg> &segs, uint32_t epi)
 {
     d2::MvArgs &a = p.a;
     a = d2::MvArgs{};
@@ -850,6 +857,55 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
             }
         }
     }
+    // mv4_kernel: every CTA of a segment takes an equal share of its tasks,
+    // not whole row tiles (224 tiles of 74 blocks on 148 SMs give some CTAs
+    // twice the tiles of others), when that lowers the most tasks any warp
+    // runs: a tile cut between CTAs is finished by the last of them to arrive
+    // (a fence, an atomic and a read-back of the partial rows at the end of
+    // the launch), which costs more than it saves when the busiest warps keep
+    // their task count. ATLAS_MV_TILE_RANGES=1 / 0 forces whole tiles / shares.
+    const char *tr = getenv("ATLAS_MV_TILE_RANGES");
+    bool shares = false;
+    if (a.engine == 1u) {
+        uint32_t worst_tiles = 0, worst_shares = 0;
+        for (size_t s = 0; s < cta_n.size(); ++s) {
+            const uint32_t per_tile = (tiles[s] + cta_n[s] - 1u) / cta_n[s] * TP;
+            const uint32_t per_share = (uint32_t)(((uint64_t)tiles[s] * TP + cta_n[s] - 1u) / cta_n[s]);
+            worst_tiles = std::max(worst_tiles, (per_tile + a.warps - 1u) / a.warps);
+            worst_shares = std::max(worst_shares, (per_share + a.warps - 1u) / a.warps);
+        }
+        shares = tr ? atoi(tr) == 0 : worst_shares < worst_tiles;
+    }
+    if (shares) {
+        ctas.clear();
+        for (size_t s = 0; s < cta_n.size(); ++s) {
+            const uint64_t n = (uint64_t)tiles[s] * TP;
+            for (uint32_t c = 0; c < cta_n[s]; ++c) {
+                d2::MvCta e{};
+                e.seg = (uint32_t)s;
+                e.j0 = (uint32_t)(n * c / cta_n[s]);
+                e.j1 = (uint32_t)(n * (c + 1) / cta_n[s]);
+                ctas.push_back(e);
+            }
+        }
+        if (!h->xpart) {
+            int rc = dalloc(h, &h->xpart, (size_t)G * 2u * 32u * sizeof(float));
+            if (!rc) rc = dalloc(h, &h->xcnt, (size_t)G * sizeof(uint32_t));
+            if (rc) return rc;
+            CU(h, cudaMemset(h->xcnt, 0, (size_t)G * sizeof(uint32_t)));
+        }
+        a.xpart = h->xpart;
+        a.xcnt = h->xcnt;
+    }
+    // neighbours holding parts of each CTA's first and last tiles
+    for (size_t k = 0; k < ctas.size(); ++k) {
+        const uint32_t f0 = ctas[k].j0 / TP * TP, l1 = ((ctas[k].j1 - 1u) / TP + 1u) * TP;
+        size_t ca = k, cb = k;
+        while (ca > 0 && ctas[ca - 1].seg == ctas[k].seg && ctas[ca - 1].j1 > f0) --ca;
+        while (cb + 1 < ctas.size() && ctas[cb + 1].seg == ctas[k].seg && ctas[cb + 1].j0 < l1) ++cb;
+        ctas[k].ca = (uint32_t)ca;
+        ctas[k].cb = (uint32_t)cb;
+    }
     d2::MvCta *dc = nullptr;
     int rc = dalloc(h, &dc, ctas.size() * sizeof(d2::MvCta));
     if (rc) return rc;
@@ -868,7 +924,7 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, std::initialize
 // the layer's own types (a Q4_K_M file mixes Q4_K and Q6_K across layers)
 // with the launch's other fields kept. Plans of a type combination are made
 // once (cache).
-int layer_plan(AtlasCuda *h, const MvPlan &p0, bool paired, std::initializer_list<d2::MvSeg> segs, MvPlan &out,
+int layer_plan(AtlasCuda *h, const MvPlan &p0, bool paired, const std::vector<d2::MvSeg> &segs, MvPlan &out,
                std::vector<std::pair<std::vector<uint32_t>, MvPlan>> &cache)
 {
     out = p0;
@@ -907,6 +963,8 @@ int layer_plan(AtlasCuda *h, const MvPlan &p0, bool paired, std::initializer_lis
     out.a.tslots = fresh->a.tslots;
     out.a.smem_bytes = fresh->a.smem_bytes;
     out.a.cta = fresh->a.cta;
+    out.a.xpart = fresh->a.xpart;
+    out.a.xcnt = fresh->a.xcnt;
     out.a.engine = fresh->a.engine;
     out.a.warps = fresh->a.warps;
     out.a.gen_type = fresh->a.gen_type;
@@ -943,9 +1001,7 @@ int split_qkv(AtlasCuda *h, const d2::MvSeg (&sg)[3], std::vector<MvPlan> &out,
         if (!fresh) {
             MvPlan p;
             int rc = ATLAS_OK;
-            if (grp.size() == 1) rc = plan_mv(h, p, h->desc.hidden, false, {grp[0]}, d2::MV_STORE);
-            else if (grp.size() == 2) rc = plan_mv(h, p, h->desc.hidden, false, {grp[0], grp[1]}, d2::MV_STORE);
-            else rc = plan_mv(h, p, h->desc.hidden, false, {grp[0], grp[1], grp[2]}, d2::MV_STORE);
+            rc = plan_mv(h, p, h->desc.hidden, false, grp, d2::MV_STORE);
             if (rc) return rc;
             cache.emplace_back(key, p);
             fresh = &cache.back().second;
@@ -961,6 +1017,45 @@ int split_qkv(AtlasCuda *h, const d2::MvSeg (&sg)[3], std::vector<MvPlan> &out,
         out.push_back(p);
     }
     return ATLAS_OK;
+}
+
+// K parts of the one-GPU down projection: one when the whole row's staged
+// input leaves shared memory for a 3-slot ring of Q6_K tasks in every one of
+// 16 warps, else the most parts (up to kMvMaxKParts, dividing the row's
+// blocks) that do. With FFN 18944 (7B) the whole row leaves room for 2 slots;
+// shorter parts also shorten every CTA's input staging (14B: 4.91 ms/token
+// with 2 parts, 4.83 with 3). ATLAS_DOWN_KPARTS=n sets the count.
+uint32_t down_kparts(const AtlasCuda *h)
+{
+    if (h->tp > 1 || h->other_types) return 1u;
+    const uint32_t nb = h->sl.ffn_rows / 256u, slot = 16u * d2::kM4Q6Row;
+    if (const char *e = getenv("ATLAS_DOWN_KPARTS")) {
+        const uint32_t n = (uint32_t)std::max(1, atoi(e));
+        return n <= d2::kMvMaxKParts && nb % n == 0 ? n : 1u;
+    }
+    if (atlas_d2_mv4_smem(nb * 256u, 16u, 3u, slot) <= 227u * 1024u) return 1u;
+    for (uint32_t n = d2::kMvMaxKParts; n >= 2u; --n)
+        if (nb % n == 0 && atlas_d2_mv4_smem(nb / n * 256u, 16u, 3u, slot) <= 227u * 1024u) return n;
+    return 1u;
+}
+
+// The down projection's segments: one per K part, each over its slice of the
+// columns (weights from the part's first block, input from x + x_off) and
+// storing its partial rows into h->kpart; one part: the residual add.
+std::vector<d2::MvSeg> down_segs(AtlasCuda *h, const uint8_t *w, uint32_t type, uint32_t parts)
+{
+    const AtlasModelDesc &d = h->desc;
+    const uint32_t cols = h->sl.ffn_rows;
+    if (parts <= 1u) return {mvseg(w, type, d.hidden, cols, nullptr, h->x)};
+    std::vector<d2::MvSeg> v;
+    const uint32_t pc = cols / parts;
+    for (uint32_t p = 0; p < parts; ++p) {
+        d2::MvSeg s = mvseg(w + (uint64_t)p * (pc / 256u) * block_bytes(type), type, d.hidden, cols, nullptr,
+                            h->kpart + (size_t)p * d.hidden);
+        s.x_off = p * pc;
+        v.push_back(s);
+    }
+    return v;
 }
 
 // Capture one decode step as a CUDA graph of PDL-chained kernels. With
@@ -1014,8 +1109,15 @@ int build_graph2(AtlasCuda *h)
                        mvseg(w0.up, w0.tu, sl.ffn_rows, d.hidden, nullptr, nullptr)},
                       d2::MV_SWIGLU)))
         return rc;
-    if ((rc = plan_mv(h, dn, sl.ffn_rows, false, {mvseg(w0.down, w0.td, d.hidden, sl.ffn_rows, nullptr, h->x)}, part)))
+    // one GPU, long FFN rows: down in K parts whose partial rows the next
+    // launch adds, with the residual alternating between x (even layers) and
+    // x2 (odd layers) - qkv of layer l + 1 stages R(l) + parts into R(l + 1)
+    h->kparts = down_kparts(h);
+    const uint32_t KP = h->kparts;
+    if ((rc = plan_mv(h, dn, sl.ffn_rows / KP, false, down_segs(h, w0.down, w0.td, KP), KP > 1 ? (uint32_t)d2::MV_STORE : part)))
         return rc;
+    if (KP > 1 && dn.a.engine != 1u) return fail(h, ATLAS_EINVAL, "graph decode: K parts need the mv4 kernel");
+    auto resid = [&](uint32_t l) { return KP > 1 && (l & 1u) ? h->x2 : h->x; };
     if ((rc = plan_mv(h, hd, d.hidden, false, {mvseg(h->head, h->t_head, sl.vocab_rows, d.hidden, nullptr, h->logits)},
                       d2::MV_LOGITS)))
         return rc;
@@ -1025,6 +1127,11 @@ int build_graph2(AtlasCuda *h)
     dn.a.x = h->ffn;
     hd.a.x = h->x;
     hd.a.norm_w = h->out_norm;
+    if (KP > 1) {
+        hd.a.x = resid(d.layers - 1u);
+        hd.a.in_part = h->kpart;
+        hd.a.in_nparts = KP;
+    }
     uint32_t arr_o = 0, arr_dn = 0, arr_hd = 0;
     if (tp > 1) {
         // arrivals per occurrence: one per CTA of every rank; o and down have
@@ -1096,9 +1203,12 @@ int build_graph2(AtlasCuda *h)
                                  {mvseg(w.gate, w.tg, sl.ffn_rows, d.hidden, nullptr, h->ffn),
                                   mvseg(w.up, w.tu, sl.ffn_rows, d.hidden, nullptr, nullptr)},
                                  lp[l][2], cache)) ||
-                (rc = layer_plan(h, dn, false, {mvseg(w.down, w.td, d.hidden, sl.ffn_rows, nullptr, h->x)}, lp[l][3],
-                                 cache)))
+                (rc = layer_plan(h, dn, false, down_segs(h, w.down, w.td, KP), lp[l][3], cache)))
                 return rc;
+            if (KP > 1) {
+                if (lp[l][3].a.engine != 1u) return fail(h, ATLAS_EINVAL, "graph decode: K parts need the mv4 kernel");
+                lp[l][1].a.seg[0].out = resid(l);   // o adds into the layer's residual buffer
+            }
             for (const MvPlan &p : lp[l]) mv_smem = std::max<size_t>(mv_smem, p.a.smem_bytes);
         }
     }
@@ -1142,6 +1252,12 @@ int build_graph2(AtlasCuda *h)
                 a.in_arrivals = arr_dn;
                 a.seq_add = l;
                 a.xout = h->x;
+            } else if (KP > 1 && l > 0) {
+                // x = R(l - 1) + the down parts of layer l - 1, kept as R(l)
+                a.x = resid(l - 1u);
+                a.in_part = h->kpart;
+                a.in_nparts = KP;
+                a.xout = resid(l);
             }
             a.trace_slot = kernels++;
             if ((e = atlas_d2_launch_mv(&a, p.grid, h->stream)) != cudaSuccess) break;
@@ -1159,6 +1275,7 @@ int build_graph2(AtlasCuda *h)
         a = lp[l][2].a;
         a.norm_w = w.ffn_norm;
         a.seq_add = l + 1u;
+        if (KP > 1) a.x = resid(l);
         a.trace_slot = kernels++;
         if ((e = atlas_d2_launch_mv(&a, lp[l][2].grid, h->stream)) != cudaSuccess) break;
         a = lp[l][3].a;
@@ -1818,7 +1935,7 @@ int build_graphb(AtlasCuda *h, uint32_t nseq)
     b.exec = nullptr;
     b.graph = nullptr;
     b.on = false;
-    const uint32_t G = (uint32_t)h->sm_count, B = h->max_batch, group = d.q_heads / d.kv_heads;
+    const uint32_t B = h->max_batch, group = d.q_heads / d.kv_heads;
     const uint32_t qkvw = d.q_dim + 2u * d.kv_dim;
     const uint32_t C = d2::kAttnCluster;
     const uint32_t splits = std::max(C, (h->g2.splits / nseq) / C * C);
@@ -2174,8 +2291,9 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     if (cudaMemset(h->att, 0, d.q_dim * 4) != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "memset failed"));
     TRY(dalloc(h, &h->ffn, (size_t)sl.ffn_rows * 4));
     TRY(dalloc(h, &h->logits, (size_t)sl.vocab_rows * 4));
+    TRY(dalloc(h, &h->x2, d.hidden * 4));
+    TRY(dalloc(h, &h->kpart, (size_t)d2::kMvMaxKParts * d.hidden * 4));
     if (tp > 1) {
-        TRY(dalloc(h, &h->x2, d.hidden * 4));
         const d2::TpLayout xl = d2::tp_layout((uint32_t)tp, d.hidden, h->desc.max_prefill);
         TRY(dalloc(h, &h->xchg, xl.bytes));
         if (cudaMemset(h->xchg, 0, xl.bytes) != cudaSuccess) TRY(fail(h, ATLAS_ECUDA, "memset failed"));

@@ -48,7 +48,14 @@ def test_tiny_untied_matches_oracle(torch_cuda, oracle, tiny_untied_model):
             assert am == m.argmax(want)
 
 
-def test_small_prefill_generate_matches_oracle(torch_cuda, oracle, small_model):
+@pytest.mark.parametrize("ranges", ["auto", "tiles", "shares"])
+def test_small_prefill_generate_matches_oracle(torch_cuda, oracle, small_model, monkeypatch, ranges):
+    """Prompt logits and 32 greedy steps against the oracle, with the decode
+    GEMVs' CTA ranges as the planner picks them, in whole row tiles
+    (ATLAS_MV_TILE_RANGES=1), and as equal task shares with the row tiles cut
+    between CTAs finished by the last CTA to arrive (=0)."""
+    if ranges != "auto":
+        monkeypatch.setenv("ATLAS_MV_TILE_RANGES", "1" if ranges == "tiles" else "0")
     m = oracle.open(small_model)
     m.begin(128)
     prompt = np.random.default_rng(1).integers(0, 4096, 40).astype(np.uint32)
@@ -218,6 +225,44 @@ def test_wide_shapes_match_oracle(torch_cuda, oracle, model_dir, name):
         assert am == want_picks[0]
         picks = rt.generate(am, len(prompt), 31)
         np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
+
+
+@pytest.mark.parametrize("kparts,layers", [(2, 3), (3, 4)])
+def test_down_k_parts_match_oracle(torch_cuda, oracle, model_dir, monkeypatch, kparts, layers):
+    """The one-GPU down projection in K parts (ATLAS_DOWN_KPARTS; chosen by
+    itself for long FFN rows such as the 7B's 18944): each part stores partial
+    rows, the next layer's q/k/v staging (or the head's) adds them to the
+    residual in part order, and the residual alternates between two buffers.
+    Odd and even layer counts (the head reads either buffer); odd layers keep
+    ffn_down in Q4_K (a Q4_K_M file's mix). Prompt logits and 16 greedy steps
+    against the oracle, and against one part."""
+    monkeypatch.setenv("ATLAS_DOWN_KPARTS", str(kparts))
+    p = os.path.join(str(model_dir), f"kparts_{layers}.gguf")
+    if not os.path.exists(p):
+        atlas_cuda.write_synthetic_gguf(p, hidden=1024, layers=layers, q_heads=8, kv_heads=2, ffn=3072, vocab=4096,
+                                        context_length=256, tied=False, layer_mix=True, seed=90 + layers)
+    m = oracle.open(p)
+    m.begin(64)
+    prompt = np.random.default_rng(layers).integers(0, 4096, 20).astype(np.uint32)
+    for i, t in enumerate(prompt):
+        want = m.forward(int(t), i, i + 1 == len(prompt))
+    want_picks, logits, lg = [], [], want
+    for s in range(16):
+        want_picks.append(m.argmax(lg))
+        lg = m.forward(want_picks[-1], len(prompt) + s)
+        logits.append(lg)
+    with atlas_cuda.Runtime(p, max_context=64) as rt:
+        got, am = rt.prefill(prompt)
+        _close(got, want, 1e-3)
+        assert am == want_picks[0]
+        picks = rt.generate(am, len(prompt), 15)
+        np.testing.assert_array_equal(picks, np.array(want_picks[1:], np.uint32))
+        lg16, _ = rt.forward(int(want_picks[15]), len(prompt) + 15)
+        _close(lg16, logits[15], 1e-3)
+    monkeypatch.setenv("ATLAS_DOWN_KPARTS", "1")
+    with atlas_cuda.Runtime(p, max_context=64) as rt:
+        got1, _ = rt.prefill(prompt)
+        _close(got1, got.astype(np.float64), 1e-4)
 
 
 @pytest.mark.slow
