@@ -106,7 +106,8 @@ __host__ __device__ constexpr uint32_t mv_desc_bytes(uint32_t nslot)
 {
     return align128(nslot * (kMvMaxSt * 16u + kMvMaxPortions * 16u));
 }
-__host__ __device__ constexpr uint32_t mv_x_bytes(uint32_t cols) { return align128(cols * 4u + cols / 16u * 4u); }
+// staged input: binary16 hi / lo per element, the 16-element sums, and (mv4_kernel) one 1 / scale per 256-element block
+__host__ __device__ constexpr uint32_t mv_x_bytes(uint32_t cols) { return align128(cols * 4u + cols / 16u * 4u + cols / 256u * 4u); }
 
 __device__ __forceinline__ float *tpart_at(const MvHdr *h, uint32_t ts, uint32_t s, uint32_t w)
 {
@@ -248,6 +249,37 @@ __device__ void mv_producer(const MvArgs &a, MvHdr *h, uint8_t *ring, const MvCt
 // word (bytes 0 and 2, bytes 1 and 3) without byte permutes.
 // W: the staging warps (threads 0 .. 32 W - 1, synchronised on named barrier 1);
 // dred / fred: W slots each for the block reductions.
+// The partial rows the input staging adds to x, after the wait for the
+// preceding kernel: tensor parallel, the preceding row-split projection's
+// slots from every rank (once their counter has seen this occurrence), x =
+// a.x + slot 0 + slot 1 + ... in rank order; one GPU, the K parts of the
+// preceding launch in part order. own0 .. own1: this CTA's share of the sum
+// (float4 indices) to write back to xout.
+template <int W>
+__device__ __forceinline__ void stage_partials(const MvArgs &a, uint32_t n4, uint64_t *t_wait, const float4 *&red,
+                                               uint32_t &nred, uint32_t &own0, uint32_t &own1)
+{
+    if (a.in_part) {
+        red = reinterpret_cast<const float4 *>(a.in_part);
+        nred = a.in_nparts;
+    } else if (a.in_red) {
+        if (threadIdx.x == 0) {
+            const uint32_t epoch = *reinterpret_cast<volatile const uint32_t *>(&a.dstate->epoch);
+            const uint32_t k = epoch * a.seq_mul + a.seq_add;
+            wait_counter_sys(reinterpret_cast<const uint32_t *>(a.peer[a.rank] + a.in_cnt), k * a.in_arrivals,
+                             a.status);
+            if (t_wait) t_wait[1] = global_ns();   // the peers' partial rows have all arrived
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
+        red = reinterpret_cast<const float4 *>(a.peer[a.rank] + a.in_red);
+        nred = a.tp;
+    } else {
+        return;
+    }
+    own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
+    own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
+}
+
 template <int W>
 __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t *xarea, bool q4_order,
                            uint64_t *t_wait = nullptr, uint32_t x_off = 0u)
@@ -273,30 +305,9 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
     }
     if (a.pdl) pdl_wait();
     if (t_wait) t_wait[0] = global_ns();
-    // tensor parallel: the partial rows of the preceding row-split projection
-    // from every rank, then x = a.x + slot 0 + slot 1 + ... in rank order
     const float4 *red = nullptr;
     uint32_t nred = 0, own0 = 0, own1 = 0;
-    if (a.in_part) {
-        // K parts of the preceding launch on this GPU (complete after the wait)
-        red = reinterpret_cast<const float4 *>(a.in_part);
-        nred = a.in_nparts;
-        own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
-        own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
-    } else if (a.in_red) {
-        if (threadIdx.x == 0) {
-            const uint32_t epoch = *reinterpret_cast<volatile const uint32_t *>(&a.dstate->epoch);
-            const uint32_t k = epoch * a.seq_mul + a.seq_add;
-            wait_counter_sys(reinterpret_cast<const uint32_t *>(a.peer[a.rank] + a.in_cnt), k * a.in_arrivals,
-                             a.status);
-            if (t_wait) t_wait[1] = global_ns();   // the peers' partial rows have all arrived
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
-        red = reinterpret_cast<const float4 *>(a.peer[a.rank] + a.in_red);
-        nred = a.tp;
-        own0 = (uint32_t)((uint64_t)n4 * blockIdx.x / gridDim.x);
-        own1 = (uint32_t)((uint64_t)n4 * (blockIdx.x + 1u) / gridDim.x);
-    }
+    stage_partials<W>(a, n4, t_wait, red, nred, own0, own1);
     for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += kDepth * kStride) {
         float4 v[kDepth];
 #pragma unroll
@@ -403,6 +414,154 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
     }
     asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
     return inv_rms / s;
+}
+
+// Input staging of mv4_kernel, in 256-element blocks: warp w stages blocks
+// w, w + W, ... (lane l holds float4s l and 32 + l of a block): x plus the
+// preceding launch's partial rows (stage_partials), times the rms_norm
+// weight, scaled by a power of two of the block's own (its largest |x| near
+// 2^13), split into binary16 hi / lo, with the 16-element sums. The block
+// scales need no CTA-wide maximum: the tasks multiply their block sums by
+// isb[b] = 1 / scale, and the rms factor (returned; 1 without a norm) is
+// applied when a tile finishes. One CTA barrier, after which every warp
+// reduces the warps' sums of squares itself.
+template <int W>
+__device__ float m4_stage_x(const MvArgs &a, double *dred, uint8_t *xarea, bool q4_order, uint64_t *t_wait,
+                            uint32_t x_off)
+{
+    constexpr int kB = 4;   // blocks of a warp per round: 8 float4 loads in flight per lane
+    const uint32_t nblk = a.cols / 256u, n4 = a.cols / 4u;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const bool norm = a.norm_w != nullptr;
+    const float4 *xin = reinterpret_cast<const float4 *>(a.x + x_off);
+    const float4 *nw = norm ? reinterpret_cast<const float4 *>(a.norm_w + x_off) : nullptr;
+    float *xs16 = reinterpret_cast<float *>(xarea + (size_t)a.cols * 4u);
+    float *isb = xs16 + a.cols / 16u;
+    uint4 *xq = reinterpret_cast<uint4 *>(xarea);
+    // the norm weights of the first round do not depend on the preceding kernel
+    float4 w[kB][2];
+    if (norm) {
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const uint32_t b = warp + (uint32_t)j * W;
+            if (b < nblk) {
+                w[j][0] = __ldg(nw + 64u * b + lane);
+                w[j][1] = __ldg(nw + 64u * b + 32u + lane);
+            }
+        }
+    }
+    if (a.pdl) pdl_wait();
+    if (t_wait) t_wait[0] = global_ns();
+    const float4 *red = nullptr;
+    uint32_t nred = 0, own0 = 0, own1 = 0;
+    stage_partials<W>(a, n4, t_wait, red, nred, own0, own1);
+    double ss = 0.0;
+    for (uint32_t b0 = warp; b0 < nblk; b0 += (uint32_t)kB * W) {
+        float4 v[kB][2];
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const uint32_t b = b0 + (uint32_t)j * W;
+#pragma unroll
+            for (uint32_t hh = 0; hh < 2u; ++hh) {
+                const uint32_t i = 64u * b + 32u * hh + lane;
+                if (b < nblk) {
+                    v[j][hh] = __ldcg(xin + i);
+                    if (norm && b0 != warp) w[j][hh] = __ldg(nw + i);
+                }
+            }
+        }
+        if (red) {
+            for (uint32_t r = 0; r < nred; ++r) {
+#pragma unroll
+                for (int j = 0; j < kB; ++j) {
+                    const uint32_t b = b0 + (uint32_t)j * W;
+#pragma unroll
+                    for (uint32_t hh = 0; hh < 2u; ++hh) {
+                        if (b < nblk) {
+                            const float4 p = __ldcg(red + (size_t)r * n4 + 64u * b + 32u * hh + lane);
+                            v[j][hh].x += p.x; v[j][hh].y += p.y; v[j][hh].z += p.z; v[j][hh].w += p.w;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                const uint32_t b = b0 + (uint32_t)j * W;
+#pragma unroll
+                for (uint32_t hh = 0; hh < 2u; ++hh) {
+                    const uint32_t i = 64u * b + 32u * hh + lane;
+                    if (b < nblk && i >= own0 && i < own1 && a.xout) reinterpret_cast<float4 *>(a.xout)[i] = v[j][hh];
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const uint32_t b = b0 + (uint32_t)j * W;
+            if (b >= nblk) break;   // warp-uniform
+            float m = 0.f;
+#pragma unroll
+            for (uint32_t hh = 0; hh < 2u; ++hh) {
+                float4 x = v[j][hh];
+                if (a.x_hi) {
+                    // the rank's slice of the attention output inside its o blocks
+                    const uint32_t e = 4u * (64u * b + 32u * hh + lane);
+                    if (e + 0u < a.x_lo || e + 0u >= a.x_hi) x.x = 0.f;
+                    if (e + 1u < a.x_lo || e + 1u >= a.x_hi) x.y = 0.f;
+                    if (e + 2u < a.x_lo || e + 2u >= a.x_hi) x.z = 0.f;
+                    if (e + 3u < a.x_lo || e + 3u >= a.x_hi) x.w = 0.f;
+                }
+                if (norm) {
+                    ss += (double)x.x * (double)x.x;
+                    ss += (double)x.y * (double)x.y;
+                    ss += (double)x.z * (double)x.z;
+                    ss += (double)x.w * (double)x.w;
+                    x.x *= w[j][hh].x; x.y *= w[j][hh].y; x.z *= w[j][hh].z; x.w *= w[j][hh].w;
+                }
+                v[j][hh] = x;
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            // scale 2^k: exponent capped at 126, so that rows of tiny values
+            // (a SwiGLU output of all-negative gates) keep a finite scale
+            const int k = (m > 0.f && isfinite(m)) ? min(13 - ilogbf(m), 126) : 0;
+            const float sc = __int_as_float((127 + k) << 23);
+            if (lane == 0) isb[b] = __int_as_float((127 - k) << 23);
+#pragma unroll
+            for (uint32_t hh = 0; hh < 2u; ++hh) {
+                const uint32_t i = 64u * b + 32u * hh + lane;
+                const float4 x = v[j][hh];
+                const float e0 = x.x * sc, e1 = x.y * sc, e2 = x.z * sc, e3 = x.w * sc;
+                float sum = e0 + e1 + e2 + e3;
+                // hi = fp16(e), lo = fp16(e - hi); Q4_K CTAs keep the order
+                // (x0, x2, x1, x3) of the quant words' nibble pairs
+                const float a0 = e0, a1 = q4_order ? e2 : e1, a2 = q4_order ? e1 : e2, a3 = e3;
+                const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                const __half2 l01 = __floats2half2_rn(a0 - f01.x, a1 - f01.y), l23 = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
+                uint4 pk;
+                pk.x = *reinterpret_cast<const uint32_t *>(&h01);
+                pk.y = *reinterpret_cast<const uint32_t *>(&h23);
+                pk.z = *reinterpret_cast<const uint32_t *>(&l01);
+                pk.w = *reinterpret_cast<const uint32_t *>(&l23);
+                xq[i] = pk;
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                if ((lane & 3u) == 0u) xs16[i / 4u] = sum;
+            }
+        }
+    }
+    if (norm) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) dred[warp] = ss;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
+    if (!norm) return 1.0f;
+    double t = lane < (uint32_t)W ? dred[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return 1.0f / sqrtf((float)(t / (double)a.cols) + a.eps);
 }
 
 // ---------------------------------------------------------- consumers ----
@@ -1211,9 +1370,15 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
     }
     const uint64_t policy = policy_evict_first();
     const uint32_t ring_w = smem_addr(ring) + warp * (uint32_t)NS * a.slot_bytes;
-    // prologue: the first NS - 1 tasks, before the wait for the preceding kernel
+    // prologue: the first NS - 1 tasks, at most kPre of them before the wait
+    // for the preceding kernel and the input staging, the rest after. Issuing
+    // copies stalls a warp once the memory pipe's queue is full (16 warps x
+    // 4 tasks of gate/up is 22 MB in flight), which delays its wait and
+    // staging; 3 before and the rest after measured best (7B 2.533 -> 2.514
+    // ms/token against all 4 before, 14B 4.82 -> 4.79).
+    constexpr uint32_t kPre = 3u;
 #pragma unroll
-    for (uint32_t k = 0; k + 1u < (uint32_t)NS; ++k) {
+    for (uint32_t k = 0; k + 1u < (uint32_t)NS && k < kPre; ++k) {
         if (k < n) {
             if constexpr (Q4 || Q6) m4_issue<Q4>(sg, h, ci, ring_w + k * a.slot_bytes, lane, policy);
             else m4_issue_gen<TY>(m4_block(sg, ci), sg.rb, ring_w + k * a.slot_bytes, lane);
@@ -1221,7 +1386,16 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         }
         m4_commit();
     }
-    const float out_scale = mv_stage_x<W>(a, h->dred, h->fred, xarea, Q4, t_wait, a.seg[c.seg].x_off);
+    const float out_scale = m4_stage_x<W>(a, h->dred, xarea, Q4, t_wait, a.seg[c.seg].x_off);
+#pragma unroll
+    for (uint32_t k = kPre; k + 1u < (uint32_t)NS; ++k) {
+        if (k < n) {
+            if constexpr (Q4 || Q6) m4_issue<Q4>(sg, h, ci, ring_w + k * a.slot_bytes, lane, policy);
+            else m4_issue_gen<TY>(m4_block(sg, ci), sg.rb, ring_w + k * a.slot_bytes, lane);
+            m4_next(ci, nb, paired);
+        }
+        m4_commit();
+    }
     t_ready = global_ns();
     if (!active) return;
     // sharing of the first and last tiles with neighbouring warps
@@ -1231,6 +1405,7 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
     const uint32_t la = m4_warp_of(c.j0, L, weff, max(last_tile * TP, c.j0)),
                    lb = m4_warp_of(c.j0, L, weff, min(last_tile * TP + TP, c.j1) - 1u);
     const float *xs16 = reinterpret_cast<const float *>(xarea + (size_t)a.cols * 4u);
+    const float *isb = xs16 + a.cols / 16u;
     const uint8_t *ringp = ring + (size_t)warp * NS * a.slot_bytes;
     const uint32_t wlow = (uint32_t)reinterpret_cast<uintptr_t>(sg.w0), wlow1 = (uint32_t)reinterpret_cast<uintptr_t>(sg.w1);
     float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
@@ -1261,6 +1436,9 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
             gen_task<TY>(slot + g * m4_gen_row(TY), slot + (g + 8u) * m4_gen_row(TY), xb, xs, lane, o0, o1);
         }
         __syncwarp();   // the slot is re-filled by a later iteration's copies
+        const float sb = isb[cc.b];
+        o0 *= sb;
+        o1 *= sb;
         if (cc.s) {
             a10 += o0;
             a11 += o1;

@@ -29,6 +29,10 @@ heads. N = 2 and 4 run one tensor-parallel group of N ranks; N = 8 runs two
 groups of 4 (each decodes its own copy of the workload). value = groups x
 tokens / max-over-ranks device time.
 
+--shape 14b: the long-context workload instead (Qwen2.5-14B shape, 48 layers,
+40 / 8 heads, FFN 13824: an 8192-token prompt, then 512 greedy decode steps),
+tensor-parallel over up to 8 GPUs (its 8 KV heads).
+
 --impl reference runs only the CPU reference (rank 0; other ranks exit) and
 prints its own JSON line; it never loads libatlas_cuda.so (its model file
 comes from the writer built into oracle/liboracle.so).
@@ -57,6 +61,13 @@ WORKLOAD = {
     "cfg1": "Qwen2.5-3B-shaped Q4_K/Q6_K (hidden 2048, 36 layers, 16/2 heads, FFN 11008, vocab 151936, tied Q6_K "
             "head): 512-token prefill + 256 greedy decode, batch 1",
 }
+# The long-context workload (--shape 14b): Qwen2.5-14B shape, an 8192-token prompt through the batched
+# prefill, then 512 greedy decode steps; tensor-parallel over up to 8 GPUs (8 KV heads).
+CFG3 = dict(hidden=5120, layers=48, q_heads=40, kv_heads=8, ffn=13824, vocab=152064, context_length=32768, seed=3,
+            tied=False)
+WORKLOAD["cfg3"] = ("Qwen2.5-14B-shaped Q4_K/Q6_K (hidden 5120, 48 layers, 40/8 heads, FFN 13824, vocab 152064, untied "
+                    "Q6_K head): 8192-token prefill + 512 greedy decode, batch 1")
+LONG_PROMPT, LONG_GEN = 8192, 512
 # The 8-sequence workload (--workload 32b-batch8): Qwen2.5-32B shape, 8 independent sequences, each a
 # 2048-token prompt prefilled batched, then 256 decode steps at batch 8 (all sequences in one step).
 CFG4 = dict(hidden=5120, layers=64, q_heads=40, kv_heads=8, ffn=27648, vocab=152064, context_length=32768, seed=4,
@@ -282,13 +293,15 @@ def allmax(pg, v):
     return float(t.item())
 
 
-def tp_layout(ws):
-    """(tensor-parallel size, groups) for N ranks of the 7B model (4 KV heads)."""
-    if ws <= 4:
+def tp_layout(ws, kv_heads=4):
+    """(tensor-parallel size, groups) for N ranks: one group over up to kv_heads ranks (the 7B model's 4, the
+    14B's 8), else groups of kv_heads ranks that each decode their own copy of the workload."""
+    if ws <= kv_heads:
         return ws, 1
-    if ws % 4:
-        raise SystemExit(f"--gpus {ws}: the 7B model is tensor-parallel over 1, 2 or 4 ranks; use 1, 2, 4 or 8")
-    return 4, ws // 4
+    if ws % kv_heads:
+        raise SystemExit(f"--gpus {ws}: the model is tensor-parallel over up to {kv_heads} ranks; use a divisor "
+                         f"or a multiple of {kv_heads}")
+    return kv_heads, ws // kv_heads
 
 
 def run_model(name, cfg, rt, steps, warmup, pg, clocks_gpu=None):
@@ -393,13 +406,17 @@ def ensure_model_product_writer(name, cfg, rank, pg):
 def run_ours(args):
     import atlas_cuda
     ws, rank, local, pg = dist_setup()
-    tp, groups = tp_layout(ws)
+    name, cfg = {"3b": ("cfg1", CFG1), "7b": ("cfg2", CFG2), "14b": ("cfg3", CFG3)}[args.shape]
+    if args.layers:
+        # profiles on a small case: the same launch shapes, fewer layers (no reference fixture applies)
+        name, cfg = f"{name}_l{args.layers}", dict(cfg, layers=args.layers)
+        WORKLOAD[name] = WORKLOAD[name.split("_")[0]] + f" (cut to {args.layers} layers)"
+    tp, groups = tp_layout(ws, cfg["kv_heads"])
     group_id, tp_rank = rank // tp, rank % tp
     tp_group = None
     if pg and groups > 1:
         subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
         tp_group = subgroups[group_id]
-    name, cfg = ("cfg1", CFG1) if args.shape == "3b" else ("cfg2", CFG2)
     path = ensure_model_product_writer(name, cfg, rank, pg)
     rt = atlas_cuda.Runtime(path, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT,
                             tp_rank=tp_rank, tp_size=tp)
@@ -564,7 +581,7 @@ def run_batch8(args):
 
 
 def main():
-    global GEN
+    global GEN, PROMPT
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -572,21 +589,25 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the 3B workload at N=1")
-    ap.add_argument("--shape", default="7b", choices=["7b", "3b"],
-                    help="the headline workload's model shape (3b: the secondary workload alone, e.g. for profiles)")
-    ap.add_argument("--gen", type=int, default=GEN, help="greedy decode steps per workload step (profiles: fewer)")
+    ap.add_argument("--shape", default="7b", choices=["7b", "3b", "14b"],
+                    help="the headline workload's model shape (3b: the secondary workload alone, e.g. for profiles; "
+                         "14b: the long-context workload, an 8192-token prompt and 512 decode steps)")
+    ap.add_argument("--gen", type=int, default=None, help="greedy decode steps per workload step (profiles: fewer)")
     ap.add_argument("--workload", default="default", choices=["default", "32b-batch8"],
                     help="32b-batch8: the 8-sequence 32B-shaped workload (one GPU)")
-    ap.add_argument("--layers", type=int, default=0, help="32b-batch8: fewer layers (profiles on a small case)")
+    ap.add_argument("--layers", type=int, default=0, help="fewer layers (profiles on a small case)")
     args = ap.parse_args()
-    GEN = args.gen
+    if args.shape == "14b":
+        PROMPT, GEN = LONG_PROMPT, LONG_GEN
+    if args.gen is not None:
+        GEN = args.gen
     if args.workload == "32b-batch8":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "32b-batch8: the reference decodes one sequence "
                               "per process; its 32B CPU run takes hours (time the default workload instead)"}))
             return
         global B8_GEN
-        B8_GEN = args.gen if args.gen != 256 else B8_GEN
+        B8_GEN = args.gen if args.gen is not None else B8_GEN
         run_batch8(args)
         return
     if args.impl == "reference":
