@@ -376,9 +376,9 @@ def summarize(name, cfg, r, steps, pg, groups, sl=None, tp=1):
         "roofline": {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(rank_gbs / hbm, 4), "peak_kind": hbm_kind,
                      "bytes_per_token": int(rank_bytes), "traffic": None,
-                     "traffic_note": "not re-measured in the timed run; ncu captures of the two largest GEMV "
-                                     "launches read 1.004x and 1.001x their algorithmic bytes "
-                                     "(profiles/mv4_kernel_gate_up_q4k_and_down_q6k_3b.md)",
+                     "traffic_note": "not re-measured in the timed run; ncu captures of one 7B-shape layer's "
+                                     "GEMV launches read within 1 % of their algorithmic bytes "
+                                     "(profiles/mv4_kernel_qkv_o_gateup_down_7b_shape_two_layers.md)",
                      "kernel": "decode step: CUDA graph of PDL-chained kernels (mv4_kernel dequant-GEMVs, attention, "
                                "embed, argmax); achieved = one GPU's weight + KV bytes per token / device time per "
                                "token"},
