@@ -717,24 +717,34 @@ int plan_mv(AtlasCuda *h, MvPlan &p, uint32_t cols, bool paired, const std::vect
         tiles.push_back(a.seg[0].rows / (uint32_t)d2::kMvRows);
         cta_n.push_back(std::min(G, tiles[0]));
     } else {
-        double total = 0;
-        for (uint32_t s = 0; s < a.n_seg; ++s) total += (double)a.seg[s].rows * (double)a.seg[s].row_bytes;
-        uint32_t used = 0;
+        // CTAs per segment: the SMs go one at a time to the segment whose
+        // warps carry the largest load, a warp's load being its tasks times
+        // the cost of one task of the segment's type (a Q6_K task issues about
+        // 1.9x the instructions of a Q4_K one: 898 against 475 at the 7B
+        // shape). Shares by bytes gave the 7B q/k/v launch's v segment 2 Q6_K
+        // tasks per warp while q and k ran 2 Q4_K ones.
+        auto cost = [](uint32_t type) { return type == 14u ? 1.9 : type == 12u ? 1.0 : 1.5; };
+        auto load = [&](uint32_t s, uint32_t n) {
+            const uint64_t per_cta = ((uint64_t)tiles[s] * a.nb + n - 1u) / n;
+            return (double)((per_cta + d2::kM4Warps - 1u) / d2::kM4Warps) * cost(a.seg[s].type);
+        };
         for (uint32_t s = 0; s < a.n_seg; ++s) {
             tiles.push_back(a.seg[s].rows / (uint32_t)d2::kMvRows);
-            const double share = (double)G * (double)a.seg[s].rows * (double)a.seg[s].row_bytes / total;
-            uint32_t n = (uint32_t)std::max(1.0, std::floor(share + 0.5));
-            n = std::min(n, tiles[s]);
-            cta_n.push_back(n);
-            used += n;
+            cta_n.push_back(1u);
         }
-        while (used > G) {
-            size_t big = 0;
-            for (size_t s = 1; s < cta_n.size(); ++s)
-                if (cta_n[s] > cta_n[big]) big = s;
-            if (cta_n[big] <= 1) return fail(h, ATLAS_EINVAL, "mv: more segments than SMs");
-            --cta_n[big];
-            --used;
+        if (a.n_seg > G) return fail(h, ATLAS_EINVAL, "mv: more segments than SMs");
+        for (uint32_t used = a.n_seg; used < G; ++used) {
+            uint32_t best = a.n_seg;
+            double bl = -1.0;
+            for (uint32_t s = 0; s < a.n_seg; ++s) {
+                const double l = load(s, cta_n[s]);
+                if (cta_n[s] < tiles[s] && l > bl) {
+                    bl = l;
+                    best = s;
+                }
+            }
+            if (best == a.n_seg) break;
+            ++cta_n[best];
         }
     }
     std::vector<d2::MvCta> ctas;
