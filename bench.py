@@ -229,15 +229,20 @@ def ensure_model_oracle_writer(name, cfg):
     return path
 
 
+SHAPES = {"3b": ("cfg1", CFG1), "7b": ("cfg2", CFG2), "14b": ("cfg3", CFG3)}
+
+
 def run_reference(args):
-    """CPU reference arm: rank 0 only; other ranks exit at once without work."""
+    """CPU reference arm: rank 0 only; other ranks exit at once without work. The workload of --shape, decoded at
+    the positions the GPU arm decodes (after a PROMPT-position cache)."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    path = ensure_model_oracle_writer("cfg2", CFG2)
+    name, cfg = SHAPES[args.shape]
+    path = ensure_model_oracle_writer(name, cfg)
     dec, pre = [], []
     smp = None
     for i in range(args.warmup + args.steps):
-        smp = cpu_reference_sample(path, CFG2, n_decode=2, n_prompt=2)
+        smp = cpu_reference_sample(path, cfg, n_decode=2, n_prompt=2)
         if smp is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libbrainref.so was not built "
                                                                   "(the reference sources were absent at build time)"}))
@@ -247,13 +252,13 @@ def run_reference(args):
             pre.append(smp["prefill_tok_s"])
     v = statistics.mean(dec)
     sample = (f"per step: 2 prompt tokens (token at a time, no logits), then 2 greedy decode tokens at positions "
-              f"{PROMPT}-{PROMPT + 1} over a {PROMPT}-position cache, 7B shape; "
+              f"{PROMPT}-{PROMPT + 1} over a {PROMPT}-position cache, {args.shape.upper()} shape; "
               f"{smp['host_cores']} host threads, {smp['gemv_threads']} GEMV workers (the reference's cap)")
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(2000.0 / v + 2000.0 / statistics.mean(pre), 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
-            "config": {"workload": WORKLOAD["cfg2"] + " (CPU: bounded sample)", "parallelism": "CPU threads",
+            "config": {"workload": WORKLOAD[name] + " (CPU: bounded sample)", "parallelism": "CPU threads",
                        "kv_cache": "fp32"},
             "prefill_tok_s": round(statistics.mean(pre), 4),
             "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": smp["gemv_threads"],
@@ -406,7 +411,7 @@ def ensure_model_product_writer(name, cfg, rank, pg):
 def run_ours(args):
     import atlas_cuda
     ws, rank, local, pg = dist_setup()
-    name, cfg = {"3b": ("cfg1", CFG1), "7b": ("cfg2", CFG2), "14b": ("cfg3", CFG3)}[args.shape]
+    name, cfg = SHAPES[args.shape]
     if args.layers:
         # profiles on a small case: the same launch shapes, fewer layers (no reference fixture applies)
         name, cfg = f"{name}_l{args.layers}", dict(cfg, layers=args.layers)
