@@ -2209,7 +2209,6 @@ int atlas_cuda_create(const AtlasModelDesc *desc, const AtlasTensorDesc *tensors
     if (tp > 1) {
         if (const char *why = tp_slice_of(d, d.tp_rank, tp, sl))
             return fail(nullptr, ATLAS_EINVAL, "tensor parallel: %s", why);
-        if (d.kv_fp16) return fail(nullptr, ATLAS_EINVAL, "tensor parallel: fp32 KV cache only");
     }
     AtlasCuda *h = new AtlasCuda();
     h->tp = tp;

@@ -66,7 +66,9 @@ WORKLOAD = {
 CFG3 = dict(hidden=5120, layers=48, q_heads=40, kv_heads=8, ffn=13824, vocab=152064, context_length=32768, seed=3,
             tied=False)
 WORKLOAD["cfg3"] = ("Qwen2.5-14B-shaped Q4_K/Q6_K (hidden 5120, 48 layers, 40/8 heads, FFN 13824, vocab 152064, untied "
-                    "Q6_K head): 8192-token prefill + 512 greedy decode, batch 1")
+                    "Q6_K head): 8192-token prefill + 512 greedy decode over a binary16 KV cache, batch 1")
+# the workloads whose KV cache is binary16 (the long-context one stresses split-K decode over a full fp16 cache)
+FP16_CACHE = {"cfg3"}
 LONG_PROMPT, LONG_GEN = 8192, 512
 # The 8-sequence workload (--workload 32b-batch8): Qwen2.5-32B shape, 8 independent sequences, each a
 # 2048-token prompt prefilled batched, then 256 decode steps at batch 8 (all sequences in one step).
@@ -94,8 +96,8 @@ def weight_bytes(c, sl=None):
     return L * per_layer + sl["vocab_rows"] * H * Q6K + 4 * H
 
 
-def kv_bytes_per_position(c, kv_heads=None):
-    return 2 * c["layers"] * (kv_heads or c["kv_heads"]) * 128 * 4
+def kv_bytes_per_position(c, kv_heads=None, elem=4):
+    return 2 * c["layers"] * (kv_heads or c["kv_heads"]) * 128 * elem
 
 
 def prefill_flops(c, T):
@@ -361,9 +363,10 @@ def summarize(name, cfg, r, steps, pg, groups, sl=None, tp=1):
     decode_tps = groups * steps * GEN / gen_dev
     per_token_s = gen_dev / (steps * GEN)
     kv_heads = sl["kv_heads"] if sl else cfg["kv_heads"]
-    kv_avg = kv_bytes_per_position(cfg, kv_heads) * (PROMPT + GEN / 2.0)
+    elem = 2 if name.split("_")[0] in FP16_CACHE else 4
+    kv_avg = kv_bytes_per_position(cfg, kv_heads, elem) * (PROMPT + GEN / 2.0)
     rank_bytes = weight_bytes(cfg, sl) + kv_avg             # one rank's algorithmic bytes per token
-    total_bytes = weight_bytes(cfg) + kv_bytes_per_position(cfg) * (PROMPT + GEN / 2.0)
+    total_bytes = weight_bytes(cfg) + kv_bytes_per_position(cfg, None, elem) * (PROMPT + GEN / 2.0)
     hbm, hbm_kind = measured("hbm_gbs", 6650.0)
     tpk, tpk_kind = measured("bf16_tflops", 1590.0)
     rank_gbs = rank_bytes / per_token_s / 1e9
@@ -423,8 +426,9 @@ def run_ours(args):
         subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
         tp_group = subgroups[group_id]
     path = ensure_model_product_writer(name, cfg, rank, pg)
+    fp16 = name.split("_")[0] in FP16_CACHE
     rt = atlas_cuda.Runtime(path, device=local, max_context=PROMPT + GEN + 16, max_prefill=PROMPT,
-                            tp_rank=tp_rank, tp_size=tp)
+                            tp_rank=tp_rank, tp_size=tp, kv_fp16=fp16)
     if tp > 1:
         atlas_cuda.connect_tp(rt, group=tp_group)
     barrier(pg)
@@ -468,7 +472,7 @@ def run_ours(args):
             "data": "synthetic (seeded random Q4_K/Q6_K weights, random prompt ids)",
             "config": {"workload": WORKLOAD[name], "parallelism": par if ws > 1 else "1 GPU",
                        "l2": f"inputs larger than L2 ({weight_bytes(cfg) / 1e9:.2f} GB of weights streamed per token)",
-                       "kv_cache": "fp32"},
+                       "kv_cache": "fp16" if fp16 else "fp32"},
             "decode_ms_per_token": round(s["decode_ms_per_token"], 4),
             "prefill_tok_s": round(s["prefill_tok_s"], 1),
             "roofline": s["roofline"],

@@ -1,11 +1,12 @@
 """One rank of a tensor-parallel run (launched by torch.distributed.run).
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
-        --master-port P tests/tp_worker.py MODEL.gguf OUT.npz PROMPT_LEN STEPS [SEED]
+        --master-port P tests/tp_worker.py MODEL.gguf OUT.npz PROMPT_LEN STEPS [SEED [fp16]]
 
 Every rank opens the model with its slice on GPU `rank`, exchanges its
 exchange-area handle through a gloo process group, prefills a seeded random
-prompt and generates STEPS - 1 greedy tokens. Rank 0 writes the picks, the
+prompt and generates STEPS - 1 greedy tokens (with a binary16 KV cache when
+the last argument is fp16). Rank 0 writes the picks, the
 prompt's last logits (all ranks' vocab slices put together) and the device
 time per decode step to OUT.npz.
 """
@@ -25,10 +26,11 @@ def main():
     path, out = sys.argv[1], sys.argv[2]
     n_prompt, steps = int(sys.argv[3]), int(sys.argv[4])
     seed = int(sys.argv[5]) if len(sys.argv) > 5 else 5
+    kv_fp16 = len(sys.argv) > 6 and sys.argv[6] == "fp16"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     rt = atlas_cuda.Runtime(path, device=int(os.environ.get("LOCAL_RANK", rank)), max_context=n_prompt + steps + 8,
-                            tp_rank=rank, tp_size=world)
+                            tp_rank=rank, tp_size=world, kv_fp16=kv_fp16)
     vocab = rt.vocab
     prompt = np.random.default_rng(seed).integers(0, vocab, n_prompt).astype(np.uint32)
     atlas_cuda.connect_tp(rt)
