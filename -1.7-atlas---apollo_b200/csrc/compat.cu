@@ -122,10 +122,11 @@ int brain_gpu_matvec_batch(const BrainGpuMatvec *ops, size_t count)
         const BrainGpuMatvec &op = ops[i];
         const uint32_t be = atlas::block_elems(op.type), bb = atlas::block_bytes(op.type);
         // rows, cols and offset above 2^32 are rejected first (as src/gpu_matvec.c:220-223
-        // does), so the byte count below cannot overflow 64 bits
+        // does); the tensor's extent is then checked by a division (rows x row bytes can
+        // exceed 64 bits: 2^32 rows of 2^27 Q8_0 blocks of 34 bytes)
         if (!op.input || !op.output || !op.rows || !op.cols || !be || op.type == 1u || op.cols % be ||
             op.rows > 0xffffffffull || op.cols > 0xffffffffull || op.offset > 0xffffffffull ||
-            op.offset > g_compat.size || op.rows * (op.cols / be) * bb > g_compat.size - op.offset) {
+            op.offset > g_compat.size || op.rows > (g_compat.size - op.offset) / ((op.cols / be) * bb)) {
             report("arguments", "invalid operation", count);
             return 0;
         }
