@@ -119,7 +119,8 @@ struct MvSeg {
     const float *bias;     // optional (MV_STORE)
     float *out;
     uint32_t copies;       // bulk copies per whole-row run of 16 rows: 1, 2, 4 or 8
-    uint32_t x_off;        // mv4_kernel: the segment's input starts at x + x_off (a K part of a longer row)
+    uint32_t x_off;        // mv4_kernel: the segment's input starts at x + x_off (a K part of a longer row;
+                           // such launches carry no rms_norm, whose factor needs the whole row)
 };
 
 struct MvCta {

@@ -1127,6 +1127,7 @@ int build_graph2(AtlasCuda *h)
     if ((rc = plan_mv(h, dn, sl.ffn_rows / KP, false, down_segs(h, w0.down, w0.td, KP), KP > 1 ? (uint32_t)d2::MV_STORE : part)))
         return rc;
     if (KP > 1 && dn.a.engine != 1u) return fail(h, ATLAS_EINVAL, "graph decode: K parts need the mv4 kernel");
+    // (down has no rms_norm: a K part's staging sees only its slice of the row)
     auto resid = [&](uint32_t l) { return KP > 1 && (l & 1u) ? h->x2 : h->x; };
     if ((rc = plan_mv(h, hd, d.hidden, false, {mvseg(h->head, h->t_head, sl.vocab_rows, d.hidden, nullptr, h->logits)},
                       d2::MV_LOGITS)))
