@@ -425,7 +425,15 @@ __device__ float mv_stage_x(const MvArgs &a, double *dred, float *fred, uint8_t 
 // isb[b] = 1 / scale, and the rms factor (returned; 1 without a norm) is
 // applied when a tile finishes. One CTA barrier, after which every warp
 // reduces the warps' sums of squares itself.
-template <int W>
+// I8 (the Q4_K / Q6_K tasks): instead of binary16 pairs, three int8 planes
+// per element, e = x 2^k ~ hi + mid / 128 + lo / 16384 with max|e| of the
+// block in [63.75, 127.5) (hi in -127..127, mid and lo in -64..64: the
+// residual is below 2^-21 of the block's largest |x|, under the rounding of
+// an fp32 dot product of these lengths). A block's 1024 bytes hold 32 chunks
+// of 8 elements, each [hi x8][mid x8][lo x8][zero x8]: the integer MMAs'
+// B operands are 8-byte loads from one plane (or the zero slice) of a chunk,
+// conflict-free per half warp. The 16-element sums are those of e.
+template <int W, bool I8 = false>
 __device__ float m4_stage_x(const MvArgs &a, double *dred, uint8_t *xarea, bool q4_order, uint64_t *t_wait,
                             uint32_t x_off)
 {
@@ -522,6 +530,53 @@ __device__ float m4_stage_x(const MvArgs &a, double *dred, uint8_t *xarea, bool 
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if constexpr (I8) {
+                int k = 0;
+                if (m > 0.f && isfinite(m)) {
+                    k = 6 - ilogbf(m);   // m 2^k in [64, 128)
+                    if (k > 126) k = 126;
+                    else if (m * __int_as_float((127 + k) << 23) >= 127.5f) --k;
+                }
+                const float sc = __int_as_float((127 + k) << 23);
+                if (lane == 0) isb[b] = __int_as_float((127 - k) << 23);
+                uint8_t *xblk = xarea + (size_t)b * 1024u;
+#pragma unroll
+                for (uint32_t hh = 0; hh < 2u; ++hh) {
+                    const uint32_t i = 64u * b + 32u * hh + lane;
+                    const float4 x = v[j][hh];
+                    const float e[4] = {x.x * sc, x.y * sc, x.z * sc, x.w * sc};
+                    int q[3][4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float h1 = rintf(e[u]);
+                        const float r1 = (e[u] - h1) * 128.0f;
+                        const float m1 = rintf(r1);
+                        const float l1 = rintf((r1 - m1) * 128.0f);
+                        q[0][u] = (int)h1;
+                        q[1][u] = (int)m1;
+                        q[2][u] = (int)l1;
+                    }
+                    uint32_t pw[3];
+#pragma unroll
+                    for (int p = 0; p < 3; ++p)
+                        pw[p] = __byte_perm(__byte_perm((uint32_t)q[p][0], (uint32_t)q[p][1], 0x0040u),
+                                            __byte_perm((uint32_t)q[p][2], (uint32_t)q[p][3], 0x0040u), 0x5410u);
+                    // lane pairs (2c, 2c + 1) hold elements 0-3 and 4-7 of chunk
+                    // 16 hh + c: the even lane stores the chunk's hi and mid
+                    // slices, the odd one lo and zero (one 16-byte store each)
+                    const uint32_t o0 = __shfl_xor_sync(0xffffffffu, pw[0], 1);
+                    const uint32_t o1 = __shfl_xor_sync(0xffffffffu, pw[1], 1);
+                    const uint32_t o2 = __shfl_xor_sync(0xffffffffu, pw[2], 1);
+                    const bool odd = lane & 1u;
+                    const uint4 st = odd ? make_uint4(o2, pw[2], 0u, 0u) : make_uint4(pw[0], o0, pw[1], o1);
+                    *reinterpret_cast<uint4 *>(xblk + (16u * hh + (lane >> 1)) * 32u + 16u * (lane & 1u)) = st;
+                    float sum = (e[0] + e[1]) + (e[2] + e[3]);
+                    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                    if ((lane & 3u) == 0u) xs16[i / 4u] = sum;
+                }
+                continue;
+            }
             // scale 2^k: exponent capped at 126, so that rows of tiny values
             // (a SwiGLU output of all-negative gates) keep a finite scale
             const int k = (m > 0.f && isfinite(m)) ? min(13 - ilogbf(m), 126) : 0;
@@ -1137,6 +1192,181 @@ __device__ __forceinline__ void ld16_u2(const uint8_t *p, uint32_t (&w)[4])
     for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
 }
 
+// 8 bytes at a 2-byte-aligned shared-memory address: three aligned loads
+// and a funnel shift by the misalignment (0 or 16 bits).
+__device__ __forceinline__ uint2 ld8_u2(const uint8_t *p)
+{
+    const uintptr_t ad = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(ad & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(ad & 3u) * 8u;
+    const uint32_t v0 = q[0], v1 = q[1], v2 = q[2];
+    return make_uint2(__funnelshift_r(v0, v1, sh), __funnelshift_r(v1, v2, sh));
+}
+
+// d += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulators
+// (lane (g, t): a0 = A[g][4t..4t+3], a1 = A[g+8][4t..], a2 = A[g][16+4t..],
+// a3 = A[g+8][16+4t..]; b.x = B[4t..4t+3][g], b.y = B[16+4t..][g];
+// d = D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1]).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
+}
+
+// Integer-MMA tasks (16 rows x one 256-element block) over the int8 planes of
+// m4_stage_x<W, true>. In one MMA, lanes t = 0, 1 of a row group carry the
+// k slots of one scale group and lanes t = 2, 3 those of another; B column
+// n holds plane n & 3 (hi, mid, lo, zero) of group n >> 2's elements and
+// zero elsewhere, so accumulator columns 2t, 2t + 1 of lane t end as exact
+// integer sums of its own group: (hi, mid) for even t, (lo, -) for odd t.
+// The group scales are applied in integers (exact: |sums| < 2^31), the block
+// scale d, the plane units and the offsets in fp32 once per task. xl: this
+// lane's B base in the staged block, m4_bsel; the caller multiplies the
+// results by the block's 1 / 2^k.
+//
+// B base of lane (g, t): plane g & 3 of the chunk when the lane's column
+// belongs to the group its k slots carry ((g >> 2) == (t >> 1)), else a
+// zero slice. q6: Q6_K chunk layout (lane t's elements 8t + 32c + 128q),
+// else Q4_K (64 (t >> 1) + 16 (t & 1) + 32 nu + 64 pi, halves of 8), whose
+// zero lanes of a half warp all read one slice (a broadcast: distinct zero
+// slices there would share banks with each other).
+__device__ __forceinline__ uint32_t m4_bsel(uint32_t lane, bool q6)
+{
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const bool act = (g >> 2) == (t >> 1) && (g & 3u) < 3u;
+    if (q6) return 32u * t + 8u * (act ? (g & 3u) : 3u);
+    return act ? 512u * (t >> 1) + 64u * (t & 1u) + 8u * (g & 3u) : 512u * (g >> 2) + 24u;
+}
+
+// Q4_K (dequant_q4_k, src/brain_runtime.c:960-1003): y = d sc_j q x - dmin
+// m_j x per 32-element sub-block j. Lane t reads the 16 quant bytes
+// 16 (t & 1) .. of chunk pi + 2 (t >> 1) (pi = 0, 1) of rows g and g + 8;
+// low nibbles (nu = 0) are sub-block 2 (pi + 2 (t >> 1)), high nibbles
+// (nu = 1, masked in place: 16 q) the next one. Two MMAs (8 bytes each) per
+// (pi, nu); the sums are 16 q x for nu = 1, so 16 sc multiplies the nu = 0
+// sums and the total is divided by 16 at the end. The min term uses the
+// staged 16-element sums of e, once per (row, sub-block), by the even lanes.
+__device__ __forceinline__ void q4k_task8(const uint8_t *r0, const uint8_t *r1, const uint8_t *xl, const float *xs,
+                                          uint32_t t, float &o0, float &o1)
+{
+    const uint4 H0 = *reinterpret_cast<const uint4 *>(r0), H1 = *reinterpret_cast<const uint4 *>(r1);
+    const bool upper = t >= 2u;   // sub-blocks 4..7 (the 6-bit scales packed across bytes)
+    uint32_t SC[2], MN[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint4 H = r ? H1 : H0;
+        const uint32_t sc03 = H.y & 0x3f3f3f3fu, m03 = H.z & 0x3f3f3f3fu;
+        const uint32_t sc47 = (H.w & 0x0f0f0f0fu) | ((H.y >> 2) & 0x30303030u);
+        const uint32_t m47 = ((H.w >> 4) & 0x0f0f0f0fu) | ((H.z >> 2) & 0x30303030u);
+        SC[r] = upper ? sc47 : sc03;
+        MN[r] = upper ? m47 : m03;
+    }
+    int T[4] = {0, 0, 0, 0};
+    float M0 = 0.f, M1 = 0.f;
+    const uint32_t off = 16u + 64u * (t >> 1) + 16u * (t & 1u);
+#pragma unroll
+    for (uint32_t pi = 0; pi < 2u; ++pi) {
+        const uint4 W0 = *reinterpret_cast<const uint4 *>(r0 + off + 32u * pi);
+        const uint4 W1 = *reinterpret_cast<const uint4 *>(r1 + off + 32u * pi);
+#pragma unroll
+        for (uint32_t nu = 0; nu < 2u; ++nu) {
+            const uint32_t k = nu ? 0xf0f0f0f0u : 0x0f0f0f0fu;
+            const uint8_t *xp = xl + 256u * pi + 128u * nu;
+            int D[4] = {0, 0, 0, 0};
+            mma_u8s8(D, W0.x & k, W1.x & k, W0.y & k, W1.y & k, *reinterpret_cast<const uint2 *>(xp));
+            mma_u8s8(D, W0.z & k, W1.z & k, W0.w & k, W1.w & k, *reinterpret_cast<const uint2 *>(xp + 32));
+            const uint32_t sh = 8u * (2u * pi + nu);
+            const int s0 = (int)(((SC[0] >> sh) & 63u) << (nu ? 0u : 4u));
+            const int s1 = (int)(((SC[1] >> sh) & 63u) << (nu ? 0u : 4u));
+            T[0] += s0 * D[0];
+            T[1] += s0 * D[1];
+            T[2] += s1 * D[2];
+            T[3] += s1 * D[3];
+            const uint32_t j = 2u * pi + 4u * (t >> 1) + nu;
+            const float xj = xs[2u * j] + xs[2u * j + 1u];
+            M0 += u2f_small((MN[0] >> sh) & 63u) * xj;
+            M1 += u2f_small((MN[1] >> sh) & 63u) * xj;
+        }
+    }
+    const bool odd = t & 1u;
+    const float u0 = odd ? 1.0f / (16384.0f * 16.0f) : 1.0f / 16.0f, u1 = odd ? 0.f : 1.0f / (128.0f * 16.0f);
+    const float mo = odd ? 0.f : 1.f;
+    o0 += h2f((uint16_t)(H0.x & 0xffffu)) * ((float)T[0] * u0 + (float)T[1] * u1) - h2f((uint16_t)(H0.x >> 16)) * (mo * M0);
+    o1 += h2f((uint16_t)(H1.x & 0xffffu)) * ((float)T[2] * u0 + (float)T[3] * u1) - h2f((uint16_t)(H1.x >> 16)) * (mo * M1);
+}
+
+// A 6-bit quant of group c (0..3) from the ql / qh words of 4 consecutive
+// l: low or high nibbles of ql, qh bit pair c moved to bits 4-5 of each byte
+// (m02 = qh & 0x33.., m13 = qh & 0xcc..: no bits cross a byte).
+__device__ __forceinline__ uint32_t q6_quant(uint32_t c, uint32_t ql_lo, uint32_t ql_hi, uint32_t m02, uint32_t m13)
+{
+    const uint32_t lowm = 0x0f0f0f0fu;
+    switch (c) {
+    case 0: return (ql_lo & lowm) | ((m02 << 4) & 0xf0f0f0f0u);
+    case 1: return (ql_hi & lowm) | ((m13 << 2) & 0xf0f0f0f0u);
+    case 2: return ((ql_lo >> 4) & lowm) | (m02 & 0xf0f0f0f0u);
+    default: return ((ql_hi >> 4) & lowm) | ((m13 >> 2) & 0xf0f0f0f0u);
+    }
+}
+
+// prmt.b32 in its default mode: a selector nibble with bit 3 set replicates
+// the sign bit of the byte its low bits select (a sign-extended int8 when
+// the four nibbles are k, k | 8, k | 8, k | 8).
+__device__ __forceinline__ uint32_t prmt_sx(uint32_t x, uint32_t sel)
+{
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(0u), "r"(sel));
+    return r;
+}
+__host__ __device__ constexpr uint32_t sx_sel(uint32_t k) { return k | ((k | 8u) * 0x1110u); }
+
+// Q6_K (dequant_q6_k, src/brain_runtime.c:1049-1083): y = d sc_G (q - 32) x
+// per 16-element group G. Lane t reads ql bytes 8t.. and 32 + 8t.. of half
+// q (64 q ..) and qh bytes 8t.. (128 + 32 q ..) of rows g and g + 8; MMA
+// (q, c) takes group c's quants of those 8 l, group 8q + 2c + (t >> 1). The
+// -32 offset is applied with the staged 16-element sums of e, once per (row,
+// group), by the even lanes. sel0 / sel1: byte_perm selectors of scale byte
+// (t >> 1) / 2 + (t >> 1) of a word, sign-extended.
+__device__ __forceinline__ void q6k_task8(const uint8_t *r0, const uint8_t *r1, const uint8_t *xl, const float *xs,
+                                          uint32_t t, uint32_t sel0, uint32_t sel1, float &o0, float &o1)
+{
+    uint32_t S0[4], S1[4];
+    ld16_u2(r0 + 192, S0);
+    ld16_u2(r1 + 192, S1);
+    int T[4] = {0, 0, 0, 0};
+    float F0 = 0.f, F1 = 0.f;
+#pragma unroll
+    for (uint32_t q = 0; q < 2u; ++q) {
+        const uint2 l0 = ld8_u2(r0 + 64u * q + 8u * t), h0 = ld8_u2(r0 + 64u * q + 32u + 8u * t);
+        const uint2 l1 = ld8_u2(r1 + 64u * q + 8u * t), h1 = ld8_u2(r1 + 64u * q + 32u + 8u * t);
+        const uint2 b0 = ld8_u2(r0 + 128u + 32u * q + 8u * t), b1 = ld8_u2(r1 + 128u + 32u * q + 8u * t);
+        const uint32_t m02[4] = {b0.x & 0x33333333u, b0.y & 0x33333333u, b1.x & 0x33333333u, b1.y & 0x33333333u};
+        const uint32_t m13[4] = {b0.x & 0xccccccccu, b0.y & 0xccccccccu, b1.x & 0xccccccccu, b1.y & 0xccccccccu};
+#pragma unroll
+        for (uint32_t c = 0; c < 4u; ++c) {
+            int D[4] = {0, 0, 0, 0};
+            mma_u8s8(D, q6_quant(c, l0.x, h0.x, m02[0], m13[0]), q6_quant(c, l1.x, h1.x, m02[2], m13[2]),
+                     q6_quant(c, l0.y, h0.y, m02[1], m13[1]), q6_quant(c, l1.y, h1.y, m02[3], m13[3]),
+                     *reinterpret_cast<const uint2 *>(xl + 512u * q + 128u * c));
+            const uint32_t sel = (c & 1u) ? sel1 : sel0;
+            const int s0 = (int)prmt_sx(S0[2u * q + (c >> 1)], sel);
+            const int s1 = (int)prmt_sx(S1[2u * q + (c >> 1)], sel);
+            T[0] += s0 * D[0];
+            T[1] += s0 * D[1];
+            T[2] += s1 * D[2];
+            T[3] += s1 * D[3];
+            const float xg = xs[8u * q + 2u * c + (t >> 1)];
+            F0 += (float)s0 * xg;
+            F1 += (float)s1 * xg;
+        }
+    }
+    const bool odd = t & 1u;
+    const float u0 = odd ? 1.0f / 16384.0f : 1.0f, u1 = odd ? 0.f : 1.0f / 128.0f, fo = odd ? 0.f : 32.0f;
+    o0 += h2f((uint16_t)ld_u16(r0 + 208)) * ((float)T[0] * u0 + (float)T[1] * u1 - fo * F0);
+    o1 += h2f((uint16_t)ld_u16(r1 + 208)) * ((float)T[2] * u0 + (float)T[3] * u1 - fo * F1);
+}
+
 // One Q6_K task (16 rows x 256 elements) for lane (g, t): rows g (r0) and
 // g + 8 (r1), block starts in shared memory (2-byte aligned). Four MMAs
 // cover four 16-element scale groups at once: the four lanes t of a row
@@ -1386,7 +1616,7 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         }
         m4_commit();
     }
-    const float out_scale = m4_stage_x<W>(a, h->dred, xarea, Q4, t_wait, a.seg[c.seg].x_off);
+    const float out_scale = m4_stage_x<W, Q4 || Q6>(a, h->dred, xarea, Q4, t_wait, a.seg[c.seg].x_off);
 #pragma unroll
     for (uint32_t k = kPre; k + 1u < (uint32_t)NS; ++k) {
         if (k < n) {
@@ -1408,6 +1638,8 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
     const float *isb = xs16 + a.cols / 16u;
     const uint8_t *ringp = ring + (size_t)warp * NS * a.slot_bytes;
     const uint32_t wlow = (uint32_t)reinterpret_cast<uintptr_t>(sg.w0), wlow1 = (uint32_t)reinterpret_cast<uintptr_t>(sg.w1);
+    const uint32_t bsel = m4_bsel(lane, Q6), t4 = lane & 3u;
+    const uint32_t sel0 = sx_sel(t4 >> 1), sel1 = sx_sel(2u + (t4 >> 1));
     float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
     uint32_t si = 0, sn = (uint32_t)NS - 1u;   // slots of the consumed and of the next issued task
     for (uint32_t k = 0; k < n; ++k) {
@@ -1426,12 +1658,13 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         const float *xs = xs16 + cc.b * 16u;
         float o0 = 0.f, o1 = 0.f;
         if constexpr (Q4) {
-            q4k_task(slot, 0u, 0u, kM4Q4Row, xb, xs, lane, o0, o1);
+            q4k_task8(slot + g * kM4Q4Row, slot + (g + 8u) * kM4Q4Row, xb + bsel, xs, t4, o0, o1);
         } else if constexpr (Q6) {
             // the block's offset inside its 16-byte-aligned window, per row
             const uint32_t lb0 = (cc.s ? wlow1 : wlow) + 16u * cc.t * sg.rb + cc.b * 210u;
-            q6k_task4(slot + g * kM4Q6Row + ((lb0 + g * sg.rb) & 15u),
-                      slot + (g + 8u) * kM4Q6Row + ((lb0 + (g + 8u) * sg.rb) & 15u), xb, xs, lane, o0, o1);
+            q6k_task8(slot + g * kM4Q6Row + ((lb0 + g * sg.rb) & 15u),
+                      slot + (g + 8u) * kM4Q6Row + ((lb0 + (g + 8u) * sg.rb) & 15u), xb + bsel, xs, t4, sel0, sel1,
+                      o0, o1);
         } else {
             gen_task<TY>(slot + g * m4_gen_row(TY), slot + (g + 8u) * m4_gen_row(TY), xb, xs, lane, o0, o1);
         }
