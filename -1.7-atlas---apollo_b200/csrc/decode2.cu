@@ -1061,6 +1061,13 @@ __device__ __forceinline__ const uint8_t *m4_block(const M4Seg &g, const M4Cur &
     return (c.s ? g.w1 : g.w0) + (uint64_t)(16u * c.t) * g.rb + c.b * g.bb;
 }
 
+// Slot row of MMA row m of a Q4_K task: rows 1 <-> 2 of every 4 swapped, so
+// that the two rows (2i, 2i + 1) a quarter warp reads with its 16-byte quant
+// loads sit two rows (288 bytes, two 16-byte bank groups) apart: with rows
+// 144 bytes apart in order, rows one apart put a lane pair's adjacent bank
+// groups onto the next row's and the loads conflicted 2-way.
+__host__ __device__ constexpr uint32_t q4_slot_row(uint32_t m) { return ((m + 1u) & 2u) ? m ^ 3u : m; }
+
 // Issue the copies of one task (16 rows x one block) into a slot: Q4_K 144
 // chunks (5 per lane, the last by lanes 0-15), Q6_K 224 (7 per lane).
 template <bool Q4>
@@ -1074,10 +1081,10 @@ __device__ __forceinline__ void m4_issue(const M4Seg &g, const M4Hdr *h, const M
         if (Q4) {
             if (i < 4u || lane < 16u) cp_async16(slot + e.y, base + e.x, policy);
         } else {
-            // the 16-byte boundary at or below the row's block, plus chunk e.y % kM4Q6Row
+            // the 16-byte boundary at or below the row's block, plus the chunk's offset
             const uint8_t *win =
                 reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(base + e.x) & ~uintptr_t(15));
-            cp_async16(slot + e.y, win + e.y % kM4Q6Row, policy);
+            cp_async16(slot + (e.y & 0xffffu), win + (e.y >> 16), policy);
         }
     }
 }
@@ -1192,15 +1199,26 @@ __device__ __forceinline__ void ld16_u2(const uint8_t *p, uint32_t (&w)[4])
     for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
 }
 
-// 8 bytes at a 2-byte-aligned shared-memory address: three aligned loads
-// and a funnel shift by the misalignment (0 or 16 bits).
-__device__ __forceinline__ uint2 ld8_u2(const uint8_t *p)
+// 8 / 16 bytes at byte offset `off` (2-byte aligned) of a 4-byte-aligned
+// shared-memory base: three / five aligned word loads and funnel shifts by
+// the misalignment (0 or 16 bits). The offset is applied to the pointer, so
+// the loads stay shared-memory loads with 32-bit addresses.
+__device__ __forceinline__ uint2 ld8_at(const uint8_t *base, uint32_t off)
 {
-    const uintptr_t ad = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(ad & ~uintptr_t(3));
-    const uint32_t sh = (uint32_t)(ad & 3u) * 8u;
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(base + (off & ~3u));
+    const uint32_t sh = (off & 3u) * 8u;
     const uint32_t v0 = q[0], v1 = q[1], v2 = q[2];
     return make_uint2(__funnelshift_r(v0, v1, sh), __funnelshift_r(v1, v2, sh));
+}
+__device__ __forceinline__ void ld16_at(const uint8_t *base, uint32_t off, uint32_t (&w)[4])
+{
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(base + (off & ~3u));
+    const uint32_t sh = (off & 3u) * 8u;
+    uint32_t v[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = q[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
 }
 
 // d += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulators
@@ -1328,21 +1346,25 @@ __host__ __device__ constexpr uint32_t sx_sel(uint32_t k) { return k | ((k | 8u)
 // -32 offset is applied with the staged 16-element sums of e, once per (row,
 // group), by the even lanes. sel0 / sel1: byte_perm selectors of scale byte
 // (t >> 1) / 2 + (t >> 1) of a word, sign-extended.
-__device__ __forceinline__ void q6k_task8(const uint8_t *r0, const uint8_t *r1, const uint8_t *xl, const float *xs,
-                                          uint32_t t, uint32_t sel0, uint32_t sel1, float &o0, float &o1)
+__device__ __forceinline__ void q6k_task8(const uint8_t *w0, uint32_t b0, const uint8_t *w1, uint32_t b1,
+                                          const uint8_t *xl, const float *xs, uint32_t t, uint32_t sel0, uint32_t sel1,
+                                          float &o0, float &o1)
 {
+    // w0 / w1: the 16-byte-aligned windows of rows g / g + 8, b0 / b1: the
+    // blocks' (even) offsets in them
     uint32_t S0[4], S1[4];
-    ld16_u2(r0 + 192, S0);
-    ld16_u2(r1 + 192, S1);
+    ld16_at(w0, b0 + 192u, S0);
+    ld16_at(w1, b1 + 192u, S1);
     int T[4] = {0, 0, 0, 0};
     float F0 = 0.f, F1 = 0.f;
 #pragma unroll
     for (uint32_t q = 0; q < 2u; ++q) {
-        const uint2 l0 = ld8_u2(r0 + 64u * q + 8u * t), h0 = ld8_u2(r0 + 64u * q + 32u + 8u * t);
-        const uint2 l1 = ld8_u2(r1 + 64u * q + 8u * t), h1 = ld8_u2(r1 + 64u * q + 32u + 8u * t);
-        const uint2 b0 = ld8_u2(r0 + 128u + 32u * q + 8u * t), b1 = ld8_u2(r1 + 128u + 32u * q + 8u * t);
-        const uint32_t m02[4] = {b0.x & 0x33333333u, b0.y & 0x33333333u, b1.x & 0x33333333u, b1.y & 0x33333333u};
-        const uint32_t m13[4] = {b0.x & 0xccccccccu, b0.y & 0xccccccccu, b1.x & 0xccccccccu, b1.y & 0xccccccccu};
+        const uint32_t ql = 64u * q + 8u * t, qh = 128u + 32u * q + 8u * t;
+        const uint2 l0 = ld8_at(w0, b0 + ql), h0 = ld8_at(w0, b0 + ql + 32u);
+        const uint2 l1 = ld8_at(w1, b1 + ql), h1 = ld8_at(w1, b1 + ql + 32u);
+        const uint2 e0 = ld8_at(w0, b0 + qh), e1 = ld8_at(w1, b1 + qh);
+        const uint32_t m02[4] = {e0.x & 0x33333333u, e0.y & 0x33333333u, e1.x & 0x33333333u, e1.y & 0x33333333u};
+        const uint32_t m13[4] = {e0.x & 0xccccccccu, e0.y & 0xccccccccu, e1.x & 0xccccccccu, e1.y & 0xccccccccu};
 #pragma unroll
         for (uint32_t c = 0; c < 4u; ++c) {
             int D[4] = {0, 0, 0, 0};
@@ -1363,8 +1385,10 @@ __device__ __forceinline__ void q6k_task8(const uint8_t *r0, const uint8_t *r1, 
     }
     const bool odd = t & 1u;
     const float u0 = odd ? 1.0f / 16384.0f : 1.0f, u1 = odd ? 0.f : 1.0f / 128.0f, fo = odd ? 0.f : 32.0f;
-    o0 += h2f((uint16_t)ld_u16(r0 + 208)) * ((float)T[0] * u0 + (float)T[1] * u1 - fo * F0);
-    o1 += h2f((uint16_t)ld_u16(r1 + 208)) * ((float)T[2] * u0 + (float)T[3] * u1 - fo * F1);
+    const float d0 = h2f(*reinterpret_cast<const uint16_t *>(w0 + b0 + 208u));
+    const float d1 = h2f(*reinterpret_cast<const uint16_t *>(w1 + b1 + 208u));
+    o0 += d0 * ((float)T[0] * u0 + (float)T[1] * u1 - fo * F0);
+    o1 += d1 * ((float)T[2] * u0 + (float)T[3] * u1 - fo * F1);
 }
 
 // One Q6_K task (16 rows x 256 elements) for lane (g, t): rows g (r0) and
@@ -1658,13 +1682,13 @@ __device__ void m4_consume(const MvArgs &a, M4Hdr *h, float *part, uint8_t *xare
         const float *xs = xs16 + cc.b * 16u;
         float o0 = 0.f, o1 = 0.f;
         if constexpr (Q4) {
-            q4k_task8(slot + g * kM4Q4Row, slot + (g + 8u) * kM4Q4Row, xb + bsel, xs, t4, o0, o1);
+            q4k_task8(slot + q4_slot_row(g) * kM4Q4Row, slot + q4_slot_row(g + 8u) * kM4Q4Row, xb + bsel, xs, t4, o0,
+                      o1);
         } else if constexpr (Q6) {
             // the block's offset inside its 16-byte-aligned window, per row
             const uint32_t lb0 = (cc.s ? wlow1 : wlow) + 16u * cc.t * sg.rb + cc.b * 210u;
-            q6k_task8(slot + g * kM4Q6Row + ((lb0 + g * sg.rb) & 15u),
-                      slot + (g + 8u) * kM4Q6Row + ((lb0 + (g + 8u) * sg.rb) & 15u), xb + bsel, xs, t4, sel0, sel1,
-                      o0, o1);
+            q6k_task8(slot + g * kM4Q6Row, (lb0 + g * sg.rb) & 15u, slot + (g + 8u) * kM4Q6Row,
+                      (lb0 + (g + 8u) * sg.rb) & 15u, xb + bsel, xs, t4, sel0, sel1, o0, o1);
         } else {
             gen_task<TY>(slot + g * m4_gen_row(TY), slot + (g + 8u) * m4_gen_row(TY), xb, xs, lane, o0, o1);
         }
@@ -1724,10 +1748,11 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) mv4_kernel(const __gri
             uint2 v = make_uint2(0u, 0xffffffffu);
             if (q4 && idx < 144u) {
                 const uint32_t r = idx / 9u, p = idx - 9u * r;
-                v = make_uint2(r * rb + 16u * p, r * kM4Q4Row + 16u * p);
+                v = make_uint2(r * rb + 16u * p, q4_slot_row(r) * kM4Q4Row + 16u * p);
             } else if (!q4 && idx < 224u) {
+                // slot offset in the low half, the chunk's offset in the window in the high half
                 const uint32_t r = idx / 14u, p = idx - 14u * r;
-                v = make_uint2(r * rb, r * kM4Q6Row + 16u * p);
+                v = make_uint2(r * rb, (r * kM4Q6Row + 16u * p) | (16u * p) << 16);
             }
             h->cp[i][l] = v;
         }

@@ -367,3 +367,34 @@ def test_b_operand_holds_each_group_once():
             g, t = lane >> 2, lane & 3
             pl = (bsel(lane, q6) % 32) // 8
             assert (pl < 3) == ((g >> 2) == (t >> 1) and (g & 3) < 3)
+
+
+def q4_slot_row(m):
+    """q4_slot_row (csrc/decode2.cu)."""
+    return m ^ 3 if (m + 1) & 2 else m
+
+
+def test_q4k_quant_loads_conflict_free_per_quarter_warp():
+    # slot rows 144 bytes apart; lane (g, t) loads 16 bytes at 16 + 64 (t >> 1) + 16 (t & 1) + 32 pi of
+    # rows g and g + 8; a 16-byte load is served a quarter warp at a time
+    assert sorted(q4_slot_row(m) for m in range(16)) == list(range(16))
+    for pi in range(2):
+        for rbase in (0, 8):
+            for quarter in range(4):
+                groups = set()
+                for lane in range(8 * quarter, 8 * quarter + 8):
+                    g, t = lane >> 2, lane & 3
+                    a = 144 * q4_slot_row(g + rbase) + 16 + 64 * (t >> 1) + 16 * (t & 1) + 32 * pi
+                    groups.add((a // 16) % 8)
+                assert len(groups) == 8, (pi, rbase, quarter)
+        # the header loads: one row per lane group of 4, two rows per quarter warp
+        for quarter in range(4):
+            assert len({(144 * q4_slot_row(g)) // 16 % 8 for g in (2 * quarter, 2 * quarter + 1)}) == 2
+
+
+def test_q6k_copy_table_encoding():
+    # slot offset in the low 16 bits, the chunk's offset inside the window in the high 16 bits
+    for idx in range(224):
+        r, p = idx // 14, idx % 14
+        y = (r * 240 + 16 * p) | (16 * p) << 16
+        assert y & 0xFFFF == r * 240 + 16 * p and y >> 16 == 16 * p
