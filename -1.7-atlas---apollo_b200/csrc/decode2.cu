@@ -1391,59 +1391,6 @@ __device__ __forceinline__ void q6k_task8(const uint8_t *w0, uint32_t b0, const 
     o1 += d1 * ((float)T[2] * u0 + (float)T[3] * u1 - fo * F1);
 }
 
-// One Q6_K task (16 rows x 256 elements) for lane (g, t): rows g (r0) and
-// g + 8 (r1), block starts in shared memory (2-byte aligned). Four MMAs
-// cover four 16-element scale groups at once: the four lanes t of a row
-// group supply the k slots of group (h, k = t, l16) - 4 elements each, word m
-// of the group's 16 quant bytes - and B holds x only in the column pair of
-// the group that lane's k slots carry (B lane t' is nonzero in columns
-// 2t', 2t' + 1), so accumulator columns 2t, 2t + 1 of lane t end as the
-// sums (hi, lo) of its own group, ready for that group's scale. A 6-bit quant
-// q, zero-extended into a 16-bit lane, is the fp16 subnormal q 2^-24
-// exactly; the -32 offset is applied through the group's sum of x
-// (dequant_q6_k, src/brain_runtime.c:1049-1083).
-__device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, const uint8_t *xb, const float *xs,
-                                          uint32_t lane, float &o0, float &o1)
-{
-    const uint32_t g = lane >> 2, t = lane & 3u;
-    const uint32_t podd = (g & 1u) * 8u;
-    const bool bmine = (g >> 1) == t;
-    const uint32_t ns = 4u * (t >> 1), rot = (4u - 2u * t) & 31u;   // low / high nibbles; qh bits 2t -> 4
-    const float d0 = h2f((uint16_t)ld_u16(r0 + 208)), d1 = h2f((uint16_t)ld_u16(r1 + 208));
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (uint32_t h = 0; h < 2u; ++h) {
-#pragma unroll
-        for (uint32_t l16 = 0; l16 < 2u; ++l16) {
-            const uint32_t oq = 64u * h + 32u * (t & 1u) + 16u * l16, oh = 128u + 32u * h + 16u * l16;
-            uint32_t q0[4], h0[4], q1[4], h1[4];
-            ld16_u2(r0 + oq, q0);
-            ld16_u2(r0 + oh, h0);
-            ld16_u2(r1 + oq, q1);
-            ld16_u2(r1 + oh, h1);
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (uint32_t m = 0; m < 4u; ++m) {
-                const uint32_t v0 = ((q0[m] >> ns) & 0x0f0f0f0fu) | (__funnelshift_l(h0[m], h0[m], rot) & 0x30303030u);
-                const uint32_t v1 = ((q1[m] >> ns) & 0x0f0f0f0fu) | (__funnelshift_l(h1[m], h1[m], rot) & 0x30303030u);
-                uint2 b = make_uint2(0u, 0u);
-                if (bmine) b = *reinterpret_cast<const uint2 *>(xb + (32u * h + 8u * t + 4u * l16 + m) * 16u + podd);
-                if (m == 0u) {
-                    mma16816(c, sub2(v0, 0x4140), sub2(v1, 0x4140), sub2(v0, 0x4342), sub2(v1, 0x4342), b, zero);
-                } else {
-                    const float cc[4] = {c[0], c[1], c[2], c[3]};
-                    mma16816(c, sub2(v0, 0x4140), sub2(v1, 0x4140), sub2(v0, 0x4342), sub2(v1, 0x4342), b, cc);
-                }
-            }
-            const uint32_t G = 8u * h + 2u * t + l16;
-            const float sx = 32.0f * xs[G];
-            const float s0 = d0 * s8f(r0[192u + G]), s1 = d1 * s8f(r1[192u + G]);
-            o0 += s0 * ((c[0] + c[1]) * kTwo24 - sx);
-            o1 += s1 * ((c[2] + c[3]) * kTwo24 - sx);
-        }
-    }
-}
-
 // ------------------------------------------------ other block types ----
 //
 // A task of type TY (F16, Q5_0, Q5_1, Q8_0, Q5_K) reads every weight of a
@@ -1455,9 +1402,9 @@ __device__ __forceinline__ void q6k_task4(const uint8_t *r0, const uint8_t *r1, 
 //   Q5_K  q = nibble | high bit << 4   S = d sc_j   M = -dmin m_j   (j = G / 2)
 //   F16   the binary16 weight itself   S = 1        M = 0
 // so a row's dot over G is  S sum(q x) + M sum(x).  q enters the MMA as a
-// zero-extended 16-bit lane (the fp16 subnormal q 2^-24 exactly). The lanes
-// share the MMAs as in q6k_task4: in round `it`, the four lanes t of a row
-// group supply the k slots of group G = 4 it + t, four elements per MMA, and
+// zero-extended 16-bit lane (the fp16 subnormal q 2^-24 exactly). The four
+// lanes of a row group share each MMA: in round `it`, lane t of a row
+// group supplies the k slots of group G = 4 it + t, four elements per MMA, and
 // B holds x only in the column pair (hi, lo) of the group its lane carries,
 // so accumulator columns 2t, 2t + 1 end as group G's sums for rows g, g + 8.
 
