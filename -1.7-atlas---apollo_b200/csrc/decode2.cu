@@ -538,7 +538,18 @@ __device__ float m4_stage_x(const MvArgs &a, double *dred, uint8_t *xarea, bool 
                     else if (m * __int_as_float((127 + k) << 23) >= 127.5f) --k;
                 }
                 const float sc = __int_as_float((127 + k) << 23);
-                if (lane == 0) isb[b] = __int_as_float((127 - k) << 23);
+                // A NaN or inf element cannot be carried by the int8 planes (the
+                // conversion makes NaN 0 and saturates inf): the block's factor
+                // becomes NaN instead, so every row sum over it is NaN, as the
+                // fp32 products of the reference are.
+                bool nonfinite = false;
+#pragma unroll
+                for (uint32_t hh = 0; hh < 2u; ++hh) {
+                    const float4 x = v[j][hh];
+                    nonfinite |= !isfinite(x.x) || !isfinite(x.y) || !isfinite(x.z) || !isfinite(x.w);
+                }
+                nonfinite = __any_sync(0xffffffffu, nonfinite);
+                if (lane == 0) isb[b] = nonfinite ? __int_as_float(0x7fc00000) : __int_as_float((127 - k) << 23);
                 uint8_t *xblk = xarea + (size_t)b * 1024u;
 #pragma unroll
                 for (uint32_t hh = 0; hh < 2u; ++hh) {

@@ -24,7 +24,7 @@ def stage_block(x):
     """m4_stage_x<W, true> for one 256-element block: (1024-byte area, the 16
     sums of e, 1 / 2^k)."""
     x = np.asarray(x, F32)
-    m = F32(np.abs(x).max())
+    m = F32(np.fmax.reduce(np.abs(x)))   # fmaxf: a NaN operand is skipped
     k = 0
     if m > 0 and np.isfinite(m):
         k = 6 - int(np.floor(np.log2(np.float64(m))))
@@ -33,14 +33,17 @@ def stage_block(x):
         elif F32(m * F32(2.0 ** k)) >= F32(127.5):
             k -= 1
     sc = F32(2.0 ** k)
-    e = (x * sc).astype(F32)
-    hi = np.rint(e).astype(F32)
-    r1 = ((e - hi).astype(F32) * F32(128)).astype(F32)
-    mid = np.rint(r1).astype(F32)
-    lo = np.rint(((r1 - mid).astype(F32) * F32(128)).astype(F32)).astype(F32)
-    planes = [hi.astype(np.int64), mid.astype(np.int64), lo.astype(np.int64)]
-    assert planes[0].min() >= -127 and planes[0].max() <= 127
-    assert all(p.min() >= -64 and p.max() <= 64 for p in planes[1:])
+    with np.errstate(invalid="ignore"):   # inf - inf in a non-finite block, as on the GPU
+        e = (x * sc).astype(F32)
+        hi = np.rint(e).astype(F32)
+        r1 = ((e - hi).astype(F32) * F32(128)).astype(F32)
+        mid = np.rint(r1).astype(F32)
+        lo = np.rint(((r1 - mid).astype(F32) * F32(128)).astype(F32)).astype(F32)
+    nonfinite = not np.isfinite(x).all()
+    planes = [cvt_s32(hi), cvt_s32(mid), cvt_s32(lo)]
+    if not nonfinite:
+        assert planes[0].min() >= -127 and planes[0].max() <= 127
+        assert all(p.min() >= -64 and p.max() <= 64 for p in planes[1:])
     area = np.zeros(1024, np.uint8)
     for ei in range(256):
         for pl in range(3):
@@ -50,7 +53,14 @@ def stage_block(x):
     s4 = ((e[0::4] + e[1::4]).astype(F32) + (e[2::4] + e[3::4]).astype(F32)).astype(F32)
     s8 = (s4 + s4.reshape(-1, 2)[:, ::-1].reshape(-1)).astype(F32)
     s16 = (s8[0::4] + s8[2::4]).astype(F32)
-    return area, s16, F32(2.0 ** -k)
+    return area, s16, (F32(np.nan) if nonfinite else F32(2.0 ** -k))
+
+
+def cvt_s32(f):
+    """The GPU's float -> int32 conversion: NaN -> 0, saturating at the int32 range."""
+    f = np.asarray(f, np.float64)
+    return np.where(np.isnan(f), 0, np.clip(np.nan_to_num(f, posinf=2.0 ** 31 - 1, neginf=-2.0 ** 31),
+                                            -2.0 ** 31, 2.0 ** 31 - 1)).astype(np.int64)
 
 
 # ------------------------------------------------------- register helpers ----
@@ -398,3 +408,19 @@ def test_q6k_copy_table_encoding():
         r, p = idx // 14, idx % 14
         y = (r * 240 + 16 * p) | (16 * p) << 16
         assert y & 0xFFFF == r * 240 + 16 * p and y >> 16 == 16 * p
+
+
+@pytest.mark.parametrize("bad", [np.nan, np.inf, -np.inf])
+def test_nonfinite_input_gives_nan_rows(oracle, bad):
+    # the staged factor of a block holding NaN or inf is NaN: every row sum over it is NaN
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal(256).astype(F32)
+    x[77] = F32(bad)
+    area, xs, isb = stage_block(x)
+    assert np.isnan(isb)
+    blocks = atlas_cuda.synth_blocks(atlas_cuda.TYPE_Q4_K, 16, seed=5)
+    with np.errstate(invalid="ignore", over="ignore"):
+        y = q4k_task8([blocks[144 * r:144 * r + 144] for r in range(16)], area, xs).astype(np.float64) * isb
+    assert np.isnan(y).all()
+    # and a finite block's factor is the plain 1 / 2^k
+    assert np.isfinite(stage_block(rng.standard_normal(256))[2])
